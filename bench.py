@@ -1,0 +1,359 @@
+"""Benchmark of the FP8 QDQ operator path on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--config NAME] [--impl ours|reference]
+
+Default workload (N=1): the FP8 QDQ GEMM of the GEMM sweep at M=N=K=8192 —
+one step is QuantizeLinear of the fp32 activation A [M,K] with its
+per-tensor scale (amax/448) followed by the fused FP8 GEMM against the
+e4m3 weight B [N,K] (DequantizeLinear of both operands and the output cast
+folded into the epilogue), bf16 output. Throughput counts 2*M*N*K FLOP per
+step. Under torchrun each rank runs the same step on its own GPU (replicas of
+a single-GPU problem: no collective on the data path); time is the max over
+ranks.
+
+`--impl reference` times the reference algorithm on the host cores instead
+(the CPU restatement in oracle/, all threads, bounded sample per step): the
+reference's own GPU path needs a graphics API that this machine lacks.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import re
+import statistics
+import subprocess
+import sys
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+L2_BYTES = 126 * 1024 * 1024
+
+
+def parse():
+    p = argparse.ArgumentParser()
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=200)
+    p.add_argument("--warmup", type=int, default=10)
+    p.add_argument("--config", default="gemm8192", choices=sorted(CONFIGS))
+    p.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--no-e2e", action="store_true")
+    return p.parse_args()
+
+
+def measured_peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(path):
+        with open(path) as f:
+            d = json.load(f)
+        return {"hbm_gbs": d["hbm_gbs"], "bf16_tflops": d["bf16_tflops"],
+                "bf16_tflops_sustained": d.get("bf16_tflops_sustained"), "source": "measured"}
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0, "source": "fallback"}
+
+
+def profile_traffic(name):
+    """Per-launch DRAM bytes from the committed ncu summary profiles/<name>.md
+    (a line 'traffic_bytes_per_launch: <int>'), or None."""
+    path = os.path.join(ROOT, "profiles", name + ".md")
+    if not os.path.exists(path):
+        return None
+    m = re.search(r"traffic_bytes_per_launch:\s*([0-9]+)", open(path).read())
+    return int(m.group(1)) if m else None
+
+
+class ClockSampler:
+    """nvidia-smi samples of SM clock / throttle reasons while the timed region runs."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index):
+        self.gpu_index = gpu_index
+        self.proc = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "100",
+                 "-i", str(self.gpu_index)], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        self.lines = []
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                out, _ = self.proc.communicate(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+                out, _ = self.proc.communicate()
+            self.lines = [l for l in out.splitlines() if l.strip()]
+
+    def summary(self):
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for l in getattr(self, "lines", []):
+            f = [x.strip() for x in l.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx = float(f[2])
+            except ValueError:
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# ----------------------------------------------------------------------------- workloads
+class GemmWorkload:
+    """QDQ GEMM: Q(A) then fused FP8 GEMM, bf16 out (GEMM sweep configuration)."""
+
+    def __init__(self, M, N, K, name):
+        self.M, self.N, self.K, self.name = M, N, K, name
+        self.flops = 2.0 * M * N * K
+
+    def describe(self):
+        return {"workload": self.name, "M": self.M, "N": self.N, "K": self.K,
+                "a": "fp32 activation, QuantizeLinear per-tensor (s = amax/448) each step",
+                "b": "e4m3 weight initializer [N,K] (Gemm transB=1), per-tensor scale",
+                "out": "bf16", "l2": "flushed between timed steps (256 MiB write, untimed)"}
+
+    def setup(self, dev, seed):
+        import torch
+        import luisaml_b200 as lb
+        g = torch.Generator(device=dev).manual_seed(seed)
+        self.A = torch.randn(self.M, self.K, device=dev, generator=g)
+        B = torch.randn(self.N, self.K, device=dev, generator=g)
+        self.sa = lb.amax(self.A)
+        self.sa = torch.where(self.sa > 0, self.sa / 448.0, torch.ones_like(self.sa))
+        sb = lb.amax(B)
+        self.sb = torch.where(sb > 0, sb / 448.0, torch.ones_like(sb))
+        self.Bq = lb.quantize(B, self.sb)
+        del B
+        self.Aq = torch.empty(self.M, self.K, dtype=torch.uint8, device=dev)
+        self.Y = torch.empty(self.M, self.N, dtype=torch.bfloat16, device=dev)
+        self.desc, _ = lb.gemm(self.Aq, self.Bq, self.sa, self.sb, out=self.Y, desc_only=True)
+        self.lib = lb.lib()
+        self.kernels_per_step = 2
+
+    def step(self, stream, ev=None):
+        import ctypes
+        import luisaml_b200 as lb
+        s = ctypes.c_void_p(stream.cuda_stream)
+        lb.check(self.lib.lcml_fp8_quantize(ctypes.c_void_p(self.A.data_ptr()), 1, 1, self.A.numel(),
+                                            ctypes.c_void_p(self.sa.data_ptr()), 0,
+                                            ctypes.c_void_p(self.Aq.data_ptr()), s))
+        if ev is not None:
+            ev[0].record(stream)
+        lb.check(self.lib.lcml_fp8_gemm(ctypes.byref(self.desc), s))
+        if ev is not None:
+            ev[1].record(stream)
+
+    # end to end: pinned host A in, bf16 Y out to pinned host, through the C ABI
+    def setup_e2e(self):
+        import torch
+        self.A_host = self.A.cpu().pin_memory()
+        self.Y_host = torch.empty(self.Y.shape, dtype=self.Y.dtype).pin_memory()
+        self.h2d = self.A_host.numel() * 4
+        self.d2h = self.Y_host.numel() * 2
+
+    def step_e2e(self, stream):
+        self.A.copy_(self.A_host, non_blocking=True)
+        self.step(stream)
+        self.Y_host.copy_(self.Y, non_blocking=True)
+
+    def dominant(self):
+        return {"kernel": "gemm_fp8_tc", "bound": "tensor", "unit": "TFLOP/s", "work": self.flops,
+                "profile": "gemm_fp8_tc_8192"}
+
+    # CPU reference: oracle quantize + oracle QDQ GEMM on a bounded row sample
+    def cpu_sample(self, budget_s=12.0):
+        import numpy as np
+        import oracle
+        rng = np.random.default_rng(0)
+        K, N = self.K, self.N
+        if getattr(self, "_cpu_bq", None) is None:
+            self._cpu_bq = rng.integers(0, 0x7e, size=(N, K), dtype=np.uint8)
+        Bq = self._cpu_bq
+        sb = np.float32([0.01])
+
+        def run(rows):
+            A = rng.standard_normal((rows, K)).astype(np.float32)
+            t0 = time.perf_counter()
+            sa = np.float32([oracle.scale_from_amax(oracle.amax(A))])
+            Aq = oracle.quantize(A, sa[0])
+            oracle.qdq_gemm(Aq, sa, Bq, sb)
+            return time.perf_counter() - t0
+
+        t = run(4)
+        rows = int(max(4, min(self.M, 4 * budget_s / max(t, 1e-3))))
+        t = run(rows)
+        return {"value": 2.0 * rows * N * K / t / 1e12, "unit": "TFLOP/s", "cores": oracle.num_threads(),
+                "kind": "port",
+                "sample": f"{rows} of {self.M} rows of the {self.M}x{self.N}x{self.K} QDQ GEMM "
+                          f"(quantize + DQ + K-ordered fp32 fma), {t:.1f} s"}
+
+
+CONFIGS = {
+    "gemm8192": lambda: GemmWorkload(8192, 8192, 8192, "qdq_gemm_8192x8192x8192"),
+    "gemm4096": lambda: GemmWorkload(4096, 4096, 4096, "qdq_gemm_4096x4096x4096"),
+    "gemm2048": lambda: GemmWorkload(2048, 2048, 2048, "qdq_gemm_2048x2048x2048"),
+    "gemm1024": lambda: GemmWorkload(1024, 1024, 1024, "qdq_gemm_1024x1024x1024"),
+}
+
+
+# ----------------------------------------------------------------------------- runners
+def dist_env():
+    ws = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return ws, rank, local
+
+
+def run_reference(args, wl):
+    ws, rank, _ = dist_env()
+    if rank != 0:
+        return
+    samples = []
+    budget = max(0.2, 120.0 / (args.steps + args.warmup))  # whole run within a few minutes
+    for i in range(args.warmup + args.steps):
+        r = wl.cpu_sample(budget_s=budget)
+        if i >= args.warmup:
+            samples.append(r)
+    v = statistics.median(s["value"] for s in samples)
+    line = {"impl": "reference", "metric": METRIC, "value": v, "unit": "TFLOP/s", "n_gpus": args.gpus,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": None, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "e4m3 x e4m3 -> fp32 accumulate", "data": "synthetic",
+            "config": wl.describe(),
+            "cpu_baseline": {"value": v, "unit": "TFLOP/s", "cores": samples[0]["cores"], "kind": "port",
+                             "sample": samples[0]["sample"]},
+            "e2e": {"value": v, "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+            "note": "the reference's GPU path (LuisaCompute dx/vk backends) is unavailable on this box; this is "
+                    "the reference algorithm restated in C (oracle/) on all host threads"}
+    print(json.dumps(line), flush=True)
+
+
+METRIC = "FP8 QDQ-GEMM TFLOP/s"
+
+
+def run_ours(args, wl):
+    import torch
+    import torch.distributed as dist
+    import luisaml_b200 as lb
+
+    ws, rank, local = dist_env()
+    if ws > 1:
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", init_method="env://", timeout=__import__("datetime").timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    lb.check(lb.lib().lcml_device_check())
+    wl.setup(dev, seed=1234 + rank)
+    stream = torch.cuda.current_stream(dev)
+    flush = torch.empty(2 * L2_BYTES // 4, dtype=torch.float32, device=dev)
+
+    for _ in range(args.warmup):
+        flush.fill_(1.0)
+        wl.step(stream)
+    torch.cuda.synchronize()
+
+    n = args.steps
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(n)]
+    kev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(n)]
+    if ws > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    launches0 = lb.launch_count()
+    with ClockSampler(local) as clk:
+        for i in range(n):
+            flush.fill_(float(i))          # evict L2 (untimed: outside the step's events)
+            ev[i][0].record(stream)
+            wl.step(stream, kev[i])
+            ev[i][1].record(stream)
+        torch.cuda.synchronize()
+    launches = lb.launch_count() - launches0
+    if ws > 1:
+        dist.barrier()
+    step_ms = [a.elapsed_time(b) for a, b in ev]
+    kern_ms = [a.elapsed_time(b) for a, b in kev]
+    total_ms = sum(step_ms)
+    t = torch.tensor([total_ms], dtype=torch.float64, device=dev)
+    if ws > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    total_ms = float(t.item())
+    assert lb.device_error() == 0
+
+    value = wl.flops * n * ws / (total_ms / 1e3) / 1e12
+    peaks = measured_peaks()
+    dom = wl.dominant()
+    kern_avg_s = (sum(kern_ms) / n) / 1e3
+    achieved = dom["work"] / kern_avg_s / 1e12
+    fp8_peak = 2.0 * peaks["bf16_tflops"]
+    traffic = profile_traffic(dom["profile"])
+    roofline = {"bound": dom["bound"], "achieved": achieved, "peak": fp8_peak, "unit": dom["unit"],
+                "frac": achieved / fp8_peak, "traffic": traffic, "kernel": dom["kernel"],
+                "peak_source": f"2 x {peaks['source']} dense bf16 burst ({peaks['bf16_tflops']} TF/s): "
+                               "the B200 FP8 dense rate is twice its bf16 rate",
+                "kernel_ms": kern_avg_s * 1e3}
+
+    e2e = None
+    if not args.no_e2e:
+        wl.setup_e2e()
+        for _ in range(3):
+            wl.step_e2e(stream)
+        torch.cuda.synchronize()
+        if ws > 1:
+            dist.barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        ne = max(3, min(20, n // 10))
+        e0.record(stream)
+        for _ in range(ne):
+            wl.step_e2e(stream)
+        e1.record(stream)
+        torch.cuda.synchronize()
+        et = torch.tensor([e0.elapsed_time(e1)], dtype=torch.float64, device=dev)
+        if ws > 1:
+            dist.all_reduce(et, op=dist.ReduceOp.MAX)
+        e2e = {"value": wl.flops * ne * ws / (float(et.item()) / 1e3) / 1e12, "unit": "TFLOP/s",
+               "h2d_bytes_per_step": wl.h2d, "d2h_bytes_per_step": wl.d2h,
+               "path": "pinned host fp32 A -> H2D -> lcml_fp8_quantize -> lcml_fp8_gemm -> D2H bf16 Y"}
+
+    cpu = None
+    if rank == 0 and ws == 1 and not args.no_cpu_baseline:
+        cpu = wl.cpu_sample()
+
+    if rank == 0:
+        line = {"metric": METRIC, "value": value, "unit": "TFLOP/s", "n_gpus": ws, "steps": n,
+                "warmup": args.warmup, "ms_per_step": total_ms / n, "higher_is_better": True, "scaling": "weak",
+                "vs_baseline": None, "dtype": "e4m3 x e4m3 -> fp32 accumulate, bf16 out", "data": "synthetic",
+                "config": wl.describe(), "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e,
+                "gpu_launches": launches, "clocks": clk.summary(),
+                "parallelism": "replicas" if ws > 1 else "single"}
+        print(json.dumps(line), flush=True)
+    if ws > 1:
+        dist.destroy_process_group()
+
+
+def main():
+    args = parse()
+    wl = CONFIGS[args.config]()
+    if args.impl == "reference":
+        run_reference(args, wl)
+    else:
+        run_ours(args, wl)
+
+
+if __name__ == "__main__":
+    main()

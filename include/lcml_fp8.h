@@ -1,0 +1,230 @@
+/*
+ * lcml_fp8.h — C ABI of the B200 (sm_100a) FP8 e4m3 operator path.
+ *
+ * A thin shim over hand-written CUDA kernels. Every entry point:
+ *   - takes device pointers, 64-bit sizes and a CUDA stream (lcml_stream_t is
+ *     layout-identical to cudaStream_t; NULL is the legacy default stream);
+ *   - enqueues work asynchronously and never synchronises the stream;
+ *   - never allocates device memory on the hot path (callers pass workspace);
+ *   - returns an lcml_status; a nonzero status leaves a message for
+ *     lcml_last_error() (thread-local). No exceptions cross the ABI and no
+ *     kernel traps: a kernel that gives up on a bounded wait records a code
+ *     readable with lcml_device_error().
+ *
+ * The operators of the ONNX graph executor (include/lcml_onnx.h) call these
+ * functions from Operator::forward. Reference interfaces each entry point
+ * stands in for are cited beside it (paths inside the LuisaML tree).
+ */
+#ifndef LCML_FP8_H
+#define LCML_FP8_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct CUstream_st *lcml_stream_t;
+
+/* Status codes. */
+typedef enum lcml_status {
+    LCML_OK = 0,
+    LCML_ERR_INVALID_ARGUMENT = 1, /* null pointer, bad shape, misaligned pointer */
+    LCML_ERR_UNSUPPORTED = 2,      /* a valid request this build does not implement */
+    LCML_ERR_CUDA = 3,             /* a CUDA runtime call failed; message has the detail */
+    LCML_ERR_NO_DEVICE = 4,        /* no sm_100 device visible */
+    LCML_ERR_DEVICE_TIMEOUT = 5    /* a kernel abandoned a bounded wait (lcml_device_error) */
+} lcml_status;
+
+/* Element types: the ONNX TensorProto.DataType numbers (include/onnx/onnx.h:31-60). */
+typedef enum lcml_dtype {
+    LCML_DTYPE_FLOAT = 1,
+    LCML_DTYPE_FLOAT16 = 10,
+    LCML_DTYPE_BFLOAT16 = 16,
+    LCML_DTYPE_FLOAT8E4M3FN = 17
+} lcml_dtype;
+
+/* Scale layouts. TENSOR: one fp32 scale. AXIS: one per index of the quantized
+ * axis. For 2-D GEMM operands ROW ([M] for A) and COL ([N] for B) are AXIS
+ * along dim 0 and the N dimension respectively. */
+typedef enum lcml_scale_mode {
+    LCML_SCALE_TENSOR = 0,
+    LCML_SCALE_AXIS = 1,
+    LCML_SCALE_ROW = 1,
+    LCML_SCALE_COL = 2
+} lcml_scale_mode;
+
+/* GEMM epilogues (the activation nodes fused behind Gemm/MatMul/Conv). */
+typedef enum lcml_epilogue {
+    LCML_EPI_NONE = 0,
+    LCML_EPI_RELU = 1,     /* Relu, src/onnx/operators/unary.cpp:85 */
+    LCML_EPI_SILU_MUL = 2  /* SiLU(gate) * up: Sigmoid+Mul+Mul (unary.cpp:86-87, binary.cpp:347).
+                              B holds gate/up rows interleaved in groups of 128:
+                              [gate 0..127; up 0..127; gate 128..255; up 128..255; ...],
+                              Y has N/2 columns. */
+} lcml_epilogue;
+
+/* Library / device state. */
+const char *lcml_last_error(void);
+int lcml_abi_version(void);
+/* 0 when an sm_100 device is current; LCML_ERR_NO_DEVICE otherwise. */
+int lcml_device_check(void);
+/* Reads and clears the device error word (synchronises the device). *code = 0: none. */
+int lcml_device_error(int *code);
+/* Number of kernels this library has launched in this process (all streams). */
+uint64_t lcml_launch_count(void);
+
+/*
+ * QuantizeLinear to float8e4m3fn, zero point 0, saturate = 1 (ONNX opset 19+):
+ *   y[i] = e4m3(x[i] / s), x / s an IEEE fp32 divide, e4m3() bit-identical to
+ *   FP8E4M3FN::from_float (include/onnx/fp_quantized.h:149-223).
+ * The reference registers no QuantizeLinear (its loader asserts at
+ * src/onnx/onnx.cpp:228-229); its FP8 conversion is Cast (src/onnx/operators/cast.cpp:63-67).
+ * x (fp32) is viewed as [outer, axis_len, inner]; TENSOR uses scale[0], AXIS
+ * uses scale[(i / inner) % axis_len].
+ */
+int lcml_fp8_quantize(const float *x, int64_t outer, int64_t axis_len, int64_t inner, const float *scale,
+                      int scale_mode, uint8_t *y, lcml_stream_t stream);
+
+/* Same, with the scale derived on the device from a per-axis amax:
+ * s[a] = amax[a] / 448 (1 when amax is 0); s is also written to scale_out
+ * when not NULL. Used after a GEMM epilogue that produced row maxima. */
+int lcml_fp8_quantize_from_amax(const float *x, int64_t outer, int64_t axis_len, int64_t inner,
+                                const float *amax, float *scale_out, uint8_t *y, lcml_stream_t stream);
+
+/* Dynamic per-row (per-token) quantization of x [rows, cols] (row stride ldx
+ * elements): s[r] = max|x[r,:]| / 448 (1 for an all-zero row; NaN ignored),
+ * y[r,c] = e4m3(x[r,c] / s[r]). The Abs -> ReduceMax -> Div -> QuantizeLinear
+ * chain (unary.cpp:110, reduce.cpp:431, binary.cpp:350) as one pass. */
+int lcml_fp8_quantize_rows_dynamic(const float *x, int64_t rows, int64_t cols, int64_t ldx, float *scale_out,
+                                   uint8_t *y, lcml_stream_t stream);
+
+/* max |x| over n fp32 values (NaN ignored) into *amax_out (device). */
+int lcml_amax(const float *x, int64_t n, float *amax_out, lcml_stream_t stream);
+
+/* Dynamic per-tensor quantization: s = max|x| / 448, y = e4m3(x / s).
+ * workspace: caller-owned device scratch of at least 4 bytes (the running
+ * amax). scale_out (device, 1 float) receives s. */
+int lcml_fp8_quantize_tensor_dynamic(const float *x, int64_t n, float *scale_out, uint8_t *y, float *workspace,
+                                     lcml_stream_t stream);
+
+/* DequantizeLinear: y = to_float(q) * s (fp32 multiply), output fp32 or bf16.
+ * to_float() is FP8E4M3FN::to_float (include/onnx/fp_quantized.h:226-249). */
+int lcml_fp8_dequantize(const uint8_t *q, int64_t outer, int64_t axis_len, int64_t inner, const float *scale,
+                        int scale_mode, void *y, int y_dtype, lcml_stream_t stream);
+
+/* e4m3 matrix transpose: src [rows, cols] -> dst [cols, rows] (row-major).
+ * Converts MatMul's [K,N] weights into the K-major layout the tensor-core
+ * GEMM reads. */
+int lcml_fp8_transpose(const uint8_t *src, int64_t rows, int64_t cols, uint8_t *dst, lcml_stream_t stream);
+
+/*
+ * Fused FP8 GEMM: the DequantizeLinear -> Gemm/MatMul -> (Relu | Sigmoid*Mul)
+ * -> (QuantizeLinear) node group of a QDQ graph in one kernel.
+ *   acc[m,n] = sum_k A[m,k] * B[k,n]   (e4m3 x e4m3, exact products, fp32 accumulate)
+ *   v = acc * (alpha * sa * sb) + beta * C     sa: [1] or [M]; sb: [1] or [N]
+ *   v = act(v)                                 (epilogue)
+ *   Y = v (f32 / bf16) or e4m3(v / y_scale)
+ * Stands in for Gemm::apply (src/onnx/operators/gemm.cpp:28-325) and MatMul
+ * (src/onnx/operators/mat_mul.cpp:51-186) fed by DequantizeLinear, which the
+ * reference cannot express (Gemm excludes FP8, gemm.cpp:11-16).
+ */
+typedef struct lcml_fp8_gemm_desc {
+    int64_t M, N, K;
+    const uint8_t *A; /* [M, K] e4m3, row stride lda bytes (K-major) */
+    int64_t lda;
+    const uint8_t *B; /* b_kmajor=1: [N, K], row stride ldb (Gemm transB=1)  */
+    int64_t ldb;      /* b_kmajor=0: [K, N], row stride ldb (MatMul layout)   */
+    int b_kmajor;
+    const float *scale_a; /* device */
+    int scale_a_mode;     /* LCML_SCALE_TENSOR or LCML_SCALE_ROW */
+    const float *scale_b; /* device */
+    int scale_b_mode;     /* LCML_SCALE_TENSOR or LCML_SCALE_COL */
+    float alpha;
+    float beta;
+    const float *c_vec;   /* optional fp32 C broadcast: [N] (COL), [M] (ROW) or [1] (TENSOR) */
+    int c_vec_mode;
+    const void *c_mat;    /* optional full C [M, N] (e.g. the FFN residual), row stride ldc elements */
+    int c_mat_dtype;      /* LCML_DTYPE_FLOAT or LCML_DTYPE_BFLOAT16 */
+    int64_t ldc;
+    int epilogue;         /* lcml_epilogue */
+    void *Y;              /* [M, N] (N/2 for SILU_MUL), row stride ldy elements */
+    int y_dtype;          /* FLOAT, BFLOAT16 or FLOAT8E4M3FN */
+    int64_t ldy;
+    const float *y_scale; /* device, per-tensor output scale when y_dtype is e4m3 */
+    float *row_amax;      /* optional device [M]: max |v| per row (atomic; zero it first) */
+} lcml_fp8_gemm_desc;
+
+int lcml_fp8_gemm(const lcml_fp8_gemm_desc *desc, lcml_stream_t stream);
+
+/*
+ * FP8 2-D convolution, NCHW, lowered to implicit GEMM on the tensor cores.
+ * Stands in for Conv::forward (src/onnx/operators/conv.cpp:35-255) fed by
+ * DequantizeLinear on X and W. X is e4m3 [N, C, H, W] with a per-tensor
+ * scale; W is prepacked by lcml_fp8_conv_pack_weight; epilogue as for GEMM
+ * (bias per output channel, Relu, optional residual [N, M, oH, oW], output
+ * fp32/bf16/e4m3). Pads are begin/end per ONNX; the reference uses begin pads
+ * only (conv.cpp:119-121), which equals ONNX when the output shape matches.
+ */
+typedef struct lcml_fp8_conv_desc {
+    int64_t N, C, H, W;     /* input */
+    int64_t M, kH, kW;      /* output channels, kernel */
+    int64_t oH, oW;         /* output spatial */
+    int sH, sW, pH, pW, dH, dW, group;
+    const uint8_t *X;       /* e4m3 activations, layout per x_nhwc */
+    int x_nhwc;             /* 0: NCHW (ONNX), 1: NHWC (internal fast layout) */
+    const float *scale_x;   /* device [1] */
+    const uint8_t *Wp;      /* packed weights from lcml_fp8_conv_pack_weight */
+    const float *scale_w;   /* device [1] or [M] */
+    int scale_w_mode;       /* LCML_SCALE_TENSOR or LCML_SCALE_AXIS (per output channel) */
+    const float *bias;      /* optional fp32 [M] */
+    const void *residual;   /* optional, same layout/dtype as Y */
+    int epilogue;           /* LCML_EPI_NONE or LCML_EPI_RELU */
+    void *Y;
+    int y_dtype;            /* FLOAT, BFLOAT16 or FLOAT8E4M3FN */
+    int y_nhwc;             /* 0: NCHW, 1: NHWC */
+    const float *y_scale;   /* per-tensor output scale when y_dtype is e4m3 */
+    void *workspace;        /* caller scratch, lcml_fp8_conv_workspace_size() bytes */
+} lcml_fp8_conv_desc;
+
+/* Bytes of scratch lcml_fp8_conv needs for `desc` (0 when none). */
+int64_t lcml_fp8_conv_workspace_size(const lcml_fp8_conv_desc *desc);
+/* Bytes of the packed weight buffer for W [M, C/group, kH, kW]. */
+int64_t lcml_fp8_conv_packed_weight_size(int64_t M, int64_t Cg, int64_t kH, int64_t kW);
+/* Packs e4m3 W [M, C/group, kH, kW] (ONNX layout) into the GEMM B layout. */
+int lcml_fp8_conv_pack_weight(const uint8_t *W, int64_t M, int64_t Cg, int64_t kH, int64_t kW, uint8_t *Wp,
+                              lcml_stream_t stream);
+int lcml_fp8_conv(const lcml_fp8_conv_desc *desc, lcml_stream_t stream);
+
+/*
+ * Memory-bound operators around the GEMMs (fp32 unless stated).
+ */
+/* Relu (unary.cpp:85) / Sigmoid (unary.cpp:86-87) / Abs (unary.cpp:110). op: 0 relu, 1 sigmoid, 2 abs */
+int lcml_unary_f32(int op, const float *x, float *y, int64_t n, lcml_stream_t stream);
+/* Add/Sub/Mul/Div (binary.cpp:341-350) with NumPy broadcast of b over a's
+ * trailing dims: b has b_n elements and b_n divides n (scalar, row or same shape).
+ * op: 0 add, 1 sub, 2 mul, 3 div. */
+int lcml_binary_f32(int op, const float *a, const float *b, int64_t n, int64_t b_n, float *y,
+                    lcml_stream_t stream);
+/* ReduceMax over the last axis (reduce.cpp:431): x [rows, cols] -> y [rows]. abs_first applies Abs. */
+int lcml_reduce_max_rows(const float *x, int64_t rows, int64_t cols, int abs_first, float *y,
+                         lcml_stream_t stream);
+/* Softmax over the last axis (softmax.cpp:216-443): x, y [rows, cols]. */
+int lcml_softmax_rows(const float *x, int64_t rows, int64_t cols, float *y, lcml_stream_t stream);
+/* MaxPool 2-D (max_pool.cpp:20-300), NCHW fp32 or e4m3 (elem_dtype), begin pads. */
+int lcml_maxpool2d(const void *x, int elem_dtype, int64_t NC, int64_t H, int64_t W, int kH, int kW, int sH,
+                   int sW, int pH, int pW, int64_t oH, int64_t oW, void *y, int x_nhwc, int64_t C,
+                   lcml_stream_t stream);
+/* GlobalAveragePool (global_average_pool.cpp:12-154): x [N, C, H*W] (or NHWC) -> y [N, C] fp32.
+ * x may be e4m3 with a per-tensor scale (x_scale) or fp32/bf16. */
+int lcml_global_avgpool(const void *x, int elem_dtype, const float *x_scale, int64_t N, int64_t C, int64_t HW,
+                        int x_nhwc, float *y, lcml_stream_t stream);
+/* Elementwise dtype conversion (Cast, cast.cpp:10-162): fp32 <-> bf16. */
+int lcml_cast(const void *x, int x_dtype, void *y, int y_dtype, int64_t n, lcml_stream_t stream);
+
+#ifdef __cplusplus
+}/* extern "C" */
+#endif
+
+#endif /* LCML_FP8_H */

@@ -1,0 +1,370 @@
+// Memory-bound operators around the FP8 GEMMs: Relu / Sigmoid / Abs,
+// Add / Sub / Mul / Div with trailing broadcast, ReduceMax over the last axis,
+// Softmax over the last axis, MaxPool, GlobalAveragePool and Cast.
+// Coalesced 16-byte accesses where the layout allows, grid-stride loops,
+// grids sized from the SM count. Each kernel's HBM bound is its bytes moved:
+// unary/cast 8 B/elem (fp32 in + out), binary 12 B/elem, reduce/softmax
+// 4-8 B/elem, pools read each input once.
+#include <cuda_bf16.h>
+
+#include "lcml_device.cuh"
+#include "lcml_internal.h"
+
+namespace lcml {
+namespace {
+
+constexpr int kThreads = 256;
+
+int grid_for(int64_t items) {
+    const int64_t per_wave = static_cast<int64_t>(sm_count()) * (2048 / kThreads);
+    int64_t b = (items + kThreads - 1) / kThreads;
+    if (b > per_wave) b = per_wave;
+    return static_cast<int>(b < 1 ? 1 : b);
+}
+
+__device__ __forceinline__ float sigmoid1(float x) {
+    const float e = expf(-fabsf(x));
+    return x >= 0.0f ? 1.0f / (1.0f + e) : e / (1.0f + e);
+}
+
+template <int OP>
+__device__ __forceinline__ float unary1(float x) {
+    if (OP == 0) return x > 0.0f ? x : 0.0f;
+    if (OP == 1) return sigmoid1(x);
+    return fabsf(x);
+}
+
+template <int OP>
+__global__ void __launch_bounds__(kThreads) k_unary(const float *__restrict__ x, float *__restrict__ y, int64_t n,
+                                                    int vec) {
+    const int64_t tid = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    const int64_t nt = static_cast<int64_t>(gridDim.x) * blockDim.x;
+    int64_t done = 0;
+    if (vec) {
+        const int64_t n4 = n >> 2;
+        for (int64_t i = tid; i < n4; i += nt) {
+            float4 v = __ldcs(reinterpret_cast<const float4 *>(x) + i);
+            v.x = unary1<OP>(v.x);
+            v.y = unary1<OP>(v.y);
+            v.z = unary1<OP>(v.z);
+            v.w = unary1<OP>(v.w);
+            __stcs(reinterpret_cast<float4 *>(y) + i, v);
+        }
+        done = n4 << 2;
+    }
+    for (int64_t i = done + tid; i < n; i += nt) y[i] = unary1<OP>(x[i]);
+}
+
+template <int OP>
+__device__ __forceinline__ float binary1(float a, float b) {
+    if (OP == 0) return a + b;
+    if (OP == 1) return a - b;
+    if (OP == 2) return a * b;
+    return a / b;
+}
+
+template <int OP>
+__global__ void __launch_bounds__(kThreads) k_binary(const float *__restrict__ a, const float *__restrict__ b,
+                                                     float *__restrict__ y, int64_t n, int64_t bn, int vec) {
+    const int64_t tid = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    const int64_t nt = static_cast<int64_t>(gridDim.x) * blockDim.x;
+    int64_t done = 0;
+    if (vec) {  // bn % 4 == 0 (or bn == 1) and all pointers 16-byte aligned
+        const int64_t n4 = n >> 2;
+        for (int64_t i = tid; i < n4; i += nt) {
+            const float4 va = __ldcs(reinterpret_cast<const float4 *>(a) + i);
+            float4 vb;
+            if (bn == 1) {
+                const float s = __ldg(b);
+                vb = make_float4(s, s, s, s);
+            } else {
+                vb = __ldg(reinterpret_cast<const float4 *>(b) + (i % (bn >> 2)));
+            }
+            __stcs(reinterpret_cast<float4 *>(y) + i,
+                   make_float4(binary1<OP>(va.x, vb.x), binary1<OP>(va.y, vb.y), binary1<OP>(va.z, vb.z),
+                               binary1<OP>(va.w, vb.w)));
+        }
+        done = n4 << 2;
+    }
+    for (int64_t i = done + tid; i < n; i += nt) y[i] = binary1<OP>(a[i], b[i % bn]);
+}
+
+__device__ __forceinline__ float warp_max_f(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+    return v;
+}
+
+__device__ __forceinline__ float warp_sum_f(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+
+template <bool MAX>
+__device__ __forceinline__ float block_reduce(float v, float *red) {
+    v = MAX ? warp_max_f(v) : warp_sum_f(v);
+    const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
+    __syncthreads();
+    if (l == 0) red[w] = v;
+    __syncthreads();
+    float r = (l < static_cast<int>(blockDim.x >> 5)) ? red[l] : (MAX ? -INFINITY : 0.0f);
+    return MAX ? warp_max_f(r) : warp_sum_f(r);
+}
+
+// ReduceMax over the last axis, one CTA per row. The reference's ReduceMax
+// uses max(); NaN inputs follow fmaxf (ignored) here.
+__global__ void __launch_bounds__(kThreads) k_reduce_max_rows(const float *__restrict__ x, int64_t cols, int abs_first,
+                                                              float *__restrict__ y) {
+    __shared__ float red[32];
+    const float *xr = x + static_cast<int64_t>(blockIdx.x) * cols;
+    float m = -INFINITY;
+    for (int64_t c = threadIdx.x; c < cols; c += kThreads) {
+        const float v = abs_first ? fabsf(xr[c]) : xr[c];
+        m = fmaxf(m, v);
+    }
+    m = block_reduce<true>(m, red);
+    if (threadIdx.x == 0) y[blockIdx.x] = m;
+}
+
+// Softmax over the last axis: max, sum of exp(x - max), then exp(x - max) / sum.
+__global__ void __launch_bounds__(kThreads) k_softmax_rows(const float *__restrict__ x, int64_t cols,
+                                                           float *__restrict__ y) {
+    __shared__ float red[32];
+    const int64_t r = blockIdx.x;
+    const float *xr = x + r * cols;
+    float m = -INFINITY;
+    for (int64_t c = threadIdx.x; c < cols; c += kThreads) m = fmaxf(m, xr[c]);
+    m = block_reduce<true>(m, red);
+    float s = 0.0f;
+    for (int64_t c = threadIdx.x; c < cols; c += kThreads) s += expf(xr[c] - m);
+    s = block_reduce<false>(s, red);
+    for (int64_t c = threadIdx.x; c < cols; c += kThreads) y[r * cols + c] = expf(xr[c] - m) / s;
+}
+
+// MaxPool 2-D, begin pads, padded taps skipped. E4M3: max of decoded values,
+// the output byte is the winning input byte (scale > 0 keeps the order).
+template <bool E4M3, bool NHWC>
+__global__ void __launch_bounds__(kThreads) k_maxpool(const void *__restrict__ xv, int64_t NC, int64_t C, int64_t H,
+                                                      int64_t W, int kH, int kW, int sH, int sW, int pH, int pW,
+                                                      int64_t oH, int64_t oW, void *__restrict__ yv) {
+    const int64_t total = NC * oH * oW;
+    const int64_t tid = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    const int64_t nt = static_cast<int64_t>(gridDim.x) * blockDim.x;
+    for (int64_t o = tid; o < total; o += nt) {
+        int64_t p, oh, ow, n = 0, c = 0;
+        if (NHWC) {  // o = ((n * oH + oh) * oW + ow) * C + c
+            c = o % C;
+            int64_t t = o / C;
+            ow = t % oW;
+            t /= oW;
+            oh = t % oH;
+            n = t / oH;
+            p = n * C + c;
+        } else {
+            ow = o % oW;
+            int64_t t = o / oW;
+            oh = t % oH;
+            p = t / oH;
+        }
+        float best = -INFINITY;
+        uint8_t best_b = 0;
+        bool found = false;
+        for (int kh = 0; kh < kH; ++kh) {
+            const int64_t ih = oh * sH + kh - pH;
+            if (ih < 0 || ih >= H) continue;
+            for (int kw = 0; kw < kW; ++kw) {
+                const int64_t iw = ow * sW + kw - pW;
+                if (iw < 0 || iw >= W) continue;
+                const int64_t idx = NHWC ? ((n * H + ih) * W + iw) * C + c : (p * H + ih) * W + iw;
+                if (E4M3) {
+                    const uint8_t b = reinterpret_cast<const uint8_t *>(xv)[idx];
+                    const float v = e4m3_decode(b);
+                    if (!found || v > best) {
+                        best = v;
+                        best_b = b;
+                        found = true;
+                    }
+                } else {
+                    best = fmaxf(best, reinterpret_cast<const float *>(xv)[idx]);
+                }
+            }
+        }
+        if (E4M3) reinterpret_cast<uint8_t *>(yv)[o] = best_b;
+        else reinterpret_cast<float *>(yv)[o] = best;
+    }
+}
+
+template <int DT>
+__device__ __forceinline__ float load_elem(const void *x, int64_t i) {
+    if (DT == LCML_DTYPE_FLOAT) return reinterpret_cast<const float *>(x)[i];
+    if (DT == LCML_DTYPE_BFLOAT16) return __bfloat162float(reinterpret_cast<const __nv_bfloat16 *>(x)[i]);
+    return e4m3_decode(reinterpret_cast<const uint8_t *>(x)[i]);
+}
+
+// GlobalAveragePool: NCHW -> one CTA per (n, c) plane; NHWC -> one thread per (n, c), strided over HW.
+template <int DT>
+__global__ void __launch_bounds__(kThreads) k_gap_nchw(const void *__restrict__ x, const float *__restrict__ xs,
+                                                       int64_t HW, float *__restrict__ y) {
+    __shared__ float red[32];
+    const int64_t p = blockIdx.x;
+    float s = 0.0f;
+    for (int64_t i = threadIdx.x; i < HW; i += kThreads) s += load_elem<DT>(x, p * HW + i);
+    s = block_reduce<false>(s, red);
+    const float scale = (DT == LCML_DTYPE_FLOAT8E4M3FN) ? __ldg(xs) : 1.0f;
+    if (threadIdx.x == 0) y[p] = (s * scale) / static_cast<float>(HW);
+}
+
+template <int DT>
+__global__ void __launch_bounds__(kThreads) k_gap_nhwc(const void *__restrict__ x, const float *__restrict__ xs,
+                                                       int64_t N, int64_t C, int64_t HW, float *__restrict__ y) {
+    const int64_t tid = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (tid >= N * C) return;
+    const int64_t n = tid / C, c = tid % C;
+    float s = 0.0f;
+    for (int64_t i = 0; i < HW; ++i) s += load_elem<DT>(x, (n * HW + i) * C + c);
+    const float scale = (DT == LCML_DTYPE_FLOAT8E4M3FN) ? __ldg(xs) : 1.0f;
+    y[tid] = (s * scale) / static_cast<float>(HW);
+}
+
+__global__ void __launch_bounds__(kThreads) k_cast_f32_bf16(const float *__restrict__ x, __nv_bfloat16 *__restrict__ y,
+                                                            int64_t n) {
+    const int64_t tid = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    const int64_t nt = static_cast<int64_t>(gridDim.x) * blockDim.x;
+    for (int64_t i = tid; i < n; i += nt) y[i] = __float2bfloat16_rn(x[i]);
+}
+
+__global__ void __launch_bounds__(kThreads) k_cast_bf16_f32(const __nv_bfloat16 *__restrict__ x, float *__restrict__ y,
+                                                            int64_t n) {
+    const int64_t tid = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    const int64_t nt = static_cast<int64_t>(gridDim.x) * blockDim.x;
+    for (int64_t i = tid; i < n; i += nt) y[i] = __bfloat162float(x[i]);
+}
+
+}// namespace
+}// namespace lcml
+
+using namespace lcml;
+
+extern "C" {
+
+int lcml_unary_f32(int op, const float *x, float *y, int64_t n, lcml_stream_t stream) {
+    LCML_CHECK_ARG(op >= 0 && op <= 2, "lcml_unary_f32: op %d unknown", op);
+    LCML_CHECK_ARG(n >= 0, "lcml_unary_f32: negative n");
+    if (n == 0) return LCML_OK;
+    LCML_CHECK_ARG(x && y, "lcml_unary_f32: null pointer");
+    const int vec = aligned(x, 16) && aligned(y, 16);
+    const int g = grid_for((n >> 2) + 1);
+    cudaStream_t st = to_cuda(stream);
+    if (op == 0) k_unary<0><<<g, kThreads, 0, st>>>(x, y, n, vec);
+    else if (op == 1) k_unary<1><<<g, kThreads, 0, st>>>(x, y, n, vec);
+    else k_unary<2><<<g, kThreads, 0, st>>>(x, y, n, vec);
+    LCML_LAUNCHED("unary");
+    return LCML_OK;
+}
+
+int lcml_binary_f32(int op, const float *a, const float *b, int64_t n, int64_t b_n, float *y, lcml_stream_t stream) {
+    LCML_CHECK_ARG(op >= 0 && op <= 3, "lcml_binary_f32: op %d unknown", op);
+    LCML_CHECK_ARG(n >= 0 && b_n >= 1, "lcml_binary_f32: bad extents");
+    if (n == 0) return LCML_OK;
+    LCML_CHECK_ARG(n % b_n == 0, "lcml_binary_f32: b (%lld) does not broadcast over a (%lld)", (long long)b_n,
+                   (long long)n);
+    LCML_CHECK_ARG(a && b && y, "lcml_binary_f32: null pointer");
+    const int vec = aligned(a, 16) && aligned(b, 16) && aligned(y, 16) && (b_n == 1 || b_n % 4 == 0);
+    const int g = grid_for((n >> 2) + 1);
+    cudaStream_t st = to_cuda(stream);
+    switch (op) {
+        case 0: k_binary<0><<<g, kThreads, 0, st>>>(a, b, y, n, b_n, vec); break;
+        case 1: k_binary<1><<<g, kThreads, 0, st>>>(a, b, y, n, b_n, vec); break;
+        case 2: k_binary<2><<<g, kThreads, 0, st>>>(a, b, y, n, b_n, vec); break;
+        default: k_binary<3><<<g, kThreads, 0, st>>>(a, b, y, n, b_n, vec); break;
+    }
+    LCML_LAUNCHED("binary");
+    return LCML_OK;
+}
+
+int lcml_reduce_max_rows(const float *x, int64_t rows, int64_t cols, int abs_first, float *y, lcml_stream_t stream) {
+    LCML_CHECK_ARG(rows >= 0 && cols >= 1, "lcml_reduce_max_rows: bad extents");
+    if (rows == 0) return LCML_OK;
+    LCML_CHECK_ARG(rows <= 0x7fffffff, "lcml_reduce_max_rows: too many rows");
+    LCML_CHECK_ARG(x && y, "lcml_reduce_max_rows: null pointer");
+    k_reduce_max_rows<<<static_cast<unsigned>(rows), kThreads, 0, to_cuda(stream)>>>(x, cols, abs_first, y);
+    LCML_LAUNCHED("reduce_max_rows");
+    return LCML_OK;
+}
+
+int lcml_softmax_rows(const float *x, int64_t rows, int64_t cols, float *y, lcml_stream_t stream) {
+    LCML_CHECK_ARG(rows >= 0 && cols >= 1, "lcml_softmax_rows: bad extents");
+    if (rows == 0) return LCML_OK;
+    LCML_CHECK_ARG(rows <= 0x7fffffff, "lcml_softmax_rows: too many rows");
+    LCML_CHECK_ARG(x && y, "lcml_softmax_rows: null pointer");
+    k_softmax_rows<<<static_cast<unsigned>(rows), kThreads, 0, to_cuda(stream)>>>(x, cols, y);
+    LCML_LAUNCHED("softmax_rows");
+    return LCML_OK;
+}
+
+int lcml_maxpool2d(const void *x, int elem_dtype, int64_t NC, int64_t H, int64_t W, int kH, int kW, int sH, int sW,
+                   int pH, int pW, int64_t oH, int64_t oW, void *y, int x_nhwc, int64_t C, lcml_stream_t stream) {
+    LCML_CHECK_ARG(elem_dtype == LCML_DTYPE_FLOAT || elem_dtype == LCML_DTYPE_FLOAT8E4M3FN,
+                   "lcml_maxpool2d: dtype %d unsupported", elem_dtype);
+    LCML_CHECK_ARG(NC >= 0 && H > 0 && W > 0 && kH > 0 && kW > 0 && sH > 0 && sW > 0 && oH >= 0 && oW >= 0,
+                   "lcml_maxpool2d: bad geometry");
+    LCML_CHECK_ARG(!x_nhwc || (C > 0 && NC % C == 0), "lcml_maxpool2d: NHWC needs C dividing NC");
+    const int64_t total = NC * oH * oW;
+    if (total == 0) return LCML_OK;
+    LCML_CHECK_ARG(x && y, "lcml_maxpool2d: null pointer");
+    const int g = grid_for(total);
+    cudaStream_t st = to_cuda(stream);
+    const bool e4 = elem_dtype == LCML_DTYPE_FLOAT8E4M3FN;
+    if (e4 && x_nhwc) k_maxpool<true, true><<<g, kThreads, 0, st>>>(x, NC, C, H, W, kH, kW, sH, sW, pH, pW, oH, oW, y);
+    else if (e4) k_maxpool<true, false><<<g, kThreads, 0, st>>>(x, NC, C, H, W, kH, kW, sH, sW, pH, pW, oH, oW, y);
+    else if (x_nhwc) k_maxpool<false, true><<<g, kThreads, 0, st>>>(x, NC, C, H, W, kH, kW, sH, sW, pH, pW, oH, oW, y);
+    else k_maxpool<false, false><<<g, kThreads, 0, st>>>(x, NC, C, H, W, kH, kW, sH, sW, pH, pW, oH, oW, y);
+    LCML_LAUNCHED("maxpool2d");
+    return LCML_OK;
+}
+
+int lcml_global_avgpool(const void *x, int elem_dtype, const float *x_scale, int64_t N, int64_t C, int64_t HW,
+                        int x_nhwc, float *y, lcml_stream_t stream) {
+    LCML_CHECK_ARG(elem_dtype == LCML_DTYPE_FLOAT || elem_dtype == LCML_DTYPE_BFLOAT16 ||
+                       elem_dtype == LCML_DTYPE_FLOAT8E4M3FN,
+                   "lcml_global_avgpool: dtype %d unsupported", elem_dtype);
+    LCML_CHECK_ARG(N >= 0 && C >= 0 && HW > 0, "lcml_global_avgpool: bad extents");
+    LCML_CHECK_ARG(elem_dtype != LCML_DTYPE_FLOAT8E4M3FN || x_scale, "lcml_global_avgpool: e4m3 input needs x_scale");
+    if (N * C == 0) return LCML_OK;
+    LCML_CHECK_ARG(x && y, "lcml_global_avgpool: null pointer");
+    cudaStream_t st = to_cuda(stream);
+    if (!x_nhwc) {
+        LCML_CHECK_ARG(N * C <= 0x7fffffff, "lcml_global_avgpool: too many planes");
+        const unsigned g = static_cast<unsigned>(N * C);
+        if (elem_dtype == LCML_DTYPE_FLOAT) k_gap_nchw<LCML_DTYPE_FLOAT><<<g, kThreads, 0, st>>>(x, x_scale, HW, y);
+        else if (elem_dtype == LCML_DTYPE_BFLOAT16) k_gap_nchw<LCML_DTYPE_BFLOAT16><<<g, kThreads, 0, st>>>(x, x_scale, HW, y);
+        else k_gap_nchw<LCML_DTYPE_FLOAT8E4M3FN><<<g, kThreads, 0, st>>>(x, x_scale, HW, y);
+    } else {
+        const unsigned g = static_cast<unsigned>((N * C + kThreads - 1) / kThreads);
+        if (elem_dtype == LCML_DTYPE_FLOAT) k_gap_nhwc<LCML_DTYPE_FLOAT><<<g, kThreads, 0, st>>>(x, x_scale, N, C, HW, y);
+        else if (elem_dtype == LCML_DTYPE_BFLOAT16) k_gap_nhwc<LCML_DTYPE_BFLOAT16><<<g, kThreads, 0, st>>>(x, x_scale, N, C, HW, y);
+        else k_gap_nhwc<LCML_DTYPE_FLOAT8E4M3FN><<<g, kThreads, 0, st>>>(x, x_scale, N, C, HW, y);
+    }
+    LCML_LAUNCHED("global_avgpool");
+    return LCML_OK;
+}
+
+int lcml_cast(const void *x, int x_dtype, void *y, int y_dtype, int64_t n, lcml_stream_t stream) {
+    LCML_CHECK_ARG(n >= 0, "lcml_cast: negative n");
+    if (n == 0) return LCML_OK;
+    LCML_CHECK_ARG(x && y, "lcml_cast: null pointer");
+    cudaStream_t st = to_cuda(stream);
+    if (x_dtype == LCML_DTYPE_FLOAT && y_dtype == LCML_DTYPE_BFLOAT16) {
+        k_cast_f32_bf16<<<grid_for(n), kThreads, 0, st>>>(static_cast<const float *>(x), static_cast<__nv_bfloat16 *>(y), n);
+    } else if (x_dtype == LCML_DTYPE_BFLOAT16 && y_dtype == LCML_DTYPE_FLOAT) {
+        k_cast_bf16_f32<<<grid_for(n), kThreads, 0, st>>>(static_cast<const __nv_bfloat16 *>(x), static_cast<float *>(y), n);
+    } else {
+        return set_error(LCML_ERR_UNSUPPORTED, "lcml_cast: %d -> %d unsupported (e4m3 goes through QuantizeLinear)",
+                         x_dtype, y_dtype);
+    }
+    LCML_LAUNCHED("cast");
+    return LCML_OK;
+}
+
+}// extern "C"

@@ -1,0 +1,247 @@
+// Device-side building blocks shared by every kernel of the FP8 operator path:
+// the bit-exact e4m3 codec, bounded mbarrier waits, TMA and tcgen05 wrappers.
+// sm_100a only.
+#pragma once
+
+#include <cstdint>
+#include <cuda_runtime.h>
+
+namespace lcml {
+
+// ---------------------------------------------------------------------------
+// Device error word. A kernel that gives up on a bounded wait records the
+// reason here and returns; the host reads and clears it via
+// lcml_device_error(). Nothing in this library traps.
+// ---------------------------------------------------------------------------
+enum DeviceError : int {
+    kDevOk = 0,
+    kDevTimeoutProducer = 1,   // TMA producer waited too long for a free stage
+    kDevTimeoutMma = 2,        // MMA issuer waited too long for a loaded stage
+    kDevTimeoutEpilogue = 3,   // epilogue waited too long for an accumulator
+    kDevTimeoutDrain = 4,      // final drain of in-flight copies timed out
+};
+
+// The word lives in runtime.cu; kernels receive its device address as a
+// parameter (lcml::device_error_word()), so no relocatable device code is needed.
+__device__ __forceinline__ void record_device_error(int *err, int code) {
+    if (err) atomicCAS(err, 0, code);
+}
+
+// ~2 s at the B200's 1.965 GHz boost clock: far above any legitimate wait in
+// this library (the largest GEMM runs well under 100 ms).
+constexpr long long kWaitLimitCycles = 4000000000LL;
+
+// ---------------------------------------------------------------------------
+// e4m3 codec (FP8 E4M3FN), bit-exact with the reference's CPU codec
+// FP8E4M3FN::from_float / to_float (include/onnx/fp_quantized.h:149-249):
+//   NaN -> 0x7f; +-0 -> 0x00; |v| > 448 (inf included) -> +-448;
+//   round-to-nearest-even; a nonzero value that rounds to zero keeps its sign.
+// Integer-only for normal results: adding 0x7ffff plus the lowest kept bit and
+// shifting by 20 is RNE on 3 mantissa bits, and a carry moves into the
+// exponent field by itself. Subnormal results are RNE(|v| * 2^9) in [0, 8],
+// where 8 is exactly the smallest normal code 0x08.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ uint32_t e4m3_encode(float v) {
+    const uint32_t u = __float_as_uint(v);
+    const uint32_t sign = (u >> 24) & 0x80u;
+    const uint32_t a = u & 0x7fffffffu;
+    if (a > 0x7f800000u) return 0x7fu;              // NaN
+    if (a == 0u) return 0u;                         // +-0 -> 0x00
+    if (a > 0x43e00000u) return sign | 0x7eu;       // > 448 saturates
+    uint32_t r;
+    if (a >= 0x3c800000u) {                         // >= 2^-6: normal result
+        r = ((a + 0x7ffffu + ((a >> 20) & 1u)) >> 20) - (120u << 3);
+    } else {                                        // subnormal or zero result
+        r = __float2uint_rn(__uint_as_float(a) * 512.0f);
+    }
+    return sign | r;
+}
+
+__device__ __forceinline__ float e4m3_decode(uint32_t b) {
+    const uint32_t sign = (b & 0x80u) << 24;
+    const uint32_t e = (b >> 3) & 0xfu;
+    const uint32_t m = b & 0x7u;
+    if ((b & 0x7fu) == 0x7fu) return __uint_as_float(0x7fc00000u);
+    float v = (e == 0u) ? float(m) * 0.001953125f : __uint_as_float(((e + 120u) << 23) | (m << 20));
+    return __uint_as_float(__float_as_uint(v) | sign);
+}
+
+// QuantizeLinear of one element: e4m3(x / s) with an IEEE round-to-nearest divide.
+__device__ __forceinline__ uint32_t quantize1(float x, float s) {
+    return e4m3_encode(__fdiv_rn(x, s));
+}
+
+// amax -> scale for every dynamic mode: amax / 448, or 1 when amax is 0.
+__device__ __forceinline__ float scale_from_amax(float amax) {
+    return amax > 0.0f ? __fdiv_rn(amax, 448.0f) : 1.0f;
+}
+
+// |x| as an integer that orders like the float; NaN maps to 0 (ignored).
+__device__ __forceinline__ uint32_t abs_bits_nan0(float x) {
+    uint32_t a = __float_as_uint(x) & 0x7fffffffu;
+    return a > 0x7f800000u ? 0u : a;
+}
+
+// ---------------------------------------------------------------------------
+// Shared memory / mbarrier helpers
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ uint32_t smem_u32(const void *p) {
+    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t *bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
+
+__device__ __forceinline__ void fence_mbar_init() {
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t *bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.release.cta.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)),
+                 "r"(bytes)
+                 : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(uint64_t *bar) {
+    asm volatile("mbarrier.arrive.release.cta.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    return ok != 0u;
+}
+
+// Bounded wait for the phase with the given parity to complete. Returns false
+// (and records `err` in *err_word) after kWaitLimitCycles instead of spinning forever.
+__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, int *err_word, int err) {
+    if (mbar_try_wait(bar, parity)) return true;
+    const long long t0 = clock64();
+    while (!mbar_try_wait(bar, parity)) {
+        if (clock64() - t0 > kWaitLimitCycles) {
+            record_device_error(err_word, err);
+            return false;
+        }
+    }
+    return true;
+}
+
+// ---------------------------------------------------------------------------
+// TMA (cp.async.bulk.tensor), no multicast anywhere in this library.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void tma_load_2d(const void *tmap, uint64_t *bar, void *smem_dst, int x, int y) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], [%2];" ::"r"(
+            smem_u32(smem_dst)),
+        "l"(tmap), "r"(smem_u32(bar)), "r"(x), "r"(y)
+        : "memory");
+}
+
+__device__ __forceinline__ void tma_prefetch_desc(const void *tmap) {
+    asm volatile("prefetch.tensormap [%0];" ::"l"(tmap) : "memory");
+}
+
+// ---------------------------------------------------------------------------
+// tcgen05 (5th-generation tensor cores, accumulators in TMEM)
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void tmem_alloc(uint32_t *dst_smem, uint32_t ncols) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(dst_smem)),
+                 "r"(ncols)
+                 : "memory");
+}
+
+__device__ __forceinline__ void tmem_relinquish() {
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+
+__device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
+
+__device__ __forceinline__ void tc_fence_before() {
+    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+}
+
+__device__ __forceinline__ void tc_fence_after() {
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+
+// D[tmem] (+)= A[smem] * B[smem]^T, e4m3 x e4m3 -> f32, shape from `idesc`.
+__device__ __forceinline__ void umma_f8f6f4(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                            uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f8f6f4 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+
+// Arrive once on `bar` when every tcgen05.mma issued so far by this thread completes.
+__device__ __forceinline__ void umma_commit(uint64_t *bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                     smem_u32(bar))
+                 : "memory");
+}
+
+__device__ __forceinline__ void tmem_wait_ld() {
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+// 32 lanes x 32-bit, 32 consecutive columns: thread i of the warp receives
+// row (lane_base + i), columns [col, col + 32).
+__device__ __forceinline__ void tmem_ld_32x32b_x32(uint32_t taddr, uint32_t (&r)[32]) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+        "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, "
+        "%16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+          "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]),
+          "=r"(r[23]), "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]),
+          "=r"(r[30]), "=r"(r[31])
+        : "r"(taddr)
+        : "memory");
+}
+
+// Shared-memory matrix descriptor, K-major operand staged by TMA with the
+// 128-byte swizzle: rows 128 B apart, 8-row groups 1024 B apart (SBO), tile
+// base 1024-byte aligned. Fields: start>>4 [0,14), LBO>>4 [16,30) (unused for
+// swizzled K-major, set to 1), SBO>>4 [32,46), version 1 [46,48),
+// layout SWIZZLE_128B = 2 at [61,64).
+__device__ __forceinline__ uint64_t sdesc_kmajor_sw128(uint32_t smem_addr) {
+    uint64_t d = 0;
+    d |= static_cast<uint64_t>((smem_addr & 0x3ffffu) >> 4);
+    d |= static_cast<uint64_t>(1u) << 16;
+    d |= static_cast<uint64_t>(1024u >> 4) << 32;
+    d |= static_cast<uint64_t>(1u) << 46;
+    d |= static_cast<uint64_t>(2u) << 61;
+    return d;
+}
+
+// Instruction descriptor for kind::f8f6f4: D f32 [4,6)=1, A/B e4m3 [7,10)=[10,13)=0,
+// A K-major [15]=0, B major [16], N>>3 [17,23), M>>4 [24,29).
+__host__ __device__ constexpr uint32_t idesc_e4m3_f32(uint32_t M, uint32_t N, uint32_t b_mn_major) {
+    return (1u << 4) | (b_mn_major << 16) | ((N >> 3) << 17) | ((M >> 4) << 24);
+}
+
+__device__ __forceinline__ uint32_t lane_id() { return threadIdx.x & 31u; }
+
+__device__ __forceinline__ bool elect_one() {
+    uint32_t pred = 0;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "elect.sync _|p, 0xffffffff;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(pred));
+    return pred != 0u;
+}
+
+}// namespace lcml

@@ -1,0 +1,54 @@
+// Host-side helpers shared by the C-ABI translation units: error reporting,
+// argument checks and the launch counter. Internal to liblcml_fp8.so.
+#pragma once
+
+#include <atomic>
+#include <cstdarg>
+#include <cstdint>
+#include <cstdio>
+#include <string>
+
+#include <cuda_runtime.h>
+
+#include "../../include/lcml_fp8.h"
+
+namespace lcml {
+
+int set_error(int status, const char *fmt, ...) __attribute__((format(printf, 2, 3)));
+void clear_error();
+
+// Kernels launched by this library (lcml_launch_count()).
+extern std::atomic<uint64_t> g_launches;
+
+inline cudaStream_t to_cuda(lcml_stream_t s) { return reinterpret_cast<cudaStream_t>(s); }
+
+// Number of SMs of the current device (cached per device).
+int sm_count();
+
+// Device address of the error word on the current device (nullptr if unavailable).
+int *device_error_word();
+
+__host__ __device__ inline bool aligned(const void *p, uintptr_t a) { return (reinterpret_cast<uintptr_t>(p) & (a - 1)) == 0; }
+
+}// namespace lcml
+
+#define LCML_CHECK_ARG(cond, ...)                                                  \
+    do {                                                                           \
+        if (!(cond)) return ::lcml::set_error(LCML_ERR_INVALID_ARGUMENT, __VA_ARGS__); \
+    } while (0)
+
+// Reports the launch error (if any) of the kernel just enqueued.
+#define LCML_LAUNCHED(name)                                                                        \
+    do {                                                                                           \
+        ::lcml::g_launches.fetch_add(1, std::memory_order_relaxed);                                \
+        cudaError_t e_ = cudaGetLastError();                                                       \
+        if (e_ != cudaSuccess)                                                                     \
+            return ::lcml::set_error(LCML_ERR_CUDA, "%s launch failed: %s", name, cudaGetErrorString(e_)); \
+    } while (0)
+
+#define LCML_CUDA(call)                                                                           \
+    do {                                                                                          \
+        cudaError_t e_ = (call);                                                                  \
+        if (e_ != cudaSuccess)                                                                    \
+            return ::lcml::set_error(LCML_ERR_CUDA, "%s failed: %s", #call, cudaGetErrorString(e_)); \
+    } while (0)

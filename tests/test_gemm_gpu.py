@@ -1,0 +1,197 @@
+"""FP8 GEMM (tcgen05 kernel and SIMT kernel) vs the CPU oracle.
+
+The oracle dequantizes both e4m3 operands (DequantizeLinear) and runs
+gemm.cpp's fp32 K-ordered fma loop; outputs must agree within rtol 2e-3 /
+atol 1e-3 (fp32 and bf16 outputs). e4m3 outputs must decode to within one
+e4m3 rounding step of the oracle's fp32 value.
+"""
+import numpy as np
+import pytest
+
+import oracle
+from conftest import assert_close
+
+pytestmark = pytest.mark.gpu
+
+
+def _t(a, dev):
+    import torch
+    return torch.from_numpy(np.ascontiguousarray(a)).to(dev)
+
+
+def make_operands(M, N, K, seed, per_row=False, per_col=False, b_std=1.0):
+    rng = np.random.default_rng(seed)
+    A = rng.standard_normal((M, K)).astype(np.float32)
+    B = (rng.standard_normal((N, K)) * b_std).astype(np.float32)  # [N, K] = Gemm transB=1
+    if per_row:
+        Aq, sa = oracle.quantize_dynamic_rows(A)
+    else:
+        sa = np.float32([oracle.scale_from_amax(oracle.amax(A))])
+        Aq = oracle.quantize(A, sa[0])
+    if per_col:
+        sb = np.array([oracle.scale_from_amax(oracle.amax(B[n])) for n in range(N)], dtype=np.float32)
+        Bq = oracle.quantize(B, sb, axis=0)
+    else:
+        sb = np.float32([oracle.scale_from_amax(oracle.amax(B))])
+        Bq = oracle.quantize(B, sb[0])
+    return Aq, sa, Bq, sb
+
+
+SHAPES = [
+    (128, 256, 128),     # exactly one tile
+    (200, 300, 160),     # ragged M, N, K (BN=128 kernel, TMA zero fill)
+    (256, 2048, 512),    # BN=256 kernel, several k-blocks
+    (32, 512, 784),      # MLP layer 1 (K = 784, not a multiple of 128)
+    (1, 4096, 4096),     # skinny decode
+    (16, 4096, 4096),
+    (1000, 1000, 1000),  # K % 128 != 0, N < 2048
+    (1024, 2048, 1024),
+]
+
+
+@pytest.mark.parametrize("M,N,K", SHAPES)
+@pytest.mark.parametrize("out", ["bf16", "f32"])
+def test_gemm_shapes(dev, M, N, K, out):
+    import torch
+    import luisaml_b200 as lb
+    Aq, sa, Bq, sb = make_operands(M, N, K, seed=M * 31 + N * 7 + K)
+    ref = oracle.qdq_gemm(Aq, sa, Bq, sb, b_kmajor=True)
+    Y = lb.gemm(_t(Aq, dev), _t(Bq, dev), _t(sa, dev), _t(sb, dev),
+                out_dtype=torch.bfloat16 if out == "bf16" else torch.float32)
+    assert_close(Y.float().cpu().numpy(), ref, what=f"gemm {M}x{N}x{K} {out}")
+    assert lb.device_error() == 0
+
+
+@pytest.mark.parametrize("per_row,per_col", [(True, False), (False, True), (True, True)])
+def test_gemm_scale_modes(dev, per_row, per_col):
+    import torch
+    import luisaml_b200 as lb
+    M, N, K = 300, 512, 256
+    Aq, sa, Bq, sb = make_operands(M, N, K, seed=5, per_row=per_row, per_col=per_col, b_std=0.02)
+    ref = oracle.qdq_gemm(Aq, sa, Bq, sb)
+    Y = lb.gemm(_t(Aq, dev), _t(Bq, dev), _t(sa, dev), _t(sb, dev), out_dtype=torch.float32)
+    assert_close(Y.cpu().numpy(), ref, what="scale modes")
+
+
+def test_gemm_bias_relu_alpha_beta(dev):
+    import torch
+    import luisaml_b200 as lb
+    M, N, K = 96, 640, 384
+    Aq, sa, Bq, sb = make_operands(M, N, K, seed=9)
+    bias = np.random.default_rng(1).standard_normal(N).astype(np.float32)
+    ref = oracle.qdq_gemm(Aq, sa, Bq, sb)
+    ref = np.maximum(0.5 * ref + 2.0 * bias, 0.0)
+    Y = lb.gemm(_t(Aq, dev), _t(Bq, dev), _t(sa, dev), _t(sb, dev), alpha=0.5, beta=2.0, c_vec=_t(bias, dev),
+                epilogue=lb.EPI_RELU, out_dtype=torch.float32)
+    assert_close(Y.cpu().numpy(), ref, what="bias+relu")
+
+
+def test_gemm_residual_and_row_amax(dev):
+    import torch
+    import luisaml_b200 as lb
+    M, N, K = 256, 512, 256
+    Aq, sa, Bq, sb = make_operands(M, N, K, seed=13)
+    res = np.random.default_rng(2).standard_normal((M, N)).astype(np.float32)
+    ref = oracle.qdq_gemm(Aq, sa, Bq, sb) + res
+    amax = torch.zeros(M, dtype=torch.float32, device=dev)
+    Y = lb.gemm(_t(Aq, dev), _t(Bq, dev), _t(sa, dev), _t(sb, dev), c_mat=_t(res, dev), out_dtype=torch.float32,
+                row_amax=amax)
+    y = Y.cpu().numpy()
+    assert_close(y, ref, what="residual")
+    assert np.array_equal(amax.cpu().numpy(), np.abs(y).max(axis=1))
+
+
+def test_gemm_silu_mul(dev):
+    import torch
+    import luisaml_b200 as lb
+    M, F, K = 200, 384, 256  # F = ffn width; B holds 2F rows (gate/up interleaved by 128)
+    rng = np.random.default_rng(17)
+    Aq, sa = oracle.quantize_dynamic_rows(rng.standard_normal((M, K)).astype(np.float32))
+    Wg = (rng.standard_normal((F, K)) * 0.05).astype(np.float32)
+    Wu = (rng.standard_normal((F, K)) * 0.05).astype(np.float32)
+    sg = np.array([oracle.scale_from_amax(oracle.amax(r)) for r in Wg], dtype=np.float32)
+    su = np.array([oracle.scale_from_amax(oracle.amax(r)) for r in Wu], dtype=np.float32)
+    Gq, Uq = oracle.quantize(Wg, sg, axis=0), oracle.quantize(Wu, su, axis=0)
+    g = oracle.qdq_gemm(Aq, sa, Gq, sg)
+    u = oracle.qdq_gemm(Aq, sa, Uq, su)
+    ref = oracle.silu_mul(g, u)
+    # interleave [gate 128 rows; up 128 rows] per group
+    Bq = np.concatenate([np.concatenate([Gq[i:i + 128], Uq[i:i + 128]]) for i in range(0, F, 128)])
+    sb = np.concatenate([np.concatenate([sg[i:i + 128], su[i:i + 128]]) for i in range(0, F, 128)])
+    amax = torch.zeros(M, dtype=torch.float32, device=dev)
+    for simt in (False, True):
+        amax.zero_()
+        Y = lb.gemm(_t(Aq, dev), _t(Bq, dev), _t(sa, dev), _t(sb, dev), epilogue=lb.EPI_SILU_MUL,
+                    out_dtype=torch.float32, row_amax=amax, simt=simt)
+        y = Y.cpu().numpy()
+        assert y.shape == (M, F)
+        assert_close(y, ref, what=f"silu_mul simt={simt}")
+        assert np.array_equal(amax.cpu().numpy(), np.abs(y).max(axis=1))
+
+
+def test_gemm_e4m3_output(dev):
+    import torch
+    import luisaml_b200 as lb
+    M, N, K = 128, 512, 512
+    Aq, sa, Bq, sb = make_operands(M, N, K, seed=23)
+    ref = oracle.qdq_gemm(Aq, sa, Bq, sb)
+    ys = np.float32([oracle.scale_from_amax(np.abs(ref).max())])
+    Y = lb.gemm(_t(Aq, dev), _t(Bq, dev), _t(sa, dev), _t(sb, dev), out_dtype=torch.uint8, y_scale=_t(ys, dev))
+    got = oracle.e4m3_decode(Y.cpu().numpy())
+    want = oracle.e4m3_decode(oracle.quantize(ref, ys[0]))
+    # one e4m3 step is at most 2^-3 relative (normal) or 2^-9 absolute (subnormal) of x / s
+    step = np.maximum(np.abs(want) * 0.125, 2.0 ** -9)
+    assert (np.abs(got - want) <= step + 1e-12).all()
+    assert (got == want).mean() > 0.99
+
+
+@pytest.mark.parametrize("M,N,K", [(200, 300, 160), (64, 1024, 128)])
+def test_simt_and_tensor_core_paths_agree(dev, M, N, K):
+    import torch
+    import luisaml_b200 as lb
+    Aq, sa, Bq, sb = make_operands(M, N, K, seed=3)
+    a, b, s1, s2 = _t(Aq, dev), _t(Bq, dev), _t(sa, dev), _t(sb, dev)
+    y_tc = lb.gemm(a, b, s1, s2, out_dtype=torch.float32).cpu().numpy()
+    y_simt = lb.gemm(a, b, s1, s2, out_dtype=torch.float32, simt=True).cpu().numpy()
+    assert_close(y_tc, y_simt, rtol=1e-5, atol=1e-4, what="tc vs simt")
+
+
+def test_mn_major_b_uses_matmul_layout(dev):
+    import torch
+    import luisaml_b200 as lb
+    M, N, K = 100, 200, 96
+    Aq, sa, Bq, sb = make_operands(M, N, K, seed=29)
+    ref = oracle.qdq_gemm(Aq, sa, Bq, sb)
+    Bkn = np.ascontiguousarray(Bq.T)  # MatMul's [K, N]
+    Y = lb.gemm(_t(Aq, dev), _t(Bkn, dev), _t(sa, dev), _t(sb, dev), b_kmajor=False, out_dtype=torch.float32)
+    assert_close(Y.cpu().numpy(), ref, what="[K,N] B")
+
+
+def test_large_8192_sampled_rows(dev):
+    """The bench configuration (M=N=K=8192): sampled rows against the oracle,
+    plus a size-independent check: row sums equal A_row . (sum of B rows)."""
+    import torch
+    import luisaml_b200 as lb
+    M = N = K = 8192
+    g = torch.Generator(device=dev).manual_seed(0)
+    A = torch.randn(M, K, device=dev, generator=g)
+    B = torch.randn(N, K, device=dev, generator=g)
+    sa = lb.amax(A)
+    sa = torch.where(sa > 0, sa / 448.0, torch.ones_like(sa))
+    sb = lb.amax(B)
+    sb = torch.where(sb > 0, sb / 448.0, torch.ones_like(sb))
+    Aq, Bq = lb.quantize(A, sa), lb.quantize(B, sb)
+    Y = lb.gemm(Aq, Bq, sa, sb, out_dtype=torch.float32)
+    torch.cuda.synchronize()
+    assert lb.device_error() == 0
+    Aqh, Bqh = Aq.cpu().numpy(), Bq.cpu().numpy()
+    sah, sbh = sa.cpu().numpy(), sb.cpu().numpy()
+    for r0 in (0, 4093, 8160):
+        ref = oracle.qdq_gemm(Aqh, sah, Bqh, sbh, rows=(r0, r0 + 32))
+        assert_close(Y[r0:r0 + 32].cpu().numpy(), ref, what=f"8192^3 rows {r0}..")
+    # linearity: Y @ 1 == A . (B^T @ 1), in float64 from the dequantized operands
+    Ad = oracle.e4m3_decode(Aqh).astype(np.float64) * float(sah[0])
+    Bd = oracle.e4m3_decode(Bqh).astype(np.float64) * float(sbh[0])
+    want = Ad @ Bd.sum(axis=0)
+    got = Y.double().sum(dim=1).cpu().numpy()
+    np.testing.assert_allclose(got, want, rtol=1e-4, atol=1e-2)

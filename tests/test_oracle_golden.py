@@ -1,0 +1,113 @@
+"""Pins the CPU oracle (oracle/oracle.c) against the reference's own codec.
+
+The golden vectors in tests/golden/ were produced by the reference's compiled
+CPU codec (FP8E4M3FN::from_float / to_float, include/onnx/fp_quantized.h:149-249).
+Where the reference tree is present (oracle/_ref built), the restatement is
+also compared with it on all 2^32 fp32 bit patterns.
+"""
+import concurrent.futures as cf
+import ctypes
+
+import numpy as np
+import pytest
+
+import oracle
+from conftest import golden
+
+
+def test_decode_all_256_codes():
+    g = golden("e4m3_decode.npz")
+    got = oracle.e4m3_decode(g["codes"])
+    ref = g["values"]
+    nan = np.isnan(ref)
+    assert np.array_equal(np.isnan(got), nan)
+    assert np.array_equal(got[~nan].view(np.uint32), ref[~nan].view(np.uint32))  # -0.0 included
+    assert nan.sum() == 2 and nan[0x7f] and nan[0xff]
+
+
+@pytest.mark.parametrize("fixture", ["e4m3_encode_structured.npz", "e4m3_encode_random.npz"])
+def test_encode_matches_reference_bytes(fixture):
+    g = golden(fixture)
+    got = oracle.e4m3_encode(g["x"])
+    bad = np.nonzero(got != g["q"])[0]
+    assert bad.size == 0, f"{bad.size} mismatches, first x={g['x'][bad[0]]!r}"
+
+
+def test_encode_edge_semantics():
+    # the reference's documented quirks (fp_quantized.h:151-171, :213-216)
+    e = oracle.e4m3_encode
+    assert e(np.float32([-0.0]))[0] == 0x00
+    assert e(np.float32([np.nan]))[0] == 0x7f
+    assert e(np.float32([-np.nan]))[0] == 0x7f
+    assert e(np.float32([np.inf]))[0] == 0x7e and e(np.float32([-np.inf]))[0] == 0xfe
+    assert e(np.float32([464.0]))[0] == 0x7e and e(np.float32([1e9]))[0] == 0x7e
+    assert e(np.float32([-2.0 ** -10]))[0] == 0x80  # rounds to zero, keeps the sign
+    assert e(np.float32([2.0 ** -9]))[0] == 0x01
+
+
+def test_quantize_tensor_fixture():
+    g = golden("e4m3_quantize_tensor.npz")
+    got = oracle.quantize(g["x"], g["scale"])
+    assert np.array_equal(got, g["q"])
+    # the fixture's scale is amax / 448 in fp32
+    assert np.float32(np.max(np.abs(g["x"])) / np.float32(448.0)) == g["scale"]
+
+
+def test_dynamic_rows_matches_per_row_quantize():
+    rng = np.random.default_rng(7)
+    x = rng.standard_normal((33, 70)).astype(np.float32)
+    x[3] = 0.0
+    q, s = oracle.quantize_dynamic_rows(x)
+    assert s[3] == 1.0
+    for r in range(x.shape[0]):
+        assert s[r] == oracle.scale_from_amax(np.max(np.abs(x[r])))
+        assert np.array_equal(q[r], oracle.quantize(x[r], s[r]))
+
+
+def test_gemm_matches_float64_reference():
+    rng = np.random.default_rng(3)
+    A = rng.standard_normal((17, 40)).astype(np.float32)
+    B = rng.standard_normal((29, 40)).astype(np.float32)
+    C = rng.standard_normal(29).astype(np.float32)
+    Y = oracle.gemm(A, B, C, alpha=0.5, beta=2.0, transB=1)
+    ref = 0.5 * (A.astype(np.float64) @ B.T.astype(np.float64)) + 2.0 * C
+    np.testing.assert_allclose(Y, ref, rtol=1e-5, atol=1e-5)
+
+
+def test_conv_matches_direct_float64():
+    rng = np.random.default_rng(4)
+    X = rng.standard_normal((2, 4, 9, 7)).astype(np.float32)
+    W = rng.standard_normal((6, 2, 3, 3)).astype(np.float32)
+    b = rng.standard_normal(6).astype(np.float32)
+    Y = oracle.conv2d(X, W, b, strides=(2, 1), pads=(1, 1, 1, 1), group=2)
+    N, C, H, Wd = X.shape
+    ref = np.zeros(Y.shape)
+    Xp = np.pad(X.astype(np.float64), ((0, 0), (0, 0), (1, 1), (1, 1)))
+    for n in range(N):
+        for m in range(6):
+            g = m // 3
+            for oh in range(Y.shape[2]):
+                for ow in range(Y.shape[3]):
+                    patch = Xp[n, g * 2:(g + 1) * 2, oh * 2:oh * 2 + 3, ow:ow + 3]
+                    ref[n, m, oh, ow] = (patch * W[m]).sum() + b[m]
+    np.testing.assert_allclose(Y, ref, rtol=1e-5, atol=1e-5)
+
+
+def test_exhaustive_against_reference_codec():
+    """All 2^32 fp32 bit patterns: restatement == reference codec (needs oracle/_ref)."""
+    r = oracle.ref_lib()
+    if r is None:
+        pytest.skip("oracle/_ref not built (reference tree absent): golden vectors pin the oracle instead")
+    cand = ctypes.cast(oracle.lib.orc_e4m3_from_float, ctypes.c_void_p).value
+    parts = 64
+    span = (1 << 32) // parts
+
+    def run(i):
+        fb = ctypes.c_uint32(0)
+        bad = r.lcml_ref_e4m3_count_mismatch(cand, i * span, (i + 1) * span, ctypes.byref(fb))
+        return bad, fb.value
+
+    with cf.ThreadPoolExecutor(8) as ex:
+        res = list(ex.map(run, range(parts)))
+    bad = sum(b for b, _ in res)
+    assert bad == 0, f"{bad} mismatches, first at bits {[hex(f) for b, f in res if b][:3]}"
