@@ -59,17 +59,6 @@ __device__ __forceinline__ float silu_mul(float g, float u) {
     return (g * sig) * u;
 }
 
-// Scale + C for one accumulator value of output element (row, gemm column n).
-__device__ __forceinline__ float epi_pre(float acc, float row_scale, int64_t row, int64_t n, const EpiParams &ep) {
-    const float sb = ep.sb_col ? __ldg(ep.sb + n) : __ldg(ep.sb);
-    float v = acc * row_scale * sb;
-    if (ep.c_vec_mode) {
-        const float c = ep.c_vec_mode == 1 ? __ldg(ep.c_vec) : (ep.c_vec_mode == 2 ? __ldg(ep.c_vec + row) : __ldg(ep.c_vec + n));
-        v = ep.beta == 1.0f ? v + c : fmaf(ep.beta, c, v);
-    }
-    return v;
-}
-
 __device__ __forceinline__ float load_cmat(const EpiParams &ep, int64_t row, int64_t col) {
     if (ep.c_mat_bf16) return __bfloat162float(reinterpret_cast<const __nv_bfloat16 *>(ep.c_mat)[row * ep.ldc + col]);
     return reinterpret_cast<const float *>(ep.c_mat)[row * ep.ldc + col];
@@ -82,32 +71,100 @@ __device__ __forceinline__ void store_out(const EpiParams &ep, int64_t row, int6
     else reinterpret_cast<uint8_t *>(ep.y)[row * ep.ldy + col] = static_cast<uint8_t>(quantize1(v, ys));
 }
 
-// Applies the epilogue to 32 consecutive output columns [col0, col0+32) of one row.
-// For EPI != SILU, g[j] holds the accumulator of gemm column col0+j; for SILU,
-// g/u hold the gate/up accumulators whose gemm columns are ng0+j / nu0+j.
-template <int EPI, int OUT>
-__device__ __forceinline__ void epi_row32(const EpiParams &ep, int64_t row, int64_t col0, int64_t ng0, int64_t nu0,
-                                          int64_t n_out, const uint32_t (&g)[32], const uint32_t (&u)[32],
-                                          float row_scale, float ys, float &amax) {
-    float v[32];
+// Per-column factors of 32 consecutive gemm columns [n0, n0+32): the B scale
+// and beta * C broadcast along N. Loaded once per chunk as broadcast vector
+// loads (every lane reads the same addresses).
+struct ColFactors {
+    float scale[32];
+    float add[32];
+};
+
+__device__ __forceinline__ void load_col_factors(const EpiParams &ep, int64_t n0, ColFactors &f) {
+    const bool in_range = n0 + 32 <= ep.N;
+    if (ep.sb_col) {
+        if (in_range && aligned(ep.sb + n0, 16)) {
 #pragma unroll
-    for (int j = 0; j < 32; ++j) {
-        const int64_t col = col0 + j;
-        if (col < n_out) {
-            float a = epi_pre(__uint_as_float(g[j]), row_scale, row, ng0 + j, ep);
-            if (EPI == LCML_EPI_SILU_MUL) {
-                const float b = epi_pre(__uint_as_float(u[j]), row_scale, row, nu0 + j, ep);
-                a = silu_mul(a, b);
+            for (int j = 0; j < 8; ++j) {
+                const float4 v = __ldg(reinterpret_cast<const float4 *>(ep.sb + n0) + j);
+                f.scale[4 * j] = v.x;
+                f.scale[4 * j + 1] = v.y;
+                f.scale[4 * j + 2] = v.z;
+                f.scale[4 * j + 3] = v.w;
             }
-            if (ep.c_mat) a += ep.beta * load_cmat(ep, row, col);
-            if (EPI == LCML_EPI_RELU) a = fmaxf(a, 0.0f);
-            v[j] = a;
-            amax = fmaxf(amax, fabsf(a));
         } else {
-            v[j] = 0.0f;
+#pragma unroll
+            for (int j = 0; j < 32; ++j) f.scale[j] = (n0 + j < ep.N) ? __ldg(ep.sb + n0 + j) : 0.0f;
+        }
+    } else {
+        const float s = __ldg(ep.sb);
+#pragma unroll
+        for (int j = 0; j < 32; ++j) f.scale[j] = s;
+    }
+    if (ep.c_vec_mode == 3) {  // C along N
+        if (in_range && aligned(ep.c_vec + n0, 16)) {
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                const float4 v = __ldg(reinterpret_cast<const float4 *>(ep.c_vec + n0) + j);
+                f.add[4 * j] = ep.beta * v.x;
+                f.add[4 * j + 1] = ep.beta * v.y;
+                f.add[4 * j + 2] = ep.beta * v.z;
+                f.add[4 * j + 3] = ep.beta * v.w;
+            }
+        } else {
+#pragma unroll
+            for (int j = 0; j < 32; ++j) f.add[j] = (n0 + j < ep.N) ? ep.beta * __ldg(ep.c_vec + n0 + j) : 0.0f;
+        }
+    } else {
+#pragma unroll
+        for (int j = 0; j < 32; ++j) f.add[j] = 0.0f;
+    }
+}
+
+// beta * C[row, col0 .. col0+32) of the full C matrix (residual), into r[].
+__device__ __forceinline__ void load_cmat32(const EpiParams &ep, int64_t row, int64_t col0, int64_t n_out, float (&r)[32]) {
+    const bool full = col0 + 32 <= n_out;
+    if (ep.c_mat_bf16) {
+        const __nv_bfloat16 *cp = reinterpret_cast<const __nv_bfloat16 *>(ep.c_mat) + row * ep.ldc + col0;
+        if (full && aligned(cp, 16)) {
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                const uint4 w = *reinterpret_cast<const uint4 *>(cp + 8 * j);
+                const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+                for (int k = 0; k < 4; ++k) {
+                    r[8 * j + 2 * k] = __uint_as_float(ws[k] << 16);
+                    r[8 * j + 2 * k + 1] = __uint_as_float(ws[k] & 0xffff0000u);
+                }
+            }
+        } else {
+#pragma unroll
+            for (int j = 0; j < 32; ++j) r[j] = (col0 + j < n_out) ? __bfloat162float(cp[j]) : 0.0f;
+        }
+    } else {
+        const float *cp = reinterpret_cast<const float *>(ep.c_mat) + row * ep.ldc + col0;
+        if (full && aligned(cp, 16)) {
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                const float4 v = *reinterpret_cast<const float4 *>(cp + 4 * j);
+                r[4 * j] = v.x;
+                r[4 * j + 1] = v.y;
+                r[4 * j + 2] = v.z;
+                r[4 * j + 3] = v.w;
+            }
+        } else {
+#pragma unroll
+            for (int j = 0; j < 32; ++j) r[j] = (col0 + j < n_out) ? cp[j] : 0.0f;
         }
     }
-    // vector store when the 32 columns are in range and the row start is aligned
+#pragma unroll
+    for (int j = 0; j < 32; ++j) r[j] *= ep.beta;
+}
+
+// Stores 32 consecutive output values of one row (vector stores when the row
+// segment is in range and 16-byte aligned).
+template <int OUT>
+__device__ __forceinline__ void store_row32(const EpiParams &ep, int64_t row, int64_t col0, int64_t n_out,
+                                            const float (&v)[32], float ys) {
     const bool full = (col0 + 32 <= n_out);
     if (OUT == kOutBF16) {
         __nv_bfloat16 *yp = reinterpret_cast<__nv_bfloat16 *>(ep.y) + row * ep.ldy + col0;
@@ -127,7 +184,8 @@ __device__ __forceinline__ void epi_row32(const EpiParams &ep, int64_t row, int6
         float *yp = reinterpret_cast<float *>(ep.y) + row * ep.ldy + col0;
         if (full && aligned(yp, 16)) {
 #pragma unroll
-            for (int j = 0; j < 8; ++j) reinterpret_cast<float4 *>(yp)[j] = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+            for (int j = 0; j < 8; ++j)
+                reinterpret_cast<float4 *>(yp)[j] = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
             return;
         }
     } else {
@@ -148,9 +206,86 @@ __device__ __forceinline__ void epi_row32(const EpiParams &ep, int64_t row, int6
         if (col0 + j < n_out) store_out<OUT>(ep, row, col0 + j, v[j], ys);
 }
 
+// Epilogue of 32 output columns [col0, col0+32) of one row. g holds the
+// accumulators of gemm columns ng0.. (for SILU_MUL: the gate columns; u the
+// up columns nu0..). All parameter-dependent branches are per chunk; the
+// element loop is branch-free.
+template <int EPI, int OUT>
+__device__ __forceinline__ void epi_row32(const EpiParams &ep, int64_t row, bool row_ok, int64_t col0, int64_t ng0,
+                                          int64_t nu0, int64_t n_out, const uint32_t (&g)[32],
+                                          const uint32_t (&u)[32], float row_scale, float row_add, float ys,
+                                          float &amax) {
+    ColFactors fg;
+    load_col_factors(ep, ng0, fg);
+    float v[32];
+#pragma unroll
+    for (int j = 0; j < 32; ++j) v[j] = fmaf(__uint_as_float(g[j]) * row_scale, fg.scale[j], fg.add[j] + row_add);
+    if (EPI == LCML_EPI_SILU_MUL) {
+        ColFactors fu;
+        load_col_factors(ep, nu0, fu);
+#pragma unroll
+        for (int j = 0; j < 32; ++j) {
+            const float up = fmaf(__uint_as_float(u[j]) * row_scale, fu.scale[j], fu.add[j] + row_add);
+            v[j] = silu_mul(v[j], up);
+        }
+    }
+    if (!row_ok) return;
+    if (ep.c_mat) {
+        float r[32];
+        load_cmat32(ep, row, col0, n_out, r);
+#pragma unroll
+        for (int j = 0; j < 32; ++j) v[j] += r[j];
+    }
+    if (EPI == LCML_EPI_RELU) {
+#pragma unroll
+        for (int j = 0; j < 32; ++j) v[j] = fmaxf(v[j], 0.0f);
+    }
+    if (ep.row_amax) {
+#pragma unroll
+        for (int j = 0; j < 32; ++j) amax = (col0 + j < n_out) ? fmaxf(amax, fabsf(v[j])) : amax;
+    }
+    store_row32<OUT>(ep, row, col0, n_out, v, ys);
+}
+
 __device__ __forceinline__ void atomic_max_abs(float *p, float v) {
     if (!(v > 0.0f)) return;  // also skips NaN
     atomicMax(reinterpret_cast<unsigned int *>(p), __float_as_uint(v));
+}
+
+// One output tile's epilogue for the calling thread: TMEM lane `row` of the
+// accumulator at `taddr` (BN fp32 columns), gemm column block `tn`.
+template <int BN, int EPI, int OUT>
+__device__ __forceinline__ void epilogue_tile(const EpiParams &ep, uint32_t taddr, int64_t row, int tn, float ys) {
+    const int64_t n_out = (EPI == LCML_EPI_SILU_MUL) ? ep.N / 2 : ep.N;
+    const bool row_ok = row < ep.M;
+    const float row_scale = ep.alpha * (ep.sa_row ? (row_ok ? __ldg(ep.sa + row) : 0.0f) : __ldg(ep.sa));
+    float row_add = 0.0f;  // beta * C broadcast as a scalar or along M
+    if (ep.c_vec_mode == 1) row_add = ep.beta * __ldg(ep.c_vec);
+    else if (ep.c_vec_mode == 2 && row_ok) row_add = ep.beta * __ldg(ep.c_vec + row);
+    float amax = 0.0f;
+    if (EPI == LCML_EPI_SILU_MUL) {
+        // BN columns = BN/2 gate columns followed by BN/2 up columns
+#pragma unroll 1
+        for (int c = 0; c < BN / 64; ++c) {
+            uint32_t g[32], u[32];
+            tmem_ld_32x32b_x32(taddr + c * 32, g);
+            tmem_ld_32x32b_x32(taddr + BN / 2 + c * 32, u);
+            tmem_wait_ld();
+            const int64_t ng0 = static_cast<int64_t>(tn) * BN + c * 32;
+            const int64_t col0 = static_cast<int64_t>(tn) * (BN / 2) + c * 32;
+            epi_row32<EPI, OUT>(ep, row, row_ok, col0, ng0, ng0 + BN / 2, n_out, g, u, row_scale, row_add, ys, amax);
+        }
+    } else {
+#pragma unroll 1
+        for (int c = 0; c < BN / 32; ++c) {
+            uint32_t g[32];
+            tmem_ld_32x32b_x32(taddr + c * 32, g);
+            tmem_wait_ld();
+            const int64_t col0 = static_cast<int64_t>(tn) * BN + c * 32;
+            epi_row32<EPI, OUT>(ep, row, row_ok, col0, col0, 0, n_out, g, g, row_scale, row_add, ys, amax);
+        }
+    }
+    if (ep.row_amax && row_ok) atomic_max_abs(ep.row_amax + row, amax);
 }
 
 // Tile index -> (m tile, n tile), banded so that CTAs running at the same time
@@ -300,7 +435,6 @@ __global__ void __launch_bounds__(kThreads, 1)
         // ---------------- epilogue warps ----------------
         const int quarter = warp & 3;  // TMEM lanes [32*quarter, 32*quarter+32)
         const float ys = (OUT == kOutE4M3) ? __ldg(ep.y_scale) : 1.0f;
-        const int64_t n_out = (EPI == LCML_EPI_SILU_MUL) ? ep.N / 2 : ep.N;
         int acc = 0;
         uint32_t acc_phase = 0;
         for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
@@ -310,39 +444,10 @@ __global__ void __launch_bounds__(kThreads, 1)
             tc_fence_after();
             const int64_t row = static_cast<int64_t>(tm) * BM + quarter * 32 + lane;
             const uint32_t taddr = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + static_cast<uint32_t>(acc * BN);
-            const bool row_ok = row < ep.M;
-            const float row_scale = ep.alpha * (ep.sa_row ? (row_ok ? __ldg(ep.sa + row) : 0.0f) : __ldg(ep.sa));
-            float amax = 0.0f;
-            if (EPI == LCML_EPI_SILU_MUL) {
-                // BN columns = BN/2 gate columns followed by BN/2 up columns
-#pragma unroll 1
-                for (int c = 0; c < BN / 64; ++c) {
-                    uint32_t g[32], u[32];
-                    tmem_ld_32x32b_x32(taddr + c * 32, g);
-                    tmem_ld_32x32b_x32(taddr + BN / 2 + c * 32, u);
-                    tmem_wait_ld();
-                    if (row_ok) {
-                        const int64_t ng0 = static_cast<int64_t>(tn) * BN + c * 32;
-                        const int64_t col0 = static_cast<int64_t>(tn) * (BN / 2) + c * 32;
-                        epi_row32<EPI, OUT>(ep, row, col0, ng0, ng0 + BN / 2, n_out, g, u, row_scale, ys, amax);
-                    }
-                }
-            } else {
-#pragma unroll 1
-                for (int c = 0; c < BN / 32; ++c) {
-                    uint32_t g[32];
-                    tmem_ld_32x32b_x32(taddr + c * 32, g);
-                    tmem_wait_ld();
-                    if (row_ok) {
-                        const int64_t col0 = static_cast<int64_t>(tn) * BN + c * 32;
-                        epi_row32<EPI, OUT>(ep, row, col0, col0, 0, n_out, g, g, row_scale, ys, amax);
-                    }
-                }
-            }
+            epilogue_tile<BN, EPI, OUT>(ep, taddr, row, tn, ys);
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(&tempty[acc]);
-            if (ep.row_amax && row_ok) atomic_max_abs(ep.row_amax + row, amax);
             if (++acc == 2) {
                 acc = 0;
                 acc_phase ^= 1u;
@@ -360,9 +465,201 @@ __global__ void __launch_bounds__(kThreads, 1)
 }
 
 // ---------------------------------------------------------------------------
+// CTA-pair kernel (cluster of 2, tcgen05.mma.cta_group::2): a 256 x 256 tile
+// per pair. Each CTA stages its 128 rows of A and 128 rows of B (32 KB per
+// k-block), so six stages fit and every staged byte feeds twice the MMA work
+// of the single-CTA kernel. The even CTA ("leader") arms the full barrier for
+// both halves and issues the MMAs; commits multicast to both CTAs' barriers;
+// both CTAs run an epilogue over their own 128 TMEM lanes. No TMA multicast.
+// ---------------------------------------------------------------------------
+constexpr int kPairStages = 6;
+
+template <int STAGES>
+struct PairLayout {
+    static constexpr int kHalfBytes = 128 * BK;           // 16 KB: A half or B half
+    static constexpr int kStageBytes = 2 * kHalfBytes;    // per CTA
+    static constexpr int kTmemCols = 512;                 // 2 x 256 fp32 accumulators
+    static constexpr int kBarOffset = STAGES * kStageBytes;
+    static constexpr int kSmemBytes = kBarOffset + (2 * STAGES + 4) * 8 + 16 + 1024;
+};
+
+template <int STAGES, int EPI, int OUT>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
+    k_gemm_fp8_tc2(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, int M, int N,
+                   int K, EpiParams ep, int *err) {
+    using L = PairLayout<STAGES>;
+    constexpr int BN = 256;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint64_t *full = reinterpret_cast<uint64_t *>(smem + L::kBarOffset);
+    uint64_t *empty = full + STAGES;
+    uint64_t *tfull = empty + STAGES;
+    uint64_t *tempty = tfull + 2;
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(tempty + 2);
+
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+    const uint32_t rank = cluster_ctarank();
+    const int pair = blockIdx.x >> 1;
+    const int npairs = gridDim.x >> 1;
+    const int num_m = (M + 255) / 256;
+    const int num_n = (N + BN - 1) / BN;
+    const int num_tiles = num_m * num_n;
+    const int kblocks = (K + BK - 1) / BK;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < STAGES; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], 1);
+        }
+        for (int b = 0; b < 2; ++b) {
+            mbar_init(&tfull[b], 1);
+            mbar_init(&tempty[b], 8);  // 4 epilogue warps in each CTA of the pair
+        }
+        fence_mbar_init();
+    }
+    if (warp == 1) {
+        tmem_alloc_pair(tmem_slot, L::kTmemCols);
+        tmem_relinquish_pair();
+    }
+    tc_fence_before();
+    cluster_sync_all();  // barrier inits and TMEM allocation visible to the peer
+    tc_fence_after();
+    const uint32_t tmem_base = *tmem_slot;
+
+    if (warp == 0) {
+        // ---------------- TMA producer (both CTAs) ----------------
+        if (elect_one()) {
+            tma_prefetch_desc(&tmA);
+            tma_prefetch_desc(&tmB);
+            int stage = 0;
+            uint32_t phase = 0;
+            int issued = 0;
+            bool ok = true;
+            for (int tile = pair; tile < num_tiles && ok; tile += npairs) {
+                int tm, tn;
+                tile_coords(tile, num_m, num_n, tm, tn);
+                const int arow = tm * 256 + static_cast<int>(rank) * 128;
+                const int brow = tn * BN + static_cast<int>(rank) * 128;
+                for (int kb = 0; kb < kblocks; ++kb) {
+                    if (!mbar_wait(&empty[stage], phase ^ 1u, err, kDevTimeoutProducer)) {
+                        ok = false;
+                        break;
+                    }
+                    uint8_t *sa = smem + stage * L::kStageBytes;
+                    uint8_t *sb = sa + L::kHalfBytes;
+                    if (rank == 0) mbar_arrive_expect_tx(&full[stage], 2 * L::kStageBytes);
+                    const uint32_t bar = mapa_shared(smem_u32(&full[stage]), 0);
+                    tma_load_2d_pair(&tmA, bar, sa, kb * BK, arow);
+                    tma_load_2d_pair(&tmB, bar, sb, kb * BK, brow);
+                    ++issued;
+                    if (++stage == STAGES) {
+                        stage = 0;
+                        phase ^= 1u;
+                    }
+                }
+            }
+            if (rank == 0) {
+                // drain: the last loads (both halves land on the leader's barriers)
+                const int pending = issued < STAGES ? issued : STAGES;
+                for (int i = 0; i < pending; ++i) {
+                    if (--stage < 0) {
+                        stage = STAGES - 1;
+                        phase ^= 1u;
+                    }
+                    mbar_wait(&full[stage], phase, err, kDevTimeoutDrain);
+                }
+            }
+        }
+    } else if (warp == 1) {
+        // ---------------- MMA issuer (leader CTA only) ----------------
+        if (rank == 0 && elect_one()) {
+            constexpr uint32_t idesc = idesc_e4m3_f32(256, BN, 0);
+            int stage = 0;
+            uint32_t phase = 0;
+            int acc = 0;
+            uint32_t acc_phase = 0;
+            bool ok = true;
+            for (int tile = pair; tile < num_tiles && ok; tile += npairs) {
+                if (!mbar_wait_cluster(&tempty[acc], acc_phase ^ 1u, err, kDevTimeoutMma)) break;
+                tc_fence_after();
+                const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * BN);
+                for (int kb = 0; kb < kblocks; ++kb) {
+                    if (!mbar_wait(&full[stage], phase, err, kDevTimeoutMma)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint32_t a_addr = smem_u32(smem + stage * L::kStageBytes);
+                    const uint32_t b_addr = a_addr + L::kHalfBytes;
+#pragma unroll
+                    for (int k = 0; k < BK / UMMA_K; ++k) {
+                        umma_f8f6f4_pair(d_tmem, sdesc_kmajor_sw128(a_addr + k * UMMA_K),
+                                         sdesc_kmajor_sw128(b_addr + k * UMMA_K), idesc, (kb | k) != 0 ? 1u : 0u);
+                    }
+                    umma_commit_pair_mc(&empty[stage], 0x3);
+                    if (++stage == STAGES) {
+                        stage = 0;
+                        phase ^= 1u;
+                    }
+                }
+                if (!ok) break;
+                umma_commit_pair_mc(&tfull[acc], 0x3);
+                if (++acc == 2) {
+                    acc = 0;
+                    acc_phase ^= 1u;
+                }
+            }
+        }
+    } else {
+        // ---------------- epilogue warps (both CTAs) ----------------
+        const int quarter = warp & 3;
+        const float ys = (OUT == kOutE4M3) ? __ldg(ep.y_scale) : 1.0f;
+        const uint32_t tempty_leader = mapa_shared(smem_u32(&tempty[0]), 0);
+        int acc = 0;
+        uint32_t acc_phase = 0;
+        for (int tile = pair; tile < num_tiles; tile += npairs) {
+            int tm, tn;
+            tile_coords(tile, num_m, num_n, tm, tn);
+            if (!mbar_wait(&tfull[acc], acc_phase, err, kDevTimeoutEpilogue)) break;
+            tc_fence_after();
+            const int64_t row = static_cast<int64_t>(tm) * 256 + rank * 128 + quarter * 32 + lane;
+            const uint32_t taddr = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + static_cast<uint32_t>(acc * BN);
+            epilogue_tile<BN, EPI, OUT>(ep, taddr, row, tn, ys);
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive_cluster(tempty_leader + 8u * static_cast<uint32_t>(acc));
+            if (++acc == 2) {
+                acc = 0;
+                acc_phase ^= 1u;
+            }
+        }
+    }
+
+    tc_fence_before();
+    cluster_sync_all();  // every MMA consumed, every accumulator read, in both CTAs
+    if (warp == 1) {
+        __syncwarp();
+        tc_fence_after();
+        tmem_dealloc_pair(tmem_base, L::kTmemCols);
+    }
+}
+
+// ---------------------------------------------------------------------------
 // SIMT fallback: 64x64 output tile per 256-thread CTA, operands decoded to
 // fp32 in shared memory, same epilogue semantics (per element).
 // ---------------------------------------------------------------------------
+// Scale + C for one accumulator value (SIMT fallback path, per element).
+__device__ __forceinline__ float simt_pre(float acc, float row_scale, int64_t row, int64_t n, const EpiParams &ep) {
+    const float sb = ep.sb_col ? __ldg(ep.sb + n) : __ldg(ep.sb);
+    float v = acc * row_scale * sb;
+    if (ep.c_vec_mode) {
+        const float c = ep.c_vec_mode == 1 ? __ldg(ep.c_vec) : (ep.c_vec_mode == 2 ? __ldg(ep.c_vec + row) : __ldg(ep.c_vec + n));
+        v = fmaf(ep.beta, c, v);
+    }
+    return v;
+}
+
 template <int EPI, int OUT>
 __global__ void __launch_bounds__(256) k_gemm_fp8_simt(const uint8_t *__restrict__ A, int64_t lda,
                                                        const uint8_t *__restrict__ B, int64_t ldb, int b_kmajor,
@@ -417,9 +714,9 @@ __global__ void __launch_bounds__(256) k_gemm_fp8_simt(const uint8_t *__restrict
             float a;
             if (EPI == LCML_EPI_SILU_MUL) {
                 const int64_t ng = (col / 128) * 256 + (col % 128);
-                a = silu_mul(epi_pre(accg[i][j], rs, row, ng, ep), epi_pre(accu[i][j], rs, row, ng + 128, ep));
+                a = silu_mul(simt_pre(accg[i][j], rs, row, ng, ep), simt_pre(accu[i][j], rs, row, ng + 128, ep));
             } else {
-                a = epi_pre(accg[i][j], rs, row, col, ep);
+                a = simt_pre(accg[i][j], rs, row, col, ep);
             }
             if (ep.c_mat) a += ep.beta * load_cmat(ep, row, col);
             if (EPI == LCML_EPI_RELU) a = fmaxf(a, 0.0f);
@@ -433,6 +730,9 @@ __global__ void __launch_bounds__(256) k_gemm_fp8_simt(const uint8_t *__restrict
 // ---------------------------------------------------------------------------
 // Host side
 // ---------------------------------------------------------------------------
+// Kernel selection override for tests: 0 automatic, 1 single-CTA, 2 CTA pair.
+int g_gemm_mode = 0;
+
 PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
     static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
     static std::once_flag once;
@@ -489,6 +789,32 @@ int launch_tc(const lcml_fp8_gemm_desc *d, const EpiParams &ep, cudaStream_t st)
 }
 
 template <int EPI, int OUT>
+int launch_tc2(const lcml_fp8_gemm_desc *d, const EpiParams &ep, cudaStream_t st) {
+    using L = PairLayout<kPairStages>;
+    auto kern = k_gemm_fp8_tc2<kPairStages, EPI, OUT>;
+    static std::once_flag once;
+    static cudaError_t attr_err = cudaSuccess;
+    std::call_once(once, [&] {
+        attr_err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kSmemBytes);
+    });
+    if (attr_err != cudaSuccess)
+        return set_error(LCML_ERR_CUDA, "cudaFuncSetAttribute(smem=%d) failed: %s", L::kSmemBytes,
+                         cudaGetErrorString(attr_err));
+    CUtensorMap ta, tb;
+    int rc = make_tmap(&ta, d->A, d->K, d->M, d->lda, 128);
+    if (rc) return rc;
+    rc = make_tmap(&tb, d->B, d->K, d->N, d->ldb, 128);
+    if (rc) return rc;
+    const int64_t tiles = ((d->M + 255) / 256) * ((d->N + 255) / 256);
+    const int64_t pairs = sm_count() / 2;
+    const int grid = static_cast<int>(2 * (tiles < pairs ? tiles : pairs));
+    kern<<<grid, kThreads, L::kSmemBytes, st>>>(ta, tb, static_cast<int>(d->M), static_cast<int>(d->N),
+                                                 static_cast<int>(d->K), ep, device_error_word());
+    LCML_LAUNCHED("gemm_fp8_tc2");
+    return LCML_OK;
+}
+
+template <int EPI, int OUT>
 int launch_simt(const lcml_fp8_gemm_desc *d, const EpiParams &ep, cudaStream_t st) {
     const int64_t n_out = (EPI == LCML_EPI_SILU_MUL) ? d->N / 2 : d->N;
     dim3 grid(static_cast<unsigned>((n_out + 63) / 64), static_cast<unsigned>((d->M + 63) / 64));
@@ -504,6 +830,10 @@ int dispatch(const lcml_fp8_gemm_desc *d, const EpiParams &ep, cudaStream_t st, 
                         aligned(d->A, 16) && aligned(d->B, 16) && d->M <= 0x7fffffff && d->N <= 0x7fffffff &&
                         d->K <= 0x7fffffff;
     if (!tma_ok) return launch_simt<EPI, OUT>(d, ep, st);
+    // CTA pairs once there are enough 256 x 256 tiles to fill the machine
+    const int64_t pair_tiles = ((d->M + 255) / 256) * ((d->N + 255) / 256);
+    if (g_gemm_mode != 1 && (g_gemm_mode == 2 || (d->M >= 256 && pair_tiles >= sm_count() / 2)))
+        return launch_tc2<EPI, OUT>(d, ep, st);
     if (EPI == LCML_EPI_SILU_MUL || d->N >= 2048) return launch_tc<256, 4, EPI, OUT>(d, ep, st);
     return launch_tc<128, 6, EPI, OUT>(d, ep, st);
 }
@@ -576,10 +906,12 @@ int lcml_fp8_gemm(const lcml_fp8_gemm_desc *desc, lcml_stream_t stream) {
     return lcml::gemm::gemm_entry(desc, stream, false);
 }
 
-// Test hook (not in the public header): forces the SIMT kernel so tests can
-// cross-check the two code paths on identical inputs.
+// Test hooks (not in the public header): force the SIMT kernel, or pick the
+// tensor-core kernel variant, so tests can cross-check the code paths.
 int lcml_fp8_gemm_simt(const lcml_fp8_gemm_desc *desc, lcml_stream_t stream) {
     return lcml::gemm::gemm_entry(desc, stream, true);
 }
+
+void lcml_fp8_gemm_set_mode(int mode) { lcml::gemm::g_gemm_mode = mode; }
 
 }// extern "C"

@@ -71,6 +71,37 @@ __device__ __forceinline__ uint32_t quantize1(float x, float s) {
     return e4m3_encode(__fdiv_rn(x, s));
 }
 
+// Fast QuantizeLinear of two elements, bit-identical to quantize1():
+// q = x * r with r = RN(1/s) is within 2.5 fp32 ulps of RN(x / s), and every
+// e4m3 rounding boundary (a midpoint between neighbouring e4m3 values, incl.
+// the binade steps) has low 20 mantissa bits 0x80000. So whenever q is
+// normal in e4m3 terms (|q| >= 2^-6), finite, and its low 20 bits are more
+// than 3 ulps from 0x80000, q and x / s round to the same e4m3 value, which
+// the hardware cvt.rn.satfinite (RNE, |v| > 448 -> +-448) produces. All other
+// cases (zeros, e4m3 subnormals, NaN/inf, near-ties, unusual scales) take the
+// exact divide + integer encoder. `s_ok` says r is usable (s normal positive,
+// r finite normal).
+__device__ __forceinline__ bool needs_exact(float q) {
+    const uint32_t a = __float_as_uint(q) & 0x7fffffffu;
+    return (a < 0x3c800000u) | (a >= 0x7f800000u) | (((a & 0xfffffu) - 0x7fffdu) <= 6u);
+}
+
+__device__ __forceinline__ uint32_t quantize2_fast(float x0, float x1, float s, float r, bool s_ok) {
+    const float q0 = x0 * r, q1 = x1 * r;
+    uint32_t out;
+    asm("{\n\t.reg .b16 t;\n\t"
+        "cvt.rn.satfinite.e4m3x2.f32 t, %2, %1;\n\t"
+        "cvt.u32.u16 %0, t;\n\t}"
+        : "=r"(out)
+        : "f"(q0), "f"(q1));
+    if (!s_ok || needs_exact(q0) || needs_exact(q1)) out = quantize1(x0, s) | (quantize1(x1, s) << 8);
+    return out;
+}
+
+__device__ __forceinline__ bool scale_fast_ok(float s, float r) {
+    return s >= 1.17549435e-38f && s < 3.0e38f && r >= 1.17549435e-38f && r < 3.0e38f;
+}
+
 // amax -> scale for every dynamic mode: amax / 448, or 1 when amax is 0.
 __device__ __forceinline__ float scale_from_amax(float amax) {
     return amax > 0.0f ? __fdiv_rn(amax, 448.0f) : 1.0f;
@@ -144,8 +175,68 @@ __device__ __forceinline__ void tma_load_2d(const void *tmap, uint64_t *bar, voi
         : "memory");
 }
 
+// CTA-pair form: the copy lands in this CTA's shared memory but completes
+// (complete_tx) on `bar_cluster`, a shared::cluster address that may name the
+// peer CTA's mbarrier (used by the 2-SM GEMM to signal the leader's barrier).
+__device__ __forceinline__ void tma_load_2d_pair(const void *tmap, uint32_t bar_cluster, void *smem_dst, int x, int y) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], [%2];" ::"r"(
+            smem_u32(smem_dst)),
+        "l"(tmap), "r"(bar_cluster), "r"(x), "r"(y)
+        : "memory");
+}
+
 __device__ __forceinline__ void tma_prefetch_desc(const void *tmap) {
     asm volatile("prefetch.tensormap [%0];" ::"l"(tmap) : "memory");
+}
+
+// ---------------------------------------------------------------------------
+// Clusters (CTA pairs)
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ uint32_t cluster_ctarank() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+    return r;
+}
+
+// Address of the same shared-memory offset in CTA `rank` of this cluster.
+__device__ __forceinline__ uint32_t mapa_shared(uint32_t addr, uint32_t rank) {
+    uint32_t r;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(addr), "r"(rank));
+    return r;
+}
+
+__device__ __forceinline__ void mbar_arrive_cluster(uint32_t bar_cluster) {
+    asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(bar_cluster) : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait_cluster(uint64_t *bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    return ok != 0u;
+}
+
+// Bounded wait with cluster-scope acquire (for barriers other CTAs arrive on).
+__device__ __forceinline__ bool mbar_wait_cluster(uint64_t *bar, uint32_t parity, int *err_word, int err) {
+    if (mbar_try_wait_cluster(bar, parity)) return true;
+    const long long t0 = clock64();
+    while (!mbar_try_wait_cluster(bar, parity)) {
+        if (clock64() - t0 > kWaitLimitCycles) {
+            record_device_error(err_word, err);
+            return false;
+        }
+    }
+    return true;
+}
+
+__device__ __forceinline__ void cluster_sync_all() {
+    asm volatile("barrier.cluster.arrive.release;\n\tbarrier.cluster.wait.acquire;" ::: "memory");
 }
 
 // ---------------------------------------------------------------------------
@@ -165,6 +256,20 @@ __device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
 }
 
+__device__ __forceinline__ void tmem_alloc_pair(uint32_t *dst_smem, uint32_t ncols) {
+    asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(dst_smem)),
+                 "r"(ncols)
+                 : "memory");
+}
+
+__device__ __forceinline__ void tmem_relinquish_pair() {
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+}
+
+__device__ __forceinline__ void tmem_dealloc_pair(uint32_t taddr, uint32_t ncols) {
+    asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
+
 __device__ __forceinline__ void tc_fence_before() {
     asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
 }
@@ -181,6 +286,28 @@ __device__ __forceinline__ void umma_f8f6f4(uint32_t d_tmem, uint64_t a_desc, ui
         "setp.ne.b32 p, %4, 0;\n\t"
         "tcgen05.mma.cta_group::1.kind::f8f6f4 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
         "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+
+// CTA-pair MMA (issued by the even CTA of the pair): A rows split across the
+// two CTAs' shared memory (M = 256), B columns split likewise, D in both CTAs' TMEM.
+__device__ __forceinline__ void umma_f8f6f4_pair(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                                 uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::2.kind::f8f6f4 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+
+// Arrive once on the mbarrier at `bar`'s offset in every CTA of `cta_mask`
+// when the pair MMAs issued so far complete.
+__device__ __forceinline__ void umma_commit_pair_mc(uint64_t *bar, uint16_t cta_mask) {
+    asm volatile(
+        "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;" ::"r"(
+            smem_u32(bar)),
+        "h"(cta_mask)
         : "memory");
 }
 

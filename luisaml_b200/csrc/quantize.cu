@@ -27,13 +27,28 @@ __device__ __forceinline__ float load_scale(const float *__restrict__ sc, int64_
     return from_amax ? scale_from_amax(v) : v;
 }
 
-__device__ __forceinline__ uint32_t pack4(float a, float b, float c, float d, float s) {
-    return quantize1(a, s) | (quantize1(b, s) << 8) | (quantize1(c, s) << 16) | (quantize1(d, s) << 24);
+// A scale with its correctly rounded reciprocal, for quantize2_fast().
+struct Scale {
+    float s, r;
+    bool ok;
+};
+
+__device__ __forceinline__ Scale make_scale(float v) {
+    Scale sc;
+    sc.s = v;
+    sc.r = __frcp_rn(v);
+    sc.ok = scale_fast_ok(v, sc.r);
+    return sc;
+}
+
+__device__ __forceinline__ uint32_t pack4(float a, float b, float c, float d, const Scale &sc) {
+    return quantize2_fast(a, b, sc.s, sc.r, sc.ok) | (quantize2_fast(c, d, sc.s, sc.r, sc.ok) << 16);
 }
 
 __device__ __forceinline__ uint32_t pack4v(float4 v, const float *s) {
-    return quantize1(v.x, s[0]) | (quantize1(v.y, s[1]) << 8) | (quantize1(v.z, s[2]) << 16) |
-           (quantize1(v.w, s[3]) << 24);
+    const Scale s0 = make_scale(s[0]), s1 = make_scale(s[1]), s2 = make_scale(s[2]), s3 = make_scale(s[3]);
+    return (quantize2_fast(v.x, v.x, s0.s, s0.r, s0.ok) & 0xffu) | ((quantize2_fast(v.y, v.y, s1.s, s1.r, s1.ok) & 0xffu) << 8) |
+           ((quantize2_fast(v.z, v.z, s2.s, s2.r, s2.ok) & 0xffu) << 16) | ((quantize2_fast(v.w, v.w, s3.s, s3.r, s3.ok) & 0xffu) << 24);
 }
 
 template <int KIND, bool FROM_AMAX>
@@ -45,17 +60,34 @@ __global__ void __launch_bounds__(kThreads) k_quantize(const float *__restrict__
     const int64_t n16 = n >> 4;
     float s_tensor = 0.0f;
     if (KIND == kScaleTensor) s_tensor = load_scale(sc, 0, FROM_AMAX);
-    for (int64_t g = tid; g < n16; g += nthreads) {
+    const Scale st = make_scale(s_tensor);
+    int64_t g = tid;
+    if (KIND == kScaleTensor) {
+        // two 16-element groups per thread per iteration: 8 loads in flight
+        for (; g + nthreads < n16; g += 2 * nthreads) {
+            const float4 *xa = reinterpret_cast<const float4 *>(x) + g * 4;
+            const float4 *xb = reinterpret_cast<const float4 *>(x) + (g + nthreads) * 4;
+            const float4 a0 = __ldcs(xa), a1 = __ldcs(xa + 1), a2 = __ldcs(xa + 2), a3 = __ldcs(xa + 3);
+            const float4 b0 = __ldcs(xb), b1 = __ldcs(xb + 1), b2 = __ldcs(xb + 2), b3 = __ldcs(xb + 3);
+            __stcs(reinterpret_cast<uint4 *>(y) + g,
+                   make_uint4(pack4(a0.x, a0.y, a0.z, a0.w, st), pack4(a1.x, a1.y, a1.z, a1.w, st),
+                              pack4(a2.x, a2.y, a2.z, a2.w, st), pack4(a3.x, a3.y, a3.z, a3.w, st)));
+            __stcs(reinterpret_cast<uint4 *>(y) + g + nthreads,
+                   make_uint4(pack4(b0.x, b0.y, b0.z, b0.w, st), pack4(b1.x, b1.y, b1.z, b1.w, st),
+                              pack4(b2.x, b2.y, b2.z, b2.w, st), pack4(b3.x, b3.y, b3.z, b3.w, st)));
+        }
+    }
+    for (; g < n16; g += nthreads) {
         const float4 *xp = reinterpret_cast<const float4 *>(x) + g * 4;
         const float4 v0 = __ldcs(xp), v1 = __ldcs(xp + 1), v2 = __ldcs(xp + 2), v3 = __ldcs(xp + 3);
         uint4 out;
         if (KIND == kScaleTensor) {
-            out.x = pack4(v0.x, v0.y, v0.z, v0.w, s_tensor);
-            out.y = pack4(v1.x, v1.y, v1.z, v1.w, s_tensor);
-            out.z = pack4(v2.x, v2.y, v2.z, v2.w, s_tensor);
-            out.w = pack4(v3.x, v3.y, v3.z, v3.w, s_tensor);
+            out.x = pack4(v0.x, v0.y, v0.z, v0.w, st);
+            out.y = pack4(v1.x, v1.y, v1.z, v1.w, st);
+            out.z = pack4(v2.x, v2.y, v2.z, v2.w, st);
+            out.w = pack4(v3.x, v3.y, v3.z, v3.w, st);
         } else if (KIND == kScaleGroup16) {
-            const float s = load_scale(sc, ((g << 4) / inner) % axis_len, FROM_AMAX);
+            const Scale s = make_scale(load_scale(sc, ((g << 4) / inner) % axis_len, FROM_AMAX));
             out.x = pack4(v0.x, v0.y, v0.z, v0.w, s);
             out.y = pack4(v1.x, v1.y, v1.z, v1.w, s);
             out.z = pack4(v2.x, v2.y, v2.z, v2.w, s);
@@ -171,8 +203,9 @@ __global__ void __launch_bounds__(kThreads) k_quantize_rows_dynamic(const float 
         }
     }
     m = block_max_u32(m, red);
-    const float s = scale_from_amax(__uint_as_float(m));
-    if (threadIdx.x == 0) scale_out[r] = s;
+    const float s_row = scale_from_amax(__uint_as_float(m));
+    if (threadIdx.x == 0) scale_out[r] = s_row;
+    const Scale s = make_scale(s_row);
     uint32_t *yr = reinterpret_cast<uint32_t *>(y + r * cols);
 #pragma unroll
     for (int j = 0; j < VPT; ++j) {

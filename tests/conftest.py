@@ -40,12 +40,26 @@ def golden(name):
     return np.load(os.path.join(GOLDEN, name))
 
 
-def assert_close(got, ref, rtol=RTOL, atol=ATOL, what=""):
+def bf16_half_ulp(x):
+    """Half the bf16 spacing at |x| (8 significant bits): the largest error of
+    a correct round-to-nearest cast of x to bf16."""
+    a = np.abs(np.asarray(x, dtype=np.float64))
+    e = np.floor(np.log2(np.maximum(a, 2.0 ** -126)))
+    return np.ldexp(1.0, (e - 8).astype(np.int64))
+
+
+def assert_close_bf16(got, ref, rtol=RTOL, atol=ATOL, what=""):
+    """bf16 output vs fp32 oracle: the fp32 accumulation must be within
+    rtol/atol and the final cast to bf16 may add its half ulp."""
+    assert_close(got, ref, rtol=rtol, atol=atol, what=what, extra=bf16_half_ulp(ref))
+
+
+def assert_close(got, ref, rtol=RTOL, atol=ATOL, what="", extra=0.0):
     got = np.asarray(got, dtype=np.float64)
     ref = np.asarray(ref, dtype=np.float64)
     assert got.shape == ref.shape, (got.shape, ref.shape)
     err = np.abs(got - ref)
-    bound = atol + rtol * np.abs(ref)
+    bound = atol + rtol * np.abs(ref) + extra
     bad = err > bound
     if bad.any():
         i = np.unravel_index(np.argmax(err - bound), err.shape)

@@ -9,7 +9,7 @@ import numpy as np
 import pytest
 
 import oracle
-from conftest import assert_close
+from conftest import assert_close, assert_close_bf16
 
 pytestmark = pytest.mark.gpu
 
@@ -56,9 +56,15 @@ def test_gemm_shapes(dev, M, N, K, out):
     import luisaml_b200 as lb
     Aq, sa, Bq, sb = make_operands(M, N, K, seed=M * 31 + N * 7 + K)
     ref = oracle.qdq_gemm(Aq, sa, Bq, sb, b_kmajor=True)
-    Y = lb.gemm(_t(Aq, dev), _t(Bq, dev), _t(sa, dev), _t(sb, dev),
-                out_dtype=torch.bfloat16 if out == "bf16" else torch.float32)
-    assert_close(Y.float().cpu().numpy(), ref, what=f"gemm {M}x{N}x{K} {out}")
+    a, b, s1, s2 = _t(Aq, dev), _t(Bq, dev), _t(sa, dev), _t(sb, dev)
+    y32 = lb.gemm(a, b, s1, s2, out_dtype=torch.float32)
+    assert_close(y32.cpu().numpy(), ref, what=f"gemm {M}x{N}x{K} f32")
+    if out == "bf16":
+        Y = lb.gemm(a, b, s1, s2, out_dtype=torch.bfloat16)
+        # the bf16 store is the correctly rounded fp32 epilogue value ...
+        assert torch.equal(Y, y32.bfloat16())
+        # ... so it is within tolerance of the oracle up to the cast's half ulp
+        assert_close_bf16(Y.float().cpu().numpy(), ref, what=f"gemm {M}x{N}x{K} bf16")
     assert lb.device_error() == 0
 
 
@@ -195,3 +201,51 @@ def test_large_8192_sampled_rows(dev):
     want = Ad @ Bd.sum(axis=0)
     got = Y.double().sum(dim=1).cpu().numpy()
     np.testing.assert_allclose(got, want, rtol=1e-4, atol=1e-2)
+
+
+@pytest.fixture
+def gemm_mode():
+    import luisaml_b200 as lb
+    yield lambda m: lb.lib().lcml_fp8_gemm_set_mode(m)
+    lb.lib().lcml_fp8_gemm_set_mode(0)
+
+
+@pytest.mark.parametrize("mode", [1, 2])
+@pytest.mark.parametrize("M,N,K,per_row,per_col", [
+    (256, 256, 128, False, False),    # one pair tile
+    (300, 520, 200, True, True),      # ragged everything
+    (1024, 1536, 640, False, True),
+    (2048, 2048, 1024, True, False),
+])
+def test_kernel_variants(dev, gemm_mode, mode, M, N, K, per_row, per_col):
+    """Single-CTA (mode 1) and CTA-pair (mode 2) tensor-core kernels vs the oracle."""
+    import torch
+    import luisaml_b200 as lb
+    gemm_mode(mode)
+    Aq, sa, Bq, sb = make_operands(M, N, K, seed=M + N + K + mode, per_row=per_row, per_col=per_col)
+    bias = np.random.default_rng(M).standard_normal(N).astype(np.float32)
+    ref = np.maximum(oracle.qdq_gemm(Aq, sa, Bq, sb) + bias, 0.0)
+    Y = lb.gemm(_t(Aq, dev), _t(Bq, dev), _t(sa, dev), _t(sb, dev), c_vec=_t(bias, dev), epilogue=lb.EPI_RELU,
+                out_dtype=torch.float32)
+    assert_close(Y.cpu().numpy(), ref, what=f"mode {mode} {M}x{N}x{K}")
+    assert lb.device_error() == 0
+
+
+@pytest.mark.parametrize("mode", [1, 2])
+def test_kernel_variants_silu(dev, gemm_mode, mode):
+    import torch
+    import luisaml_b200 as lb
+    gemm_mode(mode)
+    M, F, K = 512, 512, 384
+    rng = np.random.default_rng(41)
+    Aq, sa = oracle.quantize_dynamic_rows(rng.standard_normal((M, K)).astype(np.float32))
+    W = (rng.standard_normal((2 * F, K)) * 0.05).astype(np.float32)
+    sw = np.array([oracle.scale_from_amax(oracle.amax(r)) for r in W], dtype=np.float32)
+    Wq = oracle.quantize(W, sw, axis=0)  # rows already in the interleaved [gate 128; up 128] order
+    full = oracle.qdq_gemm(Aq, sa, Wq, sw)
+    g = np.concatenate([full[:, i:i + 128] for i in range(0, 2 * F, 256)], axis=1)
+    u = np.concatenate([full[:, i + 128:i + 256] for i in range(0, 2 * F, 256)], axis=1)
+    ref = oracle.silu_mul(g, u)
+    Y = lb.gemm(_t(Aq, dev), _t(Wq, dev), _t(sa, dev), _t(sw, dev), epilogue=lb.EPI_SILU_MUL,
+                out_dtype=torch.float32)
+    assert_close(Y.cpu().numpy(), ref, what=f"silu mode {mode}")

@@ -81,7 +81,7 @@ def test_unaligned_input(dev):
     rng = np.random.default_rng(5)
     x = rng.standard_normal(1001).astype(np.float32)
     xt = _t(x, dev)[1:]  # 4-byte offset: scalar path
-    q = lb.quantize(xt.contiguous() if False else xt, _one(dev, 0.01)).cpu().numpy()
+    q = lb.quantize(xt, _one(dev, 0.01)).cpu().numpy()
     assert np.array_equal(q, oracle.quantize(x[1:], np.float32(0.01)))
 
 
@@ -158,3 +158,26 @@ def test_invalid_arguments_are_reported(dev):
     assert rc == 1
     assert lb.device_error() == 0
     del ctypes
+
+
+@pytest.mark.parametrize("scale", [0.0123, 1.0 / 3.0, 0.7071068, 3.3e-5, 1.7e-39, 2.5e38, 1e-30])
+def test_fast_reciprocal_path_is_exact(dev, scale):
+    """The vector kernel multiplies by RN(1/s) and re-does near-tie elements
+    with an IEEE divide; the bytes must equal e4m3(x / s) exactly, including
+    for scales whose reciprocal is not usable (subnormal / huge)."""
+    import luisaml_b200 as lb
+    rng = np.random.default_rng(int(scale * 1e6) % 1000 + 1)
+    n = 1 << 24
+    x = (rng.standard_normal(n) * rng.choice([1e-3, 1.0, 30.0, 1e4], size=n)).astype(np.float32)
+    s = np.float32(scale)
+    # plant exact ties: x = (midpoint between e4m3 neighbours) * s rounded either way
+    mids = ((oracle.e4m3_decode(np.arange(1, 126, dtype=np.uint8)).astype(np.float64) +
+             oracle.e4m3_decode(np.arange(2, 127, dtype=np.uint8)).astype(np.float64)) / 2)
+    t = (mids * float(s)).astype(np.float32)
+    x[:t.size] = t
+    x[t.size:2 * t.size] = np.nextafter(t, np.float32(np.inf))
+    x[2 * t.size:3 * t.size] = np.nextafter(t, np.float32(0))
+    q = lb.quantize(_t(x, dev), _one(dev, float(s))).cpu().numpy()
+    ref = oracle.quantize(x, s)
+    bad = np.nonzero(q != ref)[0]
+    assert bad.size == 0, f"{bad.size} mismatches, first x={x[bad[0]]!r} got {q[bad[0]]:#x} want {ref[bad[0]]:#x}"
