@@ -159,6 +159,22 @@ typedef struct lcml_fp8_gemm_desc {
 int lcml_fp8_gemm(const lcml_fp8_gemm_desc *desc, lcml_stream_t stream);
 
 /*
+ * Gemm (+ epilogue) followed by dynamic per-row QuantizeLinear of its output:
+ * the Gemm -> [Sigmoid*Mul] -> Abs -> ReduceMax(axis=-1) -> Div(448) ->
+ * QuantizeLinear chain that feeds the next FP8 Gemm (the FFN's h), as two
+ * kernels. desc->Y (fp32, dense: ldy == output columns) receives the
+ * unquantized output; the GEMM epilogue accumulates each row's max |v| into
+ * `workspace`; then q[r, c] = e4m3(Y[r, c] / s[r]), s[r] = amax[r] / 448
+ * (1 for an all-zero row), written to q (dense) and q_scale [M].
+ * workspace: caller-owned device scratch of at least M floats; it is zeroed
+ * here, so its contents on entry do not matter. desc->row_amax must be NULL.
+ * Reference pieces: unary.cpp:110 (Abs), reduce.cpp:431 (ReduceMax),
+ * binary.cpp:350 (Div), fp_quantized.h:149-223 (the e4m3 encoder).
+ */
+int lcml_fp8_gemm_rowquant(const lcml_fp8_gemm_desc *desc, uint8_t *q, float *q_scale, float *workspace,
+                           lcml_stream_t stream);
+
+/*
  * FP8 2-D convolution, NCHW, lowered to implicit GEMM on the tensor cores.
  * Stands in for Conv::forward (src/onnx/operators/conv.cpp:35-255) fed by
  * DequantizeLinear on X and W. X is e4m3 [N, C, H, W] with a per-tensor

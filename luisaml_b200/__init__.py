@@ -19,7 +19,7 @@ from ._capi import (DTYPE_BFLOAT16, DTYPE_E4M3, DTYPE_FLOAT, EPI_NONE, EPI_RELU,
                     SCALE_COL, SCALE_ROW, SCALE_TENSOR, GemmDesc, LcmlError, check)
 
 __all__ = ["lib", "check", "LcmlError", "quantize", "quantize_from_amax", "quantize_rows_dynamic",
-           "quantize_tensor_dynamic", "amax", "dequantize", "transpose_u8", "gemm", "launch_count",
+           "quantize_tensor_dynamic", "amax", "dequantize", "transpose_u8", "gemm", "gemm_rowquant", "launch_count",
            "device_error"]
 
 
@@ -183,3 +183,16 @@ def gemm(A, B, sa, sb, *, b_kmajor=True, alpha=1.0, beta=1.0, c_vec=None, c_vec_
     fn = lib().lcml_fp8_gemm_simt if simt else lib().lcml_fp8_gemm
     check(fn(ctypes.byref(d), _stream()))
     return Y
+
+
+def gemm_rowquant(A, B, sa, sb, *, workspace=None, **kw):
+    """Fused GEMM (fp32 Y) + dynamic per-row e4m3 quantization of Y through
+    lcml_fp8_gemm_rowquant. Returns (Y fp32, q uint8, s fp32 [M])."""
+    torch = _torch()
+    M = A.shape[0]
+    d, Y = gemm(A, B, sa, sb, out_dtype=torch.float32, desc_only=True, **kw)
+    q = torch.empty(Y.shape, dtype=torch.uint8, device=A.device)
+    s = torch.empty(M, dtype=torch.float32, device=A.device)
+    ws = workspace if workspace is not None else torch.empty(M, dtype=torch.float32, device=A.device)
+    check(lib().lcml_fp8_gemm_rowquant(ctypes.byref(d), _p(q), _p(s), _p(ws), _stream()))
+    return Y, q, s

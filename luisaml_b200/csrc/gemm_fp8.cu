@@ -906,6 +906,24 @@ int lcml_fp8_gemm(const lcml_fp8_gemm_desc *desc, lcml_stream_t stream) {
     return lcml::gemm::gemm_entry(desc, stream, false);
 }
 
+int lcml_fp8_gemm_rowquant(const lcml_fp8_gemm_desc *desc, uint8_t *q, float *q_scale, float *workspace,
+                           lcml_stream_t stream) {
+    LCML_CHECK_ARG(desc != nullptr, "lcml_fp8_gemm_rowquant: desc is NULL");
+    LCML_CHECK_ARG(desc->y_dtype == LCML_DTYPE_FLOAT, "lcml_fp8_gemm_rowquant: Y must be fp32");
+    LCML_CHECK_ARG(desc->row_amax == nullptr, "lcml_fp8_gemm_rowquant: desc->row_amax must be NULL");
+    const int64_t n_out = desc->epilogue == LCML_EPI_SILU_MUL ? desc->N / 2 : desc->N;
+    LCML_CHECK_ARG(desc->ldy == n_out, "lcml_fp8_gemm_rowquant: Y must be dense (ldy == %lld)", (long long)n_out);
+    if (desc->M == 0 || n_out == 0) return LCML_OK;
+    LCML_CHECK_ARG(q && q_scale && workspace, "lcml_fp8_gemm_rowquant: null q / q_scale / workspace");
+    cudaStream_t st = lcml::to_cuda(stream);
+    LCML_CUDA(cudaMemsetAsync(workspace, 0, sizeof(float) * static_cast<size_t>(desc->M), st));
+    lcml_fp8_gemm_desc d = *desc;
+    d.row_amax = workspace;
+    int rc = lcml::gemm::gemm_entry(&d, stream, false);
+    if (rc != LCML_OK) return rc;
+    return lcml_fp8_quantize_from_amax(static_cast<const float *>(d.Y), 1, d.M, n_out, workspace, q_scale, q, stream);
+}
+
 // Test hooks (not in the public header): force the SIMT kernel, or pick the
 // tensor-core kernel variant, so tests can cross-check the code paths.
 int lcml_fp8_gemm_simt(const lcml_fp8_gemm_desc *desc, lcml_stream_t stream) {

@@ -1,0 +1,120 @@
+"""Memory-bound operators around the GEMMs vs the CPU oracle (through the C ABI)."""
+import ctypes
+
+import numpy as np
+import pytest
+
+import oracle
+from conftest import assert_close
+
+pytestmark = pytest.mark.gpu
+
+
+def _t(a, dev):
+    import torch
+    return torch.from_numpy(np.ascontiguousarray(a)).to(dev)
+
+
+def _p(t):
+    return ctypes.c_void_p(t.data_ptr())
+
+
+def _s():
+    import torch
+    return ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+
+
+@pytest.mark.parametrize("op", [0, 1, 2])
+@pytest.mark.parametrize("n", [1, 7, 1 << 16, (1 << 20) + 3])
+def test_unary(dev, op, n):
+    import torch
+    import luisaml_b200 as lb
+    x = (np.random.default_rng(n + op).standard_normal(n) * 5).astype(np.float32)
+    xt = _t(x, dev)
+    y = torch.empty_like(xt)
+    lb.check(lb.lib().lcml_unary_f32(op, _p(xt), _p(y), n, _s()))
+    got = y.cpu().numpy()
+    if op == 0:
+        assert np.array_equal(got, oracle.relu(x))
+    elif op == 1:
+        assert_close(got, oracle.sigmoid(x), rtol=1e-6, atol=1e-7, what="sigmoid")
+    else:
+        assert np.array_equal(got, np.abs(x))
+
+
+@pytest.mark.parametrize("op", [0, 1, 2, 3])
+@pytest.mark.parametrize("shape,bshape", [((64, 48), (48,)), ((1000,), (1,)), ((7, 13), (7, 13)), ((5, 6, 8), (8,))])
+def test_binary_broadcast(dev, op, shape, bshape):
+    import torch
+    import luisaml_b200 as lb
+    rng = np.random.default_rng(op)
+    a = rng.standard_normal(shape).astype(np.float32)
+    b = (rng.standard_normal(bshape) + 3.0).astype(np.float32)
+    at, bt = _t(a, dev), _t(b, dev)
+    y = torch.empty_like(at)
+    lb.check(lb.lib().lcml_binary_f32(op, _p(at), _p(bt), a.size, b.size, _p(y), _s()))
+    ref = [a + b, a - b, a * b, a / b][op].astype(np.float32)
+    assert np.array_equal(y.cpu().numpy(), ref)
+
+
+def test_reduce_max_and_softmax(dev):
+    import torch
+    import luisaml_b200 as lb
+    x = np.random.default_rng(1).standard_normal((37, 1000)).astype(np.float32) * 4
+    xt = _t(x, dev)
+    m = torch.empty(37, dtype=torch.float32, device=dev)
+    lb.check(lb.lib().lcml_reduce_max_rows(_p(xt), 37, 1000, 1, _p(m), _s()))
+    assert np.array_equal(m.cpu().numpy(), np.abs(x).max(axis=1))
+    y = torch.empty_like(xt)
+    lb.check(lb.lib().lcml_softmax_rows(_p(xt), 37, 1000, _p(y), _s()))
+    assert_close(y.cpu().numpy(), oracle.softmax_rows(x), rtol=1e-5, atol=1e-7, what="softmax")
+
+
+@pytest.mark.parametrize("nhwc", [0, 1])
+def test_maxpool_resnet_stem(dev, nhwc):
+    import torch
+    import luisaml_b200 as lb
+    x = np.random.default_rng(2).standard_normal((2, 8, 112, 112)).astype(np.float32)
+    ref = oracle.maxpool2d(x, (3, 3), (2, 2), (1, 1, 1, 1))
+    xin = np.ascontiguousarray(x.transpose(0, 2, 3, 1)) if nhwc else x
+    xt = _t(xin, dev)
+    y = torch.empty(ref.size, dtype=torch.float32, device=dev)
+    lb.check(lb.lib().lcml_maxpool2d(_p(xt), 1, 16, 112, 112, 3, 3, 2, 2, 1, 1, 56, 56, _p(y), nhwc, 8, _s()))
+    got = y.cpu().numpy().reshape((2, 56, 56, 8) if nhwc else ref.shape)
+    if nhwc:
+        got = got.transpose(0, 3, 1, 2)
+    assert np.array_equal(got, ref)
+
+
+def test_maxpool_e4m3_and_gap(dev):
+    import torch
+    import luisaml_b200 as lb
+    x = np.random.default_rng(3).standard_normal((2, 4, 14, 14)).astype(np.float32)
+    q = oracle.quantize(x, np.float32(0.02))
+    xd = oracle.dequantize(q, np.float32(0.02))
+    ref_pool = oracle.maxpool2d(xd, (3, 3), (2, 2), (1, 1, 1, 1))
+    qt = _t(q, dev)
+    y = torch.empty(ref_pool.size, dtype=torch.uint8, device=dev)
+    lb.check(lb.lib().lcml_maxpool2d(_p(qt), 17, 8, 14, 14, 3, 3, 2, 2, 1, 1, 7, 7, _p(y), 0, 4, _s()))
+    got = oracle.dequantize(y.cpu().numpy(), np.float32(0.02)).reshape(ref_pool.shape)
+    assert np.array_equal(got, ref_pool)
+    sc = _t(np.float32([0.02]), dev)
+    g = torch.empty(8, dtype=torch.float32, device=dev)
+    lb.check(lb.lib().lcml_global_avgpool(_p(qt), 17, _p(sc), 2, 4, 196, 0, _p(g), _s()))
+    assert_close(g.cpu().numpy(), oracle.global_avgpool(xd).reshape(-1), rtol=1e-5, atol=1e-6, what="gap e4m3")
+    xt = _t(x, dev)
+    lb.check(lb.lib().lcml_global_avgpool(_p(xt), 1, None, 2, 4, 196, 0, _p(g), _s()))
+    assert_close(g.cpu().numpy(), oracle.global_avgpool(x).reshape(-1), rtol=1e-5, atol=1e-6, what="gap f32")
+
+
+def test_cast_roundtrip(dev):
+    import torch
+    import luisaml_b200 as lb
+    x = np.random.default_rng(4).standard_normal(1003).astype(np.float32)
+    xt = _t(x, dev)
+    b = torch.empty(1003, dtype=torch.bfloat16, device=dev)
+    lb.check(lb.lib().lcml_cast(_p(xt), 1, _p(b), 16, 1003, _s()))
+    assert torch.equal(b, xt.bfloat16())
+    f = torch.empty_like(xt)
+    lb.check(lb.lib().lcml_cast(_p(b), 16, _p(f), 1, 1003, _s()))
+    assert torch.equal(f, b.float())

@@ -249,3 +249,33 @@ def test_kernel_variants_silu(dev, gemm_mode, mode):
     Y = lb.gemm(_t(Aq, dev), _t(Wq, dev), _t(sa, dev), _t(sw, dev), epilogue=lb.EPI_SILU_MUL,
                 out_dtype=torch.float32)
     assert_close(Y.cpu().numpy(), ref, what=f"silu mode {mode}")
+
+
+@pytest.mark.parametrize("epilogue", ["silu", "none"])
+def test_gemm_rowquant(dev, epilogue):
+    """Gemm -> (SiLU*up) -> per-row dynamic QuantizeLinear, as the FFN uses it:
+    the fp32 output matches the oracle within tolerance and the e4m3 bytes and
+    scales are bit-exact given that fp32 output."""
+    import torch
+    import luisaml_b200 as lb
+    M, F, K = 300, 384, 256
+    rng = np.random.default_rng(57)
+    Aq, sa = oracle.quantize_dynamic_rows(rng.standard_normal((M, K)).astype(np.float32))
+    W = (rng.standard_normal((2 * F, K)) * 0.05).astype(np.float32)
+    sw = np.array([oracle.scale_from_amax(oracle.amax(r)) for r in W], dtype=np.float32)
+    Wq = oracle.quantize(W, sw, axis=0)
+    full = oracle.qdq_gemm(Aq, sa, Wq, sw)
+    if epilogue == "silu":
+        g = np.concatenate([full[:, i:i + 128] for i in range(0, 2 * F, 256)], axis=1)
+        u = np.concatenate([full[:, i + 128:i + 256] for i in range(0, 2 * F, 256)], axis=1)
+        ref = oracle.silu_mul(g, u)
+        epi = lb.EPI_SILU_MUL
+    else:
+        ref, epi = full, lb.EPI_NONE
+    ws = torch.full((M,), 123.0, dtype=torch.float32, device=dev)  # stale contents must not matter
+    Y, q, s = lb.gemm_rowquant(_t(Aq, dev), _t(Wq, dev), _t(sa, dev), _t(sw, dev), epilogue=epi, workspace=ws)
+    y = Y.cpu().numpy()
+    assert_close(y, ref, what=f"rowquant {epilogue} fp32")
+    qr, sr = oracle.quantize_dynamic_rows(y)
+    assert np.array_equal(s.cpu().numpy(), sr)
+    assert np.array_equal(q.cpu().numpy(), qr)
