@@ -175,6 +175,25 @@ int lcml_fp8_gemm_rowquant(const lcml_fp8_gemm_desc *desc, uint8_t *q, float *q_
                            lcml_stream_t stream);
 
 /*
+ * lcml_fp8_gemm_rowquant for callers that cannot allocate device memory.
+ * No counterpart in the reference: it exists for hosts that own every byte
+ * of device memory through their own buffer abstraction and have no way to
+ * hand this library a temporary buffer, or that reserve the whole HBM up
+ * front and must not call cudaMalloc (which also synchronises the device)
+ * while serving. Same inputs, outputs and results as lcml_fp8_gemm_rowquant;
+ * the M-float row-max scratch is instead a static device array inside the
+ * library (256 KiB per GPU that loads it, held until the process exits).
+ * Limit: M <= 65536 rows; larger M is rejected with LCML_ERR_INVALID_ARGUMENT
+ * before any work is enqueued. It calls no cudaMalloc / cudaFree.
+ * The first call on each device looks up the array's device address
+ * (cudaGetSymbolAddress); make that first call before any stream capture.
+ * All calls share the array and each call zeroes the rows it uses, so calls
+ * that overlap on the GPU (e.g. on two streams) race and must be serialised.
+ */
+int lcml_fp8_gemm_rowquant_noalloc(const lcml_fp8_gemm_desc *desc, uint8_t *q, float *q_scale,
+                                   lcml_stream_t stream);
+
+/*
  * FP8 2-D convolution, NCHW, lowered to implicit GEMM on the tensor cores.
  * Stands in for Conv::forward (src/onnx/operators/conv.cpp:35-255) fed by
  * DequantizeLinear on X and W. X is e4m3 [N, C, H, W] with a per-tensor

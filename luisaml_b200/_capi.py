@@ -88,6 +88,7 @@ PROTOTYPES = {
     "lcml_fp8_gemm": [ctypes.POINTER(GemmDesc), _vp],
     "lcml_fp8_gemm_simt": [ctypes.POINTER(GemmDesc), _vp],
     "lcml_fp8_gemm_rowquant": [ctypes.POINTER(GemmDesc), _vp, _vp, _vp, _vp],
+    "lcml_fp8_gemm_rowquant_noalloc": [ctypes.POINTER(GemmDesc), _vp, _vp, _vp],
     "lcml_fp8_conv_workspace_size": [ctypes.POINTER(ConvDesc)],
     "lcml_fp8_conv_packed_weight_size": [_c_i64, _c_i64, _c_i64, _c_i64],
     "lcml_fp8_conv_pack_weight": [_vp, _c_i64, _c_i64, _c_i64, _c_i64, _vp, _vp],
