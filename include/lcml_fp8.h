@@ -75,6 +75,16 @@ int lcml_device_error(int *code);
 /* Number of kernels this library has launched in this process (all streams). */
 uint64_t lcml_launch_count(void);
 
+/* Device memory and copies for hosts that have no CUDA runtime of their own
+ * (the C++ executor allocates intermediates once, at prepare time, through
+ * these; the reference gets its buffers from LuisaCompute's Device).
+ * kind: 1 host->device, 2 device->host, 3 device->device. */
+int lcml_device_alloc(size_t bytes, void **ptr);
+int lcml_device_free(void *ptr);
+int lcml_memcpy_async(void *dst, const void *src, size_t bytes, int kind, lcml_stream_t stream);
+int lcml_memset_async(void *dst, int value, size_t bytes, lcml_stream_t stream);
+int lcml_stream_synchronize(lcml_stream_t stream);
+
 /*
  * QuantizeLinear to float8e4m3fn, zero point 0, saturate = 1 (ONNX opset 19+):
  *   y[i] = e4m3(x[i] / s), x / s an IEEE fp32 divide, e4m3() bit-identical to
@@ -192,6 +202,17 @@ int lcml_fp8_gemm_rowquant(const lcml_fp8_gemm_desc *desc, uint8_t *q, float *q_
  */
 int lcml_fp8_gemm_rowquant_noalloc(const lcml_fp8_gemm_desc *desc, uint8_t *q, float *q_scale,
                                    lcml_stream_t stream);
+
+/*
+ * Plain fp32 Gemm, Y = alpha * op(A) * op(B) + beta * C, for graphs without
+ * QDQ nodes (e.g. the reference's fp32 MLP fixture). Follows Gemm::apply
+ * (src/onnx/operators/gemm.cpp:28-325): transA/transB, C broadcast from a
+ * scalar, [N], [M], [1,N], [M,1] or [M,N] (c_ndim < 0: no C), fp32 fma
+ * accumulation. CUDA-core kernel; the FP8 path is lcml_fp8_gemm.
+ */
+int lcml_gemm_f32(const float *A, const float *B, const float *C, int64_t M, int64_t N, int64_t K, int transA,
+                  int transB, float alpha, float beta, int c_ndim, int64_t c_d0, int64_t c_d1, float *Y,
+                  lcml_stream_t stream);
 
 /*
  * FP8 2-D convolution, NCHW, lowered to implicit GEMM on the tensor cores.

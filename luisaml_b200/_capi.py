@@ -78,6 +78,13 @@ PROTOTYPES = {
     "lcml_abi_version": [],
     "lcml_device_check": [],
     "lcml_device_error": [ctypes.POINTER(ctypes.c_int)],
+    "lcml_device_alloc": [ctypes.c_size_t, ctypes.POINTER(ctypes.c_void_p)],
+    "lcml_device_free": [_vp],
+    "lcml_memcpy_async": [_vp, _vp, ctypes.c_size_t, _ci, _vp],
+    "lcml_memset_async": [_vp, _ci, ctypes.c_size_t, _vp],
+    "lcml_stream_synchronize": [_vp],
+    "lcml_gemm_f32": [_vp, _vp, _vp, _c_i64, _c_i64, _c_i64, _ci, _ci, ctypes.c_float, ctypes.c_float, _ci, _c_i64,
+                      _c_i64, _vp, _vp],
     "lcml_fp8_quantize": [_vp, _c_i64, _c_i64, _c_i64, _vp, _ci, _vp, _vp],
     "lcml_fp8_quantize_from_amax": [_vp, _c_i64, _c_i64, _c_i64, _vp, _vp, _vp, _vp],
     "lcml_fp8_quantize_rows_dynamic": [_vp, _c_i64, _c_i64, _c_i64, _vp, _vp, _vp],

@@ -97,3 +97,46 @@ int lcml_device_error(int *code) {
 uint64_t lcml_launch_count(void) { return lcml::g_launches.load(std::memory_order_relaxed); }
 
 }// extern "C"
+
+extern "C" {
+
+int lcml_device_alloc(size_t bytes, void **ptr) {
+    LCML_CHECK_ARG(ptr != nullptr, "lcml_device_alloc: ptr is NULL");
+    *ptr = nullptr;
+    if (bytes == 0) return LCML_OK;
+    LCML_CUDA(cudaMalloc(ptr, bytes));
+    return LCML_OK;
+}
+
+int lcml_device_free(void *ptr) {
+    if (ptr) LCML_CUDA(cudaFree(ptr));
+    return LCML_OK;
+}
+
+int lcml_memcpy_async(void *dst, const void *src, size_t bytes, int kind, lcml_stream_t stream) {
+    if (bytes == 0) return LCML_OK;
+    LCML_CHECK_ARG(dst && src, "lcml_memcpy_async: null pointer");
+    cudaMemcpyKind k;
+    switch (kind) {
+        case 1: k = cudaMemcpyHostToDevice; break;
+        case 2: k = cudaMemcpyDeviceToHost; break;
+        case 3: k = cudaMemcpyDeviceToDevice; break;
+        default: return lcml::set_error(LCML_ERR_INVALID_ARGUMENT, "lcml_memcpy_async: kind %d", kind);
+    }
+    LCML_CUDA(cudaMemcpyAsync(dst, src, bytes, k, lcml::to_cuda(stream)));
+    return LCML_OK;
+}
+
+int lcml_memset_async(void *dst, int value, size_t bytes, lcml_stream_t stream) {
+    if (bytes == 0) return LCML_OK;
+    LCML_CHECK_ARG(dst != nullptr, "lcml_memset_async: null pointer");
+    LCML_CUDA(cudaMemsetAsync(dst, value, bytes, lcml::to_cuda(stream)));
+    return LCML_OK;
+}
+
+int lcml_stream_synchronize(lcml_stream_t stream) {
+    LCML_CUDA(cudaStreamSynchronize(lcml::to_cuda(stream)));
+    return LCML_OK;
+}
+
+}// extern "C"

@@ -1,0 +1,582 @@
+// NetworkInstance: the graph executor (network_instance.cpp in the reference).
+//
+// prepare (first forward):
+//   0. create one Operator per node from the opset        (reference :356-365)
+//   1. bind external inputs/outputs with strict dtype and shape checks (:40-86)
+//   2. create constant tensors: `data_offsets` initializers become views into
+//      the caller's device weight buffer (e4m3 blobs padded to 4 bytes, :215-232),
+//      `raw_data` initializers are uploaded once and keep a host copy
+//   3. fusion pass: DequantizeLinear -> Gemm/MatMul -> (Relu) -> (Cast | QuantizeLinear)
+//      node groups become one FusedQdqGemm (scales, bias, activation and output
+//      cast in the GEMM epilogue, so no dequantized operand ever reaches HBM)
+//   4. allocate the intermediates the remaining nodes touch; view ops alias
+// forward: every non-folded node runs in graph order on the instance's stream
+// (the reference runs them in schedule order inside one generated shader).
+#include <algorithm>
+#include <cstdio>
+#include <cstring>
+#include <map>
+#include <set>
+#include <sstream>
+
+#include "operators.h"
+
+namespace lcml::onnx {
+
+struct FusionInfo {
+    bool skip = false;                      // folded into another node's kernel
+    std::string note;                       // what happened to the node
+    std::unique_ptr<Operator> op;           // replacement operator (fused group)
+    std::vector<std::string> inputs, outputs;  // replacement I/O variable names
+};
+
+namespace {
+
+bool is_gemm_like(const std::string &op) { return op == "Gemm" || op == "MatMul"; }
+
+int64_t attr_int(const Node &n, const char *name, int64_t dflt) {
+    if (auto p = n.try_get_attr(name)) return p->get<AttributeType::INT>();
+    return dflt;
+}
+
+float attr_float(const Node &n, const char *name, float dflt) {
+    if (auto p = n.try_get_attr(name)) return p->get<AttributeType::FLOAT>();
+    return dflt;
+}
+
+ITensor::shape_type to_shape(const std::vector<size_t> &s) {
+    ITensor::shape_type r;
+    for (auto d : s) r.push_back(static_cast<int64_t>(d));
+    return r;
+}
+
+}// namespace
+
+NetworkInstance::NetworkInstance() = default;
+NetworkInstance::~NetworkInstance() {
+    // release operators before the tensors they may reference
+    ops_.clear();
+    fusion_.clear();
+    table_.clear();
+}
+
+void NetworkInstance::set_model(Model model) {
+    model_ = std::move(model);
+    reset();
+}
+
+void NetworkInstance::set_input(std::string_view name, ITensor &t) {
+    inputs_[std::string(name)] = &t;
+    reset();
+}
+
+void NetworkInstance::set_output(std::string_view name, ITensor &t) {
+    outputs_[std::string(name)] = &t;
+    reset();
+}
+
+void NetworkInstance::set_weight_buffer(const void *p, size_t bytes) {
+    weight_buffer_ = p;
+    weight_bytes_ = bytes;
+    reset();
+}
+
+void NetworkInstance::reset() {
+    prepared_ = false;
+    ops_.clear();
+    fusion_.clear();
+    table_.clear();
+}
+
+const FusionInfo *NetworkInstance::fusion_info(size_t i) const { return i < fusion_.size() ? fusion_[i].get() : nullptr; }
+
+size_t NetworkInstance::num_executed_nodes() const {
+    size_t n = 0;
+    for (const auto &f : fusion_)
+        if (!f->skip) ++n;
+    return n;
+}
+
+std::vector<std::string> NetworkInstance::executed_node_summary() const {
+    std::vector<std::string> out;
+    const auto &nodes = model_.get_graph().get_nodes();
+    for (size_t i = 0; i < nodes.size() && i < fusion_.size(); ++i) {
+        std::string s = nodes[i].get_op_type() + " " + nodes[i].get_name() + ": ";
+        s += fusion_[i]->skip ? "folded" : (fusion_[i]->op ? "fused kernel" : "kernel");
+        if (!fusion_[i]->note.empty()) s += " (" + fusion_[i]->note + ")";
+        out.push_back(s);
+    }
+    return out;
+}
+
+void NetworkInstance::create_tensors() {
+    const Graph &g = model_.get_graph();
+    // 1. externals, strictly validated (network_instance.cpp:40-69)
+    auto bind = [&](const char *role, const Variable &v, std::map<std::string, ITensor *, std::less<>> &ext) {
+        auto it = ext.find(v.get_name());
+        if (it == ext.end()) return;
+        ITensor &t = *it->second;
+        if (t.dtype() != v.get_dtype())
+            throw Error(std::string(role) + " '" + v.get_name() + "' element type mismatch: expected " +
+                        dtype_name(v.get_dtype()) + ", got " + dtype_name(t.dtype()));
+        const auto expected = to_shape(v.get_shape());
+        if (t.shape() != expected) {
+            std::ostringstream os;
+            os << role << " '" << v.get_name() << "' shape mismatch: expected [";
+            for (auto d : expected) os << d << ",";
+            os << "], got [";
+            for (auto d : t.shape()) os << d << ",";
+            os << "]";
+            throw Error(os.str());
+        }
+        table_.bind(v.get_name(), t);
+    };
+    for (const auto *v : g.get_inputs()) bind("Input", *v, inputs_);
+    for (const auto *v : g.get_outputs()) bind("Output", *v, outputs_);
+
+    // 2. constants
+    for (const auto &kv : g.get_variables()) {
+        const Variable &v = *kv.second;
+        if (table_.contains(v.get_name()) || !v.is_constant()) continue;
+        const size_t esz = dtype_size(v.get_dtype());
+        size_t n = 1;
+        for (auto d : v.get_shape()) n *= d;
+        if (v.is_trainable_weight()) {
+            if (!weight_buffer_) throw Error("Weight buffer not set but required for variable: " + v.get_name());
+            auto [b, e] = v.get_buffer_range();
+            const bool fp8 = v.get_dtype() == DataType::FLOAT8E4M3FN || v.get_dtype() == DataType::FLOAT8E5M2;
+            const size_t expected = fp8 ? ((n + 3) / 4) * 4 : n * esz;
+            if (e - b != expected) throw Error("Weight buffer size mismatch for variable: " + v.get_name());
+            if (e > weight_bytes_) throw Error("Weight buffer too small for variable: " + v.get_name());
+            auto t = DeviceTensor::borrow(v.get_dtype(), to_shape(v.get_shape()),
+                                          const_cast<uint8_t *>(static_cast<const uint8_t *>(weight_buffer_) + b));
+            t->set_constant({});
+            table_.own(v.get_name(), std::move(t));
+        } else if (!v.get_raw_data().empty()) {
+            if (esz == 0) throw Error("unsupported element type for constant " + v.get_name());
+            if (v.get_raw_data().size() < n * esz) throw Error("raw_data too short for " + v.get_name());
+            auto t = DeviceTensor::allocate(v.get_dtype(), to_shape(v.get_shape()));
+            check_status(lcml_memcpy_async(t->data(), v.get_raw_data().data(), n * esz, 1, stream_), "upload constant");
+            t->set_constant(v.get_raw_data().substr(0, n * esz));
+            table_.own(v.get_name(), std::move(t));
+        }
+    }
+}
+
+void NetworkInstance::run_fusion_pass() {
+    const Graph &g = model_.get_graph();
+    const auto &nodes = g.get_nodes();
+    std::map<std::string, int> producer;
+    std::map<std::string, std::vector<int>> consumers;
+    std::set<std::string> graph_outputs;
+    for (const auto *v : g.get_outputs()) graph_outputs.insert(v->get_name());
+    for (size_t i = 0; i < nodes.size(); ++i) {
+        for (const auto *o : nodes[i].get_outputs()) producer[o->get_name()] = static_cast<int>(i);
+        for (const auto *in : nodes[i].get_inputs()) consumers[in->get_name()].push_back(static_cast<int>(i));
+    }
+    auto sole_consumer = [&](const std::string &var) -> int {
+        if (graph_outputs.count(var)) return -1;
+        auto it = consumers.find(var);
+        if (it == consumers.end() || it->second.size() != 1) return -1;
+        return it->second[0];
+    };
+    auto producer_of = [&](const std::string &var) -> int {
+        auto it = producer.find(var);
+        return it == producer.end() ? -1 : it->second;
+    };
+
+    // a DequantizeLinear usable as a fused operand: e4m3 input, zero point absent or all zero
+    auto dq_ok = [&](int d) {
+        if (d < 0 || nodes[d].get_op_type() != "DequantizeLinear") return false;
+        const Node &dn = nodes[d];
+        if (dn.get_inputs()[0]->get_dtype() != DataType::FLOAT8E4M3FN) return false;
+        if (dn.get_outputs()[0]->get_dtype() != DataType::FLOAT) return false;
+        if (dn.get_inputs().size() > 2) {
+            const std::string &zp = dn.get_inputs()[2]->get_raw_data();
+            if (!dn.get_inputs()[2]->is_constant()) return false;
+            for (char c : zp)
+                if (c != 0) return false;
+        }
+        return true;
+    };
+    // per-axis scale of an operand: number of scale elements and the axis it runs along
+    auto dq_scale_len = [&](int d) -> int64_t {
+        size_t n = 1;
+        for (auto s : nodes[d].get_inputs()[1]->get_shape()) n *= s;
+        return static_cast<int64_t>(n);
+    };
+
+    std::set<int> fused_gemms;
+    std::vector<std::pair<int, int>> dq_uses;  // (dq node, gemm node)
+    auto host_floats = [&](const Variable &v) -> std::vector<float> {
+        std::vector<float> out;
+        if (!table_.contains(v.get_name())) return out;
+        const std::string *h = table_.at(v.get_name()).host_data();
+        if (!h || v.get_dtype() != DataType::FLOAT) return out;
+        out.resize(h->size() / 4);
+        std::memcpy(out.data(), h->data(), out.size() * 4);
+        return out;
+    };
+
+    // ---- Rule: gate/up GEMM pair + Sigmoid / Mul / Mul (SiLU(gate) * up) -> one GEMM
+    // over the two weights interleaved in 128-row groups, SiLU*up in the epilogue.
+    for (size_t mi = 0; mi < nodes.size(); ++mi) {
+        const Node &m2 = nodes[mi];
+        if (m2.get_op_type() != "Mul" || m2.get_inputs().size() != 2) continue;
+        for (int side = 0; side < 2; ++side) {
+            const int m1 = producer_of(m2.get_inputs()[side]->get_name());
+            const int gu = producer_of(m2.get_inputs()[1 - side]->get_name());
+            if (m1 < 0 || gu < 0 || nodes[m1].get_op_type() != "Mul" || nodes[gu].get_op_type() != "Gemm") continue;
+            // m1 = Mul(g, Sigmoid(g)) in either order
+            int gg = -1, sg = -1;
+            for (int k = 0; k < 2; ++k) {
+                const int a = producer_of(nodes[m1].get_inputs()[k]->get_name());
+                const int b = producer_of(nodes[m1].get_inputs()[1 - k]->get_name());
+                if (a >= 0 && b >= 0 && nodes[a].get_op_type() == "Gemm" && nodes[b].get_op_type() == "Sigmoid" &&
+                    nodes[b].get_inputs()[0] == nodes[a].get_outputs()[0]) {
+                    gg = a;
+                    sg = b;
+                }
+            }
+            if (gg < 0) continue;
+            const Node &G = nodes[gg], &U = nodes[gu];
+            const std::string gname = G.get_outputs()[0]->get_name(), uname = U.get_outputs()[0]->get_name();
+            // consumers: g -> {Sigmoid, m1}; Sigmoid -> {m1}; m1 -> {m2}; u -> {m2}
+            if (graph_outputs.count(gname) || graph_outputs.count(uname) || consumers[gname].size() != 2 ||
+                sole_consumer(nodes[sg].get_outputs()[0]->get_name()) != m1 ||
+                sole_consumer(nodes[m1].get_outputs()[0]->get_name()) != static_cast<int>(mi) ||
+                sole_consumer(uname) != static_cast<int>(mi))
+                continue;
+            if (G.get_inputs()[0] != U.get_inputs()[0] || G.get_inputs().size() != 2 || U.get_inputs().size() != 2)
+                continue;
+            if (attr_int(G, "transB", 0) != 1 || attr_int(U, "transB", 0) != 1 || attr_int(G, "transA", 0) ||
+                attr_int(U, "transA", 0) || attr_float(G, "alpha", 1.0f) != 1.0f || attr_float(U, "alpha", 1.0f) != 1.0f)
+                continue;
+            const int da = producer_of(G.get_inputs()[0]->get_name());
+            const int dg = producer_of(G.get_inputs()[1]->get_name());
+            const int du = producer_of(U.get_inputs()[1]->get_name());
+            if (!dq_ok(da) || !dq_ok(dg) || !dq_ok(du)) continue;
+            const Variable &qa = *nodes[da].get_inputs()[0];
+            const Variable &wg = *nodes[dg].get_inputs()[0], &wu = *nodes[du].get_inputs()[0];
+            if (qa.get_shape().size() != 2 || wg.get_shape() != wu.get_shape() || wg.get_shape().size() != 2) continue;
+            const int64_t F = static_cast<int64_t>(wg.get_shape()[0]), K = static_cast<int64_t>(wg.get_shape()[1]);
+            const int64_t M = static_cast<int64_t>(qa.get_shape()[0]);
+            if (F % 128 != 0 || !wg.is_constant() || !wu.is_constant() || !table_.contains(wg.get_name()) ||
+                !table_.contains(wu.get_name()))
+                continue;
+            const int64_t la = dq_scale_len(da);
+            if (la != 1 && (la != M || attr_int(nodes[da], "axis", 1) != 0)) continue;
+            std::vector<float> sgv = host_floats(*nodes[dg].get_inputs()[1]), suv = host_floats(*nodes[du].get_inputs()[1]);
+            auto per_row = [&](std::vector<float> v, int d) -> std::vector<float> {
+                if (v.size() == 1) return std::vector<float>(static_cast<size_t>(F), v[0]);
+                if (static_cast<int64_t>(v.size()) == F && attr_int(nodes[d], "axis", 1) == 0) return v;
+                return {};
+            };
+            sgv = per_row(sgv, dg);
+            suv = per_row(suv, du);
+            if (sgv.empty() || suv.empty()) continue;
+            // interleave [gate 128 rows; up 128 rows] per group, weights on the device, scales on the host
+            auto wcat = DeviceTensor::allocate(DataType::FLOAT8E4M3FN, {2 * F, K});
+            std::vector<float> scat(static_cast<size_t>(2 * F));
+            const uint8_t *pg = table_.at(wg.get_name()).ptr<uint8_t>(), *pu = table_.at(wu.get_name()).ptr<uint8_t>();
+            for (int64_t grp = 0; grp < F / 128; ++grp) {
+                uint8_t *dst = wcat->ptr<uint8_t>() + grp * 256 * K;
+                check_status(lcml_memcpy_async(dst, pg + grp * 128 * K, 128 * K, 3, stream_), "interleave gate");
+                check_status(lcml_memcpy_async(dst + 128 * K, pu + grp * 128 * K, 128 * K, 3, stream_), "interleave up");
+                for (int64_t r = 0; r < 128; ++r) {
+                    scat[grp * 256 + r] = sgv[grp * 128 + r];
+                    scat[grp * 256 + 128 + r] = suv[grp * 128 + r];
+                }
+            }
+            wcat->set_constant({});
+            auto st = DeviceTensor::allocate(DataType::FLOAT, {2 * F});
+            check_status(lcml_memcpy_async(st->data(), scat.data(), scat.size() * 4, 1, stream_), "upload scales");
+            check_status(lcml_stream_synchronize(stream_), "interleave");  // host scale buffer goes out of scope
+            st->set_constant(std::string(reinterpret_cast<const char *>(scat.data()), scat.size() * 4));
+            const std::string wname = m2.get_name() + "#gate_up_weight", sname = m2.get_name() + "#gate_up_scale";
+            table_.own(wname, std::move(wcat));
+            table_.own(sname, std::move(st));
+            auto op = std::make_unique<FusedQdqGemm>();
+            op->epilogue = LCML_EPI_SILU_MUL;
+            auto &fi = *fusion_[mi];
+            fi.inputs = {qa.get_name(), nodes[da].get_inputs()[1]->get_name(), wname, sname};
+            fi.outputs = {m2.get_outputs()[0]->get_name()};
+            fi.note = "gate/up Gemm pair + Sigmoid + Mul + Mul fused into one FP8 GEMM (SiLU*up epilogue)";
+            fi.op = std::move(op);
+            for (int f : {gg, gu, sg, m1}) {
+                fusion_[f]->skip = true;
+                fusion_[f]->note = "folded into the gate/up GEMM at " + m2.get_name();
+            }
+            fused_gemms.insert(gg);
+            fused_gemms.insert(gu);
+            dq_uses.emplace_back(da, gg);
+            dq_uses.emplace_back(dg, gg);
+            dq_uses.emplace_back(du, gu);
+            break;
+        }
+    }
+
+    // ---- Rule: Abs -> ReduceMax(last axis, keepdims 0) -> Div(448) -> QuantizeLinear(axis 0)
+    // on a 2-D tensor -> one dynamic per-row quantization kernel producing q and s.
+    for (size_t qi = 0; qi < nodes.size(); ++qi) {
+        const Node &q = nodes[qi];
+        if (q.get_op_type() != "QuantizeLinear" || q.get_inputs().size() < 2) continue;
+        const Variable &x = *q.get_inputs()[0];
+        if (x.get_shape().size() != 2 || x.get_dtype() != DataType::FLOAT) continue;
+        if (attr_int(q, "axis", 1) != 0 || q.get_outputs()[0]->get_dtype() != DataType::FLOAT8E4M3FN) continue;
+        if (q.get_inputs().size() > 2) continue;
+        const int d = producer_of(q.get_inputs()[1]->get_name());
+        if (d < 0 || nodes[d].get_op_type() != "Div") continue;
+        const int r = producer_of(nodes[d].get_inputs()[0]->get_name());
+        const std::vector<float> c = host_floats(*nodes[d].get_inputs()[1]);
+        if (r < 0 || nodes[r].get_op_type() != "ReduceMax" || c.size() != 1 || c[0] != 448.0f) continue;
+        const std::vector<int64_t> axes = [&] {
+            if (auto p = nodes[r].try_get_attr("axes")) return p->get<AttributeType::INTS>();
+            return std::vector<int64_t>{};
+        }();
+        if (axes.size() != 1 || (axes[0] != -1 && axes[0] != 1) || attr_int(nodes[r], "keepdims", 1) != 0) continue;
+        const int a = producer_of(nodes[r].get_inputs()[0]->get_name());
+        if (a < 0 || nodes[a].get_op_type() != "Abs" || nodes[a].get_inputs()[0] != &x) continue;
+        if (sole_consumer(nodes[a].get_outputs()[0]->get_name()) != r ||
+            sole_consumer(nodes[r].get_outputs()[0]->get_name()) != d)
+            continue;
+        bool late = true;  // every consumer of the scale runs after the QuantizeLinear
+        for (int cidx : consumers[nodes[d].get_outputs()[0]->get_name()])
+            if (cidx < static_cast<int>(qi)) late = false;
+        if (!late) continue;
+        auto &fi = *fusion_[qi];
+        fi.op = std::make_unique<DynamicRowQuant>();
+        fi.inputs = {x.get_name()};
+        fi.outputs = {q.get_outputs()[0]->get_name(), nodes[d].get_outputs()[0]->get_name()};
+        fi.note = "Abs + ReduceMax + Div + QuantizeLinear fused into one dynamic per-row quantization";
+        for (int f : {a, r, d}) {
+            fusion_[f]->skip = true;
+            fusion_[f]->note = "folded into the dynamic quantization at " + q.get_name();
+        }
+    }
+
+    for (size_t gi = 0; gi < nodes.size(); ++gi) {
+        const Node &gn = nodes[gi];
+        if (!is_gemm_like(gn.get_op_type())) continue;
+        if (fusion_[gi]->skip || fusion_[gi]->op) continue;
+        const bool is_gemm = gn.get_op_type() == "Gemm";
+        if (is_gemm && attr_int(gn, "transA", 0) != 0) continue;
+        const int da = producer_of(gn.get_inputs()[0]->get_name());
+        const int db = producer_of(gn.get_inputs()[1]->get_name());
+        if (!dq_ok(da) || !dq_ok(db)) continue;
+        const Variable &qa = *nodes[da].get_inputs()[0];
+        const Variable &qb = *nodes[db].get_inputs()[0];
+        if (qb.get_shape().size() != 2 || qa.get_shape().size() < 2) continue;
+        const bool transB = is_gemm && attr_int(gn, "transB", 0) != 0;
+        const int64_t K = static_cast<int64_t>(qa.get_shape().back());
+        const int64_t N = static_cast<int64_t>(transB ? qb.get_shape()[0] : qb.get_shape()[1]);
+        int64_t M = 1;
+        for (size_t i = 0; i + 1 < qa.get_shape().size(); ++i) M *= static_cast<int64_t>(qa.get_shape()[i]);
+        // scale layouts: A per tensor or per row (axis 0 of a 2-D A); B per tensor or per output column
+        const int64_t la = dq_scale_len(da), lb = dq_scale_len(db);
+        if (la != 1) {
+            if (qa.get_shape().size() != 2 || la != M || attr_int(nodes[da], "axis", 1) != 0) continue;
+        }
+        if (lb != 1) {
+            const int64_t axis = attr_int(nodes[db], "axis", 1);
+            const int64_t want = transB ? 0 : 1;
+            if (lb != N || (axis != want && axis != want - 2)) continue;
+        }
+        (void)K;
+
+        auto op = std::make_unique<FusedQdqGemm>();
+        op->alpha = is_gemm ? attr_float(gn, "alpha", 1.0f) : 1.0f;
+        op->beta = is_gemm ? attr_float(gn, "beta", 1.0f) : 1.0f;
+        std::string b_name = qb.get_name();
+        if (transB) {
+            op->b_kmajor = 1;
+        } else if (qb.is_constant() && table_.contains(qb.get_name())) {
+            // [K, N] constant weight: transpose once into the K-major layout the tensor cores read
+            ITensor &src = table_.at(qb.get_name());
+            auto t = DeviceTensor::allocate(DataType::FLOAT8E4M3FN, {N, static_cast<int64_t>(qb.get_shape()[0])});
+            check_status(lcml_fp8_transpose(src.ptr<uint8_t>(), src.shape(0), src.shape(1), t->ptr<uint8_t>(), stream_),
+                         "transpose weight");
+            t->set_constant({});
+            b_name = qb.get_name() + "#kmajor";
+            table_.own(b_name, std::move(t));
+            op->b_kmajor = 1;
+        } else {
+            op->b_kmajor = 0;
+        }
+        auto &fi = *fusion_[gi];
+        fi.inputs = {qa.get_name(), nodes[da].get_inputs()[1]->get_name(), b_name, nodes[db].get_inputs()[1]->get_name()};
+        if (is_gemm && gn.get_inputs().size() > 2) {
+            op->has_c = true;
+            fi.inputs.push_back(gn.get_inputs()[2]->get_name());
+        }
+        // epilogue chain: (Relu) then (Cast to BFLOAT16/FLOAT | QuantizeLinear with a constant per-tensor scale)
+        std::string out = gn.get_outputs()[0]->get_name();
+        std::vector<int> folded;
+        int c = sole_consumer(out);
+        if (c >= 0 && nodes[c].get_op_type() == "Relu") {
+            op->epilogue = LCML_EPI_RELU;
+            folded.push_back(c);
+            out = nodes[c].get_outputs()[0]->get_name();
+            c = sole_consumer(out);
+        }
+        if (c >= 0 && nodes[c].get_op_type() == "Cast") {
+            const DataType to = nodes[c].get_outputs()[0]->get_dtype();
+            if (to == DataType::BFLOAT16 || to == DataType::FLOAT) {
+                folded.push_back(c);
+                out = nodes[c].get_outputs()[0]->get_name();
+            }
+        } else if (c >= 0 && nodes[c].get_op_type() == "QuantizeLinear") {
+            const Node &qn = nodes[c];
+            const Variable &qs = *qn.get_inputs()[1];
+            size_t qsn = 1;
+            for (auto s : qs.get_shape()) qsn *= s;
+            bool zp_ok = qn.get_inputs().size() < 3;
+            if (!zp_ok && qn.get_inputs()[2]->is_constant()) {
+                zp_ok = true;
+                for (char ch : qn.get_inputs()[2]->get_raw_data())
+                    if (ch != 0) zp_ok = false;
+            }
+            if (qsn == 1 && qs.is_constant() && zp_ok && qn.get_outputs()[0]->get_dtype() == DataType::FLOAT8E4M3FN) {
+                folded.push_back(c);
+                op->has_y_scale = true;
+                fi.inputs.push_back(qs.get_name());
+                out = qn.get_outputs()[0]->get_name();
+            }
+        }
+        fi.outputs = {out};
+        std::string note = "DequantizeLinear x2";
+        for (int f : folded) note += " + " + nodes[f].get_op_type();
+        fi.note = note + " fused into one FP8 GEMM";
+        fi.op = std::move(op);
+        for (int f : folded) {
+            fusion_[f]->skip = true;
+            fusion_[f]->note = "folded into " + gn.get_op_type() + " " + gn.get_name();
+        }
+        fused_gemms.insert(static_cast<int>(gi));
+        dq_uses.emplace_back(da, static_cast<int>(gi));
+        dq_uses.emplace_back(db, static_cast<int>(gi));
+    }
+    // a DequantizeLinear whose every consumer is a fused GEMM never runs
+    std::set<int> dqs;
+    for (auto &u : dq_uses) dqs.insert(u.first);
+    for (int d : dqs) {
+        const std::string &o = nodes[d].get_outputs()[0]->get_name();
+        if (graph_outputs.count(o)) continue;
+        bool all = true;
+        for (int cidx : consumers[o])
+            if (!fused_gemms.count(cidx)) all = false;
+        if (all) {
+            fusion_[d]->skip = true;
+            fusion_[d]->note = "operand read as e4m3 by the fused GEMM";
+        }
+    }
+}
+
+// DequantizeLinear / QuantizeLinear whose inputs are all constants (e.g. the
+// DQ of a weight feeding an fp32 Gemm) run once here; the node is then folded.
+void NetworkInstance::fold_constants() {
+    const Graph &g = model_.get_graph();
+    const auto &nodes = g.get_nodes();
+    std::set<std::string> graph_outputs;
+    for (const auto *v : g.get_outputs()) graph_outputs.insert(v->get_name());
+    for (size_t i = 0; i < nodes.size(); ++i) {
+        if (fusion_[i]->skip) continue;
+        const std::string &op = nodes[i].get_op_type();
+        if (op != "DequantizeLinear" && op != "QuantizeLinear") continue;
+        bool all_const = true;
+        for (const auto *in : nodes[i].get_inputs())
+            if (!in->is_constant() || !table_.contains(in->get_name())) all_const = false;
+        const Variable &out = *nodes[i].get_outputs()[0];
+        if (!all_const || graph_outputs.count(out.get_name()) || table_.contains(out.get_name())) continue;
+        auto t = DeviceTensor::allocate(out.get_dtype(), to_shape(out.get_shape()));
+        std::vector<std::reference_wrapper<ITensor>> ins, outs;
+        for (const auto *in : nodes[i].get_inputs()) ins.emplace_back(table_.at(in->get_name()));
+        outs.emplace_back(*t);
+        ops_[i]->set_environment(*this, table_);
+        ops_[i]->forward(ins, outs);
+        t->set_constant({});
+        table_.own(out.get_name(), std::move(t));
+        fusion_[i]->skip = true;
+        fusion_[i]->note = "constant-folded at prepare";
+    }
+}
+
+void NetworkInstance::prepare() {
+    const Graph &g = model_.get_graph();
+    const auto &nodes = g.get_nodes();
+    ops_.clear();
+    fusion_.clear();
+    table_.clear();
+    for (const auto &n : nodes) {
+        ops_.push_back(model_.get_opset().create_operator(n.get_op_type(), n));
+        fusion_.push_back(std::make_unique<FusionInfo>());
+    }
+    create_tensors();
+    if (fusion_enabled_) {
+        run_fusion_pass();
+        fold_constants();
+    }
+
+    // 4. intermediates touched by nodes that still run; view ops alias their input
+    auto io_inputs = [&](size_t i) {
+        std::vector<std::string> v;
+        if (!fusion_[i]->inputs.empty()) return fusion_[i]->inputs;
+        for (const auto *x : nodes[i].get_inputs()) v.push_back(x->get_name());
+        return v;
+    };
+    auto io_outputs = [&](size_t i) {
+        std::vector<std::string> v;
+        if (!fusion_[i]->outputs.empty()) return fusion_[i]->outputs;
+        for (const auto *x : nodes[i].get_outputs()) v.push_back(x->get_name());
+        return v;
+    };
+    for (size_t i = 0; i < nodes.size(); ++i) {
+        if (fusion_[i]->skip) continue;
+        for (const auto &name : io_outputs(i)) {
+            if (table_.contains(name)) continue;
+            const Variable &v = g.get_var(name);
+            const bool view = ops_[i]->is_output_view(0, nodes[i]) && !nodes[i].get_inputs().empty() &&
+                              table_.contains(nodes[i].get_inputs()[0]->get_name());
+            if (view) {
+                ITensor &src = table_.at(nodes[i].get_inputs()[0]->get_name());
+                auto t = DeviceTensor::borrow(v.get_dtype(), to_shape(v.get_shape()), src.data());
+                t->set_view(true);
+                if (t->nbytes() != src.nbytes()) throw Error(nodes[i].get_op_type() + ": view changes the byte size");
+                table_.own(name, std::move(t));
+            } else {
+                table_.own(name, DeviceTensor::allocate(v.get_dtype(), to_shape(v.get_shape())));
+            }
+        }
+        for (const auto &name : io_inputs(i))
+            if (!table_.contains(name)) throw Error("input '" + name + "' of node " + nodes[i].get_name() + " is not bound");
+    }
+    prepared_ = true;
+}
+
+void NetworkInstance::forward() {
+    if (!prepared_) prepare();
+    const auto &nodes = model_.get_graph().get_nodes();
+    std::vector<std::reference_wrapper<ITensor>> ins, outs;
+    for (size_t i = 0; i < nodes.size(); ++i) {
+        FusionInfo &fi = *fusion_[i];
+        if (fi.skip) continue;
+        ins.clear();
+        outs.clear();
+        if (!fi.inputs.empty()) {
+            for (const auto &n : fi.inputs) ins.emplace_back(table_.at(n));
+        } else {
+            for (const auto *x : nodes[i].get_inputs()) ins.emplace_back(table_.at(x->get_name()));
+        }
+        if (!fi.outputs.empty()) {
+            for (const auto &n : fi.outputs) outs.emplace_back(table_.at(n));
+        } else {
+            for (const auto *x : nodes[i].get_outputs()) outs.emplace_back(table_.at(x->get_name()));
+        }
+        Operator &op = fi.op ? *fi.op : *ops_[i];
+        op.set_environment(*this, table_);
+        if (logging_) std::fprintf(stderr, "[lcml] node %zu %s (%s)\n", i, nodes[i].get_op_type().c_str(), op.get_name().c_str());
+        op.forward(ins, outs);
+    }
+}
+
+}// namespace lcml::onnx

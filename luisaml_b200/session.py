@@ -1,0 +1,107 @@
+"""ctypes binding of include/lcml_session.h: the C++ NetworkInstance driven
+from Python with torch-owned device buffers (plumbing for tests and bench)."""
+from __future__ import annotations
+
+import ctypes
+import os
+
+from ._capi import LcmlError
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "lib", "liblcml_onnx.so")
+
+_lib = None
+_vp, _i64, _ci, _sz = ctypes.c_void_p, ctypes.c_int64, ctypes.c_int, ctypes.c_size_t
+
+
+def load():
+    global _lib
+    if _lib is not None:
+        return _lib
+    if not os.path.exists(LIB_PATH):
+        raise ImportError(f"{LIB_PATH} not built: run `make -C luisaml_b200`")
+    lib = ctypes.CDLL(LIB_PATH)
+    lib.lcml_network_last_error.restype = ctypes.c_char_p
+    lib.lcml_network_create.argtypes = [ctypes.c_char_p, _sz, ctypes.POINTER(_vp)]
+    lib.lcml_network_destroy.argtypes = [_vp]
+    lib.lcml_network_destroy.restype = None
+    lib.lcml_network_info.argtypes = [_vp, ctypes.POINTER(_i64), ctypes.POINTER(_i64), ctypes.POINTER(_i64)]
+    lib.lcml_network_set_weight_buffer.argtypes = [_vp, _vp, _sz]
+    lib.lcml_network_set_input.argtypes = [_vp, ctypes.c_char_p, _vp, _ci, ctypes.POINTER(_i64), _ci]
+    lib.lcml_network_set_output.argtypes = [_vp, ctypes.c_char_p, _vp, _ci, ctypes.POINTER(_i64), _ci]
+    lib.lcml_network_set_fusion.argtypes = [_vp, _ci]
+    lib.lcml_network_set_stream.argtypes = [_vp, _vp]
+    lib.lcml_network_forward.argtypes = [_vp]
+    lib.lcml_network_executed_nodes.argtypes = [_vp, ctypes.POINTER(_i64)]
+    lib.lcml_network_summary.argtypes = [_vp, ctypes.c_char_p, _sz]
+    lib.lcml_opset_size.argtypes = []
+    _lib = lib
+    return lib
+
+
+def _check(rc):
+    if rc != 0:
+        raise LcmlError(rc, load().lcml_network_last_error().decode(errors="replace"))
+
+
+_TORCH_DT = {"float32": 1, "bfloat16": 16, "uint8": 17}
+
+
+class Network:
+    """A loaded LuisaML-JSON model bound to device buffers."""
+
+    def __init__(self, json_text: str):
+        lib = load()
+        data = json_text.encode()
+        h = _vp()
+        _check(lib.lcml_network_create(data, len(data), ctypes.byref(h)))
+        self._h = h
+        self._keep = []
+
+    def close(self):
+        if getattr(self, "_h", None):
+            load().lcml_network_destroy(self._h)
+            self._h = None
+
+    def __del__(self):
+        self.close()
+
+    def info(self):
+        n, i, o = _i64(), _i64(), _i64()
+        _check(load().lcml_network_info(self._h, ctypes.byref(n), ctypes.byref(i), ctypes.byref(o)))
+        return n.value, i.value, o.value
+
+    def set_weight_buffer(self, t):
+        self._keep.append(t)
+        _check(load().lcml_network_set_weight_buffer(self._h, t.data_ptr(), t.numel() * t.element_size()))
+
+    def _bind(self, fn, name, t, dtype=None):
+        self._keep.append(t)
+        dt = dtype if dtype is not None else _TORCH_DT[str(t.dtype).replace("torch.", "")]
+        shape = (_i64 * max(1, t.dim()))(*t.shape)
+        _check(fn(self._h, name.encode(), t.data_ptr(), dt, shape, t.dim()))
+
+    def set_input(self, name, t, dtype=None):
+        self._bind(load().lcml_network_set_input, name, t, dtype)
+
+    def set_output(self, name, t, dtype=None):
+        self._bind(load().lcml_network_set_output, name, t, dtype)
+
+    def set_fusion(self, enable: bool):
+        _check(load().lcml_network_set_fusion(self._h, int(enable)))
+
+    def set_stream(self, stream_handle: int):
+        _check(load().lcml_network_set_stream(self._h, stream_handle))
+
+    def forward(self):
+        _check(load().lcml_network_forward(self._h))
+
+    def executed_nodes(self) -> int:
+        n = _i64()
+        _check(load().lcml_network_executed_nodes(self._h, ctypes.byref(n)))
+        return n.value
+
+    def summary(self) -> str:
+        buf = ctypes.create_string_buffer(1 << 16)
+        _check(load().lcml_network_summary(self._h, buf, len(buf)))
+        return buf.value.decode()

@@ -1,0 +1,181 @@
+"""NetworkInstance on the GPU: whole graphs through the C++ executor.
+
+* the reference's fp32 MLP known-answer fixture (tests/onnx/output/, copied to
+  tests/golden/simple_mlp/) must reproduce output_ref.bin within the
+  reference's own tolerance (abs 1e-3, tests/onnx/test_onnx_inference.cpp:232)
+  and equal the CPU oracle's K-ordered fma result bit for bit;
+* the QDQ MLP benchmark graph (e4m3 weights + DequantizeLinear) must equal the
+  oracle bit for bit;
+* a fully quantized graph (QuantizeLinear on activations) runs as fused FP8
+  GEMMs and agrees with the unfused node-by-node execution and the oracle.
+"""
+import os
+
+import numpy as np
+import pytest
+
+import oracle
+from conftest import GOLDEN, assert_close
+
+pytestmark = pytest.mark.gpu
+
+
+def _t(a, dev):
+    import torch
+    return torch.from_numpy(np.array(a, copy=True)).to(dev)
+
+
+def test_reference_fp32_mlp_fixture(dev):
+    import torch
+    from luisaml_b200.session import Network
+    d = os.path.join(GOLDEN, "simple_mlp")
+    net = Network(open(os.path.join(d, "simple_mlp.onnx.json")).read())
+    blob = np.fromfile(os.path.join(d, "simple_mlp.safetensors"), dtype=np.uint8)
+    x = np.fromfile(os.path.join(d, "input_ref.bin"), dtype=np.float32).reshape(1, 784)
+    ref = np.fromfile(os.path.join(d, "output_ref.bin"), dtype=np.float32).reshape(1, 10)
+    wb, xt = _t(blob, dev), _t(x, dev)
+    y = torch.empty((1, 10), dtype=torch.float32, device=dev)
+    net.set_weight_buffer(wb)
+    net.set_input("input", xt)
+    net.set_output("output", y)
+    net.forward()
+    got = y.cpu().numpy()
+    assert np.abs(got - ref).max() <= 1e-3, (got, ref)
+    # oracle: the same graph with gemm.cpp's loop on the host
+    f = lambda name, off, shape: np.frombuffer(blob[off[0]:off[1]].tobytes(), dtype=np.float32).reshape(shape)  # noqa: E731
+    import json
+    inits = {i["name"]: i for i in json.load(open(os.path.join(d, "simple_mlp.onnx.json")))["graph"]["initializer"]}
+    W = {k: f(k, v["data_offsets"], [int(s) for s in v["dims"]]) for k, v in inits.items()}
+    h = oracle.relu(oracle.gemm(x, W["net.0.weight"], W["net.0.bias"], transB=1))
+    h = oracle.relu(oracle.gemm(h, W["net.2.weight"], W["net.2.bias"], transB=1))
+    h = oracle.gemm(h, W["net.4.weight"], W["net.4.bias"], transB=1)
+    assert np.array_equal(got, h)
+
+
+@pytest.mark.parametrize("fusion", [True, False])
+def test_qdq_mlp_graph(dev, fusion):
+    import torch
+    from luisaml_b200 import graphs
+    from luisaml_b200.session import Network
+    text, blob, meta = graphs.mlp(batch=32)
+    net = Network(text)
+    net.set_fusion(fusion)
+    x = np.random.default_rng(1000).random((32, 784), dtype=np.float32)
+    y = torch.empty((32, 10), dtype=torch.float32, device=dev)
+    net.set_weight_buffer(_t(np.frombuffer(blob, dtype=np.uint8), dev))
+    net.set_input("input", _t(x, dev))
+    net.set_output("output", y)
+    net.forward()
+    net.forward()  # a second forward reuses the prepared state
+    h = x
+    for i, L in enumerate(meta["layers"]):
+        w = oracle.dequantize(L["q"], L["s"][0])
+        h = oracle.gemm(h, w, L["bias"], transB=1)
+        if i < 2:
+            h = oracle.relu(h)
+    assert np.array_equal(y.cpu().numpy(), h)
+    assert net.executed_nodes() == (5 if fusion else 8)  # DQ of constant weights folded at prepare
+
+
+def _quantized_mlp(batch, dims, seed):
+    """x -> QuantizeLinear(static s_x) -> DequantizeLinear -> Gemm(DQ W, b) -> Relu
+    -> QuantizeLinear(static) -> DequantizeLinear -> Gemm -> ... (activations and weights QDQ)."""
+    from luisaml_b200.export import GraphBuilder, qdq_weight, scale_from_amax
+    b = GraphBuilder("qdq_mlp_full")
+    b.input("x", "FLOAT", (batch, dims[0]))
+    rng = np.random.default_rng(seed)
+    h = "x"
+    meta = []
+    for li in range(len(dims) - 1):
+        sx = np.float32([0.02 if li else 1.0 / 448 * 4.5])  # calibrated-style static activation scales
+        b.const(f"sx{li}", sx[0:1].reshape(()))
+        q = b.value(f"xq{li}", "FLOAT8E4M3FN", (batch, dims[li]))
+        b.node("QuantizeLinear", [h, f"sx{li}"], [q])
+        dq = b.value(f"xdq{li}", "FLOAT", (batch, dims[li]))
+        b.node("DequantizeLinear", [q, f"sx{li}"], [dq])
+        w = (rng.standard_normal((dims[li + 1], dims[li])) / np.sqrt(dims[li])).astype(np.float32)
+        wdq, wq, ws = qdq_weight(b, f"w{li}", w, axis=0)
+        bias = (rng.standard_normal(dims[li + 1]) * 0.01).astype(np.float32)
+        b.const(f"b{li}", bias)
+        last = li == len(dims) - 2
+        out = "y" if last else b.value(f"g{li}", "FLOAT", (batch, dims[li + 1]))
+        if last:
+            b.output("y", "FLOAT", (batch, dims[li + 1]))
+        b.node("Gemm", [dq, wdq, f"b{li}"], [out], transB=1)
+        if not last:
+            r = b.value(f"r{li}", "FLOAT", (batch, dims[li + 1]))
+            b.node("Relu", [out], [r])
+            h = r
+        meta.append((sx, wq, ws, bias))
+    return b.to_json(), bytes(b.blob), meta
+
+
+def test_fully_quantized_graph_fuses(dev):
+    import torch
+    from luisaml_b200.session import Network
+    batch, dims = 64, (256, 512, 384, 128)
+    text, blob, meta = _quantized_mlp(batch, dims, seed=5)
+    x = np.random.default_rng(6).standard_normal((batch, dims[0])).astype(np.float32)
+    outs = {}
+    for fusion in (True, False):
+        net = Network(text)
+        net.set_fusion(fusion)
+        y = torch.empty((batch, dims[-1]), dtype=torch.float32, device=dev)
+        net.set_weight_buffer(_t(np.frombuffer(blob, dtype=np.uint8), dev))
+        net.set_input("x", _t(x, dev))
+        net.set_output("y", y)
+        net.forward()
+        outs[fusion] = y.cpu().numpy()
+        if fusion:
+            s = net.summary()
+            assert s.count("fused kernel") == 3 and "folded" in s, s
+            # the input QuantizeLinear + 3 fused GEMMs; each Relu -> QuantizeLinear pair
+            # is folded into the previous GEMM, which stores e4m3 directly
+            assert net.executed_nodes() == 1 + 3
+    # oracle: quantize activations, dequantize both, gemm.cpp's loop
+    h = x
+    for li, (sx, wq, ws, bias) in enumerate(meta):
+        hq = oracle.quantize(h, sx[0])
+        a = oracle.dequantize(hq, sx[0])
+        w = oracle.dequantize(wq, ws, axis=0)
+        h = oracle.gemm(a, w, bias, transB=1)
+        if li < len(meta) - 1:
+            h = oracle.relu(h)
+    assert_close(outs[True], h, what="fused graph vs oracle")
+    assert_close(outs[False], h, what="unfused graph vs oracle")
+
+
+def _run_ffn(dev, text, blob, x, fusion):
+    import torch
+    from luisaml_b200.session import Network
+    net = Network(text)
+    net.set_fusion(fusion)
+    y = torch.empty(x.shape, dtype=torch.bfloat16, device=dev)
+    net.set_weight_buffer(_t(np.frombuffer(blob, dtype=np.uint8), dev))
+    net.set_input("x", _t(x, dev))
+    net.set_output("y", y)
+    net.forward()
+    return net, y.float().cpu().numpy()
+
+
+def test_ffn_graph_fused_vs_oracle(dev):
+    """Llama-style FFN as ONNX nodes: the fusion pass must turn it into four
+    kernels (two dynamic per-row quantizations, the gate/up GEMM with the
+    SiLU*up epilogue, the down GEMM with residual and bf16 store) and match
+    the oracle chain and the unfused node-by-node execution."""
+    from conftest import assert_close_bf16
+    from luisaml_b200 import graphs
+    T, D, F = 256, 512, 1024
+    text, blob, meta = graphs.ffn(T, D, F)
+    x = np.random.default_rng(3000).standard_normal((T, D)).astype(np.float32)
+    net, y_fused = _run_ffn(dev, text, blob, x, True)
+    assert net.executed_nodes() == 4, net.summary()
+    _, y_unfused = _run_ffn(dev, text, blob, x, False)
+    xq, sx = oracle.quantize_dynamic_rows(x)
+    g = oracle.qdq_gemm(xq, sx, meta["wg_q"], meta["wg_s"])
+    u = oracle.qdq_gemm(xq, sx, meta["wu_q"], meta["wu_s"])
+    h = oracle.silu_mul(g, u)
+    hq, sh = oracle.quantize_dynamic_rows(h)
+    ref = oracle.qdq_gemm(hq, sh, meta["wd_q"], meta["wd_s"]) + x
+    assert_close_bf16(y_fused, ref, what="fused FFN vs oracle")
+    assert_close_bf16(y_unfused, ref, what="unfused FFN vs oracle")
