@@ -349,7 +349,133 @@ class FfnWorkload(GraphWorkload):
                 "kind": "port", "sample": f"{rows} token rows of the FFN (quantize, gate/up, SiLU*up, quantize, down)"}
 
 
+class TpGemmWorkload:
+    """A [16384, 8192] dynamically per-token quantized, B [8192, 28672]
+    per-column e4m3, Y bf16 [16384, 28672]. N is split across ranks; each rank's
+    GEMM epilogue stores its shard into every rank's output over NVLink
+    (fused all-gather, mode "fused") or the shards are all-gathered by NCCL and
+    re-laid out (mode "nccl", the library baseline). Strong scaling."""
+
+    unit = "TFLOP/s"
+    scaling = "strong"
+
+    def __init__(self, M=16384, K=8192, N=28672, mode=None):
+        self.M, self.K, self.N = M, K, N
+        self.mode = mode or os.environ.get("LCML_TP_MODE", "fused")
+        self.parallelism = ("N split; all-gather fused into the GEMM epilogue (P2P stores over NVLink)"
+                            if self.mode == "fused" else "N split; NCCL all-gather + re-layout")
+        self.e2e_path = "pinned host A -> H2D -> per-token quantize -> TP GEMM (+ all-gather) -> D2H of this rank's shard"
+
+    def describe(self):
+        return {"workload": f"tp_fp8_gemm_{self.M}x{self.N}x{self.K}", "mode": self.mode,
+                "shard_columns": self.Nr, "l2": "inputs larger than L2; L2 flushed between timed steps"}
+
+    def setup(self, dev, seed):
+        import ctypes
+        import torch
+        import torch.distributed as dist
+        import luisaml_b200 as lb
+        from luisaml_b200 import tp
+        self.ws = int(os.environ.get("WORLD_SIZE", "1"))
+        self.rank = int(os.environ.get("RANK", "0"))
+        self.dist = dist
+        M, K, N = self.M, self.K, self.N
+        start, stop = tp.shard_columns(N, self.ws, self.rank)
+        self.start, self.Nr = start, stop - start
+        self.flops = 2.0 * M * N * K / self.ws
+        self.A = torch.randn((M, K), generator=torch.Generator(device=dev).manual_seed(5000), device=dev)
+        Bt = tp.column_block_weights(torch, K, start, stop, dev, 5100, 0.02)
+        self.Bq, self.sb = lb.quantize_rows_dynamic(Bt)  # per-column scales of B = per-row of B^T
+        del Bt
+        self.Aq = torch.empty((M, K), dtype=torch.uint8, device=dev)
+        self.sa = torch.empty(M, dtype=torch.float32, device=dev)
+        self.peers = None
+        if self.ws > 1 and self.mode == "fused":
+            self.peers = tp.PeerOutputs(torch, dist, M * N * 2, dev)
+            ybase, npeers, peer_arr = self.peers.local, self.ws - 1, self.peers.peer_array.data_ptr()
+            ldy, off = N, start
+        elif self.ws > 1:
+            self.Yr = torch.empty((M, self.Nr), dtype=torch.bfloat16, device=dev)
+            self.gathered = torch.empty((self.ws * M * self.Nr,), dtype=torch.bfloat16, device=dev)
+            self.Y = torch.empty((M, N), dtype=torch.bfloat16, device=dev)
+            ybase, npeers, peer_arr, ldy, off = self.Yr.data_ptr(), 0, 0, self.Nr, 0
+        else:
+            self.Y = torch.empty((M, N), dtype=torch.bfloat16, device=dev)
+            ybase, npeers, peer_arr, ldy, off = self.Y.data_ptr(), 0, 0, N, 0
+        d = lb.GemmDesc()
+        d.M, d.N, d.K = M, self.Nr, K
+        d.A, d.lda, d.B, d.ldb, d.b_kmajor = self.Aq.data_ptr(), K, self.Bq.data_ptr(), K, 1
+        d.scale_a, d.scale_a_mode, d.scale_b, d.scale_b_mode = self.sa.data_ptr(), lb.SCALE_ROW, self.sb.data_ptr(), lb.SCALE_COL
+        d.alpha, d.beta = 1.0, 1.0
+        d.Y, d.y_dtype, d.ldy, d.y_col_offset = ybase, lb.DTYPE_BFLOAT16, ldy, off
+        d.y_peers, d.y_num_peers = peer_arr, npeers
+        self.desc = d
+        self.lib = lb.lib()
+        self.barrier_t = torch.zeros(1, device=dev)
+        self.ctypes = ctypes
+
+    def step(self, stream, ev=None):
+        import luisaml_b200 as lb
+        c = self.ctypes
+        s = c.c_void_p(stream.cuda_stream)
+        lb.check(self.lib.lcml_fp8_quantize_rows_dynamic(c.c_void_p(self.A.data_ptr()), self.M, self.K, self.K,
+                                                         c.c_void_p(self.sa.data_ptr()), c.c_void_p(self.Aq.data_ptr()), s))
+        if ev is not None:
+            ev[0].record(stream)
+        lb.check(self.lib.lcml_fp8_gemm(c.byref(self.desc), s))
+        if ev is not None:
+            ev[1].record(stream)
+        if self.ws > 1 and self.mode == "fused":
+            self.dist.all_reduce(self.barrier_t)  # every shard has landed in every rank's output
+        elif self.ws > 1:
+            self.dist.all_gather_into_tensor(self.gathered, self.Yr.reshape(-1))
+            self.Y.copy_(self.gathered.view(self.ws, self.M, self.Nr).permute(1, 0, 2).reshape(self.M, self.N))
+
+    def setup_e2e(self):
+        import torch
+        self.A_host = self.A.cpu().pin_memory()
+        self.out_host = torch.empty((self.M, self.Nr), dtype=torch.bfloat16).pin_memory()
+        self.h2d = self.A_host.numel() * 4
+        self.d2h = self.out_host.numel() * 2
+
+    def step_e2e(self, stream):
+        self.A.copy_(self.A_host, non_blocking=True)
+        self.step(stream)
+        if self.peers is not None:
+            import ctypes
+            self.lib.lcml_memcpy_async(ctypes.c_void_p(self.out_host.data_ptr()), ctypes.c_void_p(self.peers.local),
+                                       self.out_host.numel() * 2, 2, ctypes.c_void_p(stream.cuda_stream))
+        else:
+            src = self.Y[:, self.start:self.start + self.Nr] if hasattr(self, "Y") else self.Yr
+            self.out_host.copy_(src, non_blocking=True)
+
+    def dominant(self):
+        return {"kernel": "gemm_fp8_tc2" + (" (+ fused all-gather)" if self.mode == "fused" and self.ws > 1 else ""),
+                "bound": "tensor" if self.ws == 1 else "nvlink", "unit": "TFLOP/s", "work": self.flops,
+                "profile": "tp_gemm"}
+
+    def cpu_sample(self, budget_s=12.0):
+        import oracle
+        rng = np.random.default_rng(0)
+        K, N = self.K, self.N
+        rows = 1
+        x = rng.standard_normal((rows, K)).astype(np.float32)
+        bq = rng.integers(0, 0x60, size=(N, K), dtype=np.uint8)
+        sb = np.full(N, 0.001, np.float32)
+        t0 = time.perf_counter()
+        xq, sx = oracle.quantize_dynamic_rows(x)
+        oracle.qdq_gemm(xq, sx, bq, sb)
+        t = time.perf_counter() - t0
+        return {"value": 2.0 * rows * N * K / t / 1e12, "unit": "TFLOP/s", "cores": oracle.num_threads(), "kind": "port",
+                "sample": f"{rows} row of the {self.M}x{self.N}x{self.K} TP GEMM (quantize + DQ + fma loop)"}
+
+    def close(self):
+        if self.peers is not None:
+            self.peers.close()
+
+
 CONFIGS = {
+    "tp_gemm": lambda: TpGemmWorkload(),
     "mlp": lambda: MlpWorkload(),
     "ffn": lambda: FfnWorkload(),
     "gemm8192": lambda: GemmWorkload(8192, 8192, 8192, "qdq_gemm_8192x8192x8192"),
@@ -490,12 +616,18 @@ def run_ours(args, wl):
     if rank == 0:
         line = {"metric": METRIC if unit == "TFLOP/s" else f"{wl.describe()['workload']} {unit}", "value": value,
                 "unit": unit, "n_gpus": ws, "steps": n,
-                "warmup": args.warmup, "ms_per_step": total_ms / n, "higher_is_better": True, "scaling": "weak",
+                "warmup": args.warmup, "ms_per_step": total_ms / n, "higher_is_better": True,
+                "scaling": getattr(wl, "scaling", "weak"),
                 "vs_baseline": None, "dtype": "e4m3 x e4m3 -> fp32 accumulate, bf16 out", "data": "synthetic",
                 "config": wl.describe(), "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e,
                 "gpu_launches": launches, "clocks": clk.summary(),
                 "parallelism": getattr(wl, "parallelism", "replicas") if ws > 1 else "single"}
         print(json.dumps(line), flush=True)
+    if hasattr(wl, "close"):
+        torch.cuda.synchronize()
+        if ws > 1:
+            dist.barrier()
+        wl.close()
     if ws > 1:
         dist.destroy_process_group()
 

@@ -75,6 +75,16 @@ int lcml_device_error(int *code);
 /* Number of kernels this library has launched in this process (all streams). */
 uint64_t lcml_launch_count(void);
 
+/* CUDA IPC for the fused all-gather: export a buffer allocated with
+ * lcml_device_alloc as an opaque handle (LCML_IPC_HANDLE_BYTES), map a peer
+ * process's handle into this process, and unmap it. */
+#define LCML_IPC_HANDLE_BYTES 64
+int lcml_ipc_get_handle(void *device_ptr, void *handle_out);
+int lcml_ipc_open(const void *handle, void **device_ptr);
+int lcml_ipc_close(void *device_ptr);
+/* Enables peer access from the current device to `peer_device` (no-op if already on). */
+int lcml_enable_peer_access(int peer_device);
+
 /* Device memory and copies for hosts that have no CUDA runtime of their own
  * (the C++ executor allocates intermediates once, at prepare time, through
  * these; the reference gets its buffers from LuisaCompute's Device).
@@ -164,6 +174,15 @@ typedef struct lcml_fp8_gemm_desc {
     int64_t ldy;
     const float *y_scale; /* device, per-tensor output scale when y_dtype is e4m3 */
     float *row_amax;      /* optional device [M]: max |v| per row (atomic; zero it first) */
+    /* Output placement for a column shard of a larger matrix, and the fused
+     * all-gather of tensor-parallel GEMMs: every output element (row, col) is
+     * stored at Y[row * ldy + y_col_offset + col] and at the same offset of
+     * each of the y_num_peers buffers in y_peers (other GPUs' outputs mapped
+     * with lcml_ipc_open), so the shard reaches every rank while the GEMM
+     * runs. Zero-initialise these fields when unused. */
+    int64_t y_col_offset;
+    void *const *y_peers; /* device array of y_num_peers device pointers */
+    int y_num_peers;
 } lcml_fp8_gemm_desc;
 
 int lcml_fp8_gemm(const lcml_fp8_gemm_desc *desc, lcml_stream_t stream);

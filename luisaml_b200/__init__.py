@@ -179,6 +179,8 @@ def gemm(A, B, sa, sb, *, b_kmajor=True, alpha=1.0, beta=1.0, c_vec=None, c_vec_
     if row_amax is not None:
         d.row_amax = row_amax.data_ptr()
     if desc_only:
+        # the descriptor holds raw device pointers: keep the tensors they point into alive with it
+        d._refs = (A, B, sa, sb, c_vec, c_mat, Y, y_scale, row_amax)
         return d, Y
     fn = lib().lcml_fp8_gemm_simt if simt else lib().lcml_fp8_gemm
     check(fn(ctypes.byref(d), _stream()))

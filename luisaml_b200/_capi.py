@@ -51,6 +51,9 @@ class GemmDesc(ctypes.Structure):
         ("Y", ctypes.c_void_p), ("y_dtype", ctypes.c_int), ("ldy", ctypes.c_int64),
         ("y_scale", ctypes.c_void_p),
         ("row_amax", ctypes.c_void_p),
+        ("y_col_offset", ctypes.c_int64),
+        ("y_peers", ctypes.c_void_p),
+        ("y_num_peers", ctypes.c_int),
     ]
 
 
@@ -83,6 +86,10 @@ PROTOTYPES = {
     "lcml_memcpy_async": [_vp, _vp, ctypes.c_size_t, _ci, _vp],
     "lcml_memset_async": [_vp, _ci, ctypes.c_size_t, _vp],
     "lcml_stream_synchronize": [_vp],
+    "lcml_ipc_get_handle": [_vp, _vp],
+    "lcml_ipc_open": [_vp, ctypes.POINTER(ctypes.c_void_p)],
+    "lcml_ipc_close": [_vp],
+    "lcml_enable_peer_access": [_ci],
     "lcml_gemm_f32": [_vp, _vp, _vp, _c_i64, _c_i64, _c_i64, _ci, _ci, ctypes.c_float, ctypes.c_float, _ci, _c_i64,
                       _c_i64, _vp, _vp],
     "lcml_fp8_quantize": [_vp, _c_i64, _c_i64, _c_i64, _vp, _ci, _vp, _vp],

@@ -51,6 +51,9 @@ struct EpiParams {
     int64_t ldy;
     const float *y_scale;
     float *row_amax;
+    int64_t y_col_offset;
+    void *const *y_peers;
+    int y_num_peers;
 };
 
 __device__ __forceinline__ float silu_mul(float g, float u) {
@@ -65,10 +68,10 @@ __device__ __forceinline__ float load_cmat(const EpiParams &ep, int64_t row, int
 }
 
 template <int OUT>
-__device__ __forceinline__ void store_out(const EpiParams &ep, int64_t row, int64_t col, float v, float ys) {
-    if (OUT == kOutF32) reinterpret_cast<float *>(ep.y)[row * ep.ldy + col] = v;
-    else if (OUT == kOutBF16) reinterpret_cast<__nv_bfloat16 *>(ep.y)[row * ep.ldy + col] = __float2bfloat16_rn(v);
-    else reinterpret_cast<uint8_t *>(ep.y)[row * ep.ldy + col] = static_cast<uint8_t>(quantize1(v, ys));
+__device__ __forceinline__ void store_out(void *y, int64_t ldy, int64_t row, int64_t col, float v, float ys) {
+    if (OUT == kOutF32) reinterpret_cast<float *>(y)[row * ldy + col] = v;
+    else if (OUT == kOutBF16) reinterpret_cast<__nv_bfloat16 *>(y)[row * ldy + col] = __float2bfloat16_rn(v);
+    else reinterpret_cast<uint8_t *>(y)[row * ldy + col] = static_cast<uint8_t>(quantize1(v, ys));
 }
 
 // Per-column factors of 32 consecutive gemm columns [n0, n0+32): the B scale
@@ -163,11 +166,24 @@ __device__ __forceinline__ void load_cmat32(const EpiParams &ep, int64_t row, in
 // Stores 32 consecutive output values of one row (vector stores when the row
 // segment is in range and 16-byte aligned).
 template <int OUT>
+__device__ __forceinline__ void store_row32_to(const EpiParams &ep, void *ybase, int64_t row, int64_t col0, int64_t n_out,
+                                               const float (&v)[32], float ys);
+
+// Stores to the local output and, for the fused all-gather, to every peer's.
+template <int OUT>
 __device__ __forceinline__ void store_row32(const EpiParams &ep, int64_t row, int64_t col0, int64_t n_out,
                                             const float (&v)[32], float ys) {
+    store_row32_to<OUT>(ep, ep.y, row, col0, n_out, v, ys);
+    for (int p = 0; p < ep.y_num_peers; ++p) store_row32_to<OUT>(ep, ep.y_peers[p], row, col0, n_out, v, ys);
+}
+
+template <int OUT>
+__device__ __forceinline__ void store_row32_to(const EpiParams &ep, void *ybase, int64_t row, int64_t col0, int64_t n_out,
+                                               const float (&v)[32], float ys) {
     const bool full = (col0 + 32 <= n_out);
+    const int64_t ocol0 = col0 + ep.y_col_offset;
     if (OUT == kOutBF16) {
-        __nv_bfloat16 *yp = reinterpret_cast<__nv_bfloat16 *>(ep.y) + row * ep.ldy + col0;
+        __nv_bfloat16 *yp = reinterpret_cast<__nv_bfloat16 *>(ybase) + row * ep.ldy + ocol0;
         if (full && aligned(yp, 16)) {
             uint32_t p[16];
 #pragma unroll
@@ -181,7 +197,7 @@ __device__ __forceinline__ void store_row32(const EpiParams &ep, int64_t row, in
             return;
         }
     } else if (OUT == kOutF32) {
-        float *yp = reinterpret_cast<float *>(ep.y) + row * ep.ldy + col0;
+        float *yp = reinterpret_cast<float *>(ybase) + row * ep.ldy + ocol0;
         if (full && aligned(yp, 16)) {
 #pragma unroll
             for (int j = 0; j < 8; ++j)
@@ -189,7 +205,7 @@ __device__ __forceinline__ void store_row32(const EpiParams &ep, int64_t row, in
             return;
         }
     } else {
-        uint8_t *yp = reinterpret_cast<uint8_t *>(ep.y) + row * ep.ldy + col0;
+        uint8_t *yp = reinterpret_cast<uint8_t *>(ybase) + row * ep.ldy + ocol0;
         if (full && aligned(yp, 16)) {
             uint32_t p[8];
 #pragma unroll
@@ -203,7 +219,60 @@ __device__ __forceinline__ void store_row32(const EpiParams &ep, int64_t row, in
     }
 #pragma unroll
     for (int j = 0; j < 32; ++j)
-        if (col0 + j < n_out) store_out<OUT>(ep, row, col0 + j, v[j], ys);
+        if (col0 + j < n_out) store_out<OUT>(ybase, ep.ldy, row, ocol0 + j, v[j], ys);
+}
+
+// Warp-cooperative store of a 32-row x 32-column chunk through shared memory:
+// lane l holds row (row0 + l); after a swizzled transpose each store
+// instruction writes whole 16-byte pieces of (32 / P) consecutive rows, i.e.
+// (32 / P) contiguous row segments of 32 elements, instead of 32 scattered
+// 16-byte pieces. Used when the output also goes to peer GPUs, where NVLink
+// write efficiency depends on contiguous segments. `stage` holds 32 x 32
+// elements for this warp. All 32 lanes must call it.
+template <int OUT>
+__device__ __forceinline__ void store_chunk_staged(const EpiParams &ep, uint8_t *stage, int64_t row0, int64_t col0,
+                                                   const float (&v)[32], float ys) {
+    constexpr int ES = OUT == kOutF32 ? 4 : (OUT == kOutBF16 ? 2 : 1);
+    constexpr int RB = 32 * ES;      // bytes of one chunk row
+    constexpr int P = RB / 16;       // 16-byte pieces per row
+    constexpr int LPG = 8 / P;       // lanes sharing one swizzle phase (8 lanes per shared-memory wavefront)
+    const int lane = static_cast<int>(threadIdx.x & 31);
+    uint32_t w[8 * ES];
+    if (OUT == kOutF32) {
+#pragma unroll
+        for (int j = 0; j < 32; ++j) w[j] = __float_as_uint(v[j]);
+    } else if (OUT == kOutBF16) {
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+            __nv_bfloat162 h = __floats2bfloat162_rn(v[2 * j], v[2 * j + 1]);
+            w[j] = *reinterpret_cast<uint32_t *>(&h);
+        }
+    } else {
+#pragma unroll
+        for (int j = 0; j < 8; ++j)
+            w[j] = quantize1(v[4 * j], ys) | (quantize1(v[4 * j + 1], ys) << 8) | (quantize1(v[4 * j + 2], ys) << 16) |
+                   (quantize1(v[4 * j + 3], ys) << 24);
+    }
+    const int fw = (lane / LPG) % P;
+#pragma unroll
+    for (int p = 0; p < P; ++p)
+        *reinterpret_cast<uint4 *>(stage + lane * RB + ((p ^ fw) * 16)) =
+            make_uint4(w[4 * p], w[4 * p + 1], w[4 * p + 2], w[4 * p + 3]);
+    __syncwarp();
+    const int q = lane % P;
+#pragma unroll
+    for (int k = 0; k < P; ++k) {
+        const int r = lane / P + k * (32 / P);
+        const uint4 d = *reinterpret_cast<const uint4 *>(stage + r * RB + ((q ^ ((r / LPG) % P)) * 16));
+        const int64_t row = row0 + r;
+        if (row < ep.M) {
+            const int64_t off = (row * ep.ldy + ep.y_col_offset + col0) * ES + q * 16;
+            *reinterpret_cast<uint4 *>(static_cast<uint8_t *>(ep.y) + off) = d;
+            for (int pr = 0; pr < ep.y_num_peers; ++pr)
+                *reinterpret_cast<uint4 *>(static_cast<uint8_t *>(ep.y_peers[pr]) + off) = d;
+        }
+    }
+    __syncwarp();
 }
 
 // Epilogue of 32 output columns [col0, col0+32) of one row. g holds the
@@ -214,7 +283,7 @@ template <int EPI, int OUT>
 __device__ __forceinline__ void epi_row32(const EpiParams &ep, int64_t row, bool row_ok, int64_t col0, int64_t ng0,
                                           int64_t nu0, int64_t n_out, const uint32_t (&g)[32],
                                           const uint32_t (&u)[32], float row_scale, float row_add, float ys,
-                                          float &amax) {
+                                          float &amax, uint8_t *stage) {
     ColFactors fg;
     load_col_factors(ep, ng0, fg);
     float v[32];
@@ -228,6 +297,18 @@ __device__ __forceinline__ void epi_row32(const EpiParams &ep, int64_t row, bool
             const float up = fmaf(__uint_as_float(u[j]) * row_scale, fu.scale[j], fu.add[j] + row_add);
             v[j] = silu_mul(v[j], up);
         }
+    }
+    // staged (peer) path: warp-uniform condition, every lane takes part
+    constexpr int ES = OUT == kOutF32 ? 4 : (OUT == kOutBF16 ? 2 : 1);
+    const bool staged = stage != nullptr && col0 + 32 <= n_out && ((ep.ldy * ES) % 16 == 0) &&
+                        (((ep.y_col_offset + col0) * ES) % 16 == 0) && !ep.c_mat && !ep.row_amax;
+    if (staged) {
+        if (EPI == LCML_EPI_RELU) {
+#pragma unroll
+            for (int j = 0; j < 32; ++j) v[j] = fmaxf(v[j], 0.0f);
+        }
+        store_chunk_staged<OUT>(ep, stage, row - static_cast<int64_t>(threadIdx.x & 31), col0, v, ys);
+        return;
     }
     if (!row_ok) return;
     if (ep.c_mat) {
@@ -255,7 +336,8 @@ __device__ __forceinline__ void atomic_max_abs(float *p, float v) {
 // One output tile's epilogue for the calling thread: TMEM lane `row` of the
 // accumulator at `taddr` (BN fp32 columns), gemm column block `tn`.
 template <int BN, int EPI, int OUT>
-__device__ __forceinline__ void epilogue_tile(const EpiParams &ep, uint32_t taddr, int64_t row, int tn, float ys) {
+__device__ __forceinline__ void epilogue_tile(const EpiParams &ep, uint32_t taddr, int64_t row, int tn, float ys,
+                                              uint8_t *stage) {
     const int64_t n_out = (EPI == LCML_EPI_SILU_MUL) ? ep.N / 2 : ep.N;
     const bool row_ok = row < ep.M;
     const float row_scale = ep.alpha * (ep.sa_row ? (row_ok ? __ldg(ep.sa + row) : 0.0f) : __ldg(ep.sa));
@@ -273,7 +355,7 @@ __device__ __forceinline__ void epilogue_tile(const EpiParams &ep, uint32_t tadd
             tmem_wait_ld();
             const int64_t ng0 = static_cast<int64_t>(tn) * BN + c * 32;
             const int64_t col0 = static_cast<int64_t>(tn) * (BN / 2) + c * 32;
-            epi_row32<EPI, OUT>(ep, row, row_ok, col0, ng0, ng0 + BN / 2, n_out, g, u, row_scale, row_add, ys, amax);
+            epi_row32<EPI, OUT>(ep, row, row_ok, col0, ng0, ng0 + BN / 2, n_out, g, u, row_scale, row_add, ys, amax, stage);
         }
     } else {
 #pragma unroll 1
@@ -282,10 +364,11 @@ __device__ __forceinline__ void epilogue_tile(const EpiParams &ep, uint32_t tadd
             tmem_ld_32x32b_x32(taddr + c * 32, g);
             tmem_wait_ld();
             const int64_t col0 = static_cast<int64_t>(tn) * BN + c * 32;
-            epi_row32<EPI, OUT>(ep, row, row_ok, col0, col0, 0, n_out, g, g, row_scale, row_add, ys, amax);
+            epi_row32<EPI, OUT>(ep, row, row_ok, col0, col0, 0, n_out, g, g, row_scale, row_add, ys, amax, stage);
         }
     }
     if (ep.row_amax && row_ok) atomic_max_abs(ep.row_amax + row, amax);
+    if (ep.y_num_peers > 0) __threadfence_system();  // peer stores ordered before the kernel's completion
 }
 
 // Tile index -> (m tile, n tile), banded so that CTAs running at the same time
@@ -307,7 +390,8 @@ struct Layout {
     static constexpr int kStageBytes = kABytes + kBBytes;
     static constexpr int kTmemCols = 2 * BN;  // double-buffered fp32 accumulator
     static constexpr int kBarOffset = STAGES * kStageBytes;
-    static constexpr int kSmemBytes = kBarOffset + (2 * STAGES + 4) * 8 + 16 + 1024;  // +1024 for manual alignment
+    static constexpr int kEpiOffset = kBarOffset + 1024;     // 4 warps x 32 x 32 fp32 staging (peer stores)
+    static constexpr int kSmemBytes = kEpiOffset + 4 * 4096 + 1024;  // +1024 for manual alignment
 };
 
 template <int BN, int STAGES, int EPI, int OUT>
@@ -435,6 +519,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         // ---------------- epilogue warps ----------------
         const int quarter = warp & 3;  // TMEM lanes [32*quarter, 32*quarter+32)
         const float ys = (OUT == kOutE4M3) ? __ldg(ep.y_scale) : 1.0f;
+        uint8_t *stage = ep.y_num_peers > 0 ? smem + L::kEpiOffset + quarter * 4096 : nullptr;
         int acc = 0;
         uint32_t acc_phase = 0;
         for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
@@ -444,7 +529,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             tc_fence_after();
             const int64_t row = static_cast<int64_t>(tm) * BM + quarter * 32 + lane;
             const uint32_t taddr = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + static_cast<uint32_t>(acc * BN);
-            epilogue_tile<BN, EPI, OUT>(ep, taddr, row, tn, ys);
+            epilogue_tile<BN, EPI, OUT>(ep, taddr, row, tn, ys, stage);
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(&tempty[acc]);
@@ -480,7 +565,8 @@ struct PairLayout {
     static constexpr int kStageBytes = 2 * kHalfBytes;    // per CTA
     static constexpr int kTmemCols = 512;                 // 2 x 256 fp32 accumulators
     static constexpr int kBarOffset = STAGES * kStageBytes;
-    static constexpr int kSmemBytes = kBarOffset + (2 * STAGES + 4) * 8 + 16 + 1024;
+    static constexpr int kEpiOffset = kBarOffset + 1024;     // 4 warps x 32 x 32 fp32 staging (peer stores)
+    static constexpr int kSmemBytes = kEpiOffset + 4 * 4096 + 1024;
 };
 
 template <int STAGES, int EPI, int OUT>
@@ -615,6 +701,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         // ---------------- epilogue warps (both CTAs) ----------------
         const int quarter = warp & 3;
         const float ys = (OUT == kOutE4M3) ? __ldg(ep.y_scale) : 1.0f;
+        uint8_t *stage = ep.y_num_peers > 0 ? smem + L::kEpiOffset + quarter * 4096 : nullptr;
         const uint32_t tempty_leader = mapa_shared(smem_u32(&tempty[0]), 0);
         int acc = 0;
         uint32_t acc_phase = 0;
@@ -625,7 +712,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
             tc_fence_after();
             const int64_t row = static_cast<int64_t>(tm) * 256 + rank * 128 + quarter * 32 + lane;
             const uint32_t taddr = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + static_cast<uint32_t>(acc * BN);
-            epilogue_tile<BN, EPI, OUT>(ep, taddr, row, tn, ys);
+            epilogue_tile<BN, EPI, OUT>(ep, taddr, row, tn, ys, stage);
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive_cluster(tempty_leader + 8u * static_cast<uint32_t>(acc));
@@ -721,7 +808,8 @@ __global__ void __launch_bounds__(256) k_gemm_fp8_simt(const uint8_t *__restrict
             if (ep.c_mat) a += ep.beta * load_cmat(ep, row, col);
             if (EPI == LCML_EPI_RELU) a = fmaxf(a, 0.0f);
             amax = fmaxf(amax, fabsf(a));
-            store_out<OUT>(ep, row, col, a, ys);
+            store_out<OUT>(ep.y, ep.ldy, row, col + ep.y_col_offset, a, ys);
+            for (int p = 0; p < ep.y_num_peers; ++p) store_out<OUT>(ep.y_peers[p], ep.ldy, row, col + ep.y_col_offset, a, ys);
         }
         if (ep.row_amax) atomic_max_abs(ep.row_amax + row, amax);
     }
@@ -861,7 +949,8 @@ int gemm_entry(const lcml_fp8_gemm_desc *d, lcml_stream_t stream, bool force_sim
     LCML_CHECK_ARG(d->lda >= d->K, "lcml_fp8_gemm: lda < K");
     LCML_CHECK_ARG(d->b_kmajor ? d->ldb >= d->K : d->ldb >= d->N, "lcml_fp8_gemm: ldb too small");
     const int64_t n_out = d->epilogue == LCML_EPI_SILU_MUL ? d->N / 2 : d->N;
-    LCML_CHECK_ARG(d->ldy >= n_out, "lcml_fp8_gemm: ldy < output columns");
+    LCML_CHECK_ARG(d->y_col_offset >= 0 && d->ldy >= n_out + d->y_col_offset, "lcml_fp8_gemm: ldy < y_col_offset + output columns");
+    LCML_CHECK_ARG(d->y_num_peers >= 0 && (d->y_num_peers == 0 || d->y_peers), "lcml_fp8_gemm: y_peers missing");
     LCML_CHECK_ARG(d->scale_a_mode == LCML_SCALE_TENSOR || d->scale_a_mode == LCML_SCALE_ROW,
                    "lcml_fp8_gemm: scale_a_mode must be TENSOR or ROW");
     LCML_CHECK_ARG(d->scale_b_mode == LCML_SCALE_TENSOR || d->scale_b_mode == LCML_SCALE_COL,
@@ -889,6 +978,9 @@ int gemm_entry(const lcml_fp8_gemm_desc *d, lcml_stream_t stream, bool force_sim
     ep.ldy = d->ldy;
     ep.y_scale = d->y_scale;
     ep.row_amax = d->row_amax;
+    ep.y_col_offset = d->y_col_offset;
+    ep.y_peers = d->y_peers;
+    ep.y_num_peers = d->y_num_peers;
     cudaStream_t st = to_cuda(stream);
     switch (d->epilogue) {
         case LCML_EPI_NONE: return dispatch_out<LCML_EPI_NONE>(d, ep, st, force_simt);

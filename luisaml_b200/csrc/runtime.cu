@@ -140,3 +140,40 @@ int lcml_stream_synchronize(lcml_stream_t stream) {
 }
 
 }// extern "C"
+
+extern "C" {
+
+int lcml_ipc_get_handle(void *device_ptr, void *handle_out) {
+    LCML_CHECK_ARG(device_ptr && handle_out, "lcml_ipc_get_handle: null pointer");
+    static_assert(sizeof(cudaIpcMemHandle_t) == LCML_IPC_HANDLE_BYTES, "IPC handle size");
+    cudaIpcMemHandle_t h;
+    LCML_CUDA(cudaIpcGetMemHandle(&h, device_ptr));
+    std::memcpy(handle_out, &h, sizeof(h));
+    return LCML_OK;
+}
+
+int lcml_ipc_open(const void *handle, void **device_ptr) {
+    LCML_CHECK_ARG(handle && device_ptr, "lcml_ipc_open: null pointer");
+    cudaIpcMemHandle_t h;
+    std::memcpy(&h, handle, sizeof(h));
+    LCML_CUDA(cudaIpcOpenMemHandle(device_ptr, h, cudaIpcMemLazyEnablePeerAccess));
+    return LCML_OK;
+}
+
+int lcml_ipc_close(void *device_ptr) {
+    if (device_ptr) LCML_CUDA(cudaIpcCloseMemHandle(device_ptr));
+    return LCML_OK;
+}
+
+int lcml_enable_peer_access(int peer_device) {
+    const cudaError_t e = cudaDeviceEnablePeerAccess(peer_device, 0);
+    if (e == cudaErrorPeerAccessAlreadyEnabled) {
+        cudaGetLastError();
+        return LCML_OK;
+    }
+    if (e != cudaSuccess) return lcml::set_error(LCML_ERR_CUDA, "cudaDeviceEnablePeerAccess(%d): %s", peer_device,
+                                                 cudaGetErrorString(e));
+    return LCML_OK;
+}
+
+}// extern "C"

@@ -58,8 +58,13 @@ def assert_close(got, ref, rtol=RTOL, atol=ATOL, what="", extra=0.0):
     got = np.asarray(got, dtype=np.float64)
     ref = np.asarray(ref, dtype=np.float64)
     assert got.shape == ref.shape, (got.shape, ref.shape)
-    err = np.abs(got - ref)
-    bound = atol + rtol * np.abs(ref) + extra
+    nan_got, nan_ref = np.isnan(got), np.isnan(ref)
+    if (nan_got != nan_ref).any():
+        i = np.unravel_index(np.argmax(nan_got != nan_ref), got.shape)
+        raise AssertionError(f"{what}: NaN mismatch ({int((nan_got != nan_ref).sum())} elements); first at {i}: "
+                             f"got {got[i]} ref {ref[i]}")
+    err = np.where(nan_ref, 0.0, np.abs(got - ref))
+    bound = atol + rtol * np.abs(np.where(nan_ref, 0.0, ref)) + extra
     bad = err > bound
     if bad.any():
         i = np.unravel_index(np.argmax(err - bound), err.shape)

@@ -279,3 +279,39 @@ def test_gemm_rowquant(dev, epilogue):
     qr, sr = oracle.quantize_dynamic_rows(y)
     assert np.array_equal(s.cpu().numpy(), sr)
     assert np.array_equal(q.cpu().numpy(), qr)
+
+
+@pytest.mark.parametrize("out", ["bf16", "f32", "e4m3"])
+@pytest.mark.parametrize("mode", [1, 2])
+def test_gemm_column_shard_and_peer_copies(dev, gemm_mode, out, mode):
+    """The epilogue's column-offset + extra-destination stores (the fused
+    all-gather path, staged through shared memory) on one GPU: a second
+    buffer on the same device stands in for a peer's output."""
+    import ctypes
+    import torch
+    import luisaml_b200 as lb
+    gemm_mode(mode)
+    M, N, K, Ntot, off = 300, 512, 256, 1024, 256
+    Aq, sa, Bq, sb = make_operands(M, N, K, seed=61, per_row=True, per_col=True, b_std=0.05)
+    ref = oracle.qdq_gemm(Aq, sa, Bq, sb)
+    dt = {"bf16": torch.bfloat16, "f32": torch.float32, "e4m3": torch.uint8}[out]
+    Y = torch.zeros((M, Ntot), dtype=dt, device=dev)
+    Y2 = torch.zeros((M, Ntot), dtype=dt, device=dev)
+    ys = _t(np.float32([oracle.scale_from_amax(np.abs(ref).max())]), dev)
+    d, _ = lb.gemm(_t(Aq, dev), _t(Bq, dev), _t(sa, dev), _t(sb, dev), out_dtype=dt, desc_only=True,
+                   y_scale=ys if out == "e4m3" else None)
+    peers = torch.tensor([Y2.data_ptr()], dtype=torch.int64, device=dev)
+    d.Y, d.ldy, d.y_col_offset, d.y_peers, d.y_num_peers = Y.data_ptr(), Ntot, off, peers.data_ptr(), 1
+    lb.check(lb.lib().lcml_fp8_gemm(ctypes.byref(d), ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)))
+    torch.cuda.synchronize()
+    assert torch.equal(Y, Y2)
+    assert torch.count_nonzero(Y[:, :off].float()) == 0 and torch.count_nonzero(Y[:, off + N:].float()) == 0
+    got = Y[:, off:off + N]
+    if out == "e4m3":
+        g = oracle.e4m3_decode(got.cpu().numpy())
+        w = oracle.e4m3_decode(oracle.quantize(ref, ys.cpu().numpy()[0]))
+        assert (np.abs(g - w) <= np.maximum(np.abs(w) * 0.125, 2.0 ** -9) + 1e-12).all()
+    elif out == "bf16":
+        assert_close_bf16(got.float().cpu().numpy(), ref, what="bf16 shard")
+    else:
+        assert_close(got.cpu().numpy(), ref, what="f32 shard")
