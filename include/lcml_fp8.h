@@ -166,7 +166,7 @@ typedef struct lcml_fp8_gemm_desc {
     const float *c_vec;   /* optional fp32 C broadcast: [N] (COL), [M] (ROW) or [1] (TENSOR) */
     int c_vec_mode;
     const void *c_mat;    /* optional full C [M, N] (e.g. the FFN residual), row stride ldc elements */
-    int c_mat_dtype;      /* LCML_DTYPE_FLOAT or LCML_DTYPE_BFLOAT16 */
+    int c_mat_dtype;      /* LCML_DTYPE_FLOAT, LCML_DTYPE_BFLOAT16 or LCML_DTYPE_FLOAT8E4M3FN (see c_mat_scale) */
     int64_t ldc;
     int epilogue;         /* lcml_epilogue */
     void *Y;              /* [M, N] (N/2 for SILU_MUL), row stride ldy elements */
@@ -183,6 +183,7 @@ typedef struct lcml_fp8_gemm_desc {
     int64_t y_col_offset;
     void *const *y_peers; /* device array of y_num_peers device pointers */
     int y_num_peers;
+    const float *c_mat_scale; /* device [1]: DequantizeLinear scale of an e4m3 c_mat (a quantized residual) */
 } lcml_fp8_gemm_desc;
 
 int lcml_fp8_gemm(const lcml_fp8_gemm_desc *desc, lcml_stream_t stream);
@@ -234,40 +235,48 @@ int lcml_gemm_f32(const float *A, const float *B, const float *C, int64_t M, int
                   lcml_stream_t stream);
 
 /*
- * FP8 2-D convolution, NCHW, lowered to implicit GEMM on the tensor cores.
- * Stands in for Conv::forward (src/onnx/operators/conv.cpp:35-255) fed by
- * DequantizeLinear on X and W. X is e4m3 [N, C, H, W] with a per-tensor
- * scale; W is prepacked by lcml_fp8_conv_pack_weight; epilogue as for GEMM
- * (bias per output channel, Relu, optional residual [N, M, oH, oW], output
- * fp32/bf16/e4m3). Pads are begin/end per ONNX; the reference uses begin pads
- * only (conv.cpp:119-121), which equals ONNX when the output shape matches.
+ * FP8 2-D convolution on the tensor cores (the DequantizeLinear -> Conv ->
+ * (Add residual) -> (Relu) -> (QuantizeLinear) node group of a QDQ graph).
+ * Stands in for Conv::forward (src/onnx/operators/conv.cpp:35-255), which
+ * accumulates FP8 inputs in half precision; here products are exact and
+ * accumulate in fp32. Lowering: output pixels are GEMM rows, output channels
+ * GEMM columns, K = (kh, kw, c). A 1x1 / stride-1 / unpadded conv on an NHWC
+ * input reads X as the GEMM's A directly; every other conv first gathers its
+ * patches (im2col, e4m3, zero padding) into `workspace`.
+ * X: e4m3, NHWC (x_nhwc = 1) or NCHW (x_nhwc = 0), per-tensor scale.
+ * Wp: weights packed by lcml_fp8_conv_pack_weight, per-tensor or per-output-
+ * channel scales. Y: NHWC [N, oH, oW, M] (the GEMM's row-major output),
+ * fp32 / bf16 / e4m3 (with y_scale). residual: same layout as Y, fp32 or e4m3
+ * (with residual_scale), added before the activation. Pads are the begin
+ * pads (conv.cpp:119-121); group must be 1.
  */
 typedef struct lcml_fp8_conv_desc {
     int64_t N, C, H, W;     /* input */
     int64_t M, kH, kW;      /* output channels, kernel */
     int64_t oH, oW;         /* output spatial */
     int sH, sW, pH, pW, dH, dW, group;
-    const uint8_t *X;       /* e4m3 activations, layout per x_nhwc */
-    int x_nhwc;             /* 0: NCHW (ONNX), 1: NHWC (internal fast layout) */
+    const uint8_t *X;
+    int x_nhwc;
     const float *scale_x;   /* device [1] */
-    const uint8_t *Wp;      /* packed weights from lcml_fp8_conv_pack_weight */
+    const uint8_t *Wp;      /* packed weights [M, Kp] */
     const float *scale_w;   /* device [1] or [M] */
     int scale_w_mode;       /* LCML_SCALE_TENSOR or LCML_SCALE_AXIS (per output channel) */
     const float *bias;      /* optional fp32 [M] */
-    const void *residual;   /* optional, same layout/dtype as Y */
+    const void *residual;   /* optional, NHWC like Y */
+    int residual_dtype;     /* LCML_DTYPE_FLOAT or LCML_DTYPE_FLOAT8E4M3FN */
+    const float *residual_scale;
     int epilogue;           /* LCML_EPI_NONE or LCML_EPI_RELU */
     void *Y;
     int y_dtype;            /* FLOAT, BFLOAT16 or FLOAT8E4M3FN */
-    int y_nhwc;             /* 0: NCHW, 1: NHWC */
     const float *y_scale;   /* per-tensor output scale when y_dtype is e4m3 */
-    void *workspace;        /* caller scratch, lcml_fp8_conv_workspace_size() bytes */
+    void *workspace;        /* lcml_fp8_conv_workspace_size() bytes, 16-byte aligned */
 } lcml_fp8_conv_desc;
 
-/* Bytes of scratch lcml_fp8_conv needs for `desc` (0 when none). */
+/* Packed K: kH * kW * C rounded up to a multiple of 16. */
+int64_t lcml_fp8_conv_packed_k(int64_t Cg, int64_t kH, int64_t kW);
+/* Bytes of scratch lcml_fp8_conv needs for `desc` (0 for the direct 1x1 path, -1 on a bad desc). */
 int64_t lcml_fp8_conv_workspace_size(const lcml_fp8_conv_desc *desc);
-/* Bytes of the packed weight buffer for W [M, C/group, kH, kW]. */
-int64_t lcml_fp8_conv_packed_weight_size(int64_t M, int64_t Cg, int64_t kH, int64_t kW);
-/* Packs e4m3 W [M, C/group, kH, kW] (ONNX layout) into the GEMM B layout. */
+/* Packs e4m3 W [M, Cg, kH, kW] (ONNX layout) into Wp [M, Kp], K order (kh, kw, c), zero padded. */
 int lcml_fp8_conv_pack_weight(const uint8_t *W, int64_t M, int64_t Cg, int64_t kH, int64_t kW, uint8_t *Wp,
                               lcml_stream_t stream);
 int lcml_fp8_conv(const lcml_fp8_conv_desc *desc, lcml_stream_t stream);

@@ -54,6 +54,7 @@ class GemmDesc(ctypes.Structure):
         ("y_col_offset", ctypes.c_int64),
         ("y_peers", ctypes.c_void_p),
         ("y_num_peers", ctypes.c_int),
+        ("c_mat_scale", ctypes.c_void_p),
     ]
 
 
@@ -66,9 +67,10 @@ class ConvDesc(ctypes.Structure):
         ("dH", ctypes.c_int), ("dW", ctypes.c_int), ("group", ctypes.c_int),
         ("X", ctypes.c_void_p), ("x_nhwc", ctypes.c_int), ("scale_x", ctypes.c_void_p),
         ("Wp", ctypes.c_void_p), ("scale_w", ctypes.c_void_p), ("scale_w_mode", ctypes.c_int),
-        ("bias", ctypes.c_void_p), ("residual", ctypes.c_void_p), ("epilogue", ctypes.c_int),
-        ("Y", ctypes.c_void_p), ("y_dtype", ctypes.c_int), ("y_nhwc", ctypes.c_int),
-        ("y_scale", ctypes.c_void_p), ("workspace", ctypes.c_void_p),
+        ("bias", ctypes.c_void_p), ("residual", ctypes.c_void_p), ("residual_dtype", ctypes.c_int),
+        ("residual_scale", ctypes.c_void_p), ("epilogue", ctypes.c_int),
+        ("Y", ctypes.c_void_p), ("y_dtype", ctypes.c_int), ("y_scale", ctypes.c_void_p),
+        ("workspace", ctypes.c_void_p),
     ]
 
 
@@ -104,7 +106,7 @@ PROTOTYPES = {
     "lcml_fp8_gemm_rowquant": [ctypes.POINTER(GemmDesc), _vp, _vp, _vp, _vp],
     "lcml_fp8_gemm_rowquant_noalloc": [ctypes.POINTER(GemmDesc), _vp, _vp, _vp],
     "lcml_fp8_conv_workspace_size": [ctypes.POINTER(ConvDesc)],
-    "lcml_fp8_conv_packed_weight_size": [_c_i64, _c_i64, _c_i64, _c_i64],
+    "lcml_fp8_conv_packed_k": [_c_i64, _c_i64, _c_i64],
     "lcml_fp8_conv_pack_weight": [_vp, _c_i64, _c_i64, _c_i64, _c_i64, _vp, _vp],
     "lcml_fp8_conv": [ctypes.POINTER(ConvDesc), _vp],
     "lcml_unary_f32": [_ci, _vp, _vp, _c_i64, _vp],
@@ -120,7 +122,7 @@ _RESTYPES = {
     "lcml_last_error": ctypes.c_char_p,
     "lcml_launch_count": ctypes.c_uint64,
     "lcml_fp8_conv_workspace_size": ctypes.c_int64,
-    "lcml_fp8_conv_packed_weight_size": ctypes.c_int64,
+    "lcml_fp8_conv_packed_k": ctypes.c_int64,
 }
 
 _lib = None

@@ -45,7 +45,8 @@ struct EpiParams {
     const float *c_vec;
     int c_vec_mode;        // 0 none, 1 tensor, 2 row, 3 col
     const void *c_mat;
-    int c_mat_bf16;
+    int c_mat_kind;  // 0 fp32, 1 bf16, 2 e4m3 (times c_mat_scale)
+    const float *c_mat_scale;
     int64_t ldc;
     void *y;
     int64_t ldy;
@@ -63,7 +64,9 @@ __device__ __forceinline__ float silu_mul(float g, float u) {
 }
 
 __device__ __forceinline__ float load_cmat(const EpiParams &ep, int64_t row, int64_t col) {
-    if (ep.c_mat_bf16) return __bfloat162float(reinterpret_cast<const __nv_bfloat16 *>(ep.c_mat)[row * ep.ldc + col]);
+    if (ep.c_mat_kind == 1) return __bfloat162float(reinterpret_cast<const __nv_bfloat16 *>(ep.c_mat)[row * ep.ldc + col]);
+    if (ep.c_mat_kind == 2)
+        return e4m3_decode(reinterpret_cast<const uint8_t *>(ep.c_mat)[row * ep.ldc + col]) * __ldg(ep.c_mat_scale);
     return reinterpret_cast<const float *>(ep.c_mat)[row * ep.ldc + col];
 }
 
@@ -126,7 +129,22 @@ __device__ __forceinline__ void load_col_factors(const EpiParams &ep, int64_t n0
 // beta * C[row, col0 .. col0+32) of the full C matrix (residual), into r[].
 __device__ __forceinline__ void load_cmat32(const EpiParams &ep, int64_t row, int64_t col0, int64_t n_out, float (&r)[32]) {
     const bool full = col0 + 32 <= n_out;
-    if (ep.c_mat_bf16) {
+    if (ep.c_mat_kind == 2) {
+        const uint8_t *cp = reinterpret_cast<const uint8_t *>(ep.c_mat) + row * ep.ldc + col0;
+        const float cs = __ldg(ep.c_mat_scale);
+        if (full && aligned(cp, 16)) {
+#pragma unroll
+            for (int j = 0; j < 2; ++j) {
+                const uint4 w = *reinterpret_cast<const uint4 *>(cp + 16 * j);
+                const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+                for (int k = 0; k < 16; ++k) r[16 * j + k] = e4m3_decode((ws[k >> 2] >> ((k & 3) * 8)) & 0xffu) * cs;
+            }
+        } else {
+#pragma unroll
+            for (int j = 0; j < 32; ++j) r[j] = (col0 + j < n_out) ? e4m3_decode(cp[j]) * cs : 0.0f;
+        }
+    } else if (ep.c_mat_kind == 1) {
         const __nv_bfloat16 *cp = reinterpret_cast<const __nv_bfloat16 *>(ep.c_mat) + row * ep.ldc + col0;
         if (full && aligned(cp, 16)) {
 #pragma unroll
@@ -923,6 +941,7 @@ int dispatch(const lcml_fp8_gemm_desc *d, const EpiParams &ep, cudaStream_t st, 
     if (g_gemm_mode != 1 && (g_gemm_mode == 2 || (d->M >= 256 && pair_tiles >= sm_count() / 2)))
         return launch_tc2<EPI, OUT>(d, ep, st);
     if (EPI == LCML_EPI_SILU_MUL || d->N >= 2048) return launch_tc<256, 4, EPI, OUT>(d, ep, st);
+    if (EPI != LCML_EPI_SILU_MUL && d->N <= 64) return launch_tc<64, 8, EPI, OUT>(d, ep, st);
     return launch_tc<128, 6, EPI, OUT>(d, ep, st);
 }
 
@@ -956,8 +975,9 @@ int gemm_entry(const lcml_fp8_gemm_desc *d, lcml_stream_t stream, bool force_sim
     LCML_CHECK_ARG(d->scale_b_mode == LCML_SCALE_TENSOR || d->scale_b_mode == LCML_SCALE_COL,
                    "lcml_fp8_gemm: scale_b_mode must be TENSOR or COL");
     LCML_CHECK_ARG(d->y_dtype != LCML_DTYPE_FLOAT8E4M3FN || d->y_scale, "lcml_fp8_gemm: e4m3 output needs y_scale");
-    LCML_CHECK_ARG(!d->c_mat || d->c_mat_dtype == LCML_DTYPE_FLOAT || d->c_mat_dtype == LCML_DTYPE_BFLOAT16,
-                   "lcml_fp8_gemm: c_mat dtype must be FLOAT or BFLOAT16");
+    LCML_CHECK_ARG(!d->c_mat || d->c_mat_dtype == LCML_DTYPE_FLOAT || d->c_mat_dtype == LCML_DTYPE_BFLOAT16 ||
+                       (d->c_mat_dtype == LCML_DTYPE_FLOAT8E4M3FN && d->c_mat_scale),
+                   "lcml_fp8_gemm: c_mat dtype must be FLOAT, BFLOAT16 or FLOAT8E4M3FN with c_mat_scale");
     LCML_CHECK_ARG(!d->c_vec || (d->c_vec_mode >= 0 && d->c_vec_mode <= 2), "lcml_fp8_gemm: bad c_vec_mode");
     EpiParams ep;
     ep.M = d->M;
@@ -972,7 +992,8 @@ int gemm_entry(const lcml_fp8_gemm_desc *d, lcml_stream_t stream, bool force_sim
     // external modes TENSOR(0)/ROW(1)/COL(2) -> internal 1/2/3, 0 = none
     ep.c_vec_mode = d->c_vec ? (d->c_vec_mode == LCML_SCALE_TENSOR ? 1 : (d->c_vec_mode == LCML_SCALE_ROW ? 2 : 3)) : 0;
     ep.c_mat = d->c_mat;
-    ep.c_mat_bf16 = d->c_mat_dtype == LCML_DTYPE_BFLOAT16;
+    ep.c_mat_kind = d->c_mat_dtype == LCML_DTYPE_BFLOAT16 ? 1 : (d->c_mat_dtype == LCML_DTYPE_FLOAT8E4M3FN ? 2 : 0);
+    ep.c_mat_scale = d->c_mat_scale;
     ep.ldc = d->ldc;
     ep.y = d->Y;
     ep.ldy = d->ldy;

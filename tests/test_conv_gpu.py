@@ -1,0 +1,125 @@
+"""FP8 convolution (lcml_fp8_conv) vs the oracle's direct conv loop
+(conv.cpp:137-207 restated in oracle/oracle.c) on dequantized operands.
+
+X is e4m3 with a per-tensor scale (NCHW for the stem, NHWC otherwise),
+W is e4m3 with per-output-channel scales; outputs are NHWC.
+"""
+import ctypes
+
+import numpy as np
+import pytest
+
+import oracle
+from conftest import assert_close
+
+pytestmark = pytest.mark.gpu
+
+
+def _t(a, dev):
+    import torch
+    return torch.from_numpy(np.array(a, copy=True)).to(dev)
+
+
+def _run_conv(dev, X, W, bias, stride, pad, nhwc_in=True, relu=False, residual=None, out="f32", y_scale=None):
+    """Quantizes X (per tensor) and W (per channel) with the oracle, runs the
+    GPU conv; returns (gpu NCHW fp32 result, oracle result on the dequantized
+    operands, dequantization helpers)."""
+    import torch
+    import luisaml_b200 as lb
+    N, C, H, Wd = X.shape
+    M, _, kH, kW = W.shape
+    sx = np.float32(oracle.scale_from_amax(oracle.amax(X)))
+    xq = oracle.quantize(X, sx)
+    sw = np.array([oracle.scale_from_amax(oracle.amax(W[m])) for m in range(M)], dtype=np.float32)
+    wq = oracle.quantize(W, sw, axis=0)
+    oH = (H + 2 * pad - kH) // stride + 1
+    oW = (Wd + 2 * pad - kW) // stride + 1
+    ref = oracle.conv2d(oracle.dequantize(xq, sx), oracle.dequantize(wq, sw, axis=0), bias, strides=(stride, stride),
+                        pads=(pad, pad, pad, pad))
+    Kp = lb.lib().lcml_fp8_conv_packed_k(C, kH, kW)
+    Wp = torch.empty((M, Kp), dtype=torch.uint8, device=dev)
+    stream = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+    wq_t = _t(wq, dev)
+    lb.check(lb.lib().lcml_fp8_conv_pack_weight(ctypes.c_void_p(wq_t.data_ptr()), M, C, kH, kW,
+                                                ctypes.c_void_p(Wp.data_ptr()), stream))
+    xin = np.ascontiguousarray(xq.transpose(0, 2, 3, 1)) if nhwc_in else xq
+    xt, sxt, swt = _t(xin, dev), _t(np.float32([sx]), dev), _t(sw, dev)
+    dt = {"f32": torch.float32, "bf16": torch.bfloat16, "e4m3": torch.uint8}[out]
+    Y = torch.empty((N, oH, oW, M), dtype=dt, device=dev)
+    d = lb._capi.ConvDesc()
+    d.N, d.C, d.H, d.W, d.M, d.kH, d.kW, d.oH, d.oW = N, C, H, Wd, M, kH, kW, oH, oW
+    d.sH = d.sW = stride
+    d.pH = d.pW = pad
+    d.dH = d.dW = 1
+    d.group = 1
+    d.X, d.x_nhwc, d.scale_x = xt.data_ptr(), int(nhwc_in), sxt.data_ptr()
+    d.Wp, d.scale_w, d.scale_w_mode = Wp.data_ptr(), swt.data_ptr(), lb.SCALE_AXIS
+    keep = [xt, sxt, swt, Wp]
+    if bias is not None:
+        bt = _t(bias, dev)
+        keep.append(bt)
+        d.bias = bt.data_ptr()
+    res_ref = 0.0
+    if residual is not None:
+        rs = np.float32(oracle.scale_from_amax(oracle.amax(residual)))
+        rq = oracle.quantize(residual, rs)  # NCHW
+        res_ref = oracle.dequantize(rq, rs)
+        rt, rst = _t(np.ascontiguousarray(rq.transpose(0, 2, 3, 1)), dev), _t(np.float32([rs]), dev)
+        keep += [rt, rst]
+        d.residual, d.residual_dtype, d.residual_scale = rt.data_ptr(), lb.DTYPE_E4M3, rst.data_ptr()
+    d.epilogue = lb.EPI_RELU if relu else lb.EPI_NONE
+    d.Y, d.y_dtype = Y.data_ptr(), {"f32": 1, "bf16": 16, "e4m3": 17}[out]
+    if out == "e4m3":
+        yst = _t(np.float32([y_scale]), dev)
+        keep.append(yst)
+        d.y_scale = yst.data_ptr()
+    ws_bytes = lb.lib().lcml_fp8_conv_workspace_size(ctypes.byref(d))
+    ws = torch.empty(max(ws_bytes, 16), dtype=torch.uint8, device=dev)
+    d.workspace = ws.data_ptr()
+    lb.check(lb.lib().lcml_fp8_conv(ctypes.byref(d), stream))
+    torch.cuda.synchronize()
+    ref = ref + res_ref
+    if relu:
+        ref = np.maximum(ref, 0.0)
+    y = Y.cpu()
+    if out == "e4m3":
+        got = oracle.e4m3_decode(y.numpy()).astype(np.float32)
+    else:
+        got = y.float().numpy()
+    return got.transpose(0, 3, 1, 2), ref, ws_bytes
+
+
+CASES = [
+    # name, N, C, H, M, k, stride, pad, nhwc
+    ("stem7x7s2_nchw", 2, 3, 64, 64, 7, 2, 3, False),
+    ("1x1_direct", 2, 64, 56, 256, 1, 1, 0, True),
+    ("3x3_pad1", 2, 64, 56, 64, 3, 1, 1, True),
+    ("3x3_s2", 2, 128, 56, 128, 3, 2, 1, True),
+    ("1x1_s2_downsample", 2, 256, 56, 512, 1, 2, 0, True),
+    ("3x3_7x7map", 4, 512, 7, 512, 3, 1, 1, True),
+]
+
+
+@pytest.mark.parametrize("name,N,C,H,M,k,stride,pad,nhwc", CASES)
+def test_conv_shapes(dev, name, N, C, H, M, k, stride, pad, nhwc):
+    rng = np.random.default_rng(sum(name.encode()))
+    X = rng.standard_normal((N, C, H, H)).astype(np.float32)
+    W = (rng.standard_normal((M, C, k, k)) * np.sqrt(2.0 / (C * k * k))).astype(np.float32)
+    bias = (rng.standard_normal(M) * 0.01).astype(np.float32)
+    got, ref, ws = _run_conv(dev, X, W, bias, stride, pad, nhwc_in=nhwc)
+    assert (ws == 0) == (name == "1x1_direct")
+    assert_close(got, ref, what=name)
+
+
+def test_conv_residual_relu_e4m3_out(dev):
+    rng = np.random.default_rng(5)
+    X = rng.standard_normal((2, 64, 28, 28)).astype(np.float32)
+    W = (rng.standard_normal((256, 64, 1, 1)) * 0.1).astype(np.float32)
+    R = rng.standard_normal((2, 256, 28, 28)).astype(np.float32)
+    got32, ref, _ = _run_conv(dev, X, W, None, 1, 0, relu=True, residual=R)
+    assert_close(got32, ref, what="residual + relu")
+    ys = np.float32(oracle.scale_from_amax(np.abs(ref).max()))
+    got8, _, _ = _run_conv(dev, X, W, None, 1, 0, relu=True, residual=R, out="e4m3", y_scale=ys)
+    want = oracle.dequantize(oracle.quantize(ref, ys), ys)
+    step = np.maximum(np.abs(want) * 0.125, ys * 2.0 ** -9)
+    assert (np.abs(got8 * ys - want) <= step + 1e-7).all()
