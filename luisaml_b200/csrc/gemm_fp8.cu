@@ -19,6 +19,7 @@
 #include <cuda_bf16.h>
 #include <cudaTypedefs.h>
 
+#include <cstring>
 #include <mutex>
 
 #include "lcml_device.cuh"
@@ -55,6 +56,7 @@ struct EpiParams {
     int64_t y_col_offset;
     void *const *y_peers;
     int y_num_peers;
+    int tma_store;  // output written by TMA stores through the kernel's output tensor map
 };
 
 __device__ __forceinline__ float silu_mul(float g, float u) {
@@ -138,7 +140,12 @@ __device__ __forceinline__ void load_cmat32(const EpiParams &ep, int64_t row, in
                 const uint4 w = *reinterpret_cast<const uint4 *>(cp + 16 * j);
                 const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
 #pragma unroll
-                for (int k = 0; k < 16; ++k) r[16 * j + k] = e4m3_decode((ws[k >> 2] >> ((k & 3) * 8)) & 0xffu) * cs;
+                for (int k = 0; k < 8; ++k) {
+                    float lo, hi;
+                    e4m3x2_decode(ws[k >> 1] >> ((k & 1) * 16), lo, hi);
+                    r[16 * j + 2 * k] = lo * cs;
+                    r[16 * j + 2 * k + 1] = hi * cs;
+                }
             }
         } else {
 #pragma unroll
@@ -181,81 +188,30 @@ __device__ __forceinline__ void load_cmat32(const EpiParams &ep, int64_t row, in
     for (int j = 0; j < 32; ++j) r[j] *= ep.beta;
 }
 
-// Stores 32 consecutive output values of one row (vector stores when the row
-// segment is in range and 16-byte aligned).
-template <int OUT>
-__device__ __forceinline__ void store_row32_to(const EpiParams &ep, void *ybase, int64_t row, int64_t col0, int64_t n_out,
-                                               const float (&v)[32], float ys);
+constexpr int out_es(int out) { return out == kOutF32 ? 4 : (out == kOutBF16 ? 2 : 1); }
 
-// Stores to the local output and, for the fused all-gather, to every peer's.
-template <int OUT>
-__device__ __forceinline__ void store_row32(const EpiParams &ep, int64_t row, int64_t col0, int64_t n_out,
-                                            const float (&v)[32], float ys) {
-    store_row32_to<OUT>(ep, ep.y, row, col0, n_out, v, ys);
-    for (int p = 0; p < ep.y_num_peers; ++p) store_row32_to<OUT>(ep, ep.y_peers[p], row, col0, n_out, v, ys);
-}
+// Output quantization constants of one launch: y_scale, RN(1 / y_scale) and
+// whether the multiply-by-reciprocal path of quantize2_fast applies.
+struct OutQuant {
+    float ys, r;
+    bool s_ok;
+};
 
 template <int OUT>
-__device__ __forceinline__ void store_row32_to(const EpiParams &ep, void *ybase, int64_t row, int64_t col0, int64_t n_out,
-                                               const float (&v)[32], float ys) {
-    const bool full = (col0 + 32 <= n_out);
-    const int64_t ocol0 = col0 + ep.y_col_offset;
-    if (OUT == kOutBF16) {
-        __nv_bfloat16 *yp = reinterpret_cast<__nv_bfloat16 *>(ybase) + row * ep.ldy + ocol0;
-        if (full && aligned(yp, 16)) {
-            uint32_t p[16];
-#pragma unroll
-            for (int j = 0; j < 16; ++j) {
-                __nv_bfloat162 h = __floats2bfloat162_rn(v[2 * j], v[2 * j + 1]);
-                p[j] = *reinterpret_cast<uint32_t *>(&h);
-            }
-#pragma unroll
-            for (int j = 0; j < 4; ++j)
-                reinterpret_cast<uint4 *>(yp)[j] = make_uint4(p[4 * j], p[4 * j + 1], p[4 * j + 2], p[4 * j + 3]);
-            return;
-        }
-    } else if (OUT == kOutF32) {
-        float *yp = reinterpret_cast<float *>(ybase) + row * ep.ldy + ocol0;
-        if (full && aligned(yp, 16)) {
-#pragma unroll
-            for (int j = 0; j < 8; ++j)
-                reinterpret_cast<float4 *>(yp)[j] = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
-            return;
-        }
-    } else {
-        uint8_t *yp = reinterpret_cast<uint8_t *>(ybase) + row * ep.ldy + ocol0;
-        if (full && aligned(yp, 16)) {
-            uint32_t p[8];
-#pragma unroll
-            for (int j = 0; j < 8; ++j)
-                p[j] = quantize1(v[4 * j], ys) | (quantize1(v[4 * j + 1], ys) << 8) |
-                       (quantize1(v[4 * j + 2], ys) << 16) | (quantize1(v[4 * j + 3], ys) << 24);
-            reinterpret_cast<uint4 *>(yp)[0] = make_uint4(p[0], p[1], p[2], p[3]);
-            reinterpret_cast<uint4 *>(yp)[1] = make_uint4(p[4], p[5], p[6], p[7]);
-            return;
-        }
+__device__ __forceinline__ OutQuant make_out_quant(const EpiParams &ep) {
+    OutQuant q{1.0f, 1.0f, false};
+    if (OUT == kOutE4M3) {
+        q.ys = __ldg(ep.y_scale);
+        q.r = __frcp_rn(q.ys);
+        q.s_ok = scale_fast_ok(q.ys, q.r);
     }
-#pragma unroll
-    for (int j = 0; j < 32; ++j)
-        if (col0 + j < n_out) store_out<OUT>(ybase, ep.ldy, row, ocol0 + j, v[j], ys);
+    return q;
 }
 
-// Warp-cooperative store of a 32-row x 32-column chunk through shared memory:
-// lane l holds row (row0 + l); after a swizzled transpose each store
-// instruction writes whole 16-byte pieces of (32 / P) consecutive rows, i.e.
-// (32 / P) contiguous row segments of 32 elements, instead of 32 scattered
-// 16-byte pieces. Used when the output also goes to peer GPUs, where NVLink
-// write efficiency depends on contiguous segments. `stage` holds 32 x 32
-// elements for this warp. All 32 lanes must call it.
+// 32 values -> the output's bytes as 8 * element-size little-endian words
+// (e4m3 bit-identical to quantize1 through quantize2_fast).
 template <int OUT>
-__device__ __forceinline__ void store_chunk_staged(const EpiParams &ep, uint8_t *stage, int64_t row0, int64_t col0,
-                                                   const float (&v)[32], float ys) {
-    constexpr int ES = OUT == kOutF32 ? 4 : (OUT == kOutBF16 ? 2 : 1);
-    constexpr int RB = 32 * ES;      // bytes of one chunk row
-    constexpr int P = RB / 16;       // 16-byte pieces per row
-    constexpr int LPG = 8 / P;       // lanes sharing one swizzle phase (8 lanes per shared-memory wavefront)
-    const int lane = static_cast<int>(threadIdx.x & 31);
-    uint32_t w[8 * ES];
+__device__ __forceinline__ void pack32(const float (&v)[32], const OutQuant &q, uint32_t (&w)[8 * out_es(OUT)]) {
     if (OUT == kOutF32) {
 #pragma unroll
         for (int j = 0; j < 32; ++j) w[j] = __float_as_uint(v[j]);
@@ -266,25 +222,82 @@ __device__ __forceinline__ void store_chunk_staged(const EpiParams &ep, uint8_t 
             w[j] = *reinterpret_cast<uint32_t *>(&h);
         }
     } else {
+        // quantize2_fast over the whole chunk without a branch per pair: the
+        // hardware conversions of x * RN(1/s) for all 32 values, one flag for
+        // "some value needs the exact path", one branch at the end.
+        bool exact = !q.s_ok;
 #pragma unroll
-        for (int j = 0; j < 8; ++j)
-            w[j] = quantize1(v[4 * j], ys) | (quantize1(v[4 * j + 1], ys) << 8) | (quantize1(v[4 * j + 2], ys) << 16) |
-                   (quantize1(v[4 * j + 3], ys) << 24);
+        for (int j = 0; j < 8; ++j) {
+            float a[4];
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+                a[k] = v[4 * j + k] * q.r;
+                exact |= needs_exact(a[k], v[4 * j + k]);
+            }
+            uint32_t x = cvt_e4m3x2(a[0], a[1]) | (cvt_e4m3x2(a[2], a[3]) << 16);
+#pragma unroll
+            for (int k = 0; k < 4; ++k)
+                if (v[4 * j + k] == 0.0f) x &= ~(0xffu << (8 * k));  // +-0 -> 0x00
+            w[j] = x;
+        }
+        if (exact) {
+#pragma unroll 1
+            for (int j = 0; j < 8; ++j)
+                w[j] = quantize1(v[4 * j], q.ys) | (quantize1(v[4 * j + 1], q.ys) << 8) |
+                       (quantize1(v[4 * j + 2], q.ys) << 16) | (quantize1(v[4 * j + 3], q.ys) << 24);
+        }
     }
+}
+
+// Stores 32 consecutive output values of one row (vector stores when the row
+// segment is in range and 16-byte aligned).
+template <int OUT>
+__device__ __forceinline__ void store_row32_to(const EpiParams &ep, void *ybase, int64_t row, int64_t col0, int64_t n_out,
+                                               const float (&v)[32], const OutQuant &q) {
+    constexpr int ES = out_es(OUT);
+    const int64_t ocol0 = col0 + ep.y_col_offset;
+    uint8_t *yp = reinterpret_cast<uint8_t *>(ybase) + (row * ep.ldy + ocol0) * ES;
+    if (col0 + 32 <= n_out && aligned(yp, 16)) {
+        uint32_t w[8 * ES];
+        pack32<OUT>(v, q, w);
+#pragma unroll
+        for (int p = 0; p < 2 * ES; ++p)
+            reinterpret_cast<uint4 *>(yp)[p] = make_uint4(w[4 * p], w[4 * p + 1], w[4 * p + 2], w[4 * p + 3]);
+        return;
+    }
+#pragma unroll
+    for (int j = 0; j < 32; ++j)
+        if (col0 + j < n_out) store_out<OUT>(ybase, ep.ldy, row, ocol0 + j, v[j], q.ys);
+}
+
+// Warp-cooperative store of a 32-row x 32-column chunk through shared memory
+// to the local output and every peer's: lane l holds row (row0 + l); after a
+// swizzled transpose each store instruction writes whole 16-byte pieces of
+// (32 / P) consecutive rows, i.e. (32 / P) contiguous row segments, instead of
+// 32 scattered 16-byte pieces (NVLink write efficiency depends on contiguous
+// segments). `stage` holds 32 x 32 elements for this warp. All 32 lanes call it.
+template <int OUT>
+__device__ __forceinline__ void store_chunk_peers(const EpiParams &ep, uint8_t *stage, int64_t row0, int64_t col0,
+                                                  const uint32_t (&w)[8 * out_es(OUT)]) {
+    constexpr int ES = out_es(OUT);
+    constexpr int RB = 32 * ES;      // bytes of one chunk row
+    constexpr int P = RB / 16;       // 16-byte pieces per row
+    constexpr int LPG = 8 / P;       // lanes sharing one swizzle phase (8 lanes per shared-memory wavefront)
+    const int lane = static_cast<int>(threadIdx.x & 31);
     const int fw = (lane / LPG) % P;
 #pragma unroll
     for (int p = 0; p < P; ++p)
         *reinterpret_cast<uint4 *>(stage + lane * RB + ((p ^ fw) * 16)) =
             make_uint4(w[4 * p], w[4 * p + 1], w[4 * p + 2], w[4 * p + 3]);
     __syncwarp();
-    const int q = lane % P;
+    const int qq = lane % P;
 #pragma unroll
     for (int k = 0; k < P; ++k) {
         const int r = lane / P + k * (32 / P);
-        const uint4 d = *reinterpret_cast<const uint4 *>(stage + r * RB + ((q ^ ((r / LPG) % P)) * 16));
+        const uint4 d = *reinterpret_cast<const uint4 *>(stage + r * RB + ((qq ^ ((r / LPG) % P)) * 16));
         const int64_t row = row0 + r;
         if (row < ep.M) {
-            const int64_t off = (row * ep.ldy + ep.y_col_offset + col0) * ES + q * 16;
+            const int64_t off = (row * ep.ldy + ep.y_col_offset + col0) * ES + qq * 16;
             *reinterpret_cast<uint4 *>(static_cast<uint8_t *>(ep.y) + off) = d;
             for (int pr = 0; pr < ep.y_num_peers; ++pr)
                 *reinterpret_cast<uint4 *>(static_cast<uint8_t *>(ep.y_peers[pr]) + off) = d;
@@ -293,18 +306,47 @@ __device__ __forceinline__ void store_chunk_staged(const EpiParams &ep, uint8_t 
     __syncwarp();
 }
 
-// Epilogue of 32 output columns [col0, col0+32) of one row. g holds the
-// accumulators of gemm columns ng0.. (for SILU_MUL: the gate columns; u the
-// up columns nu0..). All parameter-dependent branches are per chunk; the
-// element loop is branch-free.
-template <int EPI, int OUT>
-__device__ __forceinline__ void epi_row32(const EpiParams &ep, int64_t row, bool row_ok, int64_t col0, int64_t ng0,
-                                          int64_t nu0, int64_t n_out, const uint32_t (&g)[32],
-                                          const uint32_t (&u)[32], float row_scale, float row_add, float ys,
-                                          float &amax, uint8_t *stage) {
-    ColFactors fg;
-    load_col_factors(ep, ng0, fg);
-    float v[32];
+// Per-warp staging for TMA stores: two buffers of 32 rows x 32 output
+// elements (double-buffered so the bulk copy of chunk i overlaps chunk i+1).
+// The row layout matches the output tensor map's swizzle (32B / 64B / 128B
+// for 1 / 2 / 4-byte elements: 16-byte piece p of row r sits at p ^ ((r * RB
+// / 128) mod P)), which also makes the 16-byte shared stores conflict-free.
+constexpr int kStageBytesPerWarp = 2 * 32 * 32 * 4;
+
+template <int OUT>
+__device__ __forceinline__ void store_chunk_tma(const CUtensorMap *tmY, uint8_t *stage, uint32_t &seq, int64_t row0,
+                                                int64_t col0, const uint32_t (&w)[8 * out_es(OUT)]) {
+    constexpr int ES = out_es(OUT);
+    constexpr int RB = 32 * ES;
+    constexpr int P = RB / 16;
+    const int lane = static_cast<int>(threadIdx.x & 31);
+    uint8_t *buf = stage + (seq & 1u) * (32 * RB);
+    if (lane == 0) bulk_wait_group_read<1>();  // the copy that last read `buf` (two chunks ago) is done
+    __syncwarp();
+    const int sw = (lane * RB / 128) % P;
+#pragma unroll
+    for (int p = 0; p < P; ++p)
+        *reinterpret_cast<uint4 *>(buf + lane * RB + ((p ^ sw) * 16)) =
+            make_uint4(w[4 * p], w[4 * p + 1], w[4 * p + 2], w[4 * p + 3]);
+    fence_proxy_async_smem();
+    __syncwarp();
+    if (lane == 0) {
+        tma_store_2d(tmY, buf, static_cast<int>(col0), static_cast<int>(row0));
+        bulk_commit_group();
+    }
+    ++seq;
+}
+
+// Values of 32 output columns [col0, col0+32) of one row: scale, beta*C,
+// SiLU*up, residual, Relu, running |max|. g holds the accumulators of gemm
+// columns ng0.. (for SILU_MUL the gate columns; u the up columns nu0..), fg
+// their column factors. Parameter-dependent branches are per chunk; the
+// element loops are branch-free.
+template <int EPI>
+__device__ __forceinline__ void epi_values(const EpiParams &ep, int64_t row, bool row_ok, int64_t col0, int64_t nu0,
+                                           int64_t n_out, const uint32_t (&g)[32], const uint32_t (&u)[32],
+                                           const ColFactors &fg, float row_scale, float row_add, float &amax,
+                                           float (&v)[32]) {
 #pragma unroll
     for (int j = 0; j < 32; ++j) v[j] = fmaf(__uint_as_float(g[j]) * row_scale, fg.scale[j], fg.add[j] + row_add);
     if (EPI == LCML_EPI_SILU_MUL) {
@@ -316,20 +358,7 @@ __device__ __forceinline__ void epi_row32(const EpiParams &ep, int64_t row, bool
             v[j] = silu_mul(v[j], up);
         }
     }
-    // staged (peer) path: warp-uniform condition, every lane takes part
-    constexpr int ES = OUT == kOutF32 ? 4 : (OUT == kOutBF16 ? 2 : 1);
-    const bool staged = stage != nullptr && col0 + 32 <= n_out && ((ep.ldy * ES) % 16 == 0) &&
-                        (((ep.y_col_offset + col0) * ES) % 16 == 0) && !ep.c_mat && !ep.row_amax;
-    if (staged) {
-        if (EPI == LCML_EPI_RELU) {
-#pragma unroll
-            for (int j = 0; j < 32; ++j) v[j] = fmaxf(v[j], 0.0f);
-        }
-        store_chunk_staged<OUT>(ep, stage, row - static_cast<int64_t>(threadIdx.x & 31), col0, v, ys);
-        return;
-    }
-    if (!row_ok) return;
-    if (ep.c_mat) {
+    if (ep.c_mat && row_ok) {
         float r[32];
         load_cmat32(ep, row, col0, n_out, r);
 #pragma unroll
@@ -343,7 +372,6 @@ __device__ __forceinline__ void epi_row32(const EpiParams &ep, int64_t row, bool
 #pragma unroll
         for (int j = 0; j < 32; ++j) amax = (col0 + j < n_out) ? fmaxf(amax, fabsf(v[j])) : amax;
     }
-    store_row32<OUT>(ep, row, col0, n_out, v, ys);
 }
 
 __device__ __forceinline__ void atomic_max_abs(float *p, float v) {
@@ -351,38 +379,52 @@ __device__ __forceinline__ void atomic_max_abs(float *p, float v) {
     atomicMax(reinterpret_cast<unsigned int *>(p), __float_as_uint(v));
 }
 
-// One output tile's epilogue for the calling thread: TMEM lane `row` of the
-// accumulator at `taddr` (BN fp32 columns), gemm column block `tn`.
+// One output tile's epilogue for the calling warp: TMEM lanes of rows
+// [row0, row0+32) (lane l = row row0 + l) of the accumulator at `taddr` (BN
+// fp32 columns), gemm column block `tn`. Chunks past the last output column
+// are skipped; a warp whose rows are all past M does nothing. `stage` is the
+// warp's staging area, `seq` its running chunk count (TMA buffer parity).
 template <int BN, int EPI, int OUT>
-__device__ __forceinline__ void epilogue_tile(const EpiParams &ep, uint32_t taddr, int64_t row, int tn, float ys,
-                                              uint8_t *stage) {
+__device__ __forceinline__ void epilogue_tile(const EpiParams &ep, const CUtensorMap *tmY, uint32_t taddr, int64_t row0,
+                                              int tn, const OutQuant &oq, uint8_t *stage, uint32_t &seq) {
+    if (row0 >= ep.M) return;
     const int64_t n_out = (EPI == LCML_EPI_SILU_MUL) ? ep.N / 2 : ep.N;
+    const int64_t row = row0 + static_cast<int64_t>(threadIdx.x & 31);
     const bool row_ok = row < ep.M;
     const float row_scale = ep.alpha * (ep.sa_row ? (row_ok ? __ldg(ep.sa + row) : 0.0f) : __ldg(ep.sa));
     float row_add = 0.0f;  // beta * C broadcast as a scalar or along M
     if (ep.c_vec_mode == 1) row_add = ep.beta * __ldg(ep.c_vec);
     else if (ep.c_vec_mode == 2 && row_ok) row_add = ep.beta * __ldg(ep.c_vec + row);
     float amax = 0.0f;
-    if (EPI == LCML_EPI_SILU_MUL) {
-        // BN columns = BN/2 gate columns followed by BN/2 up columns
+    constexpr int kChunks = (EPI == LCML_EPI_SILU_MUL) ? BN / 64 : BN / 32;
 #pragma unroll 1
-        for (int c = 0; c < BN / 64; ++c) {
-            uint32_t g[32], u[32];
-            tmem_ld_32x32b_x32(taddr + c * 32, g);
-            tmem_ld_32x32b_x32(taddr + BN / 2 + c * 32, u);
-            tmem_wait_ld();
-            const int64_t ng0 = static_cast<int64_t>(tn) * BN + c * 32;
-            const int64_t col0 = static_cast<int64_t>(tn) * (BN / 2) + c * 32;
-            epi_row32<EPI, OUT>(ep, row, row_ok, col0, ng0, ng0 + BN / 2, n_out, g, u, row_scale, row_add, ys, amax, stage);
-        }
-    } else {
-#pragma unroll 1
-        for (int c = 0; c < BN / 32; ++c) {
-            uint32_t g[32];
-            tmem_ld_32x32b_x32(taddr + c * 32, g);
-            tmem_wait_ld();
-            const int64_t col0 = static_cast<int64_t>(tn) * BN + c * 32;
-            epi_row32<EPI, OUT>(ep, row, row_ok, col0, col0, 0, n_out, g, g, row_scale, row_add, ys, amax, stage);
+    for (int c = 0; c < kChunks; ++c) {
+        // SILU_MUL: BN columns = BN/2 gate columns followed by BN/2 up columns
+        const int64_t ng0 = static_cast<int64_t>(tn) * BN + c * 32;
+        const int64_t col0 = (EPI == LCML_EPI_SILU_MUL) ? static_cast<int64_t>(tn) * (BN / 2) + c * 32 : ng0;
+        if (col0 >= n_out) break;  // warp-uniform
+        uint32_t g[32], u[32];
+        tmem_ld_32x32b_x32(taddr + c * 32, g);
+        if (EPI == LCML_EPI_SILU_MUL) tmem_ld_32x32b_x32(taddr + BN / 2 + c * 32, u);
+        ColFactors fg;
+        load_col_factors(ep, ng0, fg);  // global loads overlap the TMEM load
+        tmem_wait_ld();
+        float v[32];
+        epi_values<EPI>(ep, row, row_ok, col0, ng0 + BN / 2, n_out, g, EPI == LCML_EPI_SILU_MUL ? u : g, fg,
+                        row_scale, row_add, amax, v);
+        constexpr int ES = out_es(OUT);
+        if (ep.tma_store) {
+            uint32_t w[8 * ES];
+            pack32<OUT>(v, oq, w);
+            store_chunk_tma<OUT>(tmY, stage, seq, row0, col0, w);
+        } else if (ep.y_num_peers > 0 && col0 + 32 <= n_out && ((ep.ldy * ES) % 16 == 0) &&
+                   (((ep.y_col_offset + col0) * ES) % 16 == 0)) {
+            uint32_t w[8 * ES];
+            pack32<OUT>(v, oq, w);
+            store_chunk_peers<OUT>(ep, stage, row0, col0, w);
+        } else if (row_ok) {
+            store_row32_to<OUT>(ep, ep.y, row, col0, n_out, v, oq);
+            for (int p = 0; p < ep.y_num_peers; ++p) store_row32_to<OUT>(ep, ep.y_peers[p], row, col0, n_out, v, oq);
         }
     }
     if (ep.row_amax && row_ok) atomic_max_abs(ep.row_amax + row, amax);
@@ -408,14 +450,14 @@ struct Layout {
     static constexpr int kStageBytes = kABytes + kBBytes;
     static constexpr int kTmemCols = 2 * BN;  // double-buffered fp32 accumulator
     static constexpr int kBarOffset = STAGES * kStageBytes;
-    static constexpr int kEpiOffset = kBarOffset + 1024;     // 4 warps x 32 x 32 fp32 staging (peer stores)
-    static constexpr int kSmemBytes = kEpiOffset + 4 * 4096 + 1024;  // +1024 for manual alignment
+    static constexpr int kEpiOffset = kBarOffset + 1024;     // 4 epilogue warps' output staging
+    static constexpr int kSmemBytes = kEpiOffset + 4 * kStageBytesPerWarp + 1024;  // +1024 for manual alignment
 };
 
 template <int BN, int STAGES, int EPI, int OUT>
 __global__ void __launch_bounds__(kThreads, 1)
-    k_gemm_fp8_tc(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, int M, int N,
-                  int K, EpiParams ep, int *err) {
+    k_gemm_fp8_tc(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                  const __grid_constant__ CUtensorMap tmY, int M, int N, int K, EpiParams ep, int *err) {
     using L = Layout<BN, STAGES>;
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -536,8 +578,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     } else {
         // ---------------- epilogue warps ----------------
         const int quarter = warp & 3;  // TMEM lanes [32*quarter, 32*quarter+32)
-        const float ys = (OUT == kOutE4M3) ? __ldg(ep.y_scale) : 1.0f;
-        uint8_t *stage = ep.y_num_peers > 0 ? smem + L::kEpiOffset + quarter * 4096 : nullptr;
+        const OutQuant oq = make_out_quant<OUT>(ep);
+        uint8_t *stage = smem + L::kEpiOffset + quarter * kStageBytesPerWarp;
+        uint32_t seq = 0;
+        if (ep.tma_store && lane == 0) tma_prefetch_desc(&tmY);
         int acc = 0;
         uint32_t acc_phase = 0;
         for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
@@ -545,9 +589,9 @@ __global__ void __launch_bounds__(kThreads, 1)
             tile_coords(tile, num_m, num_n, tm, tn);
             if (!mbar_wait(&tfull[acc], acc_phase, err, kDevTimeoutEpilogue)) break;
             tc_fence_after();
-            const int64_t row = static_cast<int64_t>(tm) * BM + quarter * 32 + lane;
+            const int64_t row0 = static_cast<int64_t>(tm) * BM + quarter * 32;
             const uint32_t taddr = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + static_cast<uint32_t>(acc * BN);
-            epilogue_tile<BN, EPI, OUT>(ep, taddr, row, tn, ys, stage);
+            epilogue_tile<BN, EPI, OUT>(ep, &tmY, taddr, row0, tn, oq, stage, seq);
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(&tempty[acc]);
@@ -556,6 +600,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 acc_phase ^= 1u;
             }
         }
+        if (lane == 0) bulk_wait_group_all();  // TMA stores done before the staging memory goes away
     }
 
     tc_fence_before();
@@ -583,14 +628,14 @@ struct PairLayout {
     static constexpr int kStageBytes = 2 * kHalfBytes;    // per CTA
     static constexpr int kTmemCols = 512;                 // 2 x 256 fp32 accumulators
     static constexpr int kBarOffset = STAGES * kStageBytes;
-    static constexpr int kEpiOffset = kBarOffset + 1024;     // 4 warps x 32 x 32 fp32 staging (peer stores)
-    static constexpr int kSmemBytes = kEpiOffset + 4 * 4096 + 1024;
+    static constexpr int kEpiOffset = kBarOffset + 1024;     // 4 epilogue warps' output staging
+    static constexpr int kSmemBytes = kEpiOffset + 4 * kStageBytesPerWarp + 1024;
 };
 
 template <int STAGES, int EPI, int OUT>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
-    k_gemm_fp8_tc2(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, int M, int N,
-                   int K, EpiParams ep, int *err) {
+    k_gemm_fp8_tc2(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                   const __grid_constant__ CUtensorMap tmY, int M, int N, int K, EpiParams ep, int *err) {
     using L = PairLayout<STAGES>;
     constexpr int BN = 256;
     extern __shared__ uint8_t smem_raw[];
@@ -718,8 +763,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     } else {
         // ---------------- epilogue warps (both CTAs) ----------------
         const int quarter = warp & 3;
-        const float ys = (OUT == kOutE4M3) ? __ldg(ep.y_scale) : 1.0f;
-        uint8_t *stage = ep.y_num_peers > 0 ? smem + L::kEpiOffset + quarter * 4096 : nullptr;
+        const OutQuant oq = make_out_quant<OUT>(ep);
+        uint8_t *stage = smem + L::kEpiOffset + quarter * kStageBytesPerWarp;
+        uint32_t seq = 0;
+        if (ep.tma_store && lane == 0) tma_prefetch_desc(&tmY);
         const uint32_t tempty_leader = mapa_shared(smem_u32(&tempty[0]), 0);
         int acc = 0;
         uint32_t acc_phase = 0;
@@ -728,9 +775,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
             tile_coords(tile, num_m, num_n, tm, tn);
             if (!mbar_wait(&tfull[acc], acc_phase, err, kDevTimeoutEpilogue)) break;
             tc_fence_after();
-            const int64_t row = static_cast<int64_t>(tm) * 256 + rank * 128 + quarter * 32 + lane;
+            const int64_t row0 = static_cast<int64_t>(tm) * 256 + rank * 128 + quarter * 32;
             const uint32_t taddr = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + static_cast<uint32_t>(acc * BN);
-            epilogue_tile<BN, EPI, OUT>(ep, taddr, row, tn, ys, stage);
+            epilogue_tile<BN, EPI, OUT>(ep, &tmY, taddr, row0, tn, oq, stage, seq);
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive_cluster(tempty_leader + 8u * static_cast<uint32_t>(acc));
@@ -739,6 +786,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                 acc_phase ^= 1u;
             }
         }
+        if (lane == 0) bulk_wait_group_all();  // TMA stores done before the staging memory goes away
     }
 
     tc_fence_before();
@@ -836,7 +884,8 @@ __global__ void __launch_bounds__(256) k_gemm_fp8_simt(const uint8_t *__restrict
 // ---------------------------------------------------------------------------
 // Host side
 // ---------------------------------------------------------------------------
-// Kernel selection override for tests: 0 automatic, 1 single-CTA, 2 CTA pair.
+// Kernel selection override for tests: bits 0-1: 0 automatic, 1 single-CTA,
+// 2 CTA pair; bit 2: store the output with plain stores instead of TMA.
 int g_gemm_mode = 0;
 
 PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
@@ -869,6 +918,37 @@ int make_tmap(CUtensorMap *map, const void *ptr, int64_t k, int64_t rows, int64_
     return LCML_OK;
 }
 
+// Output tensor map for the TMA-store epilogue: `rows` x `cols` elements of
+// `es` bytes starting at `ptr`, row pitch `ld_bytes`, box 32 x 32 with the
+// swizzle whose span equals one box row (32 * es bytes).
+int make_tmap_out(CUtensorMap *map, void *ptr, int64_t cols, int64_t rows, int64_t ld_bytes, int es) {
+    auto fn = encode_fn();
+    if (!fn) return set_error(LCML_ERR_CUDA, "cuTensorMapEncodeTiled is not available from the driver");
+    cuuint64_t dims[2] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows)};
+    cuuint64_t strides[1] = {static_cast<cuuint64_t>(ld_bytes)};
+    cuuint32_t box[2] = {32, 32};
+    cuuint32_t estr[2] = {1, 1};
+    const CUtensorMapDataType dt =
+        es == 4 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : (es == 2 ? CU_TENSOR_MAP_DATA_TYPE_UINT16 : CU_TENSOR_MAP_DATA_TYPE_UINT8);
+    const CUtensorMapSwizzle sw =
+        es == 4 ? CU_TENSOR_MAP_SWIZZLE_128B : (es == 2 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_32B);
+    CUresult r = fn(map, dt, 2, ptr, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, sw,
+                    CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS)
+        return set_error(LCML_ERR_CUDA, "cuTensorMapEncodeTiled (output) failed (%d)", static_cast<int>(r));
+    return LCML_OK;
+}
+
+// The output map when the epilogue stores through TMA, else an unused zero map.
+template <int EPI, int OUT>
+int output_tmap(const lcml_fp8_gemm_desc *d, const EpiParams &ep, CUtensorMap *ty) {
+    memset(ty, 0, sizeof(*ty));
+    if (!ep.tma_store) return LCML_OK;
+    constexpr int ES = out_es(OUT);
+    const int64_t n_out = (EPI == LCML_EPI_SILU_MUL) ? d->N / 2 : d->N;
+    return make_tmap_out(ty, static_cast<uint8_t *>(d->Y) + d->y_col_offset * ES, n_out, d->M, d->ldy * ES, ES);
+}
+
 template <int BN, int STAGES, int EPI, int OUT>
 int launch_tc(const lcml_fp8_gemm_desc *d, const EpiParams &ep, cudaStream_t st) {
     using L = Layout<BN, STAGES>;
@@ -886,9 +966,12 @@ int launch_tc(const lcml_fp8_gemm_desc *d, const EpiParams &ep, cudaStream_t st)
     if (rc) return rc;
     rc = make_tmap(&tb, d->B, d->K, d->N, d->ldb, BN);
     if (rc) return rc;
+    CUtensorMap ty;
+    rc = output_tmap<EPI, OUT>(d, ep, &ty);
+    if (rc) return rc;
     const int64_t tiles = ((d->M + BM - 1) / BM) * ((d->N + BN - 1) / BN);
     const int grid = static_cast<int>(tiles < sm_count() ? tiles : sm_count());
-    kern<<<grid, kThreads, L::kSmemBytes, st>>>(ta, tb, static_cast<int>(d->M), static_cast<int>(d->N),
+    kern<<<grid, kThreads, L::kSmemBytes, st>>>(ta, tb, ty, static_cast<int>(d->M), static_cast<int>(d->N),
                                                  static_cast<int>(d->K), ep, device_error_word());
     LCML_LAUNCHED("gemm_fp8_tc");
     return LCML_OK;
@@ -911,10 +994,13 @@ int launch_tc2(const lcml_fp8_gemm_desc *d, const EpiParams &ep, cudaStream_t st
     if (rc) return rc;
     rc = make_tmap(&tb, d->B, d->K, d->N, d->ldb, 128);
     if (rc) return rc;
+    CUtensorMap ty;
+    rc = output_tmap<EPI, OUT>(d, ep, &ty);
+    if (rc) return rc;
     const int64_t tiles = ((d->M + 255) / 256) * ((d->N + 255) / 256);
     const int64_t pairs = sm_count() / 2;
     const int grid = static_cast<int>(2 * (tiles < pairs ? tiles : pairs));
-    kern<<<grid, kThreads, L::kSmemBytes, st>>>(ta, tb, static_cast<int>(d->M), static_cast<int>(d->N),
+    kern<<<grid, kThreads, L::kSmemBytes, st>>>(ta, tb, ty, static_cast<int>(d->M), static_cast<int>(d->N),
                                                  static_cast<int>(d->K), ep, device_error_word());
     LCML_LAUNCHED("gemm_fp8_tc2");
     return LCML_OK;
@@ -936,10 +1022,12 @@ int dispatch(const lcml_fp8_gemm_desc *d, const EpiParams &ep, cudaStream_t st, 
                         aligned(d->A, 16) && aligned(d->B, 16) && d->M <= 0x7fffffff && d->N <= 0x7fffffff &&
                         d->K <= 0x7fffffff;
     if (!tma_ok) return launch_simt<EPI, OUT>(d, ep, st);
-    // CTA pairs once there are enough 256 x 256 tiles to fill the machine
+    // CTA pairs (256 x 256 tiles, half the staged bytes per MMA) pay off once
+    // the mainloop is long and there are a couple of tiles per pair; short-K
+    // and narrow GEMMs are epilogue-bound and run single-CTA tiles as wide as N.
     const int64_t pair_tiles = ((d->M + 255) / 256) * ((d->N + 255) / 256);
-    if (g_gemm_mode != 1 && (g_gemm_mode == 2 || (d->M >= 256 && pair_tiles >= sm_count() / 2)))
-        return launch_tc2<EPI, OUT>(d, ep, st);
+    const bool pair = d->M >= 256 && d->N >= 256 && d->K >= 1024 && pair_tiles >= sm_count();
+    if ((g_gemm_mode & 3) != 1 && ((g_gemm_mode & 3) == 2 || pair)) return launch_tc2<EPI, OUT>(d, ep, st);
     if (EPI == LCML_EPI_SILU_MUL || d->N >= 2048) return launch_tc<256, 4, EPI, OUT>(d, ep, st);
     if (EPI != LCML_EPI_SILU_MUL && d->N <= 64) return launch_tc<64, 8, EPI, OUT>(d, ep, st);
     return launch_tc<128, 6, EPI, OUT>(d, ep, st);
@@ -1002,6 +1090,12 @@ int gemm_entry(const lcml_fp8_gemm_desc *d, lcml_stream_t stream, bool force_sim
     ep.y_col_offset = d->y_col_offset;
     ep.y_peers = d->y_peers;
     ep.y_num_peers = d->y_num_peers;
+    {
+        const int es = d->y_dtype == LCML_DTYPE_FLOAT ? 4 : (d->y_dtype == LCML_DTYPE_BFLOAT16 ? 2 : 1);
+        ep.tma_store = !(g_gemm_mode & 4) && d->y_num_peers == 0 && n_out <= 0x7fffffff && d->M <= 0x7fffffff &&
+                       aligned(static_cast<const uint8_t *>(d->Y) + d->y_col_offset * es, 16) &&
+                       (d->ldy * es) % 16 == 0;
+    }
     cudaStream_t st = to_cuda(stream);
     switch (d->epilogue) {
         case LCML_EPI_NONE: return dispatch_out<LCML_EPI_NONE>(d, ep, st, force_simt);

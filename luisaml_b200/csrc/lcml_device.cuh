@@ -72,18 +72,24 @@ __device__ __forceinline__ uint32_t quantize1(float x, float s) {
 }
 
 // Fast QuantizeLinear of two elements, bit-identical to quantize1():
-// q = x * r with r = RN(1/s) is within 2.5 fp32 ulps of RN(x / s), and every
-// e4m3 rounding boundary (a midpoint between neighbouring e4m3 values, incl.
-// the binade steps) has low 20 mantissa bits 0x80000. So whenever q is
-// normal in e4m3 terms (|q| >= 2^-6), finite, and its low 20 bits are more
-// than 3 ulps from 0x80000, q and x / s round to the same e4m3 value, which
-// the hardware cvt.rn.satfinite (RNE, |v| > 448 -> +-448) produces. All other
-// cases (zeros, e4m3 subnormals, NaN/inf, near-ties, unusual scales) take the
-// exact divide + integer encoder. `s_ok` says r is usable (s normal positive,
-// r finite normal).
-__device__ __forceinline__ bool needs_exact(float q) {
+// q = x * r with r = RN(1/s) is within 2.5 fp32 ulps of RN(x / s). Every e4m3
+// rounding boundary in the normal range (a midpoint between neighbouring e4m3
+// values, incl. the binade steps) has low 20 mantissa bits 0x80000; in the
+// subnormal range (|q| < 2^-6, grid 2^-9) the boundaries (2k+1) * 2^-10 have
+// low 20 bits 0. So whenever q is finite and its low 20 bits are more than 3
+// ulps away from the boundary pattern of its range, q and x / s round to the
+// same e4m3 value, which the hardware cvt.rn.satfinite (RNE, |v| > 448 ->
+// +-448, tiny values to a signed zero) produces. An exact +-0 input is 0x00
+// (x / s is +-0 for a usable scale and the codec drops the sign of zero),
+// which matters because Relu outputs are often half zeros. All other cases
+// (NaN/inf, near-boundaries, a product that underflowed to zero, unusual
+// scales) take the exact divide + integer encoder. `s_ok` says r is usable
+// (s normal positive, r finite normal).
+__device__ __forceinline__ bool needs_exact(float q, float x) {
     const uint32_t a = __float_as_uint(q) & 0x7fffffffu;
-    return (a < 0x3c800000u) | (a >= 0x7f800000u) | (((a & 0xfffffu) - 0x7fffdu) <= 6u);
+    const bool normal = a >= 0x3c800000u;
+    const uint32_t d = normal ? (a & 0xfffffu) - 0x7fffdu : (a + 3u) & 0xfffffu;
+    return (a >= 0x7f800000u) | ((d <= 6u) & (normal | (x != 0.0f)));
 }
 
 __device__ __forceinline__ uint32_t quantize2_fast(float x0, float x1, float s, float r, bool s_ok) {
@@ -94,7 +100,36 @@ __device__ __forceinline__ uint32_t quantize2_fast(float x0, float x1, float s, 
         "cvt.u32.u16 %0, t;\n\t}"
         : "=r"(out)
         : "f"(q0), "f"(q1));
-    if (!s_ok || needs_exact(q0) || needs_exact(q1)) out = quantize1(x0, s) | (quantize1(x1, s) << 8);
+    if (x0 == 0.0f) out &= 0xff00u;  // -0 -> 0x00
+    if (x1 == 0.0f) out &= 0x00ffu;
+    if (!s_ok || needs_exact(q0, x0) || needs_exact(q1, x1)) out = quantize1(x0, s) | (quantize1(x1, s) << 8);
+    return out;
+}
+
+// Two e4m3 codes (low byte, high byte of `b`) -> floats, exactly as
+// e4m3_decode: every e4m3 value, -0 and NaN included, is representable in
+// f16, so the hardware conversion through f16x2 is exact.
+__device__ __forceinline__ void e4m3x2_decode(uint32_t b, float &lo, float &hi) {
+    asm("{\n\t.reg .b16 t, h0, h1;\n\t"
+        "cvt.u16.u32 t, %2;\n\t"
+        "{\n\t.reg .b32 p;\n\t"
+        "cvt.rn.f16x2.e4m3x2 p, t;\n\t"
+        "mov.b32 {h0, h1}, p;\n\t}\n\t"
+        "cvt.f32.f16 %0, h0;\n\t"
+        "cvt.f32.f16 %1, h1;\n\t}"
+        : "=f"(lo), "=f"(hi)
+        : "r"(b));
+}
+
+// Hardware conversion of two values to e4m3 (RNE, saturating), low byte from
+// `lo`; no QuantizeLinear corner cases handled (see quantize2_fast).
+__device__ __forceinline__ uint32_t cvt_e4m3x2(float lo, float hi) {
+    uint32_t out;
+    asm("{\n\t.reg .b16 t;\n\t"
+        "cvt.rn.satfinite.e4m3x2.f32 t, %2, %1;\n\t"
+        "cvt.u32.u16 %0, t;\n\t}"
+        : "=r"(out)
+        : "f"(lo), "f"(hi));
     return out;
 }
 
@@ -188,6 +223,31 @@ __device__ __forceinline__ void tma_load_2d_pair(const void *tmap, uint32_t bar_
 
 __device__ __forceinline__ void tma_prefetch_desc(const void *tmap) {
     asm volatile("prefetch.tensormap [%0];" ::"l"(tmap) : "memory");
+}
+
+// TMA store of a 2-D box from this CTA's shared memory (bulk async-group
+// completion). The smem writes it reads must be made visible to the async
+// proxy first (fence_proxy_async_smem by every writing thread).
+__device__ __forceinline__ void tma_store_2d(const void *tmap, const void *smem_src, int x, int y) {
+    asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];" ::"l"(tmap),
+                 "r"(smem_u32(smem_src)), "r"(x), "r"(y)
+                 : "memory");
+}
+
+__device__ __forceinline__ void bulk_commit_group() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+
+// Waits until at most N committed bulk groups of this thread still read their
+// shared-memory source.
+template <int N>
+__device__ __forceinline__ void bulk_wait_group_read() {
+    asm volatile("cp.async.bulk.wait_group.read %0;" ::"n"(N) : "memory");
+}
+
+// Waits until every bulk group of this thread has completed (writes done).
+__device__ __forceinline__ void bulk_wait_group_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+
+__device__ __forceinline__ void fence_proxy_async_smem() {
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
 
 // ---------------------------------------------------------------------------

@@ -315,3 +315,43 @@ def test_gemm_column_shard_and_peer_copies(dev, gemm_mode, out, mode):
         assert_close_bf16(got.float().cpu().numpy(), ref, what="bf16 shard")
     else:
         assert_close(got.cpu().numpy(), ref, what="f32 shard")
+
+
+@pytest.mark.parametrize("out", ["f32", "bf16", "e4m3"])
+@pytest.mark.parametrize("mode", [1, 2])
+@pytest.mark.parametrize("M,N,K", [(300, 528, 200), (97, 64, 64), (1000, 96, 576)])
+def test_store_paths(dev, gemm_mode, out, mode, M, N, K):
+    """The TMA-store epilogue (default) and plain per-row stores (mode bit 4)
+    write bit-identical outputs, including ragged edges in M and N and an
+    output placed at a column offset inside a wider matrix whose other columns
+    must stay untouched; the fp32 result also matches the oracle and the e4m3
+    bytes equal the oracle's quantization of the fp32 result."""
+    import torch
+    import luisaml_b200 as lb
+    Aq, sa, Bq, sb = make_operands(M, N, K, seed=M * 7 + N + K, per_row=True, per_col=True)
+    bias = np.random.default_rng(N).standard_normal(N).astype(np.float32)
+    ref = np.maximum(oracle.qdq_gemm(Aq, sa, Bq, sb) + bias, 0.0)
+    dt = {"f32": torch.float32, "bf16": torch.bfloat16, "e4m3": torch.uint8}[out]
+    ys = _t(np.float32([oracle.scale_from_amax(np.abs(ref).max())]), dev)
+    args = (_t(Aq, dev), _t(Bq, dev), _t(sa, dev), _t(sb, dev))
+    results = []
+    for m in (mode, mode | 4):
+        gemm_mode(m)
+        wide = torch.zeros((M, N + 48), dtype=dt, device=dev)
+        wide.view(torch.uint8).fill_(0x55)
+        lb.gemm(*args, c_vec=_t(bias, dev), epilogue=lb.EPI_RELU, out=wide[:, 16:16 + N],
+                y_scale=ys if out == "e4m3" else None)
+        torch.cuda.synchronize()
+        assert lb.device_error() == 0
+        results.append(wide.view(torch.uint8).cpu().numpy())
+    np.testing.assert_array_equal(results[0], results[1])
+    es = {"f32": 4, "bf16": 2, "e4m3": 1}[out]
+    assert (results[0][:, :16 * es] == 0x55).all() and (results[0][:, (16 + N) * es:] == 0x55).all()
+    if out == "f32":
+        got = results[0].view(np.float32)[:, 16:16 + N]
+        assert_close(got, ref, what=f"store paths {M}x{N}x{K}")
+    elif out == "e4m3":
+        gemm_mode(mode)
+        y32 = lb.gemm(*args, c_vec=_t(bias, dev), epilogue=lb.EPI_RELU, out_dtype=torch.float32).cpu().numpy()
+        want = oracle.quantize(y32, float(ys.cpu()[0]))
+        np.testing.assert_array_equal(results[0][:, 16:16 + N], want)

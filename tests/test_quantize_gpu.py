@@ -39,18 +39,21 @@ def test_quantize_tensor_golden(dev):
     assert np.array_equal(q, g["q"])
 
 
-def test_encoder_exhaustive_all_fp32_patterns(dev):
-    """Every one of the 2^32 fp32 bit patterns, GPU kernel vs CPU oracle."""
+@pytest.mark.parametrize("scale", [1.0, 0.0123, 6.1e-3])
+def test_encoder_exhaustive_all_fp32_patterns(dev, scale):
+    """Every one of the 2^32 fp32 bit patterns, GPU kernel vs CPU oracle; with
+    scale 1 this checks the encoder itself, with the other scales the
+    multiply-by-reciprocal fast path (RN(1/s) inexact) over every input."""
     import torch
     import luisaml_b200 as lb
-    one = _one(dev)
+    one = _one(dev, scale)
     chunk = 1 << 28
     for c in range(1 << 4):
         bits = torch.arange(c * chunk, (c + 1) * chunk, dtype=torch.int64, device=dev)
         x = bits.to(torch.int32).view(torch.float32)  # wraps to the full uint32 range
         q = lb.quantize(x.contiguous(), one).cpu().numpy()
         xc = x.cpu().numpy()
-        ref = oracle.quantize(xc, np.float32(1.0))
+        ref = oracle.quantize(xc, np.float32(scale))
         bad = np.nonzero(q != ref)[0]
         assert bad.size == 0, f"chunk {c}: {bad.size} mismatches, first bits {xc[bad[0]:bad[0]+1].view(np.uint32)}"
 
