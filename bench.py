@@ -309,7 +309,8 @@ class FfnWorkload(GraphWorkload):
         self.T, self.D, self.F = tokens, d, f
 
     def describe(self):
-        return {"workload": f"llama_ffn_qdq_t{self.T}_d{self.D}_f{self.F}", "tokens_per_rank": self.t_rank,
+        return {"workload": f"llama_ffn_qdq_t{self.T}_d{self.D}_f{self.F}",
+                "tokens_per_rank": getattr(self, "t_rank", self.T),
                 "path": "LuisaML-JSON graph -> NetworkInstance with QDQ fusion (4 kernels per forward)",
                 "l2": "inputs larger than L2 (fp32 x and h); L2 flushed between timed steps"}
 
@@ -474,7 +475,59 @@ class TpGemmWorkload:
             self.peers.close()
 
 
+class ResnetWorkload(GraphWorkload):
+    """ResNet-50 v1.5 as a fully quantized QDQ graph at 224x224,
+    batch 128 per rank: 53 fused FP8 implicit-GEMM convs (scales, bias,
+    residual, Relu and requantization in the epilogue), e4m3 max pool and
+    global average pool, QDQ classifier. Each rank runs its own batch (weak
+    scaling, no collective)."""
+    unit = "inferences/s"
+    parallelism = "dp (independent batches per rank, no collective)"
+
+    def __init__(self, batch=128, image=224):
+        self.batch, self.image = batch, image
+        self.work_per_step = batch
+        self.flop_per_image = None  # known once the graph is built
+
+    def describe(self):
+        ws = int(os.environ.get("WORLD_SIZE", "1"))
+        return {"workload": f"resnet50_qdq_{self.image}", "batch_per_rank": self.batch,
+                "total_batch": self.batch * ws, "flop_per_image": self.flop_per_image,
+                "path": "LuisaML-JSON graph -> NetworkInstance: 53 fused FP8 convs, e4m3 pools, QDQ Gemm head",
+                "l2": "activations larger than L2; L2 flushed between timed steps"}
+
+    def setup(self, dev, seed):
+        import torch
+        from luisaml_b200 import graphs
+        text, blob, meta = graphs.resnet50(batch=self.batch, image=self.image)
+        self.flop_per_image = meta["flop_per_image"]
+        self.flops = float(self.flop_per_image) * self.batch
+        x = torch.randn((self.batch, 3, self.image, self.image), generator=torch.Generator(device=dev).manual_seed(seed),
+                        device=dev)
+        y = torch.empty((self.batch, 1000), dtype=torch.float32, device=dev)
+        self.setup_graph(dev, text, blob, {"x": x}, {"logits": y})
+
+    def dominant(self):
+        return {"kernel": "whole forward", "bound": "tensor", "unit": "TFLOP/s", "work": self.flops,
+                "profile": "resnet50", "kernel_only": False}
+
+    def cpu_sample(self, budget_s=15.0):
+        import oracle
+        from luisaml_b200 import graphs
+        _, _, meta = graphs.resnet50(batch=1, image=self.image)
+        self.flop_per_image = meta["flop_per_image"]
+        x = np.random.default_rng(0).standard_normal((1, 3, self.image, self.image)).astype(np.float32)
+        n, t0 = 0, time.perf_counter()
+        while n == 0 or time.perf_counter() - t0 < budget_s:
+            oracle.replay_plan(meta["plan"], x)
+            n += 1
+        t = time.perf_counter() - t0
+        return {"value": n / t, "unit": "inferences/s", "cores": oracle.num_threads(), "kind": "port",
+                "sample": f"{n} single-image forwards (QDQ replay: conv.cpp direct loop, pools, gemm.cpp), {t:.1f} s"}
+
+
 CONFIGS = {
+    "resnet50": lambda: ResnetWorkload(),
     "tp_gemm": lambda: TpGemmWorkload(),
     "mlp": lambda: MlpWorkload(),
     "ffn": lambda: FfnWorkload(),
@@ -504,13 +557,15 @@ def run_reference(args, wl):
         if i >= args.warmup:
             samples.append(r)
     v = statistics.median(s["value"] for s in samples)
-    line = {"impl": "reference", "metric": METRIC, "value": v, "unit": "TFLOP/s", "n_gpus": args.gpus,
+    unit = getattr(wl, "unit", "TFLOP/s")
+    metric = METRIC if unit == "TFLOP/s" else f"{wl.describe()['workload']} {unit}"
+    line = {"impl": "reference", "metric": metric, "value": v, "unit": unit, "n_gpus": args.gpus,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": None, "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "e4m3 x e4m3 -> fp32 accumulate", "data": "synthetic",
             "config": wl.describe(),
-            "cpu_baseline": {"value": v, "unit": "TFLOP/s", "cores": samples[0]["cores"], "kind": "port",
+            "cpu_baseline": {"value": v, "unit": unit, "cores": samples[0]["cores"], "kind": "port",
                              "sample": samples[0]["sample"]},
-            "e2e": {"value": v, "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+            "e2e": {"value": v, "unit": unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
             "note": "the reference's GPU path (LuisaCompute dx/vk backends) is unavailable on this box; this is "
                     "the reference algorithm restated in C (oracle/) on all host threads"}
     print(json.dumps(line), flush=True)

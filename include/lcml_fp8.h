@@ -240,9 +240,13 @@ int lcml_gemm_f32(const float *A, const float *B, const float *C, int64_t M, int
  * Stands in for Conv::forward (src/onnx/operators/conv.cpp:35-255), which
  * accumulates FP8 inputs in half precision; here products are exact and
  * accumulate in fp32. Lowering: output pixels are GEMM rows, output channels
- * GEMM columns, K = (kh, kw, c). A 1x1 / stride-1 / unpadded conv on an NHWC
- * input reads X as the GEMM's A directly; every other conv first gathers its
- * patches (im2col, e4m3, zero padding) into `workspace`.
+ * GEMM columns, K = (kh, kw, c) with c over Cp channels per tap: Cp = C
+ * when C is a multiple of 16, else C padded to 4, 8 or the next multiple of
+ * 16 (so each tap is one 4-, 8- or 16-byte vector). A 1x1 / stride-1 /
+ * unpadded conv on an NHWC input reads X as the GEMM's A directly; every other
+ * conv first gathers its patches (im2col, e4m3, zero padding) into
+ * `workspace`, after copying X into a channel-padded NHWC layout there when X
+ * is NCHW or C is not a multiple of 16.
  * X: e4m3, NHWC (x_nhwc = 1) or NCHW (x_nhwc = 0), per-tensor scale.
  * Wp: weights packed by lcml_fp8_conv_pack_weight, per-tensor or per-output-
  * channel scales. Y: NHWC [N, oH, oW, M] (the GEMM's row-major output),
@@ -269,14 +273,15 @@ typedef struct lcml_fp8_conv_desc {
     void *Y;
     int y_dtype;            /* FLOAT, BFLOAT16 or FLOAT8E4M3FN */
     const float *y_scale;   /* per-tensor output scale when y_dtype is e4m3 */
-    void *workspace;        /* lcml_fp8_conv_workspace_size() bytes, 16-byte aligned */
+    void *workspace;        /* lcml_fp8_conv_workspace_size() bytes, 256-byte aligned */
 } lcml_fp8_conv_desc;
 
-/* Packed K: kH * kW * C rounded up to a multiple of 16. */
+/* Packed K: kH * kW * Cp (Cp: C padded as above) rounded up to a multiple of 16. */
 int64_t lcml_fp8_conv_packed_k(int64_t Cg, int64_t kH, int64_t kW);
 /* Bytes of scratch lcml_fp8_conv needs for `desc` (0 for the direct 1x1 path, -1 on a bad desc). */
 int64_t lcml_fp8_conv_workspace_size(const lcml_fp8_conv_desc *desc);
-/* Packs e4m3 W [M, Cg, kH, kW] (ONNX layout) into Wp [M, Kp], K order (kh, kw, c), zero padded. */
+/* Packs e4m3 W [M, Cg, kH, kW] (ONNX layout) into Wp [M, Kp], K order (kh, kw, c) over Cp channels,
+ * zero in the padding channels and past kH * kW * Cp. */
 int lcml_fp8_conv_pack_weight(const uint8_t *W, int64_t M, int64_t Cg, int64_t kH, int64_t kW, uint8_t *Wp,
                               lcml_stream_t stream);
 int lcml_fp8_conv(const lcml_fp8_conv_desc *desc, lcml_stream_t stream);

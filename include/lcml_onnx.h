@@ -17,6 +17,7 @@
 #include <functional>
 #include <map>
 #include <memory>
+#include <set>
 #include <span>
 #include <stdexcept>
 #include <string>
@@ -369,6 +370,9 @@ public:
     size_t num_executed_nodes() const;
     std::vector<std::string> executed_node_summary() const;
     const FusionInfo *fusion_info(size_t node_index) const;
+    // True when the named tensor is stored NHWC (outputs of fused convolutions
+    // and pools); its shape() stays the ONNX NCHW shape.
+    bool is_nhwc(std::string_view name) const { return nhwc_.find(name) != nhwc_.end(); }
 
 private:
     void prepare();
@@ -387,6 +391,7 @@ private:
     TensorTable table_;
     std::vector<std::unique_ptr<Operator>> ops_;
     std::vector<std::unique_ptr<FusionInfo>> fusion_;
+    std::set<std::string, std::less<>> nhwc_;
 };
 
 // Throws Error with lcml_last_error() when a C-ABI call fails.

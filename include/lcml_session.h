@@ -45,6 +45,14 @@ int lcml_network_forward(lcml_network *net);
 /* After forward: nodes that launched work, and a one-line-per-node summary. */
 int lcml_network_executed_nodes(const lcml_network *net, int64_t *executed);
 int lcml_network_summary(const lcml_network *net, char *buf, size_t len);
+/* After forward: the device buffer of any tensor of the graph (inputs,
+ * outputs, intermediates, constants), like NetworkInstance::get_tensor_table()
+ * (include/onnx/network_instance.h:231). shape receives up to max_ndim
+ * extents of the ONNX shape; *nhwc is 1 when the tensor is stored NHWC (the
+ * outputs of fused convolutions and pools), else 0. Intermediates are
+ * separate allocations, so their contents stay valid until the next forward. */
+int lcml_network_tensor(const lcml_network *net, const char *name, void **device_ptr, int *dtype, int64_t *shape,
+                        int max_ndim, int *ndim, int *nhwc);
 /* Number of operators registered in the default opset. */
 int lcml_opset_size(void);
 

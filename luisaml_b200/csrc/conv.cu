@@ -6,6 +6,8 @@
 // no gather at all (X is already the GEMM's A). The epilogue fuses the
 // per-tensor x scale, per-channel w scale, bias, residual, Relu and the
 // requantization of the output.
+#include <type_traits>
+
 #include "lcml_device.cuh"
 #include "lcml_internal.h"
 
@@ -14,46 +16,86 @@ namespace {
 
 constexpr int kThreads = 256;
 
-int64_t packed_k(int64_t cg, int64_t kh, int64_t kw) { return ((cg * kh * kw + 15) / 16) * 16; }
+// Channels per tap in the packed K order: C itself when it is a multiple of
+// 16 (every tap is whole 16-byte vectors), else C padded to 4, 8 or the next
+// multiple of 16 so that each tap is one 4-, 8- or 16-byte vector.
+int64_t packed_c(int64_t c) { return c % 16 == 0 ? c : (c <= 4 ? 4 : (c <= 8 ? 8 : ((c + 15) / 16) * 16)); }
+
+int64_t packed_k(int64_t cg, int64_t kh, int64_t kw) { return ((packed_c(cg) * kh * kw + 15) / 16) * 16; }
 
 bool direct_path(const lcml_fp8_conv_desc *d) {
     return d->kH == 1 && d->kW == 1 && d->sH == 1 && d->sW == 1 && d->pH == 0 && d->pW == 0 && d->x_nhwc &&
            d->C % 16 == 0 && d->oH == d->H && d->oW == d->W;
 }
 
-// Wp[m, (kh*kW + kw)*Cg + c] = W[m, c, kh, kw]; zero beyond kH*kW*Cg.
+// The input is gathered straight from X (NHWC, C a multiple of 16) or from a
+// channel-padded NHWC copy of it in the workspace.
+bool needs_repack(const lcml_fp8_conv_desc *d) { return !(d->x_nhwc && d->C % 16 == 0); }
+
+int64_t repack_bytes(const lcml_fp8_conv_desc *d) {
+    return needs_repack(d) ? ((d->N * d->H * d->W * packed_c(d->C) + 255) / 256) * 256 : 0;
+}
+
+// Wp[m, (kh*kW + kw)*Cp + c] = W[m, c, kh, kw] for c < Cg; zero for the
+// padding channels and beyond kH*kW*Cp.
 __global__ void __launch_bounds__(kThreads) k_pack_weight(const uint8_t *__restrict__ W, int64_t M, int64_t Cg,
-                                                          int64_t kH, int64_t kW, int64_t Kp, uint8_t *__restrict__ Wp) {
+                                                          int64_t Cp, int64_t kH, int64_t kW, int64_t Kp,
+                                                          uint8_t *__restrict__ Wp) {
     const int64_t total = M * Kp;
     for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
          i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
         const int64_t m = i / Kp, k = i % Kp;
         uint8_t v = 0;
-        if (k < kH * kW * Cg) {
-            const int64_t tap = k / Cg, c = k % Cg;
+        if (k < kH * kW * Cp) {
+            const int64_t tap = k / Cp, c = k % Cp;
             const int64_t kh = tap / kW, kw = tap % kW;
-            v = W[((m * Cg + c) * kH + kh) * kW + kw];
+            if (c < Cg) v = W[((m * Cg + c) * kH + kh) * kW + kw];
         }
         Wp[i] = v;
     }
 }
 
-// NHWC im2col, C % 16 == 0: one 16-byte vector per (pixel, 16-channel chunk of a tap).
-__global__ void __launch_bounds__(kThreads) k_im2col_nhwc16(const uint8_t *__restrict__ X, int64_t N, int64_t C,
-                                                            int64_t H, int64_t W, int64_t kH, int64_t kW, int64_t oH,
-                                                            int64_t oW, int sH, int sW, int pH, int pW, int dH, int dW,
-                                                            int64_t Kp, uint8_t *__restrict__ A) {
-    const int64_t chunks = Kp / 16, taps_chunks = kH * kW * (C / 16);
-    const int64_t total = N * oH * oW * chunks;
-    for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
-         i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
-        const int64_t p = i / chunks, ch = i % chunks;
+// X (NCHW, or NHWC with C not a multiple of 16) -> Xc NHWC with Cp channels,
+// the padding channels zero. One thread per pixel; I is the index type.
+template <typename I, bool NHWC_IN>
+__global__ void __launch_bounds__(kThreads) k_repack_nhwc(const uint8_t *__restrict__ X, I N, I C, I HW, I Cp,
+                                                          uint8_t *__restrict__ Xc) {
+    const I total = N * HW;
+    for (I pix = static_cast<I>(blockIdx.x) * blockDim.x + threadIdx.x; pix < total;
+         pix += static_cast<I>(gridDim.x) * blockDim.x) {
+        const I n = pix / HW, hw = pix - n * HW;
+        for (I c0 = 0; c0 < Cp; c0 += 4) {
+            uint32_t w = 0;
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                const I c = c0 + j;
+                if (c < C) {
+                    const uint32_t b = NHWC_IN ? X[pix * C + c] : X[(n * C + c) * HW + hw];
+                    w |= b << (8 * j);
+                }
+            }
+            *reinterpret_cast<uint32_t *>(Xc + pix * Cp + c0) = w;
+        }
+    }
+}
+
+// im2col from NHWC with C a multiple of 16: one 16-byte vector per (pixel,
+// 16-channel piece of a tap). I is the index type (32-bit when it fits).
+template <typename I>
+__global__ void __launch_bounds__(kThreads) k_im2col_nhwc16(const uint8_t *__restrict__ X, I N, I C, I H, I W, I kH,
+                                                            I kW, I oH, I oW, I sH, I sW, I pH, I pW, I dH, I dW, I Kp,
+                                                            uint8_t *__restrict__ A) {
+    const I chunks = Kp / 16, cpt = C / 16, taps_chunks = kH * kW * cpt;
+    const I total = N * oH * oW * chunks;
+    for (I i = static_cast<I>(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
+         i += static_cast<I>(gridDim.x) * blockDim.x) {
+        const I p = i / chunks, ch = i - p * chunks;
         uint4 v = make_uint4(0, 0, 0, 0);
         if (ch < taps_chunks) {
-            const int64_t tap = ch / (C / 16), c16 = ch % (C / 16);
-            const int64_t kh = tap / kW, kw = tap % kW;
-            const int64_t ow = p % oW, t = p / oW, oh = t % oH, n = t / oH;
-            const int64_t ih = oh * sH + kh * dH - pH, iw = ow * sW + kw * dW - pW;
+            const I tap = ch / cpt, c16 = ch - tap * cpt;
+            const I kh = tap / kW, kw = tap - kh * kW;
+            const I t = p / oW, ow = p - t * oW, n = t / oH, oh = t - n * oH;
+            const I ih = oh * sH + kh * dH - pH, iw = ow * sW + kw * dW - pW;
             if (ih >= 0 && ih < H && iw >= 0 && iw < W)
                 v = __ldg(reinterpret_cast<const uint4 *>(X + ((n * H + ih) * W + iw) * C) + c16);
         }
@@ -61,26 +103,33 @@ __global__ void __launch_bounds__(kThreads) k_im2col_nhwc16(const uint8_t *__res
     }
 }
 
-// Generic im2col (any C, NHWC or NCHW input): one byte per thread-iteration.
-template <bool NHWC>
-__global__ void __launch_bounds__(kThreads) k_im2col_bytes(const uint8_t *__restrict__ X, int64_t N, int64_t C,
-                                                           int64_t H, int64_t W, int64_t kH, int64_t kW, int64_t oH,
-                                                           int64_t oW, int sH, int sW, int pH, int pW, int dH, int dW,
-                                                           int64_t Kp, uint8_t *__restrict__ A) {
-    const int64_t total = N * oH * oW * Kp;
-    for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
-         i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
-        const int64_t p = i / Kp, k = i % Kp;
-        uint8_t v = 0;
-        if (k < kH * kW * C) {
-            const int64_t tap = k / C, c = k % C;
-            const int64_t kh = tap / kW, kw = tap % kW;
-            const int64_t ow = p % oW, t = p / oW, oh = t % oH, n = t / oH;
-            const int64_t ih = oh * sH + kh * dH - pH, iw = ow * sW + kw * dW - pW;
-            if (ih >= 0 && ih < H && iw >= 0 && iw < W)
-                v = NHWC ? X[((n * H + ih) * W + iw) * C + c] : X[((n * C + c) * H + ih) * W + iw];
+// im2col from NHWC with VW (4 or 8) channels: one 16-byte output vector holds
+// 16 / VW whole taps, each one VW-byte load.
+template <typename I, int VW>
+__global__ void __launch_bounds__(kThreads) k_im2col_narrow(const uint8_t *__restrict__ X, I N, I H, I W, I kH, I kW,
+                                                            I oH, I oW, I sH, I sW, I pH, I pW, I dH, I dW, I Kp,
+                                                            uint8_t *__restrict__ A) {
+    using V = typename std::conditional<VW == 4, uint32_t, uint2>::type;
+    constexpr int TPC = 16 / VW;  // taps per 16-byte chunk
+    const I chunks = Kp / 16, taps = kH * kW;
+    const I total = N * oH * oW * chunks;
+    for (I i = static_cast<I>(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
+         i += static_cast<I>(gridDim.x) * blockDim.x) {
+        const I p = i / chunks, ch = i - p * chunks;
+        const I t = p / oW, ow = p - t * oW, n = t / oH, oh = t - n * oH;
+        V v[TPC];
+#pragma unroll
+        for (int j = 0; j < TPC; ++j) {
+            const I tap = ch * TPC + j;
+            v[j] = V{};
+            if (tap < taps) {
+                const I kh = tap / kW, kw = tap - kh * kW;
+                const I ih = oh * sH + kh * dH - pH, iw = ow * sW + kw * dW - pW;
+                if (ih >= 0 && ih < H && iw >= 0 && iw < W)
+                    v[j] = __ldg(reinterpret_cast<const V *>(X + ((n * H + ih) * W + iw) * VW));
+            }
         }
-        A[i] = v;
+        *reinterpret_cast<uint4 *>(A + static_cast<int64_t>(i) * 16) = *reinterpret_cast<const uint4 *>(v);
     }
 }
 
@@ -103,7 +152,7 @@ int64_t lcml_fp8_conv_packed_k(int64_t Cg, int64_t kH, int64_t kW) { return pack
 int64_t lcml_fp8_conv_workspace_size(const lcml_fp8_conv_desc *d) {
     if (!d) return -1;
     if (direct_path(d)) return 0;
-    return d->N * d->oH * d->oW * packed_k(d->C / (d->group > 0 ? d->group : 1), d->kH, d->kW);
+    return d->N * d->oH * d->oW * packed_k(d->C / (d->group > 0 ? d->group : 1), d->kH, d->kW) + repack_bytes(d);
 }
 
 int lcml_fp8_conv_pack_weight(const uint8_t *W, int64_t M, int64_t Cg, int64_t kH, int64_t kW, uint8_t *Wp,
@@ -111,10 +160,40 @@ int lcml_fp8_conv_pack_weight(const uint8_t *W, int64_t M, int64_t Cg, int64_t k
     LCML_CHECK_ARG(M > 0 && Cg > 0 && kH > 0 && kW > 0, "lcml_fp8_conv_pack_weight: bad extents");
     LCML_CHECK_ARG(W && Wp, "lcml_fp8_conv_pack_weight: null pointer");
     const int64_t Kp = packed_k(Cg, kH, kW);
-    k_pack_weight<<<grid_for(M * Kp), kThreads, 0, to_cuda(stream)>>>(W, M, Cg, kH, kW, Kp, Wp);
+    k_pack_weight<<<grid_for(M * Kp), kThreads, 0, to_cuda(stream)>>>(W, M, Cg, packed_c(Cg), kH, kW, Kp, Wp);
     LCML_LAUNCHED("conv_pack_weight");
     return LCML_OK;
 }
+
+}// extern "C"
+
+namespace {
+template <typename I>
+void launch_im2col(const lcml_fp8_conv_desc *d, const uint8_t *X, int64_t Cp, int64_t Kp, uint8_t *A, cudaStream_t st) {
+    const int64_t P = d->N * d->oH * d->oW;
+    const int grid = grid_for(P * (Kp / 16));
+    if (Cp == 4)
+        k_im2col_narrow<I, 4><<<grid, kThreads, 0, st>>>(X, d->N, d->H, d->W, d->kH, d->kW, d->oH, d->oW, d->sH, d->sW,
+                                                         d->pH, d->pW, d->dH, d->dW, Kp, A);
+    else if (Cp == 8)
+        k_im2col_narrow<I, 8><<<grid, kThreads, 0, st>>>(X, d->N, d->H, d->W, d->kH, d->kW, d->oH, d->oW, d->sH, d->sW,
+                                                         d->pH, d->pW, d->dH, d->dW, Kp, A);
+    else
+        k_im2col_nhwc16<I><<<grid, kThreads, 0, st>>>(X, d->N, Cp, d->H, d->W, d->kH, d->kW, d->oH, d->oW, d->sH, d->sW,
+                                                      d->pH, d->pW, d->dH, d->dW, Kp, A);
+}
+
+template <typename I>
+void launch_repack(const lcml_fp8_conv_desc *d, int64_t Cp, uint8_t *Xc, cudaStream_t st) {
+    const int grid = grid_for(d->N * d->H * d->W);
+    if (d->x_nhwc)
+        k_repack_nhwc<I, true><<<grid, kThreads, 0, st>>>(d->X, d->N, d->C, d->H * d->W, Cp, Xc);
+    else
+        k_repack_nhwc<I, false><<<grid, kThreads, 0, st>>>(d->X, d->N, d->C, d->H * d->W, Cp, Xc);
+}
+}// namespace
+
+extern "C" {
 
 int lcml_fp8_conv(const lcml_fp8_conv_desc *d, lcml_stream_t stream) {
     LCML_CHECK_ARG(d != nullptr, "lcml_fp8_conv: desc is NULL");
@@ -131,27 +210,29 @@ int lcml_fp8_conv(const lcml_fp8_conv_desc *d, lcml_stream_t stream) {
                        (d->residual_dtype == LCML_DTYPE_FLOAT8E4M3FN && d->residual_scale),
                    "lcml_fp8_conv: residual must be FLOAT or FLOAT8E4M3FN with residual_scale");
     const int64_t P = d->N * d->oH * d->oW;
+    const int64_t Cp = packed_c(d->C);
     const int64_t Kp = packed_k(d->C, d->kH, d->kW);
     cudaStream_t st = to_cuda(stream);
     const uint8_t *A = d->X;
     int64_t K = d->C;
     if (!direct_path(d)) {
-        LCML_CHECK_ARG(d->workspace != nullptr, "lcml_fp8_conv: this conv needs a workspace of %lld bytes",
-                       static_cast<long long>(P * Kp));
+        LCML_CHECK_ARG(d->workspace != nullptr && aligned(d->workspace, 256),
+                       "lcml_fp8_conv: this conv needs a 256-byte aligned workspace of %lld bytes",
+                       static_cast<long long>(lcml_fp8_conv_workspace_size(d)));
+        LCML_CHECK_ARG(aligned(d->X, 16) || needs_repack(d), "lcml_fp8_conv: X must be 16-byte aligned");
         uint8_t *ws = static_cast<uint8_t *>(d->workspace);
-        if (d->x_nhwc && d->C % 16 == 0 && aligned(d->X, 16) && aligned(ws, 16)) {
-            k_im2col_nhwc16<<<grid_for(P * (Kp / 16)), kThreads, 0, st>>>(d->X, d->N, d->C, d->H, d->W, d->kH, d->kW,
-                                                                         d->oH, d->oW, d->sH, d->sW, d->pH, d->pW,
-                                                                         d->dH, d->dW, Kp, ws);
-        } else if (d->x_nhwc) {
-            k_im2col_bytes<true><<<grid_for(P * Kp), kThreads, 0, st>>>(d->X, d->N, d->C, d->H, d->W, d->kH, d->kW,
-                                                                       d->oH, d->oW, d->sH, d->sW, d->pH, d->pW,
-                                                                       d->dH, d->dW, Kp, ws);
-        } else {
-            k_im2col_bytes<false><<<grid_for(P * Kp), kThreads, 0, st>>>(d->X, d->N, d->C, d->H, d->W, d->kH, d->kW,
-                                                                        d->oH, d->oW, d->sH, d->sW, d->pH, d->pW,
-                                                                        d->dH, d->dW, Kp, ws);
+        const uint8_t *src = d->X;
+        const bool small = d->N * d->H * d->W * Cp < (int64_t(1) << 31) && P * Kp < (int64_t(1) << 31);
+        if (needs_repack(d)) {
+            uint8_t *xc = ws + P * Kp;  // after the im2col matrix (256-byte aligned below)
+            xc = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(xc) + 255) & ~uintptr_t(255));
+            if (small) launch_repack<int32_t>(d, Cp, xc, st);
+            else launch_repack<int64_t>(d, Cp, xc, st);
+            LCML_LAUNCHED("conv_repack");
+            src = xc;
         }
+        if (small) launch_im2col<int32_t>(d, src, Cp, Kp, ws, st);
+        else launch_im2col<int64_t>(d, src, Cp, Kp, ws, st);
         LCML_LAUNCHED("conv_im2col");
         A = ws;
         K = Kp;

@@ -142,8 +142,10 @@ __global__ void __launch_bounds__(kThreads) k_softmax_rows(const float *__restri
     for (int64_t c = threadIdx.x; c < cols; c += kThreads) y[r * cols + c] = expf(xr[c] - m) / s;
 }
 
-// MaxPool 2-D, begin pads, padded taps skipped. E4M3: max of decoded values,
-// the output byte is the winning input byte (scale > 0 keeps the order).
+// MaxPool 2-D, begin pads, padded taps skipped. E4M3: the code
+// QuantizeLinear gives (at the same positive scale) for the max of the decoded
+// values, i.e. the winning input byte, with -0 written as 0x00; NaN taps lose
+// to everything (a window of NaNs gives the -inf result, saturated to 0xfe).
 template <bool E4M3, bool NHWC>
 __global__ void __launch_bounds__(kThreads) k_maxpool(const void *__restrict__ xv, int64_t NC, int64_t C, int64_t H,
                                                       int64_t W, int kH, int kW, int sH, int sW, int pH, int pW,
@@ -168,8 +170,7 @@ __global__ void __launch_bounds__(kThreads) k_maxpool(const void *__restrict__ x
             p = t / oH;
         }
         float best = -INFINITY;
-        uint8_t best_b = 0;
-        bool found = false;
+        uint8_t best_b = 0xfe;
         for (int kh = 0; kh < kH; ++kh) {
             const int64_t ih = oh * sH + kh - pH;
             if (ih < 0 || ih >= H) continue;
@@ -180,18 +181,69 @@ __global__ void __launch_bounds__(kThreads) k_maxpool(const void *__restrict__ x
                 if (E4M3) {
                     const uint8_t b = reinterpret_cast<const uint8_t *>(xv)[idx];
                     const float v = e4m3_decode(b);
-                    if (!found || v > best) {
+                    if (v > best) {
                         best = v;
                         best_b = b;
-                        found = true;
                     }
                 } else {
                     best = fmaxf(best, reinterpret_cast<const float *>(xv)[idx]);
                 }
             }
         }
-        if (E4M3) reinterpret_cast<uint8_t *>(yv)[o] = best_b;
+        if (E4M3) reinterpret_cast<uint8_t *>(yv)[o] = best_b == 0x80 ? 0 : best_b;
         else reinterpret_cast<float *>(yv)[o] = best;
+    }
+}
+
+// e4m3 codes -> bytes whose unsigned order is the order of the decoded
+// values (4 per word): NaN -> 0, negatives -> 0x7f - |code|, others -> code + 0x80.
+__device__ __forceinline__ uint32_t e4m3_order_key4(uint32_t w) {
+    const uint32_t neg = __vcmpgeu4(w, 0x80808080u);
+    const uint32_t mag = w & 0x7f7f7f7fu;
+    const uint32_t nan = __vcmpeq4(mag, 0x7f7f7f7fu);
+    const uint32_t key = ((0x7f7f7f7fu - mag) & neg) | ((w ^ 0x80808080u) & ~neg);
+    return key & ~nan;
+}
+
+// Inverse of e4m3_order_key4 with the MaxPool conventions: key 0 (only NaN
+// or nothing seen) -> 0xfe, -0 -> 0x00.
+__device__ __forceinline__ uint32_t e4m3_from_order_key4(uint32_t k) {
+    const uint32_t lt = __vcmpltu4(k, 0x80808080u);
+    uint32_t b = (~k & lt) | ((k ^ 0x80808080u) & ~lt);
+    const uint32_t z = __vcmpeq4(k, 0u);
+    b = (b & ~z) | (0xfefefefeu & z);
+    return b & ~__vcmpeq4(b, 0x80808080u);
+}
+
+// e4m3 NHWC MaxPool with C a multiple of 16: one thread per (output pixel,
+// 16 channels), 16-byte loads, per-byte max on the order keys. Same results as
+// k_maxpool<true, true>. I is the index type.
+template <typename I>
+__global__ void __launch_bounds__(kThreads) k_maxpool_e4m3_nhwc16(const uint8_t *__restrict__ x, I N, I C, I H, I W,
+                                                                  int kH, int kW, int sH, int sW, int pH, int pW, I oH,
+                                                                  I oW, uint8_t *__restrict__ y) {
+    const I groups = C / 16;
+    const I total = N * oH * oW * groups;
+    for (I o = static_cast<I>(blockIdx.x) * blockDim.x + threadIdx.x; o < total;
+         o += static_cast<I>(gridDim.x) * blockDim.x) {
+        const I pix = o / groups, g = o - pix * groups;
+        const I t = pix / oW, ow = pix - t * oW, n = t / oH, oh = t - n * oH;
+        uint4 acc = make_uint4(0, 0, 0, 0);
+        for (int kh = 0; kh < kH; ++kh) {
+            const I ih = oh * sH + kh - pH;
+            if (ih < 0 || ih >= H) continue;
+            for (int kw = 0; kw < kW; ++kw) {
+                const I iw = ow * sW + kw - pW;
+                if (iw < 0 || iw >= W) continue;
+                const uint4 v = __ldg(reinterpret_cast<const uint4 *>(x + ((n * H + ih) * W + iw) * C) + g);
+                acc.x = __vmaxu4(acc.x, e4m3_order_key4(v.x));
+                acc.y = __vmaxu4(acc.y, e4m3_order_key4(v.y));
+                acc.z = __vmaxu4(acc.z, e4m3_order_key4(v.z));
+                acc.w = __vmaxu4(acc.w, e4m3_order_key4(v.w));
+            }
+        }
+        reinterpret_cast<uint4 *>(y)[o] = make_uint4(e4m3_from_order_key4(acc.x), e4m3_from_order_key4(acc.y),
+                                                     e4m3_from_order_key4(acc.z), e4m3_from_order_key4(acc.w));
     }
 }
 
@@ -316,7 +368,18 @@ int lcml_maxpool2d(const void *x, int elem_dtype, int64_t NC, int64_t H, int64_t
     const int g = grid_for(total);
     cudaStream_t st = to_cuda(stream);
     const bool e4 = elem_dtype == LCML_DTYPE_FLOAT8E4M3FN;
-    if (e4 && x_nhwc) k_maxpool<true, true><<<g, kThreads, 0, st>>>(x, NC, C, H, W, kH, kW, sH, sW, pH, pW, oH, oW, y);
+    if (e4 && x_nhwc && C % 16 == 0 && aligned(x, 16) && aligned(y, 16)) {
+        const int64_t N = NC / C;
+        const int gv = grid_for(total / 16);
+        if (N * H * W * C < (int64_t(1) << 31))
+            k_maxpool_e4m3_nhwc16<int32_t><<<gv, kThreads, 0, st>>>(
+                static_cast<const uint8_t *>(x), static_cast<int32_t>(N), static_cast<int32_t>(C), static_cast<int32_t>(H),
+                static_cast<int32_t>(W), kH, kW, sH, sW, pH, pW, static_cast<int32_t>(oH), static_cast<int32_t>(oW),
+                static_cast<uint8_t *>(y));
+        else
+            k_maxpool_e4m3_nhwc16<int64_t><<<gv, kThreads, 0, st>>>(static_cast<const uint8_t *>(x), N, C, H, W, kH, kW,
+                                                                    sH, sW, pH, pW, oH, oW, static_cast<uint8_t *>(y));
+    } else if (e4 && x_nhwc) k_maxpool<true, true><<<g, kThreads, 0, st>>>(x, NC, C, H, W, kH, kW, sH, sW, pH, pW, oH, oW, y);
     else if (e4) k_maxpool<true, false><<<g, kThreads, 0, st>>>(x, NC, C, H, W, kH, kW, sH, sW, pH, pW, oH, oW, y);
     else if (x_nhwc) k_maxpool<false, true><<<g, kThreads, 0, st>>>(x, NC, C, H, W, kH, kW, sH, sW, pH, pW, oH, oW, y);
     else k_maxpool<false, false><<<g, kThreads, 0, st>>>(x, NC, C, H, W, kH, kW, sH, sW, pH, pW, oH, oW, y);

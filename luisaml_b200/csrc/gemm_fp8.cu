@@ -31,7 +31,7 @@ namespace gemm {
 constexpr int BM = 128;
 constexpr int BK = 128;     // bytes == e4m3 elements per k-block (one 128-byte swizzle atom)
 constexpr int UMMA_K = 32;  // K per tcgen05.mma for 8-bit inputs
-constexpr int kThreads = 192;
+constexpr int kSmemLimit = 232448;  // dynamic shared memory per CTA on sm_100
 constexpr int GROUP_M = 16; // tile rasterisation band height (in BM tiles)
 
 enum OutType : int { kOutF32 = 0, kOutBF16 = 1, kOutE4M3 = 2 };
@@ -311,7 +311,16 @@ __device__ __forceinline__ void store_chunk_peers(const EpiParams &ep, uint8_t *
 // The row layout matches the output tensor map's swizzle (32B / 64B / 128B
 // for 1 / 2 / 4-byte elements: 16-byte piece p of row r sits at p ^ ((r * RB
 // / 128) mod P)), which also makes the 16-byte shared stores conflict-free.
-constexpr int kStageBytesPerWarp = 2 * 32 * 32 * 4;
+template <int OUT>
+constexpr int stage_bytes_per_warp() { return 2 * 32 * 32 * out_es(OUT); }
+
+// Epilogue warps per CTA: 8 (two per TMEM lane quarter, each taking every
+// other 32-column chunk, so one warp's TMEM and memory latency hides behind
+// the other's math) except for SILU_MUL, whose register footprint allows 4.
+template <int EPI>
+constexpr int epi_warps() { return EPI == LCML_EPI_SILU_MUL ? 4 : 8; }
+template <int EPI>
+constexpr int threads_for() { return 64 + 32 * epi_warps<EPI>(); }
 
 template <int OUT>
 __device__ __forceinline__ void store_chunk_tma(const CUtensorMap *tmY, uint8_t *stage, uint32_t &seq, int64_t row0,
@@ -381,12 +390,14 @@ __device__ __forceinline__ void atomic_max_abs(float *p, float v) {
 
 // One output tile's epilogue for the calling warp: TMEM lanes of rows
 // [row0, row0+32) (lane l = row row0 + l) of the accumulator at `taddr` (BN
-// fp32 columns), gemm column block `tn`. Chunks past the last output column
-// are skipped; a warp whose rows are all past M does nothing. `stage` is the
-// warp's staging area, `seq` its running chunk count (TMA buffer parity).
+// fp32 columns), gemm column block `tn`, 32-column chunks c_first,
+// c_first + c_step, ... Chunks past the last output column are skipped; a
+// warp whose rows are all past M does nothing. `stage` is the warp's staging
+// area, `seq` its running chunk count (TMA buffer parity).
 template <int BN, int EPI, int OUT>
 __device__ __forceinline__ void epilogue_tile(const EpiParams &ep, const CUtensorMap *tmY, uint32_t taddr, int64_t row0,
-                                              int tn, const OutQuant &oq, uint8_t *stage, uint32_t &seq) {
+                                              int tn, const OutQuant &oq, uint8_t *stage, uint32_t &seq, int c_first,
+                                              int c_step) {
     if (row0 >= ep.M) return;
     const int64_t n_out = (EPI == LCML_EPI_SILU_MUL) ? ep.N / 2 : ep.N;
     const int64_t row = row0 + static_cast<int64_t>(threadIdx.x & 31);
@@ -398,7 +409,7 @@ __device__ __forceinline__ void epilogue_tile(const EpiParams &ep, const CUtenso
     float amax = 0.0f;
     constexpr int kChunks = (EPI == LCML_EPI_SILU_MUL) ? BN / 64 : BN / 32;
 #pragma unroll 1
-    for (int c = 0; c < kChunks; ++c) {
+    for (int c = c_first; c < kChunks; c += c_step) {
         // SILU_MUL: BN columns = BN/2 gate columns followed by BN/2 up columns
         const int64_t ng0 = static_cast<int64_t>(tn) * BN + c * 32;
         const int64_t col0 = (EPI == LCML_EPI_SILU_MUL) ? static_cast<int64_t>(tn) * (BN / 2) + c * 32 : ng0;
@@ -443,22 +454,30 @@ __device__ __forceinline__ void tile_coords(int tile, int num_m, int num_n, int 
     tn = in_group / gsize;
 }
 
-template <int BN, int STAGES>
+template <int BN, int STAGES, int EPI, int OUT>
 struct Layout {
     static constexpr int kABytes = BM * BK;
     static constexpr int kBBytes = BN * BK;
     static constexpr int kStageBytes = kABytes + kBBytes;
     static constexpr int kTmemCols = 2 * BN;  // double-buffered fp32 accumulator
     static constexpr int kBarOffset = STAGES * kStageBytes;
-    static constexpr int kEpiOffset = kBarOffset + 1024;     // 4 epilogue warps' output staging
-    static constexpr int kSmemBytes = kEpiOffset + 4 * kStageBytesPerWarp + 1024;  // +1024 for manual alignment
+    static constexpr int kEpiOffset = kBarOffset + 1024;     // epilogue warps' output staging
+    static constexpr int kSmemBytes = kEpiOffset + epi_warps<EPI>() * stage_bytes_per_warp<OUT>() + 1024;  // +1024 alignment
 };
 
+// The deepest operand ring (at most 8 stages) that fits beside the staging.
+template <int BN, int EPI, int OUT>
+constexpr int stages_for() {
+    const int room = kSmemLimit - 2048 - epi_warps<EPI>() * stage_bytes_per_warp<OUT>();
+    const int s = room / (BM * BK + BN * BK);
+    return s > 8 ? 8 : s;
+}
+
 template <int BN, int STAGES, int EPI, int OUT>
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(threads_for<EPI>(), 1)
     k_gemm_fp8_tc(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                   const __grid_constant__ CUtensorMap tmY, int M, int N, int K, EpiParams ep, int *err) {
-    using L = Layout<BN, STAGES>;
+    using L = Layout<BN, STAGES, EPI, OUT>;
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint64_t *full = reinterpret_cast<uint64_t *>(smem + L::kBarOffset);
@@ -481,7 +500,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         for (int b = 0; b < 2; ++b) {
             mbar_init(&tfull[b], 1);
-            mbar_init(&tempty[b], 4);
+            mbar_init(&tempty[b], epi_warps<EPI>());
         }
         fence_mbar_init();
     }
@@ -578,8 +597,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     } else {
         // ---------------- epilogue warps ----------------
         const int quarter = warp & 3;  // TMEM lanes [32*quarter, 32*quarter+32)
+        const int half = (warp - 2) >> 2;  // which interleaved half of the chunks (8 warps)
         const OutQuant oq = make_out_quant<OUT>(ep);
-        uint8_t *stage = smem + L::kEpiOffset + quarter * kStageBytesPerWarp;
+        uint8_t *stage = smem + L::kEpiOffset + (warp - 2) * stage_bytes_per_warp<OUT>();
         uint32_t seq = 0;
         if (ep.tma_store && lane == 0) tma_prefetch_desc(&tmY);
         int acc = 0;
@@ -591,7 +611,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             tc_fence_after();
             const int64_t row0 = static_cast<int64_t>(tm) * BM + quarter * 32;
             const uint32_t taddr = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + static_cast<uint32_t>(acc * BN);
-            epilogue_tile<BN, EPI, OUT>(ep, &tmY, taddr, row0, tn, oq, stage, seq);
+            epilogue_tile<BN, EPI, OUT>(ep, &tmY, taddr, row0, tn, oq, stage, seq, half, epi_warps<EPI>() / 4);
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(&tempty[acc]);
@@ -620,23 +640,28 @@ __global__ void __launch_bounds__(kThreads, 1)
 // both halves and issues the MMAs; commits multicast to both CTAs' barriers;
 // both CTAs run an epilogue over their own 128 TMEM lanes. No TMA multicast.
 // ---------------------------------------------------------------------------
-constexpr int kPairStages = 6;
 
-template <int STAGES>
+template <int STAGES, int EPI, int OUT>
 struct PairLayout {
     static constexpr int kHalfBytes = 128 * BK;           // 16 KB: A half or B half
     static constexpr int kStageBytes = 2 * kHalfBytes;    // per CTA
     static constexpr int kTmemCols = 512;                 // 2 x 256 fp32 accumulators
     static constexpr int kBarOffset = STAGES * kStageBytes;
-    static constexpr int kEpiOffset = kBarOffset + 1024;     // 4 epilogue warps' output staging
-    static constexpr int kSmemBytes = kEpiOffset + 4 * kStageBytesPerWarp + 1024;
+    static constexpr int kEpiOffset = kBarOffset + 1024;     // epilogue warps' output staging
+    static constexpr int kSmemBytes = kEpiOffset + epi_warps<EPI>() * stage_bytes_per_warp<OUT>() + 1024;
 };
 
+template <int EPI, int OUT>
+constexpr int pair_stages_for() {
+    const int s = (kSmemLimit - 2048 - epi_warps<EPI>() * stage_bytes_per_warp<OUT>()) / (2 * 128 * BK);
+    return s > 8 ? 8 : s;
+}
+
 template <int STAGES, int EPI, int OUT>
-__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(threads_for<EPI>(), 1)
     k_gemm_fp8_tc2(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                    const __grid_constant__ CUtensorMap tmY, int M, int N, int K, EpiParams ep, int *err) {
-    using L = PairLayout<STAGES>;
+    using L = PairLayout<STAGES, EPI, OUT>;
     constexpr int BN = 256;
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -663,7 +688,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         }
         for (int b = 0; b < 2; ++b) {
             mbar_init(&tfull[b], 1);
-            mbar_init(&tempty[b], 8);  // 4 epilogue warps in each CTA of the pair
+            mbar_init(&tempty[b], 2 * epi_warps<EPI>());  // the epilogue warps of both CTAs
         }
         fence_mbar_init();
     }
@@ -763,8 +788,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     } else {
         // ---------------- epilogue warps (both CTAs) ----------------
         const int quarter = warp & 3;
+        const int half = (warp - 2) >> 2;
         const OutQuant oq = make_out_quant<OUT>(ep);
-        uint8_t *stage = smem + L::kEpiOffset + quarter * kStageBytesPerWarp;
+        uint8_t *stage = smem + L::kEpiOffset + (warp - 2) * stage_bytes_per_warp<OUT>();
         uint32_t seq = 0;
         if (ep.tma_store && lane == 0) tma_prefetch_desc(&tmY);
         const uint32_t tempty_leader = mapa_shared(smem_u32(&tempty[0]), 0);
@@ -777,7 +803,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
             tc_fence_after();
             const int64_t row0 = static_cast<int64_t>(tm) * 256 + rank * 128 + quarter * 32;
             const uint32_t taddr = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + static_cast<uint32_t>(acc * BN);
-            epilogue_tile<BN, EPI, OUT>(ep, &tmY, taddr, row0, tn, oq, stage, seq);
+            epilogue_tile<BN, EPI, OUT>(ep, &tmY, taddr, row0, tn, oq, stage, seq, half, epi_warps<EPI>() / 4);
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive_cluster(tempty_leader + 8u * static_cast<uint32_t>(acc));
@@ -949,9 +975,11 @@ int output_tmap(const lcml_fp8_gemm_desc *d, const EpiParams &ep, CUtensorMap *t
     return make_tmap_out(ty, static_cast<uint8_t *>(d->Y) + d->y_col_offset * ES, n_out, d->M, d->ldy * ES, ES);
 }
 
-template <int BN, int STAGES, int EPI, int OUT>
+template <int BN, int EPI, int OUT>
 int launch_tc(const lcml_fp8_gemm_desc *d, const EpiParams &ep, cudaStream_t st) {
-    using L = Layout<BN, STAGES>;
+    constexpr int STAGES = stages_for<BN, EPI, OUT>();
+    using L = Layout<BN, STAGES, EPI, OUT>;
+    static_assert(STAGES >= 3 && L::kSmemBytes <= kSmemLimit, "shared memory layout does not fit");
     auto kern = k_gemm_fp8_tc<BN, STAGES, EPI, OUT>;
     static std::once_flag once;
     static cudaError_t attr_err = cudaSuccess;
@@ -971,16 +999,18 @@ int launch_tc(const lcml_fp8_gemm_desc *d, const EpiParams &ep, cudaStream_t st)
     if (rc) return rc;
     const int64_t tiles = ((d->M + BM - 1) / BM) * ((d->N + BN - 1) / BN);
     const int grid = static_cast<int>(tiles < sm_count() ? tiles : sm_count());
-    kern<<<grid, kThreads, L::kSmemBytes, st>>>(ta, tb, ty, static_cast<int>(d->M), static_cast<int>(d->N),
-                                                 static_cast<int>(d->K), ep, device_error_word());
+    kern<<<grid, threads_for<EPI>(), L::kSmemBytes, st>>>(ta, tb, ty, static_cast<int>(d->M), static_cast<int>(d->N),
+                                                          static_cast<int>(d->K), ep, device_error_word());
     LCML_LAUNCHED("gemm_fp8_tc");
     return LCML_OK;
 }
 
 template <int EPI, int OUT>
 int launch_tc2(const lcml_fp8_gemm_desc *d, const EpiParams &ep, cudaStream_t st) {
-    using L = PairLayout<kPairStages>;
-    auto kern = k_gemm_fp8_tc2<kPairStages, EPI, OUT>;
+    constexpr int STAGES = pair_stages_for<EPI, OUT>();
+    using L = PairLayout<STAGES, EPI, OUT>;
+    static_assert(STAGES >= 3 && L::kSmemBytes <= kSmemLimit, "shared memory layout does not fit");
+    auto kern = k_gemm_fp8_tc2<STAGES, EPI, OUT>;
     static std::once_flag once;
     static cudaError_t attr_err = cudaSuccess;
     std::call_once(once, [&] {
@@ -1000,8 +1030,8 @@ int launch_tc2(const lcml_fp8_gemm_desc *d, const EpiParams &ep, cudaStream_t st
     const int64_t tiles = ((d->M + 255) / 256) * ((d->N + 255) / 256);
     const int64_t pairs = sm_count() / 2;
     const int grid = static_cast<int>(2 * (tiles < pairs ? tiles : pairs));
-    kern<<<grid, kThreads, L::kSmemBytes, st>>>(ta, tb, ty, static_cast<int>(d->M), static_cast<int>(d->N),
-                                                 static_cast<int>(d->K), ep, device_error_word());
+    kern<<<grid, threads_for<EPI>(), L::kSmemBytes, st>>>(ta, tb, ty, static_cast<int>(d->M), static_cast<int>(d->N),
+                                                          static_cast<int>(d->K), ep, device_error_word());
     LCML_LAUNCHED("gemm_fp8_tc2");
     return LCML_OK;
 }
@@ -1028,9 +1058,9 @@ int dispatch(const lcml_fp8_gemm_desc *d, const EpiParams &ep, cudaStream_t st, 
     const int64_t pair_tiles = ((d->M + 255) / 256) * ((d->N + 255) / 256);
     const bool pair = d->M >= 256 && d->N >= 256 && d->K >= 1024 && pair_tiles >= sm_count();
     if ((g_gemm_mode & 3) != 1 && ((g_gemm_mode & 3) == 2 || pair)) return launch_tc2<EPI, OUT>(d, ep, st);
-    if (EPI == LCML_EPI_SILU_MUL || d->N >= 2048) return launch_tc<256, 4, EPI, OUT>(d, ep, st);
-    if (EPI != LCML_EPI_SILU_MUL && d->N <= 64) return launch_tc<64, 8, EPI, OUT>(d, ep, st);
-    return launch_tc<128, 6, EPI, OUT>(d, ep, st);
+    if (EPI == LCML_EPI_SILU_MUL || d->N >= 2048) return launch_tc<256, EPI, OUT>(d, ep, st);
+    if (EPI != LCML_EPI_SILU_MUL && d->N <= 64) return launch_tc<64, EPI, OUT>(d, ep, st);
+    return launch_tc<128, EPI, OUT>(d, ep, st);
 }
 
 template <int EPI>

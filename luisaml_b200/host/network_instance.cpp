@@ -8,7 +8,10 @@
 //      `raw_data` initializers are uploaded once and keep a host copy
 //   3. fusion pass: DequantizeLinear -> Gemm/MatMul -> (Relu) -> (Cast | QuantizeLinear)
 //      node groups become one FusedQdqGemm (scales, bias, activation and output
-//      cast in the GEMM epilogue, so no dequantized operand ever reaches HBM)
+//      cast in the GEMM epilogue, so no dequantized operand ever reaches HBM);
+//      DequantizeLinear -> Conv -> (Add residual) -> (Relu) -> QuantizeLinear
+//      becomes one FusedQdqConv with an NHWC e4m3 output; QDQ MaxPool and
+//      GlobalAveragePool read e4m3 directly; nodes left without readers drop out
 //   4. allocate the intermediates the remaining nodes touch; view ops alias
 // forward: every non-folded node runs in graph order on the instance's stream
 // (the reference runs them in schedule order inside one generated shader).
@@ -86,6 +89,7 @@ void NetworkInstance::reset() {
     ops_.clear();
     fusion_.clear();
     table_.clear();
+    nhwc_.clear();
 }
 
 const FusionInfo *NetworkInstance::fusion_info(size_t i) const { return i < fusion_.size() ? fusion_[i].get() : nullptr; }
@@ -206,8 +210,6 @@ void NetworkInstance::run_fusion_pass() {
         return static_cast<int64_t>(n);
     };
 
-    std::set<int> fused_gemms;
-    std::vector<std::pair<int, int>> dq_uses;  // (dq node, gemm node)
     auto host_floats = [&](const Variable &v) -> std::vector<float> {
         std::vector<float> out;
         if (!table_.contains(v.get_name())) return out;
@@ -307,11 +309,6 @@ void NetworkInstance::run_fusion_pass() {
                 fusion_[f]->skip = true;
                 fusion_[f]->note = "folded into the gate/up GEMM at " + m2.get_name();
             }
-            fused_gemms.insert(gg);
-            fused_gemms.insert(gu);
-            dq_uses.emplace_back(da, gg);
-            dq_uses.emplace_back(dg, gg);
-            dq_uses.emplace_back(du, gu);
             break;
         }
     }
@@ -452,22 +449,252 @@ void NetworkInstance::run_fusion_pass() {
             fusion_[f]->skip = true;
             fusion_[f]->note = "folded into " + gn.get_op_type() + " " + gn.get_name();
         }
-        fused_gemms.insert(static_cast<int>(gi));
-        dq_uses.emplace_back(da, static_cast<int>(gi));
-        dq_uses.emplace_back(db, static_cast<int>(gi));
     }
-    // a DequantizeLinear whose every consumer is a fused GEMM never runs
-    std::set<int> dqs;
-    for (auto &u : dq_uses) dqs.insert(u.first);
-    for (int d : dqs) {
-        const std::string &o = nodes[d].get_outputs()[0]->get_name();
-        if (graph_outputs.count(o)) continue;
-        bool all = true;
-        for (int cidx : consumers[o])
-            if (!fused_gemms.count(cidx)) all = false;
-        if (all) {
-            fusion_[d]->skip = true;
-            fusion_[d]->note = "operand read as e4m3 by the fused GEMM";
+    // ---- Convolutional part, in graph order (a tensor's layout is known once its
+    // producer has been visited): fused QDQ Conv, e4m3 MaxPool, e4m3 GlobalAveragePool.
+    // Their e4m3 outputs are stored NHWC, the implicit GEMM's row-major output.
+    std::set<std::string> nhwc;
+    std::vector<FusedQdqConv *> convs;
+    int64_t conv_ws = 0;
+    auto scalar_of = [&](const Variable &v, float &val) {
+        const std::vector<float> f = host_floats(v);
+        if (f.size() != 1) return false;
+        val = f[0];
+        return true;
+    };
+    // QuantizeLinear to e4m3 with a constant per-tensor scale and no zero point
+    auto static_q = [&](int qi) {
+        if (qi < 0 || nodes[qi].get_op_type() != "QuantizeLinear") return false;
+        const Node &qn = nodes[qi];
+        float s;
+        if (!scalar_of(*qn.get_inputs()[1], s) || qn.get_outputs()[0]->get_dtype() != DataType::FLOAT8E4M3FN) return false;
+        if (qn.get_inputs().size() > 2) {
+            if (!qn.get_inputs()[2]->is_constant()) return false;
+            for (char ch : qn.get_inputs()[2]->get_raw_data())
+                if (ch != 0) return false;
+        }
+        return true;
+    };
+    auto ints_or = [&](const Node &n, const char *name, std::vector<int64_t> dflt) {
+        if (auto p = n.try_get_attr(name)) return p->get<AttributeType::INTS>();
+        return dflt;
+    };
+    auto auto_pad_ok = [&](const Node &n) {
+        if (auto p = n.try_get_attr("auto_pad")) {
+            const std::string s = p->get<AttributeType::STRING>();
+            return s.empty() || s == "NOTSET";
+        }
+        return true;
+    };
+    for (size_t ci = 0; ci < nodes.size(); ++ci) {
+        const Node &cn = nodes[ci];
+        if (fusion_[ci]->skip || fusion_[ci]->op) continue;
+        const std::string &kind = cn.get_op_type();
+        if (kind == "Conv") {
+            if (cn.get_inputs().size() < 2 || attr_int(cn, "group", 1) != 1 || !auto_pad_ok(cn)) continue;
+            const int dx = producer_of(cn.get_inputs()[0]->get_name());
+            const int dw = producer_of(cn.get_inputs()[1]->get_name());
+            if (!dq_ok(dx) || !dq_ok(dw) || dq_scale_len(dx) != 1) continue;
+            const Variable &xq = *nodes[dx].get_inputs()[0], &wq = *nodes[dw].get_inputs()[0];
+            const Variable &yv = *cn.get_outputs()[0];
+            if (!wq.is_constant() || !table_.contains(wq.get_name()) || wq.get_shape().size() != 4 ||
+                xq.get_shape().size() != 4 || yv.get_shape().size() != 4)
+                continue;
+            const int64_t M = static_cast<int64_t>(wq.get_shape()[0]), C = static_cast<int64_t>(wq.get_shape()[1]);
+            const int64_t lw = dq_scale_len(dw);
+            if (lw != 1 && (lw != M || attr_int(nodes[dw], "axis", 1) != 0)) continue;
+            if (static_cast<int64_t>(xq.get_shape()[1]) != C) continue;
+            const auto ks = ints_or(cn, "kernel_shape", {static_cast<int64_t>(wq.get_shape()[2]), static_cast<int64_t>(wq.get_shape()[3])});
+            const auto st = ints_or(cn, "strides", {1, 1});
+            const auto pd = ints_or(cn, "pads", {0, 0, 0, 0});
+            const auto dl = ints_or(cn, "dilations", {1, 1});
+            if (ks.size() != 2 || st.size() != 2 || pd.size() != 4 || dl.size() != 2) continue;
+            if (ks[0] != static_cast<int64_t>(wq.get_shape()[2]) || ks[1] != static_cast<int64_t>(wq.get_shape()[3])) continue;
+            std::vector<int> folded;
+            auto op = std::make_unique<FusedQdqConv>();
+            auto &fi = *fusion_[ci];
+            fi.inputs = {xq.get_name(), nodes[dx].get_inputs()[1]->get_name(), "", nodes[dw].get_inputs()[1]->get_name()};
+            if (cn.get_inputs().size() > 2) {
+                const Variable &bv = *cn.get_inputs()[2];
+                if (!bv.is_constant() || bv.get_dtype() != DataType::FLOAT || !table_.contains(bv.get_name())) continue;
+                op->has_bias = true;
+                fi.inputs.push_back(bv.get_name());
+            }
+            // epilogue chain: (Add of a DequantizeLinear'd NHWC e4m3 residual) (Relu) QuantizeLinear
+            std::string out = yv.get_name();
+            int c = sole_consumer(out);
+            int epi = LCML_EPI_NONE;
+            if (c >= 0 && nodes[c].get_op_type() == "Add" && nodes[c].get_inputs().size() == 2) {
+                const Node &an = nodes[c];
+                const Variable *other = an.get_inputs()[0]->get_name() == out ? an.get_inputs()[1] : an.get_inputs()[0];
+                const int dr = producer_of(other->get_name());
+                if (dq_ok(dr) && dq_scale_len(dr) == 1 && nhwc.count(nodes[dr].get_inputs()[0]->get_name()) &&
+                    nodes[dr].get_inputs()[0]->get_shape() == yv.get_shape() && an.get_outputs()[0]->get_shape() == yv.get_shape()) {
+                    op->has_residual = true;
+                    fi.inputs.push_back(nodes[dr].get_inputs()[0]->get_name());
+                    fi.inputs.push_back(nodes[dr].get_inputs()[1]->get_name());
+                    folded.push_back(c);
+                    out = an.get_outputs()[0]->get_name();
+                    c = sole_consumer(out);
+                }
+            }
+            if (c >= 0 && nodes[c].get_op_type() == "Relu") {
+                epi = LCML_EPI_RELU;
+                folded.push_back(c);
+                out = nodes[c].get_outputs()[0]->get_name();
+                c = sole_consumer(out);
+            }
+            if (!static_q(c)) {
+                fi.inputs.clear();
+                continue;  // the output must be requantized to stay on the e4m3 path
+            }
+            folded.push_back(c);
+            fi.inputs.push_back(nodes[c].get_inputs()[1]->get_name());
+            out = nodes[c].get_outputs()[0]->get_name();
+            lcml_fp8_conv_desc &d = op->desc;
+            d.N = static_cast<int64_t>(xq.get_shape()[0]);
+            d.C = C;
+            d.H = static_cast<int64_t>(xq.get_shape()[2]);
+            d.W = static_cast<int64_t>(xq.get_shape()[3]);
+            d.M = M;
+            d.kH = ks[0];
+            d.kW = ks[1];
+            d.oH = static_cast<int64_t>(yv.get_shape()[2]);
+            d.oW = static_cast<int64_t>(yv.get_shape()[3]);
+            d.sH = static_cast<int>(st[0]);
+            d.sW = static_cast<int>(st[1]);
+            d.pH = static_cast<int>(pd[0]);
+            d.pW = static_cast<int>(pd[1]);
+            d.dH = static_cast<int>(dl[0]);
+            d.dW = static_cast<int>(dl[1]);
+            d.group = 1;
+            d.x_nhwc = nhwc.count(xq.get_name()) ? 1 : 0;
+            d.epilogue = epi;
+            // the output extent of the graph must be what these pads and strides give
+            if (d.oH != (d.H + pd[0] + pd[2] - d.dH * (d.kH - 1) - 1) / d.sH + 1 ||
+                d.oW != (d.W + pd[1] + pd[3] - d.dW * (d.kW - 1) - 1) / d.sW + 1) {
+                fi.inputs.clear();
+                continue;
+            }
+            // weights packed once into the GEMM's K-major [M, Kp] layout
+            const int64_t Kp = lcml_fp8_conv_packed_k(C, d.kH, d.kW);
+            auto wp = DeviceTensor::allocate(DataType::FLOAT8E4M3FN, {M, Kp});
+            check_status(lcml_fp8_conv_pack_weight(table_.at(wq.get_name()).ptr<uint8_t>(), M, C, d.kH, d.kW,
+                                                   wp->ptr<uint8_t>(), stream_),
+                         "pack conv weight");
+            wp->set_constant({});
+            const std::string wname = wq.get_name() + "#packed";
+            if (!table_.contains(wname)) table_.own(wname, std::move(wp));
+            fi.inputs[2] = wname;
+            conv_ws = std::max<int64_t>(conv_ws, lcml_fp8_conv_workspace_size(&d));
+            std::string note = "DequantizeLinear x2 + Conv";
+            for (int f : folded) note += " + " + nodes[f].get_op_type();
+            fi.note = note + " fused into one implicit-GEMM conv";
+            fi.outputs = {out};
+            convs.push_back(op.get());
+            fi.op = std::move(op);
+            for (int f : folded) {
+                fusion_[f]->skip = true;
+                fusion_[f]->note = "folded into Conv " + cn.get_name();
+            }
+            nhwc.insert(out);
+        } else if (kind == "MaxPool") {
+            const int dx = producer_of(cn.get_inputs()[0]->get_name());
+            const int q = sole_consumer(cn.get_outputs()[0]->get_name());
+            if (!dq_ok(dx) || dq_scale_len(dx) != 1 || !static_q(q) || !auto_pad_ok(cn)) continue;
+            float s_in, s_out;
+            if (!scalar_of(*nodes[dx].get_inputs()[1], s_in) || !scalar_of(*nodes[q].get_inputs()[1], s_out) ||
+                s_in != s_out || !(s_in > 0.0f))
+                continue;  // same positive scale: the max commutes with the encoding
+            const auto ks = ints_or(cn, "kernel_shape", {});
+            const auto st = ints_or(cn, "strides", {1, 1});
+            const auto pd = ints_or(cn, "pads", {0, 0, 0, 0});
+            const auto dl = ints_or(cn, "dilations", {1, 1});
+            if (ks.size() != 2 || st.size() != 2 || pd.size() != 4 || dl != std::vector<int64_t>{1, 1} ||
+                attr_int(cn, "ceil_mode", 0) != 0 || cn.get_outputs().size() != 1)
+                continue;
+            const Variable &xq = *nodes[dx].get_inputs()[0];
+            auto op = std::make_unique<QdqMaxPool>();
+            op->kH = static_cast<int>(ks[0]);
+            op->kW = static_cast<int>(ks[1]);
+            op->sH = static_cast<int>(st[0]);
+            op->sW = static_cast<int>(st[1]);
+            op->pH = static_cast<int>(pd[0]);
+            op->pW = static_cast<int>(pd[1]);
+            op->nhwc = nhwc.count(xq.get_name()) > 0;
+            auto &fi = *fusion_[ci];
+            fi.inputs = {xq.get_name()};
+            fi.outputs = {nodes[q].get_outputs()[0]->get_name()};
+            fi.note = "DequantizeLinear + MaxPool + QuantizeLinear (same scale) run as one e4m3 max pool";
+            if (op->nhwc) nhwc.insert(fi.outputs[0]);
+            fi.op = std::move(op);
+            fusion_[q]->skip = true;
+            fusion_[q]->note = "folded into MaxPool " + cn.get_name();
+        } else if (kind == "GlobalAveragePool") {
+            const int dx = producer_of(cn.get_inputs()[0]->get_name());
+            if (!dq_ok(dx) || dq_scale_len(dx) != 1 || cn.get_outputs()[0]->get_dtype() != DataType::FLOAT) continue;
+            const Variable &xq = *nodes[dx].get_inputs()[0];
+            auto op = std::make_unique<QdqGlobalAveragePool>();
+            op->nhwc = nhwc.count(xq.get_name()) > 0;
+            auto &fi = *fusion_[ci];
+            fi.inputs = {xq.get_name(), nodes[dx].get_inputs()[1]->get_name()};
+            fi.outputs = {cn.get_outputs()[0]->get_name()};
+            fi.note = "DequantizeLinear + GlobalAveragePool read the e4m3 tensor directly";
+            fi.op = std::move(op);  // [N, C, 1, 1] is the same in both layouts
+        }
+    }
+    if (!convs.empty() && conv_ws > 0) {
+        auto ws = DeviceTensor::allocate(DataType::UINT8, {conv_ws});
+        for (auto *c : convs) c->workspace = ws->data();
+        table_.own("#conv_workspace", std::move(ws));
+    }
+
+    // ---- Dead nodes: a node that still runs but whose outputs nobody reads any more
+    // (a DequantizeLinear whose consumers all read its e4m3 input inside a fusion) is dropped.
+    auto effective_inputs = [&](size_t i) {
+        std::vector<std::string> v = fusion_[i]->inputs;
+        if (v.empty())
+            for (const auto *x : nodes[i].get_inputs()) v.push_back(x->get_name());
+        return v;
+    };
+    auto effective_outputs = [&](size_t i) {
+        std::vector<std::string> v = fusion_[i]->outputs;
+        if (v.empty())
+            for (const auto *x : nodes[i].get_outputs()) v.push_back(x->get_name());
+        return v;
+    };
+    for (bool changed = true; changed;) {
+        changed = false;
+        std::set<std::string> live(graph_outputs.begin(), graph_outputs.end());
+        for (size_t i = 0; i < nodes.size(); ++i)
+            if (!fusion_[i]->skip)
+                for (const auto &n : effective_inputs(i)) live.insert(n);
+        for (size_t i = 0; i < nodes.size(); ++i) {
+            if (fusion_[i]->skip) continue;
+            bool used = false;
+            for (const auto &n : effective_outputs(i)) used |= live.count(n) > 0;
+            if (!used) {
+                fusion_[i]->skip = true;
+                fusion_[i]->note = "its output is only read inside fusions";
+                changed = true;
+            }
+        }
+    }
+
+    // every reader of an NHWC tensor must be one of the layout-aware fused kernels
+    nhwc_.insert(nhwc.begin(), nhwc.end());
+    for (const auto &name : nhwc) {
+        if (graph_outputs.count(name)) throw Error("tensor '" + name + "' is stored NHWC but is a graph output");
+        for (size_t i = 0; i < nodes.size(); ++i) {
+            if (fusion_[i]->skip) continue;
+            const auto ins = effective_inputs(i);
+            if (std::find(ins.begin(), ins.end(), name) == ins.end()) continue;
+            const Operator *o = fusion_[i]->op.get();
+            const bool aware = dynamic_cast<const FusedQdqConv *>(o) || dynamic_cast<const QdqMaxPool *>(o) ||
+                               dynamic_cast<const QdqGlobalAveragePool *>(o);
+            if (!aware)
+                throw Error("NHWC tensor '" + name + "' reaches " + nodes[i].get_op_type() + " " + nodes[i].get_name() +
+                            ", which cannot read that layout");
         }
     }
 }
@@ -507,6 +734,7 @@ void NetworkInstance::prepare() {
     ops_.clear();
     fusion_.clear();
     table_.clear();
+    nhwc_.clear();
     for (const auto &n : nodes) {
         ops_.push_back(model_.get_opset().create_operator(n.get_op_type(), n));
         fusion_.push_back(std::make_unique<FusionInfo>());

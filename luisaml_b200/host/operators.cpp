@@ -387,6 +387,53 @@ void DynamicRowQuant::forward(Span in, Span out) {
                  "dynamic row quantization");
 }
 
+void FusedQdqConv::forward(Span in, Span out) {
+    size_t i = 0;
+    const ITensor &x = in[i++].get(), &sx = in[i++].get(), &wp = in[i++].get(), &sw = in[i++].get();
+    ITensor &y = out[0].get();
+    require(x.dtype() == DataType::FLOAT8E4M3FN && wp.dtype() == DataType::FLOAT8E4M3FN, "fused Conv: e4m3 operands");
+    require(y.dtype() == DataType::FLOAT8E4M3FN, "fused Conv: e4m3 output");
+    lcml_fp8_conv_desc d = desc;
+    d.X = x.ptr<uint8_t>();
+    d.scale_x = sx.ptr<float>();
+    d.Wp = wp.ptr<uint8_t>();
+    d.scale_w = sw.ptr<float>();
+    d.scale_w_mode = sw.size() > 1 ? LCML_SCALE_AXIS : LCML_SCALE_TENSOR;
+    if (has_bias) d.bias = in[i++].get().ptr<float>();
+    if (has_residual) {
+        const ITensor &r = in[i++].get(), &rs = in[i++].get();
+        require(r.dtype() == DataType::FLOAT8E4M3FN && r.size() == y.size(), "fused Conv: residual shape");
+        d.residual = r.data();
+        d.residual_dtype = LCML_DTYPE_FLOAT8E4M3FN;
+        d.residual_scale = rs.ptr<float>();
+    }
+    d.y_scale = in[i++].get().ptr<float>();
+    d.Y = y.data();
+    d.y_dtype = LCML_DTYPE_FLOAT8E4M3FN;
+    d.workspace = workspace;
+    check_status(lcml_fp8_conv(&d, stream_), "fused Conv");
+}
+
+void QdqMaxPool::forward(Span in, Span out) {
+    const ITensor &x = in[0].get();
+    ITensor &y = out[0].get();
+    require(x.ndim() == 4 && x.dtype() == DataType::FLOAT8E4M3FN && y.dtype() == DataType::FLOAT8E4M3FN,
+            "e4m3 MaxPool: 4-D e4m3 input and output");
+    check_status(lcml_maxpool2d(x.data(), LCML_DTYPE_FLOAT8E4M3FN, x.shape(0) * x.shape(1), x.shape(2), x.shape(3), kH, kW,
+                                sH, sW, pH, pW, y.shape(2), y.shape(3), y.data(), nhwc ? 1 : 0, x.shape(1), stream_),
+                 "e4m3 MaxPool");
+}
+
+void QdqGlobalAveragePool::forward(Span in, Span out) {
+    const ITensor &x = in[0].get(), &sx = in[1].get();
+    ITensor &y = out[0].get();
+    require(x.ndim() == 4 && x.dtype() == DataType::FLOAT8E4M3FN && y.dtype() == DataType::FLOAT,
+            "e4m3 GlobalAveragePool: 4-D e4m3 input, FLOAT output");
+    check_status(lcml_global_avgpool(x.data(), LCML_DTYPE_FLOAT8E4M3FN, sx.ptr<float>(), x.shape(0), x.shape(1),
+                                     x.shape(2) * x.shape(3), nhwc ? 1 : 0, y.ptr<float>(), stream_),
+                 "e4m3 GlobalAveragePool");
+}
+
 // ------------------------------------------------------------------ registration
 REGISTER_TO_DEFAULT_OPSET(QuantizeLinear) { return std::make_unique<QuantizeLinear>(get_int(node, "axis", 1)); };
 REGISTER_TO_DEFAULT_OPSET(DequantizeLinear) { return std::make_unique<DequantizeLinear>(get_int(node, "axis", 1)); };

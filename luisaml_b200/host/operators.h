@@ -44,4 +44,45 @@ public:
     void forward(std::span<std::reference_wrapper<ITensor>> in, std::span<std::reference_wrapper<ITensor>> out) override;
 };
 
+// One fused QDQ convolution group (built by the fusion pass, not registered):
+// DequantizeLinear(x) / DequantizeLinear(W) -> Conv (+bias) -> (Add with a
+// DequantizeLinear'd residual) -> (Relu) -> QuantizeLinear, as one implicit-
+// GEMM kernel chain (lcml_fp8_conv):
+//   inputs  [x e4m3 (NCHW or NHWC), s_x [1], W packed e4m3 [M, Kp], s_w (1|M),
+//            (bias fp32 [M]), (residual e4m3 NHWC, s_r [1]), y_scale [1]]
+//   output  y e4m3 NHWC [N, oH, oW, M] (shape() keeps the ONNX NCHW shape)
+class FusedQdqConv : public StreamOperator {
+public:
+    lcml_fp8_conv_desc desc{};  // geometry and epilogue; pointers are bound per forward
+    bool has_bias = false, has_residual = false;
+    void *workspace = nullptr;  // shared by every fused conv of the instance
+
+    FusedQdqConv() : StreamOperator("FusedQdqConv") {}
+    void forward(std::span<std::reference_wrapper<ITensor>> in, std::span<std::reference_wrapper<ITensor>> out) override;
+};
+
+// DequantizeLinear -> MaxPool -> QuantizeLinear with the same per-tensor scale
+// on both sides: the max commutes with the monotonic encoding, so the pool
+// runs on the e4m3 codes directly.
+//   inputs [x e4m3 (NCHW or NHWC)]  outputs [y e4m3, same layout]
+class QdqMaxPool : public StreamOperator {
+public:
+    int kH = 1, kW = 1, sH = 1, sW = 1, pH = 0, pW = 0;
+    bool nhwc = false;
+
+    QdqMaxPool() : StreamOperator("QdqMaxPool") {}
+    void forward(std::span<std::reference_wrapper<ITensor>> in, std::span<std::reference_wrapper<ITensor>> out) override;
+};
+
+// DequantizeLinear -> GlobalAveragePool: the mean of the decoded codes times
+// the scale, read straight from the e4m3 tensor.
+//   inputs [x e4m3 (NCHW or NHWC), s_x [1]]  outputs [y fp32 [N, C, 1, 1]]
+class QdqGlobalAveragePool : public StreamOperator {
+public:
+    bool nhwc = false;
+
+    QdqGlobalAveragePool() : StreamOperator("QdqGlobalAveragePool") {}
+    void forward(std::span<std::reference_wrapper<ITensor>> in, std::span<std::reference_wrapper<ITensor>> out) override;
+};
+
 }// namespace lcml::onnx

@@ -114,6 +114,23 @@ int lcml_network_executed_nodes(const lcml_network *net, int64_t *executed) {
     return LCML_OK;
 }
 
+int lcml_network_tensor(const lcml_network *net, const char *name, void **device_ptr, int *dtype, int64_t *shape,
+                        int max_ndim, int *ndim, int *nhwc) {
+    if (!net || !name || !device_ptr || !dtype || !ndim || (max_ndim > 0 && !shape))
+        return fail(LCML_ERR_INVALID_ARGUMENT, "lcml_network_tensor: null argument");
+    auto &inst = const_cast<NetworkInstance &>(net->inst);
+    if (!inst.tensor_table().contains(name))
+        return fail(LCML_ERR_INVALID_ARGUMENT, std::string("lcml_network_tensor: no tensor '") + name +
+                                                   "' (not prepared yet, or not materialized by the fused graph)");
+    ITensor &t = inst.tensor_table().at(name);
+    *device_ptr = t.data();
+    *dtype = static_cast<int>(t.dtype());
+    *ndim = static_cast<int>(t.ndim());
+    for (int i = 0; i < max_ndim && i < *ndim; ++i) shape[i] = t.shape(i);
+    if (nhwc) *nhwc = inst.is_nhwc(name) ? 1 : 0;
+    return LCML_OK;
+}
+
 int lcml_network_summary(const lcml_network *net, char *buf, size_t len) {
     if (!net || !buf || len == 0) return fail(LCML_ERR_INVALID_ARGUMENT, "null argument");
     std::string s;

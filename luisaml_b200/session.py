@@ -34,6 +34,8 @@ def load():
     lib.lcml_network_forward.argtypes = [_vp]
     lib.lcml_network_executed_nodes.argtypes = [_vp, ctypes.POINTER(_i64)]
     lib.lcml_network_summary.argtypes = [_vp, ctypes.c_char_p, _sz]
+    lib.lcml_network_tensor.argtypes = [_vp, ctypes.c_char_p, ctypes.POINTER(_vp), ctypes.POINTER(_ci),
+                                        ctypes.POINTER(_i64), _ci, ctypes.POINTER(_ci), ctypes.POINTER(_ci)]
     lib.lcml_opset_size.argtypes = []
     _lib = lib
     return lib
@@ -105,3 +107,29 @@ class Network:
         buf = ctypes.create_string_buffer(1 << 16)
         _check(load().lcml_network_summary(self._h, buf, len(buf)))
         return buf.value.decode()
+
+    def tensor_info(self, name: str):
+        """(device pointer, ONNX dtype code, ONNX shape, stored NHWC) of any
+        tensor of the prepared graph."""
+        ptr, dt, nd, nh = _vp(), _ci(), _ci(), _ci()
+        shape = (_i64 * 8)()
+        _check(load().lcml_network_tensor(self._h, name.encode(), ctypes.byref(ptr), ctypes.byref(dt), shape, 8,
+                                          ctypes.byref(nd), ctypes.byref(nh)))
+        return ptr.value, dt.value, tuple(shape[i] for i in range(nd.value)), bool(nh.value)
+
+    def read_tensor(self, name: str):
+        """Host copy of a tensor after forward(), as a numpy array in storage
+        order (NHWC tensors come back as N, H, W, C); fp32 as float32, bf16 as
+        uint16 bit patterns, e4m3 as uint8 codes."""
+        import numpy as np
+        from . import check, lib as fp8_lib
+        ptr, dt, shape, nhwc = self.tensor_info(name)
+        npdt = {1: np.float32, 16: np.uint16, 17: np.uint8, 2: np.uint8, 7: np.int64, 6: np.int32}[dt]
+        if nhwc and len(shape) == 4:
+            shape = (shape[0], shape[2], shape[3], shape[1])
+        out = np.empty(shape, dtype=npdt)
+        if out.nbytes:
+            lib = fp8_lib()
+            check(lib.lcml_memcpy_async(out.ctypes.data, ptr, out.nbytes, 2, None))
+            check(lib.lcml_stream_synchronize(None))
+        return out

@@ -285,3 +285,47 @@ def global_avgpool(x):
     y = np.empty((N, C, 1, 1), dtype=np.float32)
     lib.orc_global_avgpool(_f(x), _f(y), _i64(N * C), _i64(H * W))
     return y
+
+
+def replay_plan(plan, x):
+    """Runs a QDQ convolutional network given as a list of steps (the order the
+    reference's NetworkInstance executes the graph's nodes,
+    src/onnx/network_instance.cpp:584-655), each through the restated operator:
+      ("qdq", s)                 QuantizeLinear + DequantizeLinear, per-tensor scale
+      ("conv", wq, ws, b, st, p) Conv on DequantizeLinear(wq, ws per output channel)
+      ("relu",) ("maxpool",) (3x3 / 2 / pad 1) ("gap",) ("add",)
+      ("fc", wq, ws, b)          Gemm(transB=1) on the dequantized weight
+      ("block_begin",) / ("downsample_begin",) / ("downsample_end",)
+                                 residual bookkeeping of a bottleneck block: the
+                                 block input is kept, a projection branch runs
+                                 from it first, and its output becomes the
+                                 residual the later ("add",) uses.
+    """
+    h, blk_in, res = x, None, None
+    for step in plan:
+        kind = step[0]
+        if kind == "qdq":
+            h = dequantize(quantize(h, step[1]), step[1])
+        elif kind == "conv":
+            _, wq, ws, bias, stride, pad = step
+            h = conv2d(h, dequantize(wq, ws, axis=0), bias, strides=(stride, stride), pads=(pad, pad, pad, pad))
+        elif kind == "relu":
+            h = relu(h)
+        elif kind == "maxpool":
+            h = maxpool2d(h, (3, 3), (2, 2), (1, 1, 1, 1))
+        elif kind == "block_begin":
+            blk_in = res = h
+        elif kind == "downsample_begin":
+            h = blk_in
+        elif kind == "downsample_end":
+            res, h = h, blk_in
+        elif kind == "add":
+            h = (h + res).astype(np.float32)
+        elif kind == "gap":
+            h = global_avgpool(h).reshape(h.shape[0], h.shape[1])
+        elif kind == "fc":
+            _, wq, ws, bias = step
+            h = gemm(h, dequantize(wq, ws, axis=0), bias, transB=1)
+        else:
+            raise ValueError(f"unknown step {kind}")
+    return h

@@ -97,6 +97,9 @@ CASES = [
     ("3x3_s2", 2, 128, 56, 128, 3, 2, 1, True),
     ("1x1_s2_downsample", 2, 256, 56, 512, 1, 2, 0, True),
     ("3x3_7x7map", 4, 512, 7, 512, 3, 1, 1, True),
+    ("nchw_c8_3x3", 2, 8, 20, 32, 3, 1, 1, False),       # 8-channel taps after the NHWC repack
+    ("nhwc_c24_3x3_s2", 2, 24, 19, 48, 3, 2, 1, True),  # C padded to 32
+    ("nchw_c32_5x5", 1, 32, 17, 16, 5, 1, 2, False),     # NCHW with 16-byte taps
 ]
 
 

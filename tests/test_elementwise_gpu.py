@@ -118,3 +118,31 @@ def test_cast_roundtrip(dev):
     f = torch.empty_like(xt)
     lb.check(lb.lib().lcml_cast(_p(b), 16, _p(f), 1, 1003, _s()))
     assert torch.equal(f, b.float())
+
+
+@pytest.mark.parametrize("layout,C", [("nhwc", 64), ("nhwc", 8), ("nchw", 64)])
+def test_maxpool_e4m3_qdq_semantics(dev, layout, C):
+    """e4m3 MaxPool equals DequantizeLinear -> MaxPool -> QuantizeLinear at the
+    same scale: -0 comes out as 0x00, NaN taps are ignored and an all-NaN
+    window gives the saturated -inf code 0xfe. C = 64 NHWC takes the 16-byte
+    vector kernel, the others the scalar one."""
+    import torch
+    import luisaml_b200 as lb
+    rng = np.random.default_rng(C)
+    N, H, W = 2, 23, 30
+    q = rng.integers(0, 256, size=(N, C, H, W), dtype=np.uint8)
+    q[rng.random(q.shape) < 0.05] = 0x80
+    q[:, :, 4:7, 4:7] = 0x7f   # the window centred at (5, 5) is all NaN
+    q[:, :, 10, :] = 0xff
+    oH, oW = (H + 2 - 3) // 2 + 1, (W + 2 - 3) // 2 + 1
+    want = oracle.quantize(oracle.maxpool2d(oracle.e4m3_decode(q).astype(np.float32), (3, 3), (2, 2), (1, 1, 1, 1)),
+                           np.float32(1.0))
+    nhwc = layout == "nhwc"
+    qin = np.ascontiguousarray(q.transpose(0, 2, 3, 1)) if nhwc else q
+    y = torch.empty(N * C * oH * oW, dtype=torch.uint8, device=dev)
+    lb.check(lb.lib().lcml_maxpool2d(_p(_t(qin, dev)), 17, N * C, H, W, 3, 3, 2, 2, 1, 1, oH, oW, _p(y), int(nhwc), C,
+                                     _s()))
+    got = y.cpu().numpy().reshape((N, oH, oW, C) if nhwc else (N, C, oH, oW))
+    if nhwc:
+        got = got.transpose(0, 3, 1, 2)
+    np.testing.assert_array_equal(got, want)

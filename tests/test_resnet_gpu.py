@@ -1,0 +1,117 @@
+"""ResNet-50-shaped QDQ conv networks through the executor (LuisaML-JSON ->
+NetworkInstance): every DequantizeLinear -> Conv -> (Add) -> Relu ->
+QuantizeLinear group must run as one fused FP8 conv, the max pool and the
+global average pool on the e4m3 bytes, and the results must agree with the
+oracle replaying the same graph (quantize/dequantize, conv.cpp's loop, max
+pool, mean, gemm.cpp's loop).
+
+Every activation is requantized to e4m3 with a static scale, so an fp32
+summation-order difference that lands on an e4m3 rounding boundary moves
+one code by one step, and in a deep network such flips compound from layer
+to layer. The full ResNet-50 is therefore checked conv by conv: each fused
+conv is replayed by the oracle from the executor's own e4m3 input (read back
+through lcml_network_tensor), and its output codes must match except for
+rare flips to the neighbouring code.
+"""
+import numpy as np
+import pytest
+
+import oracle
+from conftest import assert_close
+
+pytestmark = pytest.mark.gpu
+
+
+def _run(dev, text, blob, x, ncls):
+    import torch
+    from luisaml_b200.session import Network
+    net = Network(text)
+    y = torch.empty((x.shape[0], ncls), dtype=torch.float32, device=dev)
+    net.set_weight_buffer(torch.from_numpy(np.frombuffer(blob, dtype=np.uint8).copy()).to(dev))
+    net.set_input("x", torch.from_numpy(x).to(dev))
+    net.set_output("logits", y)
+    net.forward()
+    torch.cuda.synchronize()
+    return net, y.cpu().numpy()
+
+
+def _codes_nchw(net, name):
+    q = net.read_tensor(name)
+    _, _, _, nhwc = net.tensor_info(name)
+    return np.ascontiguousarray(q.transpose(0, 3, 1, 2)) if nhwc else q
+
+
+def _structure(net, meta):
+    s = net.summary()
+    nconv = sum(1 for st in meta["plan"] if st[0] == "conv")
+    assert s.count("implicit-GEMM conv") == nconv, s
+    # input QuantizeLinear + convs + max pool + global average pool + Flatten (a view)
+    # + head QuantizeLinear + head GEMM
+    assert net.executed_nodes() == nconv + 6, s
+
+
+def test_small_resnet_end_to_end(dev):
+    """1 bottleneck block per stage, width 16, 64x64 images: shallow enough
+    that the whole forward matches the oracle end to end."""
+    from luisaml_b200 import graphs
+    text, blob, meta = graphs.resnet50(batch=2, image=64, width=16, blocks=(1, 1, 1, 1), num_classes=10)
+    x = np.random.default_rng(4001).standard_normal((2, 3, 64, 64)).astype(np.float32)
+    net, got = _run(dev, text, blob, x, 10)
+    _structure(net, meta)
+    ref = oracle.replay_plan(meta["plan"], x)
+    assert_close(got, ref, what="small resnet logits")
+
+
+def _one_step_apart(got_codes, want_codes):
+    """Whether every differing pair of codes is one e4m3 step apart (the
+    spacing of the larger magnitude: 2^(e-3) for normals, 2^-9 below 2^-6)."""
+    g = oracle.e4m3_decode(got_codes).astype(np.float64)
+    w = oracle.e4m3_decode(want_codes).astype(np.float64)
+    m = np.maximum(np.abs(g), np.abs(w))
+    spacing = np.where(m >= 2.0 ** -6, 2.0 ** (np.floor(np.log2(np.maximum(m, 2.0 ** -6))) - 3), 2.0 ** -9)
+    return bool((np.abs(g - w) <= spacing * (1 + 1e-9)).all())
+
+
+def test_resnet50_conv_by_conv_vs_oracle(dev):
+    """Full ResNet-50 v1.5 at 224x224 (batch 2). Every one of the 53 fused
+    convs is replayed by the oracle from the executor's own e4m3 input (and
+    residual) codes: its output codes must match except for rare flips to the
+    neighbouring code. The e4m3 max pool must match exactly, and the head
+    (global average pool, QDQ classifier) within the GEMM tolerance."""
+    from luisaml_b200 import graphs
+    text, blob, meta = graphs.resnet50(batch=2, image=224)
+    x = np.random.default_rng(4002).standard_normal((2, 3, 224, 224)).astype(np.float32)
+    net, got = _run(dev, text, blob, x, 1000)
+    _structure(net, meta)
+    assert np.isfinite(got).all()
+    assert len(meta["conv_io"]) == 53
+    worst = 0.0
+    for c in meta["conv_io"]:
+        _, wq, ws, bias, stride, pad = c["conv"]
+        h = oracle.conv2d(oracle.dequantize(_codes_nchw(net, c["x"]), c["x_scale"]), oracle.dequantize(wq, ws, axis=0),
+                          bias, strides=(stride, stride), pads=(pad, pad, pad, pad))
+        if c["res"] is not None:
+            h = (h + oracle.dequantize(_codes_nchw(net, c["res"]), c["res_scale"])).astype(np.float32)
+        if c["relu"]:
+            h = oracle.relu(h)
+        want = oracle.quantize(h, c["y_scale"])
+        gotc = _codes_nchw(net, c["y"])
+        diff = gotc != want
+        frac = float(diff.mean())
+        worst = max(worst, frac)
+        assert frac <= 1e-4, (c["y"], frac)
+        assert _one_step_apart(gotc[diff], want[diff]), c["y"]
+    print(f"53 convs: worst flip rate {worst:.5%}")
+    # the max pool works on codes: exact
+    stem, pool = meta["conv_io"][0]["y"], meta["segments"][0][2]
+    s = meta["conv_io"][0]["y_scale"]
+    want = oracle.quantize(oracle.maxpool2d(oracle.dequantize(_codes_nchw(net, stem), s), (3, 3), (2, 2), (1, 1, 1, 1)), s)
+    np.testing.assert_array_equal(_codes_nchw(net, pool), want)
+    # head from the last block's codes
+    src, s_in, _, _, steps = meta["segments"][-1]
+    ref = oracle.replay_plan(steps, oracle.dequantize(_codes_nchw(net, src), s_in))
+    err = np.abs(got - ref)
+    frac = float((err > 1e-3 + 2e-3 * np.abs(ref)).mean())
+    print(f"head: {frac:.4%} of logits outside rtol 2e-3/atol 1e-3, max |err| {err.max():.3g}")
+    assert frac <= 0.02, frac
+    assert_close(got, ref, rtol=2e-2, atol=2e-2 * float(np.abs(ref).max()), what="head logits")
