@@ -113,14 +113,18 @@ __device__ __forceinline__ void load_col_factors(const EpiParams &ep, int64_t n0
 #pragma unroll
             for (int j = 0; j < 8; ++j) {
                 const float4 v = __ldg(reinterpret_cast<const float4 *>(ep.c_vec + n0) + j);
-                f.add[4 * j] = ep.beta * v.x;
-                f.add[4 * j + 1] = ep.beta * v.y;
-                f.add[4 * j + 2] = ep.beta * v.z;
-                f.add[4 * j + 3] = ep.beta * v.w;
+                f.add[4 * j] = v.x;
+                f.add[4 * j + 1] = v.y;
+                f.add[4 * j + 2] = v.z;
+                f.add[4 * j + 3] = v.w;
             }
         } else {
 #pragma unroll
-            for (int j = 0; j < 32; ++j) f.add[j] = (n0 + j < ep.N) ? ep.beta * __ldg(ep.c_vec + n0 + j) : 0.0f;
+            for (int j = 0; j < 32; ++j) f.add[j] = (n0 + j < ep.N) ? __ldg(ep.c_vec + n0 + j) : 0.0f;
+        }
+        if (ep.beta != 1.0f) {
+#pragma unroll
+            for (int j = 0; j < 32; ++j) f.add[j] *= ep.beta;
         }
     } else {
 #pragma unroll
@@ -222,30 +226,7 @@ __device__ __forceinline__ void pack32(const float (&v)[32], const OutQuant &q, 
             w[j] = *reinterpret_cast<uint32_t *>(&h);
         }
     } else {
-        // quantize2_fast over the whole chunk without a branch per pair: the
-        // hardware conversions of x * RN(1/s) for all 32 values, one flag for
-        // "some value needs the exact path", one branch at the end.
-        bool exact = !q.s_ok;
-#pragma unroll
-        for (int j = 0; j < 8; ++j) {
-            float a[4];
-#pragma unroll
-            for (int k = 0; k < 4; ++k) {
-                a[k] = v[4 * j + k] * q.r;
-                exact |= needs_exact(a[k], v[4 * j + k]);
-            }
-            uint32_t x = cvt_e4m3x2(a[0], a[1]) | (cvt_e4m3x2(a[2], a[3]) << 16);
-#pragma unroll
-            for (int k = 0; k < 4; ++k)
-                if (v[4 * j + k] == 0.0f) x &= ~(0xffu << (8 * k));  // +-0 -> 0x00
-            w[j] = x;
-        }
-        if (exact) {
-#pragma unroll 1
-            for (int j = 0; j < 8; ++j)
-                w[j] = quantize1(v[4 * j], q.ys) | (quantize1(v[4 * j + 1], q.ys) << 8) |
-                       (quantize1(v[4 * j + 2], q.ys) << 16) | (quantize1(v[4 * j + 3], q.ys) << 24);
-        }
+        quantize_block_fast<32>(v, q.ys, q.r, q.s_ok, w);
     }
 }
 
@@ -351,13 +332,42 @@ __device__ __forceinline__ void store_chunk_tma(const CUtensorMap *tmY, uint8_t 
 // columns ng0.. (for SILU_MUL the gate columns; u the up columns nu0..), fg
 // their column factors. Parameter-dependent branches are per chunk; the
 // element loops are branch-free.
+// Raw bytes of the 32 residual values of one row segment, loaded ahead of
+// the TMEM wait when the residual is e4m3 and the segment is whole and
+// 16-byte aligned (the common conv case); `ok` says the bytes are valid.
+struct ResidualRaw {
+    uint4 w[2];
+    bool ok;
+};
+
+__device__ __forceinline__ void prefetch_residual(const EpiParams &ep, int64_t row, bool row_ok, int64_t col0,
+                                                  int64_t n_out, ResidualRaw &rr) {
+    rr.ok = false;
+    if (!ep.c_mat || ep.c_mat_kind != 2 || !row_ok || col0 + 32 > n_out) return;
+    const uint8_t *cp = reinterpret_cast<const uint8_t *>(ep.c_mat) + row * ep.ldc + col0;
+    if (!aligned(cp, 16)) return;
+    rr.w[0] = __ldg(reinterpret_cast<const uint4 *>(cp));
+    rr.w[1] = __ldg(reinterpret_cast<const uint4 *>(cp) + 1);
+    rr.ok = true;
+}
+
+// Values of 32 output columns [col0, col0+32) of one row: scale, beta*C,
+// SiLU*up, residual, Relu, running |max|. g holds the accumulators of gemm
+// columns ng0.. (for SILU_MUL the gate columns; u the up columns nu0..), fg
+// their column factors, rr the prefetched residual (else it is loaded here).
+// Parameter-dependent branches are per chunk; the element loops are
+// branch-free.
 template <int EPI>
 __device__ __forceinline__ void epi_values(const EpiParams &ep, int64_t row, bool row_ok, int64_t col0, int64_t nu0,
                                            int64_t n_out, const uint32_t (&g)[32], const uint32_t (&u)[32],
-                                           const ColFactors &fg, float row_scale, float row_add, float &amax,
-                                           float (&v)[32]) {
+                                           ColFactors &fg, const ResidualRaw &rr, float row_scale, float row_add,
+                                           float &amax, float (&v)[32]) {
+    if (row_add != 0.0f) {
 #pragma unroll
-    for (int j = 0; j < 32; ++j) v[j] = fmaf(__uint_as_float(g[j]) * row_scale, fg.scale[j], fg.add[j] + row_add);
+        for (int j = 0; j < 32; ++j) fg.add[j] += row_add;
+    }
+#pragma unroll
+    for (int j = 0; j < 32; ++j) v[j] = fmaf(__uint_as_float(g[j]) * row_scale, fg.scale[j], fg.add[j]);
     if (EPI == LCML_EPI_SILU_MUL) {
         ColFactors fu;
         load_col_factors(ep, nu0, fu);
@@ -367,7 +377,17 @@ __device__ __forceinline__ void epi_values(const EpiParams &ep, int64_t row, boo
             v[j] = silu_mul(v[j], up);
         }
     }
-    if (ep.c_mat && row_ok) {
+    if (rr.ok) {
+        const float cs = __ldg(ep.c_mat_scale) * ep.beta;
+        const uint32_t ws[8] = {rr.w[0].x, rr.w[0].y, rr.w[0].z, rr.w[0].w, rr.w[1].x, rr.w[1].y, rr.w[1].z, rr.w[1].w};
+#pragma unroll
+        for (int k = 0; k < 16; ++k) {
+            float lo, hi;
+            e4m3x2_decode(ws[k >> 1] >> ((k & 1) * 16), lo, hi);
+            v[2 * k] = fmaf(lo, cs, v[2 * k]);
+            v[2 * k + 1] = fmaf(hi, cs, v[2 * k + 1]);
+        }
+    } else if (ep.c_mat && row_ok) {
         float r[32];
         load_cmat32(ep, row, col0, n_out, r);
 #pragma unroll
@@ -419,9 +439,11 @@ __device__ __forceinline__ void epilogue_tile(const EpiParams &ep, const CUtenso
         if (EPI == LCML_EPI_SILU_MUL) tmem_ld_32x32b_x32(taddr + BN / 2 + c * 32, u);
         ColFactors fg;
         load_col_factors(ep, ng0, fg);  // global loads overlap the TMEM load
+        ResidualRaw rr;
+        prefetch_residual(ep, row, row_ok, col0, n_out, rr);
         tmem_wait_ld();
         float v[32];
-        epi_values<EPI>(ep, row, row_ok, col0, ng0 + BN / 2, n_out, g, EPI == LCML_EPI_SILU_MUL ? u : g, fg,
+        epi_values<EPI>(ep, row, row_ok, col0, ng0 + BN / 2, n_out, g, EPI == LCML_EPI_SILU_MUL ? u : g, fg, rr,
                         row_scale, row_add, amax, v);
         constexpr int ES = out_es(OUT);
         if (ep.tma_store) {

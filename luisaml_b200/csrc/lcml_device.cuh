@@ -137,6 +137,39 @@ __device__ __forceinline__ bool scale_fast_ok(float s, float r) {
     return s >= 1.17549435e-38f && s < 3.0e38f && r >= 1.17549435e-38f && r < 3.0e38f;
 }
 
+// Branch-free QuantizeLinear of N values (N a multiple of 4) into N / 4
+// little-endian words, bit-identical to quantize1: q = fma(v, r, +0) with
+// r = RN(1/s) (the +0 turns -0 into +0, which the codec writes as 0x00) is
+// converted by the hardware. One flag collects the values whose q lies within
+// 3 ulps of a pattern with low 19 mantissa bits 0 — every e4m3 rounding
+// boundary has that form, normal (low 20 bits 0x80000) or subnormal (low 20
+// bits 0) — and NaN codes (the hardware may write 0xff where the codec writes
+// 0x7f); if it is set, the whole block takes the exact divide + integer
+// encoder. Zeros, values that underflow to zero and infinities need no flag:
+// the hardware keeps the sign and saturates as the codec does.
+template <int N>
+__device__ __forceinline__ void quantize_block_fast(const float *v, float s, float r, bool s_ok, uint32_t *w) {
+    bool exact = !s_ok;
+#pragma unroll
+    for (int j = 0; j < N / 4; ++j) {
+        float a[4];
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            a[k] = fmaf(v[4 * j + k], r, 0.0f);
+            const uint32_t ab = __float_as_uint(a[k]) & 0x7fffffffu;
+            exact |= (((ab + 3u) & 0x7ffffu) <= 6u) & (ab - 1u < 0x7f7fffffu);
+        }
+        w[j] = cvt_e4m3x2(a[0], a[1]) | (cvt_e4m3x2(a[2], a[3]) << 16);
+        exact |= __vcmpeq4(w[j] | 0x80808080u, 0xffffffffu) != 0u;
+    }
+    if (exact) {  // unrolled: a runtime index would move v and w to local memory
+#pragma unroll
+        for (int j = 0; j < N / 4; ++j)
+            w[j] = quantize1(v[4 * j], s) | (quantize1(v[4 * j + 1], s) << 8) | (quantize1(v[4 * j + 2], s) << 16) |
+                   (quantize1(v[4 * j + 3], s) << 24);
+    }
+}
+
 // amax -> scale for every dynamic mode: amax / 448, or 1 when amax is 0.
 __device__ __forceinline__ float scale_from_amax(float amax) {
     return amax > 0.0f ? __fdiv_rn(amax, 448.0f) : 1.0f;

@@ -41,8 +41,11 @@ __device__ __forceinline__ Scale make_scale(float v) {
     return sc;
 }
 
-__device__ __forceinline__ uint32_t pack4(float a, float b, float c, float d, const Scale &sc) {
-    return quantize2_fast(a, b, sc.s, sc.r, sc.ok) | (quantize2_fast(c, d, sc.s, sc.r, sc.ok) << 16);
+__device__ __forceinline__ uint4 pack16(float4 a, float4 b, float4 c, float4 d, const Scale &sc) {
+    const float v[16] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w, c.x, c.y, c.z, c.w, d.x, d.y, d.z, d.w};
+    uint32_t w[4];
+    quantize_block_fast<16>(v, sc.s, sc.r, sc.ok, w);
+    return make_uint4(w[0], w[1], w[2], w[3]);
 }
 
 __device__ __forceinline__ uint32_t pack4v(float4 v, const float *s) {
@@ -69,12 +72,8 @@ __global__ void __launch_bounds__(kThreads) k_quantize(const float *__restrict__
             const float4 *xb = reinterpret_cast<const float4 *>(x) + (g + nthreads) * 4;
             const float4 a0 = __ldcs(xa), a1 = __ldcs(xa + 1), a2 = __ldcs(xa + 2), a3 = __ldcs(xa + 3);
             const float4 b0 = __ldcs(xb), b1 = __ldcs(xb + 1), b2 = __ldcs(xb + 2), b3 = __ldcs(xb + 3);
-            __stcs(reinterpret_cast<uint4 *>(y) + g,
-                   make_uint4(pack4(a0.x, a0.y, a0.z, a0.w, st), pack4(a1.x, a1.y, a1.z, a1.w, st),
-                              pack4(a2.x, a2.y, a2.z, a2.w, st), pack4(a3.x, a3.y, a3.z, a3.w, st)));
-            __stcs(reinterpret_cast<uint4 *>(y) + g + nthreads,
-                   make_uint4(pack4(b0.x, b0.y, b0.z, b0.w, st), pack4(b1.x, b1.y, b1.z, b1.w, st),
-                              pack4(b2.x, b2.y, b2.z, b2.w, st), pack4(b3.x, b3.y, b3.z, b3.w, st)));
+            __stcs(reinterpret_cast<uint4 *>(y) + g, pack16(a0, a1, a2, a3, st));
+            __stcs(reinterpret_cast<uint4 *>(y) + g + nthreads, pack16(b0, b1, b2, b3, st));
         }
     }
     for (; g < n16; g += nthreads) {
@@ -82,16 +81,9 @@ __global__ void __launch_bounds__(kThreads) k_quantize(const float *__restrict__
         const float4 v0 = __ldcs(xp), v1 = __ldcs(xp + 1), v2 = __ldcs(xp + 2), v3 = __ldcs(xp + 3);
         uint4 out;
         if (KIND == kScaleTensor) {
-            out.x = pack4(v0.x, v0.y, v0.z, v0.w, st);
-            out.y = pack4(v1.x, v1.y, v1.z, v1.w, st);
-            out.z = pack4(v2.x, v2.y, v2.z, v2.w, st);
-            out.w = pack4(v3.x, v3.y, v3.z, v3.w, st);
+            out = pack16(v0, v1, v2, v3, st);
         } else if (KIND == kScaleGroup16) {
-            const Scale s = make_scale(load_scale(sc, ((g << 4) / inner) % axis_len, FROM_AMAX));
-            out.x = pack4(v0.x, v0.y, v0.z, v0.w, s);
-            out.y = pack4(v1.x, v1.y, v1.z, v1.w, s);
-            out.z = pack4(v2.x, v2.y, v2.z, v2.w, s);
-            out.w = pack4(v3.x, v3.y, v3.z, v3.w, s);
+            out = pack16(v0, v1, v2, v3, make_scale(load_scale(sc, ((g << 4) / inner) % axis_len, FROM_AMAX)));
         } else {
             float s[16];
             if (KIND == kScaleInner1) {
@@ -210,7 +202,12 @@ __global__ void __launch_bounds__(kThreads) k_quantize_rows_dynamic(const float 
 #pragma unroll
     for (int j = 0; j < VPT; ++j) {
         const int64_t i = threadIdx.x + static_cast<int64_t>(j) * kThreads;
-        if (i < c4) __stcs(yr + i, pack4(v[j].x, v[j].y, v[j].z, v[j].w, s));
+        if (i < c4) {
+            const float q4[4] = {v[j].x, v[j].y, v[j].z, v[j].w};
+            uint32_t w;
+            quantize_block_fast<4>(q4, s.s, s.r, s.ok, &w);
+            __stcs(yr + i, w);
+        }
     }
 }
 
