@@ -477,16 +477,18 @@ class TpGemmWorkload:
 
 class ResnetWorkload(GraphWorkload):
     """ResNet-50 v1.5 as a fully quantized QDQ graph at 224x224,
-    batch 128 per rank: 53 fused FP8 implicit-GEMM convs (scales, bias,
-    residual, Relu and requantization in the epilogue), e4m3 max pool and
-    global average pool, QDQ classifier. Each rank runs its own batch (weak
-    scaling, no collective)."""
+    batch 128 split across the ranks (batch split, no collective): 53 fused
+    FP8 conv GEMMs (scales, bias, residual, Relu and requantization in the
+    epilogue), e4m3 max pool and global average pool, QDQ classifier."""
     unit = "inferences/s"
-    parallelism = "dp (independent batches per rank, no collective)"
+    scaling = "strong"
+    parallelism = "batch split (no collective)"
 
     def __init__(self, batch=128, image=224):
-        self.batch, self.image = batch, image
-        self.work_per_step = batch
+        self.total_batch, self.image = batch, image
+        ws = int(os.environ.get("WORLD_SIZE", "1"))
+        self.batch = max(1, batch // ws)
+        self.work_per_step = self.batch
         self.flop_per_image = None  # known once the graph is built
 
     def describe(self):

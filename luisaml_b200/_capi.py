@@ -143,6 +143,8 @@ def load():
     lib.lcml_launch_count.argtypes = []
     lib.lcml_fp8_gemm_set_mode.restype = None
     lib.lcml_fp8_gemm_set_mode.argtypes = [ctypes.c_int]
+    lib.lcml_fp8_conv_set_mode.restype = None
+    lib.lcml_fp8_conv_set_mode.argtypes = [ctypes.c_int]
     for name, args in PROTOTYPES.items():
         fn = getattr(lib, name)
         fn.argtypes = args

@@ -23,6 +23,8 @@ int64_t packed_c(int64_t c) { return c % 16 == 0 ? c : (c <= 4 ? 4 : (c <= 8 ? 8
 
 int64_t packed_k(int64_t cg, int64_t kh, int64_t kw) { return ((packed_c(cg) * kh * kw + 15) / 16) * 16; }
 
+int g_conv_mode = 0;  // lcml_fp8_conv_set_mode
+
 bool direct_path(const lcml_fp8_conv_desc *d) {
     return d->kH == 1 && d->kW == 1 && d->sH == 1 && d->sW == 1 && d->pH == 0 && d->pW == 0 && d->x_nhwc &&
            d->C % 16 == 0 && d->oH == d->H && d->oW == d->W;
@@ -31,6 +33,15 @@ bool direct_path(const lcml_fp8_conv_desc *d) {
 // The input is gathered straight from X (NHWC, C a multiple of 16) or from a
 // channel-padded NHWC copy of it in the workspace.
 bool needs_repack(const lcml_fp8_conv_desc *d) { return !(d->x_nhwc && d->C % 16 == 0); }
+
+// Convs whose patches the GEMM can gather itself (NHWC input, C % 16 == 0,
+// 32-bit extents; the kernel keeps each output pixel's first input row and
+// column in 16 bits): no im2col pass and no workspace.
+bool implicit_ok(const lcml_fp8_conv_desc *d) {
+    return !direct_path(d) && !needs_repack(d) && d->N * d->H * d->W * d->C < (int64_t(1) << 31) &&
+           d->N * d->oH * d->oW < (int64_t(1) << 31) && d->H < 16384 && d->W < 16384 && d->pH < 16384 &&
+           d->pW < 16384 && d->oH * d->sH + d->kH * d->dH < 16384 && d->oW * d->sW + d->kW * d->dW < 16384;
+}
 
 int64_t repack_bytes(const lcml_fp8_conv_desc *d) {
     return needs_repack(d) ? ((d->N * d->H * d->W * packed_c(d->C) + 255) / 256) * 256 : 0;
@@ -215,7 +226,17 @@ int lcml_fp8_conv(const lcml_fp8_conv_desc *d, lcml_stream_t stream) {
     cudaStream_t st = to_cuda(stream);
     const uint8_t *A = d->X;
     int64_t K = d->C;
-    if (!direct_path(d)) {
+    // implicit GEMM: the GEMM's producer gathers the patches from NHWC X itself
+    // Materialized patches (im2col into the workspace, then the TMA-fed GEMM)
+    // are the faster lowering on B200; the implicit GEMM (the kernel's
+    // producer warps gather the patches with cp.async) runs when the caller
+    // passes no workspace, or when a test asks for it.
+    const bool implicit = implicit_ok(d) && aligned(d->X, 16) && g_conv_mode != 1 &&
+                          (g_conv_mode == 2 || d->workspace == nullptr);
+    if (implicit) {
+        A = nullptr;
+        K = Kp;
+    } else if (!direct_path(d)) {
         LCML_CHECK_ARG(d->workspace != nullptr && aligned(d->workspace, 256),
                        "lcml_fp8_conv: this conv needs a 256-byte aligned workspace of %lld bytes",
                        static_cast<long long>(lcml_fp8_conv_workspace_size(d)));
@@ -267,7 +288,32 @@ int lcml_fp8_conv(const lcml_fp8_conv_desc *d, lcml_stream_t stream) {
     g.y_dtype = d->y_dtype;
     g.ldy = d->M;
     g.y_scale = d->y_scale;
+    if (implicit) {
+        ConvGeom geo;
+        geo.x = d->X;
+        geo.N = static_cast<int>(d->N);
+        geo.H = static_cast<int>(d->H);
+        geo.W = static_cast<int>(d->W);
+        geo.C = static_cast<int>(d->C);
+        geo.oH = static_cast<int>(d->oH);
+        geo.oW = static_cast<int>(d->oW);
+        geo.kH = static_cast<int>(d->kH);
+        geo.kW = static_cast<int>(d->kW);
+        geo.sH = d->sH;
+        geo.sW = d->sW;
+        geo.pH = d->pH;
+        geo.pW = d->pW;
+        geo.dH = d->dH;
+        geo.dW = d->dW;
+        geo.ktaps = geo.kH * geo.kW * geo.C;
+        return fp8_gemm_implicit_conv(&g, geo, st);
+    }
     return lcml_fp8_gemm(&g, stream);
 }
+
+// Test hook (not in the public header): 0 automatic (implicit GEMM only
+// without a workspace), 1 always materialize the patches, 2 implicit GEMM
+// wherever the geometry allows it.
+void lcml_fp8_conv_set_mode(int mode) { g_conv_mode = mode; }
 
 }// extern "C"

@@ -302,6 +302,11 @@ template <int EPI>
 constexpr int epi_warps() { return EPI == LCML_EPI_SILU_MUL ? 4 : 8; }
 template <int EPI>
 constexpr int threads_for() { return 64 + 32 * epi_warps<EPI>(); }
+// The implicit-GEMM convolution adds a second patch-gathering warp after the
+// epilogue warps (warp 0 is the first).
+template <int EPI, bool IM2COL>
+constexpr int threads_for_conv() { return threads_for<EPI>() + (IM2COL ? 32 : 0); }
+constexpr int kGatherRowsPerWarp = 64;
 
 template <int OUT>
 __device__ __forceinline__ void store_chunk_tma(const CUtensorMap *tmY, uint8_t *stage, uint32_t &seq, int64_t row0,
@@ -428,19 +433,26 @@ __device__ __forceinline__ void epilogue_tile(const EpiParams &ep, const CUtenso
     else if (ep.c_vec_mode == 2 && row_ok) row_add = ep.beta * __ldg(ep.c_vec + row);
     float amax = 0.0f;
     constexpr int kChunks = (EPI == LCML_EPI_SILU_MUL) ? BN / 64 : BN / 32;
+    // SILU_MUL: BN columns = BN/2 gate columns followed by BN/2 up columns
+    auto col_of = [&](int c) {
+        return (EPI == LCML_EPI_SILU_MUL) ? static_cast<int64_t>(tn) * (BN / 2) + c * 32
+                                          : static_cast<int64_t>(tn) * BN + c * 32;
+    };
+    // the residual of the next chunk is loaded while this one is processed
+    ResidualRaw rr_next;
+    prefetch_residual(ep, row, row_ok, col_of(c_first), n_out, rr_next);
 #pragma unroll 1
     for (int c = c_first; c < kChunks; c += c_step) {
-        // SILU_MUL: BN columns = BN/2 gate columns followed by BN/2 up columns
         const int64_t ng0 = static_cast<int64_t>(tn) * BN + c * 32;
-        const int64_t col0 = (EPI == LCML_EPI_SILU_MUL) ? static_cast<int64_t>(tn) * (BN / 2) + c * 32 : ng0;
+        const int64_t col0 = col_of(c);
         if (col0 >= n_out) break;  // warp-uniform
         uint32_t g[32], u[32];
         tmem_ld_32x32b_x32(taddr + c * 32, g);
         if (EPI == LCML_EPI_SILU_MUL) tmem_ld_32x32b_x32(taddr + BN / 2 + c * 32, u);
         ColFactors fg;
         load_col_factors(ep, ng0, fg);  // global loads overlap the TMEM load
-        ResidualRaw rr;
-        prefetch_residual(ep, row, row_ok, col0, n_out, rr);
+        const ResidualRaw rr = rr_next;
+        if (c + c_step < kChunks) prefetch_residual(ep, row, row_ok, col_of(c + c_step), n_out, rr_next);
         tmem_wait_ld();
         float v[32];
         epi_values<EPI>(ep, row, row_ok, col0, ng0 + BN / 2, n_out, g, EPI == LCML_EPI_SILU_MUL ? u : g, fg, rr,
@@ -484,21 +496,33 @@ struct Layout {
     static constexpr int kTmemCols = 2 * BN;  // double-buffered fp32 accumulator
     static constexpr int kBarOffset = STAGES * kStageBytes;
     static constexpr int kEpiOffset = kBarOffset + 1024;     // epilogue warps' output staging
-    static constexpr int kSmemBytes = kEpiOffset + epi_warps<EPI>() * stage_bytes_per_warp<OUT>() + 1024;  // +1024 alignment
+    static constexpr int kRowOffset = kEpiOffset + epi_warps<EPI>() * stage_bytes_per_warp<OUT>();  // conv row table
+    static constexpr int kSmemBytes = kRowOffset + BM * 8 + 1024;  // +1024 alignment
 };
 
 // The deepest operand ring (at most 8 stages) that fits beside the staging.
 template <int BN, int EPI, int OUT>
 constexpr int stages_for() {
-    const int room = kSmemLimit - 2048 - epi_warps<EPI>() * stage_bytes_per_warp<OUT>();
+    const int room = kSmemLimit - 2048 - BM * 8 - epi_warps<EPI>() * stage_bytes_per_warp<OUT>();
     const int s = room / (BM * BK + BN * BK);
     return s > 8 ? 8 : s;
 }
 
-template <int BN, int STAGES, int EPI, int OUT>
-__global__ void __launch_bounds__(threads_for<EPI>(), 1)
+// IM2COL: A is not read through tmA but gathered from the NHWC activation
+// described by `geo` (implicit-GEMM convolution) by two warps (warp 0 and the
+// warp after the epilogue warps), 64 tile rows each. Per tile they write a row
+// table (image offset, first input row / column of each output pixel) to
+// shared memory; per K-block, lane l copies 16-byte chunk (l & 7) of rows
+// (l >> 3) + 4 i with cp.async (zero-filled for padding taps and K past the
+// taps), so each instruction reads whole 64- or 128-byte runs of a pixel's
+// channels, into the 128-byte swizzled layout the MMA descriptors expect, and
+// arrives on the stage's full barrier when its copies have landed. Lane 0 of
+// warp 0 still loads B by TMA.
+template <int BN, int STAGES, int EPI, int OUT, bool IM2COL>
+__global__ void __launch_bounds__(threads_for_conv<EPI, IM2COL>(), 1)
     k_gemm_fp8_tc(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                  const __grid_constant__ CUtensorMap tmY, int M, int N, int K, EpiParams ep, int *err) {
+                  const __grid_constant__ CUtensorMap tmY, int M, int N, int K, EpiParams ep, ConvGeom geo,
+                  int *err) {
     using L = Layout<BN, STAGES, EPI, OUT>;
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -517,7 +541,7 @@ __global__ void __launch_bounds__(threads_for<EPI>(), 1)
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < STAGES; ++s) {
-            mbar_init(&full[s], 1);
+            mbar_init(&full[s], IM2COL ? 1 + 2 * 32 : 1);  // + the gathering lanes' cp.async arrivals
             mbar_init(&empty[s], 1);
         }
         for (int b = 0; b < 2; ++b) {
@@ -535,7 +559,95 @@ __global__ void __launch_bounds__(threads_for<EPI>(), 1)
     tc_fence_after();
     const uint32_t tmem_base = *tmem_slot;
 
-    if (warp == 0) {
+    if (IM2COL && (warp == 0 || warp == 2 + epi_warps<EPI>())) {
+        // ---------------- implicit-GEMM producers (two warps) ----------------
+        const int half = warp == 0 ? 0 : 1;
+        if (warp == 0 && lane == 0) tma_prefetch_desc(&tmB);
+        int2 *rows = reinterpret_cast<int2 *>(smem + L::kRowOffset) + half * kGatherRowsPerWarp;
+        int stage = 0;
+        uint32_t phase = 0;
+        int issued = 0;
+        bool ok = true;
+        const int ohw = geo.oH * geo.oW;
+        const int j = lane & 7, rsub = lane >> 3;
+        const uint32_t row_dst = static_cast<uint32_t>(half * kGatherRowsPerWarp + rsub) * 128u;
+        for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
+            int tm, tn;
+            tile_coords(tile, num_m, num_n, tm, tn);
+            __syncwarp();  // the previous tile's reads of the table are done
+#pragma unroll
+            for (int i = 0; i < 2; ++i) {
+                const int r = lane + 32 * i;
+                const int m = tm * BM + half * kGatherRowsPerWarp + r;
+                int2 info;
+                if (m < M) {
+                    const int n = m / ohw, rem = m - n * ohw;
+                    const int oh = rem / geo.oW, ow = rem - oh * geo.oW;
+                    info.x = n * geo.H * geo.W * geo.C;
+                    info.y = static_cast<int>((static_cast<uint32_t>(oh * geo.sH - geo.pH) << 16) |
+                                              (static_cast<uint32_t>(ow * geo.sW - geo.pW) & 0xffffu));
+                } else {
+                    info.x = 0;
+                    info.y = static_cast<int>(0x80008000u);  // out of range in both directions
+                }
+                rows[r] = info;
+            }
+            __syncwarp();
+            for (int kb = 0; kb < kblocks; ++kb) {
+                if (!mbar_wait(&empty[stage], phase ^ 1u, err, kDevTimeoutProducer)) {
+                    ok = false;
+                    break;
+                }
+                uint8_t *sa = smem + stage * L::kStageBytes;
+                if (warp == 0 && lane == 0) {
+                    mbar_arrive_expect_tx(&full[stage], L::kBBytes);
+                    tma_load_2d(&tmB, &full[stage], sa + L::kABytes, kb * BK, tn * BN);
+                }
+                // this lane's K chunk: tap (kh, kw), channel c
+                const int k = kb * BK + j * 16;
+                int dh = -65536, dw = 0, c = 0;
+                if (k < geo.ktaps) {
+                    const int t = k / geo.C;
+                    c = k - t * geo.C;
+                    const int kh = t / geo.kW;
+                    dh = kh * geo.dH;
+                    dw = (t - kh * geo.kW) * geo.dW;
+                }
+                const uint32_t dst0 = smem_u32(sa) + row_dst;
+#pragma unroll
+                for (int i = 0; i < kGatherRowsPerWarp / 4; ++i) {
+                    const int r = 4 * i + rsub;
+                    const int2 info = rows[r];
+                    const int ih = (info.y >> 16) + dh;
+                    const int iw = static_cast<int>(static_cast<int16_t>(info.y & 0xffff)) + dw;
+                    const bool in = static_cast<unsigned>(ih) < static_cast<unsigned>(geo.H) &&
+                                    static_cast<unsigned>(iw) < static_cast<unsigned>(geo.W);
+                    const uint8_t *src = in ? geo.x + (info.x + (ih * geo.W + iw) * geo.C + c) : geo.x;
+                    // row r of this warp's half; 16-byte chunk j swizzled by the row's low 3 bits
+                    const uint32_t sw = static_cast<uint32_t>((rsub + 4 * i) & 7);
+                    cp_async_16_zfill(dst0 + static_cast<uint32_t>(4 * i) * 128u + ((static_cast<uint32_t>(j) ^ sw) << 4),
+                                      src, in ? 16u : 0u);
+                }
+                cp_async_mbar_arrive_noinc(&full[stage]);
+                ++issued;
+                if (++stage == STAGES) {
+                    stage = 0;
+                    phase ^= 1u;
+                }
+            }
+        }
+        if (warp == 0 && lane == 0) {
+            const int pending = issued < STAGES ? issued : STAGES;
+            for (int i = 0; i < pending; ++i) {
+                if (--stage < 0) {
+                    stage = STAGES - 1;
+                    phase ^= 1u;
+                }
+                mbar_wait(&full[stage], phase, err, kDevTimeoutDrain);
+            }
+        }
+        asm volatile("cp.async.wait_all;" ::: "memory");
+    } else if (warp == 0) {
         // ---------------- TMA producer ----------------
         if (elect_one()) {
             tma_prefetch_desc(&tmA);
@@ -593,6 +705,7 @@ __global__ void __launch_bounds__(threads_for<EPI>(), 1)
                         ok = false;
                         break;
                     }
+                    if (IM2COL) fence_proxy_async_smem();  // cp.async (generic proxy) writes -> MMA reads
                     tc_fence_after();
                     const uint32_t a_addr = smem_u32(smem + stage * L::kStageBytes);
                     const uint32_t b_addr = a_addr + L::kABytes;
@@ -997,12 +1110,12 @@ int output_tmap(const lcml_fp8_gemm_desc *d, const EpiParams &ep, CUtensorMap *t
     return make_tmap_out(ty, static_cast<uint8_t *>(d->Y) + d->y_col_offset * ES, n_out, d->M, d->ldy * ES, ES);
 }
 
-template <int BN, int EPI, int OUT>
-int launch_tc(const lcml_fp8_gemm_desc *d, const EpiParams &ep, cudaStream_t st) {
+template <int BN, int EPI, int OUT, bool IM2COL = false>
+int launch_tc(const lcml_fp8_gemm_desc *d, const EpiParams &ep, cudaStream_t st, const ConvGeom &geo = ConvGeom{}) {
     constexpr int STAGES = stages_for<BN, EPI, OUT>();
     using L = Layout<BN, STAGES, EPI, OUT>;
     static_assert(STAGES >= 3 && L::kSmemBytes <= kSmemLimit, "shared memory layout does not fit");
-    auto kern = k_gemm_fp8_tc<BN, STAGES, EPI, OUT>;
+    auto kern = k_gemm_fp8_tc<BN, STAGES, EPI, OUT, IM2COL>;
     static std::once_flag once;
     static cudaError_t attr_err = cudaSuccess;
     std::call_once(once, [&] {
@@ -1012,7 +1125,9 @@ int launch_tc(const lcml_fp8_gemm_desc *d, const EpiParams &ep, cudaStream_t st)
         return set_error(LCML_ERR_CUDA, "cudaFuncSetAttribute(smem=%d) failed: %s", L::kSmemBytes,
                          cudaGetErrorString(attr_err));
     CUtensorMap ta, tb;
-    int rc = make_tmap(&ta, d->A, d->K, d->M, d->lda, BM);
+    int rc = LCML_OK;
+    if (IM2COL) memset(&ta, 0, sizeof(ta));  // A is gathered in the kernel
+    else rc = make_tmap(&ta, d->A, d->K, d->M, d->lda, BM);
     if (rc) return rc;
     rc = make_tmap(&tb, d->B, d->K, d->N, d->ldb, BN);
     if (rc) return rc;
@@ -1021,9 +1136,9 @@ int launch_tc(const lcml_fp8_gemm_desc *d, const EpiParams &ep, cudaStream_t st)
     if (rc) return rc;
     const int64_t tiles = ((d->M + BM - 1) / BM) * ((d->N + BN - 1) / BN);
     const int grid = static_cast<int>(tiles < sm_count() ? tiles : sm_count());
-    kern<<<grid, threads_for<EPI>(), L::kSmemBytes, st>>>(ta, tb, ty, static_cast<int>(d->M), static_cast<int>(d->N),
-                                                          static_cast<int>(d->K), ep, device_error_word());
-    LCML_LAUNCHED("gemm_fp8_tc");
+    kern<<<grid, threads_for_conv<EPI, IM2COL>(), L::kSmemBytes, st>>>(
+        ta, tb, ty, static_cast<int>(d->M), static_cast<int>(d->N), static_cast<int>(d->K), ep, geo, device_error_word());
+    LCML_LAUNCHED(IM2COL ? "conv_implicit_gemm_fp8_tc" : "gemm_fp8_tc");
     return LCML_OK;
 }
 
@@ -1069,7 +1184,16 @@ int launch_simt(const lcml_fp8_gemm_desc *d, const EpiParams &ep, cudaStream_t s
 }
 
 template <int EPI, int OUT>
-int dispatch(const lcml_fp8_gemm_desc *d, const EpiParams &ep, cudaStream_t st, bool force_simt) {
+int dispatch(const lcml_fp8_gemm_desc *d, const EpiParams &ep, cudaStream_t st, bool force_simt, const ConvGeom *geo) {
+    if (geo) {  // implicit-GEMM convolution: single-CTA tiles as wide as the output channels
+        if constexpr (EPI == LCML_EPI_SILU_MUL) {
+            return set_error(LCML_ERR_UNSUPPORTED, "implicit-GEMM convolution: SILU_MUL epilogue");
+        } else {
+            if (d->N <= 64) return launch_tc<64, EPI, OUT, true>(d, ep, st, *geo);
+            if (d->N >= 2048) return launch_tc<256, EPI, OUT, true>(d, ep, st, *geo);
+            return launch_tc<128, EPI, OUT, true>(d, ep, st, *geo);
+        }
+    }
     const bool tma_ok = !force_simt && d->b_kmajor && (d->K % 16 == 0) && (d->lda % 16 == 0) && (d->ldb % 16 == 0) &&
                         aligned(d->A, 16) && aligned(d->B, 16) && d->M <= 0x7fffffff && d->N <= 0x7fffffff &&
                         d->K <= 0x7fffffff;
@@ -1086,16 +1210,17 @@ int dispatch(const lcml_fp8_gemm_desc *d, const EpiParams &ep, cudaStream_t st, 
 }
 
 template <int EPI>
-int dispatch_out(const lcml_fp8_gemm_desc *d, const EpiParams &ep, cudaStream_t st, bool force_simt) {
+int dispatch_out(const lcml_fp8_gemm_desc *d, const EpiParams &ep, cudaStream_t st, bool force_simt,
+                 const ConvGeom *geo) {
     switch (d->y_dtype) {
-        case LCML_DTYPE_FLOAT: return dispatch<EPI, kOutF32>(d, ep, st, force_simt);
-        case LCML_DTYPE_BFLOAT16: return dispatch<EPI, kOutBF16>(d, ep, st, force_simt);
-        case LCML_DTYPE_FLOAT8E4M3FN: return dispatch<EPI, kOutE4M3>(d, ep, st, force_simt);
+        case LCML_DTYPE_FLOAT: return dispatch<EPI, kOutF32>(d, ep, st, force_simt, geo);
+        case LCML_DTYPE_BFLOAT16: return dispatch<EPI, kOutBF16>(d, ep, st, force_simt, geo);
+        case LCML_DTYPE_FLOAT8E4M3FN: return dispatch<EPI, kOutE4M3>(d, ep, st, force_simt, geo);
         default: return set_error(LCML_ERR_INVALID_ARGUMENT, "lcml_fp8_gemm: y_dtype %d unsupported", d->y_dtype);
     }
 }
 
-int gemm_entry(const lcml_fp8_gemm_desc *d, lcml_stream_t stream, bool force_simt) {
+int gemm_entry(const lcml_fp8_gemm_desc *d, lcml_stream_t stream, bool force_simt, const ConvGeom *geo = nullptr) {
     LCML_CHECK_ARG(d != nullptr, "lcml_fp8_gemm: desc is NULL");
     LCML_CHECK_ARG(d->M >= 0 && d->N >= 0 && d->K >= 0, "lcml_fp8_gemm: negative extent");
     LCML_CHECK_ARG(d->epilogue >= LCML_EPI_NONE && d->epilogue <= LCML_EPI_SILU_MUL,
@@ -1104,8 +1229,8 @@ int gemm_entry(const lcml_fp8_gemm_desc *d, lcml_stream_t stream, bool force_sim
         LCML_CHECK_ARG(d->N % 256 == 0, "lcml_fp8_gemm: SILU_MUL needs N (gate+up) to be a multiple of 256, got %lld",
                        (long long)d->N);
     if (d->M == 0 || d->N == 0) return LCML_OK;
-    LCML_CHECK_ARG(d->A && d->B && d->Y && d->scale_a && d->scale_b, "lcml_fp8_gemm: null operand");
-    LCML_CHECK_ARG(d->lda >= d->K, "lcml_fp8_gemm: lda < K");
+    LCML_CHECK_ARG((d->A || geo) && d->B && d->Y && d->scale_a && d->scale_b, "lcml_fp8_gemm: null operand");
+    LCML_CHECK_ARG(geo || d->lda >= d->K, "lcml_fp8_gemm: lda < K");
     LCML_CHECK_ARG(d->b_kmajor ? d->ldb >= d->K : d->ldb >= d->N, "lcml_fp8_gemm: ldb too small");
     const int64_t n_out = d->epilogue == LCML_EPI_SILU_MUL ? d->N / 2 : d->N;
     LCML_CHECK_ARG(d->y_col_offset >= 0 && d->ldy >= n_out + d->y_col_offset, "lcml_fp8_gemm: ldy < y_col_offset + output columns");
@@ -1150,13 +1275,23 @@ int gemm_entry(const lcml_fp8_gemm_desc *d, lcml_stream_t stream, bool force_sim
     }
     cudaStream_t st = to_cuda(stream);
     switch (d->epilogue) {
-        case LCML_EPI_NONE: return dispatch_out<LCML_EPI_NONE>(d, ep, st, force_simt);
-        case LCML_EPI_RELU: return dispatch_out<LCML_EPI_RELU>(d, ep, st, force_simt);
-        default: return dispatch_out<LCML_EPI_SILU_MUL>(d, ep, st, force_simt);
+        case LCML_EPI_NONE: return dispatch_out<LCML_EPI_NONE>(d, ep, st, force_simt, geo);
+        case LCML_EPI_RELU: return dispatch_out<LCML_EPI_RELU>(d, ep, st, force_simt, geo);
+        default: return dispatch_out<LCML_EPI_SILU_MUL>(d, ep, st, force_simt, geo);
     }
 }
 
 }// namespace gemm
+
+int fp8_gemm_implicit_conv(const lcml_fp8_gemm_desc *d, const ConvGeom &geo, cudaStream_t st) {
+    LCML_CHECK_ARG(d && d->b_kmajor && d->K % 16 == 0 && d->ldb % 16 == 0 && aligned(d->B, 16),
+                   "implicit-GEMM convolution: packed weights must be K-major with 16-byte rows");
+    LCML_CHECK_ARG(geo.x && aligned(geo.x, 16) && geo.C % 16 == 0 && geo.ktaps == geo.kH * geo.kW * geo.C &&
+                       d->M == static_cast<int64_t>(geo.N) * geo.oH * geo.oW,
+                   "implicit-GEMM convolution: inconsistent geometry");
+    return gemm::gemm_entry(d, reinterpret_cast<lcml_stream_t>(st), false, &geo);
+}
+
 }// namespace lcml
 
 extern "C" {

@@ -138,29 +138,34 @@ __device__ __forceinline__ bool scale_fast_ok(float s, float r) {
 }
 
 // Branch-free QuantizeLinear of N values (N a multiple of 4) into N / 4
-// little-endian words, bit-identical to quantize1: q = fma(v, r, +0) with
-// r = RN(1/s) (the +0 turns -0 into +0, which the codec writes as 0x00) is
-// converted by the hardware. One flag collects the values whose q lies within
-// 3 ulps of a pattern with low 19 mantissa bits 0 — every e4m3 rounding
-// boundary has that form, normal (low 20 bits 0x80000) or subnormal (low 20
-// bits 0) — and NaN codes (the hardware may write 0xff where the codec writes
-// 0x7f); if it is set, the whole block takes the exact divide + integer
-// encoder. Zeros, values that underflow to zero and infinities need no flag:
-// the hardware keeps the sign and saturates as the codec does.
+// little-endian words, bit-identical to quantize1. With r = RN(1/s),
+// r_lo = RN(r (1 - 2^-21)) < 1/s < r_hi = RN(r (1 + 2^-21)), so for every v
+// the real v/s lies between v·r_lo and v·r_hi, and RN (monotone) keeps
+// RN(v/s) between RN(v·r_lo) and RN(v·r_hi). The hardware conversion
+// cvt.rn.satfinite.e4m3x2.f32 is monotone too, so where the codes of the two
+// bounds agree they are the code of RN(v/s) (saturation at 448 included).
+// The fma with a +0 addend turns v = -0 into +0, which the codec writes as
+// 0x00. One flag per block collects disagreeing bounds, NaN codes (the
+// hardware may write 0xff where the codec writes 0x7f) and 0x80 codes (a
+// quotient that rounds to -0 in fp32 is 0x00 for the codec); if it is set,
+// the whole block takes the exact divide + integer encoder.
 template <int N>
 __device__ __forceinline__ void quantize_block_fast(const float *v, float s, float r, bool s_ok, uint32_t *w) {
+    const float r_lo = r * 0.99999952316284180f;  // 1 - 2^-21
+    const float r_hi = r * 1.00000047683715820f;  // 1 + 2^-21
     bool exact = !s_ok;
 #pragma unroll
     for (int j = 0; j < N / 4; ++j) {
-        float a[4];
+        float lo[4], hi[4];
 #pragma unroll
         for (int k = 0; k < 4; ++k) {
-            a[k] = fmaf(v[4 * j + k], r, 0.0f);
-            const uint32_t ab = __float_as_uint(a[k]) & 0x7fffffffu;
-            exact |= (((ab + 3u) & 0x7ffffu) <= 6u) & (ab - 1u < 0x7f7fffffu);
+            lo[k] = fmaf(v[4 * j + k], r_lo, 0.0f);
+            hi[k] = fmaf(v[4 * j + k], r_hi, 0.0f);
         }
-        w[j] = cvt_e4m3x2(a[0], a[1]) | (cvt_e4m3x2(a[2], a[3]) << 16);
-        exact |= __vcmpeq4(w[j] | 0x80808080u, 0xffffffffu) != 0u;
+        const uint32_t wl = cvt_e4m3x2(lo[0], lo[1]) | (cvt_e4m3x2(lo[2], lo[3]) << 16);
+        const uint32_t wh = cvt_e4m3x2(hi[0], hi[1]) | (cvt_e4m3x2(hi[2], hi[3]) << 16);
+        exact |= (wl != wh) | (__vcmpeq4(wl | 0x80808080u, 0xffffffffu) != 0u) | (__vcmpeq4(wl, 0x80808080u) != 0u);
+        w[j] = wl;
     }
     if (exact) {  // unrolled: a runtime index would move v and w to local memory
 #pragma unroll
@@ -252,6 +257,19 @@ __device__ __forceinline__ void tma_load_2d_pair(const void *tmap, uint32_t bar_
             smem_u32(smem_dst)),
         "l"(tmap), "r"(bar_cluster), "r"(x), "r"(y)
         : "memory");
+}
+
+// 16-byte cp.async global -> shared (L2 only), zero-filling the bytes past
+// `src_bytes` (0 or 16): a padded tap reads nothing and writes zeros.
+__device__ __forceinline__ void cp_async_16_zfill(uint32_t dst_smem, const void *src, uint32_t src_bytes) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst_smem), "l"(src), "r"(src_bytes)
+                 : "memory");
+}
+
+// Arrives on `bar` once every cp.async issued so far by this thread has
+// landed; the arrival counts against the barrier's expected count.
+__device__ __forceinline__ void cp_async_mbar_arrive_noinc(uint64_t *bar) {
+    asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(smem_u32(bar)) : "memory");
 }
 
 __device__ __forceinline__ void tma_prefetch_desc(const void *tmap) {

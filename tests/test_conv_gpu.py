@@ -20,7 +20,8 @@ def _t(a, dev):
     return torch.from_numpy(np.array(a, copy=True)).to(dev)
 
 
-def _run_conv(dev, X, W, bias, stride, pad, nhwc_in=True, relu=False, residual=None, out="f32", y_scale=None):
+def _run_conv(dev, X, W, bias, stride, pad, nhwc_in=True, relu=False, residual=None, out="f32", y_scale=None,
+              no_workspace=False):
     """Quantizes X (per tensor) and W (per channel) with the oracle, runs the
     GPU conv; returns (gpu NCHW fp32 result, oracle result on the dequantized
     operands, dequantization helpers)."""
@@ -74,8 +75,8 @@ def _run_conv(dev, X, W, bias, stride, pad, nhwc_in=True, relu=False, residual=N
         keep.append(yst)
         d.y_scale = yst.data_ptr()
     ws_bytes = lb.lib().lcml_fp8_conv_workspace_size(ctypes.byref(d))
-    ws = torch.empty(max(ws_bytes, 16), dtype=torch.uint8, device=dev)
-    d.workspace = ws.data_ptr()
+    ws = torch.empty(max(ws_bytes, 256), dtype=torch.uint8, device=dev)
+    d.workspace = None if no_workspace else ws.data_ptr()
     lb.check(lb.lib().lcml_fp8_conv(ctypes.byref(d), stream))
     torch.cuda.synchronize()
     ref = ref + res_ref
@@ -100,11 +101,24 @@ CASES = [
     ("nchw_c8_3x3", 2, 8, 20, 32, 3, 1, 1, False),       # 8-channel taps after the NHWC repack
     ("nhwc_c24_3x3_s2", 2, 24, 19, 48, 3, 2, 1, True),  # C padded to 32
     ("nchw_c32_5x5", 1, 32, 17, 16, 5, 1, 2, False),     # NCHW with 16-byte taps
+    ("3x3_c16_ragged", 3, 16, 13, 24, 3, 1, 1, True),    # K = 144: a partial last K-block, N = 24
+    ("5x5_s2_p2", 2, 48, 23, 96, 5, 2, 2, True),          # taps straddling K-blocks (48-channel taps)
 ]
 
 
+@pytest.fixture
+def conv_mode():
+    import luisaml_b200 as lb
+    yield lambda m: lb.lib().lcml_fp8_conv_set_mode(m)
+    lb.lib().lcml_fp8_conv_set_mode(0)
+
+
 @pytest.mark.parametrize("name,N,C,H,M,k,stride,pad,nhwc", CASES)
-def test_conv_shapes(dev, name, N, C, H, M, k, stride, pad, nhwc):
+def test_conv_shapes(dev, conv_mode, name, N, C, H, M, k, stride, pad, nhwc):
+    """Every lowering vs the oracle: direct 1x1, materialized im2col (the
+    default with a workspace) and, for NHWC inputs with C % 16 == 0, the
+    implicit GEMM (mode 2, and also without a workspace), whose result must
+    equal the materialized one bit for bit."""
     rng = np.random.default_rng(sum(name.encode()))
     X = rng.standard_normal((N, C, H, H)).astype(np.float32)
     W = (rng.standard_normal((M, C, k, k)) * np.sqrt(2.0 / (C * k * k))).astype(np.float32)
@@ -112,6 +126,13 @@ def test_conv_shapes(dev, name, N, C, H, M, k, stride, pad, nhwc):
     got, ref, ws = _run_conv(dev, X, W, bias, stride, pad, nhwc_in=nhwc)
     assert (ws == 0) == (name == "1x1_direct")
     assert_close(got, ref, what=name)
+    if nhwc and C % 16 == 0 and name != "1x1_direct":
+        conv_mode(2)
+        got_i, _, _ = _run_conv(dev, X, W, bias, stride, pad, nhwc_in=nhwc)
+        np.testing.assert_array_equal(got_i, got)
+        conv_mode(0)
+        got_n, _, _ = _run_conv(dev, X, W, bias, stride, pad, nhwc_in=nhwc, no_workspace=True)
+        np.testing.assert_array_equal(got_n, got)
 
 
 def test_conv_residual_relu_e4m3_out(dev):

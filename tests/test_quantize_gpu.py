@@ -39,11 +39,12 @@ def test_quantize_tensor_golden(dev):
     assert np.array_equal(q, g["q"])
 
 
-@pytest.mark.parametrize("scale", [1.0, 0.0123, 6.1e-3])
+@pytest.mark.parametrize("scale", [1.0, 0.0123, 6.1e-3, 4.0])
 def test_encoder_exhaustive_all_fp32_patterns(dev, scale):
     """Every one of the 2^32 fp32 bit patterns, GPU kernel vs CPU oracle; with
     scale 1 this checks the encoder itself, with the other scales the
-    multiply-by-reciprocal fast path (RN(1/s) inexact) over every input."""
+    multiply-by-reciprocal fast path (RN(1/s) inexact) over every input, and
+    with scale 4 quotients of tiny inputs that round to (signed) zero."""
     import torch
     import luisaml_b200 as lb
     one = _one(dev, scale)
