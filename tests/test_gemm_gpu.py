@@ -44,6 +44,7 @@ SHAPES = [
     (32, 512, 784),      # MLP layer 1 (K = 784, not a multiple of 128)
     (1, 4096, 4096),     # skinny decode
     (16, 4096, 4096),
+    (128, 4096, 4096),   # skinny sweep point
     (1000, 1000, 1000),  # K % 128 != 0, N < 2048
     (1024, 2048, 1024),
 ]
