@@ -295,6 +295,13 @@ __device__ __forceinline__ void store_chunk_peers(const EpiParams &ep, uint8_t *
 template <int OUT>
 constexpr int stage_bytes_per_warp() { return 2 * 32 * 32 * out_es(OUT); }
 
+// In the single-CTA kernel each warp's column factors of its current chunk
+// (gate scale, gate add, up scale, up add: 4 x 32 floats) sit in a slot after
+// all staging buffers (which keep the alignment their swizzle needs); the
+// CTA-pair kernel (long K, shared memory full) keeps them in registers.
+constexpr int kFacSlotBytes = 4 * 32 * 4;
+
+
 // Epilogue warps per CTA: 8 (two per TMEM lane quarter, each taking every
 // other 32-column chunk, so one warp's TMEM and memory latency hides behind
 // the other's math) except for SILU_MUL, whose register footprint allows 4.
@@ -302,10 +309,13 @@ template <int EPI>
 constexpr int epi_warps() { return EPI == LCML_EPI_SILU_MUL ? 4 : 8; }
 template <int EPI>
 constexpr int threads_for() { return 64 + 32 * epi_warps<EPI>(); }
-// The implicit-GEMM convolution adds a second patch-gathering warp after the
-// epilogue warps (warp 0 is the first).
-template <int EPI, bool IM2COL>
-constexpr int threads_for_conv() { return threads_for<EPI>() + (IM2COL ? 32 : 0); }
+// Single-CTA kernel: epilogue warps as in the pair kernel; the implicit-GEMM
+// convolution adds a second patch-gathering warp after the epilogue warps
+// (warp 0 is the first).
+template <int EPI, int OUT>
+constexpr int sc_epi_warps() { return EPI == LCML_EPI_SILU_MUL ? 4 : 8; }
+template <int EPI, int OUT, bool IM2COL>
+constexpr int sc_threads() { return 64 + 32 * sc_epi_warps<EPI, OUT>() + (IM2COL ? 32 : 0); }
 constexpr int kGatherRowsPerWarp = 64;
 
 template <int OUT>
@@ -365,20 +375,22 @@ __device__ __forceinline__ void prefetch_residual(const EpiParams &ep, int64_t r
 template <int EPI>
 __device__ __forceinline__ void epi_values(const EpiParams &ep, int64_t row, bool row_ok, int64_t col0, int64_t nu0,
                                            int64_t n_out, const uint32_t (&g)[32], const uint32_t (&u)[32],
-                                           ColFactors &fg, const ResidualRaw &rr, float row_scale, float row_add,
-                                           float &amax, float (&v)[32]) {
-    if (row_add != 0.0f) {
+                                           const float *fs, const float *fa, const float *fsu, const float *fau,
+                                           const ResidualRaw &rr, float row_scale, float row_add, float &amax,
+                                           float (&v)[32]) {
+    // fs / fa: B scale and beta * C along N of the 32 (gate) columns (shared
+    // memory); fsu / fau the same for the up columns
+    if (row_add == 0.0f) {
 #pragma unroll
-        for (int j = 0; j < 32; ++j) fg.add[j] += row_add;
+        for (int j = 0; j < 32; ++j) v[j] = fmaf(__uint_as_float(g[j]) * row_scale, fs[j], fa[j]);
+    } else {
+#pragma unroll
+        for (int j = 0; j < 32; ++j) v[j] = fmaf(__uint_as_float(g[j]) * row_scale, fs[j], fa[j] + row_add);
     }
-#pragma unroll
-    for (int j = 0; j < 32; ++j) v[j] = fmaf(__uint_as_float(g[j]) * row_scale, fg.scale[j], fg.add[j]);
     if (EPI == LCML_EPI_SILU_MUL) {
-        ColFactors fu;
-        load_col_factors(ep, nu0, fu);
 #pragma unroll
         for (int j = 0; j < 32; ++j) {
-            const float up = fmaf(__uint_as_float(u[j]) * row_scale, fu.scale[j], fu.add[j] + row_add);
+            const float up = fmaf(__uint_as_float(u[j]) * row_scale, fsu[j], fau[j] + row_add);
             v[j] = silu_mul(v[j], up);
         }
     }
@@ -418,11 +430,16 @@ __device__ __forceinline__ void atomic_max_abs(float *p, float v) {
 // fp32 columns), gemm column block `tn`, 32-column chunks c_first,
 // c_first + c_step, ... Chunks past the last output column are skipped; a
 // warp whose rows are all past M does nothing. `stage` is the warp's staging
-// area, `seq` its running chunk count (TMA buffer parity).
-template <int BN, int EPI, int OUT>
+// area (its two TMA buffers), `seq` its running chunk count (TMA buffer
+// parity). With FACSLOT the chunk's column factors go through the warp's slot
+// `facw` (gate scale, gate add, up scale, up add): each lane loads those of
+// one column, one chunk ahead, and the element loops read them back as
+// shared-memory broadcasts; without, every lane loads them as broadcast
+// vector loads.
+template <int BN, int EPI, int OUT, bool FACSLOT>
 __device__ __forceinline__ void epilogue_tile(const EpiParams &ep, const CUtensorMap *tmY, uint32_t taddr, int64_t row0,
                                               int tn, const OutQuant &oq, uint8_t *stage, uint32_t &seq, int c_first,
-                                              int c_step) {
+                                              int c_step, float *facw) {
     if (row0 >= ep.M) return;
     const int64_t n_out = (EPI == LCML_EPI_SILU_MUL) ? ep.N / 2 : ep.N;
     const int64_t row = row0 + static_cast<int64_t>(threadIdx.x & 31);
@@ -438,9 +455,22 @@ __device__ __forceinline__ void epilogue_tile(const EpiParams &ep, const CUtenso
         return (EPI == LCML_EPI_SILU_MUL) ? static_cast<int64_t>(tn) * (BN / 2) + c * 32
                                           : static_cast<int64_t>(tn) * BN + c * 32;
     };
-    // the residual of the next chunk is loaded while this one is processed
+    const int lane = static_cast<int>(threadIdx.x & 31);
+    // this lane's column factors of chunk c: gemm column tn*BN + c*32 + lane (and its up column)
+    auto load_fac = [&](int c, float (&f)[4]) {
+        const int64_t n = static_cast<int64_t>(tn) * BN + c * 32 + lane;
+#pragma unroll
+        for (int h = 0; h < (EPI == LCML_EPI_SILU_MUL ? 2 : 1); ++h) {
+            const int64_t nn = n + h * (BN / 2);
+            f[2 * h] = ep.sb_col ? (nn < ep.N ? __ldg(ep.sb + nn) : 0.0f) : __ldg(ep.sb);
+            f[2 * h + 1] = (ep.c_vec_mode == 3 && nn < ep.N) ? ep.beta * __ldg(ep.c_vec + nn) : 0.0f;
+        }
+    };
+    // the residual and the factors of the next chunk are loaded while this one is processed
     ResidualRaw rr_next;
     prefetch_residual(ep, row, row_ok, col_of(c_first), n_out, rr_next);
+    float fnext[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+    if (FACSLOT && c_first < kChunks) load_fac(c_first, fnext);
 #pragma unroll 1
     for (int c = c_first; c < kChunks; c += c_step) {
         const int64_t ng0 = static_cast<int64_t>(tn) * BN + c * 32;
@@ -449,14 +479,33 @@ __device__ __forceinline__ void epilogue_tile(const EpiParams &ep, const CUtenso
         uint32_t g[32], u[32];
         tmem_ld_32x32b_x32(taddr + c * 32, g);
         if (EPI == LCML_EPI_SILU_MUL) tmem_ld_32x32b_x32(taddr + BN / 2 + c * 32, u);
-        ColFactors fg;
-        load_col_factors(ep, ng0, fg);  // global loads overlap the TMEM load
         const ResidualRaw rr = rr_next;
-        if (c + c_step < kChunks) prefetch_residual(ep, row, row_ok, col_of(c + c_step), n_out, rr_next);
-        tmem_wait_ld();
         float v[32];
-        epi_values<EPI>(ep, row, row_ok, col0, ng0 + BN / 2, n_out, g, EPI == LCML_EPI_SILU_MUL ? u : g, fg, rr,
-                        row_scale, row_add, amax, v);
+        if (FACSLOT) {
+            facw[lane] = fnext[0];
+            facw[32 + lane] = fnext[1];
+            if (EPI == LCML_EPI_SILU_MUL) {
+                facw[64 + lane] = fnext[2];
+                facw[96 + lane] = fnext[3];
+            }
+            if (c + c_step < kChunks) {
+                prefetch_residual(ep, row, row_ok, col_of(c + c_step), n_out, rr_next);
+                load_fac(c + c_step, fnext);
+            }
+            __syncwarp();
+            tmem_wait_ld();
+            epi_values<EPI>(ep, row, row_ok, col0, ng0 + BN / 2, n_out, g, EPI == LCML_EPI_SILU_MUL ? u : g, facw,
+                            facw + 32, facw + 64, facw + 96, rr, row_scale, row_add, amax, v);
+            __syncwarp();  // every lane has read facw before the next chunk rewrites it
+        } else {
+            ColFactors fg, fu;
+            load_col_factors(ep, ng0, fg);  // global loads overlap the TMEM load
+            if (EPI == LCML_EPI_SILU_MUL) load_col_factors(ep, ng0 + BN / 2, fu);
+            if (c + c_step < kChunks) prefetch_residual(ep, row, row_ok, col_of(c + c_step), n_out, rr_next);
+            tmem_wait_ld();
+            epi_values<EPI>(ep, row, row_ok, col0, ng0 + BN / 2, n_out, g, EPI == LCML_EPI_SILU_MUL ? u : g, fg.scale,
+                            fg.add, fu.scale, fu.add, rr, row_scale, row_add, amax, v);
+        }
         constexpr int ES = out_es(OUT);
         if (ep.tma_store) {
             uint32_t w[8 * ES];
@@ -493,17 +542,22 @@ struct Layout {
     static constexpr int kABytes = BM * BK;
     static constexpr int kBBytes = BN * BK;
     static constexpr int kStageBytes = kABytes + kBBytes;
-    static constexpr int kTmemCols = 2 * BN;  // double-buffered fp32 accumulator
+    // fp32 accumulators in TMEM: 4 buffers for BN <= 128 (the MMA can run up to
+    // three tiles ahead of the slowest epilogue warp), 2 for BN = 256
+    static constexpr int kAcc = BN <= 128 ? 4 : 2;
+    static constexpr int kTmemCols = kAcc * BN;
     static constexpr int kBarOffset = STAGES * kStageBytes;
     static constexpr int kEpiOffset = kBarOffset + 1024;     // epilogue warps' output staging
-    static constexpr int kRowOffset = kEpiOffset + epi_warps<EPI>() * stage_bytes_per_warp<OUT>();  // conv row table
-    static constexpr int kSmemBytes = kRowOffset + BM * 8 + 1024;  // +1024 alignment
+    static constexpr int kFacOffset = kEpiOffset + sc_epi_warps<EPI, OUT>() * stage_bytes_per_warp<OUT>();  // factor slots
+    static constexpr int kRowOffset = kFacOffset + sc_epi_warps<EPI, OUT>() * kFacSlotBytes;  // conv row table
+    static constexpr int kSmemBytes = kRowOffset + BM * 8 + 1024;   // +1024 alignment
 };
 
 // The deepest operand ring (at most 8 stages) that fits beside the staging.
 template <int BN, int EPI, int OUT>
 constexpr int stages_for() {
-    const int room = kSmemLimit - 2048 - BM * 8 - epi_warps<EPI>() * stage_bytes_per_warp<OUT>();
+    const int room =
+        kSmemLimit - 2048 - BM * 8 - sc_epi_warps<EPI, OUT>() * (stage_bytes_per_warp<OUT>() + kFacSlotBytes);
     const int s = room / (BM * BK + BN * BK);
     return s > 8 ? 8 : s;
 }
@@ -519,18 +573,19 @@ constexpr int stages_for() {
 // arrives on the stage's full barrier when its copies have landed. Lane 0 of
 // warp 0 still loads B by TMA.
 template <int BN, int STAGES, int EPI, int OUT, bool IM2COL>
-__global__ void __launch_bounds__(threads_for_conv<EPI, IM2COL>(), 1)
+__global__ void __launch_bounds__(sc_threads<EPI, OUT, IM2COL>(), 1)
     k_gemm_fp8_tc(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                   const __grid_constant__ CUtensorMap tmY, int M, int N, int K, EpiParams ep, ConvGeom geo,
                   int *err) {
     using L = Layout<BN, STAGES, EPI, OUT>;
+    constexpr int kEW = sc_epi_warps<EPI, OUT>();
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint64_t *full = reinterpret_cast<uint64_t *>(smem + L::kBarOffset);
     uint64_t *empty = full + STAGES;
     uint64_t *tfull = empty + STAGES;
-    uint64_t *tempty = tfull + 2;
-    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(tempty + 2);
+    uint64_t *tempty = tfull + L::kAcc;
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(tempty + L::kAcc);
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
@@ -544,9 +599,9 @@ __global__ void __launch_bounds__(threads_for_conv<EPI, IM2COL>(), 1)
             mbar_init(&full[s], IM2COL ? 1 + 2 * 32 : 1);  // + the gathering lanes' cp.async arrivals
             mbar_init(&empty[s], 1);
         }
-        for (int b = 0; b < 2; ++b) {
+        for (int b = 0; b < L::kAcc; ++b) {
             mbar_init(&tfull[b], 1);
-            mbar_init(&tempty[b], epi_warps<EPI>());
+            mbar_init(&tempty[b], kEW);
         }
         fence_mbar_init();
     }
@@ -559,7 +614,7 @@ __global__ void __launch_bounds__(threads_for_conv<EPI, IM2COL>(), 1)
     tc_fence_after();
     const uint32_t tmem_base = *tmem_slot;
 
-    if (IM2COL && (warp == 0 || warp == 2 + epi_warps<EPI>())) {
+    if (IM2COL && (warp == 0 || warp == 2 + kEW)) {
         // ---------------- implicit-GEMM producers (two warps) ----------------
         const int half = warp == 0 ? 0 : 1;
         if (warp == 0 && lane == 0) tma_prefetch_desc(&tmB);
@@ -723,7 +778,7 @@ __global__ void __launch_bounds__(threads_for_conv<EPI, IM2COL>(), 1)
                 }
                 if (!ok) break;
                 umma_commit(&tfull[acc]);
-                if (++acc == 2) {
+                if (++acc == L::kAcc) {
                     acc = 0;
                     acc_phase ^= 1u;
                 }
@@ -731,10 +786,12 @@ __global__ void __launch_bounds__(threads_for_conv<EPI, IM2COL>(), 1)
         }
     } else {
         // ---------------- epilogue warps ----------------
-        const int quarter = warp & 3;  // TMEM lanes [32*quarter, 32*quarter+32)
-        const int half = (warp - 2) >> 2;  // which interleaved half of the chunks (8 warps)
+        const int quarter = warp & 3;    // TMEM lanes [32*quarter, 32*quarter+32)
+        const int e = warp - 2;          // epilogue warp index
+        const int phase_c = e >> 2;      // this warp takes chunks phase_c, phase_c + kEW/4, ...
         const OutQuant oq = make_out_quant<OUT>(ep);
-        uint8_t *stage = smem + L::kEpiOffset + (warp - 2) * stage_bytes_per_warp<OUT>();
+        uint8_t *stage = smem + L::kEpiOffset + e * stage_bytes_per_warp<OUT>();
+        float *facw = reinterpret_cast<float *>(smem + L::kFacOffset + e * kFacSlotBytes);
         uint32_t seq = 0;
         if (ep.tma_store && lane == 0) tma_prefetch_desc(&tmY);
         int acc = 0;
@@ -746,11 +803,11 @@ __global__ void __launch_bounds__(threads_for_conv<EPI, IM2COL>(), 1)
             tc_fence_after();
             const int64_t row0 = static_cast<int64_t>(tm) * BM + quarter * 32;
             const uint32_t taddr = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + static_cast<uint32_t>(acc * BN);
-            epilogue_tile<BN, EPI, OUT>(ep, &tmY, taddr, row0, tn, oq, stage, seq, half, epi_warps<EPI>() / 4);
+            epilogue_tile<BN, EPI, OUT, true>(ep, &tmY, taddr, row0, tn, oq, stage, seq, phase_c, kEW / 4, facw);
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(&tempty[acc]);
-            if (++acc == 2) {
+            if (++acc == L::kAcc) {
                 acc = 0;
                 acc_phase ^= 1u;
             }
@@ -938,7 +995,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(threads_for<EPI>(), 
             tc_fence_after();
             const int64_t row0 = static_cast<int64_t>(tm) * 256 + rank * 128 + quarter * 32;
             const uint32_t taddr = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + static_cast<uint32_t>(acc * BN);
-            epilogue_tile<BN, EPI, OUT>(ep, &tmY, taddr, row0, tn, oq, stage, seq, half, epi_warps<EPI>() / 4);
+            epilogue_tile<BN, EPI, OUT, false>(ep, &tmY, taddr, row0, tn, oq, stage, seq, half, epi_warps<EPI>() / 4,
+                                               nullptr);
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive_cluster(tempty_leader + 8u * static_cast<uint32_t>(acc));
@@ -1136,7 +1194,7 @@ int launch_tc(const lcml_fp8_gemm_desc *d, const EpiParams &ep, cudaStream_t st,
     if (rc) return rc;
     const int64_t tiles = ((d->M + BM - 1) / BM) * ((d->N + BN - 1) / BN);
     const int grid = static_cast<int>(tiles < sm_count() ? tiles : sm_count());
-    kern<<<grid, threads_for_conv<EPI, IM2COL>(), L::kSmemBytes, st>>>(
+    kern<<<grid, sc_threads<EPI, OUT, IM2COL>(), L::kSmemBytes, st>>>(
         ta, tb, ty, static_cast<int>(d->M), static_cast<int>(d->N), static_cast<int>(d->K), ep, geo, device_error_word());
     LCML_LAUNCHED(IM2COL ? "conv_implicit_gemm_fp8_tc" : "gemm_fp8_tc");
     return LCML_OK;

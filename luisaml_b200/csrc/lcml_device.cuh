@@ -297,6 +297,22 @@ __device__ __forceinline__ void bulk_wait_group_read() {
 // Waits until every bulk group of this thread has completed (writes done).
 __device__ __forceinline__ void bulk_wait_group_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
 
+// Barrier among `nthreads` threads (a multiple of 32) on hardware barrier
+// `id` (1..15; 0 is __syncthreads) that also ANDs a per-thread flag: all
+// participants see the same result, so they can leave a loop together.
+__device__ __forceinline__ bool named_barrier_and(int id, int nthreads, bool v) {
+    uint32_t r;
+    asm volatile(
+        "{\n\t.reg .pred pi, po;\n\t"
+        "setp.ne.u32 pi, %1, 0;\n\t"
+        "bar.red.and.pred po, %2, %3, pi;\n\t"
+        "selp.u32 %0, 1, 0, po;\n\t}"
+        : "=r"(r)
+        : "r"(static_cast<uint32_t>(v)), "r"(id), "r"(nthreads)
+        : "memory");
+    return r != 0u;
+}
+
 __device__ __forceinline__ void fence_proxy_async_smem() {
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
