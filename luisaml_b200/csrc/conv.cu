@@ -34,13 +34,16 @@ bool direct_path(const lcml_fp8_conv_desc *d) {
 // channel-padded NHWC copy of it in the workspace.
 bool needs_repack(const lcml_fp8_conv_desc *d) { return !(d->x_nhwc && d->C % 16 == 0); }
 
-// Convs whose patches the GEMM can gather itself (NHWC input, C % 16 == 0,
-// 32-bit extents; the kernel keeps each output pixel's first input row and
-// column in 16 bits): no im2col pass and no workspace.
+// Convs the GEMM can run as an implicit GEMM (TMA im2col loads of the NHWC
+// activation; C % 64 == 0; with two spatial dims the im2col bounding-box
+// corners must lie in [-128, 127], the tap offsets in [0, 255], the traversal
+// strides in 1..8): no im2col pass, no workspace.
 bool implicit_ok(const lcml_fp8_conv_desc *d) {
-    return !direct_path(d) && !needs_repack(d) && d->N * d->H * d->W * d->C < (int64_t(1) << 31) &&
-           d->N * d->oH * d->oW < (int64_t(1) << 31) && d->H < 16384 && d->W < 16384 && d->pH < 16384 &&
-           d->pW < 16384 && d->oH * d->sH + d->kH * d->dH < 16384 && d->oW * d->sW + d->kW * d->dW < 16384;
+    const int64_t up_w = (d->oW - 1) * d->sW + 1 - d->W - d->pW, up_h = (d->oH - 1) * d->sH + 1 - d->H - d->pH;
+    return !direct_path(d) && d->x_nhwc && d->C % 64 == 0 && d->N * d->H * d->W * d->C < (int64_t(1) << 31) &&
+           d->N * d->oH * d->oW < (int64_t(1) << 31) && d->pH <= 128 && d->pW <= 128 && up_w >= -128 && up_w <= 127 &&
+           up_h >= -128 && up_h <= 127 && d->sH <= 8 && d->sW <= 8 && (d->kH - 1) * d->dH <= 255 &&
+           (d->kW - 1) * d->dW <= 255 && d->kH * d->kW * d->C < (int64_t(1) << 31);
 }
 
 int64_t repack_bytes(const lcml_fp8_conv_desc *d) {
@@ -162,7 +165,7 @@ int64_t lcml_fp8_conv_packed_k(int64_t Cg, int64_t kH, int64_t kW) { return pack
 
 int64_t lcml_fp8_conv_workspace_size(const lcml_fp8_conv_desc *d) {
     if (!d) return -1;
-    if (direct_path(d)) return 0;
+    if (direct_path(d) || (implicit_ok(d) && g_conv_mode != 1)) return 0;
     return d->N * d->oH * d->oW * packed_k(d->C / (d->group > 0 ? d->group : 1), d->kH, d->kW) + repack_bytes(d);
 }
 
@@ -226,13 +229,9 @@ int lcml_fp8_conv(const lcml_fp8_conv_desc *d, lcml_stream_t stream) {
     cudaStream_t st = to_cuda(stream);
     const uint8_t *A = d->X;
     int64_t K = d->C;
-    // implicit GEMM: the GEMM's producer gathers the patches from NHWC X itself
-    // Materialized patches (im2col into the workspace, then the TMA-fed GEMM)
-    // are the faster lowering on B200; the implicit GEMM (the kernel's
-    // producer warps gather the patches with cp.async) runs when the caller
-    // passes no workspace, or when a test asks for it.
-    const bool implicit = implicit_ok(d) && aligned(d->X, 16) && g_conv_mode != 1 &&
-                          (g_conv_mode == 2 || d->workspace == nullptr);
+    // Implicit GEMM where the geometry allows it (no im2col pass, no
+    // workspace); the materialized lowering otherwise, or when a test asks.
+    const bool implicit = implicit_ok(d) && aligned(d->X, 16) && g_conv_mode != 1;
     if (implicit) {
         A = nullptr;
         K = Kp;
@@ -311,9 +310,8 @@ int lcml_fp8_conv(const lcml_fp8_conv_desc *d, lcml_stream_t stream) {
     return lcml_fp8_gemm(&g, stream);
 }
 
-// Test hook (not in the public header): 0 automatic (implicit GEMM only
-// without a workspace), 1 always materialize the patches, 2 implicit GEMM
-// wherever the geometry allows it.
+// Test hook (not in the public header): 0 automatic (implicit GEMM wherever
+// the geometry allows it), 1 always materialize the patches.
 void lcml_fp8_conv_set_mode(int mode) { g_conv_mode = mode; }
 
 }// extern "C"

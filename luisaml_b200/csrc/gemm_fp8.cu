@@ -309,13 +309,11 @@ template <int EPI>
 constexpr int epi_warps() { return EPI == LCML_EPI_SILU_MUL ? 4 : 8; }
 template <int EPI>
 constexpr int threads_for() { return 64 + 32 * epi_warps<EPI>(); }
-// Single-CTA kernel: epilogue warps as in the pair kernel; the implicit-GEMM
-// convolution adds a second patch-gathering warp after the epilogue warps
-// (warp 0 is the first).
+// Single-CTA kernel: epilogue warps as in the pair kernel.
 template <int EPI, int OUT>
 constexpr int sc_epi_warps() { return EPI == LCML_EPI_SILU_MUL ? 4 : 8; }
-template <int EPI, int OUT, bool IM2COL>
-constexpr int sc_threads() { return 64 + 32 * sc_epi_warps<EPI, OUT>() + (IM2COL ? 32 : 0); }
+template <int EPI, int OUT>
+constexpr int sc_threads() { return 64 + 32 * sc_epi_warps<EPI, OUT>(); }
 constexpr int kGatherRowsPerWarp = 64;
 
 template <int OUT>
@@ -537,10 +535,10 @@ __device__ __forceinline__ void tile_coords(int tile, int num_m, int num_n, int 
     tn = in_group / gsize;
 }
 
-template <int BN, int STAGES, int EPI, int OUT>
+template <int BN, int STAGES, int EPI, int OUT, int BKB = BK>
 struct Layout {
-    static constexpr int kABytes = BM * BK;
-    static constexpr int kBBytes = BN * BK;
+    static constexpr int kABytes = BM * BKB;
+    static constexpr int kBBytes = BN * BKB;
     static constexpr int kStageBytes = kABytes + kBBytes;
     // fp32 accumulators in TMEM: 4 buffers for BN <= 128 (the MMA can run up to
     // three tiles ahead of the slowest epilogue warp), 2 for BN = 256
@@ -549,35 +547,29 @@ struct Layout {
     static constexpr int kBarOffset = STAGES * kStageBytes;
     static constexpr int kEpiOffset = kBarOffset + 1024;     // epilogue warps' output staging
     static constexpr int kFacOffset = kEpiOffset + sc_epi_warps<EPI, OUT>() * stage_bytes_per_warp<OUT>();  // factor slots
-    static constexpr int kRowOffset = kFacOffset + sc_epi_warps<EPI, OUT>() * kFacSlotBytes;  // conv row table
-    static constexpr int kSmemBytes = kRowOffset + BM * 8 + 1024;   // +1024 alignment
+    static constexpr int kSmemBytes = kFacOffset + sc_epi_warps<EPI, OUT>() * kFacSlotBytes + 1024;  // +1024 alignment
 };
 
 // The deepest operand ring (at most 8 stages) that fits beside the staging.
-template <int BN, int EPI, int OUT>
+template <int BN, int EPI, int OUT, int BKB = BK>
 constexpr int stages_for() {
-    const int room =
-        kSmemLimit - 2048 - BM * 8 - sc_epi_warps<EPI, OUT>() * (stage_bytes_per_warp<OUT>() + kFacSlotBytes);
-    const int s = room / (BM * BK + BN * BK);
+    const int room = kSmemLimit - 2048 - sc_epi_warps<EPI, OUT>() * (stage_bytes_per_warp<OUT>() + kFacSlotBytes);
+    const int s = room / (BM * BKB + BN * BKB);
     return s > 8 ? 8 : s;
 }
 
-// IM2COL: A is not read through tmA but gathered from the NHWC activation
-// described by `geo` (implicit-GEMM convolution) by two warps (warp 0 and the
-// warp after the epilogue warps), 64 tile rows each. Per tile they write a row
-// table (image offset, first input row / column of each output pixel) to
-// shared memory; per K-block, lane l copies 16-byte chunk (l & 7) of rows
-// (l >> 3) + 4 i with cp.async (zero-filled for padding taps and K past the
-// taps), so each instruction reads whole 64- or 128-byte runs of a pixel's
-// channels, into the 128-byte swizzled layout the MMA descriptors expect, and
-// arrives on the stage's full barrier when its copies have landed. Lane 0 of
-// warp 0 still loads B by TMA.
-template <int BN, int STAGES, int EPI, int OUT, bool IM2COL>
-__global__ void __launch_bounds__(sc_threads<EPI, OUT, IM2COL>(), 1)
+// IM2COL: tmA is an im2col tensor map of the NHWC activation described by
+// `geo` (implicit-GEMM convolution): per K-block the producer loads, with one
+// TMA im2col copy, the tile's 128 output positions x BKB channels of one
+// filter tap (zero outside the image), exactly the K-major A tile the MMA
+// reads. BKB = 128 needs C % 128 == 0, BKB = 64 (64-byte rows, 64-byte
+// swizzle) C % 64 == 0.
+template <int BN, int STAGES, int EPI, int OUT, bool IM2COL, int BKB = BK>
+__global__ void __launch_bounds__(sc_threads<EPI, OUT>(), 1)
     k_gemm_fp8_tc(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                   const __grid_constant__ CUtensorMap tmY, int M, int N, int K, EpiParams ep, ConvGeom geo,
                   int *err) {
-    using L = Layout<BN, STAGES, EPI, OUT>;
+    using L = Layout<BN, STAGES, EPI, OUT, BKB>;
     constexpr int kEW = sc_epi_warps<EPI, OUT>();
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -592,11 +584,11 @@ __global__ void __launch_bounds__(sc_threads<EPI, OUT, IM2COL>(), 1)
     const int num_m = (M + BM - 1) / BM;
     const int num_n = (N + BN - 1) / BN;
     const int num_tiles = num_m * num_n;
-    const int kblocks = (K + BK - 1) / BK;
+    const int kblocks = (K + BKB - 1) / BKB;
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < STAGES; ++s) {
-            mbar_init(&full[s], IM2COL ? 1 + 2 * 32 : 1);  // + the gathering lanes' cp.async arrivals
+            mbar_init(&full[s], 1);
             mbar_init(&empty[s], 1);
         }
         for (int b = 0; b < L::kAcc; ++b) {
@@ -614,84 +606,45 @@ __global__ void __launch_bounds__(sc_threads<EPI, OUT, IM2COL>(), 1)
     tc_fence_after();
     const uint32_t tmem_base = *tmem_slot;
 
-    if (IM2COL && (warp == 0 || warp == 2 + kEW)) {
-        // ---------------- implicit-GEMM producers (two warps) ----------------
-        const int half = warp == 0 ? 0 : 1;
-        if (warp == 0 && lane == 0) tma_prefetch_desc(&tmB);
-        int2 *rows = reinterpret_cast<int2 *>(smem + L::kRowOffset) + half * kGatherRowsPerWarp;
-        int stage = 0;
-        uint32_t phase = 0;
-        int issued = 0;
-        bool ok = true;
-        const int ohw = geo.oH * geo.oW;
-        const int j = lane & 7, rsub = lane >> 3;
-        const uint32_t row_dst = static_cast<uint32_t>(half * kGatherRowsPerWarp + rsub) * 128u;
-        for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
-            int tm, tn;
-            tile_coords(tile, num_m, num_n, tm, tn);
-            __syncwarp();  // the previous tile's reads of the table are done
-#pragma unroll
-            for (int i = 0; i < 2; ++i) {
-                const int r = lane + 32 * i;
-                const int m = tm * BM + half * kGatherRowsPerWarp + r;
-                int2 info;
-                if (m < M) {
-                    const int n = m / ohw, rem = m - n * ohw;
-                    const int oh = rem / geo.oW, ow = rem - oh * geo.oW;
-                    info.x = n * geo.H * geo.W * geo.C;
-                    info.y = static_cast<int>((static_cast<uint32_t>(oh * geo.sH - geo.pH) << 16) |
-                                              (static_cast<uint32_t>(ow * geo.sW - geo.pW) & 0xffffu));
-                } else {
-                    info.x = 0;
-                    info.y = static_cast<int>(0x80008000u);  // out of range in both directions
-                }
-                rows[r] = info;
-            }
-            __syncwarp();
-            for (int kb = 0; kb < kblocks; ++kb) {
-                if (!mbar_wait(&empty[stage], phase ^ 1u, err, kDevTimeoutProducer)) {
-                    ok = false;
-                    break;
-                }
-                uint8_t *sa = smem + stage * L::kStageBytes;
-                if (warp == 0 && lane == 0) {
-                    mbar_arrive_expect_tx(&full[stage], L::kBBytes);
-                    tma_load_2d(&tmB, &full[stage], sa + L::kABytes, kb * BK, tn * BN);
-                }
-                // this lane's K chunk: tap (kh, kw), channel c
-                const int k = kb * BK + j * 16;
-                int dh = -65536, dw = 0, c = 0;
-                if (k < geo.ktaps) {
-                    const int t = k / geo.C;
-                    c = k - t * geo.C;
-                    const int kh = t / geo.kW;
-                    dh = kh * geo.dH;
-                    dw = (t - kh * geo.kW) * geo.dW;
-                }
-                const uint32_t dst0 = smem_u32(sa) + row_dst;
-#pragma unroll
-                for (int i = 0; i < kGatherRowsPerWarp / 4; ++i) {
-                    const int r = 4 * i + rsub;
-                    const int2 info = rows[r];
-                    const int ih = (info.y >> 16) + dh;
-                    const int iw = static_cast<int>(static_cast<int16_t>(info.y & 0xffff)) + dw;
-                    const bool in = static_cast<unsigned>(ih) < static_cast<unsigned>(geo.H) &&
-                                    static_cast<unsigned>(iw) < static_cast<unsigned>(geo.W);
-                    const uint8_t *src = in ? geo.x + (info.x + (ih * geo.W + iw) * geo.C + c) : geo.x;
-                    // row r of this warp's half; 16-byte chunk j swizzled by the row's low 3 bits
-                    const uint32_t sw = static_cast<uint32_t>((rsub + 4 * i) & 7);
-                    cp_async_16_zfill(dst0 + static_cast<uint32_t>(4 * i) * 128u + ((static_cast<uint32_t>(j) ^ sw) << 4),
-                                      src, in ? 16u : 0u);
-                }
-                cp_async_mbar_arrive_noinc(&full[stage]);
-                ++issued;
-                if (++stage == STAGES) {
-                    stage = 0;
-                    phase ^= 1u;
+    if (IM2COL && warp == 0) {
+        // ---------------- TMA im2col producer (implicit-GEMM convolution) ----------------
+        if (elect_one()) {
+            tma_prefetch_desc(&tmA);
+            tma_prefetch_desc(&tmB);
+            int stage = 0;
+            uint32_t phase = 0;
+            int issued = 0;
+            bool ok = true;
+            const int ohw = geo.oH * geo.oW;
+            const int cblocks = geo.C / BKB;  // K-blocks per filter tap
+            for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
+                int tm, tn;
+                tile_coords(tile, num_m, num_n, tm, tn);
+                // first output position of the tile -> its input corner (rows past M read zeros: image N)
+                const int m0 = tm * BM;
+                const int n0 = m0 / ohw, rem = m0 - n0 * ohw;
+                const int oh0 = rem / geo.oW, ow0 = rem - oh0 * geo.oW;
+                const int w0 = ow0 * geo.sW - geo.pW, h0 = oh0 * geo.sH - geo.pH;
+                for (int kb = 0; kb < kblocks; ++kb) {
+                    if (!mbar_wait(&empty[stage], phase ^ 1u, err, kDevTimeoutProducer)) {
+                        ok = false;
+                        break;
+                    }
+                    uint8_t *sa = smem + stage * L::kStageBytes;
+                    uint8_t *sb = sa + L::kABytes;
+                    const int tap = kb / cblocks, c0 = (kb - tap * cblocks) * BKB;
+                    const int kh = tap / geo.kW, kw = tap - kh * geo.kW;
+                    mbar_arrive_expect_tx(&full[stage], L::kStageBytes);
+                    tma_load_im2col_4d(&tmA, &full[stage], sa, c0, w0, h0, n0, static_cast<uint16_t>(kw * geo.dW),
+                                       static_cast<uint16_t>(kh * geo.dH));
+                    tma_load_2d(&tmB, &full[stage], sb, kb * BKB, tn * BN);
+                    ++issued;
+                    if (++stage == STAGES) {
+                        stage = 0;
+                        phase ^= 1u;
+                    }
                 }
             }
-        }
-        if (warp == 0 && lane == 0) {
             const int pending = issued < STAGES ? issued : STAGES;
             for (int i = 0; i < pending; ++i) {
                 if (--stage < 0) {
@@ -701,7 +654,6 @@ __global__ void __launch_bounds__(sc_threads<EPI, OUT, IM2COL>(), 1)
                 mbar_wait(&full[stage], phase, err, kDevTimeoutDrain);
             }
         }
-        asm volatile("cp.async.wait_all;" ::: "memory");
     } else if (warp == 0) {
         // ---------------- TMA producer ----------------
         if (elect_one()) {
@@ -722,8 +674,8 @@ __global__ void __launch_bounds__(sc_threads<EPI, OUT, IM2COL>(), 1)
                     uint8_t *sa = smem + stage * L::kStageBytes;
                     uint8_t *sb = sa + L::kABytes;
                     mbar_arrive_expect_tx(&full[stage], L::kStageBytes);
-                    tma_load_2d(&tmA, &full[stage], sa, kb * BK, tm * BM);
-                    tma_load_2d(&tmB, &full[stage], sb, kb * BK, tn * BN);
+                    tma_load_2d(&tmA, &full[stage], sa, kb * BKB, tm * BM);
+                    tma_load_2d(&tmB, &full[stage], sb, kb * BKB, tn * BN);
                     ++issued;
                     if (++stage == STAGES) {
                         stage = 0;
@@ -760,14 +712,13 @@ __global__ void __launch_bounds__(sc_threads<EPI, OUT, IM2COL>(), 1)
                         ok = false;
                         break;
                     }
-                    if (IM2COL) fence_proxy_async_smem();  // cp.async (generic proxy) writes -> MMA reads
                     tc_fence_after();
                     const uint32_t a_addr = smem_u32(smem + stage * L::kStageBytes);
                     const uint32_t b_addr = a_addr + L::kABytes;
 #pragma unroll
-                    for (int k = 0; k < BK / UMMA_K; ++k) {
-                        const uint64_t adesc = sdesc_kmajor_sw128(a_addr + k * UMMA_K);
-                        const uint64_t bdesc = sdesc_kmajor_sw128(b_addr + k * UMMA_K);
+                    for (int k = 0; k < BKB / UMMA_K; ++k) {
+                        const uint64_t adesc = sdesc_kmajor<BKB>(a_addr + k * UMMA_K);
+                        const uint64_t bdesc = sdesc_kmajor<BKB>(b_addr + k * UMMA_K);
                         umma_f8f6f4(d_tmem, adesc, bdesc, idesc, (kb | k) != 0 ? 1u : 0u);
                     }
                     umma_commit(&empty[stage]);
@@ -1123,17 +1074,54 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
 
 // 2-D e4m3 K-major operand: `rows` rows of `k` bytes, row stride `ld` bytes,
 // box = [box_rows x 128 B] with the 128-byte swizzle.
-int make_tmap(CUtensorMap *map, const void *ptr, int64_t k, int64_t rows, int64_t ld, int box_rows) {
+int make_tmap(CUtensorMap *map, const void *ptr, int64_t k, int64_t rows, int64_t ld, int box_rows, int bkb = BK) {
     auto fn = encode_fn();
     if (!fn) return set_error(LCML_ERR_CUDA, "cuTensorMapEncodeTiled is not available from the driver");
     cuuint64_t dims[2] = {static_cast<cuuint64_t>(k), static_cast<cuuint64_t>(rows)};
     cuuint64_t strides[1] = {static_cast<cuuint64_t>(ld)};
-    cuuint32_t box[2] = {static_cast<cuuint32_t>(BK), static_cast<cuuint32_t>(box_rows)};
+    cuuint32_t box[2] = {static_cast<cuuint32_t>(bkb), static_cast<cuuint32_t>(box_rows)};
     cuuint32_t estr[2] = {1, 1};
     CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void *>(ptr), dims, strides, box, estr,
-                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+                    CU_TENSOR_MAP_INTERLEAVE_NONE, bkb == 128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B,
+                    CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (r != CUDA_SUCCESS) return set_error(LCML_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", static_cast<int>(r));
+    return LCML_OK;
+}
+
+// im2col tensor map of the NHWC e4m3 activation of `g`: boxes of 128 output
+// positions x bkb channels. The bounding box runs from -pad to the last
+// position a filter tap 0 reads ({w, h} order), traversed with the conv
+// strides; positions outside the image load zeros.
+int make_tmap_im2col(CUtensorMap *map, const ConvGeom &g, int bkb) {
+    using Fn = PFN_cuTensorMapEncodeIm2col_v12000;
+    static Fn fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void *p = nullptr;
+        cudaDriverEntryPointQueryResult q{};
+        if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeIm2col", &p, 12000, cudaEnableDefault, &q) ==
+                cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<Fn>(p);
+    });
+    if (!fn) return set_error(LCML_ERR_CUDA, "cuTensorMapEncodeIm2col is not available from the driver");
+    const uint64_t C = g.C, W = g.W, H = g.H, N = g.N;
+    cuuint64_t dims[4] = {C, W, H, N};
+    cuuint64_t strides[3] = {C, W * C, H * W * C};
+    int lower[2] = {-g.pW, -g.pH};
+    int upper[2] = {(g.oW - 1) * g.sW + 1 - g.W - g.pW, (g.oH - 1) * g.sH + 1 - g.H - g.pH};
+    cuuint32_t estr[4] = {1, static_cast<cuuint32_t>(g.sW), static_cast<cuuint32_t>(g.sH), 1};
+    CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 4, const_cast<uint8_t *>(g.x), dims, strides, lower, upper,
+                    static_cast<cuuint32_t>(bkb), BM, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                    bkb == 128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B,
+                    CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS)
+        return set_error(LCML_ERR_CUDA, "cuTensorMapEncodeIm2col failed (%d)", static_cast<int>(r));
+    // Drivers up to 13.1 mis-encode one field of im2col maps over tensors
+    // smaller than 128 KiB; CUTLASS clears that bit (bit 21 of word 1) for them.
+    int drv = 0;
+    if (cudaDriverGetVersion(&drv) == cudaSuccess && drv <= 13010 && N * H * W * C < 131072)
+        reinterpret_cast<uint64_t *>(map)[1] &= ~(uint64_t(1) << 21);
     return LCML_OK;
 }
 
@@ -1168,12 +1156,12 @@ int output_tmap(const lcml_fp8_gemm_desc *d, const EpiParams &ep, CUtensorMap *t
     return make_tmap_out(ty, static_cast<uint8_t *>(d->Y) + d->y_col_offset * ES, n_out, d->M, d->ldy * ES, ES);
 }
 
-template <int BN, int EPI, int OUT, bool IM2COL = false>
+template <int BN, int EPI, int OUT, bool IM2COL = false, int BKB = BK>
 int launch_tc(const lcml_fp8_gemm_desc *d, const EpiParams &ep, cudaStream_t st, const ConvGeom &geo = ConvGeom{}) {
-    constexpr int STAGES = stages_for<BN, EPI, OUT>();
-    using L = Layout<BN, STAGES, EPI, OUT>;
+    constexpr int STAGES = stages_for<BN, EPI, OUT, BKB>();
+    using L = Layout<BN, STAGES, EPI, OUT, BKB>;
     static_assert(STAGES >= 3 && L::kSmemBytes <= kSmemLimit, "shared memory layout does not fit");
-    auto kern = k_gemm_fp8_tc<BN, STAGES, EPI, OUT, IM2COL>;
+    auto kern = k_gemm_fp8_tc<BN, STAGES, EPI, OUT, IM2COL, BKB>;
     static std::once_flag once;
     static cudaError_t attr_err = cudaSuccess;
     std::call_once(once, [&] {
@@ -1183,18 +1171,16 @@ int launch_tc(const lcml_fp8_gemm_desc *d, const EpiParams &ep, cudaStream_t st,
         return set_error(LCML_ERR_CUDA, "cudaFuncSetAttribute(smem=%d) failed: %s", L::kSmemBytes,
                          cudaGetErrorString(attr_err));
     CUtensorMap ta, tb;
-    int rc = LCML_OK;
-    if (IM2COL) memset(&ta, 0, sizeof(ta));  // A is gathered in the kernel
-    else rc = make_tmap(&ta, d->A, d->K, d->M, d->lda, BM);
+    int rc = IM2COL ? make_tmap_im2col(&ta, geo, BKB) : make_tmap(&ta, d->A, d->K, d->M, d->lda, BM, BKB);
     if (rc) return rc;
-    rc = make_tmap(&tb, d->B, d->K, d->N, d->ldb, BN);
+    rc = make_tmap(&tb, d->B, d->K, d->N, d->ldb, BN, BKB);
     if (rc) return rc;
     CUtensorMap ty;
     rc = output_tmap<EPI, OUT>(d, ep, &ty);
     if (rc) return rc;
     const int64_t tiles = ((d->M + BM - 1) / BM) * ((d->N + BN - 1) / BN);
     const int grid = static_cast<int>(tiles < sm_count() ? tiles : sm_count());
-    kern<<<grid, sc_threads<EPI, OUT, IM2COL>(), L::kSmemBytes, st>>>(
+    kern<<<grid, sc_threads<EPI, OUT>(), L::kSmemBytes, st>>>(
         ta, tb, ty, static_cast<int>(d->M), static_cast<int>(d->N), static_cast<int>(d->K), ep, geo, device_error_word());
     LCML_LAUNCHED(IM2COL ? "conv_implicit_gemm_fp8_tc" : "gemm_fp8_tc");
     return LCML_OK;
@@ -1247,9 +1233,14 @@ int dispatch(const lcml_fp8_gemm_desc *d, const EpiParams &ep, cudaStream_t st, 
         if constexpr (EPI == LCML_EPI_SILU_MUL) {
             return set_error(LCML_ERR_UNSUPPORTED, "implicit-GEMM convolution: SILU_MUL epilogue");
         } else {
-            if (d->N <= 64) return launch_tc<64, EPI, OUT, true>(d, ep, st, *geo);
-            if (d->N >= 2048) return launch_tc<256, EPI, OUT, true>(d, ep, st, *geo);
-            return launch_tc<128, EPI, OUT, true>(d, ep, st, *geo);
+            if (geo->C % 128 == 0) {
+                if (d->N <= 64) return launch_tc<64, EPI, OUT, true, 128>(d, ep, st, *geo);
+                if (d->N >= 2048) return launch_tc<256, EPI, OUT, true, 128>(d, ep, st, *geo);
+                return launch_tc<128, EPI, OUT, true, 128>(d, ep, st, *geo);
+            }
+            if (d->N <= 64) return launch_tc<64, EPI, OUT, true, 64>(d, ep, st, *geo);
+            if (d->N >= 2048) return launch_tc<256, EPI, OUT, true, 64>(d, ep, st, *geo);
+            return launch_tc<128, EPI, OUT, true, 64>(d, ep, st, *geo);
         }
     }
     const bool tma_ok = !force_simt && d->b_kmajor && (d->K % 16 == 0) && (d->lda % 16 == 0) && (d->ldb % 16 == 0) &&
@@ -1344,8 +1335,8 @@ int gemm_entry(const lcml_fp8_gemm_desc *d, lcml_stream_t stream, bool force_sim
 int fp8_gemm_implicit_conv(const lcml_fp8_gemm_desc *d, const ConvGeom &geo, cudaStream_t st) {
     LCML_CHECK_ARG(d && d->b_kmajor && d->K % 16 == 0 && d->ldb % 16 == 0 && aligned(d->B, 16),
                    "implicit-GEMM convolution: packed weights must be K-major with 16-byte rows");
-    LCML_CHECK_ARG(geo.x && aligned(geo.x, 16) && geo.C % 16 == 0 && geo.ktaps == geo.kH * geo.kW * geo.C &&
-                       d->M == static_cast<int64_t>(geo.N) * geo.oH * geo.oW,
+    LCML_CHECK_ARG(geo.x && aligned(geo.x, 16) && geo.C % 64 == 0 && geo.ktaps == geo.kH * geo.kW * geo.C &&
+                       d->K == geo.ktaps && d->M == static_cast<int64_t>(geo.N) * geo.oH * geo.oW,
                    "implicit-GEMM convolution: inconsistent geometry");
     return gemm::gemm_entry(d, reinterpret_cast<lcml_stream_t>(st), false, &geo);
 }

@@ -272,6 +272,20 @@ __device__ __forceinline__ void cp_async_mbar_arrive_noinc(uint64_t *bar) {
     asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(smem_u32(bar)) : "memory");
 }
 
+// TMA load in im2col mode from an NHWC activation: the box is `pixels`
+// consecutive output positions (walked through the map's bounding box with
+// its traversal strides, wrapping rows and images) x `channels` channels
+// starting at channel c of input position (w, h) of image n, shifted by the
+// filter tap (off_w, off_h); positions outside the image read zeros.
+__device__ __forceinline__ void tma_load_im2col_4d(const void *tmap, uint64_t *bar, void *smem_dst, int c, int w, int h,
+                                                   int n, uint16_t off_w, uint16_t off_h) {
+    asm volatile(
+        "cp.async.bulk.tensor.4d.shared::cluster.global.im2col.mbarrier::complete_tx::bytes"
+        " [%0], [%1, {%3, %4, %5, %6}], [%2], {%7, %8};" ::"r"(smem_u32(smem_dst)),
+        "l"(tmap), "r"(smem_u32(bar)), "r"(c), "r"(w), "r"(h), "r"(n), "h"(off_w), "h"(off_h)
+        : "memory");
+}
+
 __device__ __forceinline__ void tma_prefetch_desc(const void *tmap) {
     asm volatile("prefetch.tensormap [%0];" ::"l"(tmap) : "memory");
 }
@@ -478,6 +492,24 @@ __device__ __forceinline__ uint64_t sdesc_kmajor_sw128(uint32_t smem_addr) {
     d |= static_cast<uint64_t>(1u) << 46;
     d |= static_cast<uint64_t>(2u) << 61;
     return d;
+}
+
+// The same for a K-major operand with 64-byte rows (64 e4m3 per K-block)
+// staged with the 64-byte swizzle: 8-row groups 512 bytes apart, layout
+// SWIZZLE_64B = 4.
+__device__ __forceinline__ uint64_t sdesc_kmajor_sw64(uint32_t smem_addr) {
+    uint64_t d = 0;
+    d |= static_cast<uint64_t>((smem_addr & 0x3ffffu) >> 4);
+    d |= static_cast<uint64_t>(1u) << 16;
+    d |= static_cast<uint64_t>(512u >> 4) << 32;
+    d |= static_cast<uint64_t>(1u) << 46;
+    d |= static_cast<uint64_t>(4u) << 61;
+    return d;
+}
+
+template <int BKB>
+__device__ __forceinline__ uint64_t sdesc_kmajor(uint32_t smem_addr) {
+    return BKB == 128 ? sdesc_kmajor_sw128(smem_addr) : sdesc_kmajor_sw64(smem_addr);
 }
 
 // Instruction descriptor for kind::f8f6f4: D f32 [4,6)=1, A/B e4m3 [7,10)=[10,13)=0,

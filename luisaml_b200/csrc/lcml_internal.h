@@ -31,13 +31,13 @@ int *device_error_word();
 __host__ __device__ inline bool aligned(const void *p, uintptr_t a) { return (reinterpret_cast<uintptr_t>(p) & (a - 1)) == 0; }
 
 // Geometry of an implicit-GEMM convolution: the GEMM's A operand (rows =
-// output pixels (n, oh, ow), K = (kh, kw, c) with c fastest) is gathered from
-// the NHWC activation by the GEMM kernel's producer warp instead of being
-// materialized by an im2col pass. 32-bit extents (the caller checks).
+// output pixels (n, oh, ow), K = (kh, kw, c) with c fastest) is loaded from
+// the NHWC activation by TMA im2col copies in the GEMM kernel instead of
+// being materialized by an im2col pass. 32-bit extents (the caller checks).
 struct ConvGeom {
-    const uint8_t *x;  // NHWC e4m3 activation, C channels, C % 16 == 0, 16-byte aligned
+    const uint8_t *x;  // NHWC e4m3 activation, C channels, C % 64 == 0, 16-byte aligned
     int N, H, W, C, oH, oW, kH, kW, sH, sW, pH, pW, dH, dW;
-    int ktaps;         // kH * kW * C: K indices past it are zero
+    int ktaps;         // kH * kW * C (the GEMM's K)
 };
 
 // lcml_fp8_gemm whose A is gathered through `geo` (d->A and d->lda unused;

@@ -21,7 +21,7 @@ def _t(a, dev):
 
 
 def _run_conv(dev, X, W, bias, stride, pad, nhwc_in=True, relu=False, residual=None, out="f32", y_scale=None,
-              no_workspace=False):
+              no_workspace=False, dil=1):
     """Quantizes X (per tensor) and W (per channel) with the oracle, runs the
     GPU conv; returns (gpu NCHW fp32 result, oracle result on the dequantized
     operands, dequantization helpers)."""
@@ -33,10 +33,10 @@ def _run_conv(dev, X, W, bias, stride, pad, nhwc_in=True, relu=False, residual=N
     xq = oracle.quantize(X, sx)
     sw = np.array([oracle.scale_from_amax(oracle.amax(W[m])) for m in range(M)], dtype=np.float32)
     wq = oracle.quantize(W, sw, axis=0)
-    oH = (H + 2 * pad - kH) // stride + 1
-    oW = (Wd + 2 * pad - kW) // stride + 1
+    oH = (H + 2 * pad - dil * (kH - 1) - 1) // stride + 1
+    oW = (Wd + 2 * pad - dil * (kW - 1) - 1) // stride + 1
     ref = oracle.conv2d(oracle.dequantize(xq, sx), oracle.dequantize(wq, sw, axis=0), bias, strides=(stride, stride),
-                        pads=(pad, pad, pad, pad))
+                        pads=(pad, pad, pad, pad), dilations=(dil, dil))
     Kp = lb.lib().lcml_fp8_conv_packed_k(C, kH, kW)
     Wp = torch.empty((M, Kp), dtype=torch.uint8, device=dev)
     stream = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
@@ -51,7 +51,7 @@ def _run_conv(dev, X, W, bias, stride, pad, nhwc_in=True, relu=False, residual=N
     d.N, d.C, d.H, d.W, d.M, d.kH, d.kW, d.oH, d.oW = N, C, H, Wd, M, kH, kW, oH, oW
     d.sH = d.sW = stride
     d.pH = d.pW = pad
-    d.dH = d.dW = 1
+    d.dH = d.dW = dil
     d.group = 1
     d.X, d.x_nhwc, d.scale_x = xt.data_ptr(), int(nhwc_in), sxt.data_ptr()
     d.Wp, d.scale_w, d.scale_w_mode = Wp.data_ptr(), swt.data_ptr(), lb.SCALE_AXIS
@@ -91,18 +91,24 @@ def _run_conv(dev, X, W, bias, stride, pad, nhwc_in=True, relu=False, residual=N
 
 
 CASES = [
-    # name, N, C, H, M, k, stride, pad, nhwc
-    ("stem7x7s2_nchw", 2, 3, 64, 64, 7, 2, 3, False),
-    ("1x1_direct", 2, 64, 56, 256, 1, 1, 0, True),
-    ("3x3_pad1", 2, 64, 56, 64, 3, 1, 1, True),
-    ("3x3_s2", 2, 128, 56, 128, 3, 2, 1, True),
-    ("1x1_s2_downsample", 2, 256, 56, 512, 1, 2, 0, True),
-    ("3x3_7x7map", 4, 512, 7, 512, 3, 1, 1, True),
-    ("nchw_c8_3x3", 2, 8, 20, 32, 3, 1, 1, False),       # 8-channel taps after the NHWC repack
-    ("nhwc_c24_3x3_s2", 2, 24, 19, 48, 3, 2, 1, True),  # C padded to 32
-    ("nchw_c32_5x5", 1, 32, 17, 16, 5, 1, 2, False),     # NCHW with 16-byte taps
-    ("3x3_c16_ragged", 3, 16, 13, 24, 3, 1, 1, True),    # K = 144: a partial last K-block, N = 24
-    ("5x5_s2_p2", 2, 48, 23, 96, 5, 2, 2, True),          # taps straddling K-blocks (48-channel taps)
+    # name, N, C, H, M, k, stride, pad, nhwc, dilation
+    ("stem7x7s2_nchw", 2, 3, 64, 64, 7, 2, 3, False, 1),
+    ("1x1_direct", 2, 64, 56, 256, 1, 1, 0, True, 1),
+    ("3x3_pad1", 2, 64, 56, 64, 3, 1, 1, True, 1),
+    ("3x3_s2", 2, 128, 56, 128, 3, 2, 1, True, 1),
+    ("1x1_s2_downsample", 2, 256, 56, 512, 1, 2, 0, True, 1),
+    ("3x3_7x7map", 4, 512, 7, 512, 3, 1, 1, True, 1),
+    ("nchw_c8_3x3", 2, 8, 20, 32, 3, 1, 1, False, 1),       # 8-channel taps after the NHWC repack
+    ("nhwc_c24_3x3_s2", 2, 24, 19, 48, 3, 2, 1, True, 1),  # C padded to 32
+    ("nchw_c32_5x5", 1, 32, 17, 16, 5, 1, 2, False, 1),     # NCHW with 16-byte taps
+    ("3x3_c16_ragged", 3, 16, 13, 24, 3, 1, 1, True, 1),    # K = 144: a partial last K-block, N = 24
+    ("5x5_s2_p2", 2, 48, 23, 96, 5, 2, 2, True, 1),          # taps straddling K-blocks (48-channel taps)
+    # implicit GEMM (TMA im2col) edge cases
+    ("3x3_c192_ragged_tiles", 3, 192, 13, 96, 3, 1, 1, True, 1),  # 64-byte K-blocks; tiles straddle images
+    ("7x7_s2_p3_c64", 2, 64, 30, 64, 7, 2, 3, True, 1),           # wide padding, odd output extent
+    ("3x3_dil2_c128", 2, 128, 17, 128, 3, 1, 2, True, 2),         # dilated taps
+    ("2x2_s2_nopad_c64", 1, 64, 15, 32, 2, 2, 0, True, 1),        # input rows/cols no tap reads
+    ("3x3_s3_c128", 2, 128, 20, 64, 3, 3, 0, True, 1),            # traversal stride 3
 ]
 
 
@@ -113,25 +119,31 @@ def conv_mode():
     lb.lib().lcml_fp8_conv_set_mode(0)
 
 
-@pytest.mark.parametrize("name,N,C,H,M,k,stride,pad,nhwc", CASES)
-def test_conv_shapes(dev, conv_mode, name, N, C, H, M, k, stride, pad, nhwc):
-    """Every lowering vs the oracle: direct 1x1, materialized im2col (the
-    default with a workspace) and, for NHWC inputs with C % 16 == 0, the
-    implicit GEMM (mode 2, and also without a workspace), whose result must
-    equal the materialized one bit for bit."""
+def _implicit(C, k, stride, pad, nhwc):
+    return nhwc and C % 64 == 0 and not (k == 1 and stride == 1 and pad == 0)
+
+
+@pytest.mark.parametrize("name,N,C,H,M,k,stride,pad,nhwc,dil", CASES)
+def test_conv_shapes(dev, conv_mode, name, N, C, H, M, k, stride, pad, nhwc, dil):
+    """Every lowering vs the oracle: direct 1x1, materialized im2col (mode 1)
+    and, for NHWC inputs with C % 64 == 0, the implicit GEMM (TMA im2col
+    loads; the default there, with or without a workspace), whose result
+    must equal the materialized one bit for bit."""
     rng = np.random.default_rng(sum(name.encode()))
     X = rng.standard_normal((N, C, H, H)).astype(np.float32)
     W = (rng.standard_normal((M, C, k, k)) * np.sqrt(2.0 / (C * k * k))).astype(np.float32)
     bias = (rng.standard_normal(M) * 0.01).astype(np.float32)
-    got, ref, ws = _run_conv(dev, X, W, bias, stride, pad, nhwc_in=nhwc)
+    conv_mode(1)
+    got, ref, ws = _run_conv(dev, X, W, bias, stride, pad, nhwc_in=nhwc, dil=dil)
     assert (ws == 0) == (name == "1x1_direct")
     assert_close(got, ref, what=name)
-    if nhwc and C % 16 == 0 and name != "1x1_direct":
-        conv_mode(2)
-        got_i, _, _ = _run_conv(dev, X, W, bias, stride, pad, nhwc_in=nhwc)
-        np.testing.assert_array_equal(got_i, got)
-        conv_mode(0)
-        got_n, _, _ = _run_conv(dev, X, W, bias, stride, pad, nhwc_in=nhwc, no_workspace=True)
+    conv_mode(0)
+    got_a, _, ws_a = _run_conv(dev, X, W, bias, stride, pad, nhwc_in=nhwc, dil=dil)
+    implicit = _implicit(C, k, stride, pad, nhwc)
+    assert (ws_a == 0) == (implicit or name == "1x1_direct")
+    np.testing.assert_array_equal(got_a, got)
+    if implicit:
+        got_n, _, _ = _run_conv(dev, X, W, bias, stride, pad, nhwc_in=nhwc, no_workspace=True, dil=dil)
         np.testing.assert_array_equal(got_n, got)
 
 
