@@ -72,11 +72,33 @@ __device__ __forceinline__ float load_cmat(const EpiParams &ep, int64_t row, int
     return reinterpret_cast<const float *>(ep.c_mat)[row * ep.ldc + col];
 }
 
+// Output quantization constants of one launch: y_scale, RN(1 / y_scale) and
+// whether the multiply-by-reciprocal rule (quantize_block_rcp) applies; for
+// unusual scales (subnormal, or a reciprocal that is not a normal float)
+// every element takes the exact divide of quantize1.
+struct OutQuant {
+    float ys, r;
+    bool s_ok;
+};
+
 template <int OUT>
-__device__ __forceinline__ void store_out(void *y, int64_t ldy, int64_t row, int64_t col, float v, float ys) {
+__device__ __forceinline__ OutQuant make_out_quant(const EpiParams &ep) {
+    OutQuant q{1.0f, 1.0f, false};
+    if (OUT == kOutE4M3) {
+        q.ys = __ldg(ep.y_scale);
+        q.r = __frcp_rn(q.ys);
+        q.s_ok = scale_fast_ok(q.ys, q.r);
+    }
+    return q;
+}
+
+template <int OUT>
+__device__ __forceinline__ void store_out(void *y, int64_t ldy, int64_t row, int64_t col, float v, const OutQuant &q) {
     if (OUT == kOutF32) reinterpret_cast<float *>(y)[row * ldy + col] = v;
     else if (OUT == kOutBF16) reinterpret_cast<__nv_bfloat16 *>(y)[row * ldy + col] = __float2bfloat16_rn(v);
-    else reinterpret_cast<uint8_t *>(y)[row * ldy + col] = static_cast<uint8_t>(quantize1(v, ys));
+    else
+        reinterpret_cast<uint8_t *>(y)[row * ldy + col] =
+            static_cast<uint8_t>(q.s_ok ? quantize_rcp1(v, q.r) : quantize1(v, q.ys));
 }
 
 // Per-column factors of 32 consecutive gemm columns [n0, n0+32): the B scale
@@ -194,26 +216,8 @@ __device__ __forceinline__ void load_cmat32(const EpiParams &ep, int64_t row, in
 
 constexpr int out_es(int out) { return out == kOutF32 ? 4 : (out == kOutBF16 ? 2 : 1); }
 
-// Output quantization constants of one launch: y_scale, RN(1 / y_scale) and
-// whether the multiply-by-reciprocal path of quantize2_fast applies.
-struct OutQuant {
-    float ys, r;
-    bool s_ok;
-};
-
-template <int OUT>
-__device__ __forceinline__ OutQuant make_out_quant(const EpiParams &ep) {
-    OutQuant q{1.0f, 1.0f, false};
-    if (OUT == kOutE4M3) {
-        q.ys = __ldg(ep.y_scale);
-        q.r = __frcp_rn(q.ys);
-        q.s_ok = scale_fast_ok(q.ys, q.r);
-    }
-    return q;
-}
-
 // 32 values -> the output's bytes as 8 * element-size little-endian words
-// (e4m3 bit-identical to quantize1 through quantize2_fast).
+// (e4m3 by the epilogue quantization rule of quantize_block_rcp).
 template <int OUT>
 __device__ __forceinline__ void pack32(const float (&v)[32], const OutQuant &q, uint32_t (&w)[8 * out_es(OUT)]) {
     if (OUT == kOutF32) {
@@ -225,8 +229,13 @@ __device__ __forceinline__ void pack32(const float (&v)[32], const OutQuant &q, 
             __nv_bfloat162 h = __floats2bfloat162_rn(v[2 * j], v[2 * j + 1]);
             w[j] = *reinterpret_cast<uint32_t *>(&h);
         }
+    } else if (q.s_ok) {
+        quantize_block_rcp<32>(v, q.r, w);
     } else {
-        quantize_block_fast<32>(v, q.ys, q.r, q.s_ok, w);
+#pragma unroll
+        for (int j = 0; j < 8; ++j)
+            w[j] = quantize1(v[4 * j], q.ys) | (quantize1(v[4 * j + 1], q.ys) << 8) |
+                   (quantize1(v[4 * j + 2], q.ys) << 16) | (quantize1(v[4 * j + 3], q.ys) << 24);
     }
 }
 
@@ -248,7 +257,7 @@ __device__ __forceinline__ void store_row32_to(const EpiParams &ep, void *ybase,
     }
 #pragma unroll
     for (int j = 0; j < 32; ++j)
-        if (col0 + j < n_out) store_out<OUT>(ybase, ep.ldy, row, ocol0 + j, v[j], q.ys);
+        if (col0 + j < n_out) store_out<OUT>(ybase, ep.ldy, row, ocol0 + j, v[j], q);
 }
 
 // Warp-cooperative store of a 32-row x 32-column chunk through shared memory
@@ -378,7 +387,10 @@ __device__ __forceinline__ void epi_values(const EpiParams &ep, int64_t row, boo
                                            float (&v)[32]) {
     // fs / fa: B scale and beta * C along N of the 32 (gate) columns (shared
     // memory); fsu / fau the same for the up columns
-    if (row_add == 0.0f) {
+    if (row_scale == 1.0f && row_add == 0.0f) {  // row scale folded into fs (or 1)
+#pragma unroll
+        for (int j = 0; j < 32; ++j) v[j] = fmaf(__uint_as_float(g[j]), fs[j], fa[j]);
+    } else if (row_add == 0.0f) {
 #pragma unroll
         for (int j = 0; j < 32; ++j) v[j] = fmaf(__uint_as_float(g[j]) * row_scale, fs[j], fa[j]);
     } else {
@@ -454,13 +466,15 @@ __device__ __forceinline__ void epilogue_tile(const EpiParams &ep, const CUtenso
                                           : static_cast<int64_t>(tn) * BN + c * 32;
     };
     const int lane = static_cast<int>(threadIdx.x & 31);
-    // this lane's column factors of chunk c: gemm column tn*BN + c*32 + lane (and its up column)
+    // this lane's column factors of chunk c: gemm column tn*BN + c*32 + lane (and its up column);
+    // a per-tensor A scale (times alpha) is folded into the slot's column scale
+    const float fold_scale = ep.sa_row ? 1.0f : row_scale;
     auto load_fac = [&](int c, float (&f)[4]) {
         const int64_t n = static_cast<int64_t>(tn) * BN + c * 32 + lane;
 #pragma unroll
         for (int h = 0; h < (EPI == LCML_EPI_SILU_MUL ? 2 : 1); ++h) {
             const int64_t nn = n + h * (BN / 2);
-            f[2 * h] = ep.sb_col ? (nn < ep.N ? __ldg(ep.sb + nn) : 0.0f) : __ldg(ep.sb);
+            f[2 * h] = (ep.sb_col ? (nn < ep.N ? __ldg(ep.sb + nn) : 0.0f) : __ldg(ep.sb)) * fold_scale;
             f[2 * h + 1] = (ep.c_vec_mode == 3 && nn < ep.N) ? ep.beta * __ldg(ep.c_vec + nn) : 0.0f;
         }
     };
@@ -493,7 +507,7 @@ __device__ __forceinline__ void epilogue_tile(const EpiParams &ep, const CUtenso
             __syncwarp();
             tmem_wait_ld();
             epi_values<EPI>(ep, row, row_ok, col0, ng0 + BN / 2, n_out, g, EPI == LCML_EPI_SILU_MUL ? u : g, facw,
-                            facw + 32, facw + 64, facw + 96, rr, row_scale, row_add, amax, v);
+                            facw + 32, facw + 64, facw + 96, rr, ep.sa_row ? row_scale : 1.0f, row_add, amax, v);
             __syncwarp();  // every lane has read facw before the next chunk rewrites it
         } else {
             ColFactors fg, fu;
@@ -1024,7 +1038,7 @@ __global__ void __launch_bounds__(256) k_gemm_fp8_simt(const uint8_t *__restrict
         }
         __syncthreads();
     }
-    const float ys = (OUT == kOutE4M3) ? __ldg(ep.y_scale) : 1.0f;
+    const OutQuant oq = make_out_quant<OUT>(ep);
     const int64_t n_out = (EPI == LCML_EPI_SILU_MUL) ? N / 2 : N;
     for (int i = 0; i < 4; ++i) {
         const int64_t row = m0 + ty * 4 + i;
@@ -1044,8 +1058,8 @@ __global__ void __launch_bounds__(256) k_gemm_fp8_simt(const uint8_t *__restrict
             if (ep.c_mat) a += ep.beta * load_cmat(ep, row, col);
             if (EPI == LCML_EPI_RELU) a = fmaxf(a, 0.0f);
             amax = fmaxf(amax, fabsf(a));
-            store_out<OUT>(ep.y, ep.ldy, row, col + ep.y_col_offset, a, ys);
-            for (int p = 0; p < ep.y_num_peers; ++p) store_out<OUT>(ep.y_peers[p], ep.ldy, row, col + ep.y_col_offset, a, ys);
+            store_out<OUT>(ep.y, ep.ldy, row, col + ep.y_col_offset, a, oq);
+            for (int p = 0; p < ep.y_num_peers; ++p) store_out<OUT>(ep.y_peers[p], ep.ldy, row, col + ep.y_col_offset, a, oq);
         }
         if (ep.row_amax) atomic_max_abs(ep.row_amax + row, amax);
     }

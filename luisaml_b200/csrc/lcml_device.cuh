@@ -175,6 +175,53 @@ __device__ __forceinline__ void quantize_block_fast(const float *v, float s, flo
     }
 }
 
+// Bytes 0x80 and 0xff of four hardware-converted codes (bit 7 set in the
+// result's byte): a = x & 0x7f7f7f7f; (a + 0x7f) sets bit 7 of a byte exactly
+// when it is nonzero, (a + 1) exactly when it is 0x7f (no carry crosses a
+// byte); the sign bit of x selects the negative ones.
+__device__ __forceinline__ uint32_t e4m3_odd_bytes(uint32_t x) {
+    const uint32_t a = x & 0x7f7f7f7fu;
+    return (~((a + 0x7f7f7f7fu) | a) | (a + 0x01010101u)) & x & 0x80808080u;
+}
+
+// One value by the epilogue quantization rule below: the codec applied to
+// the fp32 product q = RN(v * r) (+-0 -> 0x00, NaN -> 0x7f, else the RNE
+// saturating conversion, which equals the codec on every other q).
+__device__ __forceinline__ uint32_t quantize_rcp1(float v, float r) {
+    const float q = __fmul_rn(v, r);
+    if (q == 0.0f) return 0u;
+    if (q != q) return 0x7fu;
+    return cvt_e4m3x2(q, 0.0f) & 0xffu;
+}
+
+// Output quantization of the fused GEMM / conv epilogues: the codec applied
+// to q = RN(v * r), r = RN(1 / y_scale). It equals QuantizeLinear of the
+// epilogue's fp32 value v (RN(v / s), quantize1) except where v / s lies
+// within 2.5 fp32 ulps of an e4m3 rounding boundary: the same order of
+// difference as the fp32 accumulation order of the GEMM itself, whose outputs
+// match the reference within a tolerance. The hardware conversion gives the
+// codec's byte except for q = -0 (0x80 where the codec writes 0x00) and NaN
+// (possibly 0xff where the codec writes 0x7f); a block holding either byte is
+// redone element by element (both are rare: -0 needs v = -0 or an underflow).
+// Used only when r is a normal float (scale_fast_ok); QuantizeLinear proper
+// (quantize.cu) stays bit-exact.
+template <int N>
+__device__ __forceinline__ void quantize_block_rcp(const float *v, float r, uint32_t *w) {
+    uint32_t odd = 0;
+#pragma unroll
+    for (int j = 0; j < N / 4; ++j) {
+        w[j] = cvt_e4m3x2(__fmul_rn(v[4 * j], r), __fmul_rn(v[4 * j + 1], r)) |
+               (cvt_e4m3x2(__fmul_rn(v[4 * j + 2], r), __fmul_rn(v[4 * j + 3], r)) << 16);
+        odd |= e4m3_odd_bytes(w[j]);
+    }
+    if (odd) {  // unrolled: a runtime index would move v and w to local memory
+#pragma unroll
+        for (int j = 0; j < N / 4; ++j)
+            w[j] = quantize_rcp1(v[4 * j], r) | (quantize_rcp1(v[4 * j + 1], r) << 8) |
+                   (quantize_rcp1(v[4 * j + 2], r) << 16) | (quantize_rcp1(v[4 * j + 3], r) << 24);
+    }
+}
+
 // amax -> scale for every dynamic mode: amax / 448, or 1 when amax is 0.
 __device__ __forceinline__ float scale_from_amax(float amax) {
     return amax > 0.0f ? __fdiv_rn(amax, 448.0f) : 1.0f;

@@ -318,6 +318,35 @@ def test_gemm_column_shard_and_peer_copies(dev, gemm_mode, out, mode):
         assert_close(got.cpu().numpy(), ref, what="f32 shard")
 
 
+def epilogue_quantize(y, s):
+    """The fused epilogues' output quantization: the reference codec applied
+    to RN(y * RN(1 / s)) (fp32 multiply; +-0 -> 0x00, NaN -> 0x7f, |q| > 448
+    saturates, as the codec does)."""
+    r = np.float32(1.0) / np.float32(s)
+    return oracle.quantize((np.asarray(y, dtype=np.float32) * r).astype(np.float32), np.float32(1.0))
+
+
+def test_epilogue_quantize_rule(dev):
+    """The epilogue rule on hand-picked values through a 1 x K x N GEMM whose
+    output equals chosen fp32 values: zeros of both signs, NaN, values past
+    448 * s, subnormal e4m3 results and ties."""
+    import torch
+    import luisaml_b200 as lb
+    vals = np.float32([0.0, -0.0, 1e-30, -1e-30, 3.0, -3.0, 500.0, -1e9, 2.0 ** -9, -2.0 ** -10, 0.5625, 17.0,
+                       np.nan, 448.0, 464.0, -480.0])
+    N = 64
+    v = np.resize(vals, N).astype(np.float32)
+    for s in (np.float32(1.0), np.float32(0.0123)):
+        # Y = A * B^T + bias with A = 0 (e4m3 zeros): Y = bias exactly
+        A = torch.zeros((128, 64), dtype=torch.uint8, device=dev)
+        B = torch.zeros((N, 64), dtype=torch.uint8, device=dev)
+        one = torch.ones(1, device=dev)
+        ys = _t(np.float32([s]), dev)
+        Y = lb.gemm(A, B, one, one, c_vec=_t(v, dev), out_dtype=torch.uint8, y_scale=ys)
+        got = Y.cpu().numpy()
+        np.testing.assert_array_equal(got, np.broadcast_to(epilogue_quantize(v, s), got.shape))
+
+
 @pytest.mark.parametrize("out", ["f32", "bf16", "e4m3"])
 @pytest.mark.parametrize("mode", [1, 2])
 @pytest.mark.parametrize("M,N,K", [(300, 528, 200), (97, 64, 64), (1000, 96, 576)])
@@ -326,7 +355,9 @@ def test_store_paths(dev, gemm_mode, out, mode, M, N, K):
     write bit-identical outputs, including ragged edges in M and N and an
     output placed at a column offset inside a wider matrix whose other columns
     must stay untouched; the fp32 result also matches the oracle and the e4m3
-    bytes equal the oracle's quantization of the fp32 result."""
+    bytes follow the epilogue quantization rule exactly (the codec applied to
+    RN(y * RN(1 / s)) of the fp32 result y), which differs from QuantizeLinear
+    of y only for values next to an e4m3 rounding boundary."""
     import torch
     import luisaml_b200 as lb
     Aq, sa, Bq, sb = make_operands(M, N, K, seed=M * 7 + N + K, per_row=True, per_col=True)
@@ -354,5 +385,7 @@ def test_store_paths(dev, gemm_mode, out, mode, M, N, K):
     elif out == "e4m3":
         gemm_mode(mode)
         y32 = lb.gemm(*args, c_vec=_t(bias, dev), epilogue=lb.EPI_RELU, out_dtype=torch.float32).cpu().numpy()
-        want = oracle.quantize(y32, float(ys.cpu()[0]))
+        s = np.float32(ys.cpu()[0])
+        want = epilogue_quantize(y32, s)
         np.testing.assert_array_equal(results[0][:, 16:16 + N], want)
+        assert np.mean(want != oracle.quantize(y32, s)) <= 1e-3
