@@ -217,7 +217,9 @@ class GraphWorkload:
 
     unit = "TFLOP/s"
     parallelism = "batch split"
-    e2e_path = "pinned host inputs -> H2D -> NetworkInstance::forward (C ABI) -> D2H outputs"
+    e2e_path = ("pinned host inputs -> NetworkInstance::forward (C ABI) with host-staged I/O: the H2D copy of each "
+                "step's input on a second stream (overlapping the previous step once its input readers ran) -> "
+                "nodes -> D2H of the outputs")
 
     def setup_graph(self, dev, text, blob, inputs, outputs):
         import torch
@@ -249,12 +251,13 @@ class GraphWorkload:
         self.h2d = sum(t.numel() * t.element_size() for t in self.in_host.values())
         self.d2h = sum(t.numel() * t.element_size() for t in self.out_host.values())
 
+        for k, t in self.in_host.items():
+            self.net.set_input_host(k, t)
+        for k, t in self.out_host.items():
+            self.net.set_output_host(k, t)
+
     def step_e2e(self, stream):
-        for k, t in self.inputs.items():
-            t.copy_(self.in_host[k], non_blocking=True)
-        self.net.forward()
-        for k, t in self.outputs.items():
-            self.out_host[k].copy_(t, non_blocking=True)
+        self.net.forward()  # H2D of the inputs, the nodes, D2H of the outputs
 
 
 class MlpWorkload(GraphWorkload):
@@ -663,7 +666,7 @@ def run_ours(args, wl):
         if ws > 1:
             dist.barrier()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        ne = max(3, min(20, n // 10))
+        ne = max(10, min(20, n // 10))
         e0.record(stream)
         for _ in range(ne):
             wl.step_e2e(stream)

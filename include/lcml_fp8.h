@@ -26,6 +26,7 @@ extern "C" {
 #endif
 
 typedef struct CUstream_st *lcml_stream_t;
+typedef struct CUevent_st *lcml_event_t;
 
 /* Status codes. */
 typedef enum lcml_status {
@@ -94,6 +95,17 @@ int lcml_device_free(void *ptr);
 int lcml_memcpy_async(void *dst, const void *src, size_t bytes, int kind, lcml_stream_t stream);
 int lcml_memset_async(void *dst, int value, size_t bytes, lcml_stream_t stream);
 int lcml_stream_synchronize(lcml_stream_t stream);
+
+/* Streams and events for hosts without a CUDA runtime of their own (the
+ * executor's host-staged inputs copy on a second stream; the reference has
+ * LuisaCompute's Stream / Event). lcml_stream_create makes a non-blocking
+ * stream; events carry no timing. */
+int lcml_stream_create(lcml_stream_t *stream);
+int lcml_stream_destroy(lcml_stream_t stream);
+int lcml_event_create(lcml_event_t *event);
+int lcml_event_destroy(lcml_event_t event);
+int lcml_event_record(lcml_event_t event, lcml_stream_t stream);
+int lcml_stream_wait_event(lcml_stream_t stream, lcml_event_t event);
 
 /*
  * QuantizeLinear to float8e4m3fn, zero point 0, saturate = 1 (ONNX opset 19+):

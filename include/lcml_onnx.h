@@ -344,6 +344,16 @@ public:
     void set_weight_buffer(const void *device_ptr, size_t bytes);
     void set_stream(lcml_stream_t s) { stream_ = s; }
     lcml_stream_t stream() const { return stream_; }
+    // Host-staged I/O (no reference counterpart: the reference reads and
+    // writes its bound buffers itself). A bound input may name a host buffer
+    // (pinned for asynchronous copies) of the same size: every forward()
+    // first copies it into the bound device tensor on a second stream. That
+    // copy waits only until the previous forward's last reader of the input
+    // has run, so it overlaps the rest of that forward. A bound output may
+    // name a host buffer that forward() fills (device -> host on the
+    // instance's stream) after the last node. nullptr removes the binding.
+    void set_input_host(std::string_view name, const void *host);
+    void set_output_host(std::string_view name, void *host);
     // Kept for source compatibility with the reference; no effect on the CUDA path.
     void set_warp_size(uint32_t w) { warp_size_ = w; }
     uint32_t warp_size() const { return warp_size_; }
@@ -392,6 +402,11 @@ private:
     std::vector<std::unique_ptr<Operator>> ops_;
     std::vector<std::unique_ptr<FusionInfo>> fusion_;
     std::set<std::string, std::less<>> nhwc_;
+    std::map<std::string, const void *, std::less<>> host_in_;
+    std::map<std::string, void *, std::less<>> host_out_;
+    lcml_stream_t copy_stream_ = nullptr;
+    lcml_event_t in_ready_ = nullptr, in_free_ = nullptr;
+    bool in_free_recorded_ = false;
 };
 
 // Throws Error with lcml_last_error() when a C-ABI call fails.

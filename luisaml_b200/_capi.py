@@ -88,6 +88,12 @@ PROTOTYPES = {
     "lcml_memcpy_async": [_vp, _vp, ctypes.c_size_t, _ci, _vp],
     "lcml_memset_async": [_vp, _ci, ctypes.c_size_t, _vp],
     "lcml_stream_synchronize": [_vp],
+    "lcml_stream_create": [ctypes.POINTER(ctypes.c_void_p)],
+    "lcml_stream_destroy": [_vp],
+    "lcml_event_create": [ctypes.POINTER(ctypes.c_void_p)],
+    "lcml_event_destroy": [_vp],
+    "lcml_event_record": [_vp, _vp],
+    "lcml_stream_wait_event": [_vp, _vp],
     "lcml_ipc_get_handle": [_vp, _vp],
     "lcml_ipc_open": [_vp, ctypes.POINTER(ctypes.c_void_p)],
     "lcml_ipc_close": [_vp],

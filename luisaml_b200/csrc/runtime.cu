@@ -139,6 +139,44 @@ int lcml_stream_synchronize(lcml_stream_t stream) {
     return LCML_OK;
 }
 
+int lcml_stream_create(lcml_stream_t *stream) {
+    LCML_CHECK_ARG(stream != nullptr, "lcml_stream_create: stream is NULL");
+    cudaStream_t s = nullptr;
+    LCML_CUDA(cudaStreamCreateWithFlags(&s, cudaStreamNonBlocking));
+    *stream = reinterpret_cast<lcml_stream_t>(s);
+    return LCML_OK;
+}
+
+int lcml_stream_destroy(lcml_stream_t stream) {
+    if (stream) LCML_CUDA(cudaStreamDestroy(lcml::to_cuda(stream)));
+    return LCML_OK;
+}
+
+int lcml_event_create(lcml_event_t *event) {
+    LCML_CHECK_ARG(event != nullptr, "lcml_event_create: event is NULL");
+    cudaEvent_t e = nullptr;
+    LCML_CUDA(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
+    *event = reinterpret_cast<lcml_event_t>(e);
+    return LCML_OK;
+}
+
+int lcml_event_destroy(lcml_event_t event) {
+    if (event) LCML_CUDA(cudaEventDestroy(reinterpret_cast<cudaEvent_t>(event)));
+    return LCML_OK;
+}
+
+int lcml_event_record(lcml_event_t event, lcml_stream_t stream) {
+    LCML_CHECK_ARG(event != nullptr, "lcml_event_record: event is NULL");
+    LCML_CUDA(cudaEventRecord(reinterpret_cast<cudaEvent_t>(event), lcml::to_cuda(stream)));
+    return LCML_OK;
+}
+
+int lcml_stream_wait_event(lcml_stream_t stream, lcml_event_t event) {
+    LCML_CHECK_ARG(event != nullptr, "lcml_stream_wait_event: event is NULL");
+    LCML_CUDA(cudaStreamWaitEvent(lcml::to_cuda(stream), reinterpret_cast<cudaEvent_t>(event), 0));
+    return LCML_OK;
+}
+
 }// extern "C"
 
 extern "C" {

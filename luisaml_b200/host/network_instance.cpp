@@ -61,6 +61,24 @@ NetworkInstance::~NetworkInstance() {
     ops_.clear();
     fusion_.clear();
     table_.clear();
+    if (copy_stream_) {
+        lcml_stream_synchronize(copy_stream_);
+        lcml_stream_destroy(copy_stream_);
+    }
+    lcml_event_destroy(in_ready_);
+    lcml_event_destroy(in_free_);
+}
+
+void NetworkInstance::set_input_host(std::string_view name, const void *host) {
+    if (!inputs_.count(std::string(name))) throw Error("set_input_host: input '" + std::string(name) + "' is not bound");
+    if (host) host_in_[std::string(name)] = host;
+    else host_in_.erase(std::string(name));
+}
+
+void NetworkInstance::set_output_host(std::string_view name, void *host) {
+    if (!outputs_.count(std::string(name))) throw Error("set_output_host: output '" + std::string(name) + "' is not bound");
+    if (host) host_out_[std::string(name)] = host;
+    else host_out_.erase(std::string(name));
 }
 
 void NetworkInstance::set_model(Model model) {
@@ -785,6 +803,34 @@ void NetworkInstance::forward() {
     if (!prepared_) prepare();
     const auto &nodes = model_.get_graph().get_nodes();
     std::vector<std::reference_wrapper<ITensor>> ins, outs;
+    // host-staged inputs: copy on the second stream once the previous
+    // forward's last reader of them has run; this forward's nodes wait for it
+    size_t last_reader = nodes.size();
+    if (!host_in_.empty()) {
+        if (!copy_stream_) {
+            check_status(lcml_stream_create(&copy_stream_), "copy stream");
+            check_status(lcml_event_create(&in_ready_), "event");
+            check_status(lcml_event_create(&in_free_), "event");
+        }
+        if (in_free_recorded_) check_status(lcml_stream_wait_event(copy_stream_, in_free_), "wait");
+        for (const auto &[name, host] : host_in_) {
+            ITensor &t = *inputs_.at(name);
+            check_status(lcml_memcpy_async(t.data(), host, t.nbytes(), 1, copy_stream_), "input copy");
+        }
+        check_status(lcml_event_record(in_ready_, copy_stream_), "record");
+        check_status(lcml_stream_wait_event(stream_, in_ready_), "wait");
+        for (size_t i = 0; i < nodes.size(); ++i) {
+            if (fusion_[i]->skip) continue;
+            auto reads = [&](const std::string &n) { return host_in_.count(n) > 0; };
+            bool r = false;
+            if (!fusion_[i]->inputs.empty()) {
+                for (const auto &n : fusion_[i]->inputs) r = r || reads(n);
+            } else {
+                for (const auto *x : nodes[i].get_inputs()) r = r || reads(x->get_name());
+            }
+            if (r) last_reader = i;
+        }
+    }
     for (size_t i = 0; i < nodes.size(); ++i) {
         FusionInfo &fi = *fusion_[i];
         if (fi.skip) continue;
@@ -804,6 +850,14 @@ void NetworkInstance::forward() {
         op.set_environment(*this, table_);
         if (logging_) std::fprintf(stderr, "[lcml] node %zu %s (%s)\n", i, nodes[i].get_op_type().c_str(), op.get_name().c_str());
         op.forward(ins, outs);
+        if (i == last_reader) {
+            check_status(lcml_event_record(in_free_, stream_), "record");
+            in_free_recorded_ = true;
+        }
+    }
+    for (const auto &[name, host] : host_out_) {
+        ITensor &t = *outputs_.at(name);
+        check_status(lcml_memcpy_async(host, t.data(), t.nbytes(), 2, stream_), "output copy");
     }
 }
 

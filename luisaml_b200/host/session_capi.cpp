@@ -91,6 +91,16 @@ int lcml_network_set_output(lcml_network *net, const char *name, void *p, int dt
     });
 }
 
+int lcml_network_set_input_host(lcml_network *net, const char *name, const void *host) {
+    if (!net || !name) return fail(LCML_ERR_INVALID_ARGUMENT, "lcml_network_set_input_host: null argument");
+    return guard([&] { net->inst.set_input_host(name, host); });
+}
+
+int lcml_network_set_output_host(lcml_network *net, const char *name, void *host) {
+    if (!net || !name) return fail(LCML_ERR_INVALID_ARGUMENT, "lcml_network_set_output_host: null argument");
+    return guard([&] { net->inst.set_output_host(name, host); });
+}
+
 int lcml_network_set_fusion(lcml_network *net, int enable) {
     if (!net) return fail(LCML_ERR_INVALID_ARGUMENT, "null network");
     net->inst.enable_fusion(enable != 0);

@@ -29,6 +29,8 @@ def load():
     lib.lcml_network_set_weight_buffer.argtypes = [_vp, _vp, _sz]
     lib.lcml_network_set_input.argtypes = [_vp, ctypes.c_char_p, _vp, _ci, ctypes.POINTER(_i64), _ci]
     lib.lcml_network_set_output.argtypes = [_vp, ctypes.c_char_p, _vp, _ci, ctypes.POINTER(_i64), _ci]
+    lib.lcml_network_set_input_host.argtypes = [_vp, ctypes.c_char_p, _vp]
+    lib.lcml_network_set_output_host.argtypes = [_vp, ctypes.c_char_p, _vp]
     lib.lcml_network_set_fusion.argtypes = [_vp, _ci]
     lib.lcml_network_set_stream.argtypes = [_vp, _vp]
     lib.lcml_network_forward.argtypes = [_vp]
@@ -88,6 +90,21 @@ class Network:
 
     def set_output(self, name, t, dtype=None):
         self._bind(load().lcml_network_set_output, name, t, dtype)
+
+    def set_input_host(self, name, t):
+        """Host-staged input: the pinned host tensor `t` (the bound input's
+        size) is copied in at the start of every forward, overlapping the
+        previous forward once its readers of the input have run."""
+        if t is not None:
+            self._keep.append(t)
+        _check(load().lcml_network_set_input_host(self._h, name.encode(), None if t is None else t.data_ptr()))
+
+    def set_output_host(self, name, t):
+        """Host-staged output: forward() copies the bound output into the
+        pinned host tensor `t` after its last node (on the network's stream)."""
+        if t is not None:
+            self._keep.append(t)
+        _check(load().lcml_network_set_output_host(self._h, name.encode(), None if t is None else t.data_ptr()))
 
     def set_fusion(self, enable: bool):
         _check(load().lcml_network_set_fusion(self._h, int(enable)))

@@ -77,6 +77,49 @@ def test_qdq_mlp_graph(dev, fusion):
     assert net.executed_nodes() == (5 if fusion else 8)  # DQ of constant weights folded at prepare
 
 
+def test_host_staged_io(dev):
+    """Host-staged inputs and outputs: forwards issued back to back, each
+    with its own pinned input and output, give the device-bound results; the
+    input copy of one forward (on the executor's second stream) must not
+    overwrite the device input before the previous forward has read it."""
+    import torch
+    from luisaml_b200 import graphs
+    from luisaml_b200.session import Network
+    B = 2048
+    text, blob, meta = graphs.mlp(batch=B)
+    wb = _t(np.frombuffer(blob, dtype=np.uint8), dev)
+    xs = [np.random.default_rng(2000 + i).random((B, 784), dtype=np.float32) for i in range(4)]
+    ref_net = Network(text)
+    ref_net.set_weight_buffer(wb)
+    xd = torch.empty((B, 784), dtype=torch.float32, device=dev)
+    yd = torch.empty((B, 10), dtype=torch.float32, device=dev)
+    ref_net.set_input("input", xd)
+    ref_net.set_output("output", yd)
+    want = []
+    for x in xs:
+        xd.copy_(torch.from_numpy(x))
+        ref_net.forward()
+        want.append(yd.cpu().numpy())
+    net = Network(text)
+    net.set_weight_buffer(wb)
+    net.set_input("input", torch.empty((B, 784), dtype=torch.float32, device=dev))
+    net.set_output("output", torch.empty((B, 10), dtype=torch.float32, device=dev))
+    net.set_stream(torch.cuda.current_stream(dev).cuda_stream)
+    hin = [torch.from_numpy(x).pin_memory() for x in xs]
+    hout = [torch.full((B, 10), np.nan).pin_memory() for _ in xs]
+    for rep in range(2):
+        for i in range(len(xs)):
+            net.set_input_host("input", hin[i])
+            net.set_output_host("output", hout[i])
+            net.forward()
+        torch.cuda.synchronize()
+        for i in range(len(xs)):
+            np.testing.assert_array_equal(hout[i].numpy(), want[i])
+            hout[i].fill_(np.nan)
+    with pytest.raises(Exception):
+        net.set_input_host("no_such_input", hin[0])
+
+
 def _quantized_mlp(batch, dims, seed):
     """x -> QuantizeLinear(static s_x) -> DequantizeLinear -> Gemm(DQ W, b) -> Relu
     -> QuantizeLinear(static) -> DequantizeLinear -> Gemm -> ... (activations and weights QDQ)."""
