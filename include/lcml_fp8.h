@@ -255,13 +255,14 @@ int lcml_gemm_f32(const float *A, const float *B, const float *C, int64_t M, int
  * GEMM columns, K = (kh, kw, c) with c over Cp channels per tap: Cp = C
  * when C is a multiple of 16, else C padded to 4, 8 or the next multiple of
  * 16 (so each tap is one 4-, 8- or 16-byte vector). A 1x1 / stride-1 /
- * unpadded conv on an NHWC input reads X as the GEMM's A directly; every other
- * conv gathers its patches (im2col, e4m3, zero padding) into `workspace` (after
- * copying X into a channel-padded NHWC layout there when X is NCHW or C is
- * not a multiple of 16) and runs the TMA-fed GEMM on them. Given no workspace,
- * a conv on an NHWC input with C a multiple of 16 (X 16-byte aligned) runs as
- * an implicit GEMM instead: the kernel's producer warps gather the patches
- * from X themselves (slower, but it needs no scratch memory).
+ * unpadded conv on an NHWC input reads X as the GEMM's A directly. A conv on
+ * an NHWC input with C a multiple of 64 (X 16-byte aligned; pads <= 128,
+ * strides <= 8, (k - 1) * dilation <= 255) runs as an implicit GEMM: the
+ * kernel loads each K-block of patches from X with a TMA im2col copy (zero
+ * outside the image), so it needs no workspace. Every other conv gathers its
+ * patches (im2col, e4m3, zero padding) into `workspace` (after copying X into
+ * a channel-padded NHWC layout there when X is NCHW or C is not a multiple of
+ * 16) and runs the TMA-fed GEMM on them.
  * X: e4m3, NHWC (x_nhwc = 1) or NCHW (x_nhwc = 0), per-tensor scale.
  * Wp: weights packed by lcml_fp8_conv_pack_weight, per-tensor or per-output-
  * channel scales. Y: NHWC [N, oH, oW, M] (the GEMM's row-major output),
@@ -293,7 +294,7 @@ typedef struct lcml_fp8_conv_desc {
 
 /* Packed K: kH * kW * Cp (Cp: C padded as above) rounded up to a multiple of 16. */
 int64_t lcml_fp8_conv_packed_k(int64_t Cg, int64_t kH, int64_t kW);
-/* Bytes of scratch the materialized lowering needs for `desc` (0 for the direct 1x1 path, -1 on a bad desc). */
+/* Bytes of scratch `desc` needs (0 for the direct 1x1 and the implicit-GEMM paths, -1 on a bad desc). */
 int64_t lcml_fp8_conv_workspace_size(const lcml_fp8_conv_desc *desc);
 /* Packs e4m3 W [M, Cg, kH, kW] (ONNX layout) into Wp [M, Kp], K order (kh, kw, c) over Cp channels,
  * zero in the padding channels and past kH * kW * Cp. */

@@ -37,7 +37,6 @@ int lcml_network_set_input(lcml_network *net, const char *name, const void *devi
                            const int64_t *shape, int ndim);
 int lcml_network_set_output(lcml_network *net, const char *name, void *device_ptr, int dtype, const int64_t *shape,
                             int ndim);
-/* 1 (default): QDQ node groups run as fused kernels; 0: one kernel per node. */
 /* Host-staged I/O (no reference counterpart). `host` (pinned, of the bound
  * tensor's byte size; NULL removes it) is copied into the bound input at the
  * start of every forward on a second stream, overlapping the previous
@@ -46,6 +45,7 @@ int lcml_network_set_output(lcml_network *net, const char *name, void *device_pt
  * stream. The tensor must be bound (set_input / set_output) first. */
 int lcml_network_set_input_host(lcml_network *net, const char *name, const void *host);
 int lcml_network_set_output_host(lcml_network *net, const char *name, void *host);
+/* 1 (default): QDQ node groups run as fused kernels; 0: one kernel per node. */
 int lcml_network_set_fusion(lcml_network *net, int enable);
 int lcml_network_set_stream(lcml_network *net, lcml_stream_t stream);
 /* Enqueues the whole graph on the stream (prepares on the first call). */
