@@ -218,7 +218,7 @@ constexpr int out_es(int out) { return out == kOutF32 ? 4 : (out == kOutBF16 ? 2
 
 // 32 values -> the output's bytes as 8 * element-size little-endian words
 // (e4m3 by the epilogue quantization rule of quantize_block_rcp).
-template <int OUT>
+template <int OUT, bool NONNEG = false>
 __device__ __forceinline__ void pack32(const float (&v)[32], const OutQuant &q, uint32_t (&w)[8 * out_es(OUT)]) {
     if (OUT == kOutF32) {
 #pragma unroll
@@ -230,7 +230,7 @@ __device__ __forceinline__ void pack32(const float (&v)[32], const OutQuant &q, 
             w[j] = *reinterpret_cast<uint32_t *>(&h);
         }
     } else if (q.s_ok) {
-        quantize_block_rcp<32>(v, q.r, w);
+        quantize_block_rcp<32, NONNEG>(v, q.r, w);
     } else {
 #pragma unroll
         for (int j = 0; j < 8; ++j)
@@ -379,15 +379,26 @@ __device__ __forceinline__ void prefetch_residual(const EpiParams &ep, int64_t r
 // their column factors, rr the prefetched residual (else it is loaded here).
 // Parameter-dependent branches are per chunk; the element loops are
 // branch-free.
-template <int EPI>
+template <int EPI, bool VEC>
 __device__ __forceinline__ void epi_values(const EpiParams &ep, int64_t row, bool row_ok, int64_t col0, int64_t nu0,
                                            int64_t n_out, const uint32_t (&g)[32], const uint32_t (&u)[32],
                                            const float *fs, const float *fa, const float *fsu, const float *fau,
                                            const ResidualRaw &rr, float row_scale, float row_add, float &amax,
                                            float (&v)[32]) {
-    // fs / fa: B scale and beta * C along N of the 32 (gate) columns (shared
-    // memory); fsu / fau the same for the up columns
-    if (row_scale == 1.0f && row_add == 0.0f) {  // row scale folded into fs (or 1)
+    // fs / fa: B scale and beta * C along N of the 32 (gate) columns (VEC:
+    // 16-byte aligned shared memory, read as float4); fsu / fau the same for
+    // the up columns
+    if (VEC && row_scale == 1.0f && row_add == 0.0f) {  // row scale folded into fs
+        const float4 *fs4 = reinterpret_cast<const float4 *>(fs), *fa4 = reinterpret_cast<const float4 *>(fa);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            const float4 sc = fs4[j], ad = fa4[j];
+            v[4 * j] = fmaf(__uint_as_float(g[4 * j]), sc.x, ad.x);
+            v[4 * j + 1] = fmaf(__uint_as_float(g[4 * j + 1]), sc.y, ad.y);
+            v[4 * j + 2] = fmaf(__uint_as_float(g[4 * j + 2]), sc.z, ad.z);
+            v[4 * j + 3] = fmaf(__uint_as_float(g[4 * j + 3]), sc.w, ad.w);
+        }
+    } else if (row_scale == 1.0f && row_add == 0.0f) {
 #pragma unroll
         for (int j = 0; j < 32; ++j) v[j] = fmaf(__uint_as_float(g[j]), fs[j], fa[j]);
     } else if (row_add == 0.0f) {
@@ -506,7 +517,7 @@ __device__ __forceinline__ void epilogue_tile(const EpiParams &ep, const CUtenso
             }
             __syncwarp();
             tmem_wait_ld();
-            epi_values<EPI>(ep, row, row_ok, col0, ng0 + BN / 2, n_out, g, EPI == LCML_EPI_SILU_MUL ? u : g, facw,
+            epi_values<EPI, true>(ep, row, row_ok, col0, ng0 + BN / 2, n_out, g, EPI == LCML_EPI_SILU_MUL ? u : g, facw,
                             facw + 32, facw + 64, facw + 96, rr, ep.sa_row ? row_scale : 1.0f, row_add, amax, v);
             __syncwarp();  // every lane has read facw before the next chunk rewrites it
         } else {
@@ -515,18 +526,18 @@ __device__ __forceinline__ void epilogue_tile(const EpiParams &ep, const CUtenso
             if (EPI == LCML_EPI_SILU_MUL) load_col_factors(ep, ng0 + BN / 2, fu);
             if (c + c_step < kChunks) prefetch_residual(ep, row, row_ok, col_of(c + c_step), n_out, rr_next);
             tmem_wait_ld();
-            epi_values<EPI>(ep, row, row_ok, col0, ng0 + BN / 2, n_out, g, EPI == LCML_EPI_SILU_MUL ? u : g, fg.scale,
+            epi_values<EPI, false>(ep, row, row_ok, col0, ng0 + BN / 2, n_out, g, EPI == LCML_EPI_SILU_MUL ? u : g, fg.scale,
                             fg.add, fu.scale, fu.add, rr, row_scale, row_add, amax, v);
         }
         constexpr int ES = out_es(OUT);
         if (ep.tma_store) {
             uint32_t w[8 * ES];
-            pack32<OUT>(v, oq, w);
+            pack32<OUT, EPI == LCML_EPI_RELU>(v, oq, w);
             store_chunk_tma<OUT>(tmY, stage, seq, row0, col0, w);
         } else if (ep.y_num_peers > 0 && col0 + 32 <= n_out && ((ep.ldy * ES) % 16 == 0) &&
                    (((ep.y_col_offset + col0) * ES) % 16 == 0)) {
             uint32_t w[8 * ES];
-            pack32<OUT>(v, oq, w);
+            pack32<OUT, EPI == LCML_EPI_RELU>(v, oq, w);
             store_chunk_peers<OUT>(ep, stage, row0, col0, w);
         } else if (row_ok) {
             store_row32_to<OUT>(ep, ep.y, row, col0, n_out, v, oq);

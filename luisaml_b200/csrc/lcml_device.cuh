@@ -205,15 +205,19 @@ __device__ __forceinline__ uint32_t quantize_rcp1(float v, float r) {
 // redone element by element (both are rare: -0 needs v = -0 or an underflow).
 // Used only when r is a normal float (scale_fast_ok); QuantizeLinear proper
 // (quantize.cu) stays bit-exact.
-template <int N>
+// NONNEG: the values are known to be >= +0 or -0 (Relu outputs; fmaxf never
+// returns NaN for a non-NaN bound), so the only possible odd byte is 0x80 and
+// any set sign bit flags the block.
+template <int N, bool NONNEG = false>
 __device__ __forceinline__ void quantize_block_rcp(const float *v, float r, uint32_t *w) {
     uint32_t odd = 0;
 #pragma unroll
     for (int j = 0; j < N / 4; ++j) {
         w[j] = cvt_e4m3x2(__fmul_rn(v[4 * j], r), __fmul_rn(v[4 * j + 1], r)) |
                (cvt_e4m3x2(__fmul_rn(v[4 * j + 2], r), __fmul_rn(v[4 * j + 3], r)) << 16);
-        odd |= e4m3_odd_bytes(w[j]);
+        odd |= NONNEG ? w[j] : e4m3_odd_bytes(w[j]);
     }
+    if (NONNEG) odd &= 0x80808080u;
     if (odd) {  // unrolled: a runtime index would move v and w to local memory
 #pragma unroll
         for (int j = 0; j < N / 4; ++j)
