@@ -147,7 +147,8 @@ def transpose_u8(src):
 
 
 def gemm(A, B, sa, sb, *, b_kmajor=True, alpha=1.0, beta=1.0, c_vec=None, c_vec_mode=None, c_mat=None,
-         epilogue=EPI_NONE, out_dtype=None, y_scale=None, row_amax=None, out=None, simt=False, desc_only=False):
+         c_mat_scale=None, epilogue=EPI_NONE, out_dtype=None, y_scale=None, row_amax=None, out=None, simt=False,
+         desc_only=False):
     """Fused FP8 GEMM through lcml_fp8_gemm. A [M,K] e4m3 (uint8); B [N,K] (b_kmajor) or [K,N].
 
     sa: fp32 [1] or [M]; sb: fp32 [1] or [N]. Returns Y [M, N] (N/2 for SILU_MUL).
@@ -172,6 +173,8 @@ def gemm(A, B, sa, sb, *, b_kmajor=True, alpha=1.0, beta=1.0, c_vec=None, c_vec_
         d.c_vec_mode = c_vec_mode
     if c_mat is not None:
         d.c_mat, d.c_mat_dtype, d.ldc = c_mat.data_ptr(), _dtype_code(c_mat.dtype), c_mat.stride(0)
+        if c_mat_scale is not None:  # an e4m3 (uint8) residual is decoded times this per-tensor scale
+            d.c_mat_scale = c_mat_scale.data_ptr()
     d.epilogue = epilogue
     d.Y, d.y_dtype, d.ldy = Y.data_ptr(), _dtype_code(Y.dtype), Y.stride(0)
     if y_scale is not None:
@@ -180,7 +183,7 @@ def gemm(A, B, sa, sb, *, b_kmajor=True, alpha=1.0, beta=1.0, c_vec=None, c_vec_
         d.row_amax = row_amax.data_ptr()
     if desc_only:
         # the descriptor holds raw device pointers: keep the tensors they point into alive with it
-        d._refs = (A, B, sa, sb, c_vec, c_mat, Y, y_scale, row_amax)
+        d._refs = (A, B, sa, sb, c_vec, c_mat, c_mat_scale, Y, y_scale, row_amax)
         return d, Y
     fn = lib().lcml_fp8_gemm_simt if simt else lib().lcml_fp8_gemm
     check(fn(ctypes.byref(d), _stream()))

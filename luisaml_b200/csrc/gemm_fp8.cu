@@ -1008,6 +1008,196 @@ __device__ __forceinline__ float simt_pre(float acc, float row_scale, int64_t ro
     return v;
 }
 
+// ---------------------------------------------------------------------------
+// Split-K kernel for GEMMs with too few 128 x 128 output tiles to fill the
+// GPU (skinny M: decode-sized batches, classifier heads). A cluster of S CTAs
+// shares one tile; CTA r accumulates K-blocks [r*kb/S, (r+1)*kb/S) in its
+// own TMEM and writes the fp32 partial (valid rows) to its shared memory.
+// After a cluster barrier CTA r reduces rows [r*R, (r+1)*R) of the tile over
+// the S partials through distributed shared memory (ld.shared::cluster, in
+// rank order: deterministic), applies the epilogue (scales, beta*C,
+// residual, Relu, row |max|, output conversion) and stores; a second cluster
+// barrier keeps every partial alive until all of them have been read. Every
+// thread of every CTA reaches both barriers, also after a timed-out wait.
+// ---------------------------------------------------------------------------
+constexpr int kSplitBN = 128;
+constexpr int kSplitStages = 4;
+constexpr int kSplitThreads = 192;  // warp 0 TMA producer, warp 1 MMA issuer, warps 2-5 TMEM readers
+constexpr int kSplitMax = 8;        // portable cluster size
+
+struct SplitLayout {
+    static constexpr int kABytes = BM * BK;
+    static constexpr int kBBytes = kSplitBN * BK;
+    static constexpr int kStageBytes = kABytes + kBBytes;
+    static constexpr int kPartStride = kSplitBN + 4;  // floats per partial row: 16-byte skew, conflict-free rows
+    static constexpr int kPartOffset = kSplitStages * kStageBytes;
+    static constexpr int kBarOffset = kPartOffset + BM * kPartStride * 4;
+    static constexpr int kSmemBytes = kBarOffset + 256 + 1024;  // barriers, TMEM slot, +1024 alignment
+};
+
+template <int EPI, int OUT>
+__global__ void __launch_bounds__(kSplitThreads, 1)
+    k_gemm_fp8_splitk(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, int M, int N,
+                      int K, int splits, EpiParams ep, int *err) {
+    using L = SplitLayout;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint64_t *full = reinterpret_cast<uint64_t *>(smem + L::kBarOffset);
+    uint64_t *empty = full + kSplitStages;
+    uint64_t *tfull = empty + kSplitStages;
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(tfull + 1);
+    float *part = reinterpret_cast<float *>(smem + L::kPartOffset);
+
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+    const int rank = static_cast<int>(blockIdx.x) % splits;  // the cluster rank (1-D clusters of `splits` CTAs)
+    const int tile = static_cast<int>(blockIdx.x) / splits;
+    const int num_n = (N + kSplitBN - 1) / kSplitBN;
+    const int tm = tile / num_n, tn = tile - tm * num_n;
+    const int kblocks = (K + BK - 1) / BK;
+    const int kb0 = static_cast<int>(static_cast<int64_t>(rank) * kblocks / splits);
+    const int kb1 = static_cast<int>(static_cast<int64_t>(rank + 1) * kblocks / splits);
+    const int mv = min(BM, M - tm * BM);  // valid rows of the tile
+
+    if (threadIdx.x == 0) {
+        for (int st = 0; st < kSplitStages; ++st) {
+            mbar_init(&full[st], 1);
+            mbar_init(&empty[st], 1);
+        }
+        mbar_init(tfull, 1);
+        fence_mbar_init();
+    }
+    if (warp == 1) {
+        tmem_alloc(tmem_slot, kSplitBN);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem_base = *tmem_slot;
+
+    if (warp == 0) {
+        if (elect_one()) {
+            tma_prefetch_desc(&tmA);
+            tma_prefetch_desc(&tmB);
+            int stage = 0, issued = 0;
+            uint32_t phase = 0;
+            for (int kb = kb0; kb < kb1; ++kb) {
+                if (!mbar_wait(&empty[stage], phase ^ 1u, err, kDevTimeoutProducer)) break;
+                uint8_t *sa = smem + stage * L::kStageBytes;
+                mbar_arrive_expect_tx(&full[stage], L::kStageBytes);
+                tma_load_2d(&tmA, &full[stage], sa, kb * BK, tm * BM);
+                tma_load_2d(&tmB, &full[stage], sa + L::kABytes, kb * BK, tn * kSplitBN);
+                ++issued;
+                if (++stage == kSplitStages) {
+                    stage = 0;
+                    phase ^= 1u;
+                }
+            }
+            const int pending = issued < kSplitStages ? issued : kSplitStages;
+            for (int i = 0; i < pending; ++i) {
+                if (--stage < 0) {
+                    stage = kSplitStages - 1;
+                    phase ^= 1u;
+                }
+                mbar_wait(&full[stage], phase, err, kDevTimeoutDrain);
+            }
+        }
+    } else if (warp == 1) {
+        if (elect_one()) {
+            constexpr uint32_t idesc = idesc_e4m3_f32(BM, kSplitBN, 0);
+            int stage = 0;
+            uint32_t phase = 0;
+            bool ok = true;
+            for (int kb = kb0; kb < kb1; ++kb) {
+                if (!mbar_wait(&full[stage], phase, err, kDevTimeoutMma)) {
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+                const uint32_t a_addr = smem_u32(smem + stage * L::kStageBytes);
+                const uint32_t b_addr = a_addr + L::kABytes;
+#pragma unroll
+                for (int k = 0; k < BK / UMMA_K; ++k)
+                    umma_f8f6f4(tmem_base, sdesc_kmajor<BK>(a_addr + k * UMMA_K), sdesc_kmajor<BK>(b_addr + k * UMMA_K),
+                                idesc, (kb > kb0 || k > 0) ? 1u : 0u);
+                umma_commit(&empty[stage]);
+                if (++stage == kSplitStages) {
+                    stage = 0;
+                    phase ^= 1u;
+                }
+            }
+            if (ok) umma_commit(tfull);
+        }
+    } else {
+        // TMEM -> this CTA's partial (rows of lane quarter warp & 3)
+        const int quarter = warp & 3;
+        const bool ok = mbar_wait(tfull, 0, err, kDevTimeoutEpilogue);
+        tc_fence_after();
+        if (32 * quarter < mv) {  // warp-uniform
+            const int r = 32 * quarter + lane;
+#pragma unroll 1
+            for (int c = 0; c < kSplitBN / 32; ++c) {
+                uint32_t g[32];
+                tmem_ld_32x32b_x32(tmem_base + (static_cast<uint32_t>(32 * quarter) << 16) + c * 32, g);
+                tmem_wait_ld();
+                if (r < mv) {
+                    float4 *dst = reinterpret_cast<float4 *>(part + r * L::kPartStride + c * 32);
+#pragma unroll
+                    for (int j = 0; j < 8; ++j)
+                        dst[j] = ok ? make_float4(__uint_as_float(g[4 * j]), __uint_as_float(g[4 * j + 1]),
+                                                  __uint_as_float(g[4 * j + 2]), __uint_as_float(g[4 * j + 3]))
+                                    : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+                }
+            }
+        }
+    }
+    tc_fence_before();
+    cluster_sync_all();  // every partial of the cluster is written
+
+    // reduce rows [r0, r1) of the tile over the cluster's partials, epilogue, store
+    const OutQuant oq = make_out_quant<OUT>(ep);
+    const int64_t n_out = ep.N;
+    const int per = (mv + splits - 1) / splits;
+    const int r0 = rank * per, r1 = min(mv, r0 + per);
+    const int items = r1 > r0 ? (r1 - r0) * (kSplitBN / 4) : 0;
+    const uint32_t part_base = smem_u32(part);
+    for (int it = threadIdx.x; it < items; it += kSplitThreads) {
+        const int rr = r0 + it / (kSplitBN / 4), c4 = it % (kSplitBN / 4);
+        const uint32_t off = part_base + static_cast<uint32_t>((rr * L::kPartStride + c4 * 4) * 4);
+        float4 acc = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+        for (int sp = 0; sp < splits; ++sp) {
+            const float4 p = ld_shared_cluster_f4(mapa_shared(off, static_cast<uint32_t>(sp)));
+            acc.x += p.x;
+            acc.y += p.y;
+            acc.z += p.z;
+            acc.w += p.w;
+        }
+        const int64_t row = static_cast<int64_t>(tm) * BM + rr;
+        const int64_t col = static_cast<int64_t>(tn) * kSplitBN + c4 * 4;
+        const float rs = ep.alpha * (ep.sa_row ? __ldg(ep.sa + row) : __ldg(ep.sa));
+        const float a4[4] = {acc.x, acc.y, acc.z, acc.w};
+        float amax = 0.0f;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const int64_t n = col + j;
+            if (n >= n_out) break;
+            float v = simt_pre(a4[j], rs, row, n, ep);
+            if (ep.c_mat) v += ep.beta * load_cmat(ep, row, n);
+            if (EPI == LCML_EPI_RELU) v = fmaxf(v, 0.0f);
+            amax = fmaxf(amax, fabsf(v));
+            store_out<OUT>(ep.y, ep.ldy, row, n + ep.y_col_offset, v, oq);
+        }
+        if (ep.row_amax) atomic_max_abs(ep.row_amax + row, amax);
+    }
+    cluster_sync_all();  // no CTA exits while another may still read its partial
+    if (warp == 1) {
+        __syncwarp();
+        tc_fence_after();
+        tmem_dealloc(tmem_base, kSplitBN);
+    }
+}
+
 template <int EPI, int OUT>
 __global__ void __launch_bounds__(256) k_gemm_fp8_simt(const uint8_t *__restrict__ A, int64_t lda,
                                                        const uint8_t *__restrict__ B, int64_t ldb, int b_kmajor,
@@ -1242,6 +1432,61 @@ int launch_tc2(const lcml_fp8_gemm_desc *d, const EpiParams &ep, cudaStream_t st
     return LCML_OK;
 }
 
+// Split factor for a GEMM whose 128 x 128 tiles would leave most SMs idle:
+// S CTAs per tile (S <= 8, at least two K-blocks each, S x tiles <= SMs);
+// 0 when split-K does not apply.
+int splitk_factor(const lcml_fp8_gemm_desc *d, const EpiParams &ep) {
+    if (d->epilogue == LCML_EPI_SILU_MUL || ep.y_num_peers > 0 || d->M > 0x7fffffff || d->N > 0x7fffffff ||
+        d->K > 0x7fffffff)
+        return 0;
+    const int64_t tiles = ((d->M + BM - 1) / BM) * ((d->N + kSplitBN - 1) / kSplitBN);
+    const int64_t kblocks = (d->K + BK - 1) / BK;
+    const int64_t sms = sm_count();
+    if (2 * tiles > sms || kblocks < 4) return 0;
+    int64_t s = sms / tiles;
+    if (s > kSplitMax) s = kSplitMax;
+    if (s > kblocks / 2) s = kblocks / 2;
+    return s >= 2 ? static_cast<int>(s) : 0;
+}
+
+template <int EPI, int OUT>
+int launch_splitk(const lcml_fp8_gemm_desc *d, const EpiParams &ep, cudaStream_t st, int splits) {
+    using L = SplitLayout;
+    static_assert(L::kSmemBytes <= kSmemLimit, "shared memory layout does not fit");
+    auto kern = k_gemm_fp8_splitk<EPI, OUT>;
+    static std::once_flag once;
+    static cudaError_t attr_err = cudaSuccess;
+    std::call_once(once, [&] {
+        attr_err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kSmemBytes);
+    });
+    if (attr_err != cudaSuccess)
+        return set_error(LCML_ERR_CUDA, "cudaFuncSetAttribute(smem=%d) failed: %s", L::kSmemBytes,
+                         cudaGetErrorString(attr_err));
+    CUtensorMap ta, tb;
+    int rc = make_tmap(&ta, d->A, d->K, d->M, d->lda, BM);
+    if (rc) return rc;
+    rc = make_tmap(&tb, d->B, d->K, d->N, d->ldb, kSplitBN);
+    if (rc) return rc;
+    const int64_t tiles = ((d->M + BM - 1) / BM) * ((d->N + kSplitBN - 1) / kSplitBN);
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(static_cast<unsigned>(tiles * splits), 1, 1);
+    cfg.blockDim = dim3(kSplitThreads, 1, 1);
+    cfg.dynamicSmemBytes = L::kSmemBytes;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = static_cast<unsigned>(splits);
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    const cudaError_t e = cudaLaunchKernelEx(&cfg, kern, ta, tb, static_cast<int>(d->M), static_cast<int>(d->N),
+                                             static_cast<int>(d->K), splits, ep, device_error_word());
+    if (e != cudaSuccess) return set_error(LCML_ERR_CUDA, "gemm_fp8_splitk launch failed: %s", cudaGetErrorString(e));
+    LCML_LAUNCHED("gemm_fp8_splitk");
+    return LCML_OK;
+}
+
 template <int EPI, int OUT>
 int launch_simt(const lcml_fp8_gemm_desc *d, const EpiParams &ep, cudaStream_t st) {
     const int64_t n_out = (EPI == LCML_EPI_SILU_MUL) ? d->N / 2 : d->N;
@@ -1272,6 +1517,10 @@ int dispatch(const lcml_fp8_gemm_desc *d, const EpiParams &ep, cudaStream_t st, 
                         aligned(d->A, 16) && aligned(d->B, 16) && d->M <= 0x7fffffff && d->N <= 0x7fffffff &&
                         d->K <= 0x7fffffff;
     if (!tma_ok) return launch_simt<EPI, OUT>(d, ep, st);
+    if constexpr (EPI != LCML_EPI_SILU_MUL) {
+        const int splits = (g_gemm_mode & 3) == 0 ? splitk_factor(d, ep) : 0;
+        if (splits) return launch_splitk<EPI, OUT>(d, ep, st, splits);
+    }
     // CTA pairs (256 x 256 tiles, half the staged bytes per MMA) pay off once
     // the mainloop is long and there are a couple of tiles per pair; short-K
     // and narrow GEMMs are epilogue-bound and run single-CTA tiles as wide as N.

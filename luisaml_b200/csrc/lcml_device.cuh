@@ -431,6 +431,17 @@ __device__ __forceinline__ void cluster_sync_all() {
     asm volatile("barrier.cluster.arrive.release;\n\tbarrier.cluster.wait.acquire;" ::: "memory");
 }
 
+// 16-byte load from the shared memory of a CTA of this cluster (an address
+// from mapa_shared).
+__device__ __forceinline__ float4 ld_shared_cluster_f4(uint32_t addr) {
+    float4 v;
+    asm volatile("ld.shared::cluster.v4.f32 {%0, %1, %2, %3}, [%4];"
+                 : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+                 : "r"(addr)
+                 : "memory");
+    return v;
+}
+
 // ---------------------------------------------------------------------------
 // tcgen05 (5th-generation tensor cores, accumulators in TMEM)
 // ---------------------------------------------------------------------------

@@ -152,6 +152,47 @@ def test_gemm_e4m3_output(dev):
     assert (got == want).mean() > 0.99
 
 
+@pytest.mark.parametrize("M,N,K", [(1, 4096, 4096), (48, 640, 2048), (200, 1000, 2048)])
+def test_splitk_epilogues(dev, gemm_mode, M, N, K):
+    """Skinny GEMMs run split-K in a CTA cluster (partials reduced through
+    distributed shared memory): per-row / per-column scales, bias, a residual
+    (fp32 and e4m3), Relu, the row |max| and every output type against the
+    oracle, and against the single-CTA kernel (forced by mode 1)."""
+    import torch
+    import luisaml_b200 as lb
+    Aq, sa, Bq, sb = make_operands(M, N, K, seed=M + N + K, per_row=True, per_col=True, b_std=0.05)
+    rng = np.random.default_rng(K)
+    bias = rng.standard_normal(N).astype(np.float32)
+    res = rng.standard_normal((M, N)).astype(np.float32)
+    ref = np.maximum(oracle.qdq_gemm(Aq, sa, Bq, sb) + bias + res, 0.0)
+    args = (_t(Aq, dev), _t(Bq, dev), _t(sa, dev), _t(sb, dev))
+    kw = dict(c_vec=_t(bias, dev), c_mat=_t(res, dev), epilogue=lb.EPI_RELU)
+    results = {}
+    for mode in (0, 1):
+        gemm_mode(mode)
+        amax = torch.zeros(M, dtype=torch.float32, device=dev)
+        y = lb.gemm(*args, out_dtype=torch.float32, row_amax=amax, **kw).cpu().numpy()
+        assert_close(y, ref, what=f"split-K {M}x{N}x{K} mode {mode}")
+        assert np.array_equal(amax.cpu().numpy(), np.abs(y).max(axis=1))
+        yb = lb.gemm(*args, out_dtype=torch.bfloat16, **kw)
+        assert torch.equal(yb.cpu(), torch.from_numpy(y).bfloat16())
+        results[mode] = y
+    gemm_mode(0)
+    assert_close(results[0], results[1], rtol=1e-5, atol=1e-4, what="split-K vs single CTA")
+    # e4m3 residual and e4m3 output (the epilogue quantization rule on the split-K sum)
+    rs = np.float32(oracle.scale_from_amax(oracle.amax(res)))
+    rq = oracle.quantize(res, rs)
+    ys = np.float32(oracle.scale_from_amax(np.abs(ref).max()))
+    y32 = lb.gemm(*args, c_vec=_t(bias, dev), c_mat=_t(rq, dev), epilogue=lb.EPI_RELU, out_dtype=torch.float32,
+                  c_mat_scale=_t(np.float32([rs]), dev)).cpu().numpy()
+    want32 = np.maximum(oracle.qdq_gemm(Aq, sa, Bq, sb) + bias + oracle.dequantize(rq, rs), 0.0)
+    assert_close(y32, want32, what="split-K e4m3 residual")
+    y8 = lb.gemm(*args, c_vec=_t(bias, dev), c_mat=_t(rq, dev), epilogue=lb.EPI_RELU, out_dtype=torch.uint8,
+                 c_mat_scale=_t(np.float32([rs]), dev), y_scale=_t(np.float32([ys]), dev)).cpu().numpy()
+    np.testing.assert_array_equal(y8, epilogue_quantize(y32, ys))
+    assert lb.device_error() == 0
+
+
 @pytest.mark.parametrize("M,N,K", [(200, 300, 160), (64, 1024, 128)])
 def test_simt_and_tensor_core_paths_agree(dev, M, N, K):
     import torch
