@@ -6,6 +6,7 @@
 // no gather at all (X is already the GEMM's A). The epilogue fuses the
 // per-tensor x scale, per-channel w scale, bias, residual, Relu and the
 // requantization of the output.
+#include <mutex>
 #include <type_traits>
 
 #include "lcml_device.cuh"
@@ -147,6 +148,64 @@ __global__ void __launch_bounds__(kThreads) k_im2col_narrow(const uint8_t *__res
     }
 }
 
+// im2col from NHWC with VW (4 or 8) channels, one output pixel per thread:
+// the thread walks its kH x kW taps with running indices (no per-tap
+// division), packs 16 / VW taps per 16-byte vector into its row of a
+// shared-memory tile, and the block then writes its rows, which are
+// contiguous in A, with coalesced 16-byte stores. A row is Kp bytes (a
+// multiple of 16), so the tile is kRowThreads * Kp bytes of dynamic shared
+// memory.
+constexpr int kRowThreads = 128;
+
+template <int VW>
+__global__ void __launch_bounds__(kRowThreads) k_im2col_rows(const uint8_t *__restrict__ X, int H, int W, int kH,
+                                                              int kW, int oH, int oW, int sH, int sW, int pH, int pW,
+                                                              int dH, int dW, int Kp, int64_t P,
+                                                              uint8_t *__restrict__ A) {
+    using V = typename std::conditional<VW == 4, uint32_t, uint2>::type;
+    constexpr int TPC = 16 / VW;  // taps per 16-byte vector
+    extern __shared__ uint4 tile[];
+    const int chunks = Kp / 16, taps = kH * kW;
+    for (int64_t p0 = static_cast<int64_t>(blockIdx.x) * kRowThreads; p0 < P;
+         p0 += static_cast<int64_t>(gridDim.x) * kRowThreads) {
+        const int64_t p = p0 + threadIdx.x;
+        if (p < P) {
+            const int64_t t = p / oW;
+            const int ow = static_cast<int>(p - t * oW);
+            const int64_t n = t / oH;
+            const int oh = static_cast<int>(t - n * oH);
+            const int ih0 = oh * sH - pH, iw0 = ow * sW - pW;
+            const uint8_t *xn = X + n * H * W * VW;
+            uint4 *row = tile + threadIdx.x * chunks;
+            int kh = 0, kw = 0, tap = 0;
+            for (int c = 0; c < chunks; ++c) {
+                V v[TPC];
+#pragma unroll
+                for (int j = 0; j < TPC; ++j) {
+                    v[j] = V{};
+                    if (tap < taps) {
+                        const int ih = ih0 + kh * dH, iw = iw0 + kw * dW;
+                        if (ih >= 0 && ih < H && iw >= 0 && iw < W)
+                            v[j] = __ldg(reinterpret_cast<const V *>(xn + (static_cast<int64_t>(ih) * W + iw) * VW));
+                        ++tap;
+                        if (++kw == kW) {
+                            kw = 0;
+                            ++kh;
+                        }
+                    }
+                }
+                row[c] = *reinterpret_cast<const uint4 *>(v);
+            }
+        }
+        __syncthreads();
+        const int64_t rows = P - p0 < kRowThreads ? P - p0 : kRowThreads;
+        uint4 *dst = reinterpret_cast<uint4 *>(A + p0 * Kp);
+        const int64_t vecs = rows * chunks;
+        for (int64_t i = threadIdx.x; i < vecs; i += kRowThreads) dst[i] = tile[i];
+        __syncthreads();
+    }
+}
+
 int grid_for(int64_t items) {
     const int64_t per_wave = static_cast<int64_t>(sm_count()) * (2048 / kThreads);
     int64_t b = (items + kThreads - 1) / kThreads;
@@ -186,6 +245,26 @@ template <typename I>
 void launch_im2col(const lcml_fp8_conv_desc *d, const uint8_t *X, int64_t Cp, int64_t Kp, uint8_t *A, cudaStream_t st) {
     const int64_t P = d->N * d->oH * d->oW;
     const int grid = grid_for(P * (Kp / 16));
+    const int64_t row_smem = static_cast<int64_t>(kRowThreads) * Kp;
+    if ((Cp == 4 || Cp == 8) && row_smem <= 96 * 1024 && d->H * d->W * Cp < (int64_t(1) << 31)) {
+        // one pixel per thread through a shared-memory row tile (<= 96 KB: two blocks per SM)
+        int64_t blocks = (P + kRowThreads - 1) / kRowThreads;
+        const int64_t cap = static_cast<int64_t>(sm_count()) * 16;
+        if (blocks > cap) blocks = cap;
+        auto k4 = k_im2col_rows<4>;
+        auto k8 = k_im2col_rows<8>;
+        auto kern = Cp == 4 ? k4 : k8;
+        static std::once_flag once;
+        std::call_once(once, [&] {
+            cudaFuncSetAttribute(k4, cudaFuncAttributeMaxDynamicSharedMemorySize, 96 * 1024);
+            cudaFuncSetAttribute(k8, cudaFuncAttributeMaxDynamicSharedMemorySize, 96 * 1024);
+        });
+        kern<<<static_cast<int>(blocks), kRowThreads, static_cast<size_t>(row_smem), st>>>(
+            X, static_cast<int>(d->H), static_cast<int>(d->W), static_cast<int>(d->kH), static_cast<int>(d->kW),
+            static_cast<int>(d->oH), static_cast<int>(d->oW), d->sH, d->sW, d->pH, d->pW, d->dH, d->dW,
+            static_cast<int>(Kp), P, A);
+        return;
+    }
     if (Cp == 4)
         k_im2col_narrow<I, 4><<<grid, kThreads, 0, st>>>(X, d->N, d->H, d->W, d->kH, d->kW, d->oH, d->oW, d->sH, d->sW,
                                                          d->pH, d->pW, d->dH, d->dW, Kp, A);

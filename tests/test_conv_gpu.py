@@ -124,16 +124,22 @@ def _implicit(C, k, stride, pad, nhwc):
 
 
 @pytest.mark.parametrize("name,N,C,H,M,k,stride,pad,nhwc,dil", CASES)
-def test_conv_shapes(dev, conv_mode, name, N, C, H, M, k, stride, pad, nhwc, dil):
-    """Every lowering vs the oracle: direct 1x1, materialized im2col (mode 1)
-    and, for NHWC inputs with C % 64 == 0, the implicit GEMM (TMA im2col
-    loads; the default there, with or without a workspace), whose result
-    must equal the materialized one bit for bit."""
+def test_conv_shapes(dev, conv_mode, gemm_mode, name, N, C, H, M, k, stride, pad, nhwc, dil):
+    """Every lowering vs the oracle: direct 1x1, materialized im2col (conv
+    mode 1) and, for NHWC inputs with C % 64 == 0, the implicit GEMM (TMA
+    im2col loads; the default there, with or without a workspace), whose
+    result must equal the materialized one bit for bit when both run the
+    single-CTA GEMM (GEMM mode 1). With automatic GEMM selection a small
+    materialized conv may run split-K (another summation order): checked
+    against the oracle."""
     rng = np.random.default_rng(sum(name.encode()))
     X = rng.standard_normal((N, C, H, H)).astype(np.float32)
     W = (rng.standard_normal((M, C, k, k)) * np.sqrt(2.0 / (C * k * k))).astype(np.float32)
     bias = (rng.standard_normal(M) * 0.01).astype(np.float32)
     conv_mode(1)
+    got_auto, ref, _ = _run_conv(dev, X, W, bias, stride, pad, nhwc_in=nhwc, dil=dil)
+    assert_close(got_auto, ref, what=name + " (automatic GEMM selection)")
+    gemm_mode(1)
     got, ref, ws = _run_conv(dev, X, W, bias, stride, pad, nhwc_in=nhwc, dil=dil)
     assert (ws == 0) == (name == "1x1_direct")
     assert_close(got, ref, what=name)

@@ -245,12 +245,6 @@ def test_large_8192_sampled_rows(dev):
     np.testing.assert_allclose(got, want, rtol=1e-4, atol=1e-2)
 
 
-@pytest.fixture
-def gemm_mode():
-    import luisaml_b200 as lb
-    yield lambda m: lb.lib().lcml_fp8_gemm_set_mode(m)
-    lb.lib().lcml_fp8_gemm_set_mode(0)
-
 
 @pytest.mark.parametrize("mode", [1, 2])
 @pytest.mark.parametrize("M,N,K,per_row,per_col", [
