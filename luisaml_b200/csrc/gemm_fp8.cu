@@ -1021,7 +1021,7 @@ __device__ __forceinline__ float simt_pre(float acc, float row_scale, int64_t ro
 // thread of every CTA reaches both barriers, also after a timed-out wait.
 // ---------------------------------------------------------------------------
 constexpr int kSplitBN = 128;
-constexpr int kSplitStages = 4;
+constexpr int kSplitStages = 7;
 constexpr int kSplitThreads = 192;  // warp 0 TMA producer, warp 1 MMA issuer, warps 2-5 TMEM readers
 constexpr int kSplitMax = 8;        // portable cluster size
 
@@ -1030,9 +1030,12 @@ struct SplitLayout {
     static constexpr int kBBytes = kSplitBN * BK;
     static constexpr int kStageBytes = kABytes + kBBytes;
     static constexpr int kPartStride = kSplitBN + 4;  // floats per partial row: 16-byte skew, conflict-free rows
-    static constexpr int kPartOffset = kSplitStages * kStageBytes;
-    static constexpr int kBarOffset = kPartOffset + BM * kPartStride * 4;
+    // the partial reuses the operand ring: it is written only after the MMAs
+    // have committed, i.e. after every stage has been loaded and read
+    static constexpr int kPartOffset = 0;
+    static constexpr int kBarOffset = kSplitStages * kStageBytes;
     static constexpr int kSmemBytes = kBarOffset + 256 + 1024;  // barriers, TMEM slot, +1024 alignment
+    static_assert(BM * kPartStride * 4 <= kBarOffset, "partial tile must fit in the operand ring");
 };
 
 template <int EPI, int OUT>
@@ -1178,6 +1181,45 @@ __global__ void __launch_bounds__(kSplitThreads, 1)
         const float rs = ep.alpha * (ep.sa_row ? __ldg(ep.sa + row) : __ldg(ep.sa));
         const float a4[4] = {acc.x, acc.y, acc.z, acc.w};
         float amax = 0.0f;
+        constexpr int ES = out_es(OUT);
+        uint8_t *yp = static_cast<uint8_t *>(ep.y) + (row * ep.ldy + col + ep.y_col_offset) * ES;
+        if (col + 4 <= n_out && !ep.c_mat && aligned(yp, 4 * ES) && (!ep.sb_col || aligned(ep.sb + col, 16)) &&
+            (ep.c_vec_mode != 3 || aligned(ep.c_vec + col, 16))) {
+            // four whole columns: vector loads of the factors, one vector store (same arithmetic as simt_pre)
+            const float4 sb4 = ep.sb_col ? __ldg(reinterpret_cast<const float4 *>(ep.sb + col))
+                                         : make_float4(__ldg(ep.sb), __ldg(ep.sb), __ldg(ep.sb), __ldg(ep.sb));
+            float4 c4v = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+            if (ep.c_vec_mode == 3) c4v = __ldg(reinterpret_cast<const float4 *>(ep.c_vec + col));
+            else if (ep.c_vec_mode == 1) c4v = make_float4(__ldg(ep.c_vec), __ldg(ep.c_vec), __ldg(ep.c_vec), __ldg(ep.c_vec));
+            else if (ep.c_vec_mode == 2) {
+                const float c = __ldg(ep.c_vec + row);
+                c4v = make_float4(c, c, c, c);
+            }
+            const float sbs[4] = {sb4.x, sb4.y, sb4.z, sb4.w}, cs[4] = {c4v.x, c4v.y, c4v.z, c4v.w};
+            float v[4];
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                v[j] = a4[j] * rs * sbs[j];
+                if (ep.c_vec_mode) v[j] = fmaf(ep.beta, cs[j], v[j]);
+                if (EPI == LCML_EPI_RELU) v[j] = fmaxf(v[j], 0.0f);
+                amax = fmaxf(amax, fabsf(v[j]));
+            }
+            if (OUT == kOutF32) {
+                *reinterpret_cast<float4 *>(yp) = make_float4(v[0], v[1], v[2], v[3]);
+            } else if (OUT == kOutBF16) {
+                __nv_bfloat162 h0 = __floats2bfloat162_rn(v[0], v[1]), h1 = __floats2bfloat162_rn(v[2], v[3]);
+                *reinterpret_cast<uint2 *>(yp) =
+                    make_uint2(*reinterpret_cast<uint32_t *>(&h0), *reinterpret_cast<uint32_t *>(&h1));
+            } else {
+                uint32_t w = 0;
+#pragma unroll
+                for (int j = 0; j < 4; ++j)
+                    w |= (oq.s_ok ? quantize_rcp1(v[j], oq.r) : quantize1(v[j], oq.ys)) << (8 * j);
+                *reinterpret_cast<uint32_t *>(yp) = w;
+            }
+            if (ep.row_amax) atomic_max_abs(ep.row_amax + row, amax);
+            continue;
+        }
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
             const int64_t n = col + j;
