@@ -67,7 +67,10 @@ def profile_traffic(name):
 
 
 class ClockSampler:
-    """nvidia-smi samples of SM clock / throttle reasons while the timed region runs."""
+    """SM clock and throttle reasons sampled while the timed region runs: an
+    NVML polling thread (every 0.5 ms, so even a timed region of a few
+    milliseconds gets samples; one sample is taken before the region
+    starts), or nvidia-smi -lms 100 when NVML is not importable. Read-only."""
 
     FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
@@ -76,8 +79,48 @@ class ClockSampler:
     def __init__(self, gpu_index):
         self.gpu_index = gpu_index
         self.proc = None
+        self.thread = None
+        self.lines = []
+
+    def _nvml_index(self):
+        vis = os.environ.get("CUDA_VISIBLE_DEVICES", "")
+        ids = [v.strip() for v in vis.split(",") if v.strip()]
+        if ids and all(v.isdigit() for v in ids) and self.gpu_index < len(ids):
+            return int(ids[self.gpu_index])
+        return self.gpu_index
+
+    def _poll(self):
+        import pynvml
+        bits = [("hw_slowdown", pynvml.nvmlClocksEventReasonHwSlowdown),
+                ("hw_thermal_slowdown", pynvml.nvmlClocksEventReasonHwThermalSlowdown),
+                ("sw_thermal_slowdown", pynvml.nvmlClocksEventReasonSwThermalSlowdown),
+                ("sw_power_cap", pynvml.nvmlClocksEventReasonSwPowerCap)]
+        while True:
+            try:
+                sm = pynvml.nvmlDeviceGetClockInfo(self.handle, pynvml.NVML_CLOCK_SM)
+                r = pynvml.nvmlDeviceGetCurrentClocksEventReasons(self.handle)
+            except Exception:
+                return
+            f = ["Active" if r & b else "Not Active" for _, b in bits]
+            self.lines.append(", ".join([str(self.gpu_index), str(sm), str(self.max_sm), "0", hex(r)] + f))
+            if self.stop.wait(0.0005):
+                return
 
     def __enter__(self):
+        import threading
+        try:
+            import pynvml
+            pynvml.nvmlInit()
+            self.handle = pynvml.nvmlDeviceGetHandleByIndex(self._nvml_index())
+            self.max_sm = pynvml.nvmlDeviceGetMaxClockInfo(self.handle, pynvml.NVML_CLOCK_SM)
+            self.stop = threading.Event()
+            self.thread = threading.Thread(target=self._poll, daemon=True)
+            self.thread.start()
+            while not self.lines and self.thread.is_alive():  # first sample before the region starts
+                time.sleep(0.0002)
+            return self
+        except Exception:
+            self.thread = None
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "100",
@@ -87,7 +130,10 @@ class ClockSampler:
         return self
 
     def __exit__(self, *exc):
-        self.lines = []
+        if self.thread is not None:
+            self.stop.set()
+            self.thread.join(timeout=5)
+            return
         if self.proc is not None:
             self.proc.terminate()
             try:
