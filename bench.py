@@ -331,7 +331,7 @@ class MlpWorkload(GraphWorkload):
         self.setup_graph(dev, text, blob, {"input": x}, {"output": y})
 
     def dominant(self):
-        return {"kernel": "whole forward (5 kernels)", "bound": "latency", "unit": "TFLOP/s", "work": self.flops,
+        return {"kernel": "whole forward (3 kernels)", "bound": "latency", "unit": "TFLOP/s", "work": self.flops,
                 "profile": "mlp", "kernel_only": False}
 
     def cpu_sample(self, budget_s=5.0):

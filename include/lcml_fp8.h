@@ -245,6 +245,11 @@ int lcml_fp8_gemm_rowquant_noalloc(const lcml_fp8_gemm_desc *desc, uint8_t *q, f
 int lcml_gemm_f32(const float *A, const float *B, const float *C, int64_t M, int64_t N, int64_t K, int transA,
                   int transB, float alpha, float beta, int c_ndim, int64_t c_d0, int64_t c_d1, float *Y,
                   lcml_stream_t stream);
+/* The same Gemm followed by Relu (Y = Y > 0 ? Y : 0, as the Relu operator) in one
+ * kernel: the executor's fusion of an fp32 Gemm whose only reader is a Relu. */
+int lcml_gemm_f32_relu(const float *A, const float *B, const float *C, int64_t M, int64_t N, int64_t K, int transA,
+                       int transB, float alpha, float beta, int c_ndim, int64_t c_d0, int64_t c_d1, float *Y,
+                       lcml_stream_t stream);
 
 /*
  * FP8 2-D convolution on the tensor cores (the DequantizeLinear -> Conv ->

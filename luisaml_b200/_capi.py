@@ -100,6 +100,8 @@ PROTOTYPES = {
     "lcml_enable_peer_access": [_ci],
     "lcml_gemm_f32": [_vp, _vp, _vp, _c_i64, _c_i64, _c_i64, _ci, _ci, ctypes.c_float, ctypes.c_float, _ci, _c_i64,
                       _c_i64, _vp, _vp],
+    "lcml_gemm_f32_relu": [_vp, _vp, _vp, _c_i64, _c_i64, _c_i64, _ci, _ci, ctypes.c_float, ctypes.c_float, _ci, _c_i64,
+                      _c_i64, _vp, _vp],
     "lcml_fp8_quantize": [_vp, _c_i64, _c_i64, _c_i64, _vp, _ci, _vp, _vp],
     "lcml_fp8_quantize_from_amax": [_vp, _c_i64, _c_i64, _c_i64, _vp, _vp, _vp, _vp],
     "lcml_fp8_quantize_rows_dynamic": [_vp, _c_i64, _c_i64, _c_i64, _vp, _vp, _vp],

@@ -667,6 +667,25 @@ void NetworkInstance::run_fusion_pass() {
         table_.own("#conv_workspace", std::move(ws));
     }
 
+    // ---- fp32 Gemm -> Relu (graphs without QDQ on the activations, e.g. the MLP): one kernel
+    for (size_t i = 0; i < nodes.size(); ++i) {
+        FusionInfo &fi = *fusion_[i];
+        if (fi.skip || fi.op || nodes[i].get_op_type() != "Gemm") continue;
+        const auto &outs = nodes[i].get_outputs();
+        if (outs.size() != 1 || outs[0]->get_dtype() != DataType::FLOAT) continue;
+        const int r = sole_consumer(outs[0]->get_name());
+        if (r < 0 || nodes[r].get_op_type() != "Relu" || fusion_[r]->skip || fusion_[r]->op) continue;
+        bool fp32 = true;
+        for (const auto *x : nodes[i].get_inputs()) fp32 = fp32 && x->get_dtype() == DataType::FLOAT;
+        if (!fp32) continue;
+        fi.op = make_gemm_f32_relu(nodes[i]);
+        for (const auto *x : nodes[i].get_inputs()) fi.inputs.push_back(x->get_name());
+        fi.outputs = {nodes[r].get_outputs()[0]->get_name()};
+        fi.note = "fp32 Gemm + Relu in one kernel";
+        fusion_[r]->skip = true;
+        fusion_[r]->note = "Relu folded into the preceding Gemm";
+    }
+
     // ---- Dead nodes: a node that still runs but whose outputs nobody reads any more
     // (a DequantizeLinear whose consumers all read its e4m3 input inside a fusion) is dropped.
     auto effective_inputs = [&](size_t i) {

@@ -112,6 +112,7 @@ class Gemm : public StreamOperator {
 public:
     float alpha, beta;
     int64_t transA, transB;
+    bool relu = false;  // fused Relu (lcml_gemm_f32_relu)
     Gemm(float a, float b, int64_t ta, int64_t tb) : StreamOperator("Gemm"), alpha(a), beta(b), transA(ta), transB(tb) {}
     void forward(Span in, Span out) override {
         const ITensor &A = in[0].get(), &B = in[1].get();
@@ -134,9 +135,10 @@ public:
             d0 = Ct.ndim() >= 1 ? Ct.shape(0) : 0;
             d1 = Ct.ndim() >= 2 ? Ct.shape(1) : 0;
         }
-        check_status(lcml_gemm_f32(A.ptr<float>(), B.ptr<float>(), C, M, N, K, static_cast<int>(transA),
-                                   static_cast<int>(transB), alpha, beta, c_ndim, d0, d1, Y.ptr<float>(), stream_),
-                     "Gemm");
+        auto fn = relu ? lcml_gemm_f32_relu : lcml_gemm_f32;
+        check_status(fn(A.ptr<float>(), B.ptr<float>(), C, M, N, K, static_cast<int>(transA), static_cast<int>(transB),
+                        alpha, beta, c_ndim, d0, d1, Y.ptr<float>(), stream_),
+                     relu ? "Gemm + Relu" : "Gemm");
     }
 };
 
@@ -437,6 +439,13 @@ void QdqGlobalAveragePool::forward(Span in, Span out) {
 // ------------------------------------------------------------------ registration
 REGISTER_TO_DEFAULT_OPSET(QuantizeLinear) { return std::make_unique<QuantizeLinear>(get_int(node, "axis", 1)); };
 REGISTER_TO_DEFAULT_OPSET(DequantizeLinear) { return std::make_unique<DequantizeLinear>(get_int(node, "axis", 1)); };
+std::unique_ptr<Operator> make_gemm_f32_relu(const Node &node) {
+    auto g = std::make_unique<Gemm>(get_float(node, "alpha", 1.0f), get_float(node, "beta", 1.0f),
+                                    get_int(node, "transA", 0), get_int(node, "transB", 0));
+    g->relu = true;
+    return g;
+}
+
 REGISTER_TO_DEFAULT_OPSET(Gemm) {
     return std::make_unique<Gemm>(get_float(node, "alpha", 1.0f), get_float(node, "beta", 1.0f), get_int(node, "transA", 0),
                                   get_int(node, "transB", 0));

@@ -85,4 +85,9 @@ public:
     void forward(std::span<std::reference_wrapper<ITensor>> in, std::span<std::reference_wrapper<ITensor>> out) override;
 };
 
+// An fp32 Gemm node (alpha, beta, transA, transB read from it) whose output
+// goes through Relu in the same kernel (lcml_gemm_f32_relu): built by the
+// fusion pass for a Gemm whose only reader is a Relu.
+std::unique_ptr<Operator> make_gemm_f32_relu(const Node &gemm);
+
 }// namespace lcml::onnx
