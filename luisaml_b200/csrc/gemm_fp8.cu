@@ -1024,6 +1024,7 @@ constexpr int kSplitBN = 128;
 constexpr int kSplitStages = 7;
 constexpr int kSplitThreads = 192;  // warp 0 TMA producer, warp 1 MMA issuer, warps 2-5 TMEM readers
 constexpr int kSplitMax = 8;        // portable cluster size
+constexpr int kRedBatch = 2;        // items per thread whose remote loads are in flight together
 
 struct SplitLayout {
     static constexpr int kABytes = BM * BK;
@@ -1165,72 +1166,92 @@ __global__ void __launch_bounds__(kSplitThreads, 1)
     const int r0 = rank * per, r1 = min(mv, r0 + per);
     const int items = r1 > r0 ? (r1 - r0) * (kSplitBN / 4) : 0;
     const uint32_t part_base = smem_u32(part);
-    for (int it = threadIdx.x; it < items; it += kSplitThreads) {
-        const int rr = r0 + it / (kSplitBN / 4), c4 = it % (kSplitBN / 4);
-        const uint32_t off = part_base + static_cast<uint32_t>((rr * L::kPartStride + c4 * 4) * 4);
-        float4 acc = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-        for (int sp = 0; sp < splits; ++sp) {
-            const float4 p = ld_shared_cluster_f4(mapa_shared(off, static_cast<uint32_t>(sp)));
-            acc.x += p.x;
-            acc.y += p.y;
-            acc.z += p.z;
-            acc.w += p.w;
+    // A thread takes kRedBatch items at a time and issues every remote load of
+    // the batch (kRedBatch x splits) before the first add, so it waits for the
+    // distributed-shared-memory latency once per batch, not once per load.
+    // Each item's sum still runs over the partials in rank order.
+    for (int it0 = threadIdx.x; it0 < items; it0 += kSplitThreads * kRedBatch) {
+        float4 pv[kRedBatch][kSplitMax];
+#pragma unroll
+        for (int u = 0; u < kRedBatch; ++u) {
+            const int iu = it0 + u * kSplitThreads < items ? it0 + u * kSplitThreads : it0;  // past the end: reload item it0
+            const uint32_t off = part_base + static_cast<uint32_t>(((r0 + iu / (kSplitBN / 4)) * L::kPartStride +
+                                                                    (iu % (kSplitBN / 4)) * 4) * 4);
+#pragma unroll
+            for (int sp = 0; sp < kSplitMax; ++sp)
+                if (sp < splits) pv[u][sp] = ld_shared_cluster_f4(mapa_shared(off, static_cast<uint32_t>(sp)));
         }
-        const int64_t row = static_cast<int64_t>(tm) * BM + rr;
-        const int64_t col = static_cast<int64_t>(tn) * kSplitBN + c4 * 4;
-        const float rs = ep.alpha * (ep.sa_row ? __ldg(ep.sa + row) : __ldg(ep.sa));
-        const float a4[4] = {acc.x, acc.y, acc.z, acc.w};
-        float amax = 0.0f;
-        constexpr int ES = out_es(OUT);
-        uint8_t *yp = static_cast<uint8_t *>(ep.y) + (row * ep.ldy + col + ep.y_col_offset) * ES;
-        if (col + 4 <= n_out && !ep.c_mat && aligned(yp, 4 * ES) && (!ep.sb_col || aligned(ep.sb + col, 16)) &&
-            (ep.c_vec_mode != 3 || aligned(ep.c_vec + col, 16))) {
-            // four whole columns: vector loads of the factors, one vector store (same arithmetic as simt_pre)
-            const float4 sb4 = ep.sb_col ? __ldg(reinterpret_cast<const float4 *>(ep.sb + col))
-                                         : make_float4(__ldg(ep.sb), __ldg(ep.sb), __ldg(ep.sb), __ldg(ep.sb));
-            float4 c4v = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-            if (ep.c_vec_mode == 3) c4v = __ldg(reinterpret_cast<const float4 *>(ep.c_vec + col));
-            else if (ep.c_vec_mode == 1) c4v = make_float4(__ldg(ep.c_vec), __ldg(ep.c_vec), __ldg(ep.c_vec), __ldg(ep.c_vec));
-            else if (ep.c_vec_mode == 2) {
-                const float c = __ldg(ep.c_vec + row);
-                c4v = make_float4(c, c, c, c);
+#pragma unroll
+        for (int u = 0; u < kRedBatch; ++u) {
+            const int it = it0 + u * kSplitThreads;
+            if (it >= items) break;
+            const int rr = r0 + it / (kSplitBN / 4), c4 = it % (kSplitBN / 4);
+            float4 acc = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+#pragma unroll
+            for (int sp = 0; sp < kSplitMax; ++sp) {
+                if (sp < splits) {
+                    acc.x += pv[u][sp].x;
+                    acc.y += pv[u][sp].y;
+                    acc.z += pv[u][sp].z;
+                    acc.w += pv[u][sp].w;
+                }
             }
-            const float sbs[4] = {sb4.x, sb4.y, sb4.z, sb4.w}, cs[4] = {c4v.x, c4v.y, c4v.z, c4v.w};
-            float v[4];
+            const int64_t row = static_cast<int64_t>(tm) * BM + rr;
+            const int64_t col = static_cast<int64_t>(tn) * kSplitBN + c4 * 4;
+            const float rs = ep.alpha * (ep.sa_row ? __ldg(ep.sa + row) : __ldg(ep.sa));
+            const float a4[4] = {acc.x, acc.y, acc.z, acc.w};
+            float amax = 0.0f;
+            constexpr int ES = out_es(OUT);
+            uint8_t *yp = static_cast<uint8_t *>(ep.y) + (row * ep.ldy + col + ep.y_col_offset) * ES;
+            if (col + 4 <= n_out && !ep.c_mat && aligned(yp, 4 * ES) && (!ep.sb_col || aligned(ep.sb + col, 16)) &&
+                (ep.c_vec_mode != 3 || aligned(ep.c_vec + col, 16))) {
+                // four whole columns: vector loads of the factors, one vector store (same arithmetic as simt_pre)
+                const float4 sb4 = ep.sb_col ? __ldg(reinterpret_cast<const float4 *>(ep.sb + col))
+                                             : make_float4(__ldg(ep.sb), __ldg(ep.sb), __ldg(ep.sb), __ldg(ep.sb));
+                float4 c4v = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+                if (ep.c_vec_mode == 3) c4v = __ldg(reinterpret_cast<const float4 *>(ep.c_vec + col));
+                else if (ep.c_vec_mode == 1) c4v = make_float4(__ldg(ep.c_vec), __ldg(ep.c_vec), __ldg(ep.c_vec), __ldg(ep.c_vec));
+                else if (ep.c_vec_mode == 2) {
+                    const float c = __ldg(ep.c_vec + row);
+                    c4v = make_float4(c, c, c, c);
+                }
+                const float sbs[4] = {sb4.x, sb4.y, sb4.z, sb4.w}, cs[4] = {c4v.x, c4v.y, c4v.z, c4v.w};
+                float v[4];
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    v[j] = a4[j] * rs * sbs[j];
+                    if (ep.c_vec_mode) v[j] = fmaf(ep.beta, cs[j], v[j]);
+                    if (EPI == LCML_EPI_RELU) v[j] = fmaxf(v[j], 0.0f);
+                    amax = fmaxf(amax, fabsf(v[j]));
+                }
+                if (OUT == kOutF32) {
+                    *reinterpret_cast<float4 *>(yp) = make_float4(v[0], v[1], v[2], v[3]);
+                } else if (OUT == kOutBF16) {
+                    __nv_bfloat162 h0 = __floats2bfloat162_rn(v[0], v[1]), h1 = __floats2bfloat162_rn(v[2], v[3]);
+                    *reinterpret_cast<uint2 *>(yp) =
+                        make_uint2(*reinterpret_cast<uint32_t *>(&h0), *reinterpret_cast<uint32_t *>(&h1));
+                } else {
+                    uint32_t w = 0;
+#pragma unroll
+                    for (int j = 0; j < 4; ++j)
+                        w |= (oq.s_ok ? quantize_rcp1(v[j], oq.r) : quantize1(v[j], oq.ys)) << (8 * j);
+                    *reinterpret_cast<uint32_t *>(yp) = w;
+                }
+                if (ep.row_amax) atomic_max_abs(ep.row_amax + row, amax);
+                continue;
+            }
 #pragma unroll
             for (int j = 0; j < 4; ++j) {
-                v[j] = a4[j] * rs * sbs[j];
-                if (ep.c_vec_mode) v[j] = fmaf(ep.beta, cs[j], v[j]);
-                if (EPI == LCML_EPI_RELU) v[j] = fmaxf(v[j], 0.0f);
-                amax = fmaxf(amax, fabsf(v[j]));
-            }
-            if (OUT == kOutF32) {
-                *reinterpret_cast<float4 *>(yp) = make_float4(v[0], v[1], v[2], v[3]);
-            } else if (OUT == kOutBF16) {
-                __nv_bfloat162 h0 = __floats2bfloat162_rn(v[0], v[1]), h1 = __floats2bfloat162_rn(v[2], v[3]);
-                *reinterpret_cast<uint2 *>(yp) =
-                    make_uint2(*reinterpret_cast<uint32_t *>(&h0), *reinterpret_cast<uint32_t *>(&h1));
-            } else {
-                uint32_t w = 0;
-#pragma unroll
-                for (int j = 0; j < 4; ++j)
-                    w |= (oq.s_ok ? quantize_rcp1(v[j], oq.r) : quantize1(v[j], oq.ys)) << (8 * j);
-                *reinterpret_cast<uint32_t *>(yp) = w;
+                const int64_t n = col + j;
+                if (n >= n_out) break;
+                float v = simt_pre(a4[j], rs, row, n, ep);
+                if (ep.c_mat) v += ep.beta * load_cmat(ep, row, n);
+                if (EPI == LCML_EPI_RELU) v = fmaxf(v, 0.0f);
+                amax = fmaxf(amax, fabsf(v));
+                store_out<OUT>(ep.y, ep.ldy, row, n + ep.y_col_offset, v, oq);
             }
             if (ep.row_amax) atomic_max_abs(ep.row_amax + row, amax);
-            continue;
         }
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-            const int64_t n = col + j;
-            if (n >= n_out) break;
-            float v = simt_pre(a4[j], rs, row, n, ep);
-            if (ep.c_mat) v += ep.beta * load_cmat(ep, row, n);
-            if (EPI == LCML_EPI_RELU) v = fmaxf(v, 0.0f);
-            amax = fmaxf(amax, fabsf(v));
-            store_out<OUT>(ep.y, ep.ldy, row, n + ep.y_col_offset, v, oq);
-        }
-        if (ep.row_amax) atomic_max_abs(ep.row_amax + row, amax);
     }
     cluster_sync_all();  // no CTA exits while another may still read its partial
     if (warp == 1) {
@@ -1312,7 +1333,8 @@ __global__ void __launch_bounds__(256) k_gemm_fp8_simt(const uint8_t *__restrict
 // Host side
 // ---------------------------------------------------------------------------
 // Kernel selection override for tests: bits 0-1: 0 automatic, 1 single-CTA,
-// 2 CTA pair; bit 2: store the output with plain stores instead of TMA.
+// 2 CTA pair, 3 split-K wherever its tile count allows (also M > 128);
+// bit 2: store the output with plain stores instead of TMA.
 int g_gemm_mode = 0;
 
 PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
@@ -1476,10 +1498,14 @@ int launch_tc2(const lcml_fp8_gemm_desc *d, const EpiParams &ep, cudaStream_t st
 
 // Split factor for a GEMM whose 128 x 128 tiles would leave most SMs idle:
 // S CTAs per tile (S <= 8, at least two K-blocks each, S x tiles <= SMs);
-// 0 when split-K does not apply.
-int splitk_factor(const lcml_fp8_gemm_desc *d, const EpiParams &ep) {
+// 0 when split-K does not apply. Only GEMMs with one row of tiles (M <= 128)
+// split unless `any_m`: the partials cross distributed shared memory at a few
+// tens of GB/s per SM, so once M spans two or more row tiles, one CTA per
+// tile over the whole K is faster (1024^3: 12.5 vs 15.6 us; 256 x 1024 x
+// 1024: 11.8 vs 14.1 us on B200).
+int splitk_factor(const lcml_fp8_gemm_desc *d, const EpiParams &ep, bool any_m) {
     if (d->epilogue == LCML_EPI_SILU_MUL || ep.y_num_peers > 0 || d->M > 0x7fffffff || d->N > 0x7fffffff ||
-        d->K > 0x7fffffff)
+        d->K > 0x7fffffff || (!any_m && d->M > BM))
         return 0;
     const int64_t tiles = ((d->M + BM - 1) / BM) * ((d->N + kSplitBN - 1) / kSplitBN);
     const int64_t kblocks = (d->K + BK - 1) / BK;
@@ -1560,7 +1586,8 @@ int dispatch(const lcml_fp8_gemm_desc *d, const EpiParams &ep, cudaStream_t st, 
                         d->K <= 0x7fffffff;
     if (!tma_ok) return launch_simt<EPI, OUT>(d, ep, st);
     if constexpr (EPI != LCML_EPI_SILU_MUL) {
-        const int splits = (g_gemm_mode & 3) == 0 ? splitk_factor(d, ep) : 0;
+        const int mode = g_gemm_mode & 3;
+        const int splits = (mode == 0 || mode == 3) ? splitk_factor(d, ep, mode == 3) : 0;
         if (splits) return launch_splitk<EPI, OUT>(d, ep, st, splits);
     }
     // CTA pairs (256 x 256 tiles, half the staged bytes per MMA) pay off once

@@ -75,7 +75,8 @@ def assert_close(got, ref, rtol=RTOL, atol=ATOL, what="", extra=0.0):
 @pytest.fixture
 def gemm_mode():
     """Sets the GEMM kernel selection hook (0 automatic, 1 single-CTA
-    tiles, 2 CTA pairs; bit 2 plain stores) and restores automatic after."""
+    tiles, 2 CTA pairs, 3 split-K also for M > 128; bit 2 plain stores) and
+    restores automatic after."""
     import luisaml_b200 as lb
     yield lambda m: lb.lib().lcml_fp8_gemm_set_mode(m)
     lb.lib().lcml_fp8_gemm_set_mode(0)

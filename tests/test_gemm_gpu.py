@@ -157,7 +157,9 @@ def test_splitk_epilogues(dev, gemm_mode, M, N, K):
     """Skinny GEMMs run split-K in a CTA cluster (partials reduced through
     distributed shared memory): per-row / per-column scales, bias, a residual
     (fp32 and e4m3), Relu, the row |max| and every output type against the
-    oracle, and against the single-CTA kernel (forced by mode 1)."""
+    oracle, and against the single-CTA kernel (forced by mode 1). M > 128
+    (two row tiles, the last one partial) takes split-K only when mode 3
+    forces it; automatic selection gives it single-CTA tiles."""
     import torch
     import luisaml_b200 as lb
     Aq, sa, Bq, sb = make_operands(M, N, K, seed=M + N + K, per_row=True, per_col=True, b_std=0.05)
@@ -168,7 +170,7 @@ def test_splitk_epilogues(dev, gemm_mode, M, N, K):
     args = (_t(Aq, dev), _t(Bq, dev), _t(sa, dev), _t(sb, dev))
     kw = dict(c_vec=_t(bias, dev), c_mat=_t(res, dev), epilogue=lb.EPI_RELU)
     results = {}
-    for mode in (0, 1):
+    for mode in (0, 1, 3):
         gemm_mode(mode)
         amax = torch.zeros(M, dtype=torch.float32, device=dev)
         y = lb.gemm(*args, out_dtype=torch.float32, row_amax=amax, **kw).cpu().numpy()
@@ -178,7 +180,8 @@ def test_splitk_epilogues(dev, gemm_mode, M, N, K):
         assert torch.equal(yb.cpu(), torch.from_numpy(y).bfloat16())
         results[mode] = y
     gemm_mode(0)
-    assert_close(results[0], results[1], rtol=1e-5, atol=1e-4, what="split-K vs single CTA")
+    assert_close(results[0], results[1], rtol=1e-5, atol=1e-4, what="automatic vs single CTA")
+    assert_close(results[3], results[1], rtol=1e-5, atol=1e-4, what="split-K vs single CTA")
     # e4m3 residual and e4m3 output (the epilogue quantization rule on the split-K sum)
     rs = np.float32(oracle.scale_from_amax(oracle.amax(res)))
     rq = oracle.quantize(res, rs)
