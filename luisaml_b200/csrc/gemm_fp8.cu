@@ -1261,6 +1261,124 @@ __global__ void __launch_bounds__(kSplitThreads, 1)
     }
 }
 
+// ---------------------------------------------------------------------------
+// Decode-sized GEMM (M <= 4 rows of A): a streaming GEMV on the CUDA cores.
+// With one to four rows the work is one read of B (N x K e4m3 bytes); a
+// 128-row tensor-core tile would be 1-3 % used, and split-K adds two cluster
+// barriers and a reduction through distributed shared memory to the stream.
+// Each CTA stages A as floats in shared memory, laid out [row][q][chunk] so
+// that lanes reading consecutive 16-byte chunks of B read consecutive float4s
+// of A (no bank conflicts). A warp owns kGemvRows rows of B at a time; every
+// lane issues all of its 16-byte loads of a step before the first FMA,
+// decodes the codes exactly through f16x2 and accumulates the products in
+// fp32; a fixed warp-shuffle tree sums the lanes (deterministic). Lane 0 runs
+// the per-element epilogue of the other kernels (scales, beta*C, residual,
+// Relu, row |max|, output conversion).
+// ---------------------------------------------------------------------------
+constexpr int kGemvMaxM = 4;
+constexpr int kGemvThreads = 256;
+constexpr int kGemvRows = 2;     // rows of B per warp in flight
+constexpr int kGemvChunks = 8;   // 16-byte chunks per lane per row and step: 4 KB of a row per warp step
+constexpr int kGemvSmemMax = 48 * 1024;
+
+template <int MR, int EPI, int OUT>
+__global__ void __launch_bounds__(kGemvThreads) k_gemv_fp8(const uint8_t *__restrict__ A, int64_t lda,
+                                                           const uint8_t *__restrict__ B, int64_t ldb, int M, int N,
+                                                           int K, EpiParams ep) {
+    extern __shared__ float4 sA4[];  // [MR][4][K/16]: float4 q of chunk c of row m at m*(K/4) + q*(K/16) + c
+    const int kc = K / 16;           // 16-byte chunks per row (K % 16 == 0)
+    const int lane = threadIdx.x & 31;
+    const int gw = static_cast<int>(blockIdx.x) * (kGemvThreads / 32) + (threadIdx.x >> 5);
+    const int nw = static_cast<int>(gridDim.x) * (kGemvThreads / 32);
+    // start the DRAM reads of this warp's first rows of B (first 4 KB of each)
+    // before staging A, so the two latencies overlap
+#pragma unroll
+    for (int r = 0; r < kGemvRows; ++r)
+        if (gw * kGemvRows + r < N && lane * 128 < K)
+            asm volatile("prefetch.global.L2 [%0];" ::"l"(B + static_cast<int64_t>(gw * kGemvRows + r) * ldb + lane * 128));
+    for (int i = threadIdx.x; i < MR * (K / 4); i += kGemvThreads) {
+        const int m = i / (K / 4), k4 = i - m * (K / 4);
+        float v[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+        if (m < M) {
+            const uint32_t w = *reinterpret_cast<const uint32_t *>(A + m * lda + 4 * k4);
+            e4m3x2_decode(w & 0xffffu, v[0], v[1]);
+            e4m3x2_decode(w >> 16, v[2], v[3]);
+        }
+        sA4[m * (K / 4) + (k4 & 3) * kc + (k4 >> 2)] = make_float4(v[0], v[1], v[2], v[3]);
+    }
+    __syncthreads();
+
+    const OutQuant oq = make_out_quant<OUT>(ep);
+    for (int n0 = gw * kGemvRows; n0 < N; n0 += nw * kGemvRows) {
+        float acc[kGemvRows][MR];
+#pragma unroll
+        for (int r = 0; r < kGemvRows; ++r)
+#pragma unroll
+            for (int m = 0; m < MR; ++m) acc[r][m] = 0.0f;
+        for (int c0 = 0; c0 < kc; c0 += 32 * kGemvChunks) {
+            uint4 bv[kGemvRows][kGemvChunks];
+#pragma unroll
+            for (int r = 0; r < kGemvRows; ++r)
+#pragma unroll
+                for (int j = 0; j < kGemvChunks; ++j) {
+                    const int c = c0 + j * 32 + lane;
+                    bv[r][j] = (n0 + r < N && c < kc)
+                                   ? __ldcs(reinterpret_cast<const uint4 *>(B + static_cast<int64_t>(n0 + r) * ldb) + c)
+                                   : make_uint4(0u, 0u, 0u, 0u);
+                }
+#pragma unroll
+            for (int j = 0; j < kGemvChunks; ++j) {
+                const int c = c0 + j * 32 + lane;
+                if (c < kc) {
+#pragma unroll
+                    for (int q = 0; q < 4; ++q) {
+                        float4 a[MR];
+#pragma unroll
+                        for (int m = 0; m < MR; ++m) a[m] = sA4[m * (K / 4) + q * kc + c];
+#pragma unroll
+                        for (int r = 0; r < kGemvRows; ++r) {
+                            const uint32_t w = q == 0 ? bv[r][j].x : (q == 1 ? bv[r][j].y : (q == 2 ? bv[r][j].z : bv[r][j].w));
+                            float b0, b1, b2, b3;
+                            e4m3x2_decode(w & 0xffffu, b0, b1);
+                            e4m3x2_decode(w >> 16, b2, b3);
+#pragma unroll
+                            for (int m = 0; m < MR; ++m) {
+                                acc[r][m] = fmaf(a[m].x, b0, acc[r][m]);
+                                acc[r][m] = fmaf(a[m].y, b1, acc[r][m]);
+                                acc[r][m] = fmaf(a[m].z, b2, acc[r][m]);
+                                acc[r][m] = fmaf(a[m].w, b3, acc[r][m]);
+                            }
+                        }
+                    }
+                }
+            }
+        }
+#pragma unroll
+        for (int r = 0; r < kGemvRows; ++r)
+#pragma unroll
+            for (int m = 0; m < MR; ++m)
+#pragma unroll
+                for (int o = 16; o > 0; o >>= 1) acc[r][m] += __shfl_xor_sync(0xffffffffu, acc[r][m], o);
+        if (lane == 0) {
+#pragma unroll
+            for (int r = 0; r < kGemvRows; ++r) {
+                const int64_t col = n0 + r;
+                if (col >= N) continue;
+#pragma unroll
+                for (int m = 0; m < MR; ++m) {
+                    if (m >= M) continue;
+                    const float rs = ep.alpha * (ep.sa_row ? __ldg(ep.sa + m) : __ldg(ep.sa));
+                    float v = simt_pre(acc[r][m], rs, m, col, ep);
+                    if (ep.c_mat) v += ep.beta * load_cmat(ep, m, col);
+                    if (EPI == LCML_EPI_RELU) v = fmaxf(v, 0.0f);
+                    store_out<OUT>(ep.y, ep.ldy, m, col + ep.y_col_offset, v, oq);
+                    if (ep.row_amax) atomic_max_abs(ep.row_amax + m, fabsf(v));
+                }
+            }
+        }
+    }
+}
+
 template <int EPI, int OUT>
 __global__ void __launch_bounds__(256) k_gemm_fp8_simt(const uint8_t *__restrict__ A, int64_t lda,
                                                        const uint8_t *__restrict__ B, int64_t ldb, int b_kmajor,
@@ -1555,6 +1673,26 @@ int launch_splitk(const lcml_fp8_gemm_desc *d, const EpiParams &ep, cudaStream_t
     return LCML_OK;
 }
 
+// Rows of A held per GEMV instantiation for an M <= kGemvMaxM GEMM (0: not a GEMV shape).
+int gemv_rows(const lcml_fp8_gemm_desc *d, const EpiParams &ep) {
+    if (d->M < 1 || d->M > kGemvMaxM || d->epilogue == LCML_EPI_SILU_MUL || ep.y_num_peers > 0) return 0;
+    const int mr = d->M == 1 ? 1 : (d->M == 2 ? 2 : 4);
+    return static_cast<int64_t>(mr) * d->K * 4 <= kGemvSmemMax ? mr : 0;
+}
+
+template <int MR, int EPI, int OUT>
+int launch_gemv(const lcml_fp8_gemm_desc *d, const EpiParams &ep, cudaStream_t st) {
+    constexpr int rows_per_cta = (kGemvThreads / 32) * kGemvRows;
+    const int64_t want = (d->N + rows_per_cta - 1) / rows_per_cta;
+    const int64_t cap = 4LL * sm_count();
+    const int grid = static_cast<int>(want < cap ? want : cap);
+    const size_t smem = static_cast<size_t>(MR) * static_cast<size_t>(d->K) * 4;
+    k_gemv_fp8<MR, EPI, OUT><<<grid, kGemvThreads, smem, st>>>(d->A, d->lda, d->B, d->ldb, static_cast<int>(d->M),
+                                                             static_cast<int>(d->N), static_cast<int>(d->K), ep);
+    LCML_LAUNCHED("gemv_fp8");
+    return LCML_OK;
+}
+
 template <int EPI, int OUT>
 int launch_simt(const lcml_fp8_gemm_desc *d, const EpiParams &ep, cudaStream_t st) {
     const int64_t n_out = (EPI == LCML_EPI_SILU_MUL) ? d->N / 2 : d->N;
@@ -1587,6 +1725,14 @@ int dispatch(const lcml_fp8_gemm_desc *d, const EpiParams &ep, cudaStream_t st, 
     if (!tma_ok) return launch_simt<EPI, OUT>(d, ep, st);
     if constexpr (EPI != LCML_EPI_SILU_MUL) {
         const int mode = g_gemm_mode & 3;
+        if (mode == 0) {  // decode-sized M: stream B once on the CUDA cores
+            switch (gemv_rows(d, ep)) {
+                case 1: return launch_gemv<1, EPI, OUT>(d, ep, st);
+                case 2: return launch_gemv<2, EPI, OUT>(d, ep, st);
+                case 4: return launch_gemv<4, EPI, OUT>(d, ep, st);
+                default: break;
+            }
+        }
         const int splits = (mode == 0 || mode == 3) ? splitk_factor(d, ep, mode == 3) : 0;
         if (splits) return launch_splitk<EPI, OUT>(d, ep, st, splits);
     }

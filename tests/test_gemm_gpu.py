@@ -152,14 +152,17 @@ def test_gemm_e4m3_output(dev):
     assert (got == want).mean() > 0.99
 
 
-@pytest.mark.parametrize("M,N,K", [(1, 4096, 4096), (48, 640, 2048), (200, 1000, 2048)])
+@pytest.mark.parametrize("M,N,K", [(1, 4096, 4096), (3, 1000, 2048), (4, 520, 3072), (48, 640, 2048),
+                                   (200, 1000, 2048)])
 def test_splitk_epilogues(dev, gemm_mode, M, N, K):
     """Skinny GEMMs run split-K in a CTA cluster (partials reduced through
     distributed shared memory): per-row / per-column scales, bias, a residual
     (fp32 and e4m3), Relu, the row |max| and every output type against the
     oracle, and against the single-CTA kernel (forced by mode 1). M > 128
     (two row tiles, the last one partial) takes split-K only when mode 3
-    forces it; automatic selection gives it single-CTA tiles."""
+    forces it; automatic selection gives it single-CTA tiles. M <= 4 runs the
+    CUDA-core GEMV under automatic selection (mode 0) and split-K under
+    mode 3, so both are checked with the same epilogues."""
     import torch
     import luisaml_b200 as lb
     Aq, sa, Bq, sb = make_operands(M, N, K, seed=M + N + K, per_row=True, per_col=True, b_std=0.05)
