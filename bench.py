@@ -232,7 +232,7 @@ class GemmWorkload:
         if self.M <= 128:  # skinny: streaming B dominates (arithmetic intensity ~2M FLOP/B)
             bytes_ = self.M * self.K + self.N * self.K + 2 * self.M * self.N
             return {"kernel": "gemv_fp8" if self.M <= 4 else "gemm_fp8_splitk", "bound": "hbm", "unit": "GB/s", "work": bytes_,
-                    "profile": f"gemm_fp8_skinny_{self.M}"}
+                    "profile": f"gemv_fp8_skinny_{self.M}" if self.M <= 4 else f"gemm_fp8_skinny_{self.M}"}
         return {"kernel": "gemm_fp8_tc2" if self.M >= 2048 else "gemm_fp8_tc", "bound": "tensor", "unit": "TFLOP/s",
                 "work": self.flops, "profile": f"gemm_fp8_tc2_{self.M}"}
 
