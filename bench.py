@@ -3,13 +3,15 @@
     python bench.py [--gpus N] [--steps K] [--warmup W] [--config NAME] [--impl ours|reference]
 
 Default workload (N=1): the FP8 QDQ GEMM of the GEMM sweep at M=N=K=8192 —
-one step is QuantizeLinear of the fp32 activation A [M,K] with its
-per-tensor scale (amax/448) followed by the fused FP8 GEMM against the
-e4m3 weight B [N,K] (DequantizeLinear of both operands and the output cast
-folded into the epilogue), bf16 output. Throughput counts 2*M*N*K FLOP per
-step. Under torchrun each rank runs the same step on its own GPU (replicas of
-a single-GPU problem: no collective on the data path); time is the max over
-ranks.
+one step is QuantizeLinear of the fp32 activation A [M,K] with a dynamic
+per-tensor scale (amax(A)/448, computed on the device every step) followed by
+the fused FP8 GEMM against the e4m3 weight B [N,K] (DequantizeLinear of both
+operands and the output cast folded into the epilogue), bf16 output.
+Throughput counts 2*M*N*K FLOP per step. Under torchrun the same 8192^3
+problem is split by output columns across the ranks (strong scaling): each
+rank's GEMM stores its column shard into every rank's output over NVLink
+(the all-gather fused into the epilogue), and a barrier ends the step; time
+is the max over ranks.
 
 `--impl reference` times the reference algorithm on the host cores instead
 (the CPU restatement in oracle/, all threads, bounded sample per step): the
@@ -165,76 +167,159 @@ class ClockSampler:
 
 # ----------------------------------------------------------------------------- workloads
 class GemmWorkload:
-    """QDQ GEMM: Q(A) then fused FP8 GEMM, bf16 out (GEMM sweep configuration)."""
+    """QDQ GEMM of the GEMM sweep configuration: each step is the dynamic
+    per-tensor QuantizeLinear of the fp32 activation A (s = amax(A) / 448,
+    computed on the device every step) and the fused FP8 GEMM against the e4m3
+    weight B [N, K] (per-tensor scale), bf16 output.
+
+    Under torchrun (WORLD_SIZE > 1) the same problem is split by output
+    columns (strong scaling): every rank quantizes all of A, multiplies it by
+    its 256-column-block shard of B, and its GEMM epilogue stores each output
+    tile into its own full [M, N] output and, over NVLink, into every other
+    rank's (the all-gather fused into the epilogue); a barrier after the GEMM
+    ends the step. One GPU runs the same kernels with no peers."""
 
     def __init__(self, M, N, K, name):
         self.M, self.N, self.K, self.name = M, N, K, name
-        self.flops = 2.0 * M * N * K
-        # steps of up to 4096^3 are launch-bound: their two C-ABI calls are
-        # replayed as one CUDA graph; 8192^3 runs them directly, with the
-        # GEMM's events inside the timed step
-        self.graph_step = M * N * K <= 4096 ** 3
+        self.ws = int(os.environ.get("WORLD_SIZE", "1"))
+        self.rank = int(os.environ.get("RANK", "0"))
+        # steps of up to 4096^3 are launch-bound: on one GPU their C-ABI calls
+        # are replayed as one CUDA graph; 8192^3 and every multi-GPU step run
+        # them directly, with the GEMM's events inside the timed step
+        self.graph_step = M * N * K <= 4096 ** 3 and self.ws == 1
+        self.scaling = "strong" if self.ws > 1 else "weak"
+        self.same_input_all_ranks = True
+        self.parallelism = (f"N split over {self.ws} ranks; all-gather fused into the GEMM epilogue (P2P stores "
+                            "over NVLink)")
 
     def describe(self):
-        return {"workload": self.name, "M": self.M, "N": self.N, "K": self.K,
-                "a": "fp32 activation, QuantizeLinear per-tensor (s = amax/448) each step",
-                "b": "e4m3 weight initializer [N,K] (Gemm transB=1), per-tensor scale",
-                "out": "bf16", "l2": "flushed between timed steps (256 MiB write, untimed)",
-                "step": ("QuantizeLinear + GEMM C-ABI calls captured once as a CUDA graph and replayed each step; "
-                         "GEMM kernel time from a second loop with CUDA events around the GEMM") if self.graph_step
-                else "QuantizeLinear + GEMM C-ABI calls each step; CUDA events around the GEMM inside the step"}
+        d = {"workload": self.name, "M": self.M, "N": self.N, "K": self.K,
+             "a": "fp32 activation; QuantizeLinear with a dynamic per-tensor scale s = amax(A) / 448, amax "
+                  "computed on the device every step (two passes over A)",
+             "b": "e4m3 weight initializer [N,K] (Gemm transB=1), per-tensor scale", "out": "bf16",
+             "l2": "flushed between timed steps (256 MiB write, untimed)",
+             "step": ("amax + quantize + GEMM C-ABI calls captured once as a CUDA graph and replayed each step; "
+                      "GEMM kernel time from a second loop with CUDA events around the GEMM") if self.graph_step
+             else "amax + quantize + GEMM C-ABI calls each step; CUDA events around the GEMM inside the step"}
+        if self.ws > 1:
+            d["shard_columns_per_rank"] = self.Nr
+            d["step"] += "; then a barrier (all-reduce of one float) after which every rank holds all of Y"
+        return d
 
     def setup(self, dev, seed):
         import torch
         import luisaml_b200 as lb
-        g = torch.Generator(device=dev).manual_seed(seed)
+        from luisaml_b200 import tp
+        g = torch.Generator(device=dev).manual_seed(seed)  # the same A on every rank
         self.A = torch.randn(self.M, self.K, device=dev, generator=g)
-        B = torch.randn(self.N, self.K, device=dev, generator=g)
-        self.sa = lb.amax(self.A)
-        self.sa = torch.where(self.sa > 0, self.sa / 448.0, torch.ones_like(self.sa))
-        sb = lb.amax(B)
-        self.sb = torch.where(sb > 0, sb / 448.0, torch.ones_like(sb))
-        self.Bq = lb.quantize(B, self.sb)
-        del B
+        start, stop = tp.shard_columns(self.N, self.ws, self.rank)
+        self.start, self.Nr = start, stop - start
+        Bt = tp.column_block_weights(torch, self.K, start, stop, dev, seed + 100, 1.0)
+        bmax = lb.amax(Bt) if Bt.numel() else torch.zeros(1, device=dev)
+        if self.ws > 1:  # the per-tensor scale of the whole B, not of this shard
+            import torch.distributed as dist
+            dist.all_reduce(bmax, op=dist.ReduceOp.MAX)
+        self.sb = torch.where(bmax > 0, bmax / 448.0, torch.ones_like(bmax))
+        self.Bq = lb.quantize(Bt, self.sb)
+        del Bt
+        self.flops = 2.0 * self.M * self.N * self.K / self.ws  # per rank
         self.Aq = torch.empty(self.M, self.K, dtype=torch.uint8, device=dev)
-        self.Y = torch.empty(self.M, self.N, dtype=torch.bfloat16, device=dev)
-        self.desc, _ = lb.gemm(self.Aq, self.Bq, self.sa, self.sb, out=self.Y, desc_only=True)
+        self.sa = torch.empty(1, dtype=torch.float32, device=dev)
+        self.amax_ws = torch.empty(1, dtype=torch.float32, device=dev)
+        self.peers = None
+        if self.ws > 1:
+            import torch.distributed as dist
+            self.dist = dist
+            self.peers = tp.PeerOutputs(torch, dist, self.M * self.N * 2, dev)
+            self.barrier_t = torch.zeros(1, device=dev)
+            d = lb.GemmDesc()
+            d.M, d.N, d.K = self.M, self.Nr, self.K
+            d.A, d.lda, d.B, d.ldb, d.b_kmajor = self.Aq.data_ptr(), self.K, self.Bq.data_ptr(), self.K, 1
+            d.scale_a, d.scale_a_mode = self.sa.data_ptr(), lb.SCALE_TENSOR
+            d.scale_b, d.scale_b_mode = self.sb.data_ptr(), lb.SCALE_TENSOR
+            d.alpha, d.beta = 1.0, 1.0
+            d.Y, d.y_dtype, d.ldy, d.y_col_offset = self.peers.local, lb.DTYPE_BFLOAT16, self.N, start
+            d.y_peers, d.y_num_peers = self.peers.peer_array.data_ptr(), self.ws - 1
+            self.desc = d
+        else:
+            self.Y = torch.empty(self.M, self.N, dtype=torch.bfloat16, device=dev)
+            self.desc, _ = lb.gemm(self.Aq, self.Bq, self.sa, self.sb, out=self.Y, desc_only=True)
         self.lib = lb.lib()
-        self.kernels_per_step = 2
+        self.kernels_per_step = 3
 
     def step(self, stream, ev=None):
         import ctypes
         import luisaml_b200 as lb
         s = ctypes.c_void_p(stream.cuda_stream)
-        lb.check(self.lib.lcml_fp8_quantize(ctypes.c_void_p(self.A.data_ptr()), 1, 1, self.A.numel(),
-                                            ctypes.c_void_p(self.sa.data_ptr()), 0,
-                                            ctypes.c_void_p(self.Aq.data_ptr()), s))
+        lb.check(self.lib.lcml_fp8_quantize_tensor_dynamic(
+            ctypes.c_void_p(self.A.data_ptr()), self.A.numel(), ctypes.c_void_p(self.sa.data_ptr()),
+            ctypes.c_void_p(self.Aq.data_ptr()), ctypes.c_void_p(self.amax_ws.data_ptr()), s))
         if ev is not None:
             ev[0].record(stream)
         lb.check(self.lib.lcml_fp8_gemm(ctypes.byref(self.desc), s))
         if ev is not None:
             ev[1].record(stream)
+        if self.ws > 1:
+            self.dist.all_reduce(self.barrier_t)  # every shard has landed in every rank's output
 
-    # end to end: pinned host A in, bf16 Y out to pinned host, through the C ABI
+    # end to end: pinned host A in, this rank's rows of the bf16 Y out to pinned host, through the C ABI
     def setup_e2e(self):
         import torch
         self.A_host = self.A.cpu().pin_memory()
-        self.Y_host = torch.empty(self.Y.shape, dtype=self.Y.dtype).pin_memory()
+        rows = self.M // self.ws
+        self.r0 = self.rank * rows
+        self.Y_host = torch.empty((rows, self.N), dtype=torch.bfloat16).pin_memory()
         self.h2d = self.A_host.numel() * 4
         self.d2h = self.Y_host.numel() * 2
 
     def step_e2e(self, stream):
+        import ctypes
         self.A.copy_(self.A_host, non_blocking=True)
         self.step(stream)
-        self.Y_host.copy_(self.Y, non_blocking=True)
+        ybase = self.peers.local if self.peers is not None else self.Y.data_ptr()
+        self.lib.lcml_memcpy_async(ctypes.c_void_p(self.Y_host.data_ptr()),
+                                   ctypes.c_void_p(ybase + self.r0 * self.N * 2), self.Y_host.numel() * 2, 2,
+                                   ctypes.c_void_p(stream.cuda_stream))
+
+    def close(self):
+        if self.peers is not None:
+            self.peers.close()
 
     def dominant(self):
         if self.M <= 128:  # skinny: streaming B dominates (arithmetic intensity ~2M FLOP/B)
             bytes_ = self.M * self.K + self.N * self.K + 2 * self.M * self.N
-            return {"kernel": "gemv_fp8" if self.M <= 4 else "gemm_fp8_splitk", "bound": "hbm", "unit": "GB/s", "work": bytes_,
+            return {"kernel": "gemv_fp8" if self.M <= 4 else "gemm_fp8_splitk", "bound": "hbm", "unit": "GB/s",
+                    "work": bytes_,
                     "profile": f"gemv_fp8_skinny_{self.M}" if self.M <= 4 else f"gemm_fp8_skinny_{self.M}"}
-        return {"kernel": "gemm_fp8_tc2" if self.M >= 2048 else "gemm_fp8_tc", "bound": "tensor", "unit": "TFLOP/s",
-                "work": self.flops, "profile": f"gemm_fp8_tc2_{self.M}"}
+        kern = "gemm_fp8_tc2" if self.M >= 2048 else "gemm_fp8_tc"
+        if self.ws > 1:
+            kern += " (+ fused all-gather)"
+        return {"kernel": kern, "bound": "tensor", "unit": "TFLOP/s", "work": self.flops,
+                "profile": f"gemm_fp8_tc2_{self.M}"}
+
+    def fp8_anchor(self, dev, steps, flush):
+        """The same e4m3 GEMM through the library path torch offers
+        (torch._scaled_mm, per-tensor scales, bf16 out), CUDA events per call
+        after the same L2 flush: a same-box measure of the dense-FP8 rate."""
+        import torch
+        try:
+            a = self.Aq.view(torch.float8_e4m3fn)
+            b = self.Bq.view(torch.float8_e4m3fn).t()
+            out = torch._scaled_mm(a, b, scale_a=self.sa, scale_b=self.sb, out_dtype=torch.bfloat16)
+        except Exception as e:  # not every torch build has an sm_100 FP8 kernel
+            return {"unavailable": f"torch._scaled_mm failed: {type(e).__name__}: {e}"[:200]}
+        torch.cuda.synchronize()
+        ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
+        for i in range(steps):
+            flush.fill_(float(i))
+            ev[i][0].record()
+            torch._scaled_mm(a, b, scale_a=self.sa, scale_b=self.sb, out_dtype=torch.bfloat16, out=out)
+            ev[i][1].record()
+        torch.cuda.synchronize()
+        ms = sum(x.elapsed_time(y) for x, y in ev) / steps
+        return {"tflops": 2.0 * self.M * self.N * self.K / (ms / 1e3) / 1e12, "ms": ms,
+                "what": "torch._scaled_mm e4m3 x e4m3 -> bf16, per-tensor scales, same operands, CUDA events, "
+                        "L2 flushed between calls"}
 
     # CPU reference: oracle quantize + oracle QDQ GEMM on a bounded row sample
     def cpu_sample(self, budget_s=12.0):
@@ -261,7 +346,7 @@ class GemmWorkload:
         return {"value": 2.0 * rows * N * K / t / 1e12, "unit": "TFLOP/s", "cores": oracle.num_threads(),
                 "kind": "port",
                 "sample": f"{rows} of {self.M} rows of the {self.M}x{self.N}x{self.K} QDQ GEMM "
-                          f"(quantize + DQ + K-ordered fp32 fma), {t:.1f} s"}
+                          f"(amax + quantize + DQ + K-ordered fp32 fma), {t:.1f} s"}
 
 
 class GraphWorkload:
@@ -652,7 +737,7 @@ def run_ours(args, wl):
     dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
     lb.check(lb.lib().lcml_device_check())
-    wl.setup(dev, seed=1234 + rank)
+    wl.setup(dev, seed=1234 + (0 if getattr(wl, "same_input_all_ranks", False) else rank))
     stream = torch.cuda.current_stream(dev)
     flush = torch.empty(2 * L2_BYTES // 4, dtype=torch.float32, device=dev)
 
@@ -738,6 +823,13 @@ def run_ours(args, wl):
                 "frac": achieved / peak, "traffic": traffic, "kernel": dom["kernel"],
                 "peak_source": peak_source, "kernel_ms": kern_avg_s * 1e3,
                 "timed": "the dominant kernel alone" if dom.get("kernel_only", True) else "the whole step"}
+
+    if ws == 1 and dom["bound"] == "tensor" and hasattr(wl, "fp8_anchor"):
+        anchor = wl.fp8_anchor(dev, min(n, 20), flush)
+        roofline["fp8_anchor"] = anchor
+        if "tflops" in anchor:
+            roofline["frac_vs_fp8_anchor"] = achieved / anchor["tflops"]
+        roofline["frac_vs_nominal_fp8_dense"] = achieved / 4500.0
 
     e2e = None
     if not args.no_e2e:

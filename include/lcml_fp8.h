@@ -43,7 +43,9 @@ typedef enum lcml_dtype {
     LCML_DTYPE_FLOAT = 1,
     LCML_DTYPE_FLOAT16 = 10,
     LCML_DTYPE_BFLOAT16 = 16,
-    LCML_DTYPE_FLOAT8E4M3FN = 17
+    LCML_DTYPE_FLOAT8E4M3FN = 17,
+    LCML_DTYPE_FLOAT8E5M2 = 19,
+    LCML_DTYPE_FLOAT4E2M1 = 23  /* two codes per byte, element 2i in the low nibble of byte i */
 } lcml_dtype;
 
 /* Scale layouts. TENSOR: one fp32 scale. AXIS: one per index of the quantized
@@ -196,6 +198,11 @@ typedef struct lcml_fp8_gemm_desc {
     void *const *y_peers; /* device array of y_num_peers device pointers */
     int y_num_peers;
     const float *c_mat_scale; /* device [1]: DequantizeLinear scale of an e4m3 c_mat (a quantized residual) */
+    /* Kernel choice, per call (0 = automatic; results agree up to the fp32
+     * summation order). Bits 0-1: 1 single-CTA tiles, 2 CTA-pair tiles, 3
+     * split-K wherever the tile count allows it (also M > 128); bit 2: plain
+     * global stores instead of TMA stores. For cross-checking and tuning. */
+    int variant;
 } lcml_fp8_gemm_desc;
 
 int lcml_fp8_gemm(const lcml_fp8_gemm_desc *desc, lcml_stream_t stream);
@@ -229,6 +236,9 @@ int lcml_fp8_gemm_rowquant(const lcml_fp8_gemm_desc *desc, uint8_t *q, float *q_
  * before any work is enqueued. It calls no cudaMalloc / cudaFree.
  * The first call on each device looks up the array's device address
  * (cudaGetSymbolAddress); make that first call before any stream capture.
+ * The address is kept for the life of the process, like the library's other
+ * per-device state (its device error word): do not cudaDeviceReset a device
+ * while this library is in use on it.
  * All calls share the array and each call zeroes the rows it uses, so calls
  * that overlap on the GPU (e.g. on two streams) race and must be serialised.
  */
@@ -295,6 +305,10 @@ typedef struct lcml_fp8_conv_desc {
     int y_dtype;            /* FLOAT, BFLOAT16 or FLOAT8E4M3FN */
     const float *y_scale;   /* per-tensor output scale when y_dtype is e4m3 */
     void *workspace;        /* lcml_fp8_conv_workspace_size() bytes, 256-byte aligned */
+    /* Lowering choice, per call (0 = automatic). Bit 0: gather the patches
+     * (im2col into the workspace) even where the implicit GEMM applies;
+     * bits 8-10: the GEMM's lcml_fp8_gemm_desc.variant. */
+    int variant;
 } lcml_fp8_conv_desc;
 
 /* Packed K: kH * kW * Cp (Cp: C padded as above) rounded up to a multiple of 16. */
@@ -330,7 +344,13 @@ int lcml_maxpool2d(const void *x, int elem_dtype, int64_t NC, int64_t H, int64_t
  * x may be e4m3 with a per-tensor scale (x_scale) or fp32/bf16. */
 int lcml_global_avgpool(const void *x, int elem_dtype, const float *x_scale, int64_t N, int64_t C, int64_t HW,
                         int x_nhwc, float *y, lcml_stream_t stream);
-/* Elementwise dtype conversion (Cast, cast.cpp:10-162): fp32 <-> bf16. */
+/* Cast (src/onnx/operators/cast.cpp:10-162) of n elements between FLOAT,
+ * FLOAT16, BFLOAT16, FLOAT8E4M3FN, FLOAT8E5M2 and FLOAT4E2M1 (packed). As the
+ * reference: to FP8 / FP4 the value is rounded to half first and then
+ * encoded (cast.cpp:63-67, from_float(half(x)) with the fp_quantized.h
+ * encoders: e4m3 and e2m1 saturate, e5m2 overflows to inf); from FP8 / FP4 it
+ * is decoded exactly (cast.cpp:44-48); fp32 / fp16 / bf16 convert with one
+ * round-to-nearest-even. Source and destination types must differ. */
 int lcml_cast(const void *x, int x_dtype, void *y, int y_dtype, int64_t n, lcml_stream_t stream);
 
 #ifdef __cplusplus

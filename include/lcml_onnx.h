@@ -50,7 +50,10 @@ enum class AttributeType : int {
 
 const char *dtype_name(DataType t);
 DataType dtype_from_name(std::string_view name);  // "FLOAT", "FLOAT8E4M3FN", ...
-size_t dtype_size(DataType t);                     // bytes per element (0: unsupported here)
+size_t dtype_size(DataType t);                     // bytes per element (0: unsupported here; 0 for packed FP4)
+// Bytes of n elements: n * dtype_size, or (n + 1) / 2 for FLOAT4E2M1 (two codes
+// per byte, element 2i in the low nibble of byte i, as the reference's FP4Data).
+size_t dtype_nbytes(DataType t, size_t n);
 
 class Graph;
 class OperatorSet;
@@ -260,7 +263,7 @@ public:
     size_type ndim() const { return static_cast<size_type>(shape_.size()); }
     size_type size() const;
     DataType dtype() const { return dtype_; }
-    size_t nbytes() const { return static_cast<size_t>(size()) * dtype_size(dtype_); }
+    size_t nbytes() const { return dtype_nbytes(dtype_, static_cast<size_t>(size())); }
     void reshape(shape_type s);
     virtual void *data() = 0;
     virtual const void *data() const = 0;

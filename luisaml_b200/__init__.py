@@ -148,10 +148,11 @@ def transpose_u8(src):
 
 def gemm(A, B, sa, sb, *, b_kmajor=True, alpha=1.0, beta=1.0, c_vec=None, c_vec_mode=None, c_mat=None,
          c_mat_scale=None, epilogue=EPI_NONE, out_dtype=None, y_scale=None, row_amax=None, out=None, simt=False,
-         desc_only=False):
+         desc_only=False, variant=0):
     """Fused FP8 GEMM through lcml_fp8_gemm. A [M,K] e4m3 (uint8); B [N,K] (b_kmajor) or [K,N].
 
     sa: fp32 [1] or [M]; sb: fp32 [1] or [N]. Returns Y [M, N] (N/2 for SILU_MUL).
+    variant: lcml_fp8_gemm_desc.variant (0 automatic kernel choice).
     """
     torch = _torch()
     out_dtype = out_dtype or torch.bfloat16
@@ -176,6 +177,7 @@ def gemm(A, B, sa, sb, *, b_kmajor=True, alpha=1.0, beta=1.0, c_vec=None, c_vec_
         if c_mat_scale is not None:  # an e4m3 (uint8) residual is decoded times this per-tensor scale
             d.c_mat_scale = c_mat_scale.data_ptr()
     d.epilogue = epilogue
+    d.variant = variant
     d.Y, d.y_dtype, d.ldy = Y.data_ptr(), _dtype_code(Y.dtype), Y.stride(0)
     if y_scale is not None:
         d.y_scale = y_scale.data_ptr()

@@ -18,6 +18,8 @@ DTYPE_FLOAT = 1
 DTYPE_FLOAT16 = 10
 DTYPE_BFLOAT16 = 16
 DTYPE_E4M3 = 17
+DTYPE_E5M2 = 19
+DTYPE_E2M1 = 23  # packed: two codes per byte, element 2i in the low nibble
 
 SCALE_TENSOR = 0
 SCALE_AXIS = 1
@@ -55,6 +57,7 @@ class GemmDesc(ctypes.Structure):
         ("y_peers", ctypes.c_void_p),
         ("y_num_peers", ctypes.c_int),
         ("c_mat_scale", ctypes.c_void_p),
+        ("variant", ctypes.c_int),
     ]
 
 
@@ -71,6 +74,7 @@ class ConvDesc(ctypes.Structure):
         ("residual_scale", ctypes.c_void_p), ("epilogue", ctypes.c_int),
         ("Y", ctypes.c_void_p), ("y_dtype", ctypes.c_int), ("y_scale", ctypes.c_void_p),
         ("workspace", ctypes.c_void_p),
+        ("variant", ctypes.c_int),
     ]
 
 
@@ -149,10 +153,6 @@ def load():
     lib.lcml_last_error.argtypes = []
     lib.lcml_launch_count.restype = ctypes.c_uint64
     lib.lcml_launch_count.argtypes = []
-    lib.lcml_fp8_gemm_set_mode.restype = None
-    lib.lcml_fp8_gemm_set_mode.argtypes = [ctypes.c_int]
-    lib.lcml_fp8_conv_set_mode.restype = None
-    lib.lcml_fp8_conv_set_mode.argtypes = [ctypes.c_int]
     for name, args in PROTOTYPES.items():
         fn = getattr(lib, name)
         fn.argtypes = args

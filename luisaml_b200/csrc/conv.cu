@@ -6,7 +6,6 @@
 // no gather at all (X is already the GEMM's A). The epilogue fuses the
 // per-tensor x scale, per-channel w scale, bias, residual, Relu and the
 // requantization of the output.
-#include <mutex>
 #include <type_traits>
 
 #include "lcml_device.cuh"
@@ -23,8 +22,6 @@ constexpr int kThreads = 256;
 int64_t packed_c(int64_t c) { return c % 16 == 0 ? c : (c <= 4 ? 4 : (c <= 8 ? 8 : ((c + 15) / 16) * 16)); }
 
 int64_t packed_k(int64_t cg, int64_t kh, int64_t kw) { return ((packed_c(cg) * kh * kw + 15) / 16) * 16; }
-
-int g_conv_mode = 0;  // lcml_fp8_conv_set_mode
 
 bool direct_path(const lcml_fp8_conv_desc *d) {
     return d->kH == 1 && d->kW == 1 && d->sH == 1 && d->sW == 1 && d->pH == 0 && d->pW == 0 && d->x_nhwc &&
@@ -224,7 +221,7 @@ int64_t lcml_fp8_conv_packed_k(int64_t Cg, int64_t kH, int64_t kW) { return pack
 
 int64_t lcml_fp8_conv_workspace_size(const lcml_fp8_conv_desc *d) {
     if (!d) return -1;
-    if (direct_path(d) || (implicit_ok(d) && g_conv_mode != 1)) return 0;
+    if (direct_path(d) || (implicit_ok(d) && !(d->variant & 1))) return 0;
     return d->N * d->oH * d->oW * packed_k(d->C / (d->group > 0 ? d->group : 1), d->kH, d->kW) + repack_bytes(d);
 }
 
@@ -242,7 +239,7 @@ int lcml_fp8_conv_pack_weight(const uint8_t *W, int64_t M, int64_t Cg, int64_t k
 
 namespace {
 template <typename I>
-void launch_im2col(const lcml_fp8_conv_desc *d, const uint8_t *X, int64_t Cp, int64_t Kp, uint8_t *A, cudaStream_t st) {
+int launch_im2col(const lcml_fp8_conv_desc *d, const uint8_t *X, int64_t Cp, int64_t Kp, uint8_t *A, cudaStream_t st) {
     const int64_t P = d->N * d->oH * d->oW;
     const int grid = grid_for(P * (Kp / 16));
     const int64_t row_smem = static_cast<int64_t>(kRowThreads) * Kp;
@@ -254,16 +251,12 @@ void launch_im2col(const lcml_fp8_conv_desc *d, const uint8_t *X, int64_t Cp, in
         auto k4 = k_im2col_rows<4>;
         auto k8 = k_im2col_rows<8>;
         auto kern = Cp == 4 ? k4 : k8;
-        static std::once_flag once;
-        std::call_once(once, [&] {
-            cudaFuncSetAttribute(k4, cudaFuncAttributeMaxDynamicSharedMemorySize, 96 * 1024);
-            cudaFuncSetAttribute(k8, cudaFuncAttributeMaxDynamicSharedMemorySize, 96 * 1024);
-        });
+        if (const int rc = ensure_max_smem(reinterpret_cast<const void *>(kern), 96 * 1024, "im2col_rows")) return rc;
         kern<<<static_cast<int>(blocks), kRowThreads, static_cast<size_t>(row_smem), st>>>(
             X, static_cast<int>(d->H), static_cast<int>(d->W), static_cast<int>(d->kH), static_cast<int>(d->kW),
             static_cast<int>(d->oH), static_cast<int>(d->oW), d->sH, d->sW, d->pH, d->pW, d->dH, d->dW,
             static_cast<int>(Kp), P, A);
-        return;
+        return LCML_OK;
     }
     if (Cp == 4)
         k_im2col_narrow<I, 4><<<grid, kThreads, 0, st>>>(X, d->N, d->H, d->W, d->kH, d->kW, d->oH, d->oW, d->sH, d->sW,
@@ -274,6 +267,7 @@ void launch_im2col(const lcml_fp8_conv_desc *d, const uint8_t *X, int64_t Cp, in
     else
         k_im2col_nhwc16<I><<<grid, kThreads, 0, st>>>(X, d->N, Cp, d->H, d->W, d->kH, d->kW, d->oH, d->oW, d->sH, d->sW,
                                                       d->pH, d->pW, d->dH, d->dW, Kp, A);
+    return LCML_OK;
 }
 
 template <typename I>
@@ -298,6 +292,7 @@ int lcml_fp8_conv(const lcml_fp8_conv_desc *d, lcml_stream_t stream) {
                        (d->oW - 1) * d->sW + (d->kW - 1) * d->dW - d->pW < d->W + d->pW + d->kW,
                    "lcml_fp8_conv: output extent inconsistent with the input");
     LCML_CHECK_ARG(d->X && d->Wp && d->Y && d->scale_x && d->scale_w, "lcml_fp8_conv: null operand");
+    LCML_CHECK_ARG((d->variant & ~0x701) == 0, "lcml_fp8_conv: variant 0x%x unknown", d->variant);
     LCML_CHECK_ARG(d->epilogue == LCML_EPI_NONE || d->epilogue == LCML_EPI_RELU, "lcml_fp8_conv: epilogue %d", d->epilogue);
     LCML_CHECK_ARG(!d->residual || d->residual_dtype == LCML_DTYPE_FLOAT ||
                        (d->residual_dtype == LCML_DTYPE_FLOAT8E4M3FN && d->residual_scale),
@@ -309,8 +304,8 @@ int lcml_fp8_conv(const lcml_fp8_conv_desc *d, lcml_stream_t stream) {
     const uint8_t *A = d->X;
     int64_t K = d->C;
     // Implicit GEMM where the geometry allows it (no im2col pass, no
-    // workspace); the materialized lowering otherwise, or when a test asks.
-    const bool implicit = implicit_ok(d) && aligned(d->X, 16) && g_conv_mode != 1;
+    // workspace); the materialized lowering otherwise, or when the caller asks.
+    const bool implicit = implicit_ok(d) && aligned(d->X, 16) && !(d->variant & 1);
     if (implicit) {
         A = nullptr;
         K = Kp;
@@ -330,8 +325,8 @@ int lcml_fp8_conv(const lcml_fp8_conv_desc *d, lcml_stream_t stream) {
             LCML_LAUNCHED("conv_repack");
             src = xc;
         }
-        if (small) launch_im2col<int32_t>(d, src, Cp, Kp, ws, st);
-        else launch_im2col<int64_t>(d, src, Cp, Kp, ws, st);
+        const int rc = small ? launch_im2col<int32_t>(d, src, Cp, Kp, ws, st) : launch_im2col<int64_t>(d, src, Cp, Kp, ws, st);
+        if (rc != LCML_OK) return rc;
         LCML_LAUNCHED("conv_im2col");
         A = ws;
         K = Kp;
@@ -366,6 +361,7 @@ int lcml_fp8_conv(const lcml_fp8_conv_desc *d, lcml_stream_t stream) {
     g.y_dtype = d->y_dtype;
     g.ldy = d->M;
     g.y_scale = d->y_scale;
+    g.variant = (d->variant >> 8) & 7;
     if (implicit) {
         ConvGeom geo;
         geo.x = d->X;
@@ -388,9 +384,5 @@ int lcml_fp8_conv(const lcml_fp8_conv_desc *d, lcml_stream_t stream) {
     }
     return lcml_fp8_gemm(&g, stream);
 }
-
-// Test hook (not in the public header): 0 automatic (implicit GEMM wherever
-// the geometry allows it), 1 always materialize the patches.
-void lcml_fp8_conv_set_mode(int mode) { g_conv_mode = mode; }
 
 }// extern "C"

@@ -1,6 +1,6 @@
 // Memory-bound operators around the FP8 GEMMs: Relu / Sigmoid / Abs,
 // Add / Sub / Mul / Div with trailing broadcast, ReduceMax over the last axis,
-// Softmax over the last axis, MaxPool, GlobalAveragePool and Cast.
+// Softmax over the last axis, MaxPool and GlobalAveragePool (Cast: cast.cu).
 // Coalesced 16-byte accesses where the layout allows, grid-stride loops,
 // grids sized from the SM count. Each kernel's HBM bound is its bytes moved:
 // unary/cast 8 B/elem (fp32 in + out), binary 12 B/elem, reduce/softmax
@@ -279,20 +279,6 @@ __global__ void __launch_bounds__(kThreads) k_gap_nhwc(const void *__restrict__ 
     y[tid] = (s * scale) / static_cast<float>(HW);
 }
 
-__global__ void __launch_bounds__(kThreads) k_cast_f32_bf16(const float *__restrict__ x, __nv_bfloat16 *__restrict__ y,
-                                                            int64_t n) {
-    const int64_t tid = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
-    const int64_t nt = static_cast<int64_t>(gridDim.x) * blockDim.x;
-    for (int64_t i = tid; i < n; i += nt) y[i] = __float2bfloat16_rn(x[i]);
-}
-
-__global__ void __launch_bounds__(kThreads) k_cast_bf16_f32(const __nv_bfloat16 *__restrict__ x, float *__restrict__ y,
-                                                            int64_t n) {
-    const int64_t tid = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
-    const int64_t nt = static_cast<int64_t>(gridDim.x) * blockDim.x;
-    for (int64_t i = tid; i < n; i += nt) y[i] = __bfloat162float(x[i]);
-}
-
 }// namespace
 }// namespace lcml
 
@@ -410,23 +396,6 @@ int lcml_global_avgpool(const void *x, int elem_dtype, const float *x_scale, int
         else k_gap_nhwc<LCML_DTYPE_FLOAT8E4M3FN><<<g, kThreads, 0, st>>>(x, x_scale, N, C, HW, y);
     }
     LCML_LAUNCHED("global_avgpool");
-    return LCML_OK;
-}
-
-int lcml_cast(const void *x, int x_dtype, void *y, int y_dtype, int64_t n, lcml_stream_t stream) {
-    LCML_CHECK_ARG(n >= 0, "lcml_cast: negative n");
-    if (n == 0) return LCML_OK;
-    LCML_CHECK_ARG(x && y, "lcml_cast: null pointer");
-    cudaStream_t st = to_cuda(stream);
-    if (x_dtype == LCML_DTYPE_FLOAT && y_dtype == LCML_DTYPE_BFLOAT16) {
-        k_cast_f32_bf16<<<grid_for(n), kThreads, 0, st>>>(static_cast<const float *>(x), static_cast<__nv_bfloat16 *>(y), n);
-    } else if (x_dtype == LCML_DTYPE_BFLOAT16 && y_dtype == LCML_DTYPE_FLOAT) {
-        k_cast_bf16_f32<<<grid_for(n), kThreads, 0, st>>>(static_cast<const __nv_bfloat16 *>(x), static_cast<float *>(y), n);
-    } else {
-        return set_error(LCML_ERR_UNSUPPORTED, "lcml_cast: %d -> %d unsupported (e4m3 goes through QuantizeLinear)",
-                         x_dtype, y_dtype);
-    }
-    LCML_LAUNCHED("cast");
     return LCML_OK;
 }
 

@@ -204,10 +204,8 @@ int gemm_f32(const float *A, const float *B, const float *C, int64_t M, int64_t 
         const int64_t smem = (kSmTM + kSmTN) * kst * 4;
         if (K > 0 && smem <= kWholeKSmem) {
             auto kern = k_gemm_f32_small_wk<RELU>;
-            static std::once_flag once;
-            static cudaError_t attr = cudaSuccess;
-            std::call_once(once, [&] { attr = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kWholeKSmem); });
-            if (attr != cudaSuccess) return lcml::set_error(LCML_ERR_CUDA, "cudaFuncSetAttribute failed: %s", cudaGetErrorString(attr));
+            if (const int rc = lcml::ensure_max_smem(reinterpret_cast<const void *>(kern), kWholeKSmem, "gemm_f32_small"))
+                return rc;
             kern<<<grid, 256, static_cast<size_t>(smem), lcml::to_cuda(stream)>>>(
                 A, B, C, M, N, K, static_cast<int>(kst), transA, transB, alpha, beta, c_ndim, c_d0, c_d1, Y);
             LCML_LAUNCHED("gemm_f32_small");

@@ -1309,7 +1309,8 @@ __global__ void __launch_bounds__(kGemvThreads) k_gemv_fp8(const uint8_t *__rest
     __syncthreads();
 
     const OutQuant oq = make_out_quant<OUT>(ep);
-    for (int n0 = gw * kGemvRows; n0 < N; n0 += nw * kGemvRows) {
+    // 64-bit row index: N may come within one grid stride of INT_MAX
+    for (int64_t n0 = static_cast<int64_t>(gw) * kGemvRows; n0 < N; n0 += static_cast<int64_t>(nw) * kGemvRows) {
         float acc[kGemvRows][MR];
 #pragma unroll
         for (int r = 0; r < kGemvRows; ++r)
@@ -1322,9 +1323,8 @@ __global__ void __launch_bounds__(kGemvThreads) k_gemv_fp8(const uint8_t *__rest
 #pragma unroll
                 for (int j = 0; j < kGemvChunks; ++j) {
                     const int c = c0 + j * 32 + lane;
-                    bv[r][j] = (n0 + r < N && c < kc)
-                                   ? __ldcs(reinterpret_cast<const uint4 *>(B + static_cast<int64_t>(n0 + r) * ldb) + c)
-                                   : make_uint4(0u, 0u, 0u, 0u);
+                    bv[r][j] = (n0 + r < N && c < kc) ? __ldcs(reinterpret_cast<const uint4 *>(B + (n0 + r) * ldb) + c)
+                                                      : make_uint4(0u, 0u, 0u, 0u);
                 }
 #pragma unroll
             for (int j = 0; j < kGemvChunks; ++j) {
@@ -1450,11 +1450,6 @@ __global__ void __launch_bounds__(256) k_gemm_fp8_simt(const uint8_t *__restrict
 // ---------------------------------------------------------------------------
 // Host side
 // ---------------------------------------------------------------------------
-// Kernel selection override for tests: bits 0-1: 0 automatic, 1 single-CTA,
-// 2 CTA pair, 3 split-K wherever its tile count allows (also M > 128);
-// bit 2: store the output with plain stores instead of TMA.
-int g_gemm_mode = 0;
-
 PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
     static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
     static std::once_flag once;
@@ -1559,14 +1554,7 @@ int launch_tc(const lcml_fp8_gemm_desc *d, const EpiParams &ep, cudaStream_t st,
     using L = Layout<BN, STAGES, EPI, OUT, BKB>;
     static_assert(STAGES >= 3 && L::kSmemBytes <= kSmemLimit, "shared memory layout does not fit");
     auto kern = k_gemm_fp8_tc<BN, STAGES, EPI, OUT, IM2COL, BKB>;
-    static std::once_flag once;
-    static cudaError_t attr_err = cudaSuccess;
-    std::call_once(once, [&] {
-        attr_err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kSmemBytes);
-    });
-    if (attr_err != cudaSuccess)
-        return set_error(LCML_ERR_CUDA, "cudaFuncSetAttribute(smem=%d) failed: %s", L::kSmemBytes,
-                         cudaGetErrorString(attr_err));
+    if (const int rc = ensure_max_smem(reinterpret_cast<const void *>(kern), L::kSmemBytes, "gemm_fp8_tc")) return rc;
     CUtensorMap ta, tb;
     int rc = IM2COL ? make_tmap_im2col(&ta, geo, BKB) : make_tmap(&ta, d->A, d->K, d->M, d->lda, BM, BKB);
     if (rc) return rc;
@@ -1589,14 +1577,7 @@ int launch_tc2(const lcml_fp8_gemm_desc *d, const EpiParams &ep, cudaStream_t st
     using L = PairLayout<STAGES, EPI, OUT>;
     static_assert(STAGES >= 3 && L::kSmemBytes <= kSmemLimit, "shared memory layout does not fit");
     auto kern = k_gemm_fp8_tc2<STAGES, EPI, OUT>;
-    static std::once_flag once;
-    static cudaError_t attr_err = cudaSuccess;
-    std::call_once(once, [&] {
-        attr_err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kSmemBytes);
-    });
-    if (attr_err != cudaSuccess)
-        return set_error(LCML_ERR_CUDA, "cudaFuncSetAttribute(smem=%d) failed: %s", L::kSmemBytes,
-                         cudaGetErrorString(attr_err));
+    if (const int rc = ensure_max_smem(reinterpret_cast<const void *>(kern), L::kSmemBytes, "gemm_fp8_tc2")) return rc;
     CUtensorMap ta, tb;
     int rc = make_tmap(&ta, d->A, d->K, d->M, d->lda, 128);
     if (rc) return rc;
@@ -1640,14 +1621,7 @@ int launch_splitk(const lcml_fp8_gemm_desc *d, const EpiParams &ep, cudaStream_t
     using L = SplitLayout;
     static_assert(L::kSmemBytes <= kSmemLimit, "shared memory layout does not fit");
     auto kern = k_gemm_fp8_splitk<EPI, OUT>;
-    static std::once_flag once;
-    static cudaError_t attr_err = cudaSuccess;
-    std::call_once(once, [&] {
-        attr_err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kSmemBytes);
-    });
-    if (attr_err != cudaSuccess)
-        return set_error(LCML_ERR_CUDA, "cudaFuncSetAttribute(smem=%d) failed: %s", L::kSmemBytes,
-                         cudaGetErrorString(attr_err));
+    if (const int rc = ensure_max_smem(reinterpret_cast<const void *>(kern), L::kSmemBytes, "gemm_fp8_splitk")) return rc;
     CUtensorMap ta, tb;
     int rc = make_tmap(&ta, d->A, d->K, d->M, d->lda, BM);
     if (rc) return rc;
@@ -1724,7 +1698,7 @@ int dispatch(const lcml_fp8_gemm_desc *d, const EpiParams &ep, cudaStream_t st, 
                         d->K <= 0x7fffffff;
     if (!tma_ok) return launch_simt<EPI, OUT>(d, ep, st);
     if constexpr (EPI != LCML_EPI_SILU_MUL) {
-        const int mode = g_gemm_mode & 3;
+        const int mode = d->variant & 3;
         if (mode == 0) {  // decode-sized M: stream B once on the CUDA cores
             switch (gemv_rows(d, ep)) {
                 case 1: return launch_gemv<1, EPI, OUT>(d, ep, st);
@@ -1741,7 +1715,7 @@ int dispatch(const lcml_fp8_gemm_desc *d, const EpiParams &ep, cudaStream_t st, 
     // and narrow GEMMs are epilogue-bound and run single-CTA tiles as wide as N.
     const int64_t pair_tiles = ((d->M + 255) / 256) * ((d->N + 255) / 256);
     const bool pair = d->M >= 256 && d->N >= 256 && d->K >= 1024 && pair_tiles >= sm_count();
-    if ((g_gemm_mode & 3) != 1 && ((g_gemm_mode & 3) == 2 || pair)) return launch_tc2<EPI, OUT>(d, ep, st);
+    if ((d->variant & 3) != 1 && ((d->variant & 3) == 2 || pair)) return launch_tc2<EPI, OUT>(d, ep, st);
     if (EPI == LCML_EPI_SILU_MUL || d->N >= 2048) return launch_tc<256, EPI, OUT>(d, ep, st);
     if (EPI != LCML_EPI_SILU_MUL && d->N <= 64) return launch_tc<64, EPI, OUT>(d, ep, st);
     return launch_tc<128, EPI, OUT>(d, ep, st);
@@ -1782,6 +1756,7 @@ int gemm_entry(const lcml_fp8_gemm_desc *d, lcml_stream_t stream, bool force_sim
                        (d->c_mat_dtype == LCML_DTYPE_FLOAT8E4M3FN && d->c_mat_scale),
                    "lcml_fp8_gemm: c_mat dtype must be FLOAT, BFLOAT16 or FLOAT8E4M3FN with c_mat_scale");
     LCML_CHECK_ARG(!d->c_vec || (d->c_vec_mode >= 0 && d->c_vec_mode <= 2), "lcml_fp8_gemm: bad c_vec_mode");
+    LCML_CHECK_ARG(d->variant >= 0 && d->variant <= 7, "lcml_fp8_gemm: variant %d unknown", d->variant);
     EpiParams ep;
     ep.M = d->M;
     ep.N = d->N;
@@ -1807,7 +1782,7 @@ int gemm_entry(const lcml_fp8_gemm_desc *d, lcml_stream_t stream, bool force_sim
     ep.y_num_peers = d->y_num_peers;
     {
         const int es = d->y_dtype == LCML_DTYPE_FLOAT ? 4 : (d->y_dtype == LCML_DTYPE_BFLOAT16 ? 2 : 1);
-        ep.tma_store = !(g_gemm_mode & 4) && d->y_num_peers == 0 && n_out <= 0x7fffffff && d->M <= 0x7fffffff &&
+        ep.tma_store = !(d->variant & 4) && d->y_num_peers == 0 && n_out <= 0x7fffffff && d->M <= 0x7fffffff &&
                        aligned(static_cast<const uint8_t *>(d->Y) + d->y_col_offset * es, 16) &&
                        (d->ldy * es) % 16 == 0;
     }
@@ -1856,12 +1831,10 @@ int lcml_fp8_gemm_rowquant(const lcml_fp8_gemm_desc *desc, uint8_t *q, float *q_
     return lcml_fp8_quantize_from_amax(static_cast<const float *>(d.Y), 1, d.M, n_out, workspace, q_scale, q, stream);
 }
 
-// Test hooks (not in the public header): force the SIMT kernel, or pick the
-// tensor-core kernel variant, so tests can cross-check the code paths.
+// Test hook (not in the public header): the SIMT kernel on the same
+// descriptor, so tests can cross-check it against the tensor-core kernels.
 int lcml_fp8_gemm_simt(const lcml_fp8_gemm_desc *desc, lcml_stream_t stream) {
     return lcml::gemm::gemm_entry(desc, stream, true);
 }
-
-void lcml_fp8_gemm_set_mode(int mode) { lcml::gemm::g_gemm_mode = mode; }
 
 }// extern "C"

@@ -4,6 +4,7 @@
 #pragma once
 
 #include <cstdint>
+#include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
 namespace lcml {
@@ -64,6 +65,66 @@ __device__ __forceinline__ float e4m3_decode(uint32_t b) {
     if ((b & 0x7fu) == 0x7fu) return __uint_as_float(0x7fc00000u);
     float v = (e == 0u) ? float(m) * 0.001953125f : __uint_as_float(((e + 120u) << 23) | (m << 20));
     return __uint_as_float(__float_as_uint(v) | sign);
+}
+
+// ---------------------------------------------------------------------------
+// e5m2 (FP8 E5M2) and e2m1 (FP4 E2M1) codecs, bit-exact with the reference's
+// FP8E5M2::from_float / to_float (include/onnx/fp_quantized.h:259-378) and
+// FP4E2M1::from_float / to_float (:20-115), by the same integer RNE as
+// e4m3_encode (round constant + lowest kept bit, shift; carries move into the
+// exponent field) with each format's own edges:
+//   e5m2: NaN -> 0x7f; +-0 -> 0x00; |v| > 57344 (inf included) -> +-inf
+//         (0x7c / 0xfc: the reference does not saturate); subnormal grid 2^-16.
+//   e2m1: +-0 -> 0x0; |v| > 6 (inf included) -> +-6 (0x7 / 0xf); subnormal
+//         grid 0.5. NaN -> 0x0: the reference's encoder has no NaN case (the
+//         value reaches a float -> uint8 conversion of NaN, which is undefined
+//         in C++); 0x0 is what its x86-64 build returns.
+// A nonzero value that rounds to zero keeps its sign in both (0x80 / 0x8).
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ uint32_t e5m2_encode(float v) {
+    const uint32_t u = __float_as_uint(v);
+    const uint32_t sign = (u >> 24) & 0x80u;
+    const uint32_t a = u & 0x7fffffffu;
+    if (a > 0x7f800000u) return 0x7fu;              // NaN
+    if (a == 0u) return 0u;                         // +-0 -> 0x00
+    if (a > 0x47600000u) return sign | 0x7cu;       // > 57344 -> inf
+    uint32_t r;
+    if (a >= 0x38800000u) {                         // >= 2^-14: normal result
+        r = ((a + 0xfffffu + ((a >> 21) & 1u)) >> 21) - (112u << 2);
+    } else {                                        // RNE(|v| * 2^16) in [0, 4]; 4 is the smallest normal 0x04
+        r = __float2uint_rn(__uint_as_float(a) * 65536.0f);
+    }
+    return sign | r;
+}
+
+// e5m2 is the high byte of an IEEE half: the decode is exact through f16.
+// NaN codes give the canonical quiet NaN, as the reference's to_float does.
+__device__ __forceinline__ float e5m2_decode(uint32_t b) {
+    if ((b & 0x7cu) == 0x7cu && (b & 0x3u) != 0u) return __uint_as_float(0x7fc00000u);
+    return __half2float(__ushort_as_half(static_cast<unsigned short>((b & 0xffu) << 8)));
+}
+
+__device__ __forceinline__ uint32_t e2m1_encode(float v) {
+    const uint32_t u = __float_as_uint(v);
+    const uint32_t a = u & 0x7fffffffu;
+    if (a > 0x7f800000u || a == 0u) return 0u;      // NaN, +-0
+    const uint32_t sign = (u >> 28) & 0x8u;
+    if (a > 0x40c00000u) return sign | 0x7u;        // > 6 saturates
+    uint32_t r;
+    if (a >= 0x3f800000u) {                         // >= 1: normal result
+        r = ((a + 0x1fffffu + ((a >> 22) & 1u)) >> 22) - (126u << 1);
+    } else {                                        // RNE(|v| * 2) in [0, 2]; 2 is the smallest normal 0x2
+        r = __float2uint_rn(__uint_as_float(a) * 2.0f);
+    }
+    return sign | r;
+}
+
+__device__ __forceinline__ float e2m1_decode(uint32_t b) {
+    // magnitudes of codes 0..7: 0, 0.5, 1, 1.5, 2, 3, 4, 6 (bias 1, one mantissa bit)
+    const uint32_t m = b & 0x7u;
+    const float mag = m < 2u ? 0.5f * static_cast<float>(m)
+                             : __uint_as_float(((m >> 1) + 126u) << 23 | (m & 1u) << 22);
+    return __uint_as_float(__float_as_uint(mag) | ((b & 0x8u) << 28));
 }
 
 // QuantizeLinear of one element: e4m3(x / s) with an IEEE round-to-nearest divide.

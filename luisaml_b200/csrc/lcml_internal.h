@@ -28,6 +28,12 @@ int sm_count();
 // Device address of the error word on the current device (nullptr if unavailable).
 int *device_error_word();
 
+// Raises `kernel`'s dynamic shared-memory limit to `bytes` on the current
+// device, once per (kernel, device): the attribute belongs to the device that
+// is current when it is set, so a process driving several GPUs sets it on
+// each. Returns an lcml_status (the message names `what`).
+int ensure_max_smem(const void *kernel, int bytes, const char *what);
+
 __host__ __device__ inline bool aligned(const void *p, uintptr_t a) { return (reinterpret_cast<uintptr_t>(p) & (a - 1)) == 0; }
 
 // Geometry of an implicit-GEMM convolution: the GEMM's A operand (rows =

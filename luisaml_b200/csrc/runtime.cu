@@ -2,6 +2,8 @@
 // the device error word and the launch counter.
 #include <cstring>
 #include <mutex>
+#include <set>
+#include <tuple>
 #include <vector>
 
 #include "lcml_device.cuh"
@@ -59,13 +61,32 @@ int *device_error_word() {
     return cache[dev];
 }
 
+int ensure_max_smem(const void *kernel, int bytes, const char *what) {
+    static std::mutex mu;
+    static std::set<std::tuple<const void *, int, int>> done;  // (kernel, device, bytes)
+    int dev = 0;
+    LCML_CUDA(cudaGetDevice(&dev));
+    const auto key = std::make_tuple(kernel, dev, bytes);
+    {
+        std::lock_guard<std::mutex> lk(mu);
+        if (done.count(key)) return LCML_OK;
+    }
+    const cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+    if (e != cudaSuccess)
+        return set_error(LCML_ERR_CUDA, "%s: cudaFuncSetAttribute(smem=%d) on device %d failed: %s", what, bytes, dev,
+                         cudaGetErrorString(e));
+    std::lock_guard<std::mutex> lk(mu);
+    done.insert(key);
+    return LCML_OK;
+}
+
 }// namespace lcml
 
 extern "C" {
 
 const char *lcml_last_error(void) { return lcml::t_error; }
 
-int lcml_abi_version(void) { return 1; }
+int lcml_abi_version(void) { return 2; }
 
 int lcml_device_check(void) {
     int dev = 0, n = 0;

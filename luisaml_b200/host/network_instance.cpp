@@ -160,14 +160,17 @@ void NetworkInstance::create_tensors() {
     for (const auto &kv : g.get_variables()) {
         const Variable &v = *kv.second;
         if (table_.contains(v.get_name()) || !v.is_constant()) continue;
-        const size_t esz = dtype_size(v.get_dtype());
+        const bool fp4 = v.get_dtype() == DataType::FLOAT4E2M1;
         size_t n = 1;
         for (auto d : v.get_shape()) n *= d;
+        const size_t nbytes = dtype_nbytes(v.get_dtype(), n);
         if (v.is_trainable_weight()) {
             if (!weight_buffer_) throw Error("Weight buffer not set but required for variable: " + v.get_name());
             auto [b, e] = v.get_buffer_range();
+            // blob extents as the reference checks them (network_instance.cpp:218-227):
+            // FP8 padded to 4 bytes, FP4 two codes per byte
             const bool fp8 = v.get_dtype() == DataType::FLOAT8E4M3FN || v.get_dtype() == DataType::FLOAT8E5M2;
-            const size_t expected = fp8 ? ((n + 3) / 4) * 4 : n * esz;
+            const size_t expected = fp8 ? ((n + 3) / 4) * 4 : nbytes;
             if (e - b != expected) throw Error("Weight buffer size mismatch for variable: " + v.get_name());
             if (e > weight_bytes_) throw Error("Weight buffer too small for variable: " + v.get_name());
             auto t = DeviceTensor::borrow(v.get_dtype(), to_shape(v.get_shape()),
@@ -175,11 +178,17 @@ void NetworkInstance::create_tensors() {
             t->set_constant({});
             table_.own(v.get_name(), std::move(t));
         } else if (!v.get_raw_data().empty()) {
-            if (esz == 0) throw Error("unsupported element type for constant " + v.get_name());
-            if (v.get_raw_data().size() < n * esz) throw Error("raw_data too short for " + v.get_name());
+            if (nbytes == 0) throw Error("unsupported element type for constant " + v.get_name());
+            if (v.get_raw_data().size() < nbytes) throw Error("raw_data too short for " + v.get_name());
+            std::string bytes = v.get_raw_data().substr(0, nbytes);
+            // FP4 raw_data holds element 2i in the HIGH nibble of byte i (the
+            // reference's loader, network_instance.cpp:242-246), device storage
+            // in the low nibble (FP4Data): swap the nibbles on upload
+            if (fp4)
+                for (auto &c : bytes) c = static_cast<char>(((static_cast<uint8_t>(c) & 0x0f) << 4) | (static_cast<uint8_t>(c) >> 4));
             auto t = DeviceTensor::allocate(v.get_dtype(), to_shape(v.get_shape()));
-            check_status(lcml_memcpy_async(t->data(), v.get_raw_data().data(), n * esz, 1, stream_), "upload constant");
-            t->set_constant(v.get_raw_data().substr(0, n * esz));
+            check_status(lcml_memcpy_async(t->data(), bytes.data(), nbytes, 1, stream_), "upload constant");
+            t->set_constant(bytes);
             table_.own(v.get_name(), std::move(t));
         }
     }

@@ -229,6 +229,8 @@ size_t dtype_size(DataType t) {
     return 0;
 }
 
+size_t dtype_nbytes(DataType t, size_t n) { return t == DataType::FLOAT4E2M1 ? (n + 1) / 2 : n * dtype_size(t); }
+
 AttributeType Attribute::type_of(const Attribute &a) {
     switch (a.index()) {
         case 0: return AttributeType::FLOAT;
@@ -338,7 +340,7 @@ DeviceTensor::~DeviceTensor() {
 std::unique_ptr<DeviceTensor> DeviceTensor::allocate(DataType t, shape_type s) {
     size_t n = 1;
     for (auto d : s) n *= static_cast<size_t>(d);
-    const size_t bytes = n * dtype_size(t);
+    const size_t bytes = dtype_nbytes(t, n);
     void *p = nullptr;
     // round up to 256 B so every tensor starts 256-byte aligned and vector
     // tails never read past the allocation

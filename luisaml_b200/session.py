@@ -48,7 +48,7 @@ def _check(rc):
         raise LcmlError(rc, load().lcml_network_last_error().decode(errors="replace"))
 
 
-_TORCH_DT = {"float32": 1, "bfloat16": 16, "uint8": 17}
+_TORCH_DT = {"float32": 1, "float16": 10, "bfloat16": 16, "uint8": 17}
 
 
 class Network:
@@ -141,7 +141,8 @@ class Network:
         import numpy as np
         from . import check, lib as fp8_lib
         ptr, dt, shape, nhwc = self.tensor_info(name)
-        npdt = {1: np.float32, 16: np.uint16, 17: np.uint8, 2: np.uint8, 7: np.int64, 6: np.int32}[dt]
+        npdt = {1: np.float32, 10: np.uint16, 16: np.uint16, 17: np.uint8, 19: np.uint8, 2: np.uint8, 7: np.int64,
+                6: np.int32}[dt]
         if nhwc and len(shape) == 4:
             shape = (shape[0], shape[2], shape[3], shape[1])
         out = np.empty(shape, dtype=npdt)

@@ -28,8 +28,9 @@ _i64 = ctypes.c_int64
 
 
 def build(quiet: bool = True) -> None:
-    """Compile liboracle.so (and _ref/ when the reference tree is present)."""
-    out = subprocess.run(["make", "-C", HERE, "all"], capture_output=True, text=True)
+    """Compile liboracle.so (and _ref/ when $LCML_REFERENCE_TREE names a reference checkout)."""
+    out = subprocess.run(["make", "-C", HERE, "all", "REF=" + os.environ.get("LCML_REFERENCE_TREE", "")],
+                         capture_output=True, text=True)
     if out.returncode != 0:
         raise RuntimeError("oracle build failed:\n" + out.stdout + out.stderr)
     if not quiet:
@@ -44,6 +45,11 @@ def _load():
     lib.orc_e4m3_from_float.argtypes = [ctypes.c_float]
     lib.orc_e4m3_to_float.restype = ctypes.c_float
     lib.orc_e4m3_to_float.argtypes = [ctypes.c_uint8]
+    for fmt in ("e5m2", "e2m1"):
+        enc, dec = getattr(lib, f"orc_{fmt}_from_float"), getattr(lib, f"orc_{fmt}_to_float")
+        enc.restype, enc.argtypes = ctypes.c_uint8, [ctypes.c_float]
+        dec.restype, dec.argtypes = ctypes.c_float, [ctypes.c_uint8]
+    lib.orc_cast.restype = ctypes.c_int
     lib.orc_amax.restype = ctypes.c_float
     lib.orc_scale_from_amax.restype = ctypes.c_float
     lib.orc_scale_from_amax.argtypes = [ctypes.c_float]
@@ -65,9 +71,13 @@ def ref_lib():
     r.lcml_ref_e4m3_from_float.argtypes = [ctypes.c_float]
     r.lcml_ref_e4m3_to_float.restype = ctypes.c_float
     r.lcml_ref_e4m3_to_float.argtypes = [ctypes.c_uint8]
-    r.lcml_ref_e4m3_count_mismatch.restype = ctypes.c_int64
-    r.lcml_ref_e4m3_count_mismatch.argtypes = [ctypes.c_void_p, ctypes.c_uint64, ctypes.c_uint64,
-                                               ctypes.POINTER(ctypes.c_uint32)]
+    for fmt in ("e4m3", "e5m2", "e2m1"):
+        f = getattr(r, f"lcml_ref_{fmt}_count_mismatch")
+        f.restype = ctypes.c_int64
+        f.argtypes = [ctypes.c_void_p, ctypes.c_uint64, ctypes.c_uint64, ctypes.POINTER(ctypes.c_uint32)]
+        enc, dec = getattr(r, f"lcml_ref_{fmt}_from_float"), getattr(r, f"lcml_ref_{fmt}_to_float")
+        enc.restype, enc.argtypes = ctypes.c_uint8, [ctypes.c_float]
+        dec.restype, dec.argtypes = ctypes.c_float, [ctypes.c_uint8]
     r.lcml_ref_e4m3_quantize_tensor.argtypes = [_f32p, ctypes.c_float, _u8p, _i64]
     return r
 
@@ -97,6 +107,35 @@ def e4m3_decode(q) -> np.ndarray:
     y = np.empty(q.shape, dtype=np.float32)
     lib.orc_e4m3_decode_n(_u(q), _f(y), _i64(q.size))
     return y
+
+
+# ONNX type numbers of the Cast restatement and their numpy storage
+CAST_TYPES = {1: np.float32, 10: np.float16, 16: np.uint16, 17: np.uint8, 19: np.uint8, 23: np.uint8}
+
+
+def cast(x, src: int, dst: int, n: int | None = None) -> np.ndarray:
+    """Cast (cast.cpp:10-162) of n elements of storage `x` (type code `src`)
+    to type `dst` (ONNX numbers; 16 = bf16 held as uint16, 23 = FP4 E2M1 packed
+    two per byte, element 2i in the low nibble). Returns the raw storage."""
+    x = np.ascontiguousarray(x)
+    if n is None:
+        n = x.size * 2 if src == 23 else x.size
+    out = np.zeros((n + 1) // 2 if dst == 23 else n, dtype=CAST_TYPES[dst])
+    rc = lib.orc_cast(x.ctypes.data_as(ctypes.c_void_p), ctypes.c_int(src), out.ctypes.data_as(ctypes.c_void_p),
+                      ctypes.c_int(dst), _i64(n))
+    if rc != 0:
+        raise ValueError(f"oracle cast {src} -> {dst} unsupported")
+    return out
+
+
+def e5m2_encode(x) -> np.ndarray:
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    return np.array([lib.orc_e5m2_from_float(float(v)) for v in x.ravel()], dtype=np.uint8).reshape(x.shape)
+
+
+def e2m1_encode(x) -> np.ndarray:
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    return np.array([lib.orc_e2m1_from_float(float(v)) for v in x.ravel()], dtype=np.uint8).reshape(x.shape)
 
 
 # --------------------------------------------------------------------------- QDQ

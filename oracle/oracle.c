@@ -89,6 +89,167 @@ ORC_EXPORT void orc_e4m3_decode_n(const uint8_t *q, float *y, int64_t n) {
 }
 
 /* ------------------------------------------------------------------------- */
+/* e5m2 and e2m1 codecs                                                       */
+/* ------------------------------------------------------------------------- */
+
+/*
+ * Round-to-nearest-even of a finite a > 0 onto a minifloat grid with `mbits`
+ * mantissa bits, exponent bias `bias` and subnormal ulp 2^(1 - bias - mbits):
+ * returns the code without sign (exponent field << mbits | mantissa); a carry
+ * out of the mantissa moves into the exponent by plain addition.
+ */
+static uint32_t orc_minifloat_rne(float a, int mbits, int bias) {
+    int ex;
+    float fr = frexpf(a, &ex);      /* a = fr * 2^ex, fr in [0.5, 1) */
+    int e = ex - 1 + bias;          /* biased exponent of the leading bit */
+    float units;                    /* a in units of the result's ulp */
+    if (e <= 0) {
+        e = 0;
+        units = ldexpf(a, bias - 1 + mbits);
+    } else {
+        units = ldexpf(fr, mbits + 1);  /* [2^mbits, 2^(mbits+1)): implicit bit + mantissa */
+    }
+    float fl = floorf(units);
+    float rem = units - fl;
+    uint32_t m = (uint32_t)fl;
+    if (rem > 0.5f || (rem == 0.5f && (m & 1u))) m += 1u;
+    if (e == 0) return m;           /* m == 2^mbits is exactly the smallest normal code */
+    return ((uint32_t)e << mbits) + (m - (1u << mbits));
+}
+
+/*
+ * fp32 -> FP8 E5M2 byte. Restates FP8E5M2::from_float
+ * (include/onnx/fp_quantized.h:271-353): NaN -> 0x7f (:273-276); +-inf and
+ * |v| > 57344 -> +-inf 0x7c/0xfc, no saturation (:277-294); +-0 -> 0x00
+ * (:281-284); RNE on 2 mantissa bits, subnormal ulp 2^-16 (:296-327); a
+ * result that rounds to zero keeps the sign (:337-341).
+ */
+ORC_EXPORT uint8_t orc_e5m2_from_float(float v) {
+    if (isnan(v)) return 0x7f;
+    if (v == 0.0f) return 0x00;
+    uint8_t sign = signbit(v) ? 0x80 : 0x00;
+    float a = fabsf(v);
+    if (a > 57344.0f) return (uint8_t)(sign | 0x7c);
+    return (uint8_t)(sign | orc_minifloat_rne(a, 2, 15));
+}
+
+/* FP8 E5M2 byte -> fp32 (fp_quantized.h:356-377): 0x7c/0xfc -> +-inf, other
+ * exponent-31 codes NaN, subnormal m * 2^-16, normal (1 + m/4) * 2^(e-15). */
+ORC_EXPORT float orc_e5m2_to_float(uint8_t b) {
+    int neg = (b & 0x80) != 0;
+    int e = (b >> 2) & 0x1f;
+    int m = b & 0x3;
+    float v;
+    if (e == 31) {
+        if (m != 0) return NAN;
+        return neg ? -INFINITY : INFINITY;
+    }
+    if (e == 0) v = ldexpf((float)m, -16);
+    else v = ldexpf((float)(4 + m), e - 17);
+    return neg ? -v : v;
+}
+
+/*
+ * fp32 -> FP4 E2M1 code (low nibble). Restates FP4E2M1::from_float
+ * (include/onnx/fp_quantized.h:33-93): +-0 -> 0x0 (:34-36); |v| > 6 (inf
+ * included) -> +-6 = 0x7/0xf (:43-46); RNE on 1 mantissa bit, subnormal ulp
+ * 0.5 (:48-79); a result that rounds to zero keeps the sign (:87-89). The
+ * reference has no NaN case (NaN reaches an undefined float -> uint8
+ * conversion); its x86-64 build returns 0x0, which is the value used here.
+ */
+ORC_EXPORT uint8_t orc_e2m1_from_float(float v) {
+    if (isnan(v) || v == 0.0f) return 0x0;
+    uint8_t sign = signbit(v) ? 0x8 : 0x0;
+    float a = fabsf(v);
+    if (a > 6.0f) return (uint8_t)(sign | 0x7);
+    return (uint8_t)(sign | orc_minifloat_rne(a, 1, 1));
+}
+
+/* FP4 E2M1 code -> fp32 (fp_quantized.h:96-114): subnormal m * 0.5, normal
+ * (1 + m/2) * 2^(e-1), code 0x8 -> -0.0. */
+ORC_EXPORT float orc_e2m1_to_float(uint8_t b) {
+    int neg = (b & 0x8) != 0;
+    int e = (b >> 1) & 0x3;
+    int m = b & 0x1;
+    float v = e == 0 ? 0.5f * (float)m : ldexpf((float)(2 + m), e - 2);
+    return neg ? -v : v;
+}
+
+/*
+ * Cast (src/onnx/operators/cast.cpp:10-162) of n elements. Type codes are the
+ * ONNX numbers: 1 FLOAT, 10 FLOAT16, 16 BFLOAT16, 17 FLOAT8E4M3FN,
+ * 19 FLOAT8E5M2, 23 FLOAT4E2M1 (packed, element 2i in the low nibble of byte
+ * i). To an FP8 / FP4 type the value is first rounded to half and then
+ * encoded (cast.cpp:58-72: `fp8_from(input[i].cast<half>())`); from FP8 / FP4
+ * it is decoded (cast.cpp:39-53, exact in every floating type); between the
+ * floating types one round-to-nearest-even conversion (_Float16 / bf16 RNE).
+ */
+static float orc_bf16_to_float(uint16_t h) {
+    uint32_t u = (uint32_t)h << 16;
+    float f;
+    memcpy(&f, &u, 4);
+    return f;
+}
+
+static uint16_t orc_float_to_bf16(float f) {
+    uint32_t u;
+    memcpy(&u, &f, 4);
+    if ((u & 0x7fffffffu) > 0x7f800000u) return (uint16_t)((u >> 16) | 0x40u);  /* quiet NaN, sign kept */
+    u += 0x7fffu + ((u >> 16) & 1u);
+    return (uint16_t)(u >> 16);
+}
+
+static float orc_load(const uint8_t *x, int t, int64_t i) {
+    switch (t) {
+        case 1: { float f; memcpy(&f, x + 4 * i, 4); return f; }
+        case 10: { _Float16 h; memcpy(&h, x + 2 * i, 2); return (float)h; }
+        case 16: { uint16_t h; memcpy(&h, x + 2 * i, 2); return orc_bf16_to_float(h); }
+        case 17: return orc_e4m3_to_float(x[i]);
+        case 19: return orc_e5m2_to_float(x[i]);
+        default: return orc_e2m1_to_float((uint8_t)((x[i >> 1] >> ((i & 1) * 4)) & 0xf));
+    }
+}
+
+static int orc_cast_type_ok(int t) { return t == 1 || t == 10 || t == 16 || t == 17 || t == 19 || t == 23; }
+
+/* The destination bits of value v (already rounded to half where the Cast
+ * semantics ask for it). */
+static uint32_t orc_cast_bits(float v, int dst) {
+    if (dst == 1) {
+        uint32_t u;
+        memcpy(&u, &v, 4);
+        return u;
+    }
+    if (dst == 10) {
+        _Float16 h = (_Float16)v;
+        uint16_t u;
+        memcpy(&u, &h, 2);
+        return u;
+    }
+    if (dst == 16) return orc_float_to_bf16(v);
+    if (dst == 17) return orc_e4m3_from_float(v);
+    if (dst == 19) return orc_e5m2_from_float(v);
+    return orc_e2m1_from_float(v);
+}
+
+ORC_EXPORT int orc_cast(const void *xv, int src, void *yv, int dst, int64_t n) {
+    if (!orc_cast_type_ok(src) || !orc_cast_type_ok(dst)) return -1;
+    const uint8_t *x = (const uint8_t *)xv;
+    uint8_t *y = (uint8_t *)yv;
+    const int quantized_dst = dst == 17 || dst == 19 || dst == 23;
+    const int bytes = dst == 1 ? 4 : (dst == 10 || dst == 16) ? 2 : 1;
+    if (dst == 23) memset(y, 0, (size_t)((n + 1) / 2));
+    for (int64_t i = 0; i < n; ++i) {
+        float v = orc_load(x, src, i);
+        if (quantized_dst && (src == 1 || src == 16)) v = (float)(_Float16)v;  /* cast<half>() first */
+        const uint32_t b = orc_cast_bits(v, dst);
+        if (dst == 23) y[i >> 1] |= (uint8_t)(b << ((i & 1) * 4));
+        else memcpy(y + bytes * i, &b, (size_t)bytes);  /* little-endian low bytes */
+    }
+    return 0;
+}
+
+/* ------------------------------------------------------------------------- */
 /* QuantizeLinear / DequantizeLinear (ONNX semantics, float8e4m3fn, zp = 0,    */
 /* saturate = 1). The reference registers neither op; the encoder is the      */
 /* reference codec above applied to the fp32 quotient x / s.                  */

@@ -39,21 +39,35 @@ void lcml_ref_e4m3_quantize_tensor(const float *x, float s, uint8_t *y, int64_t 
     for (int64_t i = 0; i < n; ++i) y[i] = FP8E4M3FN::from_float(x[i] / s);
 }
 
-// Counts encoder disagreements between the reference codec and a candidate
-// encoder over the fp32 bit patterns [lo, hi). Used by the exhaustive check.
-int64_t lcml_ref_e4m3_count_mismatch(uint8_t (*candidate)(float), uint64_t lo, uint64_t hi,
-                                     uint32_t *first_bad) {
+// Counts encoder disagreements between a reference encoder and a candidate
+// encoder over the fp32 bit patterns [lo, hi). Used by the exhaustive checks.
+extern "C++" {
+template <uint8_t (*REF)(float)>
+static int64_t count_mismatch(uint8_t (*candidate)(float), uint64_t lo, uint64_t hi, uint32_t *first_bad) {
     int64_t bad = 0;
     for (uint64_t u = lo; u < hi; ++u) {
         uint32_t bits = static_cast<uint32_t>(u);
         float v;
         __builtin_memcpy(&v, &bits, 4);
-        if (FP8E4M3FN::from_float(v) != candidate(v)) {
+        if (REF(v) != candidate(v)) {
             if (bad == 0 && first_bad) *first_bad = bits;
             ++bad;
         }
     }
     return bad;
+}
+}
+
+int64_t lcml_ref_e4m3_count_mismatch(uint8_t (*candidate)(float), uint64_t lo, uint64_t hi, uint32_t *first_bad) {
+    return count_mismatch<FP8E4M3FN::from_float>(candidate, lo, hi, first_bad);
+}
+
+int64_t lcml_ref_e5m2_count_mismatch(uint8_t (*candidate)(float), uint64_t lo, uint64_t hi, uint32_t *first_bad) {
+    return count_mismatch<FP8E5M2::from_float>(candidate, lo, hi, first_bad);
+}
+
+int64_t lcml_ref_e2m1_count_mismatch(uint8_t (*candidate)(float), uint64_t lo, uint64_t hi, uint32_t *first_bad) {
+    return count_mismatch<FP4E2M1::from_float>(candidate, lo, hi, first_bad);
 }
 
 }// extern "C"

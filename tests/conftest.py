@@ -70,13 +70,3 @@ def assert_close(got, ref, rtol=RTOL, atol=ATOL, what="", extra=0.0):
         i = np.unravel_index(np.argmax(err - bound), err.shape)
         raise AssertionError(f"{what}: {bad.sum()} / {bad.size} elements out of tolerance "
                              f"(rtol {rtol}, atol {atol}); worst at {i}: got {got[i]} ref {ref[i]}")
-
-
-@pytest.fixture
-def gemm_mode():
-    """Sets the GEMM kernel selection hook (0 automatic, 1 single-CTA
-    tiles, 2 CTA pairs, 3 split-K also for M > 128; bit 2 plain stores) and
-    restores automatic after."""
-    import luisaml_b200 as lb
-    yield lambda m: lb.lib().lcml_fp8_gemm_set_mode(m)
-    lb.lib().lcml_fp8_gemm_set_mode(0)

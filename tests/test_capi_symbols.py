@@ -27,7 +27,7 @@ def test_fp8_header_symbols_exported():
     assert len(names) >= 20
     missing = [n for n in names if not hasattr(lib, n)]
     assert not missing, missing
-    assert lib.lcml_abi_version() == 1
+    assert lib.lcml_abi_version() == 2  # 2: per-call `variant` fields in the GEMM and conv descriptors
 
 
 def test_python_prototypes_cover_header():

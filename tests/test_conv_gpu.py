@@ -21,7 +21,7 @@ def _t(a, dev):
 
 
 def _run_conv(dev, X, W, bias, stride, pad, nhwc_in=True, relu=False, residual=None, out="f32", y_scale=None,
-              no_workspace=False, dil=1):
+              no_workspace=False, dil=1, variant=0):
     """Quantizes X (per tensor) and W (per channel) with the oracle, runs the
     GPU conv; returns (gpu NCHW fp32 result, oracle result on the dequantized
     operands, dequantization helpers)."""
@@ -53,6 +53,7 @@ def _run_conv(dev, X, W, bias, stride, pad, nhwc_in=True, relu=False, residual=N
     d.pH = d.pW = pad
     d.dH = d.dW = dil
     d.group = 1
+    d.variant = variant
     d.X, d.x_nhwc, d.scale_x = xt.data_ptr(), int(nhwc_in), sxt.data_ptr()
     d.Wp, d.scale_w, d.scale_w_mode = Wp.data_ptr(), swt.data_ptr(), lb.SCALE_AXIS
     keep = [xt, sxt, swt, Wp]
@@ -112,44 +113,36 @@ CASES = [
 ]
 
 
-@pytest.fixture
-def conv_mode():
-    import luisaml_b200 as lb
-    yield lambda m: lb.lib().lcml_fp8_conv_set_mode(m)
-    lb.lib().lcml_fp8_conv_set_mode(0)
-
-
 def _implicit(C, k, stride, pad, nhwc):
     return nhwc and C % 64 == 0 and not (k == 1 and stride == 1 and pad == 0)
 
 
 @pytest.mark.parametrize("name,N,C,H,M,k,stride,pad,nhwc,dil", CASES)
-def test_conv_shapes(dev, conv_mode, gemm_mode, name, N, C, H, M, k, stride, pad, nhwc, dil):
+def test_conv_shapes(dev, name, N, C, H, M, k, stride, pad, nhwc, dil):
     """Every lowering vs the oracle: direct 1x1, materialized im2col (conv
-    mode 1) and, for NHWC inputs with C % 64 == 0, the implicit GEMM (TMA
-    im2col loads; the default there, with or without a workspace), whose
+    variant bit 0) and, for NHWC inputs with C % 64 == 0, the implicit GEMM
+    (TMA im2col loads; the default there, with or without a workspace), whose
     result must equal the materialized one bit for bit when both run the
-    single-CTA GEMM (GEMM mode 1). With automatic GEMM selection a small
-    materialized conv may run split-K (another summation order): checked
-    against the oracle."""
+    single-CTA GEMM (GEMM variant 1 in bits 8-10). With automatic GEMM
+    selection a small materialized conv may run split-K (another summation
+    order): checked against the oracle."""
     rng = np.random.default_rng(sum(name.encode()))
     X = rng.standard_normal((N, C, H, H)).astype(np.float32)
     W = (rng.standard_normal((M, C, k, k)) * np.sqrt(2.0 / (C * k * k))).astype(np.float32)
     bias = (rng.standard_normal(M) * 0.01).astype(np.float32)
-    conv_mode(1)
-    got_auto, ref, _ = _run_conv(dev, X, W, bias, stride, pad, nhwc_in=nhwc, dil=dil)
+    got_auto, ref, _ = _run_conv(dev, X, W, bias, stride, pad, nhwc_in=nhwc, dil=dil, variant=1)
     assert_close(got_auto, ref, what=name + " (automatic GEMM selection)")
-    gemm_mode(1)
-    got, ref, ws = _run_conv(dev, X, W, bias, stride, pad, nhwc_in=nhwc, dil=dil)
+    single_cta = 1 << 8
+    got, ref, ws = _run_conv(dev, X, W, bias, stride, pad, nhwc_in=nhwc, dil=dil, variant=1 | single_cta)
     assert (ws == 0) == (name == "1x1_direct")
     assert_close(got, ref, what=name)
-    conv_mode(0)
-    got_a, _, ws_a = _run_conv(dev, X, W, bias, stride, pad, nhwc_in=nhwc, dil=dil)
+    got_a, _, ws_a = _run_conv(dev, X, W, bias, stride, pad, nhwc_in=nhwc, dil=dil, variant=single_cta)
     implicit = _implicit(C, k, stride, pad, nhwc)
     assert (ws_a == 0) == (implicit or name == "1x1_direct")
     np.testing.assert_array_equal(got_a, got)
     if implicit:
-        got_n, _, _ = _run_conv(dev, X, W, bias, stride, pad, nhwc_in=nhwc, no_workspace=True, dil=dil)
+        got_n, _, _ = _run_conv(dev, X, W, bias, stride, pad, nhwc_in=nhwc, no_workspace=True, dil=dil,
+                                variant=single_cta)
         np.testing.assert_array_equal(got_n, got)
 
 

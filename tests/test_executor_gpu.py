@@ -223,3 +223,76 @@ def test_ffn_graph_fused_vs_oracle(dev):
     ref = oracle.qdq_gemm(hq, sh, meta["wd_q"], meta["wd_s"]) + x
     assert_close_bf16(y_fused, ref, what="fused FFN vs oracle")
     assert_close_bf16(y_unfused, ref, what="unfused FFN vs oracle")
+
+
+def test_ffn_config_shape_stage_by_stage(dev):
+    """The configuration's FFN, 4096 tokens x d_model 4096 x ffn 11008,
+    through NetworkInstance, each stage held to the oracle on the executor's
+    own input (read back with lcml_network_tensor):
+      * x's dynamic per-token quantization: codes and scales bit-exact (all rows);
+      * the gate/up GEMM with the SiLU*up epilogue (a 22016-wide CTA-pair GEMM,
+        fp32 h): sampled token rows at rtol 2e-3 / atol 1e-3 against the
+        oracle's K-ordered fp32 chain on the executor's x codes;
+      * h's dynamic per-token quantization: bit-exact on the executor's h (all rows);
+      * the down GEMM + residual, bf16 out: sampled rows at rtol 2e-3 /
+        atol 1e-3 plus the bf16 half ulp, on the executor's h codes."""
+    import torch
+    from conftest import assert_close_bf16
+    from luisaml_b200 import graphs
+    from luisaml_b200.session import Network
+    T, D, F = 4096, 4096, 11008
+    text, blob, meta = graphs.ffn(T, D, F)
+    x = np.random.default_rng(3001).standard_normal((T, D)).astype(np.float32)
+    net = Network(text)
+    y = torch.empty((T, D), dtype=torch.bfloat16, device=dev)
+    net.set_weight_buffer(_t(np.frombuffer(blob, dtype=np.uint8), dev))
+    net.set_input("x", _t(x, dev))
+    net.set_output("y", y)
+    net.forward()
+    torch.cuda.synchronize()
+    assert net.executed_nodes() == 4, net.summary()
+    import luisaml_b200 as lb
+    assert lb.device_error() == 0
+    xq, sx = net.read_tensor("x_q"), net.read_tensor("x_scale")
+    xq_ref, sx_ref = oracle.quantize_dynamic_rows(x)
+    assert np.array_equal(sx, sx_ref) and np.array_equal(xq, xq_ref), "x quantization differs from the oracle"
+    rows = np.unique(np.concatenate([[0, 1, 127, 128, 2047, 4095], np.random.default_rng(5).integers(0, T, 10)]))
+    h = net.read_tensor("h")
+    g = oracle.qdq_gemm(xq[rows], sx[rows], meta["wg_q"], meta["wg_s"])
+    u = oracle.qdq_gemm(xq[rows], sx[rows], meta["wu_q"], meta["wu_s"])
+    assert_close(h[rows], oracle.silu_mul(g, u), what="gate/up GEMM + SiLU*up at the config shape")
+    hq, sh = net.read_tensor("h_q"), net.read_tensor("h_scale")
+    hq_ref, sh_ref = oracle.quantize_dynamic_rows(h)
+    assert np.array_equal(sh, sh_ref) and np.array_equal(hq, hq_ref), "h quantization differs from the oracle"
+    ref = oracle.qdq_gemm(hq[rows], sh[rows], meta["wd_q"], meta["wd_s"]) + x[rows]
+    assert_close_bf16(y.float().cpu().numpy()[rows], ref, what="down GEMM + residual at the config shape")
+
+
+def test_dynamic_row_quant_all_zero_row(dev):
+    """An all-zero token row: the fused executor's dynamic quantization uses
+    scale 1 (codes 0), the kernel rule for an all-zero slice; the unfused
+    ONNX chain Abs -> ReduceMax -> Div(448) -> QuantizeLinear computes
+    scale 0 and 0 / 0 = NaN codes (0x7f) for that row. Both are pinned."""
+    import torch
+    from luisaml_b200 import graphs
+    from luisaml_b200.session import Network
+    T, D, F = 128, 256, 256
+    text, blob, meta = graphs.ffn(T, D, F)
+    x = np.random.default_rng(3002).standard_normal((T, D)).astype(np.float32)
+    x[5] = 0.0
+    out = {}
+    for fusion in (True, False):
+        net = Network(text)
+        net.set_fusion(fusion)
+        y = torch.empty((T, D), dtype=torch.bfloat16, device=dev)
+        net.set_weight_buffer(_t(np.frombuffer(blob, dtype=np.uint8), dev))
+        net.set_input("x", _t(x, dev))
+        net.set_output("y", y)
+        net.forward()
+        torch.cuda.synchronize()
+        out[fusion] = (net.read_tensor("x_q"), net.read_tensor("x_scale"))
+    q, s = out[True]
+    assert s[5] == 1.0 and (q[5] == 0).all()
+    q, s = out[False]
+    assert s[5] == 0.0 and (q[5] == 0x7f).all()
+    np.testing.assert_array_equal(out[True][0][:5], out[False][0][:5])

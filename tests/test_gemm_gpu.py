@@ -152,17 +152,17 @@ def test_gemm_e4m3_output(dev):
     assert (got == want).mean() > 0.99
 
 
-@pytest.mark.parametrize("M,N,K", [(1, 4096, 4096), (3, 1000, 2048), (4, 520, 3072), (48, 640, 2048),
-                                   (200, 1000, 2048)])
-def test_splitk_epilogues(dev, gemm_mode, M, N, K):
+@pytest.mark.parametrize("M,N,K", [(1, 4096, 4096), (2, 1001, 4096), (3, 1000, 2048), (4, 520, 3072),
+                                   (48, 640, 2048), (200, 1000, 2048)])
+def test_splitk_epilogues(dev, M, N, K):
     """Skinny GEMMs run split-K in a CTA cluster (partials reduced through
     distributed shared memory): per-row / per-column scales, bias, a residual
     (fp32 and e4m3), Relu, the row |max| and every output type against the
-    oracle, and against the single-CTA kernel (forced by mode 1). M > 128
-    (two row tiles, the last one partial) takes split-K only when mode 3
+    oracle, and against the single-CTA kernel (forced by variant 1). M > 128
+    (two row tiles, the last one partial) takes split-K only when variant 3
     forces it; automatic selection gives it single-CTA tiles. M <= 4 runs the
-    CUDA-core GEMV under automatic selection (mode 0) and split-K under
-    mode 3, so both are checked with the same epilogues."""
+    CUDA-core GEMV under automatic selection (variant 0) and split-K under
+    variant 3, so both are checked with the same epilogues."""
     import torch
     import luisaml_b200 as lb
     Aq, sa, Bq, sb = make_operands(M, N, K, seed=M + N + K, per_row=True, per_col=True, b_std=0.05)
@@ -174,15 +174,13 @@ def test_splitk_epilogues(dev, gemm_mode, M, N, K):
     kw = dict(c_vec=_t(bias, dev), c_mat=_t(res, dev), epilogue=lb.EPI_RELU)
     results = {}
     for mode in (0, 1, 3):
-        gemm_mode(mode)
         amax = torch.zeros(M, dtype=torch.float32, device=dev)
-        y = lb.gemm(*args, out_dtype=torch.float32, row_amax=amax, **kw).cpu().numpy()
-        assert_close(y, ref, what=f"split-K {M}x{N}x{K} mode {mode}")
+        y = lb.gemm(*args, out_dtype=torch.float32, row_amax=amax, variant=mode, **kw).cpu().numpy()
+        assert_close(y, ref, what=f"split-K {M}x{N}x{K} variant {mode}")
         assert np.array_equal(amax.cpu().numpy(), np.abs(y).max(axis=1))
-        yb = lb.gemm(*args, out_dtype=torch.bfloat16, **kw)
+        yb = lb.gemm(*args, out_dtype=torch.bfloat16, variant=mode, **kw)
         assert torch.equal(yb.cpu(), torch.from_numpy(y).bfloat16())
         results[mode] = y
-    gemm_mode(0)
     assert_close(results[0], results[1], rtol=1e-5, atol=1e-4, what="automatic vs single CTA")
     assert_close(results[3], results[1], rtol=1e-5, atol=1e-4, what="split-K vs single CTA")
     # e4m3 residual and e4m3 output (the epilogue quantization rule on the split-K sum)
@@ -259,25 +257,23 @@ def test_large_8192_sampled_rows(dev):
     (1024, 1536, 640, False, True),
     (2048, 2048, 1024, True, False),
 ])
-def test_kernel_variants(dev, gemm_mode, mode, M, N, K, per_row, per_col):
-    """Single-CTA (mode 1) and CTA-pair (mode 2) tensor-core kernels vs the oracle."""
+def test_kernel_variants(dev, mode, M, N, K, per_row, per_col):
+    """Single-CTA (variant 1) and CTA-pair (variant 2) tensor-core kernels vs the oracle."""
     import torch
     import luisaml_b200 as lb
-    gemm_mode(mode)
     Aq, sa, Bq, sb = make_operands(M, N, K, seed=M + N + K + mode, per_row=per_row, per_col=per_col)
     bias = np.random.default_rng(M).standard_normal(N).astype(np.float32)
     ref = np.maximum(oracle.qdq_gemm(Aq, sa, Bq, sb) + bias, 0.0)
     Y = lb.gemm(_t(Aq, dev), _t(Bq, dev), _t(sa, dev), _t(sb, dev), c_vec=_t(bias, dev), epilogue=lb.EPI_RELU,
-                out_dtype=torch.float32)
-    assert_close(Y.cpu().numpy(), ref, what=f"mode {mode} {M}x{N}x{K}")
+                out_dtype=torch.float32, variant=mode)
+    assert_close(Y.cpu().numpy(), ref, what=f"variant {mode} {M}x{N}x{K}")
     assert lb.device_error() == 0
 
 
 @pytest.mark.parametrize("mode", [1, 2])
-def test_kernel_variants_silu(dev, gemm_mode, mode):
+def test_kernel_variants_silu(dev, mode):
     import torch
     import luisaml_b200 as lb
-    gemm_mode(mode)
     M, F, K = 512, 512, 384
     rng = np.random.default_rng(41)
     Aq, sa = oracle.quantize_dynamic_rows(rng.standard_normal((M, K)).astype(np.float32))
@@ -289,8 +285,8 @@ def test_kernel_variants_silu(dev, gemm_mode, mode):
     u = np.concatenate([full[:, i + 128:i + 256] for i in range(0, 2 * F, 256)], axis=1)
     ref = oracle.silu_mul(g, u)
     Y = lb.gemm(_t(Aq, dev), _t(Wq, dev), _t(sa, dev), _t(sw, dev), epilogue=lb.EPI_SILU_MUL,
-                out_dtype=torch.float32)
-    assert_close(Y.cpu().numpy(), ref, what=f"silu mode {mode}")
+                out_dtype=torch.float32, variant=mode)
+    assert_close(Y.cpu().numpy(), ref, what=f"silu variant {mode}")
 
 
 @pytest.mark.parametrize("epilogue", ["silu", "none"])
@@ -325,14 +321,13 @@ def test_gemm_rowquant(dev, epilogue):
 
 @pytest.mark.parametrize("out", ["bf16", "f32", "e4m3"])
 @pytest.mark.parametrize("mode", [1, 2])
-def test_gemm_column_shard_and_peer_copies(dev, gemm_mode, out, mode):
+def test_gemm_column_shard_and_peer_copies(dev, out, mode):
     """The epilogue's column-offset + extra-destination stores (the fused
     all-gather path, staged through shared memory) on one GPU: a second
     buffer on the same device stands in for a peer's output."""
     import ctypes
     import torch
     import luisaml_b200 as lb
-    gemm_mode(mode)
     M, N, K, Ntot, off = 300, 512, 256, 1024, 256
     Aq, sa, Bq, sb = make_operands(M, N, K, seed=61, per_row=True, per_col=True, b_std=0.05)
     ref = oracle.qdq_gemm(Aq, sa, Bq, sb)
@@ -341,7 +336,7 @@ def test_gemm_column_shard_and_peer_copies(dev, gemm_mode, out, mode):
     Y2 = torch.zeros((M, Ntot), dtype=dt, device=dev)
     ys = _t(np.float32([oracle.scale_from_amax(np.abs(ref).max())]), dev)
     d, _ = lb.gemm(_t(Aq, dev), _t(Bq, dev), _t(sa, dev), _t(sb, dev), out_dtype=dt, desc_only=True,
-                   y_scale=ys if out == "e4m3" else None)
+                   y_scale=ys if out == "e4m3" else None, variant=mode)
     peers = torch.tensor([Y2.data_ptr()], dtype=torch.int64, device=dev)
     d.Y, d.ldy, d.y_col_offset, d.y_peers, d.y_num_peers = Y.data_ptr(), Ntot, off, peers.data_ptr(), 1
     lb.check(lb.lib().lcml_fp8_gemm(ctypes.byref(d), ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)))
@@ -391,8 +386,8 @@ def test_epilogue_quantize_rule(dev):
 @pytest.mark.parametrize("out", ["f32", "bf16", "e4m3"])
 @pytest.mark.parametrize("mode", [1, 2])
 @pytest.mark.parametrize("M,N,K", [(300, 528, 200), (97, 64, 64), (1000, 96, 576)])
-def test_store_paths(dev, gemm_mode, out, mode, M, N, K):
-    """The TMA-store epilogue (default) and plain per-row stores (mode bit 4)
+def test_store_paths(dev, out, mode, M, N, K):
+    """The TMA-store epilogue (default) and plain per-row stores (variant bit 4)
     write bit-identical outputs, including ragged edges in M and N and an
     output placed at a column offset inside a wider matrix whose other columns
     must stay untouched; the fp32 result also matches the oracle and the e4m3
@@ -409,11 +404,10 @@ def test_store_paths(dev, gemm_mode, out, mode, M, N, K):
     args = (_t(Aq, dev), _t(Bq, dev), _t(sa, dev), _t(sb, dev))
     results = []
     for m in (mode, mode | 4):
-        gemm_mode(m)
         wide = torch.zeros((M, N + 48), dtype=dt, device=dev)
         wide.view(torch.uint8).fill_(0x55)
         lb.gemm(*args, c_vec=_t(bias, dev), epilogue=lb.EPI_RELU, out=wide[:, 16:16 + N],
-                y_scale=ys if out == "e4m3" else None)
+                y_scale=ys if out == "e4m3" else None, variant=m)
         torch.cuda.synchronize()
         assert lb.device_error() == 0
         results.append(wide.view(torch.uint8).cpu().numpy())
@@ -424,8 +418,8 @@ def test_store_paths(dev, gemm_mode, out, mode, M, N, K):
         got = results[0].view(np.float32)[:, 16:16 + N]
         assert_close(got, ref, what=f"store paths {M}x{N}x{K}")
     elif out == "e4m3":
-        gemm_mode(mode)
-        y32 = lb.gemm(*args, c_vec=_t(bias, dev), epilogue=lb.EPI_RELU, out_dtype=torch.float32).cpu().numpy()
+        y32 = lb.gemm(*args, c_vec=_t(bias, dev), epilogue=lb.EPI_RELU, out_dtype=torch.float32,
+                      variant=mode).cpu().numpy()
         s = np.float32(ys.cpu()[0])
         want = epilogue_quantize(y32, s)
         np.testing.assert_array_equal(results[0][:, 16:16 + N], want)

@@ -82,3 +82,73 @@ def test_fused_allgather_two_gpus():
     ref = oracle.qdq_gemm(aq, sa, bq, sb)
     assert_close(full, ref, what="rank 0 gathered output")
     assert np.array_equal(full, r1[1]), "ranks hold different outputs"
+
+
+def test_tp_config_shape_one_gpu(dev):
+    """The configuration's TP GEMM problem on one GPU, 16384 x 8192 x 28672:
+    A ~N(0,1) per-token dynamically quantized, B ~N(0,0.02) per-column e4m3,
+    bf16 out (the CTA-pair kernel). Per-token codes and scales bit-exact on
+    sampled rows, per-column codes and scales on sampled columns, and sampled
+    full rows of Y (all 28672 columns, full K) at rtol 2e-3 / atol 1e-3 plus
+    the bf16 half ulp."""
+    import torch
+    import luisaml_b200 as lb
+    import oracle
+    from conftest import assert_close_bf16
+    from luisaml_b200 import tp
+    M, K, N = 16384, 8192, 28672
+    A = torch.randn((M, K), generator=torch.Generator(device=dev).manual_seed(5000), device=dev)
+    Bt = tp.column_block_weights(torch, K, 0, N, dev, 5100, 0.02)
+    Bq, sb = lb.quantize_rows_dynamic(Bt)  # per-column scales of B = per-row of B^T
+    Aq, sa = lb.quantize_rows_dynamic(A)
+    Y = lb.gemm(Aq, Bq, sa, sb, out_dtype=torch.bfloat16)
+    torch.cuda.synchronize()
+    assert lb.device_error() == 0
+    rng = np.random.default_rng(8)
+    rows = np.unique(np.concatenate([[0, 255, 256, M - 1], rng.integers(0, M, 4)]))
+    cols = np.unique(np.concatenate([[0, 127, 128, N - 1], rng.integers(0, N, 8)]))
+    ri = torch.from_numpy(rows).to(dev)
+    ci = torch.from_numpy(cols).to(dev)
+    aq_ref, sa_ref = oracle.quantize_dynamic_rows(A[ri].cpu().numpy())
+    assert np.array_equal(Aq[ri].cpu().numpy(), aq_ref) and np.array_equal(sa[ri].cpu().numpy(), sa_ref)
+    bq_ref, sb_ref = oracle.quantize_dynamic_rows(Bt[ci].cpu().numpy())
+    assert np.array_equal(Bq[ci].cpu().numpy(), bq_ref) and np.array_equal(sb[ci].cpu().numpy(), sb_ref)
+    del Bt, A
+    ref = oracle.qdq_gemm(aq_ref, sa_ref, Bq.cpu().numpy(), sb.cpu().numpy())
+    assert_close_bf16(Y[ri].float().cpu().numpy(), ref, what="TP GEMM at the config shape (sampled rows)")
+
+
+def test_same_process_two_devices():
+    """One process drives the CTA-pair GEMM and an implicit-GEMM conv on
+    device 0 and then on device 1: the kernels' shared-memory limits are set
+    per device, so the second device's launches must work and give the same
+    results (skipped with fewer than 2 GPUs)."""
+    import ctypes
+    import torch
+    import luisaml_b200 as lb
+    import oracle
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    from conftest import assert_close
+    from test_conv_gpu import _run_conv
+    rng = np.random.default_rng(12)
+    M, N, K = 512, 512, 1024
+    Aq, sa = oracle.quantize_dynamic_rows(rng.standard_normal((M, K)).astype(np.float32))
+    Bq, sb = oracle.quantize_dynamic_rows((rng.standard_normal((N, K)) * 0.05).astype(np.float32))
+    ref = oracle.qdq_gemm(Aq, sa, Bq, sb)
+    X = rng.standard_normal((2, 64, 14, 14)).astype(np.float32)
+    W = (rng.standard_normal((64, 64, 3, 3)) * 0.05).astype(np.float32)
+    results = []
+    for d in (0, 1):
+        dev = torch.device("cuda", d)
+        with torch.cuda.device(dev):
+            t = lambda a: torch.from_numpy(np.ascontiguousarray(a)).to(dev)  # noqa: E731
+            Y = lb.gemm(t(Aq), t(Bq), t(sa), t(sb), out_dtype=torch.float32, variant=2)  # CTA pair
+            torch.cuda.synchronize(dev)
+            assert_close(Y.cpu().numpy(), ref, what=f"CTA-pair GEMM on device {d}")
+            got, cref, ws = _run_conv(dev, X, W, None, 1, 1)
+            assert ws == 0  # the implicit GEMM (TMA im2col), no workspace
+            assert_close(got, cref, what=f"implicit-GEMM conv on device {d}")
+            results.append((Y.cpu().numpy(), got))
+    np.testing.assert_array_equal(results[0][0], results[1][0])
+    np.testing.assert_array_equal(results[0][1], results[1][1])
