@@ -350,7 +350,8 @@ int lcml_global_avgpool(const void *x, int elem_dtype, const float *x_scale, int
  * encoded (cast.cpp:63-67, from_float(half(x)) with the fp_quantized.h
  * encoders: e4m3 and e2m1 saturate, e5m2 overflows to inf); from FP8 / FP4 it
  * is decoded exactly (cast.cpp:44-48); fp32 / fp16 / bf16 convert with one
- * round-to-nearest-even. Source and destination types must differ. */
+ * round-to-nearest-even. Source and destination types must differ; x and y
+ * must be aligned to their element size (LCML_ERR_INVALID_ARGUMENT otherwise). */
 int lcml_cast(const void *x, int x_dtype, void *y, int y_dtype, int64_t n, lcml_stream_t stream);
 
 #ifdef __cplusplus

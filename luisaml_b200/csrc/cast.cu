@@ -226,6 +226,10 @@ extern "C" int lcml_cast(const void *x, int x_dtype, void *y, int y_dtype, int64
     if (n == 0) return LCML_OK;
     LCML_CHECK_ARG(x && y, "lcml_cast: null pointer");
     LCML_CHECK_ARG(src != dst, "lcml_cast: same source and destination type (a copy)");
+    // element alignment (the kernel's scalar path loads and stores whole elements)
+    auto elem_align = [](int t) -> uintptr_t { return t == kF32 ? 4 : (t == kF16 || t == kBF16) ? 2 : 1; };
+    LCML_CHECK_ARG(aligned(x, elem_align(src)) && aligned(y, elem_align(dst)),
+                   "lcml_cast: x / y not aligned to their element size");
     cudaStream_t st = to_cuda(stream);
     switch (src) {
         case kF32: return dispatch_dst<kF32>(dst, x, y, n, st);

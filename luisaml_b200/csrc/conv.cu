@@ -97,6 +97,7 @@ template <typename I>
 __global__ void __launch_bounds__(kThreads) k_im2col_nhwc16(const uint8_t *__restrict__ X, I N, I C, I H, I W, I kH,
                                                             I kW, I oH, I oW, I sH, I sW, I pH, I pW, I dH, I dW, I Kp,
                                                             uint8_t *__restrict__ A) {
+    griddep_launch_dependents();  // the next GEMM may start its set-up
     const I chunks = Kp / 16, cpt = C / 16, taps_chunks = kH * kW * cpt;
     const I total = N * oH * oW * chunks;
     for (I i = static_cast<I>(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
@@ -121,6 +122,7 @@ template <typename I, int VW>
 __global__ void __launch_bounds__(kThreads) k_im2col_narrow(const uint8_t *__restrict__ X, I N, I H, I W, I kH, I kW,
                                                             I oH, I oW, I sH, I sW, I pH, I pW, I dH, I dW, I Kp,
                                                             uint8_t *__restrict__ A) {
+    griddep_launch_dependents();  // the next GEMM may start its set-up
     using V = typename std::conditional<VW == 4, uint32_t, uint2>::type;
     constexpr int TPC = 16 / VW;  // taps per 16-byte chunk
     const I chunks = Kp / 16, taps = kH * kW;
@@ -159,6 +161,7 @@ __global__ void __launch_bounds__(kRowThreads) k_im2col_rows(const uint8_t *__re
                                                               int kW, int oH, int oW, int sH, int sW, int pH, int pW,
                                                               int dH, int dW, int Kp, int64_t P,
                                                               uint8_t *__restrict__ A) {
+    griddep_launch_dependents();  // the next GEMM may start its set-up
     using V = typename std::conditional<VW == 4, uint32_t, uint2>::type;
     constexpr int TPC = 16 / VW;  // taps per 16-byte vector
     extern __shared__ uint4 tile[];

@@ -150,6 +150,7 @@ template <bool E4M3, bool NHWC>
 __global__ void __launch_bounds__(kThreads) k_maxpool(const void *__restrict__ xv, int64_t NC, int64_t C, int64_t H,
                                                       int64_t W, int kH, int kW, int sH, int sW, int pH, int pW,
                                                       int64_t oH, int64_t oW, void *__restrict__ yv) {
+    griddep_launch_dependents();  // the next GEMM may start its set-up
     const int64_t total = NC * oH * oW;
     const int64_t tid = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
     const int64_t nt = static_cast<int64_t>(gridDim.x) * blockDim.x;
@@ -222,6 +223,7 @@ template <typename I>
 __global__ void __launch_bounds__(kThreads) k_maxpool_e4m3_nhwc16(const uint8_t *__restrict__ x, I N, I C, I H, I W,
                                                                   int kH, int kW, int sH, int sW, int pH, int pW, I oH,
                                                                   I oW, uint8_t *__restrict__ y) {
+    griddep_launch_dependents();  // the next GEMM may start its set-up
     const I groups = C / 16;
     const I total = N * oH * oW * groups;
     for (I o = static_cast<I>(blockIdx.x) * blockDim.x + threadIdx.x; o < total;

@@ -21,6 +21,7 @@
 
 #include <cstring>
 #include <mutex>
+#include <utility>
 
 #include "lcml_device.cuh"
 #include "lcml_internal.h"
@@ -630,6 +631,7 @@ __global__ void __launch_bounds__(sc_threads<EPI, OUT>(), 1)
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem_base = *tmem_slot;
+    griddep_wait();  // operands, scales and residuals may come from the previous kernel
 
     if (IM2COL && warp == 0) {
         // ---------------- TMA im2col producer (implicit-GEMM convolution) ----------------
@@ -791,6 +793,7 @@ __global__ void __launch_bounds__(sc_threads<EPI, OUT>(), 1)
         if (lane == 0) bulk_wait_group_all();  // TMA stores done before the staging memory goes away
     }
 
+    griddep_launch_dependents();
     tc_fence_before();
     __syncthreads();
     if (warp == 1) {
@@ -868,6 +871,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(threads_for<EPI>(), 
     cluster_sync_all();  // barrier inits and TMEM allocation visible to the peer
     tc_fence_after();
     const uint32_t tmem_base = *tmem_slot;
+    griddep_wait();  // operands, scales and residuals may come from the previous kernel
 
     if (warp == 0) {
         // ---------------- TMA producer (both CTAs) ----------------
@@ -984,6 +988,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(threads_for<EPI>(), 
         if (lane == 0) bulk_wait_group_all();  // TMA stores done before the staging memory goes away
     }
 
+    griddep_launch_dependents();
     tc_fence_before();
     cluster_sync_all();  // every MMA consumed, every accumulator read, in both CTAs
     if (warp == 1) {
@@ -1079,6 +1084,7 @@ __global__ void __launch_bounds__(kSplitThreads, 1)
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem_base = *tmem_slot;
+    griddep_wait();  // operands, scales and residuals may come from the previous kernel
 
     if (warp == 0) {
         if (elect_one()) {
@@ -1253,6 +1259,7 @@ __global__ void __launch_bounds__(kSplitThreads, 1)
             if (ep.row_amax) atomic_max_abs(ep.row_amax + row, amax);
         }
     }
+    griddep_launch_dependents();
     cluster_sync_all();  // no CTA exits while another may still read its partial
     if (warp == 1) {
         __syncwarp();
@@ -1296,6 +1303,8 @@ __global__ void __launch_bounds__(kGemvThreads) k_gemv_fp8(const uint8_t *__rest
     for (int r = 0; r < kGemvRows; ++r)
         if (gw * kGemvRows + r < N && lane * 128 < K)
             asm volatile("prefetch.global.L2 [%0];" ::"l"(B + static_cast<int64_t>(gw * kGemvRows + r) * ldb + lane * 128));
+    griddep_wait();  // A, the scales and a residual may come from the previous kernel
+    griddep_launch_dependents();
     for (int i = threadIdx.x; i < MR * (K / 4); i += kGemvThreads) {
         const int m = i / (K / 4), k4 = i - m * (K / 4);
         float v[4] = {0.0f, 0.0f, 0.0f, 0.0f};
@@ -1548,6 +1557,39 @@ int output_tmap(const lcml_fp8_gemm_desc *d, const EpiParams &ep, CUtensorMap *t
     return make_tmap_out(ty, static_cast<uint8_t *>(d->Y) + d->y_col_offset * ES, n_out, d->M, d->ldy * ES, ES);
 }
 
+// Every GEMM kernel is launched with programmatic stream serialization (its
+// set-up overlaps the tail of the previous kernel on the stream; the kernel
+// reads nothing that kernel wrote before griddep_wait), and with a cluster
+// shape when cluster_x > 0 (kernels with compile-time cluster dimensions
+// pass 0).
+template <typename... Params, typename... Args>
+int launch_gemm_kernel(void (*kern)(Params...), unsigned grid, unsigned threads, size_t smem, cudaStream_t st,
+                       unsigned cluster_x, const char *name, Args &&...args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(grid, 1, 1);
+    cfg.blockDim = dim3(threads, 1, 1);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[2];
+    int na = 0;
+    attr[na].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[na].val.programmaticStreamSerializationAllowed = 1;
+    ++na;
+    if (cluster_x > 0) {
+        attr[na].id = cudaLaunchAttributeClusterDimension;
+        attr[na].val.clusterDim.x = cluster_x;
+        attr[na].val.clusterDim.y = 1;
+        attr[na].val.clusterDim.z = 1;
+        ++na;
+    }
+    cfg.attrs = attr;
+    cfg.numAttrs = na;
+    const cudaError_t e = cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...);
+    g_launches.fetch_add(1, std::memory_order_relaxed);
+    if (e != cudaSuccess) return set_error(LCML_ERR_CUDA, "%s launch failed: %s", name, cudaGetErrorString(e));
+    return LCML_OK;
+}
+
 template <int BN, int EPI, int OUT, bool IM2COL = false, int BKB = BK>
 int launch_tc(const lcml_fp8_gemm_desc *d, const EpiParams &ep, cudaStream_t st, const ConvGeom &geo = ConvGeom{}) {
     constexpr int STAGES = stages_for<BN, EPI, OUT, BKB>();
@@ -1565,10 +1607,9 @@ int launch_tc(const lcml_fp8_gemm_desc *d, const EpiParams &ep, cudaStream_t st,
     if (rc) return rc;
     const int64_t tiles = ((d->M + BM - 1) / BM) * ((d->N + BN - 1) / BN);
     const int grid = static_cast<int>(tiles < sm_count() ? tiles : sm_count());
-    kern<<<grid, sc_threads<EPI, OUT>(), L::kSmemBytes, st>>>(
-        ta, tb, ty, static_cast<int>(d->M), static_cast<int>(d->N), static_cast<int>(d->K), ep, geo, device_error_word());
-    LCML_LAUNCHED(IM2COL ? "conv_implicit_gemm_fp8_tc" : "gemm_fp8_tc");
-    return LCML_OK;
+    return launch_gemm_kernel(kern, static_cast<unsigned>(grid), sc_threads<EPI, OUT>(), L::kSmemBytes, st, 0,
+                              IM2COL ? "conv_implicit_gemm_fp8_tc" : "gemm_fp8_tc", ta, tb, ty, static_cast<int>(d->M),
+                              static_cast<int>(d->N), static_cast<int>(d->K), ep, geo, device_error_word());
 }
 
 template <int EPI, int OUT>
@@ -1589,10 +1630,9 @@ int launch_tc2(const lcml_fp8_gemm_desc *d, const EpiParams &ep, cudaStream_t st
     const int64_t tiles = ((d->M + 255) / 256) * ((d->N + 255) / 256);
     const int64_t pairs = sm_count() / 2;
     const int grid = static_cast<int>(2 * (tiles < pairs ? tiles : pairs));
-    kern<<<grid, threads_for<EPI>(), L::kSmemBytes, st>>>(ta, tb, ty, static_cast<int>(d->M), static_cast<int>(d->N),
-                                                          static_cast<int>(d->K), ep, device_error_word());
-    LCML_LAUNCHED("gemm_fp8_tc2");
-    return LCML_OK;
+    return launch_gemm_kernel(kern, static_cast<unsigned>(grid), threads_for<EPI>(), L::kSmemBytes, st, 0,
+                              "gemm_fp8_tc2", ta, tb, ty, static_cast<int>(d->M), static_cast<int>(d->N),
+                              static_cast<int>(d->K), ep, device_error_word());
 }
 
 // Split factor for a GEMM whose 128 x 128 tiles would leave most SMs idle:
@@ -1628,23 +1668,9 @@ int launch_splitk(const lcml_fp8_gemm_desc *d, const EpiParams &ep, cudaStream_t
     rc = make_tmap(&tb, d->B, d->K, d->N, d->ldb, kSplitBN);
     if (rc) return rc;
     const int64_t tiles = ((d->M + BM - 1) / BM) * ((d->N + kSplitBN - 1) / kSplitBN);
-    cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(static_cast<unsigned>(tiles * splits), 1, 1);
-    cfg.blockDim = dim3(kSplitThreads, 1, 1);
-    cfg.dynamicSmemBytes = L::kSmemBytes;
-    cfg.stream = st;
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeClusterDimension;
-    attr[0].val.clusterDim.x = static_cast<unsigned>(splits);
-    attr[0].val.clusterDim.y = 1;
-    attr[0].val.clusterDim.z = 1;
-    cfg.attrs = attr;
-    cfg.numAttrs = 1;
-    const cudaError_t e = cudaLaunchKernelEx(&cfg, kern, ta, tb, static_cast<int>(d->M), static_cast<int>(d->N),
-                                             static_cast<int>(d->K), splits, ep, device_error_word());
-    if (e != cudaSuccess) return set_error(LCML_ERR_CUDA, "gemm_fp8_splitk launch failed: %s", cudaGetErrorString(e));
-    LCML_LAUNCHED("gemm_fp8_splitk");
-    return LCML_OK;
+    return launch_gemm_kernel(kern, static_cast<unsigned>(tiles * splits), kSplitThreads, L::kSmemBytes, st,
+                              static_cast<unsigned>(splits), "gemm_fp8_splitk", ta, tb, static_cast<int>(d->M),
+                              static_cast<int>(d->N), static_cast<int>(d->K), splits, ep, device_error_word());
 }
 
 // Rows of A held per GEMV instantiation for an M <= kGemvMaxM GEMM (0: not a GEMV shape).
@@ -1661,10 +1687,9 @@ int launch_gemv(const lcml_fp8_gemm_desc *d, const EpiParams &ep, cudaStream_t s
     const int64_t cap = 4LL * sm_count();
     const int grid = static_cast<int>(want < cap ? want : cap);
     const size_t smem = static_cast<size_t>(MR) * static_cast<size_t>(d->K) * 4;
-    k_gemv_fp8<MR, EPI, OUT><<<grid, kGemvThreads, smem, st>>>(d->A, d->lda, d->B, d->ldb, static_cast<int>(d->M),
-                                                             static_cast<int>(d->N), static_cast<int>(d->K), ep);
-    LCML_LAUNCHED("gemv_fp8");
-    return LCML_OK;
+    return launch_gemm_kernel(k_gemv_fp8<MR, EPI, OUT>, static_cast<unsigned>(grid), kGemvThreads, smem, st, 0,
+                              "gemv_fp8", d->A, d->lda, d->B, d->ldb, static_cast<int>(d->M), static_cast<int>(d->N),
+                              static_cast<int>(d->K), ep);
 }
 
 template <int EPI, int OUT>

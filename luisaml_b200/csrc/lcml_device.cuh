@@ -299,6 +299,23 @@ __device__ __forceinline__ uint32_t abs_bits_nan0(float x) {
 }
 
 // ---------------------------------------------------------------------------
+// Programmatic dependent launch. The GEMM kernels are launched with
+// programmatic stream serialization: their CTAs may be scheduled while the
+// previous kernel on the stream is still running, run their set-up (barrier
+// init, TMEM allocation, tensor-map prefetch) and then block in
+// griddep_wait() until that kernel has completed and its memory writes are
+// visible; nothing written by an earlier kernel is read before the wait.
+// Producer kernels call griddep_launch_dependents() to let that happen as
+// early as they like (without the call the dependent starts when the
+// producer's last CTA exits). Both are no-ops for a kernel launched without
+// the attribute.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void griddep_launch_dependents() {
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
+// ---------------------------------------------------------------------------
 // Shared memory / mbarrier helpers
 // ---------------------------------------------------------------------------
 __device__ __forceinline__ uint32_t smem_u32(const void *p) {

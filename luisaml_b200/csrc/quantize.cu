@@ -58,6 +58,7 @@ template <int KIND, bool FROM_AMAX>
 __global__ void __launch_bounds__(kThreads) k_quantize(const float *__restrict__ x, int64_t n, int64_t axis_len,
                                                        int64_t inner, const float *__restrict__ sc,
                                                        float *__restrict__ scale_out, uint8_t *__restrict__ y) {
+    griddep_launch_dependents();  // the next GEMM may start its set-up
     const int64_t tid = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
     const int64_t nthreads = static_cast<int64_t>(gridDim.x) * blockDim.x;
     const int64_t n16 = n >> 4;
@@ -120,6 +121,7 @@ __global__ void __launch_bounds__(kThreads) k_quantize_scalar(const float *__res
                                                               const float *__restrict__ sc, int per_axis,
                                                               float *__restrict__ scale_out,
                                                               uint8_t *__restrict__ y) {
+    griddep_launch_dependents();  // the next GEMM may start its set-up
     const int64_t tid = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
     const int64_t nthreads = static_cast<int64_t>(gridDim.x) * blockDim.x;
     for (int64_t i = tid; i < n; i += nthreads) {
@@ -179,6 +181,7 @@ template <int VPT>
 __global__ void __launch_bounds__(kThreads) k_quantize_rows_dynamic(const float *__restrict__ x, int64_t cols,
                                                                     int64_t ldx, float *__restrict__ scale_out,
                                                                     uint8_t *__restrict__ y) {
+    griddep_launch_dependents();  // the next GEMM may start its set-up
     __shared__ uint32_t red[32];
     const int64_t r = blockIdx.x;
     const float4 *xr = reinterpret_cast<const float4 *>(x + r * ldx);
@@ -217,6 +220,7 @@ __global__ void __launch_bounds__(kThreads) k_quantize_rows_dynamic_generic(cons
                                                                             int64_t cols, int64_t ldx,
                                                                             float *__restrict__ scale_out,
                                                                             uint8_t *__restrict__ y) {
+    griddep_launch_dependents();  // the next GEMM may start its set-up
     __shared__ uint32_t red[32];
     const int64_t r = blockIdx.x;
     const float *xr = x + r * ldx;
@@ -282,6 +286,7 @@ __global__ void __launch_bounds__(kThreads) k_dequantize(const uint8_t *__restri
 // ---------------------------------------------------------------------------
 __global__ void __launch_bounds__(256) k_transpose_u8(const uint8_t *__restrict__ src, int64_t rows, int64_t cols,
                                                       uint8_t *__restrict__ dst) {
+    griddep_launch_dependents();  // the next GEMM may start its set-up
     __shared__ uint8_t tile[64][65];
     const int64_t r0 = static_cast<int64_t>(blockIdx.y) * 64, c0 = static_cast<int64_t>(blockIdx.x) * 64;
     for (int i = threadIdx.x; i < 64 * 64; i += 256) {

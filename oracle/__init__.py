@@ -198,8 +198,10 @@ def dequantize(q, scale, axis: int | None = None) -> np.ndarray:
 
 
 # --------------------------------------------------------------------------- Gemm / Conv
-def gemm(A, B, C=None, alpha=1.0, beta=1.0, transA=0, transB=0, rows=None) -> np.ndarray:
-    """ONNX Gemm in fp32 with the reference's K-ordered fma accumulation."""
+def gemm(A, B, C=None, alpha=1.0, beta=1.0, transA=0, transB=0, rows=None, lanes=1) -> np.ndarray:
+    """ONNX Gemm in fp32 with the reference's fma accumulation: K-ordered
+    (lanes=1, gemm.cpp:153-157), or the four-lane order of its vector path
+    for byte-buffer operands (lanes=4, gemm.cpp:123-152)."""
     A = np.ascontiguousarray(A, dtype=np.float32)
     B = np.ascontiguousarray(B, dtype=np.float32)
     M = A.shape[1] if transA else A.shape[0]
@@ -215,9 +217,10 @@ def gemm(A, B, C=None, alpha=1.0, beta=1.0, transA=0, transB=0, rows=None) -> np
         d0 = C.shape[0] if C.ndim >= 1 else 0
         d1 = C.shape[1] if C.ndim >= 2 else 0
         cptr = _f(C)
-    lib.orc_gemm_f32_rows(_f(A), _f(B), cptr, _i64(M), _i64(N), _i64(K), ctypes.c_int(transA),
-                          ctypes.c_int(transB), ctypes.c_float(alpha), ctypes.c_float(beta),
-                          ctypes.c_int(cnd), _i64(d0), _i64(d1), _f(Y), _i64(r0), _i64(r1))
+    lib.orc_gemm_f32_rows_lanes(_f(A), _f(B), cptr, _i64(M), _i64(N), _i64(K), ctypes.c_int(transA),
+                                ctypes.c_int(transB), ctypes.c_float(alpha), ctypes.c_float(beta),
+                                ctypes.c_int(cnd), _i64(d0), _i64(d1), _f(Y), _i64(r0), _i64(r1),
+                                ctypes.c_int(lanes))
     return Y
 
 

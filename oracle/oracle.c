@@ -323,16 +323,33 @@ ORC_EXPORT void orc_dequantize_axis(const uint8_t *q, int64_t outer, int64_t axi
  * c_ndim < 0 means no C. Rows [row0, row1) only (row1 <= M) so callers can
  * time a bounded sample of a large problem.
  */
-ORC_EXPORT void orc_gemm_f32_rows(const float *A, const float *B, const float *C,
-                                  int64_t M, int64_t N, int64_t K, int transA, int transB,
-                                  float alpha, float beta, int c_ndim, int64_t c_d0, int64_t c_d1,
-                                  float *Y, int64_t row0, int64_t row1) {
-    (void)M;
+/*
+ * lanes == 4 restates the reference's vector path for byte-buffer operands
+ * with unit stride along K (gemm.cpp:123-152): four lane accumulators, lane
+ * l taking k = 4j + l with fma in j order, summed as ((x + y) + z) + w and
+ * added to the running sum (starting at 0), then the K % 4 tail with fma in
+ * order. lanes == 1 is the scalar loop (gemm.cpp:153-157).
+ */
+ORC_EXPORT void orc_gemm_f32_rows_lanes(const float *A, const float *B, const float *C,
+                                        int64_t M, int64_t N, int64_t K, int transA, int transB,
+                                        float alpha, float beta, int c_ndim, int64_t c_d0, int64_t c_d1,
+                                        float *Y, int64_t row0, int64_t row1, int lanes) {
 #pragma omp parallel for schedule(dynamic, 1)
     for (int64_t m = row0; m < row1; ++m) {
         for (int64_t n = 0; n < N; ++n) {
             float sum = 0.0f;
-            for (int64_t k = 0; k < K; ++k) {
+            int64_t k0 = 0;
+            if (lanes == 4) {
+                float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+                for (int64_t j = 0; j < K / 4; ++j)
+                    for (int l = 0; l < 4; ++l) {
+                        const int64_t k = 4 * j + l;
+                        acc[l] = fmaf(transA ? A[k * M + m] : A[m * K + k], transB ? B[n * K + k] : B[k * N + n], acc[l]);
+                    }
+                sum += ((acc[0] + acc[1]) + acc[2]) + acc[3];
+                k0 = (K / 4) * 4;
+            }
+            for (int64_t k = k0; k < K; ++k) {
                 float a = transA ? A[k * M + m] : A[m * K + k];
                 float b = transB ? B[n * K + k] : B[k * N + n];
                 sum = fmaf(a, b, sum);
@@ -353,6 +370,13 @@ ORC_EXPORT void orc_gemm_f32_rows(const float *A, const float *B, const float *C
             Y[(m - row0) * N + n] = sum;
         }
     }
+}
+
+ORC_EXPORT void orc_gemm_f32_rows(const float *A, const float *B, const float *C,
+                                  int64_t M, int64_t N, int64_t K, int transA, int transB,
+                                  float alpha, float beta, int c_ndim, int64_t c_d0, int64_t c_d1,
+                                  float *Y, int64_t row0, int64_t row1) {
+    orc_gemm_f32_rows_lanes(A, B, C, M, N, K, transA, transB, alpha, beta, c_ndim, c_d0, c_d1, Y, row0, row1, 1);
 }
 
 /*

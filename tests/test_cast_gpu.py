@@ -26,26 +26,35 @@ def _nbytes(t, n):
     return (n + 1) // 2 if t == E2M1 else n * np.dtype(STORAGE[t]).itemsize
 
 
+def _esize(t):
+    """Bytes of one element's storage unit (a packed FP4 byte for E2M1)."""
+    return 1 if t == E2M1 else np.dtype(STORAGE[t]).itemsize
+
+
 def _gpu_cast(dev, x_bytes, src, dst, n, offset=0):
-    """Runs lcml_cast on n elements of the raw storage x_bytes placed `offset`
-    bytes into a device buffer (offset breaks the vector alignment)."""
+    """Runs lcml_cast on n elements of the raw storage x_bytes; x and y start
+    `offset` elements (bytes for packed FP4) into their device buffers, which
+    keeps each pointer aligned to its element but breaks the kernel's vector
+    alignment for offset > 0."""
     import torch
     import luisaml_b200 as lb
-    xin = torch.zeros(len(x_bytes) + offset + 64, dtype=torch.uint8, device=dev)
-    xin[offset:offset + len(x_bytes)] = torch.from_numpy(np.frombuffer(x_bytes, dtype=np.uint8).copy()).to(dev)
+    xo, yo = offset * _esize(src), offset * _esize(dst)
+    xin = torch.zeros(len(x_bytes) + xo + 64, dtype=torch.uint8, device=dev)
+    xin[xo:xo + len(x_bytes)] = torch.from_numpy(np.frombuffer(x_bytes, dtype=np.uint8).copy()).to(dev)
     nb = _nbytes(dst, n)
-    yout = torch.full((nb + offset + 64,), 0xA5, dtype=torch.uint8, device=dev)
-    lb.check(lb.lib().lcml_cast(ctypes.c_void_p(xin.data_ptr() + offset), src, ctypes.c_void_p(yout.data_ptr() + offset),
+    yout = torch.full((nb + yo + 64,), 0xA5, dtype=torch.uint8, device=dev)
+    lb.check(lb.lib().lcml_cast(ctypes.c_void_p(xin.data_ptr() + xo), src, ctypes.c_void_p(yout.data_ptr() + yo),
                                 dst, n, ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)))
     torch.cuda.synchronize()
     out = yout.cpu().numpy()
-    assert (out[:offset] == 0xA5).all() and (out[offset + nb:] == 0xA5).all(), "cast wrote outside its output"
-    return out[offset:offset + nb].tobytes()
+    assert (out[:yo] == 0xA5).all() and (out[yo + nb:] == 0xA5).all(), "cast wrote outside its output"
+    return out[yo:yo + nb].tobytes()
 
 
 def _values(t, raw, n):
     """Decoded float64 values of raw storage of type t (for NaN-aware compares)."""
-    return oracle.cast(np.frombuffer(raw, dtype=np.uint8), t, F32, n).astype(np.float64)
+    with np.errstate(invalid="ignore"):  # signalling-NaN bit patterns widen to quiet NaNs
+        return oracle.cast(np.frombuffer(raw, dtype=np.uint8), t, F32, n).astype(np.float64)
 
 
 def _assert_same(got, want, dst, n, what):
@@ -108,10 +117,19 @@ def test_cast_ragged_and_misaligned(dev, n, offset):
 
 
 def test_cast_rejects_unsupported(dev):
+    """Unsupported types, a same-type "cast" and pointers not aligned to their
+    element are refused on the host (nothing is launched)."""
+    import torch
     import luisaml_b200 as lb
     lib = lb.lib()
     assert lib.lcml_cast(None, F32, None, 6, 4, None) == 2  # INT32 destination
     assert lib.lcml_cast(None, F32, None, F32, 4, None) == 1  # same type: a copy, not a cast
+    buf = torch.zeros(256, dtype=torch.uint8, device=dev)
+    p = buf.data_ptr()
+    before = lb.launch_count()
+    assert lib.lcml_cast(ctypes.c_void_p(p + 1), F32, ctypes.c_void_p(p + 128), E4M3, 8, None) == 1
+    assert lib.lcml_cast(ctypes.c_void_p(p), E4M3, ctypes.c_void_p(p + 129), BF16, 8, None) == 1
+    assert lb.launch_count() == before
 
 
 def test_cast_graph_through_executor(dev):
@@ -143,4 +161,4 @@ def test_cast_graph_through_executor(dev):
     want8 = oracle.cast(oracle.cast(x, F32, E4M3), E4M3, F32, x.size).reshape(x.shape)
     want5 = oracle.cast(oracle.cast(x, F32, E5M2), E5M2, F16, x.size).reshape(x.shape)
     np.testing.assert_array_equal(y8.cpu().numpy(), want8)
-    np.testing.assert_array_equal(y5.cpu().numpy().view(np.uint16), want5)
+    np.testing.assert_array_equal(y5.cpu().numpy().view(np.uint16), want5.view(np.uint16))

@@ -171,3 +171,35 @@ def test_cast_restatement():
     assert np.array_equal(oracle.cast(codes8, 17, 1), oracle.e4m3_decode(codes8), equal_nan=True)
     # FP4 odd length: the last byte's high nibble stays zero
     assert oracle.cast(np.float32([1.0, 2.0, 3.0]), 1, 23).tolist() == [0x2 | (0x4 << 4), 0x5]
+
+
+def test_mlp_fixture_both_reference_summation_orders():
+    """The reference's fp32 MLP fixture (tests/onnx/output/) through the
+    oracle with both of the reference Gemm's summation orders: the scalar
+    K-ordered fma chain (gemm.cpp:153-157) and the four-lane order of its
+    vector path for byte-buffer operands (gemm.cpp:123-152). Both reproduce
+    output_ref.bin within the reference test's tolerance (abs 1e-3,
+    test_onnx_inference.cpp:232); they differ from each other only in fp32
+    rounding."""
+    import json
+    import os
+    from conftest import GOLDEN
+    d = os.path.join(GOLDEN, "simple_mlp")
+    blob = np.fromfile(os.path.join(d, "simple_mlp.safetensors"), dtype=np.uint8)
+    x = np.fromfile(os.path.join(d, "input_ref.bin"), dtype=np.float32).reshape(1, 784)
+    ref = np.fromfile(os.path.join(d, "output_ref.bin"), dtype=np.float32).reshape(1, 10)
+    inits = {i["name"]: i for i in json.load(open(os.path.join(d, "simple_mlp.onnx.json")))["graph"]["initializer"]}
+    W = {k: np.frombuffer(blob[v["data_offsets"][0]:v["data_offsets"][1]].tobytes(), dtype=np.float32).reshape(
+        [int(s) for s in v["dims"]]) for k, v in inits.items()}
+    outs = []
+    for lanes in (1, 4):
+        h = oracle.relu(oracle.gemm(x, W["net.0.weight"], W["net.0.bias"], transB=1, lanes=lanes))
+        h = oracle.relu(oracle.gemm(h, W["net.2.weight"], W["net.2.bias"], transB=1, lanes=lanes))
+        h = oracle.gemm(h, W["net.4.weight"], W["net.4.bias"], transB=1, lanes=lanes)
+        assert np.abs(h - ref).max() <= 1e-3
+        outs.append(h)
+    np.testing.assert_allclose(outs[0], outs[1], rtol=1e-5, atol=1e-6)
+    # and the four-lane order is a different order: it is not the scalar chain everywhere
+    rng = np.random.default_rng(0)
+    A, B = rng.standard_normal((16, 301)).astype(np.float32), rng.standard_normal((16, 301)).astype(np.float32)
+    assert not np.array_equal(oracle.gemm(A, B, transB=1, lanes=1), oracle.gemm(A, B, transB=1, lanes=4))
