@@ -225,7 +225,7 @@ class GemmWorkload:
         self.flops = 2.0 * self.M * self.N * self.K / self.ws  # per rank
         self.Aq = torch.empty(self.M, self.K, dtype=torch.uint8, device=dev)
         self.sa = torch.empty(1, dtype=torch.float32, device=dev)
-        self.amax_ws = torch.empty(1, dtype=torch.float32, device=dev)
+        self.amax_ws = torch.empty(lb.TENSOR_DYNAMIC_WORKSPACE_BYTES // 4, dtype=torch.float32, device=dev)
         self.peers = None
         if self.ws > 1:
             import torch.distributed as dist

@@ -137,9 +137,14 @@ int lcml_fp8_quantize_rows_dynamic(const float *x, int64_t rows, int64_t cols, i
 /* max |x| over n fp32 values (NaN ignored) into *amax_out (device). */
 int lcml_amax(const float *x, int64_t n, float *amax_out, lcml_stream_t stream);
 
-/* Dynamic per-tensor quantization: s = max|x| / 448, y = e4m3(x / s).
- * workspace: caller-owned device scratch of at least 4 bytes (the running
- * amax). scale_out (device, 1 float) receives s. */
+/* Dynamic per-tensor quantization: s = max|x| / 448 (1 for an all-zero
+ * tensor; NaN ignored), y = e4m3(x / s). workspace: caller-owned device
+ * scratch of at least LCML_FP8_TENSOR_DYNAMIC_WORKSPACE_BYTES (per-block
+ * partial maxima; its contents on entry do not matter). scale_out (device,
+ * 1 float) receives s. Two kernels: the partial maxima front to back, then
+ * the reduction and the quantization back to front, so the part of x still in
+ * the L2 is read first. */
+#define LCML_FP8_TENSOR_DYNAMIC_WORKSPACE_BYTES 4096
 int lcml_fp8_quantize_tensor_dynamic(const float *x, int64_t n, float *scale_out, uint8_t *y, float *workspace,
                                      lcml_stream_t stream);
 
@@ -283,7 +288,11 @@ int lcml_gemm_f32_relu(const float *A, const float *B, const float *C, int64_t M
  * channel scales. Y: NHWC [N, oH, oW, M] (the GEMM's row-major output),
  * fp32 / bf16 / e4m3 (with y_scale). residual: same layout as Y, fp32 or e4m3
  * (with residual_scale), added before the activation. Pads are the begin
- * pads (conv.cpp:119-121); group must be 1.
+ * pads (conv.cpp:119-121). group > 1 (grouped and depthwise convs, conv.cpp:
+ * 62-63, :122-139: input channels [g*C/group, (g+1)*C/group) feed output
+ * channels [g*M/group, (g+1)*M/group)) runs a direct kernel on the CUDA cores
+ * (little reuse per output: memory-bound), with weights packed for C/group
+ * channels and the same epilogue; it needs no workspace.
  */
 typedef struct lcml_fp8_conv_desc {
     int64_t N, C, H, W;     /* input */
@@ -320,6 +329,18 @@ int64_t lcml_fp8_conv_workspace_size(const lcml_fp8_conv_desc *desc);
 int lcml_fp8_conv_pack_weight(const uint8_t *W, int64_t M, int64_t Cg, int64_t kH, int64_t kW, uint8_t *Wp,
                               lcml_stream_t stream);
 int lcml_fp8_conv(const lcml_fp8_conv_desc *desc, lcml_stream_t stream);
+
+/*
+ * fp32 Conv (src/onnx/operators/conv.cpp:115-207) for graphs without QDQ:
+ * X NCHW [N, C, H, W], W [M, C/group, kH, kW], optional bias B [M], begin
+ * pads, strides, dilations, group; Y NCHW [N, M, oH, oW]. The sum order is the
+ * reference's: taps in (kh, kw) order, within a tap four lane sums over the
+ * group's channels (fma) added as ((x + y) + z) + w, the remaining C/group % 4
+ * channels by fma, then + bias. A 1-D conv is H = kH = oH = 1.
+ */
+int lcml_conv2d_f32(const float *X, const float *W, const float *B, int64_t N, int64_t C, int64_t H, int64_t Wd,
+                    int64_t M, int64_t kH, int64_t kW, int64_t oH, int64_t oW, int sH, int sW, int pH, int pW, int dH,
+                    int dW, int group, float *Y, lcml_stream_t stream);
 
 /*
  * Memory-bound operators around the GEMMs (fp32 unless stated).

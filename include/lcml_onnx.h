@@ -369,6 +369,20 @@ public:
         fusion_enabled_ = e;
         reset();
     }
+    // Intermediate tensors share one device arena by lifetime (on by default,
+    // the role of build_last_use_map + the pooled allocation in the reference,
+    // network_instance.cpp:369-582): a tensor's bytes are reused once its last
+    // reader has run. Off: every intermediate has its own allocation, so all of
+    // them stay readable after forward() (for inspection and tests).
+    void enable_memory_reuse(bool e) {
+        reuse_memory_ = e;
+        reset();
+    }
+    // After prepare: bytes of the intermediate arena (or of the separate
+    // intermediate allocations when reuse is off), and the bytes the
+    // intermediates would take without reuse.
+    size_t intermediate_bytes() const { return intermediate_bytes_; }
+    size_t intermediate_bytes_unplanned() const { return intermediate_unplanned_; }
 
     const Model &get_model() const { return model_; }
     TensorTable &tensor_table() { return table_; }
@@ -392,6 +406,7 @@ private:
     void create_tensors();
     void run_fusion_pass();
     void fold_constants();
+    void allocate_intermediates();
 
     Model model_;
     std::map<std::string, ITensor *, std::less<>> inputs_, outputs_;
@@ -399,7 +414,8 @@ private:
     size_t weight_bytes_ = 0;
     lcml_stream_t stream_ = nullptr;
     uint32_t warp_size_ = 32;
-    bool coop_vec_ = false, logging_ = false, fusion_enabled_ = true;
+    bool coop_vec_ = false, logging_ = false, fusion_enabled_ = true, reuse_memory_ = true;
+    size_t intermediate_bytes_ = 0, intermediate_unplanned_ = 0;
     bool prepared_ = false;
     TensorTable table_;
     std::vector<std::unique_ptr<Operator>> ops_;

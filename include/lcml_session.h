@@ -48,6 +48,15 @@ int lcml_network_set_output_host(lcml_network *net, const char *name, void *host
 /* 1 (default): QDQ node groups run as fused kernels; 0: one kernel per node. */
 int lcml_network_set_fusion(lcml_network *net, int enable);
 int lcml_network_set_stream(lcml_network *net, lcml_stream_t stream);
+/* 1 (default): intermediates share one device arena by lifetime (the last-use
+ * analysis and pooled allocation of network_instance.cpp:369-582), so an
+ * intermediate's bytes are reused once its last reader has run; 0: one
+ * allocation per intermediate, all readable after forward (inspection). */
+int lcml_network_set_memory_reuse(lcml_network *net, int enable);
+/* After the first forward: device bytes of the intermediates as allocated
+ * (the arena, or the sum of the separate allocations), and the bytes they
+ * would take with one allocation each. */
+int lcml_network_memory(const lcml_network *net, size_t *intermediate_bytes, size_t *unplanned_bytes);
 /* Enqueues the whole graph on the stream (prepares on the first call). */
 int lcml_network_forward(lcml_network *net);
 /* After forward: nodes that launched work, and a one-line-per-node summary. */
@@ -57,8 +66,10 @@ int lcml_network_summary(const lcml_network *net, char *buf, size_t len);
  * outputs, intermediates, constants), like NetworkInstance::get_tensor_table()
  * (include/onnx/network_instance.h:231). shape receives up to max_ndim
  * extents of the ONNX shape; *nhwc is 1 when the tensor is stored NHWC (the
- * outputs of fused convolutions and pools), else 0. Intermediates are
- * separate allocations, so their contents stay valid until the next forward. */
+ * outputs of fused convolutions and pools), else 0. With memory reuse off
+ * (lcml_network_set_memory_reuse) every intermediate keeps its contents until
+ * the next forward; with it on, an intermediate's bytes may hold a later
+ * tensor once its last reader has run. */
 int lcml_network_tensor(const lcml_network *net, const char *name, void **device_ptr, int *dtype, int64_t *shape,
                         int max_ndim, int *ndim, int *nhwc);
 /* Number of operators registered in the default opset. */

@@ -15,7 +15,7 @@ from __future__ import annotations
 import ctypes
 
 from . import _capi
-from ._capi import (DTYPE_BFLOAT16, DTYPE_E4M3, DTYPE_FLOAT, EPI_NONE, EPI_RELU, EPI_SILU_MUL, SCALE_AXIS,
+from ._capi import (TENSOR_DYNAMIC_WORKSPACE_BYTES, DTYPE_BFLOAT16, DTYPE_E4M3, DTYPE_FLOAT, EPI_NONE, EPI_RELU, EPI_SILU_MUL, SCALE_AXIS,
                     SCALE_COL, SCALE_ROW, SCALE_TENSOR, GemmDesc, LcmlError, check)
 
 __all__ = ["lib", "check", "LcmlError", "quantize", "quantize_from_amax", "quantize_rows_dynamic",
@@ -117,7 +117,8 @@ def amax(x, out=None):
 
 def quantize_tensor_dynamic(x, workspace=None, out=None, scale_out=None):
     torch = _torch()
-    ws = workspace if workspace is not None else torch.empty(1, dtype=torch.float32, device=x.device)
+    ws = workspace if workspace is not None else torch.empty(TENSOR_DYNAMIC_WORKSPACE_BYTES // 4, dtype=torch.float32,
+                                                             device=x.device)
     y = out if out is not None else torch.empty(x.shape, dtype=torch.uint8, device=x.device)
     s = scale_out if scale_out is not None else torch.empty(1, dtype=torch.float32, device=x.device)
     check(lib().lcml_fp8_quantize_tensor_dynamic(_p(x), x.numel(), _p(s), _p(y), _p(ws), _stream()))

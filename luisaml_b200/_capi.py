@@ -26,6 +26,9 @@ SCALE_AXIS = 1
 SCALE_ROW = 1
 SCALE_COL = 2
 
+# LCML_FP8_TENSOR_DYNAMIC_WORKSPACE_BYTES: scratch of lcml_fp8_quantize_tensor_dynamic
+TENSOR_DYNAMIC_WORKSPACE_BYTES = 4096
+
 EPI_NONE = 0
 EPI_RELU = 1
 EPI_SILU_MUL = 2
@@ -121,6 +124,8 @@ PROTOTYPES = {
     "lcml_fp8_conv_packed_k": [_c_i64, _c_i64, _c_i64],
     "lcml_fp8_conv_pack_weight": [_vp, _c_i64, _c_i64, _c_i64, _c_i64, _vp, _vp],
     "lcml_fp8_conv": [ctypes.POINTER(ConvDesc), _vp],
+    "lcml_conv2d_f32": [_vp, _vp, _vp, _c_i64, _c_i64, _c_i64, _c_i64, _c_i64, _c_i64, _c_i64, _c_i64, _c_i64, _ci,
+                        _ci, _ci, _ci, _ci, _ci, _ci, _vp, _vp],
     "lcml_unary_f32": [_ci, _vp, _vp, _c_i64, _vp],
     "lcml_binary_f32": [_ci, _vp, _vp, _c_i64, _c_i64, _vp, _vp],
     "lcml_reduce_max_rows": [_vp, _c_i64, _c_i64, _ci, _vp, _vp],

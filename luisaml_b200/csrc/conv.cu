@@ -224,6 +224,7 @@ int64_t lcml_fp8_conv_packed_k(int64_t Cg, int64_t kH, int64_t kW) { return pack
 
 int64_t lcml_fp8_conv_workspace_size(const lcml_fp8_conv_desc *d) {
     if (!d) return -1;
+    if (d->group > 1) return 0;  // the grouped direct kernel reads X and the packed weights as they are
     if (direct_path(d) || (implicit_ok(d) && !(d->variant & 1))) return 0;
     return d->N * d->oH * d->oW * packed_k(d->C / (d->group > 0 ? d->group : 1), d->kH, d->kW) + repack_bytes(d);
 }
@@ -290,7 +291,9 @@ int lcml_fp8_conv(const lcml_fp8_conv_desc *d, lcml_stream_t stream) {
     LCML_CHECK_ARG(d->N > 0 && d->C > 0 && d->H > 0 && d->W > 0 && d->M > 0 && d->kH > 0 && d->kW > 0 && d->oH > 0 &&
                        d->oW > 0 && d->sH > 0 && d->sW > 0 && d->dH > 0 && d->dW > 0 && d->pH >= 0 && d->pW >= 0,
                    "lcml_fp8_conv: bad geometry");
-    if (d->group != 1) return set_error(LCML_ERR_UNSUPPORTED, "lcml_fp8_conv: group %d (only 1 is built)", d->group);
+    LCML_CHECK_ARG(d->group >= 1 && d->C % d->group == 0 && d->M % d->group == 0,
+                   "lcml_fp8_conv: group %d must divide C = %lld and M = %lld", d->group, (long long)d->C,
+                   (long long)d->M);
     LCML_CHECK_ARG((d->oH - 1) * d->sH + (d->kH - 1) * d->dH - d->pH < d->H + d->pH + d->kH &&
                        (d->oW - 1) * d->sW + (d->kW - 1) * d->dW - d->pW < d->W + d->pW + d->kW,
                    "lcml_fp8_conv: output extent inconsistent with the input");
@@ -300,10 +303,17 @@ int lcml_fp8_conv(const lcml_fp8_conv_desc *d, lcml_stream_t stream) {
     LCML_CHECK_ARG(!d->residual || d->residual_dtype == LCML_DTYPE_FLOAT ||
                        (d->residual_dtype == LCML_DTYPE_FLOAT8E4M3FN && d->residual_scale),
                    "lcml_fp8_conv: residual must be FLOAT or FLOAT8E4M3FN with residual_scale");
+    cudaStream_t st = to_cuda(stream);
+    if (d->group > 1) {  // grouped / depthwise: memory-bound direct kernel on the CUDA cores
+        LCML_CHECK_ARG(d->y_dtype == LCML_DTYPE_FLOAT || d->y_dtype == LCML_DTYPE_BFLOAT16 ||
+                           (d->y_dtype == LCML_DTYPE_FLOAT8E4M3FN && d->y_scale),
+                       "lcml_fp8_conv: y_dtype %d (FLOAT, BFLOAT16 or FLOAT8E4M3FN with y_scale)", d->y_dtype);
+        const int64_t cg = d->C / d->group;
+        return fp8_conv_grouped(d, packed_k(cg, d->kH, d->kW), packed_c(cg), st);
+    }
     const int64_t P = d->N * d->oH * d->oW;
     const int64_t Cp = packed_c(d->C);
     const int64_t Kp = packed_k(d->C, d->kH, d->kW);
-    cudaStream_t st = to_cuda(stream);
     const uint8_t *A = d->X;
     int64_t K = d->C;
     // Implicit GEMM where the geometry allows it (no im2col pass, no

@@ -218,9 +218,12 @@ __device__ __forceinline__ void load_cmat32(const EpiParams &ep, int64_t row, in
 constexpr int out_es(int out) { return out == kOutF32 ? 4 : (out == kOutBF16 ? 2 : 1); }
 
 // 32 values -> the output's bytes as 8 * element-size little-endian words
-// (e4m3 by the epilogue quantization rule of quantize_block_rcp).
-template <int OUT, bool NONNEG = false>
+// (e4m3 by the epilogue quantization rule of quantize_block_rcp). RELU: the
+// values have not been through Relu yet (e4m3 output only: Relu is folded
+// into the conversion); NONNEG: they have.
+template <int OUT, bool NONNEG = false, bool RELU = false>
 __device__ __forceinline__ void pack32(const float (&v)[32], const OutQuant &q, uint32_t (&w)[8 * out_es(OUT)]) {
+    static_assert(!RELU || OUT == kOutE4M3, "Relu is folded into the conversion for e4m3 outputs only");
     if (OUT == kOutF32) {
 #pragma unroll
         for (int j = 0; j < 32; ++j) w[j] = __float_as_uint(v[j]);
@@ -231,12 +234,13 @@ __device__ __forceinline__ void pack32(const float (&v)[32], const OutQuant &q, 
             w[j] = *reinterpret_cast<uint32_t *>(&h);
         }
     } else if (q.s_ok) {
-        quantize_block_rcp<32, NONNEG>(v, q.r, w);
+        quantize_block_rcp<32, NONNEG, RELU>(v, q.r, w);
     } else {
+        auto rl = [](float x) { return RELU ? fmaxf(x, 0.0f) : x; };
 #pragma unroll
         for (int j = 0; j < 8; ++j)
-            w[j] = quantize1(v[4 * j], q.ys) | (quantize1(v[4 * j + 1], q.ys) << 8) |
-                   (quantize1(v[4 * j + 2], q.ys) << 16) | (quantize1(v[4 * j + 3], q.ys) << 24);
+            w[j] = quantize1(rl(v[4 * j]), q.ys) | (quantize1(rl(v[4 * j + 1]), q.ys) << 8) |
+                   (quantize1(rl(v[4 * j + 2]), q.ys) << 16) | (quantize1(rl(v[4 * j + 3]), q.ys) << 24);
     }
 }
 
@@ -360,12 +364,14 @@ __device__ __forceinline__ void store_chunk_tma(const CUtensorMap *tmY, uint8_t 
 // 16-byte aligned (the common conv case); `ok` says the bytes are valid.
 struct ResidualRaw {
     uint4 w[2];
+    float scale;  // beta * the residual's DequantizeLinear scale
     bool ok;
 };
 
 __device__ __forceinline__ void prefetch_residual(const EpiParams &ep, int64_t row, bool row_ok, int64_t col0,
-                                                  int64_t n_out, ResidualRaw &rr) {
+                                                  int64_t n_out, float scale, ResidualRaw &rr) {
     rr.ok = false;
+    rr.scale = scale;
     if (!ep.c_mat || ep.c_mat_kind != 2 || !row_ok || col0 + 32 > n_out) return;
     const uint8_t *cp = reinterpret_cast<const uint8_t *>(ep.c_mat) + row * ep.ldc + col0;
     if (!aligned(cp, 16)) return;
@@ -380,7 +386,9 @@ __device__ __forceinline__ void prefetch_residual(const EpiParams &ep, int64_t r
 // their column factors, rr the prefetched residual (else it is loaded here).
 // Parameter-dependent branches are per chunk; the element loops are
 // branch-free.
-template <int EPI, bool VEC>
+// RELU_LATER: Relu is left to the output conversion (pack32<..., RELU>), so
+// the values come back before Relu (the row |max| still takes Relu into account).
+template <int EPI, bool VEC, bool RELU_LATER = false>
 __device__ __forceinline__ void epi_values(const EpiParams &ep, int64_t row, bool row_ok, int64_t col0, int64_t nu0,
                                            int64_t n_out, const uint32_t (&g)[32], const uint32_t (&u)[32],
                                            const float *fs, const float *fa, const float *fsu, const float *fau,
@@ -394,10 +402,10 @@ __device__ __forceinline__ void epi_values(const EpiParams &ep, int64_t row, boo
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
             const float4 sc = fs4[j], ad = fa4[j];
-            v[4 * j] = fmaf(__uint_as_float(g[4 * j]), sc.x, ad.x);
-            v[4 * j + 1] = fmaf(__uint_as_float(g[4 * j + 1]), sc.y, ad.y);
-            v[4 * j + 2] = fmaf(__uint_as_float(g[4 * j + 2]), sc.z, ad.z);
-            v[4 * j + 3] = fmaf(__uint_as_float(g[4 * j + 3]), sc.w, ad.w);
+            fma2(v[4 * j], v[4 * j + 1], __uint_as_float(g[4 * j]), __uint_as_float(g[4 * j + 1]), sc.x, sc.y, ad.x,
+                 ad.y);
+            fma2(v[4 * j + 2], v[4 * j + 3], __uint_as_float(g[4 * j + 2]), __uint_as_float(g[4 * j + 3]), sc.z, sc.w,
+                 ad.z, ad.w);
         }
     } else if (row_scale == 1.0f && row_add == 0.0f) {
 #pragma unroll
@@ -417,14 +425,13 @@ __device__ __forceinline__ void epi_values(const EpiParams &ep, int64_t row, boo
         }
     }
     if (rr.ok) {
-        const float cs = __ldg(ep.c_mat_scale) * ep.beta;
+        const float cs = rr.scale;
         const uint32_t ws[8] = {rr.w[0].x, rr.w[0].y, rr.w[0].z, rr.w[0].w, rr.w[1].x, rr.w[1].y, rr.w[1].z, rr.w[1].w};
 #pragma unroll
         for (int k = 0; k < 16; ++k) {
             float lo, hi;
             e4m3x2_decode(ws[k >> 1] >> ((k & 1) * 16), lo, hi);
-            v[2 * k] = fmaf(lo, cs, v[2 * k]);
-            v[2 * k + 1] = fmaf(hi, cs, v[2 * k + 1]);
+            fma2(v[2 * k], v[2 * k + 1], lo, hi, cs, cs, v[2 * k], v[2 * k + 1]);
         }
     } else if (ep.c_mat && row_ok) {
         float r[32];
@@ -432,13 +439,15 @@ __device__ __forceinline__ void epi_values(const EpiParams &ep, int64_t row, boo
 #pragma unroll
         for (int j = 0; j < 32; ++j) v[j] += r[j];
     }
-    if (EPI == LCML_EPI_RELU) {
+    if (EPI == LCML_EPI_RELU && !RELU_LATER) {
 #pragma unroll
         for (int j = 0; j < 32; ++j) v[j] = fmaxf(v[j], 0.0f);
     }
     if (ep.row_amax) {
+        // |Relu(v)| = max(v, 0) (NaN ignored either way) when Relu is applied later
 #pragma unroll
-        for (int j = 0; j < 32; ++j) amax = (col0 + j < n_out) ? fmaxf(amax, fabsf(v[j])) : amax;
+        for (int j = 0; j < 32; ++j)
+            amax = (col0 + j < n_out) ? fmaxf(amax, (EPI == LCML_EPI_RELU && RELU_LATER) ? v[j] : fabsf(v[j])) : amax;
     }
 }
 
@@ -490,9 +499,12 @@ __device__ __forceinline__ void epilogue_tile(const EpiParams &ep, const CUtenso
             f[2 * h + 1] = (ep.c_vec_mode == 3 && nn < ep.N) ? ep.beta * __ldg(ep.c_vec + nn) : 0.0f;
         }
     };
+    // Relu of an e4m3 output is folded into the conversion (pack32)
+    constexpr bool kReluInPack = EPI == LCML_EPI_RELU && OUT == kOutE4M3;
     // the residual and the factors of the next chunk are loaded while this one is processed
+    const float res_scale = (ep.c_mat && ep.c_mat_kind == 2) ? __ldg(ep.c_mat_scale) * ep.beta : 0.0f;
     ResidualRaw rr_next;
-    prefetch_residual(ep, row, row_ok, col_of(c_first), n_out, rr_next);
+    prefetch_residual(ep, row, row_ok, col_of(c_first), n_out, res_scale, rr_next);
     float fnext[4] = {0.0f, 0.0f, 0.0f, 0.0f};
     if (FACSLOT && c_first < kChunks) load_fac(c_first, fnext);
 #pragma unroll 1
@@ -513,34 +525,42 @@ __device__ __forceinline__ void epilogue_tile(const EpiParams &ep, const CUtenso
                 facw[96 + lane] = fnext[3];
             }
             if (c + c_step < kChunks) {
-                prefetch_residual(ep, row, row_ok, col_of(c + c_step), n_out, rr_next);
+                prefetch_residual(ep, row, row_ok, col_of(c + c_step), n_out, res_scale, rr_next);
                 load_fac(c + c_step, fnext);
             }
             __syncwarp();
             tmem_wait_ld();
-            epi_values<EPI, true>(ep, row, row_ok, col0, ng0 + BN / 2, n_out, g, EPI == LCML_EPI_SILU_MUL ? u : g, facw,
-                            facw + 32, facw + 64, facw + 96, rr, ep.sa_row ? row_scale : 1.0f, row_add, amax, v);
+            epi_values<EPI, true, kReluInPack>(ep, row, row_ok, col0, ng0 + BN / 2, n_out, g,
+                                               EPI == LCML_EPI_SILU_MUL ? u : g, facw, facw + 32, facw + 64, facw + 96,
+                                               rr, ep.sa_row ? row_scale : 1.0f, row_add, amax, v);
             __syncwarp();  // every lane has read facw before the next chunk rewrites it
         } else {
             ColFactors fg, fu;
             load_col_factors(ep, ng0, fg);  // global loads overlap the TMEM load
             if (EPI == LCML_EPI_SILU_MUL) load_col_factors(ep, ng0 + BN / 2, fu);
-            if (c + c_step < kChunks) prefetch_residual(ep, row, row_ok, col_of(c + c_step), n_out, rr_next);
+            if (c + c_step < kChunks)
+                prefetch_residual(ep, row, row_ok, col_of(c + c_step), n_out, res_scale, rr_next);
             tmem_wait_ld();
-            epi_values<EPI, false>(ep, row, row_ok, col0, ng0 + BN / 2, n_out, g, EPI == LCML_EPI_SILU_MUL ? u : g, fg.scale,
-                            fg.add, fu.scale, fu.add, rr, row_scale, row_add, amax, v);
+            epi_values<EPI, false, kReluInPack>(ep, row, row_ok, col0, ng0 + BN / 2, n_out, g,
+                                                EPI == LCML_EPI_SILU_MUL ? u : g, fg.scale, fg.add, fu.scale, fu.add, rr,
+                                                row_scale, row_add, amax, v);
         }
         constexpr int ES = out_es(OUT);
+        constexpr bool kNonNeg = EPI == LCML_EPI_RELU && !kReluInPack;
         if (ep.tma_store) {
             uint32_t w[8 * ES];
-            pack32<OUT, EPI == LCML_EPI_RELU>(v, oq, w);
+            pack32<OUT, kNonNeg, kReluInPack>(v, oq, w);
             store_chunk_tma<OUT>(tmY, stage, seq, row0, col0, w);
         } else if (ep.y_num_peers > 0 && col0 + 32 <= n_out && ((ep.ldy * ES) % 16 == 0) &&
                    (((ep.y_col_offset + col0) * ES) % 16 == 0)) {
             uint32_t w[8 * ES];
-            pack32<OUT, EPI == LCML_EPI_RELU>(v, oq, w);
+            pack32<OUT, kNonNeg, kReluInPack>(v, oq, w);
             store_chunk_peers<OUT>(ep, stage, row0, col0, w);
         } else if (row_ok) {
+            if (kReluInPack) {
+#pragma unroll
+                for (int j = 0; j < 32; ++j) v[j] = fmaxf(v[j], 0.0f);
+            }
             store_row32_to<OUT>(ep, ep.y, row, col0, n_out, v, oq);
             for (int p = 0; p < ep.y_num_peers; ++p) store_row32_to<OUT>(ep, ep.y_peers[p], row, col0, n_out, v, oq);
         }

@@ -236,6 +236,44 @@ __device__ __forceinline__ void quantize_block_fast(const float *v, float s, flo
     }
 }
 
+// ---------------------------------------------------------------------------
+// Packed fp32 pair arithmetic (sm_100 fma/mul .rn.f32x2: one instruction for
+// two lanes, each lane rounded exactly like fmaf / __fmul_rn; subnormals kept).
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void fma2(float &d0, float &d1, float a0, float a1, float b0, float b1, float c0, float c1) {
+    asm("{\n\t.reg .b64 ra, rb, rc, rd;\n\t"
+        "mov.b64 ra, {%2, %3};\n\t"
+        "mov.b64 rb, {%4, %5};\n\t"
+        "mov.b64 rc, {%6, %7};\n\t"
+        "fma.rn.f32x2 rd, ra, rb, rc;\n\t"
+        "mov.b64 {%0, %1}, rd;\n\t}"
+        : "=f"(d0), "=f"(d1)
+        : "f"(a0), "f"(a1), "f"(b0), "f"(b1), "f"(c0), "f"(c1));
+}
+
+__device__ __forceinline__ void mul2(float &d0, float &d1, float a0, float a1, float b0, float b1) {
+    asm("{\n\t.reg .b64 ra, rb, rd;\n\t"
+        "mov.b64 ra, {%2, %3};\n\t"
+        "mov.b64 rb, {%4, %5};\n\t"
+        "mul.rn.f32x2 rd, ra, rb;\n\t"
+        "mov.b64 {%0, %1}, rd;\n\t}"
+        : "=f"(d0), "=f"(d1)
+        : "f"(a0), "f"(a1), "f"(b0), "f"(b1));
+}
+
+// Hardware conversion of two values to e4m3 with Relu folded in (negative
+// values become +0; RNE, saturating). NaN stays NaN (0x7f / 0xff), unlike
+// fmaxf(NaN, 0) = 0: callers that need Relu's NaN -> 0 check for NaN codes.
+__device__ __forceinline__ uint32_t cvt_e4m3x2_relu(float lo, float hi) {
+    uint32_t out;
+    asm("{\n\t.reg .b16 t;\n\t"
+        "cvt.rn.satfinite.relu.e4m3x2.f32 t, %2, %1;\n\t"
+        "cvt.u32.u16 %0, t;\n\t}"
+        : "=r"(out)
+        : "f"(lo), "f"(hi));
+    return out;
+}
+
 // Bytes 0x80 and 0xff of four hardware-converted codes (bit 7 set in the
 // result's byte): a = x & 0x7f7f7f7f; (a + 0x7f) sets bit 7 of a byte exactly
 // when it is nonzero, (a + 1) exactly when it is 0x7f (no carry crosses a
@@ -269,21 +307,37 @@ __device__ __forceinline__ uint32_t quantize_rcp1(float v, float r) {
 // NONNEG: the values are known to be >= +0 or -0 (Relu outputs; fmaxf never
 // returns NaN for a non-NaN bound), so the only possible odd byte is 0x80 and
 // any set sign bit flags the block.
-template <int N, bool NONNEG = false>
+// RELU: v has not been through Relu yet; the rule is applied to Relu(v)
+// (fmaxf(v, 0), so NaN -> 0), with Relu folded into the conversion
+// (cvt ... .relu: q < 0 -> +0, and r > 0 keeps the sign of v): its only odd
+// outputs are NaN codes (where Relu(v) = 0) and a possible 0x80, both flagged.
+template <int N, bool NONNEG = false, bool RELU = false>
 __device__ __forceinline__ void quantize_block_rcp(const float *v, float r, uint32_t *w) {
     uint32_t odd = 0;
 #pragma unroll
     for (int j = 0; j < N / 4; ++j) {
-        w[j] = cvt_e4m3x2(__fmul_rn(v[4 * j], r), __fmul_rn(v[4 * j + 1], r)) |
-               (cvt_e4m3x2(__fmul_rn(v[4 * j + 2], r), __fmul_rn(v[4 * j + 3], r)) << 16);
-        odd |= NONNEG ? w[j] : e4m3_odd_bytes(w[j]);
+        float q[4];
+        mul2(q[0], q[1], v[4 * j], v[4 * j + 1], r, r);
+        mul2(q[2], q[3], v[4 * j + 2], v[4 * j + 3], r, r);
+        if (RELU) {
+            w[j] = cvt_e4m3x2_relu(q[0], q[1]) | (cvt_e4m3x2_relu(q[2], q[3]) << 16);
+            // bit 7 of a byte: a sign (0x80) or, after adding 1 to the low 7 bits, a NaN code (0x7f)
+            odd |= w[j] | ((w[j] & 0x7f7f7f7fu) + 0x01010101u);
+        } else {
+            w[j] = cvt_e4m3x2(q[0], q[1]) | (cvt_e4m3x2(q[2], q[3]) << 16);
+            odd |= NONNEG ? w[j] : e4m3_odd_bytes(w[j]);
+        }
     }
-    if (NONNEG) odd &= 0x80808080u;
+    if (NONNEG || RELU) odd &= 0x80808080u;
     if (odd) {  // unrolled: a runtime index would move v and w to local memory
 #pragma unroll
-        for (int j = 0; j < N / 4; ++j)
-            w[j] = quantize_rcp1(v[4 * j], r) | (quantize_rcp1(v[4 * j + 1], r) << 8) |
-                   (quantize_rcp1(v[4 * j + 2], r) << 16) | (quantize_rcp1(v[4 * j + 3], r) << 24);
+        for (int j = 0; j < N / 4; ++j) {
+            float x[4];
+#pragma unroll
+            for (int k = 0; k < 4; ++k) x[k] = RELU ? fmaxf(v[4 * j + k], 0.0f) : v[4 * j + k];
+            w[j] = quantize_rcp1(x[0], r) | (quantize_rcp1(x[1], r) << 8) | (quantize_rcp1(x[2], r) << 16) |
+                   (quantize_rcp1(x[3], r) << 24);
+        }
     }
 }
 

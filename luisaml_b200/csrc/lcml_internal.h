@@ -50,6 +50,10 @@ struct ConvGeom {
 // d->M = N * oH * oW, d->K = the packed K of the weights).
 int fp8_gemm_implicit_conv(const lcml_fp8_gemm_desc *d, const ConvGeom &geo, cudaStream_t st);
 
+// lcml_fp8_conv for group > 1: the direct grouped kernel (conv_direct.cu);
+// Kp / Cp are the packed K and channels per tap of C / group channels.
+int fp8_conv_grouped(const lcml_fp8_conv_desc *d, int64_t Kp, int64_t Cp, cudaStream_t st);
+
 }// namespace lcml
 
 #define LCML_CHECK_ARG(cond, ...)                                                  \

@@ -175,6 +175,58 @@ __global__ void __launch_bounds__(kThreads) k_amax(const float *__restrict__ x, 
     if (threadIdx.x == 0) atomicMax(out, m);
 }
 
+// Dynamic per-tensor quantization, pass 1: block b's max |x| (as ordered
+// bits, NaN ignored) into partial[b], so nothing needs zeroing first. x is
+// read front to back with normal caching: the last ~100 MB stay in the L2
+// for pass 2, which walks the tensor back to front.
+constexpr int kMaxAmaxParts = 1024;  // LCML_FP8_TENSOR_DYNAMIC_WORKSPACE_BYTES / 4
+
+__global__ void __launch_bounds__(kThreads) k_amax_partial(const float *__restrict__ x, int64_t n,
+                                                           uint32_t *__restrict__ partial) {
+    __shared__ uint32_t red[32];
+    griddep_launch_dependents();  // pass 2 may start its set-up
+    const int64_t tid = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    const int64_t nthreads = static_cast<int64_t>(gridDim.x) * blockDim.x;
+    uint32_t m = 0;
+    const int64_t n4 = n >> 2;
+    for (int64_t i = tid; i < n4; i += nthreads) {
+        const float4 v = __ldg(reinterpret_cast<const float4 *>(x) + i);
+        m = max(m, max(max(abs_bits_nan0(v.x), abs_bits_nan0(v.y)), max(abs_bits_nan0(v.z), abs_bits_nan0(v.w))));
+    }
+    for (int64_t i = (n4 << 2) + tid; i < n; i += nthreads) m = max(m, abs_bits_nan0(x[i]));
+    m = block_max_u32(m, red);
+    if (threadIdx.x == 0) partial[blockIdx.x] = m;
+}
+
+// Pass 2 (launched with programmatic serialization after pass 1): every
+// block reduces the partial maxima (an L2-resident read), s = amax / 448
+// (1 for an all-zero tensor), and quantizes its share of x back to front.
+__global__ void __launch_bounds__(kThreads) k_quantize_tensor_dynamic(const float *__restrict__ x, int64_t n,
+                                                                      const uint32_t *__restrict__ partial,
+                                                                      int nparts, float *__restrict__ scale_out,
+                                                                      uint8_t *__restrict__ y) {
+    __shared__ uint32_t red[32];
+    griddep_wait();  // pass 1 has completed and its partials are visible
+    uint32_t m = 0;
+    for (int i = threadIdx.x; i < nparts; i += blockDim.x) m = max(m, partial[i]);
+    m = block_max_u32(m, red);
+    const float s = scale_from_amax(__uint_as_float(m));
+    if (blockIdx.x == 0 && threadIdx.x == 0) *scale_out = s;
+    griddep_launch_dependents();  // the next GEMM may start its set-up
+    const Scale st = make_scale(s);
+    const int64_t tid = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    const int64_t nthreads = static_cast<int64_t>(gridDim.x) * blockDim.x;
+    const int64_t n16 = n >> 4;
+    for (int64_t g = tid; g < n16; g += nthreads) {
+        const int64_t gg = n16 - 1 - g;  // back to front: the tail pass 1 left in L2 first
+        const float4 *xp = reinterpret_cast<const float4 *>(x) + gg * 4;
+        const float4 v0 = __ldcs(xp), v1 = __ldcs(xp + 1), v2 = __ldcs(xp + 2), v3 = __ldcs(xp + 3);
+        __stcs(reinterpret_cast<uint4 *>(y) + gg, pack16(v0, v1, v2, v3, st));
+    }
+    const int64_t t = (n16 << 4) + tid;
+    if (t < n) y[t] = static_cast<uint8_t>(quantize1(x[t], s));
+}
+
 // One CTA per row; the row stays in registers between the amax and the
 // quantize pass (VPT float4 per thread, so cols <= VPT * 4 * kThreads).
 template <int VPT>
@@ -404,6 +456,31 @@ int lcml_fp8_quantize_tensor_dynamic(const float *x, int64_t n, float *scale_out
     LCML_CHECK_ARG(n >= 0, "lcml_fp8_quantize_tensor_dynamic: negative n");
     LCML_CHECK_ARG(scale_out && workspace, "lcml_fp8_quantize_tensor_dynamic: null scale_out/workspace");
     LCML_CHECK_ARG(n == 0 || (x && y), "lcml_fp8_quantize_tensor_dynamic: null pointer");
+    if (n > 0 && aligned(x, 16) && aligned(y, 16)) {
+        // two kernels, no memset: per-block partial maxima, then the quantize
+        // pass (programmatic dependent launch, back to front over the L2-warm tail)
+        cudaStream_t st = to_cuda(stream);
+        int parts = grid_for((n >> 2) + 1);
+        if (parts > kMaxAmaxParts) parts = kMaxAmaxParts;
+        uint32_t *partial = reinterpret_cast<uint32_t *>(workspace);
+        k_amax_partial<<<parts, kThreads, 0, st>>>(x, n, partial);
+        LCML_LAUNCHED("amax_partial");
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3(static_cast<unsigned>(grid_for((n >> 4) > 0 ? (n >> 4) : 1)), 1, 1);
+        cfg.blockDim = dim3(kThreads, 1, 1);
+        cfg.stream = st;
+        cudaLaunchAttribute attr[1];
+        attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr[0].val.programmaticStreamSerializationAllowed = 1;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+        const cudaError_t e = cudaLaunchKernelEx(&cfg, k_quantize_tensor_dynamic, x, n,
+                                                 static_cast<const uint32_t *>(partial), parts, scale_out, y);
+        g_launches.fetch_add(1, std::memory_order_relaxed);
+        if (e != cudaSuccess)
+            return set_error(LCML_ERR_CUDA, "quantize_tensor_dynamic launch failed: %s", cudaGetErrorString(e));
+        return LCML_OK;
+    }
     int rc = lcml_amax(x, n, workspace, stream);
     if (rc != LCML_OK) return rc;
     if (n == 0) {

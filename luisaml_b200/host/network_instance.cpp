@@ -518,7 +518,8 @@ void NetworkInstance::run_fusion_pass() {
         if (fusion_[ci]->skip || fusion_[ci]->op) continue;
         const std::string &kind = cn.get_op_type();
         if (kind == "Conv") {
-            if (cn.get_inputs().size() < 2 || attr_int(cn, "group", 1) != 1 || !auto_pad_ok(cn)) continue;
+            const int64_t G = attr_int(cn, "group", 1);  // grouped: conv.cpp:62-63, :122-139
+            if (cn.get_inputs().size() < 2 || G < 1 || !auto_pad_ok(cn)) continue;
             const int dx = producer_of(cn.get_inputs()[0]->get_name());
             const int dw = producer_of(cn.get_inputs()[1]->get_name());
             if (!dq_ok(dx) || !dq_ok(dw) || dq_scale_len(dx) != 1) continue;
@@ -530,7 +531,7 @@ void NetworkInstance::run_fusion_pass() {
             const int64_t M = static_cast<int64_t>(wq.get_shape()[0]), C = static_cast<int64_t>(wq.get_shape()[1]);
             const int64_t lw = dq_scale_len(dw);
             if (lw != 1 && (lw != M || attr_int(nodes[dw], "axis", 1) != 0)) continue;
-            if (static_cast<int64_t>(xq.get_shape()[1]) != C) continue;
+            if (static_cast<int64_t>(xq.get_shape()[1]) != C * G || M % G != 0) continue;  // C: channels per group
             const auto ks = ints_or(cn, "kernel_shape", {static_cast<int64_t>(wq.get_shape()[2]), static_cast<int64_t>(wq.get_shape()[3])});
             const auto st = ints_or(cn, "strides", {1, 1});
             const auto pd = ints_or(cn, "pads", {0, 0, 0, 0});
@@ -580,7 +581,7 @@ void NetworkInstance::run_fusion_pass() {
             out = nodes[c].get_outputs()[0]->get_name();
             lcml_fp8_conv_desc &d = op->desc;
             d.N = static_cast<int64_t>(xq.get_shape()[0]);
-            d.C = C;
+            d.C = C * G;
             d.H = static_cast<int64_t>(xq.get_shape()[2]);
             d.W = static_cast<int64_t>(xq.get_shape()[3]);
             d.M = M;
@@ -594,7 +595,7 @@ void NetworkInstance::run_fusion_pass() {
             d.pW = static_cast<int>(pd[1]);
             d.dH = static_cast<int>(dl[0]);
             d.dW = static_cast<int>(dl[1]);
-            d.group = 1;
+            d.group = static_cast<int>(G);
             d.x_nhwc = nhwc.count(xq.get_name()) ? 1 : 0;
             d.epilogue = epi;
             // the output extent of the graph must be what these pads and strides give
@@ -791,7 +792,22 @@ void NetworkInstance::prepare() {
         fold_constants();
     }
 
-    // 4. intermediates touched by nodes that still run; view ops alias their input
+    allocate_intermediates();
+    prepared_ = true;
+}
+
+// 4. Intermediates touched by nodes that still run; view ops alias their input.
+// With memory reuse, each intermediate lives from the step of the node that
+// writes it to the step of its last reader (a view's readers count for the
+// tensor it aliases), and the tensors are placed in one arena: largest first,
+// each at the lowest 256-byte aligned offset whose range no tensor of an
+// overlapping lifetime occupies (the reference colours registers with the
+// same last-use information, network_instance.cpp:369-474, :476-582). Nodes
+// run in order on one stream, so a dead tensor's bytes are rewritten only
+// after its readers have run.
+void NetworkInstance::allocate_intermediates() {
+    const Graph &g = model_.get_graph();
+    const auto &nodes = g.get_nodes();
     auto io_inputs = [&](size_t i) {
         std::vector<std::string> v;
         if (!fusion_[i]->inputs.empty()) return fusion_[i]->inputs;
@@ -804,27 +820,107 @@ void NetworkInstance::prepare() {
         for (const auto *x : nodes[i].get_outputs()) v.push_back(x->get_name());
         return v;
     };
-    for (size_t i = 0; i < nodes.size(); ++i) {
-        if (fusion_[i]->skip) continue;
-        for (const auto &name : io_outputs(i)) {
-            if (table_.contains(name)) continue;
-            const Variable &v = g.get_var(name);
-            const bool view = ops_[i]->is_output_view(0, nodes[i]) && !nodes[i].get_inputs().empty() &&
-                              table_.contains(nodes[i].get_inputs()[0]->get_name());
-            if (view) {
-                ITensor &src = table_.at(nodes[i].get_inputs()[0]->get_name());
-                auto t = DeviceTensor::borrow(v.get_dtype(), to_shape(v.get_shape()), src.data());
-                t->set_view(true);
-                if (t->nbytes() != src.nbytes()) throw Error(nodes[i].get_op_type() + ": view changes the byte size");
-                table_.own(name, std::move(t));
-            } else {
-                table_.own(name, DeviceTensor::allocate(v.get_dtype(), to_shape(v.get_shape())));
-            }
+    struct Life {
+        std::string name;
+        size_t bytes;
+        int first, last;
+        size_t offset = 0;
+    };
+    std::vector<Life> lives;
+    std::map<std::string, size_t> life_of;   // planned tensor -> index in lives
+    std::map<std::string, std::string> alias;  // view -> the tensor whose bytes it names
+    std::vector<std::pair<std::string, size_t>> views;  // (view name, node index) in creation order
+    auto root = [&](std::string n) {
+        for (auto it = alias.find(n); it != alias.end(); it = alias.find(n)) n = it->second;
+        return n;
+    };
+    int step = 0;
+    for (size_t i = 0; i < nodes.size(); ++i, ++step) {
+        if (fusion_[i]->skip) {
+            --step;
+            continue;
         }
-        for (const auto &name : io_inputs(i))
-            if (!table_.contains(name)) throw Error("input '" + name + "' of node " + nodes[i].get_name() + " is not bound");
+        for (const auto &name : io_inputs(i)) {
+            auto it = life_of.find(root(name));
+            if (it != life_of.end()) lives[it->second].last = step;
+            else if (!table_.contains(name) && !alias.count(name))
+                throw Error("input '" + name + "' of node " + nodes[i].get_name() + " is not bound");
+        }
+        for (const auto &name : io_outputs(i)) {
+            if (table_.contains(name) || life_of.count(name) || alias.count(name)) continue;
+            const Variable &v = g.get_var(name);
+            const std::string src = nodes[i].get_inputs().empty() ? std::string() : nodes[i].get_inputs()[0]->get_name();
+            const bool view = ops_[i]->is_output_view(0, nodes[i]) && !src.empty() &&
+                              (table_.contains(src) || life_of.count(root(src)));
+            if (view) {
+                alias[name] = src;
+                views.emplace_back(name, i);
+                continue;
+            }
+            life_of[name] = lives.size();
+            lives.push_back({name, ((dtype_nbytes(v.get_dtype(), [&] {
+                                         size_t n = 1;
+                                         for (auto d : v.get_shape()) n *= d;
+                                         return n;
+                                     }()) + 255) / 256) * 256,
+                             step, step});
+        }
     }
-    prepared_ = true;
+    // a graph output the caller did not bind stays intact to the end (the
+    // reference never reclaims graph outputs, network_instance.cpp:453-456)
+    for (const auto *o : g.get_outputs()) {
+        auto it = life_of.find(root(o->get_name()));
+        if (it != life_of.end()) lives[it->second].last = step;
+    }
+    size_t unplanned = 0;
+    for (const auto &l : lives) unplanned += l.bytes;
+    intermediate_unplanned_ = unplanned;
+    if (reuse_memory_ && !lives.empty()) {
+        std::vector<size_t> order(lives.size());
+        for (size_t k = 0; k < order.size(); ++k) order[k] = k;
+        std::stable_sort(order.begin(), order.end(), [&](size_t a, size_t b) { return lives[a].bytes > lives[b].bytes; });
+        std::vector<size_t> placed;
+        size_t arena = 0;
+        for (size_t k : order) {
+            Life &t = lives[k];
+            // offsets of placed tensors alive at the same time, by start
+            std::vector<std::pair<size_t, size_t>> busy;
+            for (size_t p : placed)
+                if (lives[p].first <= t.last && t.first <= lives[p].last)
+                    busy.emplace_back(lives[p].offset, lives[p].offset + lives[p].bytes);
+            std::sort(busy.begin(), busy.end());
+            size_t off = 0;
+            for (const auto &[b, e] : busy) {
+                if (off + t.bytes <= b) break;  // fits in the gap before this range
+                off = std::max(off, e);
+            }
+            t.offset = off;
+            arena = std::max(arena, off + t.bytes);
+            placed.push_back(k);
+        }
+        auto buf = DeviceTensor::allocate(DataType::UINT8, {static_cast<int64_t>(arena)});
+        uint8_t *base = buf->ptr<uint8_t>();
+        table_.own("#intermediate_arena", std::move(buf));
+        for (const auto &t : lives) {
+            const Variable &v = g.get_var(t.name);
+            table_.own(t.name, DeviceTensor::borrow(v.get_dtype(), to_shape(v.get_shape()), base + t.offset));
+        }
+        intermediate_bytes_ = arena;
+    } else {
+        for (const auto &t : lives) {
+            const Variable &v = g.get_var(t.name);
+            table_.own(t.name, DeviceTensor::allocate(v.get_dtype(), to_shape(v.get_shape())));
+        }
+        intermediate_bytes_ = unplanned;
+    }
+    for (const auto &[name, i] : views) {
+        const Variable &v = g.get_var(name);
+        ITensor &src = table_.at(alias.at(name));
+        auto t = DeviceTensor::borrow(v.get_dtype(), to_shape(v.get_shape()), src.data());
+        t->set_view(true);
+        if (t->nbytes() != src.nbytes()) throw Error(nodes[i].get_op_type() + ": view changes the byte size");
+        table_.own(name, std::move(t));
+    }
 }
 
 void NetworkInstance::forward() {

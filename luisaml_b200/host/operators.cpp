@@ -317,11 +317,43 @@ public:
     }
 };
 
+// Conv (src/onnx/operators/conv.cpp:35-255). fp32 tensors run the direct
+// kernel lcml_conv2d_f32 (1-D or 2-D, group, strides, begin pads,
+// dilations, optional bias); DequantizeLinear-fed FP8 convs are taken by the
+// fusion pass (FusedQdqConv) before they get here.
 class Conv : public StreamOperator {
+    std::vector<int64_t> strides_, pads_, dilations_;
+    int64_t group_;
+
 public:
-    Conv() : StreamOperator("Conv") {}
-    void forward(Span, Span) override {
-        throw Error("Conv: only QDQ (DequantizeLinear-fed) convolutions run on this path; enable fusion");
+    Conv(std::vector<int64_t> strides, std::vector<int64_t> pads, std::vector<int64_t> dilations, int64_t group)
+        : StreamOperator("Conv"), strides_(std::move(strides)), pads_(std::move(pads)),
+          dilations_(std::move(dilations)), group_(group) {}
+    void forward(Span in, Span out) override {
+        const ITensor &x = in[0].get(), &w = in[1].get();
+        ITensor &y = out[0].get();
+        require(x.dtype() == DataType::FLOAT && w.dtype() == DataType::FLOAT && y.dtype() == DataType::FLOAT,
+                "Conv: fp32 tensors here; FP8 convs run fused (DequantizeLinear -> Conv -> QuantizeLinear)");
+        const size_t sd = x.ndim() - 2;  // spatial dims: 1 or 2
+        require((sd == 1 || sd == 2) && w.ndim() == x.ndim() && y.ndim() == x.ndim(),
+                "Conv: only 1D and 2D convolution are supported");
+        const ITensor *b = in.size() > 2 ? &in[2].get() : nullptr;
+        require(!b || (b->dtype() == DataType::FLOAT && b->size() == w.shape(0)), "Conv: bias must be fp32 [M]");
+        auto at = [](const std::vector<int64_t> &v, size_t i, int64_t dflt) { return i < v.size() ? v[i] : dflt; };
+        // a 1-D conv is the 2-D one with H = kH = oH = 1
+        const int64_t H = sd == 2 ? x.shape(2) : 1, W = x.shape(sd + 1);
+        const int64_t kH = sd == 2 ? w.shape(2) : 1, kW = w.shape(sd + 1);
+        const int64_t oH = sd == 2 ? y.shape(2) : 1, oW = y.shape(sd + 1);
+        const int sH = sd == 2 ? static_cast<int>(at(strides_, 0, 1)) : 1;
+        const int sW = static_cast<int>(at(strides_, sd - 1, 1));
+        const int pH = sd == 2 ? static_cast<int>(at(pads_, 0, 0)) : 0;  // begin pads (conv.cpp:119-121)
+        const int pW = static_cast<int>(at(pads_, sd - 1, 0));
+        const int dH = sd == 2 ? static_cast<int>(at(dilations_, 0, 1)) : 1;
+        const int dW = static_cast<int>(at(dilations_, sd - 1, 1));
+        check_status(lcml_conv2d_f32(x.ptr<float>(), w.ptr<float>(), b ? b->ptr<float>() : nullptr, x.shape(0),
+                                     x.shape(1), H, W, w.shape(0), kH, kW, oH, oW, sH, sW, pH, pW, dH, dW,
+                                     static_cast<int>(group_), y.ptr<float>(), stream_),
+                     "Conv");
     }
 };
 
@@ -451,7 +483,14 @@ REGISTER_TO_DEFAULT_OPSET(Gemm) {
                                   get_int(node, "transB", 0));
 };
 REGISTER_TO_DEFAULT_OPSET(MatMul) { return std::make_unique<MatMul>(); };
-REGISTER_TO_DEFAULT_OPSET(Conv) { return std::make_unique<Conv>(); };
+REGISTER_TO_DEFAULT_OPSET(Conv) {
+    if (auto p = node.try_get_attr("auto_pad")) {
+        const std::string s = p->get<AttributeType::STRING>();
+        if (!s.empty() && s != "NOTSET") throw Error("Conv: auto_pad " + s + " is not supported (explicit pads only)");
+    }
+    return std::make_unique<Conv>(get_ints(node, "strides"), get_ints(node, "pads"), get_ints(node, "dilations"),
+                                  get_int(node, "group", 1));
+};
 REGISTER_TO_DEFAULT_OPSET(Relu) { return std::make_unique<Unary>("Relu", 0); };
 REGISTER_TO_DEFAULT_OPSET(Sigmoid) { return std::make_unique<Unary>("Sigmoid", 1); };
 REGISTER_TO_DEFAULT_OPSET(Abs) { return std::make_unique<Unary>("Abs", 2); };

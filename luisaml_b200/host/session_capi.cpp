@@ -107,6 +107,19 @@ int lcml_network_set_fusion(lcml_network *net, int enable) {
     return LCML_OK;
 }
 
+int lcml_network_set_memory_reuse(lcml_network *net, int enable) {
+    if (!net) return fail(LCML_ERR_INVALID_ARGUMENT, "null network");
+    net->inst.enable_memory_reuse(enable != 0);
+    return LCML_OK;
+}
+
+int lcml_network_memory(const lcml_network *net, size_t *intermediate_bytes, size_t *unplanned_bytes) {
+    if (!net || !intermediate_bytes || !unplanned_bytes) return fail(LCML_ERR_INVALID_ARGUMENT, "null argument");
+    *intermediate_bytes = net->inst.intermediate_bytes();
+    *unplanned_bytes = net->inst.intermediate_bytes_unplanned();
+    return LCML_OK;
+}
+
 int lcml_network_set_stream(lcml_network *net, lcml_stream_t s) {
     if (!net) return fail(LCML_ERR_INVALID_ARGUMENT, "null network");
     net->inst.set_stream(s);

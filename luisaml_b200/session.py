@@ -32,6 +32,8 @@ def load():
     lib.lcml_network_set_input_host.argtypes = [_vp, ctypes.c_char_p, _vp]
     lib.lcml_network_set_output_host.argtypes = [_vp, ctypes.c_char_p, _vp]
     lib.lcml_network_set_fusion.argtypes = [_vp, _ci]
+    lib.lcml_network_set_memory_reuse.argtypes = [_vp, _ci]
+    lib.lcml_network_memory.argtypes = [_vp, ctypes.POINTER(ctypes.c_size_t), ctypes.POINTER(ctypes.c_size_t)]
     lib.lcml_network_set_stream.argtypes = [_vp, _vp]
     lib.lcml_network_forward.argtypes = [_vp]
     lib.lcml_network_executed_nodes.argtypes = [_vp, ctypes.POINTER(_i64)]
@@ -108,6 +110,16 @@ class Network:
 
     def set_fusion(self, enable: bool):
         _check(load().lcml_network_set_fusion(self._h, int(enable)))
+
+    def set_memory_reuse(self, enable: bool):
+        """Intermediates in one lifetime-planned arena (default) or one allocation each."""
+        _check(load().lcml_network_set_memory_reuse(self._h, int(enable)))
+
+    def memory(self):
+        """(intermediate bytes as allocated, bytes with one allocation each), after the first forward."""
+        a, b = ctypes.c_size_t(), ctypes.c_size_t()
+        _check(load().lcml_network_memory(self._h, ctypes.byref(a), ctypes.byref(b)))
+        return a.value, b.value
 
     def set_stream(self, stream_handle: int):
         _check(load().lcml_network_set_stream(self._h, stream_handle))

@@ -249,8 +249,10 @@ def qdq_gemm(Aq, sa, Bq, sb, b_kmajor=True, bias=None, rows=None) -> np.ndarray:
 
 
 def conv2d(X, W, bias=None, strides=(1, 1), pads=(0, 0, 0, 0), dilations=(1, 1), group=1,
-           images=None) -> np.ndarray:
-    """ONNX Conv (2-D NCHW) following conv.cpp; output shape from the ONNX formula."""
+           images=None, lanes=1) -> np.ndarray:
+    """ONNX Conv (2-D NCHW) following conv.cpp; output shape from the ONNX formula.
+    lanes=1: one fma chain over (kh, kw, c); lanes=4: the reference's fp32
+    order (per tap four lane sums over the channels, conv.cpp:150-191)."""
     X = np.ascontiguousarray(X, dtype=np.float32)
     W = np.ascontiguousarray(W, dtype=np.float32)
     N, C, H, Wd = X.shape
@@ -268,9 +270,9 @@ def conv2d(X, W, bias=None, strides=(1, 1), pads=(0, 0, 0, 0), dilations=(1, 1),
         bias = np.ascontiguousarray(bias, dtype=np.float32)
         bptr = _f(bias)
     ci = ctypes.c_int
-    lib.orc_conv2d_f32(_f(X), _f(W), bptr, _i64(N), _i64(C), _i64(H), _i64(Wd), _i64(M), _i64(kH),
-                       _i64(kW), _i64(oH), _i64(oW), ci(sH), ci(sW), ci(pH), ci(pW), ci(dH), ci(dW),
-                       ci(group), _f(Y), _i64(n0), _i64(n1))
+    lib.orc_conv2d_f32_lanes(_f(X), _f(W), bptr, _i64(N), _i64(C), _i64(H), _i64(Wd), _i64(M), _i64(kH),
+                             _i64(kW), _i64(oH), _i64(oW), ci(sH), ci(sW), ci(pH), ci(pW), ci(dH), ci(dW),
+                             ci(group), _f(Y), _i64(n0), _i64(n1), ci(lanes))
     return Y
 
 

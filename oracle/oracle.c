@@ -430,13 +430,20 @@ ORC_EXPORT void orc_qdq_gemm_rows(const uint8_t *Aq, const float *sa, int sa_mod
  * kh, kw, c with fma accumulation (conv.cpp:141-195), then + bias
  * (conv.cpp:197-200). Images [n0, n1) only.
  */
-ORC_EXPORT void orc_conv2d_f32(const float *X, const float *W, const float *bias,
-                               int64_t N, int64_t C, int64_t H, int64_t Wd,
-                               int64_t M, int64_t kH, int64_t kW, int64_t oH, int64_t oW,
-                               int sH, int sW, int pH, int pW, int dH, int dW, int group,
-                               float *Y, int64_t n0, int64_t n1) {
+/*
+ * lanes == 4 restates the reference's fp32 order (conv.cpp:150-191): per
+ * tap, the group's channels four at a time into four lane sums (fma),
+ * added as ((x + y) + z) + w to the running sum, the last Cg % 4 channels
+ * by fma into the running sum. lanes == 1: one fma chain over (kh, kw, c).
+ */
+ORC_EXPORT void orc_conv2d_f32_lanes(const float *X, const float *W, const float *bias,
+                                     int64_t N, int64_t C, int64_t H, int64_t Wd,
+                                     int64_t M, int64_t kH, int64_t kW, int64_t oH, int64_t oW,
+                                     int sH, int sW, int pH, int pW, int dH, int dW, int group,
+                                     float *Y, int64_t n0, int64_t n1, int lanes) {
     (void)N;
     int64_t Cg = C / group, Mg = M / group;
+    int64_t c4 = lanes == 4 ? (Cg / 4) * 4 : 0;
 #pragma omp parallel for collapse(2) schedule(dynamic, 1)
     for (int64_t n = n0; n < n1; ++n) {
         for (int64_t m = 0; m < M; ++m) {
@@ -450,7 +457,14 @@ ORC_EXPORT void orc_conv2d_f32(const float *X, const float *W, const float *bias
                         for (int64_t kw = 0; kw < kW; ++kw) {
                             int64_t iw = ow * sW + kw * dW - pW;
                             if (iw < 0 || iw >= Wd) continue;
-                            for (int64_t c = 0; c < Cg; ++c) {
+                            if (c4 > 0) {
+                                float a[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+                                for (int64_t c = 0; c < c4; ++c)
+                                    a[c & 3] = fmaf(X[((n * C + g * Cg + c) * H + ih) * Wd + iw],
+                                                    W[((m * Cg + c) * kH + kh) * kW + kw], a[c & 3]);
+                                sum += ((a[0] + a[1]) + a[2]) + a[3];
+                            }
+                            for (int64_t c = c4; c < Cg; ++c) {
                                 float xv = X[((n * C + g * Cg + c) * H + ih) * Wd + iw];
                                 float wv = W[((m * Cg + c) * kH + kh) * kW + kw];
                                 sum = fmaf(xv, wv, sum);
@@ -463,6 +477,14 @@ ORC_EXPORT void orc_conv2d_f32(const float *X, const float *W, const float *bias
             }
         }
     }
+}
+
+ORC_EXPORT void orc_conv2d_f32(const float *X, const float *W, const float *bias,
+                               int64_t N, int64_t C, int64_t H, int64_t Wd,
+                               int64_t M, int64_t kH, int64_t kW, int64_t oH, int64_t oW,
+                               int sH, int sW, int pH, int pW, int dH, int dW, int group,
+                               float *Y, int64_t n0, int64_t n1) {
+    orc_conv2d_f32_lanes(X, W, bias, N, C, H, Wd, M, kH, kW, oH, oW, sH, sW, pH, pW, dH, dW, group, Y, n0, n1, 1);
 }
 
 /* ------------------------------------------------------------------------- */

@@ -158,3 +158,104 @@ def test_conv_residual_relu_e4m3_out(dev):
     want = oracle.dequantize(oracle.quantize(ref, ys), ys)
     step = np.maximum(np.abs(want) * 0.125, ys * 2.0 ** -9)
     assert (np.abs(got8 * ys - want) <= step + 1e-7).all()
+
+
+FP32_CASES = [
+    # name, N, C, H, W, M, kH, kW, stride, pad, dil, group, bias
+    ("3x3_pad1", 2, 8, 11, 9, 6, 3, 3, 1, 1, 1, 1, True),
+    ("5x5_s2_dil", 1, 7, 17, 15, 5, 5, 3, 2, 2, 2, 1, False),   # C % 4 = 3: the lane tail
+    ("grouped", 2, 12, 10, 10, 8, 3, 3, 1, 1, 1, 4, True),      # 3 channels per group: tail only
+    ("grouped_wide", 1, 32, 9, 9, 16, 3, 3, 1, 0, 1, 2, True),  # 16 channels per group: four lanes
+    ("depthwise", 2, 16, 13, 13, 16, 3, 3, 2, 1, 1, 16, True),
+    ("1d", 3, 9, 1, 40, 7, 1, 5, 2, 2, 1, 1, True),              # a 1-D conv as H = 1
+]
+
+
+@pytest.mark.parametrize("name,N,C,H,W,M,kH,kW,stride,pad,dil,group,bias", FP32_CASES)
+def test_conv2d_f32_matches_reference_order(dev, name, N, C, H, W, M, kH, kW, stride, pad, dil, group, bias):
+    """The fp32 Conv (conv.cpp:115-207) bit for bit against the oracle in the
+    reference's summation order (per tap, four lane sums over the group's
+    channels), and within 1e-5 of the single fma chain."""
+    import torch
+    import luisaml_b200 as lb
+    rng = np.random.default_rng(len(name) * 7 + C)
+    X = rng.standard_normal((N, C, H, W)).astype(np.float32)
+    Wt = rng.standard_normal((M, C // group, kH, kW)).astype(np.float32)
+    b = rng.standard_normal(M).astype(np.float32) if bias else None
+    sh = (stride, stride) if H > 1 else (1, stride)
+    pd = (pad, pad, pad, pad) if H > 1 else (0, pad, 0, pad)
+    dl = (dil, dil) if H > 1 else (1, dil)
+    ref4 = oracle.conv2d(X, Wt, b, strides=sh, pads=pd, dilations=dl, group=group, lanes=4)
+    ref1 = oracle.conv2d(X, Wt, b, strides=sh, pads=pd, dilations=dl, group=group)
+    oH, oW = ref4.shape[2], ref4.shape[3]
+    Y = torch.empty((N, M, oH, oW), dtype=torch.float32, device=dev)
+    xt, wt = _t(X, dev), _t(Wt, dev)
+    bt = _t(b, dev) if bias else None
+    lb.check(lb.lib().lcml_conv2d_f32(ctypes.c_void_p(xt.data_ptr()), ctypes.c_void_p(wt.data_ptr()),
+                                      ctypes.c_void_p(bt.data_ptr()) if bias else None, N, C, H, W, M, kH, kW, oH, oW,
+                                      sh[0], sh[1], pd[0], pd[1], dl[0], dl[1], group, ctypes.c_void_p(Y.data_ptr()),
+                                      ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)))
+    got = Y.cpu().numpy()
+    np.testing.assert_array_equal(got, ref4)
+    assert_close(got, ref1, rtol=1e-5, atol=1e-5, what=name)
+
+
+@pytest.mark.parametrize("nhwc", [True, False])
+@pytest.mark.parametrize("group,C,M", [(2, 32, 48), (64, 64, 64), (4, 24, 8)])
+def test_grouped_fp8_conv(dev, nhwc, group, C, M):
+    """Grouped and depthwise QDQ convs (group > 1) through lcml_fp8_conv: the
+    direct kernel vs the oracle's grouped conv on the dequantized operands,
+    with bias, e4m3 residual and Relu, fp32 and e4m3 outputs."""
+    import torch
+    import luisaml_b200 as lb
+    rng = np.random.default_rng(group * 100 + C)
+    N, H, k = 2, 14, 3
+    X = rng.standard_normal((N, C, H, H)).astype(np.float32)
+    Wt = (rng.standard_normal((M, C // group, k, k)) * 0.2).astype(np.float32)
+    bias = (rng.standard_normal(M) * 0.01).astype(np.float32)
+    R = rng.standard_normal((N, M, H, H)).astype(np.float32)
+    sx = np.float32(oracle.scale_from_amax(oracle.amax(X)))
+    xq = oracle.quantize(X, sx)
+    sw = np.array([oracle.scale_from_amax(oracle.amax(Wt[m])) for m in range(M)], dtype=np.float32)
+    wq = oracle.quantize(Wt, sw, axis=0)
+    rs = np.float32(oracle.scale_from_amax(oracle.amax(R)))
+    rq = oracle.quantize(R, rs)
+    ref = oracle.conv2d(oracle.dequantize(xq, sx), oracle.dequantize(wq, sw, axis=0), bias, pads=(1, 1, 1, 1),
+                        group=group)
+    ref = np.maximum(ref + oracle.dequantize(rq, rs), 0.0)
+    Kp = lb.lib().lcml_fp8_conv_packed_k(C // group, k, k)
+    Wp = torch.empty((M, Kp), dtype=torch.uint8, device=dev)
+    st = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+    wqt = _t(wq, dev)
+    lb.check(lb.lib().lcml_fp8_conv_pack_weight(ctypes.c_void_p(wqt.data_ptr()), M, C // group, k, k,
+                                                ctypes.c_void_p(Wp.data_ptr()), st))
+    xt = _t(np.ascontiguousarray(xq.transpose(0, 2, 3, 1)) if nhwc else xq, dev)
+    sxt, swt, bt = _t(np.float32([sx]), dev), _t(sw, dev), _t(bias, dev)
+    rt, rst = _t(np.ascontiguousarray(rq.transpose(0, 2, 3, 1)), dev), _t(np.float32([rs]), dev)
+    ys = np.float32(oracle.scale_from_amax(np.abs(ref).max()))
+    yst = _t(np.float32([ys]), dev)
+    outs = {}
+    for out, dt, code in (("f32", torch.float32, 1), ("e4m3", torch.uint8, 17)):
+        Y = torch.empty((N, H, H, M), dtype=dt, device=dev)
+        d = lb._capi.ConvDesc()
+        d.N, d.C, d.H, d.W, d.M, d.kH, d.kW, d.oH, d.oW = N, C, H, H, M, k, k, H, H
+        d.sH = d.sW = 1
+        d.pH = d.pW = 1
+        d.dH = d.dW = 1
+        d.group = group
+        d.X, d.x_nhwc, d.scale_x = xt.data_ptr(), int(nhwc), sxt.data_ptr()
+        d.Wp, d.scale_w, d.scale_w_mode = Wp.data_ptr(), swt.data_ptr(), lb.SCALE_AXIS
+        d.bias = bt.data_ptr()
+        d.residual, d.residual_dtype, d.residual_scale = rt.data_ptr(), lb.DTYPE_E4M3, rst.data_ptr()
+        d.epilogue = lb.EPI_RELU
+        d.Y, d.y_dtype, d.y_scale = Y.data_ptr(), code, yst.data_ptr()
+        assert lb.lib().lcml_fp8_conv_workspace_size(ctypes.byref(d)) == 0
+        lb.check(lb.lib().lcml_fp8_conv(ctypes.byref(d), st))
+        torch.cuda.synchronize()
+        outs[out] = Y.cpu().numpy()
+    got = outs["f32"].transpose(0, 3, 1, 2)
+    assert_close(got, ref, what=f"grouped conv g={group}")
+    # e4m3 output: the epilogue rule on the kernel's own fp32 value
+    r = np.float32(1.0) / ys
+    want = oracle.quantize((outs["f32"] * r).astype(np.float32), np.float32(1.0))
+    np.testing.assert_array_equal(outs["e4m3"], want)

@@ -244,6 +244,7 @@ def test_ffn_config_shape_stage_by_stage(dev):
     text, blob, meta = graphs.ffn(T, D, F)
     x = np.random.default_rng(3001).standard_normal((T, D)).astype(np.float32)
     net = Network(text)
+    net.set_memory_reuse(False)  # keep every intermediate readable
     y = torch.empty((T, D), dtype=torch.bfloat16, device=dev)
     net.set_weight_buffer(_t(np.frombuffer(blob, dtype=np.uint8), dev))
     net.set_input("x", _t(x, dev))
@@ -266,6 +267,17 @@ def test_ffn_config_shape_stage_by_stage(dev):
     assert np.array_equal(sh, sh_ref) and np.array_equal(hq, hq_ref), "h quantization differs from the oracle"
     ref = oracle.qdq_gemm(hq[rows], sh[rows], meta["wd_q"], meta["wd_s"]) + x[rows]
     assert_close_bf16(y.float().cpu().numpy()[rows], ref, what="down GEMM + residual at the config shape")
+    # the default lifetime-planned arena: the same output bit for bit
+    net2 = Network(text)
+    y2 = torch.empty((T, D), dtype=torch.bfloat16, device=dev)
+    net2.set_weight_buffer(_t(np.frombuffer(blob, dtype=np.uint8), dev))
+    net2.set_input("x", _t(x, dev))
+    net2.set_output("y", y2)
+    net2.forward()
+    torch.cuda.synchronize()
+    assert torch.equal(y, y2)
+    arena, unplanned = net2.memory()
+    assert arena < unplanned, (arena, unplanned)
 
 
 def test_dynamic_row_quant_all_zero_row(dev):
@@ -284,6 +296,7 @@ def test_dynamic_row_quant_all_zero_row(dev):
     for fusion in (True, False):
         net = Network(text)
         net.set_fusion(fusion)
+        net.set_memory_reuse(False)
         y = torch.empty((T, D), dtype=torch.bfloat16, device=dev)
         net.set_weight_buffer(_t(np.frombuffer(blob, dtype=np.uint8), dev))
         net.set_input("x", _t(x, dev))
@@ -296,3 +309,122 @@ def test_dynamic_row_quant_all_zero_row(dev):
     q, s = out[False]
     assert s[5] == 0.0 and (q[5] == 0x7f).all()
     np.testing.assert_array_equal(out[True][0][:5], out[False][0][:5])
+
+
+def _run_graph(dev, b, inputs, outputs, fusion=True, reuse=True):
+    """Runs a GraphBuilder graph: inputs {name: np array}, outputs {name: (shape, torch dtype)}."""
+    import torch
+    from luisaml_b200.session import Network
+    net = Network(b.to_json())
+    net.set_fusion(fusion)
+    net.set_memory_reuse(reuse)
+    if b.blob:
+        net.set_weight_buffer(_t(np.frombuffer(bytes(b.blob), dtype=np.uint8), dev))
+    for k, v in inputs.items():
+        net.set_input(k, _t(v, dev))
+    outs = {k: torch.empty(shape, dtype=dt, device=dev) for k, (shape, dt) in outputs.items()}
+    for k, t in outs.items():
+        net.set_output(k, t)
+    net.forward()
+    torch.cuda.synchronize()
+    return net, {k: t.cpu().numpy() for k, t in outs.items()}
+
+
+def test_fp32_conv_graph(dev):
+    """An fp32 Conv node (no QDQ: conv.cpp:115-207) through NetworkInstance,
+    grouped with bias and stride, then Relu: bit-exact against the oracle in
+    the reference's summation order."""
+    import torch
+    from luisaml_b200.export import GraphBuilder
+    rng = np.random.default_rng(77)
+    b = GraphBuilder("conv_f32")
+    b.input("x", "FLOAT", (2, 8, 12, 12))
+    W = rng.standard_normal((6, 4, 3, 3)).astype(np.float32)
+    bias = rng.standard_normal(6).astype(np.float32)
+    b.const("w", W)
+    b.const("b", bias)
+    c = b.value("c", "FLOAT", (2, 6, 6, 6))
+    b.node("Conv", ["x", "w", "b"], [c], kernel_shape=[3, 3], strides=[2, 2], pads=[1, 1, 1, 1], group=2)
+    b.output("y", "FLOAT", (2, 6, 6, 6))
+    b.node("Relu", [c], ["y"])
+    x = rng.standard_normal((2, 8, 12, 12)).astype(np.float32)
+    _, out = _run_graph(dev, b, {"x": x}, {"y": ((2, 6, 6, 6), torch.float32)})
+    ref = oracle.relu(oracle.conv2d(x, W, bias, strides=(2, 2), pads=(1, 1, 1, 1), group=2, lanes=4))
+    np.testing.assert_array_equal(out["y"], ref)
+
+
+def test_qdq_depthwise_conv_graph(dev):
+    """A QDQ depthwise conv (group = channels) fused by the executor: Q(x) ->
+    DQ -> Conv(DQ(W), group=C) -> Relu -> Q -> DQ -> GlobalAveragePool, fused
+    and unfused, against the oracle (codes within one step, pooled output
+    within the GEMM tolerance)."""
+    import torch
+    from luisaml_b200.export import GraphBuilder, qdq_weight
+    rng = np.random.default_rng(78)
+    N, C, H = 2, 32, 10
+    b = GraphBuilder("dw_qdq")
+    b.input("x", "FLOAT", (N, C, H, H))
+    sx = np.float32(0.01)
+    b.const("sx", np.float32(sx).reshape(()))
+    xq = b.value("xq", "FLOAT8E4M3FN", (N, C, H, H))
+    b.node("QuantizeLinear", ["x", "sx"], [xq])
+    xdq = b.value("xdq", "FLOAT", (N, C, H, H))
+    b.node("DequantizeLinear", [xq, "sx"], [xdq])
+    Wt = (rng.standard_normal((C, 1, 3, 3)) * 0.3).astype(np.float32)
+    wdq, wq, ws = qdq_weight(b, "w", Wt, axis=0)
+    bias = (rng.standard_normal(C) * 0.01).astype(np.float32)
+    b.const("bias", bias)
+    cv = b.value("cv", "FLOAT", (N, C, H, H))
+    b.node("Conv", [xdq, wdq, "bias"], [cv], kernel_shape=[3, 3], pads=[1, 1, 1, 1], group=C)
+    r = b.value("r", "FLOAT", (N, C, H, H))
+    b.node("Relu", [cv], [r])
+    sy = np.float32(0.004)
+    b.const("sy", np.float32(sy).reshape(()))
+    yq = b.value("yq", "FLOAT8E4M3FN", (N, C, H, H))
+    b.node("QuantizeLinear", [r, "sy"], [yq])
+    ydq = b.value("ydq", "FLOAT", (N, C, H, H))
+    b.node("DequantizeLinear", [yq, "sy"], [ydq])
+    b.output("y", "FLOAT", (N, C, 1, 1))
+    b.node("GlobalAveragePool", [ydq], ["y"])
+    x = (rng.standard_normal((N, C, H, H))).astype(np.float32)
+    h = oracle.conv2d(oracle.dequantize(oracle.quantize(x, sx), sx), oracle.dequantize(wq, ws, axis=0), bias,
+                      pads=(1, 1, 1, 1), group=C)
+    codes = oracle.quantize(oracle.relu(h), sy)
+    ref = oracle.global_avgpool(oracle.dequantize(codes, sy))
+    for fusion in (True, False):
+        net, out = _run_graph(dev, b, {"x": x}, {"y": ((N, C, 1, 1), torch.float32)}, fusion=fusion)
+        if fusion:
+            assert "implicit-GEMM conv" in net.summary() or "fused" in net.summary()
+        # one e4m3 step per pooled pixel at most moves the mean by sy * 2^-3 * |y| / 100
+        assert_close(out["y"], ref, rtol=2e-3, atol=1e-3, what=f"depthwise fusion={fusion}")
+
+
+def test_qdq_matmul_graph(dev):
+    """A MatMul node (mat_mul.cpp:51-186) with DequantizeLinear'd operands:
+    x -> Q -> DQ -> MatMul(DQ(W [K, N] e4m3, per-column scales)) + Add(bias),
+    fused into one FP8 GEMM (W transposed to K-major at prepare) and unfused,
+    against the oracle."""
+    import torch
+    from luisaml_b200.export import GraphBuilder, qdq_weight
+    rng = np.random.default_rng(79)
+    M, K, N = 96, 256, 200
+    b = GraphBuilder("matmul_qdq")
+    b.input("x", "FLOAT", (M, K))
+    sx = np.float32(oracle.scale_from_amax(4.5))
+    b.const("sx", np.float32(sx).reshape(()))
+    xq = b.value("xq", "FLOAT8E4M3FN", (M, K))
+    b.node("QuantizeLinear", ["x", "sx"], [xq])
+    xdq = b.value("xdq", "FLOAT", (M, K))
+    b.node("DequantizeLinear", [xq, "sx"], [xdq])
+    Wt = (rng.standard_normal((K, N)) * 0.05).astype(np.float32)
+    wdq, wq, ws = qdq_weight(b, "w", Wt, axis=1)
+    b.output("y", "FLOAT", (M, N))
+    b.node("MatMul", [xdq, wdq], ["y"])
+    x = rng.standard_normal((M, K)).astype(np.float32)
+    aq = oracle.quantize(x, sx)
+    ref = oracle.qdq_gemm(aq, np.float32([sx]), wq, ws, b_kmajor=False)
+    for fusion in (True, False):
+        net, out = _run_graph(dev, b, {"x": x}, {"y": ((M, N), torch.float32)}, fusion=fusion)
+        assert_close(out["y"], ref, what=f"QDQ MatMul fusion={fusion}")
+        if fusion:
+            assert net.executed_nodes() == 2, net.summary()  # input quantize + one fused GEMM

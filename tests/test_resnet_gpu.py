@@ -25,10 +25,13 @@ from conftest import assert_close
 pytestmark = pytest.mark.gpu
 
 
-def _run(dev, text, blob, x, ncls):
+def _run(dev, text, blob, x, ncls, reuse=False):
+    """Runs the graph; with reuse=False every intermediate keeps its own
+    allocation, so the conv-by-conv checks can read them back."""
     import torch
     from luisaml_b200.session import Network
     net = Network(text)
+    net.set_memory_reuse(reuse)
     y = torch.empty((x.shape[0], ncls), dtype=torch.float32, device=dev)
     net.set_weight_buffer(torch.from_numpy(np.frombuffer(blob, dtype=np.uint8).copy()).to(dev))
     net.set_input("x", torch.from_numpy(x).to(dev))
@@ -162,6 +165,11 @@ def test_resnet50_conv_by_conv_vs_oracle(dev):
     print(f"53 convs: worst flip rate {worst:.5%}")
     _check_pool(net, meta, [0, 1])
     _check_head(net, meta, got)
+    # the lifetime-planned arena (the default) gives the same logits bit for bit
+    net2, got2 = _run(dev, text, blob, x, 1000, reuse=True)
+    np.testing.assert_array_equal(got2, got)
+    arena, unplanned = net2.memory()
+    assert arena < unplanned / 3, (arena, unplanned)
 
 
 def test_resnet50_batch128_sampled_images(dev):
@@ -179,3 +187,9 @@ def test_resnet50_batch128_sampled_images(dev):
     print(f"batch 128, images {imgs}: worst conv flip rate {worst:.5%}")
     _check_pool(net, meta, imgs)
     _check_head(net, meta, got)
+    del net
+    net2, got2 = _run(dev, text, blob, x, 1000, reuse=True)
+    np.testing.assert_array_equal(got2, got)
+    arena, unplanned = net2.memory()
+    print(f"batch 128 intermediates: {arena / 2**20:.0f} MiB in the arena vs {unplanned / 2**20:.0f} MiB unplanned")
+    assert arena < unplanned / 3, (arena, unplanned)
