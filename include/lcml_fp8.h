@@ -341,6 +341,16 @@ int lcml_fp8_conv(const lcml_fp8_conv_desc *desc, lcml_stream_t stream);
 int lcml_conv2d_f32(const float *X, const float *W, const float *B, int64_t N, int64_t C, int64_t H, int64_t Wd,
                     int64_t M, int64_t kH, int64_t kW, int64_t oH, int64_t oW, int sH, int sW, int pH, int pW, int dH,
                     int dW, int group, float *Y, lcml_stream_t stream);
+/* fp32 ConvTranspose (src/onnx/operators/conv_transpose.cpp): X NCHW
+ * [N, C, H, W], W [C, M/group, kH, kW], optional bias [M], Y NCHW
+ * [N, M, oH, oW] (oH / oW as the graph declares them, output_padding
+ * included). Gather form: Y[n, m, oh, ow] sums X[n, c, ih, iw] *
+ * W[c, m % (M/group), kh, kw] over the channels c of m's group and the taps
+ * with oh + pH - kh * dH = ih * sH (likewise ow), in the reference's order
+ * (taps, then four lane sums over c), then + bias. */
+int lcml_conv_transpose2d_f32(const float *X, const float *W, const float *B, int64_t N, int64_t C, int64_t H,
+                              int64_t Wd, int64_t M, int64_t kH, int64_t kW, int64_t oH, int64_t oW, int sH, int sW,
+                              int pH, int pW, int dH, int dW, int group, float *Y, lcml_stream_t stream);
 
 /*
  * Memory-bound operators around the GEMMs (fp32 unless stated).
@@ -357,6 +367,19 @@ int lcml_reduce_max_rows(const float *x, int64_t rows, int64_t cols, int abs_fir
                          lcml_stream_t stream);
 /* Softmax over the last axis (softmax.cpp:216-443): x, y [rows, cols]. */
 int lcml_softmax_rows(const float *x, int64_t rows, int64_t cols, float *y, lcml_stream_t stream);
+/* Add/Sub/Mul/Div of FP8-typed tensors (FLOAT8E4M3FN or FLOAT8E5M2 values,
+ * no scale), the reference's quantized Binary path (binary.cpp:185-283):
+ * both operands decoded to half, the op in IEEE half arithmetic, the half
+ * result encoded with the fp_quantized.h codec. Broadcast of b as in
+ * lcml_binary_f32. op: 0 add, 1 sub, 2 mul, 3 div. */
+int lcml_binary_fp8(int op, const uint8_t *a, const uint8_t *b, int64_t n, int64_t b_n, uint8_t *y, int dtype,
+                    lcml_stream_t stream);
+/* Softmax over the last axis of an FP8-typed tensor (softmax.cpp:245-280:
+ * decode, softmax, encode). The softmax runs in fp32 (the reference's half
+ * arithmetic and half exp are not reproduced); its result is rounded to half
+ * and encoded with the codec. */
+int lcml_softmax_rows_fp8(const uint8_t *x, int64_t rows, int64_t cols, uint8_t *y, int dtype,
+                          lcml_stream_t stream);
 /* MaxPool 2-D (max_pool.cpp:20-300), NCHW fp32 or e4m3 (elem_dtype), begin pads. */
 int lcml_maxpool2d(const void *x, int elem_dtype, int64_t NC, int64_t H, int64_t W, int kH, int kW, int sH,
                    int sW, int pH, int pW, int64_t oH, int64_t oW, void *y, int x_nhwc, int64_t C,

@@ -126,10 +126,14 @@ PROTOTYPES = {
     "lcml_fp8_conv": [ctypes.POINTER(ConvDesc), _vp],
     "lcml_conv2d_f32": [_vp, _vp, _vp, _c_i64, _c_i64, _c_i64, _c_i64, _c_i64, _c_i64, _c_i64, _c_i64, _c_i64, _ci,
                         _ci, _ci, _ci, _ci, _ci, _ci, _vp, _vp],
+    "lcml_conv_transpose2d_f32": [_vp, _vp, _vp, _c_i64, _c_i64, _c_i64, _c_i64, _c_i64, _c_i64, _c_i64, _c_i64,
+                                  _c_i64, _ci, _ci, _ci, _ci, _ci, _ci, _ci, _vp, _vp],
     "lcml_unary_f32": [_ci, _vp, _vp, _c_i64, _vp],
     "lcml_binary_f32": [_ci, _vp, _vp, _c_i64, _c_i64, _vp, _vp],
     "lcml_reduce_max_rows": [_vp, _c_i64, _c_i64, _ci, _vp, _vp],
     "lcml_softmax_rows": [_vp, _c_i64, _c_i64, _vp, _vp],
+    "lcml_binary_fp8": [_ci, _vp, _vp, _c_i64, _c_i64, _vp, _ci, _vp],
+    "lcml_softmax_rows_fp8": [_vp, _c_i64, _c_i64, _vp, _ci, _vp],
     "lcml_maxpool2d": [_vp, _ci, _c_i64, _c_i64, _c_i64, _ci, _ci, _ci, _ci, _ci, _ci, _c_i64, _c_i64, _vp,
                        _ci, _c_i64, _vp],
     "lcml_global_avgpool": [_vp, _ci, _vp, _c_i64, _c_i64, _c_i64, _ci, _vp, _vp],

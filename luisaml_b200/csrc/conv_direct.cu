@@ -79,6 +79,58 @@ __global__ void __launch_bounds__(kThreads) k_conv2d_f32(const float *__restrict
     }
 }
 
+// ConvTranspose (conv_transpose.cpp) as a gather: output (n, m, oh, ow) sums
+// X[n, g*Cg + c, ih, iw] * W[g*Cg + c, m % Mg, kh, kw] over the taps with
+// ih = (oh + pH - kh*dH) / sH exact and in range (likewise iw), in the
+// reference's order: taps (kh, kw), within a tap four lane sums over c added
+// as ((x + y) + z) + w, the C/group % 4 tail by fma; then + bias.
+__global__ void __launch_bounds__(kThreads)
+    k_conv_transpose2d_f32(const float *__restrict__ X, const float *__restrict__ W, const float *__restrict__ B,
+                           int64_t N, int64_t C, int64_t H, int64_t Wd, int64_t M, int64_t kH, int64_t kW, int64_t oH,
+                           int64_t oW, int sH, int sW, int pH, int pW, int dH, int dW, int64_t Cg, int64_t Mg,
+                           float *__restrict__ Y) {
+    const int64_t total = N * M * oH * oW;
+    const int64_t c4 = (Cg / 4) * 4;
+    for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
+         i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+        const int64_t ow = i % oW;
+        int64_t t = i / oW;
+        const int64_t oh = t % oH;
+        t /= oH;
+        const int64_t m = t % M, n = t / M;
+        const int64_t g = m / Mg, mg = m % Mg;
+        const float *xg = X + (n * C + g * Cg) * H * Wd;
+        const float *wg = W + (g * Cg * Mg + mg) * kH * kW;  // W[g*Cg + c, mg, kh, kw] at wg + c * Mg*kH*kW
+        float sum = 0.0f;
+        for (int64_t kh = 0; kh < kH; ++kh) {
+            const int64_t ihs = oh + pH - kh * dH;
+            if (ihs < 0 || ihs % sH != 0 || ihs / sH >= H) continue;
+            const int64_t ih = ihs / sH;
+            for (int64_t kw = 0; kw < kW; ++kw) {
+                const int64_t iws = ow + pW - kw * dW;
+                if (iws < 0 || iws % sW != 0 || iws / sW >= Wd) continue;
+                const int64_t iw = iws / sW;
+                const float *xp = xg + ih * Wd + iw;
+                const float *wp = wg + kh * kW + kw;
+                const int64_t wcs = Mg * kH * kW;  // weight stride between input channels
+                if (c4 > 0) {
+                    float a0 = 0.0f, a1 = 0.0f, a2 = 0.0f, a3 = 0.0f;
+                    for (int64_t c = 0; c < c4; c += 4) {
+                        a0 = fmaf(__ldg(xp + (c + 0) * H * Wd), __ldg(wp + (c + 0) * wcs), a0);
+                        a1 = fmaf(__ldg(xp + (c + 1) * H * Wd), __ldg(wp + (c + 1) * wcs), a1);
+                        a2 = fmaf(__ldg(xp + (c + 2) * H * Wd), __ldg(wp + (c + 2) * wcs), a2);
+                        a3 = fmaf(__ldg(xp + (c + 3) * H * Wd), __ldg(wp + (c + 3) * wcs), a3);
+                    }
+                    sum += ((a0 + a1) + a2) + a3;
+                }
+                for (int64_t c = c4; c < Cg; ++c) sum = fmaf(__ldg(xp + c * H * Wd), __ldg(wp + c * wcs), sum);
+            }
+        }
+        if (B) sum += __ldg(B + m);
+        Y[i] = sum;
+    }
+}
+
 // Grouped FP8 conv: one output (pixel p = (n, oh, ow), channel m) per thread,
 // m fastest (NHWC output rows). Packed weights Wp[m, (kh * kW + kw) * Cp + c].
 template <int OUT, bool RELU>
@@ -175,5 +227,23 @@ extern "C" int lcml_conv2d_f32(const float *X, const float *W, const float *B, i
     k_conv2d_f32<<<grid_for(total), kThreads, 0, to_cuda(stream)>>>(X, W, B, N, C, H, Wd, M, kH, kW, oH, oW, sH, sW, pH,
                                                                      pW, dH, dW, C / group, M / group, Y);
     LCML_LAUNCHED("conv2d_f32");
+    return LCML_OK;
+}
+
+extern "C" int lcml_conv_transpose2d_f32(const float *X, const float *W, const float *B, int64_t N, int64_t C,
+                                         int64_t H, int64_t Wd, int64_t M, int64_t kH, int64_t kW, int64_t oH,
+                                         int64_t oW, int sH, int sW, int pH, int pW, int dH, int dW, int group,
+                                         float *Y, lcml_stream_t stream) {
+    using namespace lcml;
+    LCML_CHECK_ARG(N >= 0 && C > 0 && H > 0 && Wd > 0 && M > 0 && kH > 0 && kW > 0 && oH >= 0 && oW >= 0 && sH > 0 &&
+                       sW > 0 && dH > 0 && dW > 0 && pH >= 0 && pW >= 0 && group > 0,
+                   "lcml_conv_transpose2d_f32: bad geometry");
+    LCML_CHECK_ARG(C % group == 0 && M % group == 0, "lcml_conv_transpose2d_f32: C and M must be multiples of group");
+    if (N == 0 || oH == 0 || oW == 0) return LCML_OK;
+    LCML_CHECK_ARG(X && W && Y, "lcml_conv_transpose2d_f32: null pointer");
+    const int64_t total = N * M * oH * oW;
+    k_conv_transpose2d_f32<<<grid_for(total), kThreads, 0, to_cuda(stream)>>>(
+        X, W, B, N, C, H, Wd, M, kH, kW, oH, oW, sH, sW, pH, pW, dH, dW, C / group, M / group, Y);
+    LCML_LAUNCHED("conv_transpose2d_f32");
     return LCML_OK;
 }

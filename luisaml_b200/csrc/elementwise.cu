@@ -142,6 +142,56 @@ __global__ void __launch_bounds__(kThreads) k_softmax_rows(const float *__restri
     for (int64_t c = threadIdx.x; c < cols; c += kThreads) y[r * cols + c] = expf(xr[c] - m) / s;
 }
 
+// ---------------------------------------------------------------------------
+// FP8-typed tensors (FLOAT8E4M3FN / FLOAT8E5M2 values without a scale) in
+// Add / Sub / Mul / Div and Softmax: the reference decodes to half, computes
+// and re-encodes (binary.cpp:185-283, softmax.cpp:245-280).
+// ---------------------------------------------------------------------------
+template <int DT>
+__device__ __forceinline__ float fp8_decode(uint32_t b) {
+    return DT == LCML_DTYPE_FLOAT8E5M2 ? e5m2_decode(b) : e4m3_decode(b);
+}
+
+template <int DT>
+__device__ __forceinline__ uint32_t fp8_encode(float v) {
+    return DT == LCML_DTYPE_FLOAT8E5M2 ? e5m2_encode(v) : e4m3_encode(v);
+}
+
+// Binary: both operands decoded (exactly) to half, the op in IEEE half
+// arithmetic (correctly rounded), the half result encoded with the codec.
+template <int OP, int DT>
+__global__ void __launch_bounds__(kThreads) k_binary_fp8(const uint8_t *__restrict__ a, const uint8_t *__restrict__ b,
+                                                         uint8_t *__restrict__ y, int64_t n, int64_t bn) {
+    for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
+         i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+        const __half va = __float2half_rn(fp8_decode<DT>(a[i]));
+        const __half vb = __float2half_rn(fp8_decode<DT>(b[bn == n ? i : i % bn]));
+        const __half r = OP == 0 ? __hadd(va, vb) : OP == 1 ? __hsub(va, vb) : OP == 2 ? __hmul(va, vb) : __hdiv(va, vb);
+        y[i] = static_cast<uint8_t>(fp8_encode<DT>(__half2float(r)));
+    }
+}
+
+// Softmax of an FP8 row: decoded values, max, sum of exp(x - max) and the
+// quotient in fp32 (the reference's half arithmetic and half exp are not
+// reproduced), the result rounded to half and encoded, as the reference
+// encodes a half value.
+template <int DT>
+__global__ void __launch_bounds__(kThreads) k_softmax_rows_fp8(const uint8_t *__restrict__ x, int64_t cols,
+                                                               uint8_t *__restrict__ y) {
+    __shared__ float red[32];
+    const int64_t r = blockIdx.x;
+    const uint8_t *xr = x + r * cols;
+    float m = -INFINITY;
+    for (int64_t c = threadIdx.x; c < cols; c += kThreads) m = fmaxf(m, fp8_decode<DT>(xr[c]));
+    m = block_reduce<true>(m, red);
+    float s = 0.0f;
+    for (int64_t c = threadIdx.x; c < cols; c += kThreads) s += expf(fp8_decode<DT>(xr[c]) - m);
+    s = block_reduce<false>(s, red);
+    for (int64_t c = threadIdx.x; c < cols; c += kThreads)
+        y[r * cols + c] = static_cast<uint8_t>(
+            fp8_encode<DT>(__half2float(__float2half_rn(expf(fp8_decode<DT>(xr[c]) - m) / s))));
+}
+
 // MaxPool 2-D, begin pads, padded taps skipped. E4M3: the code
 // QuantizeLinear gives (at the same positive scale) for the max of the decoded
 // values, i.e. the winning input byte, with -0 written as 0x00; NaN taps lose
@@ -330,6 +380,52 @@ int lcml_reduce_max_rows(const float *x, int64_t rows, int64_t cols, int abs_fir
     LCML_CHECK_ARG(x && y, "lcml_reduce_max_rows: null pointer");
     k_reduce_max_rows<<<static_cast<unsigned>(rows), kThreads, 0, to_cuda(stream)>>>(x, cols, abs_first, y);
     LCML_LAUNCHED("reduce_max_rows");
+    return LCML_OK;
+}
+
+int lcml_binary_fp8(int op, const uint8_t *a, const uint8_t *b, int64_t n, int64_t b_n, uint8_t *y, int dtype,
+                    lcml_stream_t stream) {
+    LCML_CHECK_ARG(op >= 0 && op <= 3, "lcml_binary_fp8: op %d unknown", op);
+    LCML_CHECK_ARG(dtype == LCML_DTYPE_FLOAT8E4M3FN || dtype == LCML_DTYPE_FLOAT8E5M2,
+                   "lcml_binary_fp8: dtype %d (FLOAT8E4M3FN or FLOAT8E5M2)", dtype);
+    LCML_CHECK_ARG(n >= 0 && b_n >= 1, "lcml_binary_fp8: bad extents");
+    if (n == 0) return LCML_OK;
+    LCML_CHECK_ARG(n % b_n == 0, "lcml_binary_fp8: b (%lld) does not broadcast over a (%lld)", (long long)b_n,
+                   (long long)n);
+    LCML_CHECK_ARG(a && b && y, "lcml_binary_fp8: null pointer");
+    const int g = grid_for(n);
+    cudaStream_t st = to_cuda(stream);
+    if (dtype == LCML_DTYPE_FLOAT8E4M3FN) {
+        switch (op) {
+            case 0: k_binary_fp8<0, LCML_DTYPE_FLOAT8E4M3FN><<<g, kThreads, 0, st>>>(a, b, y, n, b_n); break;
+            case 1: k_binary_fp8<1, LCML_DTYPE_FLOAT8E4M3FN><<<g, kThreads, 0, st>>>(a, b, y, n, b_n); break;
+            case 2: k_binary_fp8<2, LCML_DTYPE_FLOAT8E4M3FN><<<g, kThreads, 0, st>>>(a, b, y, n, b_n); break;
+            default: k_binary_fp8<3, LCML_DTYPE_FLOAT8E4M3FN><<<g, kThreads, 0, st>>>(a, b, y, n, b_n); break;
+        }
+    } else {
+        switch (op) {
+            case 0: k_binary_fp8<0, LCML_DTYPE_FLOAT8E5M2><<<g, kThreads, 0, st>>>(a, b, y, n, b_n); break;
+            case 1: k_binary_fp8<1, LCML_DTYPE_FLOAT8E5M2><<<g, kThreads, 0, st>>>(a, b, y, n, b_n); break;
+            case 2: k_binary_fp8<2, LCML_DTYPE_FLOAT8E5M2><<<g, kThreads, 0, st>>>(a, b, y, n, b_n); break;
+            default: k_binary_fp8<3, LCML_DTYPE_FLOAT8E5M2><<<g, kThreads, 0, st>>>(a, b, y, n, b_n); break;
+        }
+    }
+    LCML_LAUNCHED("binary_fp8");
+    return LCML_OK;
+}
+
+int lcml_softmax_rows_fp8(const uint8_t *x, int64_t rows, int64_t cols, uint8_t *y, int dtype, lcml_stream_t stream) {
+    LCML_CHECK_ARG(dtype == LCML_DTYPE_FLOAT8E4M3FN || dtype == LCML_DTYPE_FLOAT8E5M2,
+                   "lcml_softmax_rows_fp8: dtype %d (FLOAT8E4M3FN or FLOAT8E5M2)", dtype);
+    LCML_CHECK_ARG(rows >= 0 && cols >= 1, "lcml_softmax_rows_fp8: bad extents");
+    if (rows == 0) return LCML_OK;
+    LCML_CHECK_ARG(rows <= 0x7fffffff, "lcml_softmax_rows_fp8: too many rows");
+    LCML_CHECK_ARG(x && y, "lcml_softmax_rows_fp8: null pointer");
+    if (dtype == LCML_DTYPE_FLOAT8E4M3FN)
+        k_softmax_rows_fp8<LCML_DTYPE_FLOAT8E4M3FN><<<static_cast<unsigned>(rows), kThreads, 0, to_cuda(stream)>>>(x, cols, y);
+    else
+        k_softmax_rows_fp8<LCML_DTYPE_FLOAT8E5M2><<<static_cast<unsigned>(rows), kThreads, 0, to_cuda(stream)>>>(x, cols, y);
+    LCML_LAUNCHED("softmax_rows_fp8");
     return LCML_OK;
 }
 

@@ -149,22 +149,56 @@ public:
         const ITensor &A = in[0].get(), &B = in[1].get();
         ITensor &Y = out[0].get();
         require(A.dtype() == DataType::FLOAT && B.dtype() == DataType::FLOAT, "MatMul: unfused MatMul runs in FLOAT");
-        require(A.ndim() >= 2 && B.ndim() >= 2, "MatMul: 1-D operands are not supported");
-        const int64_t M = A.shape(A.ndim() - 2), K = A.shape(A.ndim() - 1);
-        const int64_t N = B.shape(B.ndim() - 1);
-        require(B.shape(B.ndim() - 2) == K, "MatMul: inner dimensions mismatch");
-        int64_t batchA = A.size() / (M * K), batchB = B.size() / (K * N);
-        if (batchB == 1) {  // fold A's batch into rows
-            check_status(lcml_gemm_f32(A.ptr<float>(), B.ptr<float>(), nullptr, batchA * M, N, K, 0, 0, 1.0f, 0.0f, -1, 0,
+        require(A.ndim() >= 1 && B.ndim() >= 1, "MatMul: scalar operands");
+        // numpy matmul semantics (mat_mul.cpp:51-303): a 1-D A is [1, K], a 1-D B is [K, 1]
+        // (the extra dimension does not appear in Y); batch dimensions broadcast
+        const int64_t M = A.ndim() >= 2 ? A.shape(A.ndim() - 2) : 1, K = A.shape(A.ndim() - 1);
+        const int64_t N = B.ndim() >= 2 ? B.shape(B.ndim() - 1) : 1;
+        require((B.ndim() >= 2 ? B.shape(B.ndim() - 2) : B.shape(0)) == K, "MatMul: inner dimensions mismatch");
+        const size_t ba = A.ndim() > 2 ? A.ndim() - 2 : 0, bb = B.ndim() > 2 ? B.ndim() - 2 : 0;
+        const size_t nb = std::max(ba, bb);
+        std::vector<int64_t> da(nb, 1), db(nb, 1), dy(nb, 1);
+        for (size_t i = 0; i < ba; ++i) da[nb - ba + i] = A.shape(i);
+        for (size_t i = 0; i < bb; ++i) db[nb - bb + i] = B.shape(i);
+        for (size_t i = 0; i < nb; ++i) {
+            require(da[i] == db[i] || da[i] == 1 || db[i] == 1, "MatMul: batch dimensions do not broadcast");
+            dy[i] = std::max(da[i], db[i]);
+        }
+        int64_t batchY = 1, batchB = 1;
+        for (size_t i = 0; i < nb; ++i) {
+            batchY *= dy[i];
+            batchB *= db[i];
+        }
+        require(Y.size() == batchY * M * N, "MatMul: Y shape mismatch");
+        if (batchB == 1) {  // a 2-D right operand: A's batch folds into rows, one GEMM
+            int64_t batchA = 1;
+            for (auto d : da) batchA *= d;
+            require(batchA == batchY, "MatMul: Y shape mismatch");
+            check_status(lcml_gemm_f32(A.ptr<float>(), B.ptr<float>(), nullptr, batchY * M, N, K, 0, 0, 1.0f, 0.0f, -1, 0,
                                        0, Y.ptr<float>(), stream_),
                          "MatMul");
             return;
         }
-        require(batchA == batchB, "MatMul: only equal batch shapes or a 2-D right operand are supported");
-        for (int64_t b = 0; b < batchA; ++b)
-            check_status(lcml_gemm_f32(A.ptr<float>() + b * M * K, B.ptr<float>() + b * K * N, nullptr, M, N, K, 0, 0, 1.0f,
-                                       0.0f, -1, 0, 0, Y.ptr<float>() + b * M * N, stream_),
+        // one GEMM per output batch, operands found through broadcast strides
+        std::vector<int64_t> sa(nb, 0), sb(nb, 0);
+        for (int64_t i = static_cast<int64_t>(nb) - 1, accA = M * K, accB = K * N; i >= 0; --i) {
+            sa[i] = da[i] == 1 ? 0 : accA;
+            sb[i] = db[i] == 1 ? 0 : accB;
+            accA *= da[i];
+            accB *= db[i];
+        }
+        for (int64_t by = 0; by < batchY; ++by) {
+            int64_t oa = 0, ob = 0, r = by;
+            for (int64_t i = static_cast<int64_t>(nb) - 1; i >= 0; --i) {
+                const int64_t c = r % dy[i];
+                r /= dy[i];
+                oa += c * sa[i];
+                ob += c * sb[i];
+            }
+            check_status(lcml_gemm_f32(A.ptr<float>() + oa, B.ptr<float>() + ob, nullptr, M, N, K, 0, 0, 1.0f, 0.0f, -1, 0,
+                                       0, Y.ptr<float>() + by * M * N, stream_),
                          "MatMul");
+        }
     }
 };
 
@@ -202,15 +236,24 @@ public:
     void forward(Span in, Span out) override {
         const ITensor *a = &in[0].get(), *b = &in[1].get();
         ITensor &y = out[0].get();
-        require(a->dtype() == DataType::FLOAT && b->dtype() == DataType::FLOAT, get_name() + ": FLOAT only on this path");
+        const DataType t = a->dtype();
+        const bool fp8 = t == DataType::FLOAT8E4M3FN || t == DataType::FLOAT8E5M2;
+        require((t == DataType::FLOAT || fp8) && b->dtype() == t && y.dtype() == t,
+                get_name() + ": FLOAT, FLOAT8E4M3FN or FLOAT8E5M2 operands of one type");
         if (a->size() < b->size()) {
             require(op_ == 0 || op_ == 2, get_name() + ": left-operand broadcast is supported for Add and Mul only");
             std::swap(a, b);
         }
         require(trailing_broadcast(*a, *b), get_name() + ": unsupported broadcast");
         require(y.size() == a->size(), get_name() + ": output shape mismatch");
-        check_status(lcml_binary_f32(op_, a->ptr<float>(), b->ptr<float>(), a->size(), b->size(), y.ptr<float>(), stream_),
-                     get_name().c_str());
+        if (fp8)  // decode -> half op -> encode (binary.cpp:185-283)
+            check_status(lcml_binary_fp8(op_, a->ptr<uint8_t>(), b->ptr<uint8_t>(), a->size(), b->size(),
+                                         y.ptr<uint8_t>(), static_cast<int>(t), stream_),
+                         get_name().c_str());
+        else
+            check_status(lcml_binary_f32(op_, a->ptr<float>(), b->ptr<float>(), a->size(), b->size(), y.ptr<float>(),
+                                         stream_),
+                         get_name().c_str());
     }
 };
 
@@ -244,9 +287,16 @@ public:
         const ITensor &x = in[0].get();
         ITensor &y = out[0].get();
         require(norm_axis(axis_, x.ndim()) == x.ndim() - 1, "Softmax: only the last axis is supported");
-        require(x.dtype() == DataType::FLOAT, "Softmax: FLOAT only on this path");
+        const DataType t = x.dtype();
+        require((t == DataType::FLOAT || t == DataType::FLOAT8E4M3FN || t == DataType::FLOAT8E5M2) && y.dtype() == t,
+                "Softmax: FLOAT, FLOAT8E4M3FN or FLOAT8E5M2, the same type in and out");
         const int64_t cols = x.shape(x.ndim() - 1);
-        check_status(lcml_softmax_rows(x.ptr<float>(), x.size() / cols, cols, y.ptr<float>(), stream_), "Softmax");
+        if (t == DataType::FLOAT)
+            check_status(lcml_softmax_rows(x.ptr<float>(), x.size() / cols, cols, y.ptr<float>(), stream_), "Softmax");
+        else  // decode -> softmax -> encode (softmax.cpp:245-280)
+            check_status(lcml_softmax_rows_fp8(x.ptr<uint8_t>(), x.size() / cols, cols, y.ptr<uint8_t>(),
+                                               static_cast<int>(t), stream_),
+                         "Softmax");
     }
 };
 
@@ -354,6 +404,39 @@ public:
                                      x.shape(1), H, W, w.shape(0), kH, kW, oH, oW, sH, sW, pH, pW, dH, dW,
                                      static_cast<int>(group_), y.ptr<float>(), stream_),
                      "Conv");
+    }
+};
+
+// ConvTranspose (src/onnx/operators/conv_transpose.cpp:37-283), fp32, 2-D:
+// the gather kernel lcml_conv_transpose2d_f32; the output extent (pads and
+// output_padding) is the one the graph declares for Y.
+class ConvTranspose : public StreamOperator {
+    std::vector<int64_t> strides_, pads_, dilations_;
+    int64_t group_;
+
+public:
+    ConvTranspose(std::vector<int64_t> strides, std::vector<int64_t> pads, std::vector<int64_t> dilations,
+                  int64_t group)
+        : StreamOperator("ConvTranspose"), strides_(std::move(strides)), pads_(std::move(pads)),
+          dilations_(std::move(dilations)), group_(group) {}
+    void forward(Span in, Span out) override {
+        const ITensor &x = in[0].get(), &w = in[1].get();
+        ITensor &y = out[0].get();
+        require(x.dtype() == DataType::FLOAT && w.dtype() == DataType::FLOAT && y.dtype() == DataType::FLOAT,
+                "ConvTranspose: fp32 tensors");
+        require(x.ndim() == 4 && w.ndim() == 4 && y.ndim() == 4, "ConvTranspose: only 2D is supported");
+        const ITensor *b = in.size() > 2 ? &in[2].get() : nullptr;
+        require(!b || (b->dtype() == DataType::FLOAT && b->size() == y.shape(1)), "ConvTranspose: bias must be fp32 [M]");
+        require(w.shape(0) == x.shape(1) && w.shape(1) * group_ == y.shape(1), "ConvTranspose: W must be [C, M/group, kH, kW]");
+        auto at = [](const std::vector<int64_t> &v, size_t i, int64_t dflt) { return i < v.size() ? v[i] : dflt; };
+        check_status(lcml_conv_transpose2d_f32(x.ptr<float>(), w.ptr<float>(), b ? b->ptr<float>() : nullptr, x.shape(0),
+                                               x.shape(1), x.shape(2), x.shape(3), y.shape(1), w.shape(2), w.shape(3),
+                                               y.shape(2), y.shape(3), static_cast<int>(at(strides_, 0, 1)),
+                                               static_cast<int>(at(strides_, 1, 1)), static_cast<int>(at(pads_, 0, 0)),
+                                               static_cast<int>(at(pads_, 1, 0)), static_cast<int>(at(dilations_, 0, 1)),
+                                               static_cast<int>(at(dilations_, 1, 1)), static_cast<int>(group_),
+                                               y.ptr<float>(), stream_),
+                     "ConvTranspose");
     }
 };
 
@@ -490,6 +573,15 @@ REGISTER_TO_DEFAULT_OPSET(Conv) {
     }
     return std::make_unique<Conv>(get_ints(node, "strides"), get_ints(node, "pads"), get_ints(node, "dilations"),
                                   get_int(node, "group", 1));
+};
+REGISTER_TO_DEFAULT_OPSET(ConvTranspose) {
+    if (auto p = node.try_get_attr("auto_pad")) {
+        const std::string s = p->get<AttributeType::STRING>();
+        if (!s.empty() && s != "NOTSET")
+            throw Error("ConvTranspose: auto_pad " + s + " is not supported (explicit pads only)");
+    }
+    return std::make_unique<ConvTranspose>(get_ints(node, "strides"), get_ints(node, "pads"),
+                                           get_ints(node, "dilations"), get_int(node, "group", 1));
 };
 REGISTER_TO_DEFAULT_OPSET(Relu) { return std::make_unique<Unary>("Relu", 0); };
 REGISTER_TO_DEFAULT_OPSET(Sigmoid) { return std::make_unique<Unary>("Sigmoid", 1); };

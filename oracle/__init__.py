@@ -128,6 +128,15 @@ def cast(x, src: int, dst: int, n: int | None = None) -> np.ndarray:
     return out
 
 
+def binary_fp8(op: int, a, b, dtype: int) -> np.ndarray:
+    """FP8-typed Add/Sub/Mul/Div (op 0..3) with b broadcast over a (binary.cpp:185-283)."""
+    a = np.ascontiguousarray(a, dtype=np.uint8)
+    b = np.ascontiguousarray(b, dtype=np.uint8)
+    y = np.empty(a.shape, dtype=np.uint8)
+    lib.orc_binary_fp8(ctypes.c_int(op), _u(a), _u(b), _i64(a.size), _i64(b.size), _u(y), ctypes.c_int(dtype))
+    return y
+
+
 def e5m2_encode(x) -> np.ndarray:
     x = np.ascontiguousarray(x, dtype=np.float32)
     return np.array([lib.orc_e5m2_from_float(float(v)) for v in x.ravel()], dtype=np.uint8).reshape(x.shape)
@@ -273,6 +282,31 @@ def conv2d(X, W, bias=None, strides=(1, 1), pads=(0, 0, 0, 0), dilations=(1, 1),
     lib.orc_conv2d_f32_lanes(_f(X), _f(W), bptr, _i64(N), _i64(C), _i64(H), _i64(Wd), _i64(M), _i64(kH),
                              _i64(kW), _i64(oH), _i64(oW), ci(sH), ci(sW), ci(pH), ci(pW), ci(dH), ci(dW),
                              ci(group), _f(Y), _i64(n0), _i64(n1), ci(lanes))
+    return Y
+
+
+def conv_transpose2d(X, W, bias=None, strides=(1, 1), pads=(0, 0, 0, 0), dilations=(1, 1), group=1,
+                     output_padding=(0, 0)) -> np.ndarray:
+    """ONNX ConvTranspose (2-D NCHW, W [C, M/group, kH, kW]) following
+    conv_transpose.cpp; output extent (H - 1) * s - pads + d * (k - 1) + 1 + output_padding."""
+    X = np.ascontiguousarray(X, dtype=np.float32)
+    W = np.ascontiguousarray(W, dtype=np.float32)
+    N, C, H, Wd = X.shape
+    _, Mg, kH, kW = W.shape
+    M = Mg * group
+    sH, sW = strides
+    dH, dW = dilations
+    oH = (H - 1) * sH - pads[0] - pads[2] + dH * (kH - 1) + 1 + output_padding[0]
+    oW = (Wd - 1) * sW - pads[1] - pads[3] + dW * (kW - 1) + 1 + output_padding[1]
+    Y = np.empty((N, M, oH, oW), dtype=np.float32)
+    bptr = None
+    if bias is not None:
+        bias = np.ascontiguousarray(bias, dtype=np.float32)
+        bptr = _f(bias)
+    ci = ctypes.c_int
+    lib.orc_conv_transpose2d_f32(_f(X), _f(W), bptr, _i64(N), _i64(C), _i64(H), _i64(Wd), _i64(M), _i64(kH),
+                                 _i64(kW), _i64(oH), _i64(oW), ci(sH), ci(sW), ci(pads[0]), ci(pads[1]), ci(dH),
+                                 ci(dW), ci(group), _f(Y))
     return Y
 
 

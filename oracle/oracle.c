@@ -232,6 +232,27 @@ static uint32_t orc_cast_bits(float v, int dst) {
     return orc_e2m1_from_float(v);
 }
 
+/*
+ * Add/Sub/Mul/Div of FP8-typed tensors (binary.cpp:185-283): both operands
+ * decoded to half (exact), the op in half (_Float16 arithmetic: computed in
+ * float and rounded to half, which is the correctly rounded half result for
+ * these four ops since float carries more than 2 * 11 + 2 bits), the half
+ * result encoded. dtype 17 (e4m3) or 19 (e5m2); b broadcast by b[i % bn].
+ */
+ORC_EXPORT void orc_binary_fp8(int op, const uint8_t *a, const uint8_t *b, int64_t n, int64_t bn, uint8_t *y,
+                               int dtype) {
+    for (int64_t i = 0; i < n; ++i) {
+        float fa = dtype == 19 ? orc_e5m2_to_float(a[i]) : orc_e4m3_to_float(a[i]);
+        float fb = dtype == 19 ? orc_e5m2_to_float(b[i % bn]) : orc_e4m3_to_float(b[i % bn]);
+        _Float16 ha = (_Float16)fa, hb = (_Float16)fb, r;
+        if (op == 0) r = ha + hb;
+        else if (op == 1) r = ha - hb;
+        else if (op == 2) r = ha * hb;
+        else r = ha / hb;
+        y[i] = dtype == 19 ? orc_e5m2_from_float((float)r) : orc_e4m3_from_float((float)r);
+    }
+}
+
 ORC_EXPORT int orc_cast(const void *xv, int src, void *yv, int dst, int64_t n) {
     if (!orc_cast_type_ok(src) || !orc_cast_type_ok(dst)) return -1;
     const uint8_t *x = (const uint8_t *)xv;
@@ -473,6 +494,52 @@ ORC_EXPORT void orc_conv2d_f32_lanes(const float *X, const float *W, const float
                     }
                     if (bias) sum += bias[m];
                     Y[(((n - n0) * M + m) * oH + oh) * oW + ow] = sum;
+                }
+            }
+        }
+    }
+}
+
+/*
+ * ConvTranspose (src/onnx/operators/conv_transpose.cpp), the reference's
+ * gather loop: Y[n, m, oh, ow] = sum over taps (kh, kw) with
+ * oh + pH - kh*dH = ih * sH, 0 <= ih < H (likewise w), of the group's
+ * channels in four lane sums (conv_transpose.cpp:215-232), tail by fma, then
+ * + bias (:270-273). W is [C, M/group, kH, kW].
+ */
+ORC_EXPORT void orc_conv_transpose2d_f32(const float *X, const float *W, const float *bias, int64_t N, int64_t C,
+                                         int64_t H, int64_t Wd, int64_t M, int64_t kH, int64_t kW, int64_t oH,
+                                         int64_t oW, int sH, int sW, int pH, int pW, int dH, int dW, int group,
+                                         float *Y) {
+    int64_t Cg = C / group, Mg = M / group, c4 = (Cg / 4) * 4;
+#pragma omp parallel for collapse(2) schedule(dynamic, 1)
+    for (int64_t n = 0; n < N; ++n) {
+        for (int64_t m = 0; m < M; ++m) {
+            int64_t g = m / Mg, mg = m % Mg;
+            for (int64_t oh = 0; oh < oH; ++oh) {
+                for (int64_t ow = 0; ow < oW; ++ow) {
+                    float sum = 0.0f;
+                    for (int64_t kh = 0; kh < kH; ++kh) {
+                        int64_t ihs = oh + pH - kh * dH;
+                        if (ihs < 0 || ihs % sH != 0 || ihs / sH >= H) continue;
+                        for (int64_t kw = 0; kw < kW; ++kw) {
+                            int64_t iws = ow + pW - kw * dW;
+                            if (iws < 0 || iws % sW != 0 || iws / sW >= Wd) continue;
+                            int64_t ih = ihs / sH, iw = iws / sW;
+#define XV(c) X[((n * C + g * Cg + (c)) * H + ih) * Wd + iw]
+#define WV(c) W[(((g * Cg + (c)) * Mg + mg) * kH + kh) * kW + kw]
+                            if (c4 > 0) {
+                                float a[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+                                for (int64_t c = 0; c < c4; ++c) a[c & 3] = fmaf(XV(c), WV(c), a[c & 3]);
+                                sum += ((a[0] + a[1]) + a[2]) + a[3];
+                            }
+                            for (int64_t c = c4; c < Cg; ++c) sum = fmaf(XV(c), WV(c), sum);
+#undef XV
+#undef WV
+                        }
+                    }
+                    if (bias) sum += bias[m];
+                    Y[((n * M + m) * oH + oh) * oW + ow] = sum;
                 }
             }
         }

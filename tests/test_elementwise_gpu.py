@@ -146,3 +146,62 @@ def test_maxpool_e4m3_qdq_semantics(dev, layout, C):
     if nhwc:
         got = got.transpose(0, 3, 1, 2)
     np.testing.assert_array_equal(got, want)
+
+
+@pytest.mark.parametrize("dtype", [17, 19])
+@pytest.mark.parametrize("op", [0, 1, 2, 3])
+def test_binary_fp8_typed(dev, dtype, op):
+    """Add/Sub/Mul/Div on FP8-typed tensors (binary.cpp:185-283): every pair
+    of codes (256 x 256, decode -> half op -> encode) bit-exact against the
+    oracle, and a row broadcast."""
+    import ctypes
+    import torch
+    import luisaml_b200 as lb
+    codes = np.arange(256, dtype=np.uint8)
+    a = np.repeat(codes, 256)
+    b = np.tile(codes, 256)
+    want = oracle.binary_fp8(op, a, b, dtype)
+    at, bt = _t(a, dev), _t(b, dev)
+    y = torch.empty(a.size, dtype=torch.uint8, device=dev)
+    st = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+    lb.check(lb.lib().lcml_binary_fp8(op, ctypes.c_void_p(at.data_ptr()), ctypes.c_void_p(bt.data_ptr()), a.size,
+                                      b.size, ctypes.c_void_p(y.data_ptr()), dtype, st))
+    np.testing.assert_array_equal(y.cpu().numpy(), want)
+    row = np.arange(0, 256, 3, dtype=np.uint8)  # broadcast of one row over 256 rows
+    a2 = np.random.default_rng(op).integers(0, 256, size=(256, row.size), dtype=np.uint8)
+    want2 = oracle.binary_fp8(op, a2, row, dtype)
+    a2t, rt = _t(a2, dev), _t(row, dev)
+    y2 = torch.empty(a2.shape, dtype=torch.uint8, device=dev)
+    lb.check(lb.lib().lcml_binary_fp8(op, ctypes.c_void_p(a2t.data_ptr()), ctypes.c_void_p(rt.data_ptr()), a2.size,
+                                      row.size, ctypes.c_void_p(y2.data_ptr()), dtype, st))
+    np.testing.assert_array_equal(y2.cpu().numpy(), want2)
+
+
+@pytest.mark.parametrize("dtype", [17, 19])
+def test_softmax_fp8_typed(dev, dtype):
+    """Softmax of an FP8-typed tensor (softmax.cpp:245-280): decode, softmax,
+    encode of the half-rounded result; codes equal to the oracle's fp32
+    softmax of the decoded values except flips to the neighbouring code
+    (exp differs in its last bits between implementations)."""
+    import ctypes
+    import torch
+    import luisaml_b200 as lb
+    rng = np.random.default_rng(dtype)
+    x = (rng.standard_normal((64, 200)) * 3).astype(np.float32)
+    if dtype == 17:
+        xq, dec, enc = oracle.e4m3_encode(x), oracle.e4m3_decode, oracle.e4m3_encode
+    else:
+        xq = oracle.e5m2_encode(x)
+        dec = lambda q: oracle.cast(q, 19, 1).reshape(q.shape)  # noqa: E731
+        enc = oracle.e5m2_encode
+    ref = oracle.softmax_rows(dec(xq)).astype(np.float16).astype(np.float32)
+    want = enc(ref)
+    xt = _t(xq, dev)
+    y = torch.empty(xq.shape, dtype=torch.uint8, device=dev)
+    lb.check(lb.lib().lcml_softmax_rows_fp8(ctypes.c_void_p(xt.data_ptr()), 64, 200, ctypes.c_void_p(y.data_ptr()),
+                                            dtype, ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)))
+    got = y.cpu().numpy()
+    g, w = dec(got).astype(np.float64), dec(want).astype(np.float64)
+    step = np.maximum(np.abs(w) * (0.125 if dtype == 17 else 0.25), 2.0 ** (-9 if dtype == 17 else -16))
+    assert (np.abs(g - w) <= step + 1e-12).all()
+    assert (got == want).mean() > 0.99

@@ -428,3 +428,50 @@ def test_qdq_matmul_graph(dev):
         assert_close(out["y"], ref, what=f"QDQ MatMul fusion={fusion}")
         if fusion:
             assert net.executed_nodes() == 2, net.summary()  # input quantize + one fused GEMM
+
+
+def test_matmul_nd_broadcast_graph(dev):
+    """fp32 MatMul with numpy batch broadcasting (mat_mul.cpp:187-303):
+    [2, 1, 5, 8] @ [3, 8, 4] -> [2, 3, 5, 4], and a 1-D right operand
+    [2, 3, 5, 4] @ [4] -> [2, 3, 5], against numpy in float64."""
+    import torch
+    from luisaml_b200.export import GraphBuilder
+    rng = np.random.default_rng(80)
+    b = GraphBuilder("matmul_nd")
+    b.input("a", "FLOAT", (2, 1, 5, 8))
+    b.input("b", "FLOAT", (3, 8, 4))
+    b.input("v", "FLOAT", (4,))
+    b.output("y", "FLOAT", (2, 3, 5, 4))
+    b.node("MatMul", ["a", "b"], ["y"])
+    b.output("z", "FLOAT", (2, 3, 5))
+    b.node("MatMul", ["y", "v"], ["z"])
+    a = rng.standard_normal((2, 1, 5, 8)).astype(np.float32)
+    bb = rng.standard_normal((3, 8, 4)).astype(np.float32)
+    v = rng.standard_normal(4).astype(np.float32)
+    _, out = _run_graph(dev, b, {"a": a, "b": bb, "v": v},
+                        {"y": ((2, 3, 5, 4), torch.float32), "z": ((2, 3, 5), torch.float32)})
+    want_y = np.matmul(a.astype(np.float64), bb.astype(np.float64))
+    assert_close(out["y"], want_y, rtol=1e-5, atol=1e-5, what="batched matmul")
+    assert_close(out["z"], np.matmul(out["y"].astype(np.float64), v), rtol=1e-5, atol=1e-5, what="matrix-vector")
+
+
+def test_fp8_typed_binary_softmax_graph(dev):
+    """Add and Softmax nodes on FLOAT8E4M3FN-typed tensors (no scales), the
+    reference's quantized Binary / Softmax paths, through NetworkInstance."""
+    import torch
+    from luisaml_b200.export import GraphBuilder
+    rng = np.random.default_rng(81)
+    b = GraphBuilder("fp8_typed")
+    b.input("p", "FLOAT8E4M3FN", (16, 40))
+    b.input("q", "FLOAT8E4M3FN", (40,))
+    s = b.value("s", "FLOAT8E4M3FN", (16, 40))
+    b.node("Add", ["p", "q"], [s])
+    b.output("y", "FLOAT8E4M3FN", (16, 40))
+    b.node("Softmax", [s], ["y"], axis=-1)
+    p = oracle.e4m3_encode((rng.standard_normal((16, 40)) * 2).astype(np.float32))
+    q = oracle.e4m3_encode((rng.standard_normal(40)).astype(np.float32))
+    _, out = _run_graph(dev, b, {"p": p, "q": q}, {"y": ((16, 40), torch.uint8)})
+    sq = oracle.binary_fp8(0, p, q, 17)
+    ref = oracle.e4m3_encode(oracle.softmax_rows(oracle.e4m3_decode(sq)).astype(np.float16).astype(np.float32))
+    g, w = oracle.e4m3_decode(out["y"]).astype(np.float64), oracle.e4m3_decode(ref).astype(np.float64)
+    assert (np.abs(g - w) <= np.maximum(np.abs(w) * 0.125, 2.0 ** -9) + 1e-12).all()

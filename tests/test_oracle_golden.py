@@ -203,3 +203,40 @@ def test_mlp_fixture_both_reference_summation_orders():
     rng = np.random.default_rng(0)
     A, B = rng.standard_normal((16, 301)).astype(np.float32), rng.standard_normal((16, 301)).astype(np.float32)
     assert not np.array_equal(oracle.gemm(A, B, transB=1, lanes=1), oracle.gemm(A, B, transB=1, lanes=4))
+
+
+def test_conv_transpose_matches_scatter_definition():
+    """The gather restatement of ConvTranspose (conv_transpose.cpp) equals
+    the scatter definition y[oh = ih*s - p + kh*d] += x * w in float64."""
+    rng = np.random.default_rng(21)
+    X = rng.standard_normal((2, 6, 5, 4)).astype(np.float32)
+    W = rng.standard_normal((6, 2, 3, 2)).astype(np.float32)  # [C, M/group, kH, kW], group 3 -> M = 6
+    b = rng.standard_normal(6).astype(np.float32)
+    s, p, d, op = (2, 3), (1, 0, 1, 0), (1, 2), (1, 0)
+    Y = oracle.conv_transpose2d(X, W, b, strides=s, pads=p, dilations=d, group=3, output_padding=op)
+    N, C, H, Wd = X.shape
+    oH, oW = Y.shape[2], Y.shape[3]
+    ref = np.zeros((N, 6, oH, oW))
+    for n in range(N):
+        for c in range(C):
+            g = c // 2
+            for mg in range(2):
+                for ih in range(H):
+                    for iw in range(Wd):
+                        for kh in range(3):
+                            for kw in range(2):
+                                oh, ow = ih * s[0] - p[0] + kh * d[0], iw * s[1] - p[1] + kw * d[1]
+                                if 0 <= oh < oH and 0 <= ow < oW:
+                                    ref[n, g * 2 + mg, oh, ow] += float(X[n, c, ih, iw]) * float(W[c, mg, kh, kw])
+    ref += b.reshape(1, 6, 1, 1)
+    np.testing.assert_allclose(Y, ref, rtol=1e-5, atol=1e-5)
+
+
+def test_conv_lane_order_matches_float64():
+    rng = np.random.default_rng(22)
+    X = rng.standard_normal((1, 10, 7, 7)).astype(np.float32)
+    W = rng.standard_normal((3, 10, 3, 3)).astype(np.float32)
+    Y = oracle.conv2d(X, W, pads=(1, 1, 1, 1), lanes=4)
+    ref = oracle.conv2d(X.astype(np.float32), W, pads=(1, 1, 1, 1))
+    np.testing.assert_allclose(Y, ref, rtol=1e-5, atol=1e-5)
+    assert not np.array_equal(Y, ref)  # a different summation order
