@@ -315,6 +315,13 @@ constexpr int stage_bytes_per_warp() { return 2 * 32 * 32 * out_es(OUT); }
 // CTA-pair kernel (long K, shared memory full) keeps them in registers.
 constexpr int kFacSlotBytes = 4 * 32 * 4;
 
+// Column-factor table of the single-CTA kernel: for GEMMs with N <= kTabMaxN
+// (every convolution of ResNet-50) the epilogue warps load each column's
+// factors (B scale times the per-tensor A scale and alpha; beta * C along N)
+// into shared memory once per CTA, so no chunk waits on a global load for
+// them. SILU_MUL GEMMs (the FFN's 22016 columns) keep the per-chunk slots.
+constexpr int kTabMaxN = 2048;
+
 
 // Epilogue warps per CTA: 8 (two per TMEM lane quarter, each taking every
 // other 32-column chunk, so one warp's TMEM and memory latency hides behind
@@ -462,20 +469,28 @@ __device__ __forceinline__ void atomic_max_abs(float *p, float v) {
 // c_first + c_step, ... Chunks past the last output column are skipped; a
 // warp whose rows are all past M does nothing. `stage` is the warp's staging
 // area (its two TMA buffers), `seq` its running chunk count (TMA buffer
-// parity). With FACSLOT the chunk's column factors go through the warp's slot
-// `facw` (gate scale, gate add, up scale, up add): each lane loads those of
-// one column, one chunk ahead, and the element loops read them back as
-// shared-memory broadcasts; without, every lane loads them as broadcast
-// vector loads.
-template <int BN, int EPI, int OUT, bool FACSLOT>
+// parity). Column factors by FAC: kFacTable, the CTA's shared-memory table
+// `facw` of every column (scale with the per-tensor A scale folded in at
+// [n], beta * C at [kTabMaxN + n]), read as broadcasts; kFacSlot, the warp's
+// slot `facw` (gate scale, gate add, up scale, up add), each lane loading
+// those of one column one chunk ahead; kFacLoad, every lane loads them as
+// broadcast vector loads.
+enum FacMode : int { kFacLoad = 0, kFacSlot = 1, kFacTable = 2 };
+
+template <int BN, int EPI, int OUT, int FAC>
 __device__ __forceinline__ void epilogue_tile(const EpiParams &ep, const CUtensorMap *tmY, uint32_t taddr, int64_t row0,
                                               int tn, const OutQuant &oq, uint8_t *stage, uint32_t &seq, int c_first,
                                               int c_step, float *facw) {
+    constexpr bool FACSLOT = FAC == kFacSlot;
     if (row0 >= ep.M) return;
     const int64_t n_out = (EPI == LCML_EPI_SILU_MUL) ? ep.N / 2 : ep.N;
     const int64_t row = row0 + static_cast<int64_t>(threadIdx.x & 31);
     const bool row_ok = row < ep.M;
-    const float row_scale = ep.alpha * (ep.sa_row ? (row_ok ? __ldg(ep.sa + row) : 0.0f) : __ldg(ep.sa));
+    // alpha * the A scale of this row; a per-tensor A scale is folded into the
+    // table's column scales (kFacTable), so nothing is loaded for it here
+    float row_scale = 1.0f;
+    if (ep.sa_row) row_scale = ep.alpha * (row_ok ? __ldg(ep.sa + row) : 0.0f);
+    else if (FAC != kFacTable) row_scale = ep.alpha * __ldg(ep.sa);
     float row_add = 0.0f;  // beta * C broadcast as a scalar or along M
     if (ep.c_vec_mode == 1) row_add = ep.beta * __ldg(ep.c_vec);
     else if (ep.c_vec_mode == 2 && row_ok) row_add = ep.beta * __ldg(ep.c_vec + row);
@@ -517,7 +532,12 @@ __device__ __forceinline__ void epilogue_tile(const EpiParams &ep, const CUtenso
         if (EPI == LCML_EPI_SILU_MUL) tmem_ld_32x32b_x32(taddr + BN / 2 + c * 32, u);
         const ResidualRaw rr = rr_next;
         float v[32];
-        if (FACSLOT) {
+        if (FAC == kFacTable) {
+            if (c + c_step < kChunks) prefetch_residual(ep, row, row_ok, col_of(c + c_step), n_out, res_scale, rr_next);
+            tmem_wait_ld();
+            epi_values<EPI, true, kReluInPack>(ep, row, row_ok, col0, ng0 + BN / 2, n_out, g, g, facw + ng0,
+                                               facw + kTabMaxN + ng0, facw, facw, rr, row_scale, row_add, amax, v);
+        } else if (FACSLOT) {
             facw[lane] = fnext[0];
             facw[32 + lane] = fnext[1];
             if (EPI == LCML_EPI_SILU_MUL) {
@@ -581,6 +601,15 @@ __device__ __forceinline__ void tile_coords(int tile, int num_m, int num_n, int 
     tn = in_group / gsize;
 }
 
+// Bytes of the column-factor table: none for SILU_MUL, and none where it
+// would leave fewer than three operand stages (BN = 256 with fp32 output).
+template <int BN, int EPI, int OUT, int BKB>
+constexpr int tab_bytes() {
+    const int room = kSmemLimit - 2048 - sc_epi_warps<EPI, OUT>() * (stage_bytes_per_warp<OUT>() + kFacSlotBytes) -
+                     2 * kTabMaxN * 4;
+    return (EPI != LCML_EPI_SILU_MUL && room / (BM * BKB + BN * BKB) >= 3) ? 2 * kTabMaxN * 4 : 0;
+}
+
 template <int BN, int STAGES, int EPI, int OUT, int BKB = BK>
 struct Layout {
     static constexpr int kABytes = BM * BKB;
@@ -593,13 +622,16 @@ struct Layout {
     static constexpr int kBarOffset = STAGES * kStageBytes;
     static constexpr int kEpiOffset = kBarOffset + 1024;     // epilogue warps' output staging
     static constexpr int kFacOffset = kEpiOffset + sc_epi_warps<EPI, OUT>() * stage_bytes_per_warp<OUT>();  // factor slots
-    static constexpr int kSmemBytes = kFacOffset + sc_epi_warps<EPI, OUT>() * kFacSlotBytes + 1024;  // +1024 alignment
+    static constexpr int kTabOffset = kFacOffset + sc_epi_warps<EPI, OUT>() * kFacSlotBytes;  // column-factor table
+    static constexpr int kSmemBytes = kTabOffset + tab_bytes<BN, EPI, OUT, BKB>() + 1024;  // +1024 alignment
 };
 
-// The deepest operand ring (at most 8 stages) that fits beside the staging.
+// The deepest operand ring (at most 8 stages) that fits beside the staging
+// and the column-factor table.
 template <int BN, int EPI, int OUT, int BKB = BK>
 constexpr int stages_for() {
-    const int room = kSmemLimit - 2048 - sc_epi_warps<EPI, OUT>() * (stage_bytes_per_warp<OUT>() + kFacSlotBytes);
+    const int room = kSmemLimit - 2048 - sc_epi_warps<EPI, OUT>() * (stage_bytes_per_warp<OUT>() + kFacSlotBytes) -
+                     tab_bytes<BN, EPI, OUT, BKB>();
     const int s = room / (BM * BKB + BN * BKB);
     return s > 8 ? 8 : s;
 }
@@ -790,6 +822,20 @@ __global__ void __launch_bounds__(sc_threads<EPI, OUT>(), 1)
         const OutQuant oq = make_out_quant<OUT>(ep);
         uint8_t *stage = smem + L::kEpiOffset + e * stage_bytes_per_warp<OUT>();
         float *facw = reinterpret_cast<float *>(smem + L::kFacOffset + e * kFacSlotBytes);
+        float *tab = reinterpret_cast<float *>(smem + L::kTabOffset);
+        // every column's factors into the shared table once (N <= kTabMaxN; zero past N up to the chunk edge)
+        constexpr bool kHasTable = tab_bytes<BN, EPI, OUT, BKB>() > 0;
+        const bool use_table = kHasTable && N <= kTabMaxN;
+        if (use_table) {
+            const float fold = ep.sa_row ? 1.0f : ep.alpha * __ldg(ep.sa);
+            const int nfill = ((N + 31) / 32) * 32;
+            for (int n = e * 32 + lane; n < nfill; n += kEW * 32) {
+                const bool ok = n < N;
+                tab[n] = ok ? (ep.sb_col ? __ldg(ep.sb + n) : __ldg(ep.sb)) * fold : 0.0f;
+                tab[kTabMaxN + n] = (ok && ep.c_vec_mode == 3) ? ep.beta * __ldg(ep.c_vec + n) : 0.0f;
+            }
+            named_barrier_sync(1, kEW * 32);  // the epilogue warps only
+        }
         uint32_t seq = 0;
         if (ep.tma_store && lane == 0) tma_prefetch_desc(&tmY);
         int acc = 0;
@@ -801,7 +847,14 @@ __global__ void __launch_bounds__(sc_threads<EPI, OUT>(), 1)
             tc_fence_after();
             const int64_t row0 = static_cast<int64_t>(tm) * BM + quarter * 32;
             const uint32_t taddr = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + static_cast<uint32_t>(acc * BN);
-            epilogue_tile<BN, EPI, OUT, true>(ep, &tmY, taddr, row0, tn, oq, stage, seq, phase_c, kEW / 4, facw);
+            if constexpr (kHasTable) {
+                if (use_table)
+                    epilogue_tile<BN, EPI, OUT, kFacTable>(ep, &tmY, taddr, row0, tn, oq, stage, seq, phase_c, kEW / 4, tab);
+                else
+                    epilogue_tile<BN, EPI, OUT, kFacSlot>(ep, &tmY, taddr, row0, tn, oq, stage, seq, phase_c, kEW / 4, facw);
+            } else {
+                epilogue_tile<BN, EPI, OUT, kFacSlot>(ep, &tmY, taddr, row0, tn, oq, stage, seq, phase_c, kEW / 4, facw);
+            }
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(&tempty[acc]);
@@ -995,8 +1048,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(threads_for<EPI>(), 
             tc_fence_after();
             const int64_t row0 = static_cast<int64_t>(tm) * 256 + rank * 128 + quarter * 32;
             const uint32_t taddr = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + static_cast<uint32_t>(acc * BN);
-            epilogue_tile<BN, EPI, OUT, false>(ep, &tmY, taddr, row0, tn, oq, stage, seq, half, epi_warps<EPI>() / 4,
-                                               nullptr);
+            epilogue_tile<BN, EPI, OUT, kFacLoad>(ep, &tmY, taddr, row0, tn, oq, stage, seq, half, epi_warps<EPI>() / 4,
+                                                  nullptr);
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive_cluster(tempty_leader + 8u * static_cast<uint32_t>(acc));

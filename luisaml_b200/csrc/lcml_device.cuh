@@ -494,6 +494,11 @@ __device__ __forceinline__ void bulk_wait_group_read() {
 // Waits until every bulk group of this thread has completed (writes done).
 __device__ __forceinline__ void bulk_wait_group_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
 
+// Barrier among `nthreads` threads (a multiple of 32) on hardware barrier `id` (1..15).
+__device__ __forceinline__ void named_barrier_sync(int id, int nthreads) {
+    asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
+}
+
 // Barrier among `nthreads` threads (a multiple of 32) on hardware barrier
 // `id` (1..15; 0 is __syncthreads) that also ANDs a per-thread flag: all
 // participants see the same result, so they can leave a loop together.
