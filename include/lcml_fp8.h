@@ -239,11 +239,12 @@ int lcml_fp8_gemm_rowquant(const lcml_fp8_gemm_desc *desc, uint8_t *q, float *q_
  * library (256 KiB per GPU that loads it, held until the process exits).
  * Limit: M <= 65536 rows; larger M is rejected with LCML_ERR_INVALID_ARGUMENT
  * before any work is enqueued. It calls no cudaMalloc / cudaFree.
- * The first call on each device looks up the array's device address
- * (cudaGetSymbolAddress); make that first call before any stream capture.
- * The address is kept for the life of the process, like the library's other
- * per-device state (its device error word): do not cudaDeviceReset a device
- * while this library is in use on it.
+ * Each call looks up the array's device address (cudaGetSymbolAddress), so
+ * the address follows a module reload after cudaDeviceReset; the first call
+ * on a device may load the module, so make it before any stream capture.
+ * The library's other per-device state (its device error word) is kept for
+ * the life of the process: do not cudaDeviceReset a device while this
+ * library is in use on it.
  * All calls share the array and each call zeroes the rows it uses, so calls
  * that overlap on the GPU (e.g. on two streams) race and must be serialised.
  */

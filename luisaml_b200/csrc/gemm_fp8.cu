@@ -463,6 +463,11 @@ __device__ __forceinline__ void atomic_max_abs(float *p, float v) {
     atomicMax(reinterpret_cast<unsigned int *>(p), __float_as_uint(v));
 }
 
+// beta * the DequantizeLinear scale of an e4m3 residual (0 without one).
+__device__ __forceinline__ float residual_scale(const EpiParams &ep) {
+    return (ep.c_mat && ep.c_mat_kind == 2) ? __ldg(ep.c_mat_scale) * ep.beta : 0.0f;
+}
+
 // One output tile's epilogue for the calling warp: TMEM lanes of rows
 // [row0, row0+32) (lane l = row row0 + l) of the accumulator at `taddr` (BN
 // fp32 columns), gemm column block `tn`, 32-column chunks c_first,
@@ -480,7 +485,7 @@ enum FacMode : int { kFacLoad = 0, kFacSlot = 1, kFacTable = 2 };
 template <int BN, int EPI, int OUT, int FAC>
 __device__ __forceinline__ void epilogue_tile(const EpiParams &ep, const CUtensorMap *tmY, uint32_t taddr, int64_t row0,
                                               int tn, const OutQuant &oq, uint8_t *stage, uint32_t &seq, int c_first,
-                                              int c_step, float *facw) {
+                                              int c_step, float *facw, float res_scale) {
     constexpr bool FACSLOT = FAC == kFacSlot;
     if (row0 >= ep.M) return;
     const int64_t n_out = (EPI == LCML_EPI_SILU_MUL) ? ep.N / 2 : ep.N;
@@ -517,7 +522,7 @@ __device__ __forceinline__ void epilogue_tile(const EpiParams &ep, const CUtenso
     // Relu of an e4m3 output is folded into the conversion (pack32)
     constexpr bool kReluInPack = EPI == LCML_EPI_RELU && OUT == kOutE4M3;
     // the residual and the factors of the next chunk are loaded while this one is processed
-    const float res_scale = (ep.c_mat && ep.c_mat_kind == 2) ? __ldg(ep.c_mat_scale) * ep.beta : 0.0f;
+    // (res_scale: beta * the e4m3 residual's scale, loaded once per kernel)
     ResidualRaw rr_next;
     prefetch_residual(ep, row, row_ok, col_of(c_first), n_out, res_scale, rr_next);
     float fnext[4] = {0.0f, 0.0f, 0.0f, 0.0f};
@@ -838,6 +843,7 @@ __global__ void __launch_bounds__(sc_threads<EPI, OUT>(), 1)
         }
         uint32_t seq = 0;
         if (ep.tma_store && lane == 0) tma_prefetch_desc(&tmY);
+        const float res_scale = residual_scale(ep);
         int acc = 0;
         uint32_t acc_phase = 0;
         for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
@@ -849,11 +855,14 @@ __global__ void __launch_bounds__(sc_threads<EPI, OUT>(), 1)
             const uint32_t taddr = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + static_cast<uint32_t>(acc * BN);
             if constexpr (kHasTable) {
                 if (use_table)
-                    epilogue_tile<BN, EPI, OUT, kFacTable>(ep, &tmY, taddr, row0, tn, oq, stage, seq, phase_c, kEW / 4, tab);
+                    epilogue_tile<BN, EPI, OUT, kFacTable>(ep, &tmY, taddr, row0, tn, oq, stage, seq, phase_c, kEW / 4, tab,
+                                                           res_scale);
                 else
-                    epilogue_tile<BN, EPI, OUT, kFacSlot>(ep, &tmY, taddr, row0, tn, oq, stage, seq, phase_c, kEW / 4, facw);
+                    epilogue_tile<BN, EPI, OUT, kFacSlot>(ep, &tmY, taddr, row0, tn, oq, stage, seq, phase_c, kEW / 4, facw,
+                                                          res_scale);
             } else {
-                epilogue_tile<BN, EPI, OUT, kFacSlot>(ep, &tmY, taddr, row0, tn, oq, stage, seq, phase_c, kEW / 4, facw);
+                epilogue_tile<BN, EPI, OUT, kFacSlot>(ep, &tmY, taddr, row0, tn, oq, stage, seq, phase_c, kEW / 4, facw,
+                                                      res_scale);
             }
             tc_fence_before();
             __syncwarp();
@@ -1039,6 +1048,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(threads_for<EPI>(), 
         uint32_t seq = 0;
         if (ep.tma_store && lane == 0) tma_prefetch_desc(&tmY);
         const uint32_t tempty_leader = mapa_shared(smem_u32(&tempty[0]), 0);
+        const float res_scale = residual_scale(ep);
         int acc = 0;
         uint32_t acc_phase = 0;
         for (int tile = pair; tile < num_tiles; tile += npairs) {
@@ -1049,7 +1059,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(threads_for<EPI>(), 
             const int64_t row0 = static_cast<int64_t>(tm) * 256 + rank * 128 + quarter * 32;
             const uint32_t taddr = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + static_cast<uint32_t>(acc * BN);
             epilogue_tile<BN, EPI, OUT, kFacLoad>(ep, &tmY, taddr, row0, tn, oq, stage, seq, half, epi_warps<EPI>() / 4,
-                                                  nullptr);
+                                                  nullptr, res_scale);
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive_cluster(tempty_leader + 8u * static_cast<uint32_t>(acc));
@@ -1775,6 +1785,16 @@ int launch_simt(const lcml_fp8_gemm_desc *d, const EpiParams &ep, cudaStream_t s
     return LCML_OK;
 }
 
+// 128 x 256 single-CTA tiles instead of 128 x 128 where they still give
+// every SM two tiles or more: each epilogue warp then works through four
+// chunks per tile instead of two, so the per-tile start-up (the first
+// chunk's TMEM, factor and residual latency) is paid half as often. On the
+// ResNet-50 1x1 convs (N = 256 / 512, epilogue-bound) this is 10-13 % faster.
+bool wide_tiles(const lcml_fp8_gemm_desc *d) {
+    const int64_t tiles256 = ((d->M + BM - 1) / BM) * ((d->N + 255) / 256);
+    return d->N >= 256 && tiles256 >= 2 * static_cast<int64_t>(sm_count());
+}
+
 template <int EPI, int OUT>
 int dispatch(const lcml_fp8_gemm_desc *d, const EpiParams &ep, cudaStream_t st, bool force_simt, const ConvGeom *geo) {
     if (geo) {  // implicit-GEMM convolution: single-CTA tiles as wide as the output channels
@@ -1783,11 +1803,11 @@ int dispatch(const lcml_fp8_gemm_desc *d, const EpiParams &ep, cudaStream_t st, 
         } else {
             if (geo->C % 128 == 0) {
                 if (d->N <= 64) return launch_tc<64, EPI, OUT, true, 128>(d, ep, st, *geo);
-                if (d->N >= 2048) return launch_tc<256, EPI, OUT, true, 128>(d, ep, st, *geo);
+                if (d->N >= 2048 || wide_tiles(d)) return launch_tc<256, EPI, OUT, true, 128>(d, ep, st, *geo);
                 return launch_tc<128, EPI, OUT, true, 128>(d, ep, st, *geo);
             }
             if (d->N <= 64) return launch_tc<64, EPI, OUT, true, 64>(d, ep, st, *geo);
-            if (d->N >= 2048) return launch_tc<256, EPI, OUT, true, 64>(d, ep, st, *geo);
+            if (d->N >= 2048 || wide_tiles(d)) return launch_tc<256, EPI, OUT, true, 64>(d, ep, st, *geo);
             return launch_tc<128, EPI, OUT, true, 64>(d, ep, st, *geo);
         }
     }
@@ -1814,7 +1834,7 @@ int dispatch(const lcml_fp8_gemm_desc *d, const EpiParams &ep, cudaStream_t st, 
     const int64_t pair_tiles = ((d->M + 255) / 256) * ((d->N + 255) / 256);
     const bool pair = d->M >= 256 && d->N >= 256 && d->K >= 1024 && pair_tiles >= sm_count();
     if ((d->variant & 3) != 1 && ((d->variant & 3) == 2 || pair)) return launch_tc2<EPI, OUT>(d, ep, st);
-    if (EPI == LCML_EPI_SILU_MUL || d->N >= 2048) return launch_tc<256, EPI, OUT>(d, ep, st);
+    if (EPI == LCML_EPI_SILU_MUL || d->N >= 2048 || wide_tiles(d)) return launch_tc<256, EPI, OUT>(d, ep, st);
     if (EPI != LCML_EPI_SILU_MUL && d->N <= 64) return launch_tc<64, EPI, OUT>(d, ep, st);
     return launch_tc<128, EPI, OUT>(d, ep, st);
 }

@@ -2,9 +2,6 @@
 // for callers that cannot give this library any device memory to use as
 // scratch. Its only scratch, the per-row max |value| buffer, lives in a
 // static device array compiled into the library.
-#include <mutex>
-#include <vector>
-
 #include "lcml_internal.h"
 
 // Scratch rows available to the no-allocation entry point. 65536 rows x 4 B
@@ -20,24 +17,17 @@ namespace {
 // The device address of g_noalloc_row_amax on the current device. In host
 // code the array's name only stands in for the device symbol, and its address
 // is not a device address: handing it to a kernel would fault, or on a system
-// where the GPU can reach host memory silently use the wrong memory. So the
-// address is looked up once per device (with that device current) and cached.
+// where the GPU can reach host memory silently use the wrong memory. The
+// address is looked up on every call rather than cached: after a
+// cudaDeviceReset the module is loaded again, possibly elsewhere, and a cached
+// address would dangle. Once the module is loaded the lookup is a table read.
 int noalloc_scratch(float **out) {
-    static std::mutex mu;
-    static std::vector<float *> cache;
-    int dev = 0;
-    LCML_CUDA(cudaGetDevice(&dev));
-    std::lock_guard<std::mutex> lk(mu);
-    if (static_cast<int>(cache.size()) <= dev) cache.resize(dev + 1, nullptr);
-    if (cache[dev] == nullptr) {
-        void *p = nullptr;
-        const cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_row_amax);
-        if (e != cudaSuccess)
-            return lcml::set_error(LCML_ERR_CUDA, "no-allocation scratch: cudaGetSymbolAddress failed: %s",
-                                   cudaGetErrorString(e));
-        cache[dev] = static_cast<float *>(p);
-    }
-    *out = cache[dev];
+    void *p = nullptr;
+    const cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_row_amax);
+    if (e != cudaSuccess)
+        return lcml::set_error(LCML_ERR_CUDA, "no-allocation scratch: cudaGetSymbolAddress failed: %s",
+                               cudaGetErrorString(e));
+    *out = static_cast<float *>(p);
     return LCML_OK;
 }
 
