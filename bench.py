@@ -8,10 +8,11 @@ per-tensor scale (amax(A)/448, computed on the device every step) followed by
 the fused FP8 GEMM against the e4m3 weight B [N,K] (DequantizeLinear of both
 operands and the output cast folded into the epilogue), bf16 output.
 Throughput counts 2*M*N*K FLOP per step. Under torchrun the same 8192^3
-problem is split by output columns across the ranks (strong scaling): each
-rank's GEMM stores its column shard into every rank's output over NVLink
-(the all-gather fused into the epilogue), and a barrier ends the step; time
-is the max over ranks.
+problem is split by rows of A across the ranks (strong scaling): one
+all-reduce of max|A| keeps the one-GPU scale, each rank quantizes its rows,
+and its GEMM stores its rows of Y into every rank's output over NVLink (the
+all-gather fused into the epilogue); a barrier ends the step; time is the
+max over ranks. The `tp_gemm` configuration splits the columns instead.
 
 `--impl reference` times the reference algorithm on the host cores instead
 (the CPU restatement in oracle/, all threads, bounded sample per step): the
@@ -172,12 +173,16 @@ class GemmWorkload:
     computed on the device every step) and the fused FP8 GEMM against the e4m3
     weight B [N, K] (per-tensor scale), bf16 output.
 
-    Under torchrun (WORLD_SIZE > 1) the same problem is split by output
-    columns (strong scaling): every rank quantizes all of A, multiplies it by
-    its 256-column-block shard of B, and its GEMM epilogue stores each output
-    tile into its own full [M, N] output and, over NVLink, into every other
-    rank's (the all-gather fused into the epilogue); a barrier after the GEMM
-    ends the step. One GPU runs the same kernels with no peers."""
+    Under torchrun (WORLD_SIZE > 1) the same problem is split by rows of A
+    (tokens; strong scaling): every rank takes max |A| over its M / N rows,
+    one all-reduce (MAX of one float) gives the whole tensor's amax, the rank
+    quantizes its rows with the resulting scale (the same s as one GPU), and
+    its GEMM against all of B stores each output tile into its own full
+    [M, N] output and, over NVLink, into every other rank's (the all-gather
+    fused into the epilogue); a barrier after the GEMM ends the step. Every
+    rank's Y equals the one-GPU Y bit for bit. Splitting rows rather than
+    columns also splits the quantize of A, which a column split repeats on
+    every rank. One GPU runs the same kernels with no peers."""
 
     def __init__(self, M, N, K, name):
         self.M, self.N, self.K, self.name = M, N, K, name
@@ -189,8 +194,8 @@ class GemmWorkload:
         self.graph_step = M * N * K <= 4096 ** 3 and self.ws == 1
         self.scaling = "strong" if self.ws > 1 else "weak"
         self.same_input_all_ranks = True
-        self.parallelism = (f"N split over {self.ws} ranks; all-gather fused into the GEMM epilogue (P2P stores "
-                            "over NVLink)")
+        self.parallelism = (f"M (token) split over {self.ws} ranks: amax all-reduce, per-rank quantize, GEMM with "
+                            "the all-gather of Y fused into its epilogue (P2P stores over NVLink)")
 
     def describe(self):
         d = {"workload": self.name, "M": self.M, "N": self.N, "K": self.K,
@@ -202,44 +207,50 @@ class GemmWorkload:
                       "GEMM kernel time from a second loop with CUDA events around the GEMM") if self.graph_step
              else "amax + quantize + GEMM C-ABI calls each step; CUDA events around the GEMM inside the step"}
         if self.ws > 1:
-            d["shard_columns_per_rank"] = self.Nr
-            d["step"] += "; then a barrier (all-reduce of one float) after which every rank holds all of Y"
+            d["rows_per_rank"] = self.rows
+            d["step"] = ("amax of the rank's rows, all-reduce MAX (one float), quantize of the rank's rows, GEMM "
+                         "(rank's rows x all of B) storing into every rank's Y; CUDA events around the GEMM; then a "
+                         "barrier (all-reduce of one float) after which every rank holds all of Y")
         return d
 
     def setup(self, dev, seed):
         import torch
         import luisaml_b200 as lb
         from luisaml_b200 import tp
-        g = torch.Generator(device=dev).manual_seed(seed)  # the same A on every rank
-        self.A = torch.randn(self.M, self.K, device=dev, generator=g)
-        start, stop = tp.shard_columns(self.N, self.ws, self.rank)
-        self.start, self.Nr = start, stop - start
-        Bt = tp.column_block_weights(torch, self.K, start, stop, dev, seed + 100, 1.0)
-        bmax = lb.amax(Bt) if Bt.numel() else torch.zeros(1, device=dev)
-        if self.ws > 1:  # the per-tensor scale of the whole B, not of this shard
-            import torch.distributed as dist
-            dist.all_reduce(bmax, op=dist.ReduceOp.MAX)
+        if self.M % self.ws:
+            raise SystemExit(f"M = {self.M} rows do not split evenly over {self.ws} ranks")
+        self.rows = self.M // self.ws
+        self.r0 = self.rank * self.rows
+        g = torch.Generator(device=dev).manual_seed(seed)  # the same A on every rank; each uses its rows
+        A = torch.randn(self.M, self.K, device=dev, generator=g)
+        self.A = A[self.r0:self.r0 + self.rows].clone() if self.ws > 1 else A
+        del A
+        Bt = tp.column_block_weights(torch, self.K, 0, self.N, dev, seed + 100, 1.0)  # all of B on every rank
+        bmax = lb.amax(Bt)
         self.sb = torch.where(bmax > 0, bmax / 448.0, torch.ones_like(bmax))
         self.Bq = lb.quantize(Bt, self.sb)
         del Bt
-        self.flops = 2.0 * self.M * self.N * self.K / self.ws  # per rank
-        self.Aq = torch.empty(self.M, self.K, dtype=torch.uint8, device=dev)
+        self.flops = 2.0 * self.rows * self.N * self.K  # per rank
+        self.Aq = torch.empty(self.rows, self.K, dtype=torch.uint8, device=dev)
         self.sa = torch.empty(1, dtype=torch.float32, device=dev)
         self.amax_ws = torch.empty(lb.TENSOR_DYNAMIC_WORKSPACE_BYTES // 4, dtype=torch.float32, device=dev)
         self.peers = None
         if self.ws > 1:
             import torch.distributed as dist
             self.dist = dist
+            self.amax_t = torch.zeros(1, dtype=torch.float32, device=dev)
             self.peers = tp.PeerOutputs(torch, dist, self.M * self.N * 2, dev)
+            row_off = self.r0 * self.N * 2  # this rank's rows start here in every rank's Y
+            self.peer_rows = (self.peers.peer_array + row_off).contiguous()
             self.barrier_t = torch.zeros(1, device=dev)
             d = lb.GemmDesc()
-            d.M, d.N, d.K = self.M, self.Nr, self.K
+            d.M, d.N, d.K = self.rows, self.N, self.K
             d.A, d.lda, d.B, d.ldb, d.b_kmajor = self.Aq.data_ptr(), self.K, self.Bq.data_ptr(), self.K, 1
             d.scale_a, d.scale_a_mode = self.sa.data_ptr(), lb.SCALE_TENSOR
             d.scale_b, d.scale_b_mode = self.sb.data_ptr(), lb.SCALE_TENSOR
             d.alpha, d.beta = 1.0, 1.0
-            d.Y, d.y_dtype, d.ldy, d.y_col_offset = self.peers.local, lb.DTYPE_BFLOAT16, self.N, start
-            d.y_peers, d.y_num_peers = self.peers.peer_array.data_ptr(), self.ws - 1
+            d.Y, d.y_dtype, d.ldy, d.y_col_offset = self.peers.local + row_off, lb.DTYPE_BFLOAT16, self.N, 0
+            d.y_peers, d.y_num_peers = self.peer_rows.data_ptr(), self.ws - 1
             self.desc = d
         else:
             self.Y = torch.empty(self.M, self.N, dtype=torch.bfloat16, device=dev)
@@ -251,9 +262,17 @@ class GemmWorkload:
         import ctypes
         import luisaml_b200 as lb
         s = ctypes.c_void_p(stream.cuda_stream)
-        lb.check(self.lib.lcml_fp8_quantize_tensor_dynamic(
-            ctypes.c_void_p(self.A.data_ptr()), self.A.numel(), ctypes.c_void_p(self.sa.data_ptr()),
-            ctypes.c_void_p(self.Aq.data_ptr()), ctypes.c_void_p(self.amax_ws.data_ptr()), s))
+        if self.ws > 1:  # amax of this rank's rows -> the whole tensor's amax -> s = amax / 448
+            lb.check(self.lib.lcml_amax(ctypes.c_void_p(self.A.data_ptr()), self.A.numel(),
+                                        ctypes.c_void_p(self.amax_t.data_ptr()), s))
+            self.dist.all_reduce(self.amax_t, op=self.dist.ReduceOp.MAX)
+            lb.check(self.lib.lcml_fp8_quantize_from_amax(
+                ctypes.c_void_p(self.A.data_ptr()), 1, 1, self.A.numel(), ctypes.c_void_p(self.amax_t.data_ptr()),
+                ctypes.c_void_p(self.sa.data_ptr()), ctypes.c_void_p(self.Aq.data_ptr()), s))
+        else:
+            lb.check(self.lib.lcml_fp8_quantize_tensor_dynamic(
+                ctypes.c_void_p(self.A.data_ptr()), self.A.numel(), ctypes.c_void_p(self.sa.data_ptr()),
+                ctypes.c_void_p(self.Aq.data_ptr()), ctypes.c_void_p(self.amax_ws.data_ptr()), s))
         if ev is not None:
             ev[0].record(stream)
         lb.check(self.lib.lcml_fp8_gemm(ctypes.byref(self.desc), s))
@@ -262,13 +281,12 @@ class GemmWorkload:
         if self.ws > 1:
             self.dist.all_reduce(self.barrier_t)  # every shard has landed in every rank's output
 
-    # end to end: pinned host A in, this rank's rows of the bf16 Y out to pinned host, through the C ABI
+    # end to end: this rank's rows of A in from pinned host, its rows of the bf16 Y out to pinned host,
+    # through the C ABI
     def setup_e2e(self):
         import torch
-        self.A_host = self.A.cpu().pin_memory()
-        rows = self.M // self.ws
-        self.r0 = self.rank * rows
-        self.Y_host = torch.empty((rows, self.N), dtype=torch.bfloat16).pin_memory()
+        self.A_host = self.A.cpu().pin_memory()  # this rank's rows of A
+        self.Y_host = torch.empty((self.rows, self.N), dtype=torch.bfloat16).pin_memory()
         self.h2d = self.A_host.numel() * 4
         self.d2h = self.Y_host.numel() * 2
 
@@ -291,7 +309,7 @@ class GemmWorkload:
             return {"kernel": "gemv_fp8" if self.M <= 4 else "gemm_fp8_splitk", "bound": "hbm", "unit": "GB/s",
                     "work": bytes_,
                     "profile": f"gemv_fp8_skinny_{self.M}" if self.M <= 4 else f"gemm_fp8_skinny_{self.M}"}
-        kern = "gemm_fp8_tc2" if self.M >= 2048 else "gemm_fp8_tc"
+        kern = "gemm_fp8_tc2" if self.rows >= 1024 and self.K >= 1024 else "gemm_fp8_tc"
         if self.ws > 1:
             kern += " (+ fused all-gather)"
         return {"kernel": kern, "bound": "tensor", "unit": "TFLOP/s", "work": self.flops,

@@ -91,6 +91,29 @@ __global__ void __launch_bounds__(kThreads) k_repack_nhwc(const uint8_t *__restr
     }
 }
 
+// NCHW with C <= 4 -> NHWC with 4 channels (the stem's image): one thread per
+// 4 consecutive pixels of one image (HW % 4 == 0, X 4-byte aligned), one
+// 4-byte load per channel plane and one 16-byte store, instead of a byte load
+// per (pixel, channel). Same bytes as k_repack_nhwc<I, false> with Cp = 4.
+__global__ void __launch_bounds__(kThreads) k_repack_nchw_c4(const uint8_t *__restrict__ X, int64_t N, int C,
+                                                             int64_t HW, uint8_t *__restrict__ Xc) {
+    const int64_t quads = HW / 4, total = N * quads;
+    for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
+         i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+        const int64_t n = i / quads, hw = (i - n * quads) * 4;
+        uint32_t plane[4] = {0u, 0u, 0u, 0u};
+#pragma unroll
+        for (int c = 0; c < 4; ++c)
+            if (c < C) plane[c] = __ldg(reinterpret_cast<const uint32_t *>(X + (n * C + c) * HW + hw));
+        uint32_t px[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j)  // pixel j: byte c = channel c
+            px[j] = ((plane[0] >> (8 * j)) & 0xffu) | (((plane[1] >> (8 * j)) & 0xffu) << 8) |
+                    (((plane[2] >> (8 * j)) & 0xffu) << 16) | (((plane[3] >> (8 * j)) & 0xffu) << 24);
+        reinterpret_cast<uint4 *>(Xc)[i] = make_uint4(px[0], px[1], px[2], px[3]);
+    }
+}
+
 // im2col from NHWC with C a multiple of 16: one 16-byte vector per (pixel,
 // 16-channel piece of a tap). I is the index type (32-bit when it fits).
 template <typename I>
@@ -156,7 +179,11 @@ __global__ void __launch_bounds__(kThreads) k_im2col_narrow(const uint8_t *__res
 // memory.
 constexpr int kRowThreads = 128;
 
-template <int VW>
+// MAXCH > 0: the chunk loop is unrolled over at most MAXCH chunks (Kp <=
+// 16 * MAXCH), so every tap load of the row is issued before the first one is
+// stored (the ResNet stem, Kp = 208: 49 loads in flight per thread instead of
+// 4); MAXCH = 0 loops over any Kp.
+template <int VW, int MAXCH>
 __global__ void __launch_bounds__(kRowThreads) k_im2col_rows(const uint8_t *__restrict__ X, int H, int W, int kH,
                                                               int kW, int oH, int oW, int sH, int sW, int pH, int pW,
                                                               int dH, int dW, int Kp, int64_t P,
@@ -178,8 +205,8 @@ __global__ void __launch_bounds__(kRowThreads) k_im2col_rows(const uint8_t *__re
             const uint8_t *xn = X + n * H * W * VW;
             uint4 *row = tile + threadIdx.x * chunks;
             int kh = 0, kw = 0, tap = 0;
-            for (int c = 0; c < chunks; ++c) {
-                V v[TPC];
+            // the taps of one 16-byte chunk (zero past the last tap and outside the image)
+            auto gather = [&](V (&v)[TPC]) {
 #pragma unroll
                 for (int j = 0; j < TPC; ++j) {
                     v[j] = V{};
@@ -194,7 +221,21 @@ __global__ void __launch_bounds__(kRowThreads) k_im2col_rows(const uint8_t *__re
                         }
                     }
                 }
-                row[c] = *reinterpret_cast<const uint4 *>(v);
+            };
+            if constexpr (MAXCH > 0) {
+                V v[MAXCH][TPC];
+#pragma unroll
+                for (int c = 0; c < MAXCH; ++c)
+                    if (c < chunks) gather(v[c]);
+#pragma unroll
+                for (int c = 0; c < MAXCH; ++c)
+                    if (c < chunks) row[c] = *reinterpret_cast<const uint4 *>(v[c]);
+            } else {
+                for (int c = 0; c < chunks; ++c) {
+                    V v[TPC];
+                    gather(v);
+                    row[c] = *reinterpret_cast<const uint4 *>(v);
+                }
             }
         }
         __syncthreads();
@@ -252,9 +293,9 @@ int launch_im2col(const lcml_fp8_conv_desc *d, const uint8_t *X, int64_t Cp, int
         int64_t blocks = (P + kRowThreads - 1) / kRowThreads;
         const int64_t cap = static_cast<int64_t>(sm_count()) * 16;
         if (blocks > cap) blocks = cap;
-        auto k4 = k_im2col_rows<4>;
-        auto k8 = k_im2col_rows<8>;
-        auto kern = Cp == 4 ? k4 : k8;
+        const bool unrolled = Kp <= 16 * 16;  // up to 16 chunks: the whole row's loads in flight
+        auto kern = Cp == 4 ? (unrolled ? k_im2col_rows<4, 16> : k_im2col_rows<4, 0>)
+                            : (unrolled ? k_im2col_rows<8, 16> : k_im2col_rows<8, 0>);
         if (const int rc = ensure_max_smem(reinterpret_cast<const void *>(kern), 96 * 1024, "im2col_rows")) return rc;
         kern<<<static_cast<int>(blocks), kRowThreads, static_cast<size_t>(row_smem), st>>>(
             X, static_cast<int>(d->H), static_cast<int>(d->W), static_cast<int>(d->kH), static_cast<int>(d->kW),
@@ -276,6 +317,16 @@ int launch_im2col(const lcml_fp8_conv_desc *d, const uint8_t *X, int64_t Cp, int
 
 template <typename I>
 void launch_repack(const lcml_fp8_conv_desc *d, int64_t Cp, uint8_t *Xc, cudaStream_t st) {
+    const int64_t HW = d->H * d->W;
+    if (!d->x_nhwc && Cp == 4 && HW % 4 == 0 && aligned(d->X, 4)) {
+        // every thread's four plane loads in flight at once: up to 32 blocks of 256 per SM
+        const int64_t items = d->N * (HW / 4);
+        int64_t blocks = (items + kThreads - 1) / kThreads;
+        const int64_t cap = static_cast<int64_t>(sm_count()) * 32;
+        if (blocks > cap) blocks = cap;
+        k_repack_nchw_c4<<<static_cast<int>(blocks), kThreads, 0, st>>>(d->X, d->N, static_cast<int>(d->C), HW, Xc);
+        return;
+    }
     const int grid = grid_for(d->N * d->H * d->W);
     if (d->x_nhwc)
         k_repack_nhwc<I, true><<<grid, kThreads, 0, st>>>(d->X, d->N, d->C, d->H * d->W, Cp, Xc);

@@ -266,10 +266,21 @@ __device__ __forceinline__ uint32_t e4m3_from_order_key4(uint32_t k) {
     return b & ~__vcmpeq4(b, 0x80808080u);
 }
 
+__device__ __forceinline__ void max_keys4(uint4 &acc, const uint4 &v) {
+    acc.x = __vmaxu4(acc.x, e4m3_order_key4(v.x));
+    acc.y = __vmaxu4(acc.y, e4m3_order_key4(v.y));
+    acc.z = __vmaxu4(acc.z, e4m3_order_key4(v.z));
+    acc.w = __vmaxu4(acc.w, e4m3_order_key4(v.w));
+}
+
 // e4m3 NHWC MaxPool with C a multiple of 16: one thread per (output pixel,
 // 16 channels), 16-byte loads, per-byte max on the order keys. Same results as
-// k_maxpool<true, true>. I is the index type.
-template <typename I>
+// k_maxpool<true, true>. I is the index type. KH x KW > 0 fixes the window at
+// compile time: every tap's load is issued before the first max (a window
+// tap outside the image contributes key 0, the identity of the max), so a
+// thread has the whole window in flight instead of one load at a time; 0 x 0
+// reads kH x kW at run time.
+template <typename I, int KH, int KW>
 __global__ void __launch_bounds__(kThreads) k_maxpool_e4m3_nhwc16(const uint8_t *__restrict__ x, I N, I C, I H, I W,
                                                                   int kH, int kW, int sH, int sW, int pH, int pW, I oH,
                                                                   I oW, uint8_t *__restrict__ y) {
@@ -281,17 +292,33 @@ __global__ void __launch_bounds__(kThreads) k_maxpool_e4m3_nhwc16(const uint8_t 
         const I pix = o / groups, g = o - pix * groups;
         const I t = pix / oW, ow = pix - t * oW, n = t / oH, oh = t - n * oH;
         uint4 acc = make_uint4(0, 0, 0, 0);
-        for (int kh = 0; kh < kH; ++kh) {
-            const I ih = oh * sH + kh - pH;
-            if (ih < 0 || ih >= H) continue;
-            for (int kw = 0; kw < kW; ++kw) {
-                const I iw = ow * sW + kw - pW;
-                if (iw < 0 || iw >= W) continue;
-                const uint4 v = __ldg(reinterpret_cast<const uint4 *>(x + ((n * H + ih) * W + iw) * C) + g);
-                acc.x = __vmaxu4(acc.x, e4m3_order_key4(v.x));
-                acc.y = __vmaxu4(acc.y, e4m3_order_key4(v.y));
-                acc.z = __vmaxu4(acc.z, e4m3_order_key4(v.z));
-                acc.w = __vmaxu4(acc.w, e4m3_order_key4(v.w));
+        if constexpr (KH > 0) {
+            uint4 v[KH * KW];
+            bool in[KH * KW];
+#pragma unroll
+            for (int kh = 0; kh < KH; ++kh) {
+                const I ih = oh * sH + kh - pH;
+#pragma unroll
+                for (int kw = 0; kw < KW; ++kw) {
+                    const I iw = ow * sW + kw - pW;
+                    const int k = kh * KW + kw;
+                    in[k] = ih >= 0 && ih < H && iw >= 0 && iw < W;
+                    v[k] = in[k] ? __ldg(reinterpret_cast<const uint4 *>(x + ((n * H + ih) * W + iw) * C) + g)
+                                 : make_uint4(0, 0, 0, 0);
+                }
+            }
+#pragma unroll
+            for (int k = 0; k < KH * KW; ++k)
+                if (in[k]) max_keys4(acc, v[k]);
+        } else {
+            for (int kh = 0; kh < kH; ++kh) {
+                const I ih = oh * sH + kh - pH;
+                if (ih < 0 || ih >= H) continue;
+                for (int kw = 0; kw < kW; ++kw) {
+                    const I iw = ow * sW + kw - pW;
+                    if (iw < 0 || iw >= W) continue;
+                    max_keys4(acc, __ldg(reinterpret_cast<const uint4 *>(x + ((n * H + ih) * W + iw) * C) + g));
+                }
             }
         }
         reinterpret_cast<uint4 *>(y)[o] = make_uint4(e4m3_from_order_key4(acc.x), e4m3_from_order_key4(acc.y),
@@ -319,16 +346,63 @@ __global__ void __launch_bounds__(kThreads) k_gap_nchw(const void *__restrict__ 
     if (threadIdx.x == 0) y[p] = (s * scale) / static_cast<float>(HW);
 }
 
+// Four consecutive channels of element i (i a multiple of 4, the tensor
+// aligned to four elements) as floats, with one vector load.
 template <int DT>
+__device__ __forceinline__ void load_elem4(const void *x, int64_t i, float (&v)[4]) {
+    if (DT == LCML_DTYPE_FLOAT) {
+        const float4 f = __ldg(reinterpret_cast<const float4 *>(static_cast<const float *>(x) + i));
+        v[0] = f.x, v[1] = f.y, v[2] = f.z, v[3] = f.w;
+    } else if (DT == LCML_DTYPE_BFLOAT16) {
+        const uint2 w = __ldg(reinterpret_cast<const uint2 *>(static_cast<const __nv_bfloat16 *>(x) + i));
+        v[0] = __uint_as_float(w.x << 16), v[1] = __uint_as_float(w.x & 0xffff0000u);
+        v[2] = __uint_as_float(w.y << 16), v[3] = __uint_as_float(w.y & 0xffff0000u);
+    } else {
+        const uint32_t w = __ldg(reinterpret_cast<const uint32_t *>(static_cast<const uint8_t *>(x) + i));
+#pragma unroll
+        for (int k = 0; k < 4; ++k) v[k] = e4m3_decode(static_cast<uint8_t>(w >> (8 * k)));
+    }
+}
+
+// NHWC GlobalAveragePool: one thread per (n, CPT channels), each channel
+// summed over HW in pixel order (the order of global_average_pool.cpp's
+// loop). CPT = 4 reads the four channels with one vector load and issues the
+// loads of 8 pixels before adding them, so a thread keeps 8 loads in flight
+// instead of one.
+template <int DT, int CPT>
 __global__ void __launch_bounds__(kThreads) k_gap_nhwc(const void *__restrict__ x, const float *__restrict__ xs,
                                                        int64_t N, int64_t C, int64_t HW, float *__restrict__ y) {
+    const int64_t groups = C / CPT;
     const int64_t tid = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
-    if (tid >= N * C) return;
-    const int64_t n = tid / C, c = tid % C;
-    float s = 0.0f;
-    for (int64_t i = 0; i < HW; ++i) s += load_elem<DT>(x, (n * HW + i) * C + c);
+    if (tid >= N * groups) return;
+    const int64_t n = tid / groups, c = (tid - n * groups) * CPT;
     const float scale = (DT == LCML_DTYPE_FLOAT8E4M3FN) ? __ldg(xs) : 1.0f;
-    y[tid] = (s * scale) / static_cast<float>(HW);
+    if constexpr (CPT == 1) {
+        float s = 0.0f;
+        for (int64_t i = 0; i < HW; ++i) s += load_elem<DT>(x, (n * HW + i) * C + c);
+        y[tid] = (s * scale) / static_cast<float>(HW);
+    } else {
+        constexpr int U = 8;
+        float s[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+        int64_t i = 0;
+        for (; i + U <= HW; i += U) {
+            float v[U][4];
+#pragma unroll
+            for (int u = 0; u < U; ++u) load_elem4<DT>(x, (n * HW + i + u) * C + c, v[u]);
+#pragma unroll
+            for (int u = 0; u < U; ++u)
+#pragma unroll
+                for (int k = 0; k < 4; ++k) s[k] += v[u][k];
+        }
+        for (; i < HW; ++i) {
+            float v[4];
+            load_elem4<DT>(x, (n * HW + i) * C + c, v);
+#pragma unroll
+            for (int k = 0; k < 4; ++k) s[k] += v[k];
+        }
+#pragma unroll
+        for (int k = 0; k < 4; ++k) y[n * C + c + k] = (s[k] * scale) / static_cast<float>(HW);
+    }
 }
 
 }// namespace
@@ -455,14 +529,18 @@ int lcml_maxpool2d(const void *x, int elem_dtype, int64_t NC, int64_t H, int64_t
     if (e4 && x_nhwc && C % 16 == 0 && aligned(x, 16) && aligned(y, 16)) {
         const int64_t N = NC / C;
         const int gv = grid_for(total / 16);
-        if (N * H * W * C < (int64_t(1) << 31))
-            k_maxpool_e4m3_nhwc16<int32_t><<<gv, kThreads, 0, st>>>(
-                static_cast<const uint8_t *>(x), static_cast<int32_t>(N), static_cast<int32_t>(C), static_cast<int32_t>(H),
-                static_cast<int32_t>(W), kH, kW, sH, sW, pH, pW, static_cast<int32_t>(oH), static_cast<int32_t>(oW),
-                static_cast<uint8_t *>(y));
-        else
-            k_maxpool_e4m3_nhwc16<int64_t><<<gv, kThreads, 0, st>>>(static_cast<const uint8_t *>(x), N, C, H, W, kH, kW,
-                                                                    sH, sW, pH, pW, oH, oW, static_cast<uint8_t *>(y));
+        const bool w3 = kH == 3 && kW == 3;
+        if (N * H * W * C < (int64_t(1) << 31)) {
+            auto kern = w3 ? k_maxpool_e4m3_nhwc16<int32_t, 3, 3> : k_maxpool_e4m3_nhwc16<int32_t, 0, 0>;
+            kern<<<gv, kThreads, 0, st>>>(static_cast<const uint8_t *>(x), static_cast<int32_t>(N),
+                                          static_cast<int32_t>(C), static_cast<int32_t>(H), static_cast<int32_t>(W), kH,
+                                          kW, sH, sW, pH, pW, static_cast<int32_t>(oH), static_cast<int32_t>(oW),
+                                          static_cast<uint8_t *>(y));
+        } else {
+            auto kern = w3 ? k_maxpool_e4m3_nhwc16<int64_t, 3, 3> : k_maxpool_e4m3_nhwc16<int64_t, 0, 0>;
+            kern<<<gv, kThreads, 0, st>>>(static_cast<const uint8_t *>(x), N, C, H, W, kH, kW, sH, sW, pH, pW, oH, oW,
+                                          static_cast<uint8_t *>(y));
+        }
     } else if (e4 && x_nhwc) k_maxpool<true, true><<<g, kThreads, 0, st>>>(x, NC, C, H, W, kH, kW, sH, sW, pH, pW, oH, oW, y);
     else if (e4) k_maxpool<true, false><<<g, kThreads, 0, st>>>(x, NC, C, H, W, kH, kW, sH, sW, pH, pW, oH, oW, y);
     else if (x_nhwc) k_maxpool<false, true><<<g, kThreads, 0, st>>>(x, NC, C, H, W, kH, kW, sH, sW, pH, pW, oH, oW, y);
@@ -488,10 +566,18 @@ int lcml_global_avgpool(const void *x, int elem_dtype, const float *x_scale, int
         else if (elem_dtype == LCML_DTYPE_BFLOAT16) k_gap_nchw<LCML_DTYPE_BFLOAT16><<<g, kThreads, 0, st>>>(x, x_scale, HW, y);
         else k_gap_nchw<LCML_DTYPE_FLOAT8E4M3FN><<<g, kThreads, 0, st>>>(x, x_scale, HW, y);
     } else {
-        const unsigned g = static_cast<unsigned>((N * C + kThreads - 1) / kThreads);
-        if (elem_dtype == LCML_DTYPE_FLOAT) k_gap_nhwc<LCML_DTYPE_FLOAT><<<g, kThreads, 0, st>>>(x, x_scale, N, C, HW, y);
-        else if (elem_dtype == LCML_DTYPE_BFLOAT16) k_gap_nhwc<LCML_DTYPE_BFLOAT16><<<g, kThreads, 0, st>>>(x, x_scale, N, C, HW, y);
-        else k_gap_nhwc<LCML_DTYPE_FLOAT8E4M3FN><<<g, kThreads, 0, st>>>(x, x_scale, N, C, HW, y);
+        const int es = elem_dtype == LCML_DTYPE_FLOAT ? 4 : (elem_dtype == LCML_DTYPE_BFLOAT16 ? 2 : 1);
+        const bool v4 = C % 4 == 0 && aligned(x, 4 * es);
+        const unsigned g = static_cast<unsigned>((N * (v4 ? C / 4 : C) + kThreads - 1) / kThreads);
+        if (v4) {
+            if (elem_dtype == LCML_DTYPE_FLOAT) k_gap_nhwc<LCML_DTYPE_FLOAT, 4><<<g, kThreads, 0, st>>>(x, x_scale, N, C, HW, y);
+            else if (elem_dtype == LCML_DTYPE_BFLOAT16) k_gap_nhwc<LCML_DTYPE_BFLOAT16, 4><<<g, kThreads, 0, st>>>(x, x_scale, N, C, HW, y);
+            else k_gap_nhwc<LCML_DTYPE_FLOAT8E4M3FN, 4><<<g, kThreads, 0, st>>>(x, x_scale, N, C, HW, y);
+        } else {
+            if (elem_dtype == LCML_DTYPE_FLOAT) k_gap_nhwc<LCML_DTYPE_FLOAT, 1><<<g, kThreads, 0, st>>>(x, x_scale, N, C, HW, y);
+            else if (elem_dtype == LCML_DTYPE_BFLOAT16) k_gap_nhwc<LCML_DTYPE_BFLOAT16, 1><<<g, kThreads, 0, st>>>(x, x_scale, N, C, HW, y);
+            else k_gap_nhwc<LCML_DTYPE_FLOAT8E4M3FN, 1><<<g, kThreads, 0, st>>>(x, x_scale, N, C, HW, y);
+        }
     }
     LCML_LAUNCHED("global_avgpool");
     return LCML_OK;

@@ -102,6 +102,10 @@ CASES = [
     ("nchw_c8_3x3", 2, 8, 20, 32, 3, 1, 1, False, 1),       # 8-channel taps after the NHWC repack
     ("nhwc_c24_3x3_s2", 2, 24, 19, 48, 3, 2, 1, True, 1),  # C padded to 32
     ("nchw_c32_5x5", 1, 32, 17, 16, 5, 1, 2, False, 1),     # NCHW with 16-byte taps
+    ("stem7x7s2_nchw_odd_hw", 2, 3, 15, 24, 7, 2, 3, False, 1),  # H*W % 4 != 0: the per-pixel repack
+    ("nchw_c2_3x3", 2, 2, 16, 8, 3, 1, 1, False, 1),        # two planes into 4-channel taps
+    ("nchw_c3_9x9", 1, 3, 20, 16, 9, 1, 4, False, 1),       # Kp = 336 > 256: the looped row im2col
+    ("nhwc_c6_7x7_s2", 1, 6, 18, 16, 7, 2, 3, True, 1),     # NHWC repack to 8 channels, Kp = 392
     ("3x3_c16_ragged", 3, 16, 13, 24, 3, 1, 1, True, 1),    # K = 144: a partial last K-block, N = 24
     ("5x5_s2_p2", 2, 48, 23, 96, 5, 2, 2, True, 1),          # taps straddling K-blocks (48-channel taps)
     # implicit GEMM (TMA im2col) edge cases

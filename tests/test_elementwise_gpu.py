@@ -120,12 +120,48 @@ def test_cast_roundtrip(dev):
     assert torch.equal(f, b.float())
 
 
-@pytest.mark.parametrize("layout,C", [("nhwc", 64), ("nhwc", 8), ("nchw", 64)])
-def test_maxpool_e4m3_qdq_semantics(dev, layout, C):
+@pytest.mark.parametrize("C,HW", [(8, 49), (64, 5), (6, 49), (12, 17)])
+@pytest.mark.parametrize("dtype", [1, 16, 17])
+def test_gap_nhwc(dev, dtype, C, HW):
+    """NHWC GlobalAveragePool (the ResNet head's layout) vs the oracle's
+    per-channel sequential sum: C % 4 == 0 takes the four-channel vector
+    kernel (8 pixels per unrolled step plus a tail), the others one channel
+    per thread. fp32 and bf16 inputs sum in the oracle's order: bit-exact;
+    e4m3 sums the codes' values before the scale (rtol 1e-5 / atol 1e-6, as
+    the NCHW test)."""
+    import torch
+    import luisaml_b200 as lb
+    N = 3
+    rng = np.random.default_rng(C * 100 + HW)
+    x = rng.standard_normal((N, HW, C)).astype(np.float32)
+    if dtype == 1:
+        xt, xd, sc = _t(x, dev), x, None
+    elif dtype == 16:
+        xt = _t(x, dev).bfloat16()
+        xd, sc = xt.float().cpu().numpy(), None
+    else:
+        s = np.float32(0.02)
+        q = oracle.quantize(x, s)
+        xt, xd, sc = _t(q, dev), oracle.dequantize(q, s), _t(np.float32([s]), dev)
+    want = oracle.global_avgpool(np.ascontiguousarray(xd.transpose(0, 2, 1)).reshape(N, C, HW, 1)).reshape(N, C)
+    g = torch.empty(N * C, dtype=torch.float32, device=dev)
+    lb.check(lb.lib().lcml_global_avgpool(_p(xt), dtype, _p(sc) if sc is not None else None, N, C, HW, 1, _p(g),
+                                          _s()))
+    got = g.cpu().numpy().reshape(N, C)
+    if dtype == 17:
+        assert_close(got, want, rtol=1e-5, atol=1e-6, what="gap nhwc e4m3")
+    else:
+        np.testing.assert_array_equal(got, want)
+
+
+@pytest.mark.parametrize("layout,C,k,s,p", [("nhwc", 64, 3, 2, 1), ("nhwc", 8, 3, 2, 1), ("nchw", 64, 3, 2, 1),
+                                             ("nhwc", 32, 2, 2, 0), ("nhwc", 16, 3, 1, 1)])
+def test_maxpool_e4m3_qdq_semantics(dev, layout, C, k, s, p):
     """e4m3 MaxPool equals DequantizeLinear -> MaxPool -> QuantizeLinear at the
     same scale: -0 comes out as 0x00, NaN taps are ignored and an all-NaN
-    window gives the saturated -inf code 0xfe. C = 64 NHWC takes the 16-byte
-    vector kernel, the others the scalar one."""
+    window gives the saturated -inf code 0xfe. NHWC with C % 16 == 0 takes the
+    16-byte vector kernel (3x3 windows unrolled at compile time, others read
+    at run time), the others the scalar one."""
     import torch
     import luisaml_b200 as lb
     rng = np.random.default_rng(C)
@@ -134,13 +170,13 @@ def test_maxpool_e4m3_qdq_semantics(dev, layout, C):
     q[rng.random(q.shape) < 0.05] = 0x80
     q[:, :, 4:7, 4:7] = 0x7f   # the window centred at (5, 5) is all NaN
     q[:, :, 10, :] = 0xff
-    oH, oW = (H + 2 - 3) // 2 + 1, (W + 2 - 3) // 2 + 1
-    want = oracle.quantize(oracle.maxpool2d(oracle.e4m3_decode(q).astype(np.float32), (3, 3), (2, 2), (1, 1, 1, 1)),
+    oH, oW = (H + 2 * p - k) // s + 1, (W + 2 * p - k) // s + 1
+    want = oracle.quantize(oracle.maxpool2d(oracle.e4m3_decode(q).astype(np.float32), (k, k), (s, s), (p, p, p, p)),
                            np.float32(1.0))
     nhwc = layout == "nhwc"
     qin = np.ascontiguousarray(q.transpose(0, 2, 3, 1)) if nhwc else q
     y = torch.empty(N * C * oH * oW, dtype=torch.uint8, device=dev)
-    lb.check(lb.lib().lcml_maxpool2d(_p(_t(qin, dev)), 17, N * C, H, W, 3, 3, 2, 2, 1, 1, oH, oW, _p(y), int(nhwc), C,
+    lb.check(lb.lib().lcml_maxpool2d(_p(_t(qin, dev)), 17, N * C, H, W, k, k, s, s, p, p, oH, oW, _p(y), int(nhwc), C,
                                      _s()))
     got = y.cpu().numpy().reshape((N, oH, oW, C) if nhwc else (N, C, oH, oW))
     if nhwc:

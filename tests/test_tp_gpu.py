@@ -152,3 +152,67 @@ def test_same_process_two_devices():
             results.append((Y.cpu().numpy(), got))
     np.testing.assert_array_equal(results[0][0], results[1][0])
     np.testing.assert_array_equal(results[0][1], results[1][1])
+
+
+def _row_split_worker(rank, world, port, q):
+    import datetime
+    import sys
+    import torch
+    import torch.distributed as dist
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0",
+                      WORLD_SIZE=str(world), RANK=str(rank))
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60),
+                            device_id=dev)
+    sys.path.insert(0, os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
+    import bench
+    import luisaml_b200 as lb
+    try:
+        wl = bench.GemmWorkload(1024, 768, 1024, "row_split_test")
+        wl.setup(dev, 77)
+        stream = torch.cuda.current_stream(dev)
+        for _ in range(2):  # the second step overwrites the first's output with the same values
+            wl.step(stream)
+        torch.cuda.synchronize()
+        assert lb.device_error() == 0
+        full = wl.peers.to_host((wl.M, wl.N), torch.bfloat16).view(torch.int16).numpy()
+        rows = [None] * world
+        dist.all_gather_object(rows, wl.A.cpu().numpy())
+        q.put((rank, full, np.concatenate(rows), wl.Bq.cpu().numpy(), float(wl.sb.item()), float(wl.sa.item())))
+        dist.barrier()
+        wl.close()
+    finally:
+        dist.destroy_process_group()
+
+
+def test_row_split_gemm_two_gpus():
+    """The headline GEMM step under torchrun (bench.GemmWorkload, M split over
+    2 ranks): the amax all-reduce gives each rank the whole tensor's scale,
+    and the GEMM epilogue's peer stores leave the full Y on every rank. Both
+    ranks' Y must be equal bit for bit and equal to one GPU running the same
+    problem unsplit (per-tensor dynamic quantize of all of A, then the GEMM)."""
+    import torch
+    import torch.multiprocessing as mp
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    import luisaml_b200 as lb
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_row_split_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = sorted([q.get(timeout=300) for _ in range(2)], key=lambda r: r[0])
+    for p in procs:
+        p.join(timeout=120)
+    assert all(p.exitcode == 0 for p in procs)
+    (_, y0, A, Bq, sb, sa0), (_, y1, _, _, _, sa1) = res
+    np.testing.assert_array_equal(y0, y1)
+    dev = torch.device("cuda", 0)
+    At = torch.from_numpy(A).to(dev)
+    Aq, sa = lb.quantize_tensor_dynamic(At)
+    assert sa.item() == sa0 == sa1
+    Y = lb.gemm(Aq, torch.from_numpy(Bq).to(dev), sa, torch.tensor([sb], device=dev), out_dtype=torch.bfloat16)
+    torch.cuda.synchronize()
+    np.testing.assert_array_equal(Y.view(torch.int16).cpu().numpy(), y0)
