@@ -8,8 +8,8 @@ per-tensor scale (amax(A)/448, computed on the device every step) followed by
 the fused FP8 GEMM against the e4m3 weight B [N,K] (DequantizeLinear of both
 operands and the output cast folded into the epilogue), bf16 output.
 Throughput counts 2*M*N*K FLOP per step. Under torchrun the same 8192^3
-problem is split by rows of A across the ranks (strong scaling): one
-all-reduce of max|A| keeps the one-GPU scale, each rank quantizes its rows,
+problem is split by rows of A across the ranks (strong scaling): a max of
+max|A| over the ranks keeps the one-GPU scale, each rank quantizes its rows,
 and its GEMM stores its rows of Y into every rank's output over NVLink (the
 all-gather fused into the epilogue); a barrier ends the step; time is the
 max over ranks. The `tp_gemm` configuration splits the columns instead.
@@ -175,14 +175,15 @@ class GemmWorkload:
 
     Under torchrun (WORLD_SIZE > 1) the same problem is split by rows of A
     (tokens; strong scaling): every rank takes max |A| over its M / N rows,
-    one all-reduce (MAX of one float) gives the whole tensor's amax, the rank
-    quantizes its rows with the resulting scale (the same s as one GPU), and
-    its GEMM against all of B stores each output tile into its own full
-    [M, N] output and, over NVLink, into every other rank's (the all-gather
-    fused into the epilogue); a barrier after the GEMM ends the step. Every
-    rank's Y equals the one-GPU Y bit for bit. Splitting rows rather than
-    columns also splits the quantize of A, which a column split repeats on
-    every rank. One GPU runs the same kernels with no peers."""
+    one exchange over NVLink (lcml_peer_exchange_max) gives the whole
+    tensor's amax, the rank quantizes its rows with the resulting scale (the
+    same s as one GPU), and its GEMM against all of B stores each output
+    tile into its own full [M, N] output and, over NVLink, into every other
+    rank's (the all-gather fused into the epilogue); a barrier exchange after
+    the GEMM ends the step. Every rank's Y equals the one-GPU Y bit for bit.
+    Splitting rows rather than columns also splits the quantize of A, which
+    a column split repeats on every rank. One GPU runs the same kernels with
+    no peers."""
 
     def __init__(self, M, N, K, name):
         self.M, self.N, self.K, self.name = M, N, K, name
@@ -194,8 +195,8 @@ class GemmWorkload:
         self.graph_step = M * N * K <= 4096 ** 3 and self.ws == 1
         self.scaling = "strong" if self.ws > 1 else "weak"
         self.same_input_all_ranks = True
-        self.parallelism = (f"M (token) split over {self.ws} ranks: amax all-reduce, per-rank quantize, GEMM with "
-                            "the all-gather of Y fused into its epilogue (P2P stores over NVLink)")
+        self.parallelism = (f"M (token) split over {self.ws} ranks: amax exchange, per-rank quantize, GEMM with "
+                            "the all-gather of Y fused into its epilogue (P2P stores over NVLink), barrier exchange")
 
     def describe(self):
         d = {"workload": self.name, "M": self.M, "N": self.N, "K": self.K,
@@ -208,9 +209,10 @@ class GemmWorkload:
              else "amax + quantize + GEMM C-ABI calls each step; CUDA events around the GEMM inside the step"}
         if self.ws > 1:
             d["rows_per_rank"] = self.rows
-            d["step"] = ("amax of the rank's rows, all-reduce MAX (one float), quantize of the rank's rows, GEMM "
-                         "(rank's rows x all of B) storing into every rank's Y; CUDA events around the GEMM; then a "
-                         "barrier (all-reduce of one float) after which every rank holds all of Y")
+            d["step"] = ("amax of the rank's rows, max over the ranks (lcml_peer_exchange_max: one 64-bit NVLink store "
+                         "per peer), quantize of the rank's rows, GEMM (rank's rows x all of B) storing into every "
+                         "rank's Y; CUDA events around the GEMM; then a barrier (the same exchange without a value) "
+                         "after which every rank holds all of Y")
         return d
 
     def setup(self, dev, seed):
@@ -238,7 +240,9 @@ class GemmWorkload:
         if self.ws > 1:
             import torch.distributed as dist
             self.dist = dist
-            self.amax_t = torch.zeros(1, dtype=torch.float32, device=dev)
+            self.amax_t = torch.zeros(1, dtype=torch.float32, device=dev)  # this rank's rows
+            self.amax_g = torch.zeros(1, dtype=torch.float32, device=dev)  # the whole tensor
+            self.xchg = tp.PeerExchange(torch, dist, dev)
             self.peers = tp.PeerOutputs(torch, dist, self.M * self.N * 2, dev)
             row_off = self.r0 * self.N * 2  # this rank's rows start here in every rank's Y
             self.peer_rows = (self.peers.peer_array + row_off).contiguous()
@@ -265,9 +269,9 @@ class GemmWorkload:
         if self.ws > 1:  # amax of this rank's rows -> the whole tensor's amax -> s = amax / 448
             lb.check(self.lib.lcml_amax(ctypes.c_void_p(self.A.data_ptr()), self.A.numel(),
                                         ctypes.c_void_p(self.amax_t.data_ptr()), s))
-            self.dist.all_reduce(self.amax_t, op=self.dist.ReduceOp.MAX)
+            self.xchg.max(self.amax_t.data_ptr(), self.amax_g.data_ptr(), stream.cuda_stream)
             lb.check(self.lib.lcml_fp8_quantize_from_amax(
-                ctypes.c_void_p(self.A.data_ptr()), 1, 1, self.A.numel(), ctypes.c_void_p(self.amax_t.data_ptr()),
+                ctypes.c_void_p(self.A.data_ptr()), 1, 1, self.A.numel(), ctypes.c_void_p(self.amax_g.data_ptr()),
                 ctypes.c_void_p(self.sa.data_ptr()), ctypes.c_void_p(self.Aq.data_ptr()), s))
         else:
             lb.check(self.lib.lcml_fp8_quantize_tensor_dynamic(
@@ -279,7 +283,7 @@ class GemmWorkload:
         if ev is not None:
             ev[1].record(stream)
         if self.ws > 1:
-            self.dist.all_reduce(self.barrier_t)  # every shard has landed in every rank's output
+            self.xchg.barrier(stream.cuda_stream)  # every rank's rows have landed in every rank's output
 
     # end to end: this rank's rows of A in from pinned host, its rows of the bf16 Y out to pinned host,
     # through the C ABI
@@ -302,6 +306,7 @@ class GemmWorkload:
     def close(self):
         if self.peers is not None:
             self.peers.close()
+            self.xchg.close()
 
     def dominant(self):
         if self.M <= 128:  # skinny: streaming B dominates (arithmetic intensity ~2M FLOP/B)

@@ -88,6 +88,24 @@ int lcml_ipc_close(void *device_ptr);
 /* Enables peer access from the current device to `peer_device` (no-op if already on). */
 int lcml_enable_peer_access(int peer_device);
 
+/* Max of one float over the `world` ranks of a peer group, and a barrier
+ * (value = NULL): one single-warp kernel per rank instead of a one-float
+ * collective. No counterpart in the reference (single device). Rank `rank`
+ * stores (epoch, *value) into its slot of every rank's slot array with one
+ * 64-bit release store over NVLink, then waits until every slot of its own
+ * array carries `epoch` and writes the max of the ranks' values to *out.
+ * slots: this rank's array of LCML_PEER_SLOTS_BYTES, zeroed once before the
+ * first call and mapped into every other rank (lcml_ipc_get_handle /
+ * lcml_ipc_open); peer_slots: device array of the other ranks' mapped
+ * arrays in rank order (world - 1 pointers, this rank skipped). Every rank
+ * calls it with the same epoch sequence 1, 2, 3, ... (never 0). The wait is
+ * bounded by timeout_us; a rank that gives up leaves *out unchanged and
+ * records device error 5 (lcml_device_error). The stream's earlier peer
+ * stores are ordered before this rank's slot store. world <= 32. */
+#define LCML_PEER_SLOTS_BYTES 512
+int lcml_peer_exchange_max(const float *value, float *out, uint64_t *slots, uint64_t *const *peer_slots, int rank,
+                           int world, uint32_t epoch, uint32_t timeout_us, lcml_stream_t stream);
+
 /* Device memory and copies for hosts that have no CUDA runtime of their own
  * (the C++ executor allocates intermediates once, at prepare time, through
  * these; the reference gets its buffers from LuisaCompute's Device).

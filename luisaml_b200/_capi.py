@@ -18,6 +18,7 @@ DTYPE_FLOAT = 1
 DTYPE_FLOAT16 = 10
 DTYPE_BFLOAT16 = 16
 DTYPE_E4M3 = 17
+PEER_SLOTS_BYTES = 512  # LCML_PEER_SLOTS_BYTES
 DTYPE_E5M2 = 19
 DTYPE_E2M1 = 23  # packed: two codes per byte, element 2i in the low nibble
 
@@ -105,6 +106,7 @@ PROTOTYPES = {
     "lcml_ipc_open": [_vp, ctypes.POINTER(ctypes.c_void_p)],
     "lcml_ipc_close": [_vp],
     "lcml_enable_peer_access": [_ci],
+    "lcml_peer_exchange_max": [_vp, _vp, _vp, _vp, _ci, _ci, ctypes.c_uint32, ctypes.c_uint32, _vp],
     "lcml_gemm_f32": [_vp, _vp, _vp, _c_i64, _c_i64, _c_i64, _ci, _ci, ctypes.c_float, ctypes.c_float, _ci, _c_i64,
                       _c_i64, _vp, _vp],
     "lcml_gemm_f32_relu": [_vp, _vp, _vp, _c_i64, _c_i64, _c_i64, _ci, _ci, ctypes.c_float, ctypes.c_float, _ci, _c_i64,

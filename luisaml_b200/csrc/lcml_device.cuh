@@ -20,6 +20,7 @@ enum DeviceError : int {
     kDevTimeoutMma = 2,        // MMA issuer waited too long for a loaded stage
     kDevTimeoutEpilogue = 3,   // epilogue waited too long for an accumulator
     kDevTimeoutDrain = 4,      // final drain of in-flight copies timed out
+    kDevTimeoutPeer = 5,       // a peer rank's slot did not reach the expected epoch in time
 };
 
 // The word lives in runtime.cu; kernels receive its device address as a

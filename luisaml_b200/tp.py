@@ -85,3 +85,40 @@ class PeerOutputs:
                                          out.numel() * out.element_size(), 2, None))
         check(self.lib.lcml_stream_synchronize(None))
         return out
+
+
+class PeerExchange:
+    """The step's two small exchanges over NVLink (lcml_peer_exchange_max):
+    the max of one device float across the ranks, and a barrier. Each rank's
+    slot array (LCML_PEER_SLOTS_BYTES) is mapped into every other rank and
+    zeroed before any rank may write into it; every rank then runs the same
+    sequence of exchanges, which numbers them (epochs 1, 2, ...)."""
+
+    def __init__(self, torch, dist, device, timeout_us: int = 2_000_000):
+        lib = _capi.load()
+        self.lib = lib
+        self.world, self.rank = dist.get_world_size(), dist.get_rank()
+        self.timeout_us = timeout_us
+        self.buf = PeerOutputs(torch, dist, _capi.PEER_SLOTS_BYTES, device)
+        check(lib.lcml_memset_async(ctypes.c_void_p(self.buf.local), 0, _capi.PEER_SLOTS_BYTES, None))
+        check(lib.lcml_stream_synchronize(None))
+        dist.barrier()  # every rank's slots are zero before any rank writes into them
+        self.epoch = 0
+
+    def _run(self, value, out, stream):
+        self.epoch += 1
+        check(self.lib.lcml_peer_exchange_max(
+            ctypes.c_void_p(value), ctypes.c_void_p(out), ctypes.c_void_p(self.buf.local),
+            ctypes.c_void_p(self.buf.peer_array.data_ptr()), self.rank, self.world, self.epoch, self.timeout_us,
+            ctypes.c_void_p(stream)))
+
+    def max(self, value_ptr: int, out_ptr: int, stream: int):
+        """*out = max over the ranks of *value (device floats), enqueued on `stream`."""
+        self._run(value_ptr, out_ptr, stream)
+
+    def barrier(self, stream: int):
+        """Returns (on the device) once every rank has reached this point of its stream."""
+        self._run(None, None, stream)
+
+    def close(self):
+        self.buf.close()

@@ -216,3 +216,88 @@ def test_row_split_gemm_two_gpus():
     Y = lb.gemm(Aq, torch.from_numpy(Bq).to(dev), sa, torch.tensor([sb], device=dev), out_dtype=torch.bfloat16)
     torch.cuda.synchronize()
     np.testing.assert_array_equal(Y.view(torch.int16).cpu().numpy(), y0)
+
+
+def test_peer_exchange_one_gpu(dev):
+    """lcml_peer_exchange_max on one GPU: with world = 1 it returns the rank's
+    own value; with world = 2 and a stand-in peer array in local memory that
+    no rank writes back into, rank 0's wait for slot 1 runs out after the
+    20 ms limit: the kernel returns, records device error 5, leaves *out as it
+    was, and has written its own word into the stand-in peer's slot 0."""
+    import ctypes
+    import torch
+    import luisaml_b200 as lb
+    lib = lb.lib()
+    st = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+    p = lambda t: ctypes.c_void_p(t.data_ptr())  # noqa: E731
+    nslot = lb._capi.PEER_SLOTS_BYTES // 8
+    slots = torch.zeros(nslot, dtype=torch.int64, device=dev)
+    val = torch.tensor([3.25], device=dev)
+    out = torch.full((1,), -7.0, device=dev)
+    lb.check(lib.lcml_peer_exchange_max(p(val), p(out), p(slots), None, 0, 1, 1, 1_000_000, st))
+    torch.cuda.synchronize()
+    assert out.item() == 3.25 and lb.device_error() == 0
+    peer = torch.zeros(nslot, dtype=torch.int64, device=dev)
+    peer_ptrs = torch.tensor([peer.data_ptr()], dtype=torch.int64, device=dev)
+    slots.zero_()
+    out.fill_(-7.0)
+    lb.check(lib.lcml_peer_exchange_max(p(val), p(out), p(slots), p(peer_ptrs), 0, 2, 1, 20_000, st))
+    torch.cuda.synchronize()
+    assert lb.device_error() == 5
+    assert out.item() == -7.0
+    word = int(peer[32 + 0].item()) & 0xFFFFFFFFFFFFFFFF  # epoch 1 -> bank 1 (slots 32..63), slot of rank 0
+    assert word >> 32 == 1 and np.uint32(word & 0xFFFFFFFF).view(np.float32) == np.float32(3.25)
+    with pytest.raises(lb._capi.LcmlError):
+        lb.check(lib.lcml_peer_exchange_max(p(val), p(out), p(slots), None, 0, 1, 0, 1000, st))  # epoch 0
+
+
+def _exchange_worker(rank, world, port, q):
+    import datetime
+    import torch
+    import torch.distributed as dist
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60),
+                            device_id=dev)
+    import luisaml_b200 as lb
+    from luisaml_b200 import tp
+    try:
+        x = tp.PeerExchange(torch, dist, dev)
+        stream = torch.cuda.current_stream(dev).cuda_stream
+        got = []
+        out = torch.zeros(1, device=dev)
+        for i in range(6):  # successive epochs use alternate banks; the max moves between the ranks
+            v = torch.tensor([float(10 * i + (rank if i % 2 else world - 1 - rank))], device=dev)
+            x.max(v.data_ptr(), out.data_ptr(), stream)
+            x.barrier(stream)
+            torch.cuda.synchronize()
+            got.append(out.item())
+        q.put((rank, got, lb.device_error()))
+        dist.barrier()
+        x.close()
+    finally:
+        dist.destroy_process_group()
+
+
+def test_peer_exchange_two_gpus():
+    """Max of one float and barriers over NVLink between two ranks, six
+    exchanges (both slot banks, each rank holding the max in turn)."""
+    import torch
+    import torch.multiprocessing as mp
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_exchange_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = [q.get(timeout=300) for _ in range(2)]
+    for p in procs:
+        p.join(timeout=120)
+    assert all(p.exitcode == 0 for p in procs)
+    want = [float(10 * i + 1) for i in range(6)]
+    for rank, got, err in res:
+        assert err == 0, (rank, err)
+        assert got == want, (rank, got)
