@@ -560,6 +560,7 @@ class TpGemmWorkload:
         self.sa = torch.empty(M, dtype=torch.float32, device=dev)
         self.peers = None
         if self.ws > 1 and self.mode == "fused":
+            self.xchg = tp.PeerExchange(torch, dist, dev)
             self.peers = tp.PeerOutputs(torch, dist, M * N * 2, dev)
             ybase, npeers, peer_arr = self.peers.local, self.ws - 1, self.peers.peer_array.data_ptr()
             ldy, off = N, start
@@ -595,7 +596,7 @@ class TpGemmWorkload:
         if ev is not None:
             ev[1].record(stream)
         if self.ws > 1 and self.mode == "fused":
-            self.dist.all_reduce(self.barrier_t)  # every shard has landed in every rank's output
+            self.xchg.barrier(stream.cuda_stream)  # every shard has landed in every rank's output
         elif self.ws > 1:
             self.dist.all_gather_into_tensor(self.gathered, self.Yr.reshape(-1))
             self.Y.copy_(self.gathered.view(self.ws, self.M, self.Nr).permute(1, 0, 2).reshape(self.M, self.N))
@@ -641,6 +642,7 @@ class TpGemmWorkload:
     def close(self):
         if self.peers is not None:
             self.peers.close()
+            self.xchg.close()
 
 
 class ResnetWorkload(GraphWorkload):

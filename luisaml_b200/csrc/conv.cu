@@ -179,6 +179,59 @@ __global__ void __launch_bounds__(kThreads) k_im2col_narrow(const uint8_t *__res
 // memory.
 constexpr int kRowThreads = 128;
 
+// A KH x KW window with dilation 1 over 4-byte pixels (4 channels: the ResNet
+// stem's 7 x 7): the KW taps of one window row are KW consecutive input
+// pixels, so each is a 4-byte load at an immediate offset from one row
+// address, and tap t lands in word t of the patch row (K = (kh, kw, c), c
+// fastest). Every load of the row is issued before the first store, with a
+// few integer operations per tap (the generic kernel spends most of its
+// instructions on per-tap index arithmetic). The patch row is staged in
+// shared memory and written out with coalesced 16-byte stores.
+template <int KH, int KW>
+__global__ void __launch_bounds__(kRowThreads) k_im2col_rows_w4(const uint8_t *__restrict__ X, int H, int W, int oH,
+                                                                 int oW, int sH, int sW, int pH, int pW, int64_t P,
+                                                                 uint8_t *__restrict__ A) {
+    griddep_launch_dependents();  // the next GEMM may start its set-up
+    constexpr int kTaps = KH * KW;
+    constexpr int kChunks = (kTaps + 3) / 4;  // Kp / 16
+    extern __shared__ uint4 tile[];
+    for (int64_t p0 = static_cast<int64_t>(blockIdx.x) * kRowThreads; p0 < P;
+         p0 += static_cast<int64_t>(gridDim.x) * kRowThreads) {
+        const int64_t p = p0 + threadIdx.x;
+        if (p < P) {
+            const int64_t t = p / oW;
+            const int ow = static_cast<int>(p - t * oW);
+            const int64_t n = t / oH;
+            const int oh = static_cast<int>(t - n * oH);
+            const int ih0 = oh * sH - pH, iw0 = ow * sW - pW;
+            const uint32_t *xn = reinterpret_cast<const uint32_t *>(X) + n * H * W;
+            uint32_t v[kChunks * 4];
+#pragma unroll
+            for (int kh = 0; kh < KH; ++kh) {
+                const int ih = ih0 + kh;
+                const bool row_in = static_cast<unsigned>(ih) < static_cast<unsigned>(H);
+                const uint32_t *xr = xn + static_cast<int64_t>(row_in ? ih : 0) * W;
+#pragma unroll
+                for (int kw = 0; kw < KW; ++kw) {
+                    const int iw = iw0 + kw;
+                    v[kh * KW + kw] = (row_in && static_cast<unsigned>(iw) < static_cast<unsigned>(W)) ? __ldg(xr + iw) : 0u;
+                }
+            }
+#pragma unroll
+            for (int k = kTaps; k < kChunks * 4; ++k) v[k] = 0u;
+            uint4 *row = tile + threadIdx.x * kChunks;
+#pragma unroll
+            for (int c = 0; c < kChunks; ++c) row[c] = make_uint4(v[4 * c], v[4 * c + 1], v[4 * c + 2], v[4 * c + 3]);
+        }
+        __syncthreads();
+        const int64_t rows = P - p0 < kRowThreads ? P - p0 : kRowThreads;
+        uint4 *dst = reinterpret_cast<uint4 *>(A + p0 * kChunks * 16);
+        const int64_t vecs = rows * kChunks;
+        for (int64_t i = threadIdx.x; i < vecs; i += kRowThreads) dst[i] = tile[i];
+        __syncthreads();
+    }
+}
+
 // MAXCH > 0: the chunk loop is unrolled over at most MAXCH chunks (Kp <=
 // 16 * MAXCH), so every tap load of the row is issued before the first one is
 // stored (the ResNet stem, Kp = 208: 49 loads in flight per thread instead of
@@ -293,6 +346,15 @@ int launch_im2col(const lcml_fp8_conv_desc *d, const uint8_t *X, int64_t Cp, int
         int64_t blocks = (P + kRowThreads - 1) / kRowThreads;
         const int64_t cap = static_cast<int64_t>(sm_count()) * 16;
         if (blocks > cap) blocks = cap;
+        if (Cp == 4 && d->kH == 7 && d->kW == 7 && d->dH == 1 && d->dW == 1) {  // the stem
+            auto k77 = k_im2col_rows_w4<7, 7>;
+            if (const int rc = ensure_max_smem(reinterpret_cast<const void *>(k77), 96 * 1024, "im2col_rows_w4"))
+                return rc;
+            k77<<<static_cast<int>(blocks), kRowThreads, static_cast<size_t>(row_smem), st>>>(
+                X, static_cast<int>(d->H), static_cast<int>(d->W), static_cast<int>(d->oH), static_cast<int>(d->oW),
+                d->sH, d->sW, d->pH, d->pW, P, A);
+            return LCML_OK;
+        }
         const bool unrolled = Kp <= 16 * 16;  // up to 16 chunks: the whole row's loads in flight
         auto kern = Cp == 4 ? (unrolled ? k_im2col_rows<4, 16> : k_im2col_rows<4, 0>)
                             : (unrolled ? k_im2col_rows<8, 16> : k_im2col_rows<8, 0>);

@@ -246,40 +246,62 @@ __global__ void __launch_bounds__(kThreads) k_maxpool(const void *__restrict__ x
     }
 }
 
-// e4m3 codes -> bytes whose unsigned order is the order of the decoded
-// values (4 per word): NaN -> 0, negatives -> 0x7f - |code|, others -> code + 0x80.
-__device__ __forceinline__ uint32_t e4m3_order_key4(uint32_t w) {
-    const uint32_t neg = __vcmpgeu4(w, 0x80808080u);
-    const uint32_t mag = w & 0x7f7f7f7fu;
-    const uint32_t nan = __vcmpeq4(mag, 0x7f7f7f7fu);
-    const uint32_t key = ((0x7f7f7f7fu - mag) & neg) | ((w ^ 0x80808080u) & ~neg);
-    return key & ~nan;
+// Max of e4m3 codes through f16x2: every e4m3 value, -0 and NaN included, is
+// exact in f16 (the hardware conversions both ways are exact for them), and
+// max.f16x2 returns the other operand when one is NaN, so NaN taps drop out
+// as MaxPool of the dequantized values ignores them. The running max starts
+// at -448 (code 0xfe), which is also the result of a window that holds only
+// NaN codes or lies outside the image. A 16-byte vector is 8 f16x2 words.
+constexpr uint32_t kF16x2Neg448 = 0xDF00DF00u;  // two f16 -448.0
+
+__device__ __forceinline__ void e4m3x4_to_f16x2(uint32_t w, uint32_t &lo, uint32_t &hi) {
+    asm("{\n\t.reg .b16 a, b;\n\t"
+        "mov.b32 {a, b}, %2;\n\t"
+        "cvt.rn.f16x2.e4m3x2 %0, a;\n\t"
+        "cvt.rn.f16x2.e4m3x2 %1, b;\n\t}"
+        : "=r"(lo), "=r"(hi)
+        : "r"(w));
 }
 
-// Inverse of e4m3_order_key4 with the MaxPool conventions: key 0 (only NaN
-// or nothing seen) -> 0xfe, -0 -> 0x00.
-__device__ __forceinline__ uint32_t e4m3_from_order_key4(uint32_t k) {
-    const uint32_t lt = __vcmpltu4(k, 0x80808080u);
-    uint32_t b = (~k & lt) | ((k ^ 0x80808080u) & ~lt);
-    const uint32_t z = __vcmpeq4(k, 0u);
-    b = (b & ~z) | (0xfefefefeu & z);
-    return b & ~__vcmpeq4(b, 0x80808080u);
+// -0 -> +0 (adding +0 under round-to-nearest), then back to four codes.
+__device__ __forceinline__ uint32_t f16x2_to_e4m3x4(uint32_t lo, uint32_t hi) {
+    uint32_t out;
+    asm("{\n\t.reg .b16 a, b;\n\t.reg .b32 l, h, z;\n\t"
+        "mov.b32 z, 0;\n\t"
+        "add.rn.f16x2 l, %1, z;\n\t"
+        "add.rn.f16x2 h, %2, z;\n\t"
+        "cvt.rn.satfinite.e4m3x2.f16x2 a, l;\n\t"
+        "cvt.rn.satfinite.e4m3x2.f16x2 b, h;\n\t"
+        "mov.b32 %0, {a, b};\n\t}"
+        : "=r"(out)
+        : "r"(lo), "r"(hi));
+    return out;
 }
 
-__device__ __forceinline__ void max_keys4(uint4 &acc, const uint4 &v) {
-    acc.x = __vmaxu4(acc.x, e4m3_order_key4(v.x));
-    acc.y = __vmaxu4(acc.y, e4m3_order_key4(v.y));
-    acc.z = __vmaxu4(acc.z, e4m3_order_key4(v.z));
-    acc.w = __vmaxu4(acc.w, e4m3_order_key4(v.w));
+__device__ __forceinline__ uint32_t hmax2_bits(uint32_t a, uint32_t b) {
+    uint32_t d;
+    asm("max.f16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+    return d;
+}
+
+// acc[8] (f16x2) = max(acc, the 16 codes of v)
+__device__ __forceinline__ void max_codes16(uint32_t (&acc)[8], const uint4 &v) {
+    const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+        uint32_t lo, hi;
+        e4m3x4_to_f16x2(w[j], lo, hi);
+        acc[2 * j] = hmax2_bits(acc[2 * j], lo);
+        acc[2 * j + 1] = hmax2_bits(acc[2 * j + 1], hi);
+    }
 }
 
 // e4m3 NHWC MaxPool with C a multiple of 16: one thread per (output pixel,
-// 16 channels), 16-byte loads, per-byte max on the order keys. Same results as
-// k_maxpool<true, true>. I is the index type. KH x KW > 0 fixes the window at
-// compile time: every tap's load is issued before the first max (a window
-// tap outside the image contributes key 0, the identity of the max), so a
-// thread has the whole window in flight instead of one load at a time; 0 x 0
-// reads kH x kW at run time.
+// 16 channels), 16-byte loads, the max taken in f16x2 (above). Same results
+// as k_maxpool<true, true>. I is the index type. KH x KW > 0 fixes the window
+// at compile time: every tap's load is issued before the first max (a tap
+// outside the image reads as code 0xfe, which changes no max), so a thread
+// has the whole window in flight; 0 x 0 reads kH x kW at run time.
 template <typename I, int KH, int KW>
 __global__ void __launch_bounds__(kThreads) k_maxpool_e4m3_nhwc16(const uint8_t *__restrict__ x, I N, I C, I H, I W,
                                                                   int kH, int kW, int sH, int sW, int pH, int pW, I oH,
@@ -291,25 +313,25 @@ __global__ void __launch_bounds__(kThreads) k_maxpool_e4m3_nhwc16(const uint8_t 
          o += static_cast<I>(gridDim.x) * blockDim.x) {
         const I pix = o / groups, g = o - pix * groups;
         const I t = pix / oW, ow = pix - t * oW, n = t / oH, oh = t - n * oH;
-        uint4 acc = make_uint4(0, 0, 0, 0);
+        uint32_t acc[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) acc[j] = kF16x2Neg448;
         if constexpr (KH > 0) {
+            constexpr uint32_t kNeg = 0xfefefefeu;  // four codes of -448
             uint4 v[KH * KW];
-            bool in[KH * KW];
 #pragma unroll
             for (int kh = 0; kh < KH; ++kh) {
                 const I ih = oh * sH + kh - pH;
 #pragma unroll
                 for (int kw = 0; kw < KW; ++kw) {
                     const I iw = ow * sW + kw - pW;
-                    const int k = kh * KW + kw;
-                    in[k] = ih >= 0 && ih < H && iw >= 0 && iw < W;
-                    v[k] = in[k] ? __ldg(reinterpret_cast<const uint4 *>(x + ((n * H + ih) * W + iw) * C) + g)
-                                 : make_uint4(0, 0, 0, 0);
+                    const bool in = ih >= 0 && ih < H && iw >= 0 && iw < W;
+                    v[kh * KW + kw] = in ? __ldg(reinterpret_cast<const uint4 *>(x + ((n * H + ih) * W + iw) * C) + g)
+                                         : make_uint4(kNeg, kNeg, kNeg, kNeg);
                 }
             }
 #pragma unroll
-            for (int k = 0; k < KH * KW; ++k)
-                if (in[k]) max_keys4(acc, v[k]);
+            for (int k = 0; k < KH * KW; ++k) max_codes16(acc, v[k]);
         } else {
             for (int kh = 0; kh < kH; ++kh) {
                 const I ih = oh * sH + kh - pH;
@@ -317,12 +339,12 @@ __global__ void __launch_bounds__(kThreads) k_maxpool_e4m3_nhwc16(const uint8_t 
                 for (int kw = 0; kw < kW; ++kw) {
                     const I iw = ow * sW + kw - pW;
                     if (iw < 0 || iw >= W) continue;
-                    max_keys4(acc, __ldg(reinterpret_cast<const uint4 *>(x + ((n * H + ih) * W + iw) * C) + g));
+                    max_codes16(acc, __ldg(reinterpret_cast<const uint4 *>(x + ((n * H + ih) * W + iw) * C) + g));
                 }
             }
         }
-        reinterpret_cast<uint4 *>(y)[o] = make_uint4(e4m3_from_order_key4(acc.x), e4m3_from_order_key4(acc.y),
-                                                     e4m3_from_order_key4(acc.z), e4m3_from_order_key4(acc.w));
+        reinterpret_cast<uint4 *>(y)[o] = make_uint4(f16x2_to_e4m3x4(acc[0], acc[1]), f16x2_to_e4m3x4(acc[2], acc[3]),
+                                                     f16x2_to_e4m3x4(acc[4], acc[5]), f16x2_to_e4m3x4(acc[6], acc[7]));
     }
 }
 
@@ -381,6 +403,27 @@ __global__ void __launch_bounds__(kThreads) k_gap_nhwc(const void *__restrict__ 
         float s = 0.0f;
         for (int64_t i = 0; i < HW; ++i) s += load_elem<DT>(x, (n * HW + i) * C + c);
         y[tid] = (s * scale) / static_cast<float>(HW);
+    } else if (DT == LCML_DTYPE_FLOAT8E4M3FN && HW <= 64) {
+        // e4m3 with at most 64 pixels (the ResNet head: 7 x 7): every pixel's
+        // 4-code word is loaded before the first add, so the whole sum waits
+        // on one memory latency; the adds then run in pixel order
+        uint32_t w[64];
+        const uint32_t *px = reinterpret_cast<const uint32_t *>(static_cast<const uint8_t *>(x) + n * HW * C + c);
+        const int64_t cw = C / 4;  // words per pixel
+#pragma unroll
+        for (int i = 0; i < 64; ++i) w[i] = i < HW ? __ldg(px + i * cw) : 0u;
+        float s[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+#pragma unroll
+        for (int i = 0; i < 64; ++i)
+            if (i < HW) {  // hardware decode through f16x2 (exact for every code)
+                float d[4];
+                e4m3x2_decode(w[i], d[0], d[1]);
+                e4m3x2_decode(w[i] >> 16, d[2], d[3]);
+#pragma unroll
+                for (int k = 0; k < 4; ++k) s[k] += d[k];
+            }
+#pragma unroll
+        for (int k = 0; k < 4; ++k) y[n * C + c + k] = (s[k] * scale) / static_cast<float>(HW);
     } else {
         constexpr int U = 8;
         float s[4] = {0.0f, 0.0f, 0.0f, 0.0f};

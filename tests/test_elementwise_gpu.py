@@ -120,13 +120,14 @@ def test_cast_roundtrip(dev):
     assert torch.equal(f, b.float())
 
 
-@pytest.mark.parametrize("C,HW", [(8, 49), (64, 5), (6, 49), (12, 17)])
+@pytest.mark.parametrize("C,HW", [(8, 49), (64, 5), (6, 49), (12, 17), (8, 100)])
 @pytest.mark.parametrize("dtype", [1, 16, 17])
 def test_gap_nhwc(dev, dtype, C, HW):
     """NHWC GlobalAveragePool (the ResNet head's layout) vs the oracle's
     per-channel sequential sum: C % 4 == 0 takes the four-channel vector
-    kernel (8 pixels per unrolled step plus a tail), the others one channel
-    per thread. fp32 and bf16 inputs sum in the oracle's order: bit-exact;
+    kernel (e4m3 with HW <= 64: all pixels loaded up front; otherwise 8
+    pixels per unrolled step plus a tail), the others one channel per
+    thread. fp32 and bf16 inputs sum in the oracle's order: bit-exact;
     e4m3 sums the codes' values before the scale (rtol 1e-5 / atol 1e-6, as
     the NCHW test)."""
     import torch
