@@ -285,23 +285,87 @@ class GemmWorkload:
         if self.ws > 1:
             self.xchg.barrier(stream.cuda_stream)  # every rank's rows have landed in every rank's output
 
-    # end to end: this rank's rows of A in from pinned host, its rows of the bf16 Y out to pinned host,
-    # through the C ABI
+    # End to end through the C ABI: every step copies this rank's rows of A in
+    # from pinned host memory and its rows of the bf16 Y out to pinned host
+    # memory. On one GPU the steps are pipelined over two slots of A and Y:
+    # step i's host-to-device copy (one stream) and step i-1's device-to-host
+    # copy (another) run while the compute stream quantizes and multiplies,
+    # with events keeping each slot's copy, quantize, GEMM and read-back in
+    # order (the executor's host-staged I/O does the same for the graphs).
+    # Every step still moves all of its bytes; the copies of different steps
+    # overlap each other and the compute. Under torchrun, and for steps that
+    # copy less than 8 MB, the steps run in sequence on one stream.
     def setup_e2e(self):
+        import ctypes
         import torch
         self.A_host = self.A.cpu().pin_memory()  # this rank's rows of A
-        self.Y_host = torch.empty((self.rows, self.N), dtype=torch.bfloat16).pin_memory()
         self.h2d = self.A_host.numel() * 4
-        self.d2h = self.Y_host.numel() * 2
+        self.d2h = self.rows * self.N * 2
+        # pipelining pays for large copies; a step of a few KB is launch-bound
+        # and only gains the extra events and stream waits
+        self.pipelined = self.ws == 1 and self.h2d + self.d2h >= (8 << 20)
+        if not self.pipelined:
+            self.Y_host = torch.empty((self.rows, self.N), dtype=torch.bfloat16).pin_memory()
+            return
+        dev = self.A.device
+        self.e2e_path = ("pinned host A -> H2D (copy stream) -> amax + quantize + GEMM (compute stream) -> D2H of Y "
+                         "(second copy stream), two slots, consecutive steps overlapped")
+        self.slot_A = [self.A, torch.empty_like(self.A)]
+        self.slot_Y = [self.Y, torch.empty_like(self.Y)]
+        d2 = type(self.desc)()
+        ctypes.memmove(ctypes.byref(d2), ctypes.byref(self.desc), ctypes.sizeof(d2))
+        d2.Y = self.slot_Y[1].data_ptr()
+        self.slot_desc = [self.desc, d2]
+        self.slot_Yh = [torch.empty((self.rows, self.N), dtype=torch.bfloat16).pin_memory() for _ in range(2)]
+        self.s_in, self.s_out = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
+        ev = lambda: [torch.cuda.Event(), torch.cuda.Event()]  # noqa: E731
+        self.ev_ready, self.ev_read, self.ev_ydone, self.ev_out = ev(), ev(), ev(), ev()
+        self.used = [False, False]
+        self.e2e_i = 0
+
+    def e2e_begin(self, stream):
+        if getattr(self, "pipelined", False):  # the copy streams start after the timed region's first event
+            self.s_in.wait_stream(stream)
+            self.s_out.wait_stream(stream)
+
+    def e2e_join(self, stream):
+        if getattr(self, "pipelined", False):
+            stream.wait_stream(self.s_in)
+            stream.wait_stream(self.s_out)
 
     def step_e2e(self, stream):
         import ctypes
-        self.A.copy_(self.A_host, non_blocking=True)
-        self.step(stream)
-        ybase = self.peers.local if self.peers is not None else self.Y.data_ptr()
-        self.lib.lcml_memcpy_async(ctypes.c_void_p(self.Y_host.data_ptr()),
-                                   ctypes.c_void_p(ybase + self.r0 * self.N * 2), self.Y_host.numel() * 2, 2,
-                                   ctypes.c_void_p(stream.cuda_stream))
+        import luisaml_b200 as lb
+        c = lambda p: ctypes.c_void_p(p)  # noqa: E731
+        if not self.pipelined:
+            self.A.copy_(self.A_host, non_blocking=True)
+            self.step(stream)
+            ybase = self.peers.local if self.peers is not None else self.Y.data_ptr()
+            lb.check(self.lib.lcml_memcpy_async(c(self.Y_host.data_ptr()), c(ybase + self.r0 * self.N * 2),
+                                                self.d2h, 2, c(stream.cuda_stream)))
+            return
+        k = self.e2e_i % 2
+        self.e2e_i += 1
+        A, desc, Y, Yh = self.slot_A[k], self.slot_desc[k], self.slot_Y[k], self.slot_Yh[k]
+        if self.used[k]:  # slot k's A was last read by the quantize of step i-2
+            self.s_in.wait_event(self.ev_read[k])
+        lb.check(self.lib.lcml_memcpy_async(c(A.data_ptr()), c(self.A_host.data_ptr()), self.h2d, 1,
+                                            c(self.s_in.cuda_stream)))
+        self.ev_ready[k].record(self.s_in)
+        stream.wait_event(self.ev_ready[k])
+        s = c(stream.cuda_stream)
+        lb.check(self.lib.lcml_fp8_quantize_tensor_dynamic(c(A.data_ptr()), A.numel(), c(self.sa.data_ptr()),
+                                                           c(self.Aq.data_ptr()), c(self.amax_ws.data_ptr()), s))
+        self.ev_read[k].record(stream)
+        if self.used[k]:  # slot k's Y was last read by the device-to-host copy of step i-2
+            stream.wait_event(self.ev_out[k])
+        lb.check(self.lib.lcml_fp8_gemm(ctypes.byref(desc), s))
+        self.ev_ydone[k].record(stream)
+        self.s_out.wait_event(self.ev_ydone[k])
+        lb.check(self.lib.lcml_memcpy_async(c(Yh.data_ptr()), c(Y.data_ptr()), self.d2h, 2,
+                                            c(self.s_out.cuda_stream)))
+        self.ev_out[k].record(self.s_out)
+        self.used[k] = True
 
     def close(self):
         if self.peers is not None:
@@ -380,7 +444,8 @@ class GraphWorkload:
     parallelism = "batch split"
     e2e_path = ("pinned host inputs -> NetworkInstance::forward (C ABI) with host-staged I/O: the H2D copy of each "
                 "step's input on a second stream (overlapping the previous step once its input readers ran) -> "
-                "nodes -> D2H of the outputs")
+                "nodes -> D2H of the outputs on a third stream (overlapping the next step until its writer of the "
+                "output runs)")
 
     def setup_graph(self, dev, text, blob, inputs, outputs):
         import torch
@@ -416,9 +481,13 @@ class GraphWorkload:
             self.net.set_input_host(k, t)
         for k, t in self.out_host.items():
             self.net.set_output_host(k, t)
+        self.net.set_async_outputs(True)
 
     def step_e2e(self, stream):
         self.net.forward()  # H2D of the inputs, the nodes, D2H of the outputs
+
+    def e2e_join(self, stream):
+        self.net.wait_outputs(stream.cuda_stream)  # the timed region ends after the last output copy
 
 
 class MlpWorkload(GraphWorkload):
@@ -867,8 +936,12 @@ def run_ours(args, wl):
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         ne = max(10, min(20, n // 10))
         e0.record(stream)
+        if hasattr(wl, "e2e_begin"):
+            wl.e2e_begin(stream)
         for _ in range(ne):
             wl.step_e2e(stream)
+        if hasattr(wl, "e2e_join"):
+            wl.e2e_join(stream)
         e1.record(stream)
         torch.cuda.synchronize()
         et = torch.tensor([e0.elapsed_time(e1)], dtype=torch.float64, device=dev)

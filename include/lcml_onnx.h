@@ -357,6 +357,15 @@ public:
     // instance's stream) after the last node. nullptr removes the binding.
     void set_input_host(std::string_view name, const void *host);
     void set_output_host(std::string_view name, void *host);
+    // Off (default): the host-staged outputs are copied on the instance's
+    // stream, so they are complete when that stream is. On: they are copied
+    // on a third stream after the last node, overlapping the next forward's
+    // nodes; the next forward's writer of an output waits only for that
+    // copy to have read it. The host buffers are then complete after
+    // wait_outputs() (the host waits for the copies enqueued so far), or on
+    // a stream `s` after wait_outputs(s) (the stream waits for them).
+    void enable_async_output_copy(bool e) { async_out_ = e; }
+    void wait_outputs(lcml_stream_t s = nullptr);
     // Kept for source compatibility with the reference; no effect on the CUDA path.
     void set_warp_size(uint32_t w) { warp_size_ = w; }
     uint32_t warp_size() const { return warp_size_; }
@@ -426,6 +435,10 @@ private:
     lcml_stream_t copy_stream_ = nullptr;
     lcml_event_t in_ready_ = nullptr, in_free_ = nullptr;
     bool in_free_recorded_ = false;
+    bool async_out_ = false;
+    lcml_stream_t out_stream_ = nullptr;
+    lcml_event_t out_ready_ = nullptr, out_free_ = nullptr;
+    bool out_free_recorded_ = false;
 };
 
 // Throws Error with lcml_last_error() when a C-ABI call fails.

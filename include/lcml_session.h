@@ -45,6 +45,14 @@ int lcml_network_set_output(lcml_network *net, const char *name, void *device_pt
  * stream. The tensor must be bound (set_input / set_output) first. */
 int lcml_network_set_input_host(lcml_network *net, const char *name, const void *host);
 int lcml_network_set_output_host(lcml_network *net, const char *name, void *host);
+/* 1: host-staged outputs are copied on a third stream after the last node,
+ * overlapping the next forward (whose writer of each output waits only for
+ * that copy); the host buffers are complete after lcml_network_wait_outputs.
+ * 0 (default): copied on the network's stream. */
+int lcml_network_set_async_outputs(lcml_network *net, int enable);
+/* stream NULL: the host waits until every output copy enqueued so far is
+ * done; otherwise `stream` waits for them (enqueued, no host wait). */
+int lcml_network_wait_outputs(lcml_network *net, lcml_stream_t stream);
 /* 1 (default): QDQ node groups run as fused kernels; 0: one kernel per node. */
 int lcml_network_set_fusion(lcml_network *net, int enable);
 int lcml_network_set_stream(lcml_network *net, lcml_stream_t stream);

@@ -591,7 +591,6 @@ __device__ __forceinline__ void epilogue_tile(const EpiParams &ep, const CUtenso
         }
     }
     if (ep.row_amax && row_ok) atomic_max_abs(ep.row_amax + row, amax);
-    if (ep.y_num_peers > 0) __threadfence_system();  // peer stores ordered before the kernel's completion
 }
 
 // Tile index -> (m tile, n tile), banded so that CTAs running at the same time
@@ -873,6 +872,9 @@ __global__ void __launch_bounds__(sc_threads<EPI, OUT>(), 1)
             }
         }
         if (lane == 0) bulk_wait_group_all();  // TMA stores done before the staging memory goes away
+        // this warp's peer stores ordered before the kernel's completion: once
+        // per kernel, not per tile (a system fence waits for the NVLink stores)
+        if (ep.y_num_peers > 0) __threadfence_system();
     }
 
     griddep_launch_dependents();
@@ -1069,6 +1071,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(threads_for<EPI>(), 
             }
         }
         if (lane == 0) bulk_wait_group_all();  // TMA stores done before the staging memory goes away
+        // this warp's peer stores ordered before the kernel's completion: once
+        // per kernel, not per tile (a system fence waits for the NVLink stores)
+        if (ep.y_num_peers > 0) __threadfence_system();
     }
 
     griddep_launch_dependents();
@@ -1537,6 +1542,7 @@ __global__ void __launch_bounds__(256) k_gemm_fp8_simt(const uint8_t *__restrict
         }
         if (ep.row_amax) atomic_max_abs(ep.row_amax + row, amax);
     }
+    if (ep.y_num_peers > 0) __threadfence_system();  // peer stores ordered before the kernel's completion
 }
 
 // ---------------------------------------------------------------------------

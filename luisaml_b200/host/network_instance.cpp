@@ -65,8 +65,30 @@ NetworkInstance::~NetworkInstance() {
         lcml_stream_synchronize(copy_stream_);
         lcml_stream_destroy(copy_stream_);
     }
+    if (out_stream_) {
+        lcml_stream_synchronize(out_stream_);
+        lcml_stream_destroy(out_stream_);
+    }
     lcml_event_destroy(in_ready_);
     lcml_event_destroy(in_free_);
+    lcml_event_destroy(out_ready_);
+    lcml_event_destroy(out_free_);
+}
+
+void NetworkInstance::wait_outputs(lcml_stream_t s) {
+    const bool async = out_stream_ && out_free_recorded_;
+    if (s) {
+        if (async) check_status(lcml_stream_wait_event(s, out_free_), "wait_outputs");
+        else if (s != stream_) {  // the copies ran on the instance's stream
+            lcml_event_t e = nullptr;
+            check_status(lcml_event_create(&e), "event");
+            check_status(lcml_event_record(e, stream_), "record");
+            check_status(lcml_stream_wait_event(s, e), "wait_outputs");
+            lcml_event_destroy(e);
+        }
+        return;
+    }
+    check_status(lcml_stream_synchronize(async ? out_stream_ : stream_), "wait_outputs");
 }
 
 void NetworkInstance::set_input_host(std::string_view name, const void *host) {
@@ -955,9 +977,26 @@ void NetworkInstance::forward() {
             if (r) last_reader = i;
         }
     }
+    // asynchronous output copies: the first node that writes a host-staged
+    // output waits until the previous forward's copy of it has been read
+    size_t first_out_writer = nodes.size();
+    if (async_out_ && !host_out_.empty() && out_free_recorded_) {
+        auto writes = [&](const std::string &n) { return host_out_.count(n) > 0; };
+        for (size_t i = 0; i < nodes.size() && first_out_writer == nodes.size(); ++i) {
+            if (fusion_[i]->skip) continue;
+            bool w = false;
+            if (!fusion_[i]->outputs.empty()) {
+                for (const auto &n : fusion_[i]->outputs) w = w || writes(n);
+            } else {
+                for (const auto *x : nodes[i].get_outputs()) w = w || writes(x->get_name());
+            }
+            if (w) first_out_writer = i;
+        }
+    }
     for (size_t i = 0; i < nodes.size(); ++i) {
         FusionInfo &fi = *fusion_[i];
         if (fi.skip) continue;
+        if (i == first_out_writer) check_status(lcml_stream_wait_event(stream_, out_free_), "wait");
         ins.clear();
         outs.clear();
         if (!fi.inputs.empty()) {
@@ -979,9 +1018,25 @@ void NetworkInstance::forward() {
             in_free_recorded_ = true;
         }
     }
+    if (host_out_.empty()) return;
+    lcml_stream_t out = stream_;
+    if (async_out_) {
+        if (!out_stream_) {
+            check_status(lcml_stream_create(&out_stream_), "output stream");
+            check_status(lcml_event_create(&out_ready_), "event");
+            check_status(lcml_event_create(&out_free_), "event");
+        }
+        check_status(lcml_event_record(out_ready_, stream_), "record");
+        check_status(lcml_stream_wait_event(out_stream_, out_ready_), "wait");
+        out = out_stream_;
+    }
     for (const auto &[name, host] : host_out_) {
         ITensor &t = *outputs_.at(name);
-        check_status(lcml_memcpy_async(host, t.data(), t.nbytes(), 2, stream_), "output copy");
+        check_status(lcml_memcpy_async(host, t.data(), t.nbytes(), 2, out), "output copy");
+    }
+    if (async_out_) {
+        check_status(lcml_event_record(out_free_, out_stream_), "record");
+        out_free_recorded_ = true;
     }
 }
 

@@ -101,6 +101,17 @@ int lcml_network_set_output_host(lcml_network *net, const char *name, void *host
     return guard([&] { net->inst.set_output_host(name, host); });
 }
 
+int lcml_network_set_async_outputs(lcml_network *net, int enable) {
+    if (!net) return fail(LCML_ERR_INVALID_ARGUMENT, "null network");
+    net->inst.enable_async_output_copy(enable != 0);
+    return LCML_OK;
+}
+
+int lcml_network_wait_outputs(lcml_network *net, lcml_stream_t stream) {
+    if (!net) return fail(LCML_ERR_INVALID_ARGUMENT, "null network");
+    return guard([&] { net->inst.wait_outputs(stream); });
+}
+
 int lcml_network_set_fusion(lcml_network *net, int enable) {
     if (!net) return fail(LCML_ERR_INVALID_ARGUMENT, "null network");
     net->inst.enable_fusion(enable != 0);

@@ -31,6 +31,8 @@ def load():
     lib.lcml_network_set_output.argtypes = [_vp, ctypes.c_char_p, _vp, _ci, ctypes.POINTER(_i64), _ci]
     lib.lcml_network_set_input_host.argtypes = [_vp, ctypes.c_char_p, _vp]
     lib.lcml_network_set_output_host.argtypes = [_vp, ctypes.c_char_p, _vp]
+    lib.lcml_network_set_async_outputs.argtypes = [_vp, _ci]
+    lib.lcml_network_wait_outputs.argtypes = [_vp, _vp]
     lib.lcml_network_set_fusion.argtypes = [_vp, _ci]
     lib.lcml_network_set_memory_reuse.argtypes = [_vp, _ci]
     lib.lcml_network_memory.argtypes = [_vp, ctypes.POINTER(ctypes.c_size_t), ctypes.POINTER(ctypes.c_size_t)]
@@ -107,6 +109,16 @@ class Network:
         if t is not None:
             self._keep.append(t)
         _check(load().lcml_network_set_output_host(self._h, name.encode(), None if t is None else t.data_ptr()))
+
+    def set_async_outputs(self, enable: bool):
+        """Host-staged outputs copied on a third stream, overlapping the next
+        forward; they are complete after wait_outputs()."""
+        _check(load().lcml_network_set_async_outputs(self._h, int(enable)))
+
+    def wait_outputs(self, stream_handle=None):
+        """No stream: the host waits for every output copy enqueued so far;
+        with a stream handle: that stream waits for them."""
+        _check(load().lcml_network_wait_outputs(self._h, stream_handle))
 
     def set_fusion(self, enable: bool):
         _check(load().lcml_network_set_fusion(self._h, int(enable)))

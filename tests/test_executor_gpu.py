@@ -82,7 +82,9 @@ def test_host_staged_io(dev):
     """Host-staged inputs and outputs: forwards issued back to back, each
     with its own pinned input and output, give the device-bound results; the
     input copy of one forward (on the executor's second stream) must not
-    overwrite the device input before the previous forward has read it."""
+    overwrite the device input before the previous forward has read it, and
+    with asynchronous output copies the next forward must not overwrite the
+    device output before the previous copy has read it."""
     import torch
     from luisaml_b200 import graphs
     from luisaml_b200.session import Network
@@ -119,6 +121,26 @@ def test_host_staged_io(dev):
             hout[i].fill_(np.nan)
     with pytest.raises(Exception):
         net.set_input_host("no_such_input", hin[0])
+    # asynchronous output copies (third stream): the next forward's last
+    # Gemm waits only for the previous copy of the output to have read it
+    net.set_async_outputs(True)
+    for rep in range(2):
+        for i in range(len(xs)):
+            net.set_input_host("input", hin[i])
+            net.set_output_host("output", hout[i])
+            net.forward()
+        net.wait_outputs()
+        for i in range(len(xs)):
+            np.testing.assert_array_equal(hout[i].numpy(), want[i])
+            hout[i].fill_(np.nan)
+    s = torch.cuda.Stream(dev)
+    net.forward()
+    net.wait_outputs(s.cuda_stream)  # the stream waits: its copy of the host output sees the finished one
+    got = torch.empty((B, 10), dtype=torch.float32, device=dev)
+    with torch.cuda.stream(s):
+        got.copy_(hout[len(xs) - 1], non_blocking=True)
+    s.synchronize()
+    np.testing.assert_array_equal(got.cpu().numpy(), want[len(xs) - 1])
 
 
 def _quantized_mlp(batch, dims, seed):
