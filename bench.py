@@ -207,6 +207,9 @@ class GemmWorkload:
              "step": ("amax + quantize + GEMM C-ABI calls captured once as a CUDA graph and replayed each step; "
                       "GEMM kernel time from a second loop with CUDA events around the GEMM") if self.graph_step
              else "amax + quantize + GEMM C-ABI calls each step; CUDA events around the GEMM inside the step"}
+        if self.M <= 4:
+            d["step"] = ("one kernel (lcml_fp8_gemm_quantize_a: max|A|, QuantizeLinear of A and the GEMV) captured "
+                         "once as a CUDA graph and replayed each step; its time from a second loop with CUDA events")
         if self.ws > 1:
             d["rows_per_rank"] = self.rows
             d["step"] = ("amax of the rank's rows, max over the ranks (lcml_peer_exchange_max: one 64-bit NVLink store "
@@ -273,6 +276,15 @@ class GemmWorkload:
             lb.check(self.lib.lcml_fp8_quantize_from_amax(
                 ctypes.c_void_p(self.A.data_ptr()), 1, 1, self.A.numel(), ctypes.c_void_p(self.amax_g.data_ptr()),
                 ctypes.c_void_p(self.sa.data_ptr()), ctypes.c_void_p(self.Aq.data_ptr()), s))
+        elif self.M <= 4:  # decode: the quantize of A runs inside the GEMV (one kernel per step)
+            if ev is not None:
+                ev[0].record(stream)
+            lb.check(self.lib.lcml_fp8_gemm_quantize_a(
+                ctypes.byref(self.desc), ctypes.c_void_p(self.A.data_ptr()), self.K,
+                ctypes.c_void_p(self.Aq.data_ptr()), ctypes.c_void_p(self.sa.data_ptr()), None, s))
+            if ev is not None:
+                ev[1].record(stream)
+            return
         else:
             lb.check(self.lib.lcml_fp8_quantize_tensor_dynamic(
                 ctypes.c_void_p(self.A.data_ptr()), self.A.numel(), ctypes.c_void_p(self.sa.data_ptr()),
@@ -374,8 +386,10 @@ class GemmWorkload:
 
     def dominant(self):
         if self.M <= 128:  # skinny: streaming B dominates (arithmetic intensity ~2M FLOP/B)
-            bytes_ = self.M * self.K + self.N * self.K + 2 * self.M * self.N
-            return {"kernel": "gemv_fp8" if self.M <= 4 else "gemm_fp8_splitk", "bound": "hbm", "unit": "GB/s",
+            a_bytes = (4 if self.M <= 4 else 1) * self.M * self.K  # the fused GEMV reads A as fp32
+            bytes_ = a_bytes + self.N * self.K + 2 * self.M * self.N
+            return {"kernel": "gemv_fp8 (quantize of A fused)" if self.M <= 4 else "gemm_fp8_splitk",
+                    "bound": "hbm", "unit": "GB/s",
                     "work": bytes_,
                     "profile": f"gemv_fp8_skinny_{self.M}" if self.M <= 4 else f"gemm_fp8_skinny_{self.M}"}
         kern = "gemm_fp8_tc2" if self.rows >= 1024 and self.K >= 1024 else "gemm_fp8_tc"

@@ -247,6 +247,26 @@ int lcml_fp8_gemm_rowquant(const lcml_fp8_gemm_desc *desc, uint8_t *q, float *q_
                            lcml_stream_t stream);
 
 /*
+ * QuantizeLinear of an fp32 activation with a dynamic per-tensor scale
+ * followed by the GEMM that consumes it (the DynamicQuantizeLinear /
+ * Abs -> ReduceMax -> Div -> QuantizeLinear -> DequantizeLinear -> Gemm
+ * chain of a decode step; no counterpart in the reference, which has no
+ * QuantizeLinear): s = max|A| / 448 (1 for an all-zero A, NaN ignored),
+ * aq = e4m3(A / s) bit-exact as lcml_fp8_quantize, then lcml_fp8_gemm on
+ * (aq, s) with desc's B, scales, epilogue and output; desc->A, lda,
+ * scale_a and scale_a_mode are ignored. a: [M, K] fp32, row stride lda
+ * elements. scale_a_out receives s. For M <= 4 on the GEMV path (desc
+ * variant 0, no peers, not SILU_MUL) it is one kernel: every CTA derives s
+ * from all of A and quantizes A while staging it; aq may then be NULL
+ * (written when given) and workspace is unused. Otherwise A must be dense
+ * (lda == K) and it runs lcml_fp8_quantize_tensor_dynamic into aq (M*K
+ * bytes) with workspace (LCML_FP8_TENSOR_DYNAMIC_WORKSPACE_BYTES), then the
+ * GEMM.
+ */
+int lcml_fp8_gemm_quantize_a(const lcml_fp8_gemm_desc *desc, const float *a, int64_t lda, uint8_t *aq,
+                             float *scale_a_out, float *workspace, lcml_stream_t stream);
+
+/*
  * lcml_fp8_gemm_rowquant for callers that cannot allocate device memory.
  * No counterpart in the reference: it exists for hosts that own every byte
  * of device memory through their own buffer abstraction and have no way to

@@ -193,6 +193,26 @@ def gemm(A, B, sa, sb, *, b_kmajor=True, alpha=1.0, beta=1.0, c_vec=None, c_vec_
     return Y
 
 
+def gemm_quantize_a(A, B, sb, *, aq=None, workspace=None, **kw):
+    """lcml_fp8_gemm_quantize_a: fp32 A [M, K] quantized with a dynamic
+    per-tensor scale and multiplied by e4m3 B in one call (one kernel for
+    M <= 4 on the GEMV path). Returns (Y, Aq or None, s). kw as for gemm()
+    (variant, epilogue, out_dtype, ...)."""
+    torch = _torch()
+    M, K = A.shape
+    s = torch.empty(1, dtype=torch.float32, device=A.device)
+    fused = M <= 4 and kw.get("variant", 0) == 0
+    if aq is None and not fused:
+        aq = torch.empty((M, K), dtype=torch.uint8, device=A.device)
+    if workspace is None and not fused:
+        workspace = torch.empty(TENSOR_DYNAMIC_WORKSPACE_BYTES // 4, dtype=torch.float32, device=A.device)
+    placeholder = aq if aq is not None else torch.empty((M, K), dtype=torch.uint8, device=A.device)
+    d, Y = gemm(placeholder, B, s, sb, desc_only=True, **kw)
+    check(lib().lcml_fp8_gemm_quantize_a(ctypes.byref(d), _p(A), A.stride(0), _p(aq) if aq is not None else None,
+                                         _p(s), _p(workspace) if workspace is not None else None, _stream()))
+    return Y, aq, s
+
+
 def gemm_rowquant(A, B, sa, sb, *, workspace=None, **kw):
     """Fused GEMM (fp32 Y) + dynamic per-row e4m3 quantization of Y through
     lcml_fp8_gemm_rowquant. Returns (Y fp32, q uint8, s fp32 [M])."""

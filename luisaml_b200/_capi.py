@@ -119,6 +119,7 @@ PROTOTYPES = {
     "lcml_fp8_dequantize": [_vp, _c_i64, _c_i64, _c_i64, _vp, _ci, _vp, _ci, _vp],
     "lcml_fp8_transpose": [_vp, _c_i64, _c_i64, _vp, _vp],
     "lcml_fp8_gemm": [ctypes.POINTER(GemmDesc), _vp],
+    "lcml_fp8_gemm_quantize_a": [ctypes.POINTER(GemmDesc), _vp, _c_i64, _vp, _vp, _vp, _vp],
     "lcml_fp8_gemm_simt": [ctypes.POINTER(GemmDesc), _vp],
     "lcml_fp8_gemm_rowquant": [ctypes.POINTER(GemmDesc), _vp, _vp, _vp, _vp],
     "lcml_fp8_gemm_rowquant_noalloc": [ctypes.POINTER(GemmDesc), _vp, _vp, _vp],

@@ -1376,10 +1376,23 @@ constexpr int kGemvRows = 2;     // rows of B per warp in flight
 constexpr int kGemvChunks = 8;   // 16-byte chunks per lane per row and step: 4 KB of a row per warp step
 constexpr int kGemvSmemMax = 48 * 1024;
 
-template <int MR, int EPI, int OUT>
+// QuantizeLinear of an fp32 A with a dynamic per-tensor scale fused into the
+// GEMV (QA kernels): A is at most kGemvMaxM rows, so every CTA takes max|A|
+// over all of it (an L2-resident read), derives s = amax / 448 (1 for an
+// all-zero A) exactly as the quantize kernels do, and quantizes A with the
+// bit-exact block quantizer while staging it; CTA 0 also writes s and the
+// codes. One launch instead of the two quantize passes and the GEMV.
+struct GemvQuantA {
+    const float *a;    // [M, K] fp32, row stride lda (elements, a multiple of 4), 16-byte aligned
+    int64_t lda;
+    float *scale_out;  // s (one float)
+    uint8_t *aq_out;   // the codes [M, K] (row stride K), or nullptr
+};
+
+template <int MR, int EPI, int OUT, bool QA = false>
 __global__ void __launch_bounds__(kGemvThreads) k_gemv_fp8(const uint8_t *__restrict__ A, int64_t lda,
                                                            const uint8_t *__restrict__ B, int64_t ldb, int M, int N,
-                                                           int K, EpiParams ep) {
+                                                           int K, EpiParams ep, GemvQuantA qa) {
     extern __shared__ float4 sA4[];  // [MR][4][K/16]: float4 q of chunk c of row m at m*(K/4) + q*(K/16) + c
     const int kc = K / 16;           // 16-byte chunks per row (K % 16 == 0)
     const int lane = threadIdx.x & 31;
@@ -1393,15 +1406,57 @@ __global__ void __launch_bounds__(kGemvThreads) k_gemv_fp8(const uint8_t *__rest
             asm volatile("prefetch.global.L2 [%0];" ::"l"(B + static_cast<int64_t>(gw * kGemvRows + r) * ldb + lane * 128));
     griddep_wait();  // A, the scales and a residual may come from the previous kernel
     griddep_launch_dependents();
-    for (int i = threadIdx.x; i < MR * (K / 4); i += kGemvThreads) {
-        const int m = i / (K / 4), k4 = i - m * (K / 4);
-        float v[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-        if (m < M) {
-            const uint32_t w = *reinterpret_cast<const uint32_t *>(A + m * lda + 4 * k4);
-            e4m3x2_decode(w & 0xffffu, v[0], v[1]);
-            e4m3x2_decode(w >> 16, v[2], v[3]);
+    float s_a = 0.0f;  // QA: the per-tensor scale of A derived here
+    if constexpr (QA) {
+        __shared__ uint32_t red[kGemvThreads / 32];
+        uint32_t mx = 0;
+        for (int i = threadIdx.x; i < M * (K / 4); i += kGemvThreads) {
+            const int m = i / (K / 4), k4 = i - m * (K / 4);
+            const float4 v = __ldg(reinterpret_cast<const float4 *>(qa.a + m * qa.lda) + k4);
+            mx = max(mx, max(max(abs_bits_nan0(v.x), abs_bits_nan0(v.y)), max(abs_bits_nan0(v.z), abs_bits_nan0(v.w))));
         }
-        sA4[m * (K / 4) + (k4 & 3) * kc + (k4 >> 2)] = make_float4(v[0], v[1], v[2], v[3]);
+        mx = __reduce_max_sync(0xffffffffu, mx);
+        if (lane == 0) red[threadIdx.x >> 5] = mx;
+        __syncthreads();
+        mx = 0;
+#pragma unroll
+        for (int w = 0; w < kGemvThreads / 32; ++w) mx = max(mx, red[w]);
+        s_a = scale_from_amax(__uint_as_float(mx));
+        const float r = __frcp_rn(s_a);
+        const bool s_ok = scale_fast_ok(s_a, r);
+        for (int i = threadIdx.x; i < MR * kc; i += kGemvThreads) {  // 16 elements per step
+            const int m = i / kc, c = i - m * kc;
+            uint32_t w[4] = {0u, 0u, 0u, 0u};
+            if (m < M) {
+                const float4 *p = reinterpret_cast<const float4 *>(qa.a + m * qa.lda) + 4 * c;
+                const float4 v0 = __ldg(p), v1 = __ldg(p + 1), v2 = __ldg(p + 2), v3 = __ldg(p + 3);
+                const float v[16] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w,
+                                     v2.x, v2.y, v2.z, v2.w, v3.x, v3.y, v3.z, v3.w};
+                quantize_block_fast<16>(v, s_a, r, s_ok, w);
+                if (blockIdx.x == 0 && qa.aq_out)
+                    *reinterpret_cast<uint4 *>(qa.aq_out + static_cast<int64_t>(m) * K + 16 * c) =
+                        make_uint4(w[0], w[1], w[2], w[3]);
+            }
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {  // word q = elements 16c + 4q .. +3: float4 q of chunk c
+                float d[4];
+                e4m3x2_decode(w[q] & 0xffffu, d[0], d[1]);
+                e4m3x2_decode(w[q] >> 16, d[2], d[3]);
+                sA4[m * (K / 4) + q * kc + c] = make_float4(d[0], d[1], d[2], d[3]);
+            }
+        }
+        if (blockIdx.x == 0 && threadIdx.x == 0) *qa.scale_out = s_a;
+    } else {
+        for (int i = threadIdx.x; i < MR * (K / 4); i += kGemvThreads) {
+            const int m = i / (K / 4), k4 = i - m * (K / 4);
+            float v[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+            if (m < M) {
+                const uint32_t w = *reinterpret_cast<const uint32_t *>(A + m * lda + 4 * k4);
+                e4m3x2_decode(w & 0xffffu, v[0], v[1]);
+                e4m3x2_decode(w >> 16, v[2], v[3]);
+            }
+            sA4[m * (K / 4) + (k4 & 3) * kc + (k4 >> 2)] = make_float4(v[0], v[1], v[2], v[3]);
+        }
     }
     __syncthreads();
 
@@ -1464,7 +1519,7 @@ __global__ void __launch_bounds__(kGemvThreads) k_gemv_fp8(const uint8_t *__rest
 #pragma unroll
                 for (int m = 0; m < MR; ++m) {
                     if (m >= M) continue;
-                    const float rs = ep.alpha * (ep.sa_row ? __ldg(ep.sa + m) : __ldg(ep.sa));
+                    const float rs = ep.alpha * (QA ? s_a : (ep.sa_row ? __ldg(ep.sa + m) : __ldg(ep.sa)));
                     float v = simt_pre(acc[r][m], rs, m, col, ep);
                     if (ep.c_mat) v += ep.beta * load_cmat(ep, m, col);
                     if (EPI == LCML_EPI_RELU) v = fmaxf(v, 0.0f);
@@ -1769,16 +1824,16 @@ int gemv_rows(const lcml_fp8_gemm_desc *d, const EpiParams &ep) {
     return static_cast<int64_t>(mr) * d->K * 4 <= kGemvSmemMax ? mr : 0;
 }
 
-template <int MR, int EPI, int OUT>
-int launch_gemv(const lcml_fp8_gemm_desc *d, const EpiParams &ep, cudaStream_t st) {
+template <int MR, int EPI, int OUT, bool QA = false>
+int launch_gemv(const lcml_fp8_gemm_desc *d, const EpiParams &ep, cudaStream_t st, const GemvQuantA &qa = {}) {
     constexpr int rows_per_cta = (kGemvThreads / 32) * kGemvRows;
     const int64_t want = (d->N + rows_per_cta - 1) / rows_per_cta;
     const int64_t cap = 4LL * sm_count();
     const int grid = static_cast<int>(want < cap ? want : cap);
     const size_t smem = static_cast<size_t>(MR) * static_cast<size_t>(d->K) * 4;
-    return launch_gemm_kernel(k_gemv_fp8<MR, EPI, OUT>, static_cast<unsigned>(grid), kGemvThreads, smem, st, 0,
-                              "gemv_fp8", d->A, d->lda, d->B, d->ldb, static_cast<int>(d->M), static_cast<int>(d->N),
-                              static_cast<int>(d->K), ep);
+    return launch_gemm_kernel(k_gemv_fp8<MR, EPI, OUT, QA>, static_cast<unsigned>(grid), kGemvThreads, smem, st, 0,
+                              QA ? "gemv_fp8_quantize_a" : "gemv_fp8", d->A, d->lda, d->B, d->ldb,
+                              static_cast<int>(d->M), static_cast<int>(d->N), static_cast<int>(d->K), ep, qa);
 }
 
 template <int EPI, int OUT>
@@ -1802,7 +1857,19 @@ bool wide_tiles(const lcml_fp8_gemm_desc *d) {
 }
 
 template <int EPI, int OUT>
-int dispatch(const lcml_fp8_gemm_desc *d, const EpiParams &ep, cudaStream_t st, bool force_simt, const ConvGeom *geo) {
+int dispatch(const lcml_fp8_gemm_desc *d, const EpiParams &ep, cudaStream_t st, bool force_simt, const ConvGeom *geo,
+             const GemvQuantA *qa) {
+    if (qa) {  // fp32 A quantized inside the GEMV (the caller checked the GEMV conditions)
+        if constexpr (EPI != LCML_EPI_SILU_MUL) {
+            switch (gemv_rows(d, ep)) {
+                case 1: return launch_gemv<1, EPI, OUT, true>(d, ep, st, *qa);
+                case 2: return launch_gemv<2, EPI, OUT, true>(d, ep, st, *qa);
+                case 4: return launch_gemv<4, EPI, OUT, true>(d, ep, st, *qa);
+                default: break;
+            }
+        }
+        return set_error(LCML_ERR_UNSUPPORTED, "fused A quantization: not a GEMV shape");
+    }
     if (geo) {  // implicit-GEMM convolution: single-CTA tiles as wide as the output channels
         if constexpr (EPI == LCML_EPI_SILU_MUL) {
             return set_error(LCML_ERR_UNSUPPORTED, "implicit-GEMM convolution: SILU_MUL epilogue");
@@ -1847,16 +1914,17 @@ int dispatch(const lcml_fp8_gemm_desc *d, const EpiParams &ep, cudaStream_t st, 
 
 template <int EPI>
 int dispatch_out(const lcml_fp8_gemm_desc *d, const EpiParams &ep, cudaStream_t st, bool force_simt,
-                 const ConvGeom *geo) {
+                 const ConvGeom *geo, const GemvQuantA *qa) {
     switch (d->y_dtype) {
-        case LCML_DTYPE_FLOAT: return dispatch<EPI, kOutF32>(d, ep, st, force_simt, geo);
-        case LCML_DTYPE_BFLOAT16: return dispatch<EPI, kOutBF16>(d, ep, st, force_simt, geo);
-        case LCML_DTYPE_FLOAT8E4M3FN: return dispatch<EPI, kOutE4M3>(d, ep, st, force_simt, geo);
+        case LCML_DTYPE_FLOAT: return dispatch<EPI, kOutF32>(d, ep, st, force_simt, geo, qa);
+        case LCML_DTYPE_BFLOAT16: return dispatch<EPI, kOutBF16>(d, ep, st, force_simt, geo, qa);
+        case LCML_DTYPE_FLOAT8E4M3FN: return dispatch<EPI, kOutE4M3>(d, ep, st, force_simt, geo, qa);
         default: return set_error(LCML_ERR_INVALID_ARGUMENT, "lcml_fp8_gemm: y_dtype %d unsupported", d->y_dtype);
     }
 }
 
-int gemm_entry(const lcml_fp8_gemm_desc *d, lcml_stream_t stream, bool force_simt, const ConvGeom *geo = nullptr) {
+int gemm_entry(const lcml_fp8_gemm_desc *d, lcml_stream_t stream, bool force_simt, const ConvGeom *geo = nullptr,
+               const GemvQuantA *qa = nullptr) {
     LCML_CHECK_ARG(d != nullptr, "lcml_fp8_gemm: desc is NULL");
     LCML_CHECK_ARG(d->M >= 0 && d->N >= 0 && d->K >= 0, "lcml_fp8_gemm: negative extent");
     LCML_CHECK_ARG(d->epilogue >= LCML_EPI_NONE && d->epilogue <= LCML_EPI_SILU_MUL,
@@ -1865,8 +1933,8 @@ int gemm_entry(const lcml_fp8_gemm_desc *d, lcml_stream_t stream, bool force_sim
         LCML_CHECK_ARG(d->N % 256 == 0, "lcml_fp8_gemm: SILU_MUL needs N (gate+up) to be a multiple of 256, got %lld",
                        (long long)d->N);
     if (d->M == 0 || d->N == 0) return LCML_OK;
-    LCML_CHECK_ARG((d->A || geo) && d->B && d->Y && d->scale_a && d->scale_b, "lcml_fp8_gemm: null operand");
-    LCML_CHECK_ARG(geo || d->lda >= d->K, "lcml_fp8_gemm: lda < K");
+    LCML_CHECK_ARG((d->A || geo || qa) && d->B && d->Y && d->scale_a && d->scale_b, "lcml_fp8_gemm: null operand");
+    LCML_CHECK_ARG(geo || qa || d->lda >= d->K, "lcml_fp8_gemm: lda < K");
     LCML_CHECK_ARG(d->b_kmajor ? d->ldb >= d->K : d->ldb >= d->N, "lcml_fp8_gemm: ldb too small");
     const int64_t n_out = d->epilogue == LCML_EPI_SILU_MUL ? d->N / 2 : d->N;
     LCML_CHECK_ARG(d->y_col_offset >= 0 && d->ldy >= n_out + d->y_col_offset, "lcml_fp8_gemm: ldy < y_col_offset + output columns");
@@ -1912,9 +1980,9 @@ int gemm_entry(const lcml_fp8_gemm_desc *d, lcml_stream_t stream, bool force_sim
     }
     cudaStream_t st = to_cuda(stream);
     switch (d->epilogue) {
-        case LCML_EPI_NONE: return dispatch_out<LCML_EPI_NONE>(d, ep, st, force_simt, geo);
-        case LCML_EPI_RELU: return dispatch_out<LCML_EPI_RELU>(d, ep, st, force_simt, geo);
-        default: return dispatch_out<LCML_EPI_SILU_MUL>(d, ep, st, force_simt, geo);
+        case LCML_EPI_NONE: return dispatch_out<LCML_EPI_NONE>(d, ep, st, force_simt, geo, qa);
+        case LCML_EPI_RELU: return dispatch_out<LCML_EPI_RELU>(d, ep, st, force_simt, geo, qa);
+        default: return dispatch_out<LCML_EPI_SILU_MUL>(d, ep, st, force_simt, geo, qa);
     }
 }
 
@@ -1953,6 +2021,35 @@ int lcml_fp8_gemm_rowquant(const lcml_fp8_gemm_desc *desc, uint8_t *q, float *q_
     int rc = lcml::gemm::gemm_entry(&d, stream, false);
     if (rc != LCML_OK) return rc;
     return lcml_fp8_quantize_from_amax(static_cast<const float *>(d.Y), 1, d.M, n_out, workspace, q_scale, q, stream);
+}
+
+int lcml_fp8_gemm_quantize_a(const lcml_fp8_gemm_desc *desc, const float *a, int64_t lda, uint8_t *aq,
+                             float *scale_a_out, float *workspace, lcml_stream_t stream) {
+    LCML_CHECK_ARG(desc != nullptr, "lcml_fp8_gemm_quantize_a: desc is NULL");
+    LCML_CHECK_ARG(desc->M >= 0 && desc->K >= 0 && lda >= desc->K, "lcml_fp8_gemm_quantize_a: bad extents / lda");
+    if (desc->M == 0 || desc->N == 0) return LCML_OK;
+    LCML_CHECK_ARG(a && scale_a_out, "lcml_fp8_gemm_quantize_a: null a / scale_a_out");
+    lcml_fp8_gemm_desc d = *desc;
+    d.A = aq;
+    d.lda = desc->K;
+    d.scale_a = scale_a_out;
+    d.scale_a_mode = LCML_SCALE_TENSOR;
+    // one fused kernel for decode-sized M on the GEMV path (its conditions as in dispatch: automatic kernel
+    // choice, K-major 16-byte B rows, A rows of whole float4s)
+    const bool fused = d.variant == 0 && d.M <= lcml::gemm::kGemvMaxM && d.epilogue != LCML_EPI_SILU_MUL &&
+                       d.y_num_peers == 0 && d.b_kmajor && d.K % 16 == 0 && d.ldb % 16 == 0 && d.B &&
+                       lcml::aligned(d.B, 16) && lda % 4 == 0 && lcml::aligned(a, 16) &&
+                       static_cast<int64_t>(d.M == 1 ? 1 : (d.M == 2 ? 2 : 4)) * d.K * 4 <= lcml::gemm::kGemvSmemMax &&
+                       d.N <= 0x7fffffff && d.K <= 0x7fffffff;
+    if (fused) {
+        const lcml::gemm::GemvQuantA qa{a, lda, scale_a_out, aq};
+        return lcml::gemm::gemm_entry(&d, stream, false, nullptr, &qa);
+    }
+    LCML_CHECK_ARG(aq && workspace, "lcml_fp8_gemm_quantize_a: this shape needs aq and workspace");
+    LCML_CHECK_ARG(lda == desc->K, "lcml_fp8_gemm_quantize_a: this shape needs a dense A (lda == K)");
+    const int rc = lcml_fp8_quantize_tensor_dynamic(a, desc->M * desc->K, scale_a_out, aq, workspace, stream);
+    if (rc != LCML_OK) return rc;
+    return lcml::gemm::gemm_entry(&d, stream, false);
 }
 
 // Test hook (not in the public header): the SIMT kernel on the same

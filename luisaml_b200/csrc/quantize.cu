@@ -189,11 +189,19 @@ __global__ void __launch_bounds__(kThreads) k_amax_partial(const float *__restri
     const int64_t nthreads = static_cast<int64_t>(gridDim.x) * blockDim.x;
     uint32_t m = 0;
     const int64_t n4 = n >> 2;
-    for (int64_t i = tid; i < n4; i += nthreads) {
-        const float4 v = __ldg(reinterpret_cast<const float4 *>(x) + i);
-        m = max(m, max(max(abs_bits_nan0(v.x), abs_bits_nan0(v.y)), max(abs_bits_nan0(v.z), abs_bits_nan0(v.w))));
+    auto max4 = [](uint32_t a, const float4 &v) {
+        return max(a, max(max(abs_bits_nan0(v.x), abs_bits_nan0(v.y)), max(abs_bits_nan0(v.z), abs_bits_nan0(v.w))));
+    };
+    // four independent 16-byte loads in flight per thread per step
+    int64_t i = tid;
+    for (; i + 3 * nthreads < n4; i += 4 * nthreads) {
+        const float4 *p = reinterpret_cast<const float4 *>(x) + i;
+        const float4 v0 = __ldg(p), v1 = __ldg(p + nthreads), v2 = __ldg(p + 2 * nthreads), v3 = __ldg(p + 3 * nthreads);
+        m = max4(max4(m, v0), v1);
+        m = max4(max4(m, v2), v3);
     }
-    for (int64_t i = (n4 << 2) + tid; i < n; i += nthreads) m = max(m, abs_bits_nan0(x[i]));
+    for (; i < n4; i += nthreads) m = max4(m, __ldg(reinterpret_cast<const float4 *>(x) + i));
+    for (int64_t j = (n4 << 2) + tid; j < n; j += nthreads) m = max(m, abs_bits_nan0(x[j]));
     m = block_max_u32(m, red);
     if (threadIdx.x == 0) partial[blockIdx.x] = m;
 }

@@ -114,6 +114,9 @@ CASES = [
     ("3x3_dil2_c128", 2, 128, 17, 128, 3, 1, 2, True, 2),         # dilated taps
     ("2x2_s2_nopad_c64", 1, 64, 15, 32, 2, 2, 0, True, 1),        # input rows/cols no tap reads
     ("3x3_s3_c128", 2, 128, 20, 64, 3, 3, 0, True, 1),            # traversal stride 3
+    ("5x5_s1_p2_c64", 2, 64, 20, 64, 5, 1, 2, True, 1),           # two-pixel borders
+    ("3x3_s1_c128_ragged", 3, 128, 11, 96, 3, 1, 1, True, 1),     # 128-byte rows; tiles straddle images
+    ("3x3_s1_c64_w1", 2, 64, 1, 64, 3, 1, 1, True, 1),            # 1 x 1 images: every off-centre tap is an edge
 ]
 
 

@@ -424,3 +424,47 @@ def test_store_paths(dev, out, mode, M, N, K):
         want = epilogue_quantize(y32, s)
         np.testing.assert_array_equal(results[0][:, 16:16 + N], want)
         assert np.mean(want != oracle.quantize(y32, s)) <= 1e-3
+
+
+@pytest.mark.parametrize("M,pad", [(1, 0), (2, 64), (3, 0), (4, 4), (5, 0), (64, 0)])
+def test_gemm_quantize_a(dev, M, pad):
+    """lcml_fp8_gemm_quantize_a: dynamic per-tensor QuantizeLinear of an fp32
+    A fused with the GEMM (one GEMV kernel for M <= 4, the quantize kernels
+    and the GEMM otherwise). The scale and the codes are bit-exact against
+    the oracle's amax / 448 and QuantizeLinear (a NaN in A is ignored by the
+    amax and becomes code 0x7f), Y is bit-identical to lcml_fp8_gemm on those
+    codes and within rtol 2e-3 / atol 1e-3 of the oracle's QDQ GEMM. pad > 0
+    gives A a row stride of K + pad elements (fused path only)."""
+    import torch
+    import luisaml_b200 as lb
+    N, K = 1000, 2048
+    rng = np.random.default_rng(300 + M)
+    A = (rng.standard_normal((M, K)) * 3).astype(np.float32)
+    A[0, 7] = np.nan
+    Abig = np.zeros((M, K + pad), np.float32)
+    Abig[:, :K] = A
+    At = _t(Abig, dev)[:, :K]
+    B = (rng.standard_normal((N, K)) * 0.05).astype(np.float32)
+    Bq, sb = oracle.quantize_dynamic_rows(B)
+    Bt, sbt = _t(Bq, dev), _t(sb, dev)
+    aq = torch.empty((M, K), dtype=torch.uint8, device=dev)
+    Y, aq_out, s = lb.gemm_quantize_a(At, Bt, sbt, aq=aq, out_dtype=torch.float32)
+    torch.cuda.synchronize()
+    assert lb.device_error() == 0
+    s_ref = oracle.scale_from_amax(np.nanmax(np.abs(A)))
+    assert np.float32(s.item()) == s_ref
+    codes = aq.cpu().numpy()
+    np.testing.assert_array_equal(codes, oracle.quantize(A, s_ref))
+    assert codes[0, 7] == 0x7f
+    Y2 = lb.gemm(aq, Bt, s, sbt, out_dtype=torch.float32)
+    torch.cuda.synchronize()
+    np.testing.assert_array_equal(Y.cpu().numpy(), Y2.cpu().numpy())
+    rows = np.arange(1, M)  # row 0 holds the NaN code: every output of it is NaN
+    if rows.size:
+        ref = oracle.qdq_gemm(codes[rows], np.float32([s_ref]), Bq, sb)
+        assert_close(Y.cpu().numpy()[rows], ref, what=f"fused quantize-A GEMM M={M}")
+    assert np.isnan(Y.cpu().numpy()[0]).all()
+    if M <= 4:  # codes are optional on the fused path; an all-zero A gets scale 1
+        Y3, none, s3 = lb.gemm_quantize_a(torch.zeros((M, K), device=dev), Bt, sbt, out_dtype=torch.float32)
+        torch.cuda.synchronize()
+        assert none is None and s3.item() == 1.0 and not Y3.cpu().numpy().any()
