@@ -393,7 +393,12 @@ class GemmWorkload:
                     "bound": "hbm", "unit": "GB/s",
                     "work": bytes_,
                     "profile": f"gemv_fp8_skinny_{self.M}" if self.M <= 4 else f"gemm_fp8_skinny_{self.M}"}
-        kern = "gemm_fp8_tc2" if self.rows >= 1024 and self.K >= 1024 else "gemm_fp8_tc"
+        # the library's choice (gemm_fp8.cu dispatch): CTA pairs for long K once the 256 x 256 tiles fill the SMs
+        import torch
+        sms = torch.cuda.get_device_properties(self.A.device).multi_processor_count
+        pair_tiles = ((self.rows + 255) // 256) * ((self.N + 255) // 256)
+        pair = self.rows >= 256 and self.N >= 256 and self.K >= 1024 and pair_tiles >= sms
+        kern = "gemm_fp8_tc2" if pair else "gemm_fp8_tc"
         if self.ws > 1:
             kern += " (+ fused all-gather)"
         return {"kernel": kern, "bound": "tensor", "unit": "TFLOP/s", "work": self.flops,
