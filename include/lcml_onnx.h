@@ -438,7 +438,7 @@ private:
     bool async_out_ = false;
     lcml_stream_t out_stream_ = nullptr;
     lcml_event_t out_ready_ = nullptr, out_free_ = nullptr;
-    bool out_free_recorded_ = false;
+    bool last_out_async_ = false;  // the last forward copied its host outputs on out_stream_
 };
 
 // Throws Error with lcml_last_error() when a C-ABI call fails.

@@ -76,7 +76,7 @@ NetworkInstance::~NetworkInstance() {
 }
 
 void NetworkInstance::wait_outputs(lcml_stream_t s) {
-    const bool async = out_stream_ && out_free_recorded_;
+    const bool async = out_stream_ && last_out_async_;
     if (s) {
         if (async) check_status(lcml_stream_wait_event(s, out_free_), "wait_outputs");
         else if (s != stream_) {  // the copies ran on the instance's stream
@@ -977,11 +977,11 @@ void NetworkInstance::forward() {
             if (r) last_reader = i;
         }
     }
-    // asynchronous output copies: the first node that writes a host-staged
-    // output waits until the previous forward's copy of it has been read
+    // the previous forward copied its outputs on the output stream: the
+    // first node that writes a bound output waits until that copy has read it
     size_t first_out_writer = nodes.size();
-    if (async_out_ && !host_out_.empty() && out_free_recorded_) {
-        auto writes = [&](const std::string &n) { return host_out_.count(n) > 0; };
+    if (last_out_async_) {
+        auto writes = [&](const std::string &n) { return outputs_.count(n) > 0; };
         for (size_t i = 0; i < nodes.size() && first_out_writer == nodes.size(); ++i) {
             if (fusion_[i]->skip) continue;
             bool w = false;
@@ -1018,6 +1018,7 @@ void NetworkInstance::forward() {
             in_free_recorded_ = true;
         }
     }
+    last_out_async_ = false;
     if (host_out_.empty()) return;
     lcml_stream_t out = stream_;
     if (async_out_) {
@@ -1036,7 +1037,7 @@ void NetworkInstance::forward() {
     }
     if (async_out_) {
         check_status(lcml_event_record(out_free_, out_stream_), "record");
-        out_free_recorded_ = true;
+        last_out_async_ = true;
     }
 }
 

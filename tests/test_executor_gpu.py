@@ -141,6 +141,17 @@ def test_host_staged_io(dev):
         got.copy_(hout[len(xs) - 1], non_blocking=True)
     s.synchronize()
     np.testing.assert_array_equal(got.cpu().numpy(), want[len(xs) - 1])
+    # back to copies on the network's stream: the first writer of the output
+    # still waits for the last asynchronous copy, and wait_outputs() now waits
+    # for the network's stream
+    net.set_async_outputs(False)
+    for i in range(len(xs)):
+        net.set_input_host("input", hin[i])
+        net.set_output_host("output", hout[i])
+        net.forward()
+    net.wait_outputs()
+    for i in range(len(xs)):
+        np.testing.assert_array_equal(hout[i].numpy(), want[i])
 
 
 def _quantized_mlp(batch, dims, seed):
