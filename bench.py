@@ -393,11 +393,14 @@ class GemmWorkload:
                     "bound": "hbm", "unit": "GB/s",
                     "work": bytes_,
                     "profile": f"gemv_fp8_skinny_{self.M}" if self.M <= 4 else f"gemm_fp8_skinny_{self.M}"}
-        # the library's choice (gemm_fp8.cu dispatch): CTA pairs for long K once the 256 x 256 tiles fill the SMs
+        # the library's choice (gemm_fp8.cu dispatch): CTA pairs for long K with a 256 x 256 tile for every
+        # SM, for every pair when K >= 2048, for every other pair when K >= 4096
         import torch
-        sms = torch.cuda.get_device_properties(self.A.device).multi_processor_count
+        pairs = torch.cuda.get_device_properties(self.A.device).multi_processor_count // 2
         pair_tiles = ((self.rows + 255) // 256) * ((self.N + 255) // 256)
-        pair = self.rows >= 256 and self.N >= 256 and self.K >= 1024 and pair_tiles >= sms
+        pair = (self.rows >= 256 and self.N >= 256 and self.K >= 1024 and
+                (pair_tiles >= 2 * pairs or (self.K >= 2048 and pair_tiles >= pairs) or
+                 (self.K >= 4096 and 2 * pair_tiles >= pairs)))
         kern = "gemm_fp8_tc2" if pair else "gemm_fp8_tc"
         if self.ws > 1:
             kern += " (+ fused all-gather)"

@@ -302,7 +302,8 @@ __device__ __forceinline__ void store_chunk_peers(const EpiParams &ep, uint8_t *
 }
 
 // Per-warp staging for TMA stores: two buffers of 32 rows x 32 output
-// elements (double-buffered so the bulk copy of chunk i overlaps chunk i+1).
+// elements (double-buffered so the bulk copy of chunk i overlaps chunk i+1;
+// four buffers for e4m3 outputs measured 3 % slower on the short-K convs).
 // The row layout matches the output tensor map's swizzle (32B / 64B / 128B
 // for 1 / 2 / 4-byte elements: 16-byte piece p of row r sits at p ^ ((r * RB
 // / 128) mod P)), which also makes the 16-byte shared stores conflict-free.
@@ -484,8 +485,8 @@ enum FacMode : int { kFacLoad = 0, kFacSlot = 1, kFacTable = 2 };
 
 template <int BN, int EPI, int OUT, int FAC>
 __device__ __forceinline__ void epilogue_tile(const EpiParams &ep, const CUtensorMap *tmY, uint32_t taddr, int64_t row0,
-                                              int tn, const OutQuant &oq, uint8_t *stage, uint32_t &seq, int c_first,
-                                              int c_step, float *facw, float res_scale) {
+                                              int tn, int split, const OutQuant &oq, uint8_t *stage, uint32_t &seq,
+                                              int c_first, int c_step, float *facw, float res_scale) {
     constexpr bool FACSLOT = FAC == kFacSlot;
     if (row0 >= ep.M) return;
     const int64_t n_out = (EPI == LCML_EPI_SILU_MUL) ? ep.N / 2 : ep.N;
@@ -501,17 +502,21 @@ __device__ __forceinline__ void epilogue_tile(const EpiParams &ep, const CUtenso
     else if (ep.c_vec_mode == 2 && row_ok) row_add = ep.beta * __ldg(ep.c_vec + row);
     float amax = 0.0f;
     constexpr int kChunks = (EPI == LCML_EPI_SILU_MUL) ? BN / 64 : BN / 32;
+    // a split item (split 0 / 1, never for SILU_MUL) is the first / last BN/2
+    // columns of tile column tn, its accumulator in the buffer's first BN/2
+    // TMEM columns
+    const int nchunks = split < 0 ? kChunks : kChunks / 2;
+    const int64_t gbase = static_cast<int64_t>(tn) * BN + (split < 0 ? 0 : split * (BN / 2));  // gemm column of chunk 0
     // SILU_MUL: BN columns = BN/2 gate columns followed by BN/2 up columns
     auto col_of = [&](int c) {
-        return (EPI == LCML_EPI_SILU_MUL) ? static_cast<int64_t>(tn) * (BN / 2) + c * 32
-                                          : static_cast<int64_t>(tn) * BN + c * 32;
+        return (EPI == LCML_EPI_SILU_MUL) ? static_cast<int64_t>(tn) * (BN / 2) + c * 32 : gbase + c * 32;
     };
     const int lane = static_cast<int>(threadIdx.x & 31);
-    // this lane's column factors of chunk c: gemm column tn*BN + c*32 + lane (and its up column);
+    // this lane's column factors of chunk c: gemm column gbase + c*32 + lane (and its up column);
     // a per-tensor A scale (times alpha) is folded into the slot's column scale
     const float fold_scale = ep.sa_row ? 1.0f : row_scale;
     auto load_fac = [&](int c, float (&f)[4]) {
-        const int64_t n = static_cast<int64_t>(tn) * BN + c * 32 + lane;
+        const int64_t n = gbase + c * 32 + lane;
 #pragma unroll
         for (int h = 0; h < (EPI == LCML_EPI_SILU_MUL ? 2 : 1); ++h) {
             const int64_t nn = n + h * (BN / 2);
@@ -526,10 +531,10 @@ __device__ __forceinline__ void epilogue_tile(const EpiParams &ep, const CUtenso
     ResidualRaw rr_next;
     prefetch_residual(ep, row, row_ok, col_of(c_first), n_out, res_scale, rr_next);
     float fnext[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-    if (FACSLOT && c_first < kChunks) load_fac(c_first, fnext);
+    if (FACSLOT && c_first < nchunks) load_fac(c_first, fnext);
 #pragma unroll 1
-    for (int c = c_first; c < kChunks; c += c_step) {
-        const int64_t ng0 = static_cast<int64_t>(tn) * BN + c * 32;
+    for (int c = c_first; c < nchunks; c += c_step) {
+        const int64_t ng0 = gbase + c * 32;
         const int64_t col0 = col_of(c);
         if (col0 >= n_out) break;  // warp-uniform
         uint32_t g[32], u[32];
@@ -538,7 +543,7 @@ __device__ __forceinline__ void epilogue_tile(const EpiParams &ep, const CUtenso
         const ResidualRaw rr = rr_next;
         float v[32];
         if (FAC == kFacTable) {
-            if (c + c_step < kChunks) prefetch_residual(ep, row, row_ok, col_of(c + c_step), n_out, res_scale, rr_next);
+            if (c + c_step < nchunks) prefetch_residual(ep, row, row_ok, col_of(c + c_step), n_out, res_scale, rr_next);
             tmem_wait_ld();
             epi_values<EPI, true, kReluInPack>(ep, row, row_ok, col0, ng0 + BN / 2, n_out, g, g, facw + ng0,
                                                facw + kTabMaxN + ng0, facw, facw, rr, row_scale, row_add, amax, v);
@@ -549,7 +554,7 @@ __device__ __forceinline__ void epilogue_tile(const EpiParams &ep, const CUtenso
                 facw[64 + lane] = fnext[2];
                 facw[96 + lane] = fnext[3];
             }
-            if (c + c_step < kChunks) {
+            if (c + c_step < nchunks) {
                 prefetch_residual(ep, row, row_ok, col_of(c + c_step), n_out, res_scale, rr_next);
                 load_fac(c + c_step, fnext);
             }
@@ -563,7 +568,7 @@ __device__ __forceinline__ void epilogue_tile(const EpiParams &ep, const CUtenso
             ColFactors fg, fu;
             load_col_factors(ep, ng0, fg);  // global loads overlap the TMEM load
             if (EPI == LCML_EPI_SILU_MUL) load_col_factors(ep, ng0 + BN / 2, fu);
-            if (c + c_step < kChunks)
+            if (c + c_step < nchunks)
                 prefetch_residual(ep, row, row_ok, col_of(c + c_step), n_out, res_scale, rr_next);
             tmem_wait_ld();
             epi_values<EPI, false, kReluInPack>(ep, row, row_ok, col0, ng0 + BN / 2, n_out, g,
@@ -638,6 +643,21 @@ constexpr int stages_for() {
                      tab_bytes<BN, EPI, OUT, BKB>();
     const int s = room / (BM * BKB + BN * BKB);
     return s > 8 ? 8 : s;
+}
+
+// Work item j of the CTA-pair kernel's persistent schedule -> (tile, half):
+// items below n_whole are whole 256 x 256 tiles (half = -1); each tile from
+// n_whole on is split into two 256 x 128 items (half 0 and 1: its first and
+// last 128 columns). The host splits the tiles of a last wave that would
+// leave at least half of the pairs idle, so that wave takes half a tile's
+// time.
+__device__ __forceinline__ int split_item_tile(int j, int n_whole, int &half) {
+    if (j < n_whole) {
+        half = -1;
+        return j;
+    }
+    half = (j - n_whole) & 1;
+    return n_whole + ((j - n_whole) >> 1);
 }
 
 // IM2COL: tmA is an im2col tensor map of the NHWC activation described by
@@ -854,14 +874,14 @@ __global__ void __launch_bounds__(sc_threads<EPI, OUT>(), 1)
             const uint32_t taddr = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + static_cast<uint32_t>(acc * BN);
             if constexpr (kHasTable) {
                 if (use_table)
-                    epilogue_tile<BN, EPI, OUT, kFacTable>(ep, &tmY, taddr, row0, tn, oq, stage, seq, phase_c, kEW / 4, tab,
-                                                           res_scale);
+                    epilogue_tile<BN, EPI, OUT, kFacTable>(ep, &tmY, taddr, row0, tn, -1, oq, stage, seq, phase_c,
+                                                           kEW / 4, tab, res_scale);
                 else
-                    epilogue_tile<BN, EPI, OUT, kFacSlot>(ep, &tmY, taddr, row0, tn, oq, stage, seq, phase_c, kEW / 4, facw,
-                                                          res_scale);
+                    epilogue_tile<BN, EPI, OUT, kFacSlot>(ep, &tmY, taddr, row0, tn, -1, oq, stage, seq, phase_c,
+                                                          kEW / 4, facw, res_scale);
             } else {
-                epilogue_tile<BN, EPI, OUT, kFacSlot>(ep, &tmY, taddr, row0, tn, oq, stage, seq, phase_c, kEW / 4, facw,
-                                                      res_scale);
+                epilogue_tile<BN, EPI, OUT, kFacSlot>(ep, &tmY, taddr, row0, tn, -1, oq, stage, seq, phase_c, kEW / 4,
+                                                      facw, res_scale);
             }
             tc_fence_before();
             __syncwarp();
@@ -912,10 +932,13 @@ constexpr int pair_stages_for() {
     return s > 8 ? 8 : s;
 }
 
+// tmB2: B with 64-row boxes, for the split tiles (each CTA supplies 64 of
+// the 128 columns); n_split: tiles split in two at the end of the schedule.
 template <int STAGES, int EPI, int OUT>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(threads_for<EPI>(), 1)
     k_gemm_fp8_tc2(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                   const __grid_constant__ CUtensorMap tmY, int M, int N, int K, EpiParams ep, int *err) {
+                   const __grid_constant__ CUtensorMap tmB2, const __grid_constant__ CUtensorMap tmY, int M, int N,
+                   int K, int n_split, EpiParams ep, int *err) {
     using L = PairLayout<STAGES, EPI, OUT>;
     constexpr int BN = 256;
     extern __shared__ uint8_t smem_raw[];
@@ -934,6 +957,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(threads_for<EPI>(), 
     const int num_m = (M + 255) / 256;
     const int num_n = (N + BN - 1) / BN;
     const int num_tiles = num_m * num_n;
+    const int n_whole = num_tiles - n_split;
+    const int num_items = num_tiles + n_split;
     const int kblocks = (K + BK - 1) / BK;
 
     if (threadIdx.x == 0) {
@@ -966,11 +991,15 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(threads_for<EPI>(), 
             uint32_t phase = 0;
             int issued = 0;
             bool ok = true;
-            for (int tile = pair; tile < num_tiles && ok; tile += npairs) {
-                int tm, tn;
-                tile_coords(tile, num_m, num_n, tm, tn);
+            for (int item = pair; item < num_items && ok; item += npairs) {
+                int half, tm, tn;
+                tile_coords(split_item_tile(item, n_whole, half), num_m, num_n, tm, tn);
                 const int arow = tm * 256 + static_cast<int>(rank) * 128;
-                const int brow = tn * BN + static_cast<int>(rank) * 128;
+                // a split tile's 128 columns: 64 B rows from each CTA
+                const int brow = half < 0 ? tn * BN + static_cast<int>(rank) * 128
+                                          : tn * BN + half * 128 + static_cast<int>(rank) * 64;
+                const CUtensorMap *tb = half < 0 ? &tmB : &tmB2;
+                const uint32_t tx = half < 0 ? 2 * L::kStageBytes : 2 * (L::kHalfBytes + L::kHalfBytes / 2);
                 for (int kb = 0; kb < kblocks; ++kb) {
                     if (!mbar_wait(&empty[stage], phase ^ 1u, err, kDevTimeoutProducer)) {
                         ok = false;
@@ -978,10 +1007,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(threads_for<EPI>(), 
                     }
                     uint8_t *sa = smem + stage * L::kStageBytes;
                     uint8_t *sb = sa + L::kHalfBytes;
-                    if (rank == 0) mbar_arrive_expect_tx(&full[stage], 2 * L::kStageBytes);
+                    if (rank == 0) mbar_arrive_expect_tx(&full[stage], tx);
                     const uint32_t bar = mapa_shared(smem_u32(&full[stage]), 0);
                     tma_load_2d_pair(&tmA, bar, sa, kb * BK, arow);
-                    tma_load_2d_pair(&tmB, bar, sb, kb * BK, brow);
+                    tma_load_2d_pair(tb, bar, sb, kb * BK, brow);
                     ++issued;
                     if (++stage == STAGES) {
                         stage = 0;
@@ -1004,13 +1033,15 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(threads_for<EPI>(), 
     } else if (warp == 1) {
         // ---------------- MMA issuer (leader CTA only) ----------------
         if (rank == 0 && elect_one()) {
-            constexpr uint32_t idesc = idesc_e4m3_f32(256, BN, 0);
+            constexpr uint32_t idesc_whole = idesc_e4m3_f32(256, BN, 0);
+            constexpr uint32_t idesc_split = idesc_e4m3_f32(256, BN / 2, 0);
             int stage = 0;
             uint32_t phase = 0;
             int acc = 0;
             uint32_t acc_phase = 0;
             bool ok = true;
-            for (int tile = pair; tile < num_tiles && ok; tile += npairs) {
+            for (int item = pair; item < num_items && ok; item += npairs) {
+                const uint32_t idesc = item < n_whole ? idesc_whole : idesc_split;
                 if (!mbar_wait_cluster(&tempty[acc], acc_phase ^ 1u, err, kDevTimeoutMma)) break;
                 tc_fence_after();
                 const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * BN);
@@ -1053,15 +1084,16 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(threads_for<EPI>(), 
         const float res_scale = residual_scale(ep);
         int acc = 0;
         uint32_t acc_phase = 0;
-        for (int tile = pair; tile < num_tiles; tile += npairs) {
-            int tm, tn;
-            tile_coords(tile, num_m, num_n, tm, tn);
+        for (int item = pair; item < num_items; item += npairs) {
+            int split, tm, tn;
+            tile_coords(split_item_tile(item, n_whole, split), num_m, num_n, tm, tn);
             if (!mbar_wait(&tfull[acc], acc_phase, err, kDevTimeoutEpilogue)) break;
             tc_fence_after();
             const int64_t row0 = static_cast<int64_t>(tm) * 256 + rank * 128 + quarter * 32;
             const uint32_t taddr = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + static_cast<uint32_t>(acc * BN);
-            epilogue_tile<BN, EPI, OUT, kFacLoad>(ep, &tmY, taddr, row0, tn, oq, stage, seq, half, epi_warps<EPI>() / 4,
-                                                  nullptr, res_scale);
+            // split: -1 for a whole tile, else which 128-column half of tile column tn
+            epilogue_tile<BN, EPI, OUT, kFacLoad>(ep, &tmY, taddr, row0, tn, split, oq, stage, seq, half,
+                                                  epi_warps<EPI>() / 4, nullptr, res_scale);
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive_cluster(tempty_leader + 8u * static_cast<uint32_t>(acc));
@@ -1734,6 +1766,20 @@ int launch_gemm_kernel(void (*kern)(Params...), unsigned grid, unsigned threads,
     return LCML_OK;
 }
 
+// Tiles of the CTA-pair schedule to split into two 256 x 128 items: the
+// tiles of a last wave that would leave at least half of the pairs idle
+// (with fewer tiles than pairs, every tile), so the pairs that would wait
+// take half a tile each (4096^3 on B200: 49.4 vs 54.8 us). None for
+// SILU_MUL (a tile's gate and up columns are its two halves). The
+// single-CTA kernel does not split: its 128 x 128 halves gained nothing
+// measurable on the ResNet-50 convs, and the extra schedule state cost its
+// epilogue registers.
+int split_tiles(int64_t tiles, int64_t pairs, bool silu_mul) {
+    if (silu_mul || pairs < 2) return 0;
+    const int64_t rem = tiles % pairs;
+    return (rem > 0 && 2 * rem <= pairs) ? static_cast<int>(rem) : 0;
+}
+
 template <int BN, int EPI, int OUT, bool IM2COL = false, int BKB = BK>
 int launch_tc(const lcml_fp8_gemm_desc *d, const EpiParams &ep, cudaStream_t st, const ConvGeom &geo = ConvGeom{}) {
     constexpr int STAGES = stages_for<BN, EPI, OUT, BKB>();
@@ -1763,20 +1809,28 @@ int launch_tc2(const lcml_fp8_gemm_desc *d, const EpiParams &ep, cudaStream_t st
     static_assert(STAGES >= 3 && L::kSmemBytes <= kSmemLimit, "shared memory layout does not fit");
     auto kern = k_gemm_fp8_tc2<STAGES, EPI, OUT>;
     if (const int rc = ensure_max_smem(reinterpret_cast<const void *>(kern), L::kSmemBytes, "gemm_fp8_tc2")) return rc;
-    CUtensorMap ta, tb;
+    CUtensorMap ta, tb, tb2;
     int rc = make_tmap(&ta, d->A, d->K, d->M, d->lda, 128);
     if (rc) return rc;
     rc = make_tmap(&tb, d->B, d->K, d->N, d->ldb, 128);
     if (rc) return rc;
+    const int64_t tiles = ((d->M + 255) / 256) * ((d->N + 255) / 256);
+    const int64_t pairs = sm_count() / 2;
+    const int n_split = split_tiles(tiles, pairs, EPI == LCML_EPI_SILU_MUL);
+    if (n_split > 0) {
+        rc = make_tmap(&tb2, d->B, d->K, d->N, d->ldb, 64);
+        if (rc) return rc;
+    } else {
+        tb2 = tb;  // not read
+    }
     CUtensorMap ty;
     rc = output_tmap<EPI, OUT>(d, ep, &ty);
     if (rc) return rc;
-    const int64_t tiles = ((d->M + 255) / 256) * ((d->N + 255) / 256);
-    const int64_t pairs = sm_count() / 2;
-    const int grid = static_cast<int>(2 * (tiles < pairs ? tiles : pairs));
+    const int64_t items = tiles + n_split;
+    const int grid = static_cast<int>(2 * (items < pairs ? items : pairs));
     return launch_gemm_kernel(kern, static_cast<unsigned>(grid), threads_for<EPI>(), L::kSmemBytes, st, 0,
-                              "gemm_fp8_tc2", ta, tb, ty, static_cast<int>(d->M), static_cast<int>(d->N),
-                              static_cast<int>(d->K), ep, device_error_word());
+                              "gemm_fp8_tc2", ta, tb, tb2, ty, static_cast<int>(d->M), static_cast<int>(d->N),
+                              static_cast<int>(d->K), n_split, ep, device_error_word());
 }
 
 // Split factor for a GEMM whose 128 x 128 tiles would leave most SMs idle:
@@ -1902,10 +1956,18 @@ int dispatch(const lcml_fp8_gemm_desc *d, const EpiParams &ep, cudaStream_t st, 
         if (splits) return launch_splitk<EPI, OUT>(d, ep, st, splits);
     }
     // CTA pairs (256 x 256 tiles, half the staged bytes per MMA) pay off once
-    // the mainloop is long and there are a couple of tiles per pair; short-K
-    // and narrow GEMMs are epilogue-bound and run single-CTA tiles as wide as N.
+    // the mainloop is long: K >= 1024 with a tile for every SM, K >= 2048 with
+    // a tile for every pair, K >= 4096 with a tile for every other pair (B200,
+    // warm L2: 1024 x 8192 x 8192 49.9 vs 61.9 us single-CTA, 512 x 8192 x
+    // 8192 27.9 vs 35.6, 3072^3 22.3 vs 23.2; but 2048^3, 64 tiles of K =
+    // 2048, 12.8 vs 11.4, and ResNet-50's 1024 -> 256 1x1 convs, 98 tiles of
+    // K = 1024, slower as pairs). Short-K and narrow GEMMs are epilogue-bound
+    // and run single-CTA tiles as wide as N.
     const int64_t pair_tiles = ((d->M + 255) / 256) * ((d->N + 255) / 256);
-    const bool pair = d->M >= 256 && d->N >= 256 && d->K >= 1024 && pair_tiles >= sm_count();
+    const int64_t pairs = sm_count() / 2;
+    const bool pair = d->M >= 256 && d->N >= 256 && d->K >= 1024 &&
+                      (pair_tiles >= 2 * pairs || (d->K >= 2048 && pair_tiles >= pairs) ||
+                       (d->K >= 4096 && 2 * pair_tiles >= pairs));
     if ((d->variant & 3) != 1 && ((d->variant & 3) == 2 || pair)) return launch_tc2<EPI, OUT>(d, ep, st);
     if (EPI == LCML_EPI_SILU_MUL || d->N >= 2048 || wide_tiles(d)) return launch_tc<256, EPI, OUT>(d, ep, st);
     if (EPI != LCML_EPI_SILU_MUL && d->N <= 64) return launch_tc<64, EPI, OUT>(d, ep, st);

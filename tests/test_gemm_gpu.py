@@ -270,6 +270,45 @@ def test_kernel_variants(dev, mode, M, N, K, per_row, per_col):
     assert lb.device_error() == 0
 
 
+@pytest.mark.parametrize("out", ["f32", "e4m3"])
+def test_pair_schedule_split_last_wave(dev, out):
+    """CTA-pair kernel whose schedule ends in split tiles: with P pairs and
+    P + r tiles (r <= P / 2) the last r tiles run as two 256 x 128 items each.
+    M and N are ragged, so the split items include partial rows and an
+    item past the last column. fp32 output and the row |max| against the
+    oracle (with an fp32 residual), e4m3 output bit-identical to the
+    single-CTA kernel's (same epilogue rule, fp32 sums within the tolerance)."""
+    import torch
+    import luisaml_b200 as lb
+    pairs = torch.cuda.get_device_properties(dev).multi_processor_count // 2
+    num_n = 8
+    num_m = (pairs + 5 + num_n - 1) // num_n  # tiles = num_m * num_n: a few more than one wave
+    M, N, K = 256 * num_m - 40, 256 * num_n - 200, 384
+    tiles = num_m * num_n
+    assert 0 < tiles % pairs <= pairs // 2, (tiles, pairs)
+    Aq, sa, Bq, sb = make_operands(M, N, K, seed=71, per_row=True, per_col=True)
+    bias = np.random.default_rng(5).standard_normal(N).astype(np.float32)
+    res = np.random.default_rng(6).standard_normal((M, N)).astype(np.float32)
+    args = (_t(Aq, dev), _t(Bq, dev), _t(sa, dev), _t(sb, dev))
+    if out == "f32":
+        ref = np.maximum(oracle.qdq_gemm(Aq, sa, Bq, sb) + bias + res, 0.0)
+        amax = torch.zeros(M, dtype=torch.float32, device=dev)
+        Y = lb.gemm(*args, c_vec=_t(bias, dev), c_mat=_t(res, dev), epilogue=lb.EPI_RELU,
+                    out_dtype=torch.float32, row_amax=amax, variant=2)
+        y = Y.cpu().numpy()
+        assert_close(y, ref, what="pair schedule with split tiles")
+        assert np.array_equal(amax.cpu().numpy(), np.abs(y).max(axis=1))
+    else:
+        ys = _t(np.float32([0.05]), dev)
+        got = [lb.gemm(*args, c_vec=_t(bias, dev), epilogue=lb.EPI_RELU, out_dtype=torch.uint8, y_scale=ys,
+                       variant=m).cpu().numpy() for m in (2, 1)]
+        assert np.mean(got[0] != got[1]) <= 1e-4
+        diff = np.abs(oracle.e4m3_decode(got[0]) - oracle.e4m3_decode(got[1]))
+        step = np.maximum(np.abs(oracle.e4m3_decode(got[1])), 2.0 ** -6) / 8.0
+        assert (diff <= step + 1e-12).all()
+    assert lb.device_error() == 0
+
+
 @pytest.mark.parametrize("mode", [1, 2])
 def test_kernel_variants_silu(dev, mode):
     import torch
