@@ -598,6 +598,75 @@ __device__ __forceinline__ void epilogue_tile(const EpiParams &ep, const CUtenso
     if (ep.row_amax && row_ok) atomic_max_abs(ep.row_amax + row, amax);
 }
 
+// Fast path of the single-CTA epilogue for whole tiles in the common
+// convolution case, chosen once per kernel by the caller: column factors
+// from the shared table (per-tensor A scale and alpha folded in, beta * C
+// along N or none), e4m3 output through TMA stores by the reciprocal rule,
+// no row |max|, no peers, N a multiple of 32, and either no residual (RES =
+// false) or an e4m3 residual with 16-byte aligned rows (RES = true). With
+// those decided at compile time the unrolled chunk loop carries no
+// per-chunk tests besides the last-column one, and the same arithmetic as
+// epilogue_tile (fma2 by the table's factors, the residual's fma2, the
+// block conversion). Two warps share a TMEM lane quarter, taking alternate
+// chunks from c_first. Rows past M read row M - 1's residual; the TMA store
+// drops their outputs.
+template <int BN, int EPI, bool RES>
+__device__ __forceinline__ void epilogue_tile_fast(const EpiParams &ep, const CUtensorMap *tmY, uint32_t taddr,
+                                                   int64_t row0, int tn, float r_out, uint8_t *stage, uint32_t &seq,
+                                                   int c_first, const float *tab, float res_scale) {
+    constexpr int kIter = BN / 64;  // chunks per warp
+    if (row0 >= ep.M) return;
+    const int lane = static_cast<int>(threadIdx.x & 31);
+    int64_t row = row0 + lane;
+    if (row >= ep.M) row = ep.M - 1;
+    const int64_t colt = static_cast<int64_t>(tn) * BN;
+    const uint8_t *res_row = RES ? reinterpret_cast<const uint8_t *>(ep.c_mat) + row * ep.ldc : nullptr;
+    uint4 rn0 = make_uint4(0, 0, 0, 0), rn1 = rn0;
+    if (RES && colt + c_first * 32 < ep.N) {
+        const uint4 *p = reinterpret_cast<const uint4 *>(res_row + colt + c_first * 32);
+        rn0 = __ldg(p);
+        rn1 = __ldg(p + 1);
+    }
+#pragma unroll 1
+    for (int i = 0; i < kIter; ++i) {
+        const int c = c_first + 2 * i;
+        const int64_t col0 = colt + c * 32;
+        if (col0 >= ep.N) break;  // warp-uniform
+        uint32_t g[32];
+        tmem_ld_32x32b_x32(taddr + c * 32, g);
+        const uint4 r0 = rn0, r1 = rn1;
+        if (RES && i + 1 < kIter && col0 + 64 < ep.N) {  // the residual of this warp's next chunk
+            const uint4 *p = reinterpret_cast<const uint4 *>(res_row + col0 + 64);
+            rn0 = __ldg(p);
+            rn1 = __ldg(p + 1);
+        }
+        tmem_wait_ld();
+        float v[32];
+        const float4 *fs4 = reinterpret_cast<const float4 *>(tab + col0);
+        const float4 *fa4 = reinterpret_cast<const float4 *>(tab + kTabMaxN + col0);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            const float4 sc = fs4[j], ad = fa4[j];
+            fma2(v[4 * j], v[4 * j + 1], __uint_as_float(g[4 * j]), __uint_as_float(g[4 * j + 1]), sc.x, sc.y, ad.x,
+                 ad.y);
+            fma2(v[4 * j + 2], v[4 * j + 3], __uint_as_float(g[4 * j + 2]), __uint_as_float(g[4 * j + 3]), sc.z, sc.w,
+                 ad.z, ad.w);
+        }
+        if (RES) {
+            const uint32_t ws[8] = {r0.x, r0.y, r0.z, r0.w, r1.x, r1.y, r1.z, r1.w};
+#pragma unroll
+            for (int k = 0; k < 16; ++k) {
+                float lo, hi;
+                e4m3x2_decode(ws[k >> 1] >> ((k & 1) * 16), lo, hi);
+                fma2(v[2 * k], v[2 * k + 1], lo, hi, res_scale, res_scale, v[2 * k], v[2 * k + 1]);
+            }
+        }
+        uint32_t w[8];
+        quantize_block_rcp<32, false, EPI == LCML_EPI_RELU>(v, r_out, w);
+        store_chunk_tma<kOutE4M3>(tmY, stage, seq, row0, col0, w);
+    }
+}
+
 // Tile index -> (m tile, n tile), banded so that CTAs running at the same time
 // share A rows and B columns in L2.
 __device__ __forceinline__ void tile_coords(int tile, int num_m, int num_n, int &tm, int &tn) {
@@ -863,6 +932,16 @@ __global__ void __launch_bounds__(sc_threads<EPI, OUT>(), 1)
         uint32_t seq = 0;
         if (ep.tma_store && lane == 0) tma_prefetch_desc(&tmY);
         const float res_scale = residual_scale(ep);
+        // epilogue_tile_fast's conditions, once per kernel: 1 without a residual, 2 with an e4m3 one
+        constexpr bool kFastPath = kHasTable && OUT == kOutE4M3 && EPI != LCML_EPI_SILU_MUL && kEW == 8;
+        int fast = 0;
+        if constexpr (kFastPath) {
+            if (use_table && ep.tma_store && ep.y_num_peers == 0 && !ep.row_amax && !ep.sa_row &&
+                (ep.c_vec_mode == 0 || ep.c_vec_mode == 3) && oq.s_ok && N % 32 == 0) {
+                if (!ep.c_mat) fast = 1;
+                else if (ep.c_mat_kind == 2 && ep.ldc % 16 == 0 && aligned(ep.c_mat, 16)) fast = 2;
+            }
+        }
         int acc = 0;
         uint32_t acc_phase = 0;
         for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
@@ -872,16 +951,28 @@ __global__ void __launch_bounds__(sc_threads<EPI, OUT>(), 1)
             tc_fence_after();
             const int64_t row0 = static_cast<int64_t>(tm) * BM + quarter * 32;
             const uint32_t taddr = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + static_cast<uint32_t>(acc * BN);
-            if constexpr (kHasTable) {
-                if (use_table)
-                    epilogue_tile<BN, EPI, OUT, kFacTable>(ep, &tmY, taddr, row0, tn, -1, oq, stage, seq, phase_c,
-                                                           kEW / 4, tab, res_scale);
-                else
+            bool done = false;
+            if constexpr (kFastPath) {
+                if (fast == 2)
+                    epilogue_tile_fast<BN, EPI, true>(ep, &tmY, taddr, row0, tn, oq.r, stage, seq, phase_c, tab,
+                                                      res_scale);
+                else if (fast == 1)
+                    epilogue_tile_fast<BN, EPI, false>(ep, &tmY, taddr, row0, tn, oq.r, stage, seq, phase_c, tab,
+                                                       res_scale);
+                done = fast != 0;
+            }
+            if (!done) {
+                if constexpr (kHasTable) {
+                    if (use_table)
+                        epilogue_tile<BN, EPI, OUT, kFacTable>(ep, &tmY, taddr, row0, tn, -1, oq, stage, seq,
+                                                               phase_c, kEW / 4, tab, res_scale);
+                    else
+                        epilogue_tile<BN, EPI, OUT, kFacSlot>(ep, &tmY, taddr, row0, tn, -1, oq, stage, seq,
+                                                              phase_c, kEW / 4, facw, res_scale);
+                } else {
                     epilogue_tile<BN, EPI, OUT, kFacSlot>(ep, &tmY, taddr, row0, tn, -1, oq, stage, seq, phase_c,
                                                           kEW / 4, facw, res_scale);
-            } else {
-                epilogue_tile<BN, EPI, OUT, kFacSlot>(ep, &tmY, taddr, row0, tn, -1, oq, stage, seq, phase_c, kEW / 4,
-                                                      facw, res_scale);
+                }
             }
             tc_fence_before();
             __syncwarp();
