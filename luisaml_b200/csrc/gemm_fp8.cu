@@ -598,22 +598,23 @@ __device__ __forceinline__ void epilogue_tile(const EpiParams &ep, const CUtenso
     if (ep.row_amax && row_ok) atomic_max_abs(ep.row_amax + row, amax);
 }
 
-// Fast path of the single-CTA epilogue for whole tiles in the common
-// convolution case, chosen once per kernel by the caller: column factors
+// Fast path of the single-CTA epilogue for the common convolution case,
+// compiled as its own kernels (FAST = 1, 2) that the host picks: column factors
 // from the shared table (per-tensor A scale and alpha folded in, beta * C
 // along N or none), e4m3 output through TMA stores by the reciprocal rule,
 // no row |max|, no peers, N a multiple of 32, and either no residual (RES =
 // false) or an e4m3 residual with 16-byte aligned rows (RES = true). With
-// those decided at compile time the unrolled chunk loop carries no
-// per-chunk tests besides the last-column one, and the same arithmetic as
+// those decided at compile time the chunk loop carries no per-chunk tests
+// besides the last-column one and the output scale's (pack32), and the
+// kernel holds no generic epilogue beside it; the same arithmetic as
 // epilogue_tile (fma2 by the table's factors, the residual's fma2, the
 // block conversion). Two warps share a TMEM lane quarter, taking alternate
 // chunks from c_first. Rows past M read row M - 1's residual; the TMA store
 // drops their outputs.
 template <int BN, int EPI, bool RES>
 __device__ __forceinline__ void epilogue_tile_fast(const EpiParams &ep, const CUtensorMap *tmY, uint32_t taddr,
-                                                   int64_t row0, int tn, float r_out, uint8_t *stage, uint32_t &seq,
-                                                   int c_first, const float *tab, float res_scale) {
+                                                   int64_t row0, int tn, const OutQuant &oq, uint8_t *stage,
+                                                   uint32_t &seq, int c_first, const float *tab, float res_scale) {
     constexpr int kIter = BN / 64;  // chunks per warp
     if (row0 >= ep.M) return;
     const int lane = static_cast<int>(threadIdx.x & 31);
@@ -662,7 +663,7 @@ __device__ __forceinline__ void epilogue_tile_fast(const EpiParams &ep, const CU
             }
         }
         uint32_t w[8];
-        quantize_block_rcp<32, false, EPI == LCML_EPI_RELU>(v, r_out, w);
+        pack32<kOutE4M3, false, EPI == LCML_EPI_RELU>(v, oq, w);
         store_chunk_tma<kOutE4M3>(tmY, stage, seq, row0, col0, w);
     }
 }
@@ -735,7 +736,7 @@ __device__ __forceinline__ int split_item_tile(int j, int n_whole, int &half) {
 // filter tap (zero outside the image), exactly the K-major A tile the MMA
 // reads. BKB = 128 needs C % 128 == 0, BKB = 64 (64-byte rows, 64-byte
 // swizzle) C % 64 == 0.
-template <int BN, int STAGES, int EPI, int OUT, bool IM2COL, int BKB = BK>
+template <int BN, int STAGES, int EPI, int OUT, bool IM2COL, int BKB = BK, int FAST = 0>
 __global__ void __launch_bounds__(sc_threads<EPI, OUT>(), 1)
     k_gemm_fp8_tc(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                   const __grid_constant__ CUtensorMap tmY, int M, int N, int K, EpiParams ep, ConvGeom geo,
@@ -932,16 +933,8 @@ __global__ void __launch_bounds__(sc_threads<EPI, OUT>(), 1)
         uint32_t seq = 0;
         if (ep.tma_store && lane == 0) tma_prefetch_desc(&tmY);
         const float res_scale = residual_scale(ep);
-        // epilogue_tile_fast's conditions, once per kernel: 1 without a residual, 2 with an e4m3 one
-        constexpr bool kFastPath = kHasTable && OUT == kOutE4M3 && EPI != LCML_EPI_SILU_MUL && kEW == 8;
-        int fast = 0;
-        if constexpr (kFastPath) {
-            if (use_table && ep.tma_store && ep.y_num_peers == 0 && !ep.row_amax && !ep.sa_row &&
-                (ep.c_vec_mode == 0 || ep.c_vec_mode == 3) && oq.s_ok && N % 32 == 0) {
-                if (!ep.c_mat) fast = 1;
-                else if (ep.c_mat_kind == 2 && ep.ldc % 16 == 0 && aligned(ep.c_mat, 16)) fast = 2;
-            }
-        }
+        static_assert(FAST == 0 || (kHasTable && OUT == kOutE4M3 && EPI != LCML_EPI_SILU_MUL && kEW == 8),
+                      "the fast epilogue needs the column-factor table, e4m3 output and two warps per quarter");
         int acc = 0;
         uint32_t acc_phase = 0;
         for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
@@ -951,28 +944,19 @@ __global__ void __launch_bounds__(sc_threads<EPI, OUT>(), 1)
             tc_fence_after();
             const int64_t row0 = static_cast<int64_t>(tm) * BM + quarter * 32;
             const uint32_t taddr = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + static_cast<uint32_t>(acc * BN);
-            bool done = false;
-            if constexpr (kFastPath) {
-                if (fast == 2)
-                    epilogue_tile_fast<BN, EPI, true>(ep, &tmY, taddr, row0, tn, oq.r, stage, seq, phase_c, tab,
-                                                      res_scale);
-                else if (fast == 1)
-                    epilogue_tile_fast<BN, EPI, false>(ep, &tmY, taddr, row0, tn, oq.r, stage, seq, phase_c, tab,
+            if constexpr (FAST != 0) {  // the host checked epilogue_tile_fast's conditions
+                epilogue_tile_fast<BN, EPI, FAST == 2>(ep, &tmY, taddr, row0, tn, oq, stage, seq, phase_c, tab,
                                                        res_scale);
-                done = fast != 0;
-            }
-            if (!done) {
-                if constexpr (kHasTable) {
-                    if (use_table)
-                        epilogue_tile<BN, EPI, OUT, kFacTable>(ep, &tmY, taddr, row0, tn, -1, oq, stage, seq,
-                                                               phase_c, kEW / 4, tab, res_scale);
-                    else
-                        epilogue_tile<BN, EPI, OUT, kFacSlot>(ep, &tmY, taddr, row0, tn, -1, oq, stage, seq,
-                                                              phase_c, kEW / 4, facw, res_scale);
-                } else {
+            } else if constexpr (kHasTable) {
+                if (use_table)
+                    epilogue_tile<BN, EPI, OUT, kFacTable>(ep, &tmY, taddr, row0, tn, -1, oq, stage, seq, phase_c,
+                                                           kEW / 4, tab, res_scale);
+                else
                     epilogue_tile<BN, EPI, OUT, kFacSlot>(ep, &tmY, taddr, row0, tn, -1, oq, stage, seq, phase_c,
                                                           kEW / 4, facw, res_scale);
-                }
+            } else {
+                epilogue_tile<BN, EPI, OUT, kFacSlot>(ep, &tmY, taddr, row0, tn, -1, oq, stage, seq, phase_c, kEW / 4,
+                                                      facw, res_scale);
             }
             tc_fence_before();
             __syncwarp();
@@ -1871,12 +1855,12 @@ int split_tiles(int64_t tiles, int64_t pairs, bool silu_mul) {
     return (rem > 0 && 2 * rem <= pairs) ? static_cast<int>(rem) : 0;
 }
 
-template <int BN, int EPI, int OUT, bool IM2COL = false, int BKB = BK>
-int launch_tc(const lcml_fp8_gemm_desc *d, const EpiParams &ep, cudaStream_t st, const ConvGeom &geo = ConvGeom{}) {
+template <int BN, int EPI, int OUT, bool IM2COL = false, int BKB = BK, int FAST = 0>
+int launch_tc_kernel(const lcml_fp8_gemm_desc *d, const EpiParams &ep, cudaStream_t st, const ConvGeom &geo) {
     constexpr int STAGES = stages_for<BN, EPI, OUT, BKB>();
     using L = Layout<BN, STAGES, EPI, OUT, BKB>;
     static_assert(STAGES >= 3 && L::kSmemBytes <= kSmemLimit, "shared memory layout does not fit");
-    auto kern = k_gemm_fp8_tc<BN, STAGES, EPI, OUT, IM2COL, BKB>;
+    auto kern = k_gemm_fp8_tc<BN, STAGES, EPI, OUT, IM2COL, BKB, FAST>;
     if (const int rc = ensure_max_smem(reinterpret_cast<const void *>(kern), L::kSmemBytes, "gemm_fp8_tc")) return rc;
     CUtensorMap ta, tb;
     int rc = IM2COL ? make_tmap_im2col(&ta, geo, BKB) : make_tmap(&ta, d->A, d->K, d->M, d->lda, BM, BKB);
@@ -1891,6 +1875,34 @@ int launch_tc(const lcml_fp8_gemm_desc *d, const EpiParams &ep, cudaStream_t st,
     return launch_gemm_kernel(kern, static_cast<unsigned>(grid), sc_threads<EPI, OUT>(), L::kSmemBytes, st, 0,
                               IM2COL ? "conv_implicit_gemm_fp8_tc" : "gemm_fp8_tc", ta, tb, ty, static_cast<int>(d->M),
                               static_cast<int>(d->N), static_cast<int>(d->K), ep, geo, device_error_word());
+}
+
+// Which single-CTA kernel serves a GEMM: the fast-epilogue ones (1 without
+// a residual, 2 with an e4m3 residual) when every condition of
+// epilogue_tile_fast holds, else the generic one (0).
+template <int BN, int EPI, int OUT, int BKB>
+int fast_kind(const lcml_fp8_gemm_desc *d, const EpiParams &ep) {
+    if constexpr (OUT != kOutE4M3 || EPI == LCML_EPI_SILU_MUL || tab_bytes<BN, EPI, OUT, BKB>() == 0) {
+        return 0;
+    } else {
+        if (d->N > kTabMaxN || d->N % 32 != 0 || !ep.tma_store || ep.y_num_peers != 0 || ep.row_amax || ep.sa_row ||
+            (ep.c_vec_mode != 0 && ep.c_vec_mode != 3))
+            return 0;
+        if (!ep.c_mat) return 1;
+        return (ep.c_mat_kind == 2 && ep.ldc % 16 == 0 && aligned(ep.c_mat, 16)) ? 2 : 0;
+    }
+}
+
+template <int BN, int EPI, int OUT, bool IM2COL = false, int BKB = BK>
+int launch_tc(const lcml_fp8_gemm_desc *d, const EpiParams &ep, cudaStream_t st, const ConvGeom &geo = ConvGeom{}) {
+    if constexpr (OUT == kOutE4M3 && EPI != LCML_EPI_SILU_MUL && tab_bytes<BN, EPI, OUT, BKB>() > 0) {
+        switch (fast_kind<BN, EPI, OUT, BKB>(d, ep)) {
+            case 1: return launch_tc_kernel<BN, EPI, OUT, IM2COL, BKB, 1>(d, ep, st, geo);
+            case 2: return launch_tc_kernel<BN, EPI, OUT, IM2COL, BKB, 2>(d, ep, st, geo);
+            default: break;
+        }
+    }
+    return launch_tc_kernel<BN, EPI, OUT, IM2COL, BKB, 0>(d, ep, st, geo);
 }
 
 template <int EPI, int OUT>
