@@ -154,7 +154,7 @@ def test_same_process_two_devices():
     np.testing.assert_array_equal(results[0][1], results[1][1])
 
 
-def _row_split_worker(rank, world, port, q):
+def _row_split_worker(rank, world, port, q, shape=(1024, 768, 1024)):
     import datetime
     import sys
     import torch
@@ -169,7 +169,7 @@ def _row_split_worker(rank, world, port, q):
     import bench
     import luisaml_b200 as lb
     try:
-        wl = bench.GemmWorkload(1024, 768, 1024, "row_split_test")
+        wl = bench.GemmWorkload(*shape, "row_split_test")
         wl.setup(dev, 77)
         stream = torch.cuda.current_stream(dev)
         for _ in range(2):  # the second step overwrites the first's output with the same values
@@ -186,12 +186,16 @@ def _row_split_worker(rank, world, port, q):
         dist.destroy_process_group()
 
 
-def test_row_split_gemm_two_gpus():
+@pytest.mark.parametrize("shape", [(1024, 768, 1024), (5120, 2048, 2048)])
+def test_row_split_gemm_two_gpus(shape):
     """The headline GEMM step under torchrun (bench.GemmWorkload, M split over
-    2 ranks): the amax all-reduce gives each rank the whole tensor's scale,
+    2 ranks): the amax exchange gives each rank the whole tensor's scale,
     and the GEMM epilogue's peer stores leave the full Y on every rank. Both
     ranks' Y must be equal bit for bit and equal to one GPU running the same
-    problem unsplit (per-tensor dynamic quantize of all of A, then the GEMM)."""
+    problem unsplit (per-tensor dynamic quantize of all of A, then the GEMM).
+    The second shape runs each rank's 2560 rows on the CTA-pair kernel with
+    split tiles at the end of its schedule (80 tiles of 256 x 256 on 74
+    pairs) and the peer stores in the pair epilogue."""
     import torch
     import torch.multiprocessing as mp
     if torch.cuda.device_count() < 2:
@@ -200,7 +204,7 @@ def test_row_split_gemm_two_gpus():
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_row_split_worker, args=(r, 2, port, q)) for r in range(2)]
+    procs = [ctx.Process(target=_row_split_worker, args=(r, 2, port, q, shape)) for r in range(2)]
     for p in procs:
         p.start()
     res = sorted([q.get(timeout=300) for _ in range(2)], key=lambda r: r[0])
