@@ -197,6 +197,44 @@ def test_splitk_epilogues(dev, M, N, K):
     assert lb.device_error() == 0
 
 
+@pytest.mark.parametrize("res", [True, False])
+@pytest.mark.parametrize("M,N,K,relu", [(300, 256, 64, True), (1000, 128, 192, True), (200, 64, 576, False),
+                                         (777, 2048, 128, True)])
+def test_fast_epilogue_kernels(dev, M, N, K, relu, res):
+    """The fast-epilogue kernels (e4m3 out, column-factor table, per-tensor A
+    scale, bias along N, optional e4m3 residual) against the generic epilogue
+    on the same GEMM (selected by asking for the row |max|, which the fast
+    kernels do not compute): e4m3 bytes identical, and equal to the epilogue
+    rule applied to the oracle-checked fp32 result. Ragged M leaves the last
+    tile's rows past M reading a clamped residual row; N = 64 / 128 / 256 /
+    2048 covers the BN = 64, 128 and 256 kernels."""
+    import torch
+    import luisaml_b200 as lb
+    Aq, sa, Bq, sb = make_operands(M, N, K, seed=M + K, per_col=True)
+    rng = np.random.default_rng(N)
+    bias = rng.standard_normal(N).astype(np.float32)
+    r32 = rng.standard_normal((M, N)).astype(np.float32)
+    rs = np.float32(oracle.scale_from_amax(oracle.amax(r32)))
+    rq = oracle.quantize(r32, rs)
+    ref = oracle.qdq_gemm(Aq, sa, Bq, sb) + bias + (oracle.dequantize(rq, rs) if res else 0.0)
+    if relu:
+        ref = np.maximum(ref, 0.0)
+    ys = np.float32(oracle.scale_from_amax(np.abs(ref).max()))
+    kw = dict(c_vec=_t(bias, dev), epilogue=lb.EPI_RELU if relu else lb.EPI_NONE)
+    if res:
+        kw.update(c_mat=_t(rq, dev), c_mat_scale=_t(np.float32([rs]), dev))
+    args = (_t(Aq, dev), _t(Bq, dev), _t(sa, dev), _t(sb, dev))
+    y32 = lb.gemm(*args, out_dtype=torch.float32, **kw).cpu().numpy()
+    assert_close(y32, ref, what=f"fast-epilogue shape {M}x{N}x{K} fp32")
+    fast = lb.gemm(*args, out_dtype=torch.uint8, y_scale=_t(np.float32([ys]), dev), **kw).cpu().numpy()
+    amax = torch.zeros(M, dtype=torch.float32, device=dev)
+    generic = lb.gemm(*args, out_dtype=torch.uint8, y_scale=_t(np.float32([ys]), dev), row_amax=amax,
+                      **kw).cpu().numpy()
+    np.testing.assert_array_equal(fast, generic)
+    np.testing.assert_array_equal(fast, epilogue_quantize(y32, ys))
+    assert lb.device_error() == 0
+
+
 @pytest.mark.parametrize("M,N,K", [(200, 300, 160), (64, 1024, 128)])
 def test_simt_and_tensor_core_paths_agree(dev, M, N, K):
     import torch
