@@ -334,8 +334,15 @@ constexpr int threads_for() { return 64 + 32 * epi_warps<EPI>(); }
 // Single-CTA kernel: epilogue warps as in the pair kernel.
 template <int EPI, int OUT>
 constexpr int sc_epi_warps() { return EPI == LCML_EPI_SILU_MUL ? 4 : 8; }
+// The fast-epilogue kernel without a residual (FAST = 1) fits in 128
+// registers, the cap of a 14-warp CTA, and runs 12 epilogue warps: three
+// per TMEM lane quarter.
+template <int EPI, int OUT, int FAST>
+constexpr int sc_epi_warps_f() { return FAST == 1 ? 12 : sc_epi_warps<EPI, OUT>(); }
 template <int EPI, int OUT>
 constexpr int sc_threads() { return 64 + 32 * sc_epi_warps<EPI, OUT>(); }
+template <int EPI, int OUT, int FAST>
+constexpr int sc_threads_f() { return 64 + 32 * sc_epi_warps_f<EPI, OUT, FAST>(); }
 constexpr int kGatherRowsPerWarp = 64;
 
 template <int OUT>
@@ -611,11 +618,11 @@ __device__ __forceinline__ void epilogue_tile(const EpiParams &ep, const CUtenso
 // block conversion). Two warps share a TMEM lane quarter, taking alternate
 // chunks from c_first. Rows past M read row M - 1's residual; the TMA store
 // drops their outputs.
-template <int BN, int EPI, bool RES>
+template <int BN, int EPI, bool RES, int S>
 __device__ __forceinline__ void epilogue_tile_fast(const EpiParams &ep, const CUtensorMap *tmY, uint32_t taddr,
                                                    int64_t row0, int tn, const OutQuant &oq, uint8_t *stage,
                                                    uint32_t &seq, int c_first, const float *tab, float res_scale) {
-    constexpr int kIter = BN / 64;  // chunks per warp
+    constexpr int kChunks = BN / 32;  // S warps share the tile's chunks: c_first, c_first + S, ...
     if (row0 >= ep.M) return;
     const int lane = static_cast<int>(threadIdx.x & 31);
     int64_t row = row0 + lane;
@@ -623,21 +630,20 @@ __device__ __forceinline__ void epilogue_tile_fast(const EpiParams &ep, const CU
     const int64_t colt = static_cast<int64_t>(tn) * BN;
     const uint8_t *res_row = RES ? reinterpret_cast<const uint8_t *>(ep.c_mat) + row * ep.ldc : nullptr;
     uint4 rn0 = make_uint4(0, 0, 0, 0), rn1 = rn0;
-    if (RES && colt + c_first * 32 < ep.N) {
+    if (RES && c_first < kChunks && colt + c_first * 32 < ep.N) {
         const uint4 *p = reinterpret_cast<const uint4 *>(res_row + colt + c_first * 32);
         rn0 = __ldg(p);
         rn1 = __ldg(p + 1);
     }
 #pragma unroll 1
-    for (int i = 0; i < kIter; ++i) {
-        const int c = c_first + 2 * i;
+    for (int c = c_first; c < kChunks; c += S) {
         const int64_t col0 = colt + c * 32;
         if (col0 >= ep.N) break;  // warp-uniform
         uint32_t g[32];
         tmem_ld_32x32b_x32(taddr + c * 32, g);
         const uint4 r0 = rn0, r1 = rn1;
-        if (RES && i + 1 < kIter && col0 + 64 < ep.N) {  // the residual of this warp's next chunk
-            const uint4 *p = reinterpret_cast<const uint4 *>(res_row + col0 + 64);
+        if (RES && c + S < kChunks && col0 + 32 * S < ep.N) {  // the residual of this warp's next chunk
+            const uint4 *p = reinterpret_cast<const uint4 *>(res_row + col0 + 32 * S);
             rn0 = __ldg(p);
             rn1 = __ldg(p + 1);
         }
@@ -682,14 +688,14 @@ __device__ __forceinline__ void tile_coords(int tile, int num_m, int num_n, int 
 
 // Bytes of the column-factor table: none for SILU_MUL, and none where it
 // would leave fewer than three operand stages (BN = 256 with fp32 output).
-template <int BN, int EPI, int OUT, int BKB>
+template <int BN, int EPI, int OUT, int BKB, int FAST = 0>
 constexpr int tab_bytes() {
-    const int room = kSmemLimit - 2048 - sc_epi_warps<EPI, OUT>() * (stage_bytes_per_warp<OUT>() + kFacSlotBytes) -
+    const int room = kSmemLimit - 2048 - sc_epi_warps_f<EPI, OUT, FAST>() * (stage_bytes_per_warp<OUT>() + kFacSlotBytes) -
                      2 * kTabMaxN * 4;
     return (EPI != LCML_EPI_SILU_MUL && room / (BM * BKB + BN * BKB) >= 3) ? 2 * kTabMaxN * 4 : 0;
 }
 
-template <int BN, int STAGES, int EPI, int OUT, int BKB = BK>
+template <int BN, int STAGES, int EPI, int OUT, int BKB = BK, int FAST = 0>
 struct Layout {
     static constexpr int kABytes = BM * BKB;
     static constexpr int kBBytes = BN * BKB;
@@ -700,17 +706,17 @@ struct Layout {
     static constexpr int kTmemCols = kAcc * BN;
     static constexpr int kBarOffset = STAGES * kStageBytes;
     static constexpr int kEpiOffset = kBarOffset + 1024;     // epilogue warps' output staging
-    static constexpr int kFacOffset = kEpiOffset + sc_epi_warps<EPI, OUT>() * stage_bytes_per_warp<OUT>();  // factor slots
-    static constexpr int kTabOffset = kFacOffset + sc_epi_warps<EPI, OUT>() * kFacSlotBytes;  // column-factor table
-    static constexpr int kSmemBytes = kTabOffset + tab_bytes<BN, EPI, OUT, BKB>() + 1024;  // +1024 alignment
+    static constexpr int kFacOffset = kEpiOffset + sc_epi_warps_f<EPI, OUT, FAST>() * stage_bytes_per_warp<OUT>();  // factor slots
+    static constexpr int kTabOffset = kFacOffset + sc_epi_warps_f<EPI, OUT, FAST>() * kFacSlotBytes;  // column-factor table
+    static constexpr int kSmemBytes = kTabOffset + tab_bytes<BN, EPI, OUT, BKB, FAST>() + 1024;  // +1024 alignment
 };
 
 // The deepest operand ring (at most 8 stages) that fits beside the staging
 // and the column-factor table.
-template <int BN, int EPI, int OUT, int BKB = BK>
+template <int BN, int EPI, int OUT, int BKB = BK, int FAST = 0>
 constexpr int stages_for() {
-    const int room = kSmemLimit - 2048 - sc_epi_warps<EPI, OUT>() * (stage_bytes_per_warp<OUT>() + kFacSlotBytes) -
-                     tab_bytes<BN, EPI, OUT, BKB>();
+    const int room = kSmemLimit - 2048 - sc_epi_warps_f<EPI, OUT, FAST>() * (stage_bytes_per_warp<OUT>() + kFacSlotBytes) -
+                     tab_bytes<BN, EPI, OUT, BKB, FAST>();
     const int s = room / (BM * BKB + BN * BKB);
     return s > 8 ? 8 : s;
 }
@@ -737,12 +743,12 @@ __device__ __forceinline__ int split_item_tile(int j, int n_whole, int &half) {
 // reads. BKB = 128 needs C % 128 == 0, BKB = 64 (64-byte rows, 64-byte
 // swizzle) C % 64 == 0.
 template <int BN, int STAGES, int EPI, int OUT, bool IM2COL, int BKB = BK, int FAST = 0>
-__global__ void __launch_bounds__(sc_threads<EPI, OUT>(), 1)
+__global__ void __launch_bounds__(sc_threads_f<EPI, OUT, FAST>(), 1)
     k_gemm_fp8_tc(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                   const __grid_constant__ CUtensorMap tmY, int M, int N, int K, EpiParams ep, ConvGeom geo,
                   int *err) {
-    using L = Layout<BN, STAGES, EPI, OUT, BKB>;
-    constexpr int kEW = sc_epi_warps<EPI, OUT>();
+    using L = Layout<BN, STAGES, EPI, OUT, BKB, FAST>;
+    constexpr int kEW = sc_epi_warps_f<EPI, OUT, FAST>();
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint64_t *full = reinterpret_cast<uint64_t *>(smem + L::kBarOffset);
@@ -918,7 +924,7 @@ __global__ void __launch_bounds__(sc_threads<EPI, OUT>(), 1)
         float *facw = reinterpret_cast<float *>(smem + L::kFacOffset + e * kFacSlotBytes);
         float *tab = reinterpret_cast<float *>(smem + L::kTabOffset);
         // every column's factors into the shared table once (N <= kTabMaxN; zero past N up to the chunk edge)
-        constexpr bool kHasTable = tab_bytes<BN, EPI, OUT, BKB>() > 0;
+        constexpr bool kHasTable = tab_bytes<BN, EPI, OUT, BKB, FAST>() > 0;
         const bool use_table = kHasTable && N <= kTabMaxN;
         if (use_table) {
             const float fold = ep.sa_row ? 1.0f : ep.alpha * __ldg(ep.sa);
@@ -933,11 +939,12 @@ __global__ void __launch_bounds__(sc_threads<EPI, OUT>(), 1)
         uint32_t seq = 0;
         if (ep.tma_store && lane == 0) tma_prefetch_desc(&tmY);
         const float res_scale = residual_scale(ep);
-        static_assert(FAST == 0 || (kHasTable && OUT == kOutE4M3 && EPI != LCML_EPI_SILU_MUL && kEW == 8),
-                      "the fast epilogue needs the column-factor table, e4m3 output and two warps per quarter");
+        static_assert(FAST == 0 || (kHasTable && OUT == kOutE4M3 && EPI != LCML_EPI_SILU_MUL && kEW % 4 == 0),
+                      "the fast epilogue needs the column-factor table and e4m3 output");
         int acc = 0;
         uint32_t acc_phase = 0;
-        for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
+        int tile_iter = 0;
+        for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++tile_iter) {
             int tm, tn;
             tile_coords(tile, num_m, num_n, tm, tn);
             if (!mbar_wait(&tfull[acc], acc_phase, err, kDevTimeoutEpilogue)) break;
@@ -945,8 +952,11 @@ __global__ void __launch_bounds__(sc_threads<EPI, OUT>(), 1)
             const int64_t row0 = static_cast<int64_t>(tm) * BM + quarter * 32;
             const uint32_t taddr = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + static_cast<uint32_t>(acc * BN);
             if constexpr (FAST != 0) {  // the host checked epilogue_tile_fast's conditions
-                epilogue_tile_fast<BN, EPI, FAST == 2>(ep, &tmY, taddr, row0, tn, oq, stage, seq, phase_c, tab,
-                                                       res_scale);
+                // three warps per quarter: the chunk rotation moves on by one each tile, so no warp
+                // always takes the extra chunk of a tile whose chunk count three does not divide
+                const int first = kEW == 12 ? (phase_c + tile_iter) % 3 : phase_c;
+                epilogue_tile_fast<BN, EPI, FAST == 2, kEW / 4>(ep, &tmY, taddr, row0, tn, oq, stage, seq, first, tab,
+                                                                res_scale);
             } else if constexpr (kHasTable) {
                 if (use_table)
                     epilogue_tile<BN, EPI, OUT, kFacTable>(ep, &tmY, taddr, row0, tn, -1, oq, stage, seq, phase_c,
@@ -1857,8 +1867,8 @@ int split_tiles(int64_t tiles, int64_t pairs, bool silu_mul) {
 
 template <int BN, int EPI, int OUT, bool IM2COL = false, int BKB = BK, int FAST = 0>
 int launch_tc_kernel(const lcml_fp8_gemm_desc *d, const EpiParams &ep, cudaStream_t st, const ConvGeom &geo) {
-    constexpr int STAGES = stages_for<BN, EPI, OUT, BKB>();
-    using L = Layout<BN, STAGES, EPI, OUT, BKB>;
+    constexpr int STAGES = stages_for<BN, EPI, OUT, BKB, FAST>();
+    using L = Layout<BN, STAGES, EPI, OUT, BKB, FAST>;
     static_assert(STAGES >= 3 && L::kSmemBytes <= kSmemLimit, "shared memory layout does not fit");
     auto kern = k_gemm_fp8_tc<BN, STAGES, EPI, OUT, IM2COL, BKB, FAST>;
     if (const int rc = ensure_max_smem(reinterpret_cast<const void *>(kern), L::kSmemBytes, "gemm_fp8_tc")) return rc;
@@ -1872,7 +1882,7 @@ int launch_tc_kernel(const lcml_fp8_gemm_desc *d, const EpiParams &ep, cudaStrea
     if (rc) return rc;
     const int64_t tiles = ((d->M + BM - 1) / BM) * ((d->N + BN - 1) / BN);
     const int grid = static_cast<int>(tiles < sm_count() ? tiles : sm_count());
-    return launch_gemm_kernel(kern, static_cast<unsigned>(grid), sc_threads<EPI, OUT>(), L::kSmemBytes, st, 0,
+    return launch_gemm_kernel(kern, static_cast<unsigned>(grid), sc_threads_f<EPI, OUT, FAST>(), L::kSmemBytes, st, 0,
                               IM2COL ? "conv_implicit_gemm_fp8_tc" : "gemm_fp8_tc", ta, tb, ty, static_cast<int>(d->M),
                               static_cast<int>(d->N), static_cast<int>(d->K), ep, geo, device_error_word());
 }
