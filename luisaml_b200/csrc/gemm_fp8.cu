@@ -615,9 +615,9 @@ __device__ __forceinline__ void epilogue_tile(const EpiParams &ep, const CUtenso
 // besides the last-column one and the output scale's (pack32), and the
 // kernel holds no generic epilogue beside it; the same arithmetic as
 // epilogue_tile (fma2 by the table's factors, the residual's fma2, the
-// block conversion). Two warps share a TMEM lane quarter, taking alternate
-// chunks from c_first. Rows past M read row M - 1's residual; the TMA store
-// drops their outputs.
+// block conversion). S warps share a TMEM lane quarter (two, or three in
+// the 12-warp kernels), each taking every S-th chunk from c_first. Rows
+// past M read row M - 1's residual; the TMA store drops their outputs.
 template <int BN, int EPI, bool RES, int S>
 __device__ __forceinline__ void epilogue_tile_fast(const EpiParams &ep, const CUtensorMap *tmY, uint32_t taddr,
                                                    int64_t row0, int tn, const OutQuant &oq, uint8_t *stage,
